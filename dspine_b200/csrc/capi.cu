@@ -1,0 +1,127 @@
+// capi.cu -- extern "C" entry points: host-side validation, then the kernel launchers.
+#include <cuda_runtime.h>
+
+#include "../../include/dspine_b200.h"
+#include "dsv_common.cuh"
+#include "dsv_kernels.h"
+
+namespace {
+
+inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+}  // namespace
+
+extern "C" {
+
+const char* dsv_version(void) { return "dspine_b200 0.1.0 (sm_100a)"; }
+
+const char* dsv_status_string(int s) {
+    switch (s) {
+        case DSV_OK: return "ok";
+        case DSV_BAD_SHAPE: return "bad shape";
+        case DSV_BAD_DTYPE: return "bad dtype";
+        case DSV_BAD_POINTER: return "bad pointer";
+        case DSV_BAD_ALIGNMENT: return "bad alignment";
+        case DSV_LAUNCH_FAILED: return "kernel launch failed";
+        case DSV_WORKSPACE_TOO_SMALL: return "workspace too small";
+        case DSV_DEVICE_TIMEOUT: return "device wait timed out";
+        case DSV_UNSUPPORTED: return "unsupported configuration";
+        default: return "unknown status";
+    }
+}
+
+int dsv_verify_workspace_size(int32_t batch, size_t* bytes) {
+    if (bytes == nullptr) return DSV_BAD_POINTER;
+    if (batch < 0) return DSV_BAD_SHAPE;
+    *bytes = dsv::verify_workspace_bytes(batch);
+    return DSV_OK;
+}
+
+int dsv_workspace_init(void* ws, size_t bytes, dsv_stream_t stream) {
+    if (ws == nullptr) return DSV_BAD_POINTER;
+    if (cudaMemsetAsync(ws, 0, bytes, (cudaStream_t)stream) != cudaSuccess) return DSV_LAUNCH_FAILED;
+    return DSV_OK;
+}
+
+int dsv_workspace_error(void* ws, uint32_t* err, dsv_stream_t stream) {
+    if (ws == nullptr || err == nullptr) return DSV_BAD_POINTER;
+    dsv::WsHeader* h = reinterpret_cast<dsv::WsHeader*>(ws);
+    uint32_t v = 0;
+    if (cudaMemcpyAsync(&v, &h->err, sizeof(v), cudaMemcpyDeviceToHost, (cudaStream_t)stream) != cudaSuccess)
+        return DSV_LAUNCH_FAILED;
+    if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) return DSV_LAUNCH_FAILED;
+    if (cudaMemsetAsync(&h->err, 0, sizeof(v), (cudaStream_t)stream) != cudaSuccess) return DSV_LAUNCH_FAILED;
+    *err = v;
+    return DSV_OK;
+}
+
+int dsv_verify_logits(int32_t batch, int32_t vocab, int32_t dtype, const int64_t* candidates,
+                      const void* target_logits, const int64_t* target_row, int64_t target_rows,
+                      const void* draft_logits, const int64_t* draft_row, int64_t draft_rows,
+                      int64_t row_stride, const float* temperature, const int32_t* top_k,
+                      const float* top_p, const int32_t* verify_lens, const float* uniforms,
+                      const float* uniform_final, const int32_t* prefix_lens, int32_t* accept,
+                      int32_t* commit, int64_t* bonus, int64_t* output, int32_t* new_seq,
+                      const dsv_compact_out* compact, void* workspace, size_t workspace_bytes,
+                      dsv_stream_t stream) {
+    if (batch < 0 || vocab < 1 || row_stride < vocab || target_rows < 0) return DSV_BAD_SHAPE;
+    if (dtype != DSV_BF16 && dtype != DSV_F32) return DSV_BAD_DTYPE;
+    if (batch == 0) return DSV_OK;
+    if (target_rows < 1 || (draft_logits && draft_rows < 1)) return DSV_BAD_SHAPE;
+    if (!candidates || !target_logits || !target_row || !temperature || !top_k || !top_p ||
+        !verify_lens || !uniforms || !uniform_final || !prefix_lens || !accept || !commit ||
+        !bonus || !output || !new_seq || !workspace)
+        return DSV_BAD_POINTER;
+    if (draft_logits && (!draft_row || draft_rows < 0)) return DSV_BAD_POINTER;
+    if (compact && compact->slots_len < 0) return DSV_BAD_SHAPE;
+    if (compact && (!compact->slots || !compact->slot_row || !compact->tokens ||
+                    !compact->kept_slots || !compact->offsets || !compact->freed_slots ||
+                    !compact->freed_offsets))
+        return DSV_BAD_POINTER;
+    if (workspace_bytes < dsv::verify_workspace_bytes(batch)) return DSV_WORKSPACE_TOO_SMALL;
+    if (!aligned(workspace, 16)) return DSV_BAD_ALIGNMENT;
+    const size_t esz = dtype == DSV_BF16 ? 2 : 4;
+    if (!aligned(target_logits, esz) || (draft_logits && !aligned(draft_logits, esz)))
+        return DSV_BAD_ALIGNMENT;
+
+    dsv::VerifyArgs a = {};
+    a.B = batch;
+    a.V = vocab;
+    a.cand = candidates;
+    a.tgt = target_logits;
+    a.tgt_row = target_row;
+    a.tgt_rows = target_rows;
+    a.drf = draft_logits;
+    a.drf_row = draft_row;
+    a.drf_rows = draft_rows;
+    a.stride = row_stride;
+    a.temperature = temperature;
+    a.top_k = top_k;
+    a.top_p = top_p;
+    a.caps = verify_lens;
+    a.u = uniforms;
+    a.uf = uniform_final;
+    a.prefix = prefix_lens;
+    a.accept = accept;
+    a.commit = commit;
+    a.bonus = bonus;
+    a.output = output;
+    a.new_seq = new_seq;
+    if (compact) {
+        a.slots = compact->slots;
+        a.slots_len = compact->slots_len;
+        a.slot_row = compact->slot_row;
+        a.tok_out = compact->tokens;
+        a.slot_out = compact->kept_slots;
+        a.offsets = compact->offsets;
+        a.free_out = compact->freed_slots;
+        a.free_offsets = compact->freed_offsets;
+    }
+    char* base = reinterpret_cast<char*>(workspace);
+    a.ws = reinterpret_cast<dsv::WsHeader*>(base);
+    a.done = reinterpret_cast<unsigned int*>(base + 64);
+    a.res = reinterpret_cast<dsv::TaskResult*>(base + 64 + ((((size_t)batch * 4) + 63) & ~(size_t)63));
+    return dsv::launch_verify(a, dtype, (cudaStream_t)stream);
+}
+
+}  // extern "C"

@@ -1,0 +1,71 @@
+// dsv_kernels.h -- argument blocks and launchers shared by the kernels and the C ABI.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace dsv {
+
+struct TaskResult {
+    int32_t d;       // accept decision of draft s+1 against target row s
+    int32_t bonus;   // draw on row s if the chain stops there (-1: not drawn)
+    float p;         // target probability of the drafted token (diagnostics)
+    float q;         // draft probability of the drafted token (diagnostics)
+};
+
+struct WsHeader {
+    unsigned int next;       // dynamic task counter
+    unsigned int exited;     // clusters that left the task loop
+    unsigned int finalized;  // requests finalized in this launch
+    unsigned int err;        // bit 0: bulk copy timed out; bit 1: bad row; bit 2: bad slot
+};
+
+// Workspace layout: [WsHeader (64 B)][done: u32 x B, padded to 64 B][TaskResult x 16B]
+inline size_t verify_workspace_bytes(int B) {
+    size_t done = ((size_t)B * 4 + 63) & ~(size_t)63;
+    return 64 + done + (size_t)B * 16 * sizeof(TaskResult);
+}
+
+struct VerifyArgs {
+    int B, V;
+    int slice;                 // vocabulary elements per CTA of a cluster
+    int num_clusters;
+    const int64_t* cand;       // [B,16]
+    const void* tgt;           // target logits, rows of `stride` elements
+    const int64_t* tgt_row;    // [B] first target row of request b
+    long long tgt_rows;        // rows in the target tensor (bounds)
+    const void* drf;           // draft logits or null (q one-hot at the draft)
+    const int64_t* drf_row;    // [B] first draft row of request b
+    long long drf_rows;
+    long long stride;
+    const float* temperature;  // [B]
+    const int32_t* top_k;      // [B]
+    const float* top_p;        // [B]
+    const int32_t* caps;       // [B] verify lengths
+    const float* u;            // [B,15]
+    const float* uf;           // [B]
+    const int32_t* prefix;     // [B]
+    int32_t* accept;
+    int32_t* commit;
+    int64_t* bonus;
+    int64_t* output;           // [B,16]
+    int32_t* new_seq;
+    // optional accept-compact
+    const int32_t* slots;      // KV slot of verify position s of request b: slots[slot_row[b]+s]
+    long long slots_len;
+    const int64_t* slot_row;
+    int64_t* tok_out;          // [sum commit]
+    int32_t* slot_out;         // [sum commit]
+    int32_t* offsets;          // [B+1]
+    int32_t* free_out;         // [sum (cap - commit)]
+    int32_t* free_offsets;     // [B+1]
+    // workspace
+    WsHeader* ws;
+    unsigned int* done;
+    TaskResult* res;
+};
+
+// launchers (return a dsv::Status)
+int launch_verify(const VerifyArgs& a, int dtype, cudaStream_t stream);
+
+}  // namespace dsv

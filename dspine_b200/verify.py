@@ -1,0 +1,175 @@
+"""Host API of the fused verification kernel (C ABI: dsv_verify_logits).
+
+``verify_logits`` is the one call that replaces the reference's two-step verify
+(runtime/worker.py:440-508 build_dspine_target_probs, then sampling/rejection.py:12-153
+sample_capped_chain_from_probs): it reads target (and draft) logits once and writes the same
+five outputs (accept, commit, bonus, output, new_seq).  Argument checks raise ValueError before
+anything is launched, like the reference's launchers (sampling/rejection.py:113-138).
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+
+T = 16
+_DTYPES = {torch.bfloat16: 0, torch.float32: 1}
+
+
+class Workspace:
+    """Device scratch of dsv_verify_logits (task counters and per-row decisions).
+
+    Zeroed once at allocation; every launch leaves it zeroed.  Launches that may overlap on
+    the GPU (different streams) need different workspaces."""
+
+    def __init__(self, batch: int, device):
+        size = ctypes.c_size_t()
+        _lib.call("dsv_verify_workspace_size", int(batch), ctypes.byref(size))
+        self.batch = int(batch)
+        self.nbytes = int(size.value)
+        self.buf = torch.empty(self.nbytes, dtype=torch.uint8, device=device)
+        _lib.call("dsv_workspace_init", self.buf.data_ptr(), self.nbytes, _stream(device))
+
+    def error_word(self) -> int:
+        """Device error bits (synchronizes the current stream); cleared after reading."""
+        err = ctypes.c_uint32()
+        _lib.call("dsv_workspace_error", self.buf.data_ptr(), ctypes.byref(err),
+                  _stream(self.buf.device))
+        return int(err.value)
+
+
+_workspaces: dict = {}
+
+
+def workspace_for(batch: int, device) -> Workspace:
+    device = torch.device(device)
+    key = (device.index, int(batch))
+    ws = _workspaces.get(key)
+    if ws is None:
+        # grow to the largest batch seen on this device
+        ws = Workspace(batch, device)
+        _workspaces[key] = ws
+    return ws
+
+
+def _stream(device) -> int:
+    return torch.cuda.current_stream(torch.device(device)).cuda_stream
+
+
+@dataclass
+class CompactOutputs:
+    """Packed accepted tokens / kept and freed KV slots (see dsv_compact_out)."""
+
+    tokens: torch.Tensor
+    kept_slots: torch.Tensor
+    offsets: torch.Tensor
+    freed_slots: torch.Tensor
+    freed_offsets: torch.Tensor
+
+    @staticmethod
+    def allocate(batch: int, device) -> "CompactOutputs":
+        n = batch * T
+        return CompactOutputs(
+            torch.empty(n, dtype=torch.int64, device=device),
+            torch.empty(n, dtype=torch.int32, device=device),
+            torch.empty(batch + 1, dtype=torch.int32, device=device),
+            torch.empty(n, dtype=torch.int32, device=device),
+            torch.empty(batch + 1, dtype=torch.int32, device=device),
+        )
+
+
+def new_outputs(batch: int, device):
+    return (torch.empty(batch, dtype=torch.int32, device=device),
+            torch.empty(batch, dtype=torch.int32, device=device),
+            torch.empty(batch, dtype=torch.int64, device=device),
+            torch.empty((batch, T), dtype=torch.int64, device=device),
+            torch.empty(batch, dtype=torch.int32, device=device))
+
+
+def _check(cond, msg):
+    if not cond:
+        raise ValueError(msg)
+
+
+def verify_logits(*, candidates, target_logits, target_rows, temperature, top_k, top_p,
+                  verify_lens, uniforms, uniform_final, prefix_lens, draft_logits=None,
+                  draft_rows=None, outputs=None, slots=None, slot_rows=None, compact=None,
+                  workspace: Workspace | None = None):
+    """Verify a ragged batch of 16-token draft blocks directly from logits.
+
+    candidates [B,16] int64 (anchor + 15 drafts); target_logits [R,V] bf16/fp32 rows;
+    target_rows [B] int64: request b's verify position s uses target row target_rows[b]+s;
+    draft_logits [R',V] (same dtype) with draft_rows [B], or None for one-hot q;
+    temperature [B] f32, top_k [B] i32 (>= V: off, <= 1: greedy), top_p [B] f32;
+    verify_lens [B] i32 in [1,16]; uniforms [B,15] f32; uniform_final [B] f32;
+    prefix_lens [B] i32.  Optional ``slots`` [*] i32 with ``slot_rows`` [B] i64 and a
+    ``compact`` CompactOutputs receive the packed accepted tokens and KV slots.
+    Returns (accept, commit, bonus, output, new_seq)."""
+    _check(candidates.dim() == 2 and candidates.shape[1] == T, "candidates must be [B,16]")
+    B = candidates.shape[0]
+    dev = candidates.device
+    _check(dev.type == "cuda", "verify_logits runs on CUDA tensors")
+    _check(target_logits.dim() == 2 and target_logits.dtype in _DTYPES,
+           "target_logits must be [rows, V] bf16 or fp32")
+    _check(target_logits.stride(1) == 1, "target_logits rows must be contiguous")
+    V = target_logits.shape[1]
+    stride = target_logits.stride(0)
+    if draft_logits is not None:
+        _check(draft_logits.dtype == target_logits.dtype, "draft and target dtypes differ")
+        _check(draft_logits.dim() == 2 and draft_logits.shape[1] == V, "draft vocab differs")
+        _check(draft_logits.stride(1) == 1 and draft_logits.stride(0) == stride,
+               "draft rows must use the target row stride")
+        _check(draft_rows is not None and draft_rows.shape == (B,), "draft_rows must be [B]")
+    expect = {
+        "candidates": (candidates, torch.int64, (B, T)),
+        "target_rows": (target_rows, torch.int64, (B,)),
+        "temperature": (temperature, torch.float32, (B,)),
+        "top_k": (top_k, torch.int32, (B,)),
+        "top_p": (top_p, torch.float32, (B,)),
+        "verify_lens": (verify_lens, torch.int32, (B,)),
+        "uniforms": (uniforms, torch.float32, (B, T - 1)),
+        "uniform_final": (uniform_final, torch.float32, (B,)),
+        "prefix_lens": (prefix_lens, torch.int32, (B,)),
+    }
+    if draft_rows is not None:
+        expect["draft_rows"] = (draft_rows, torch.int64, (B,))
+    for name, (t, dt, shape) in expect.items():
+        _check(t.dtype == dt, f"{name} must be {dt}")
+        _check(tuple(t.shape) == shape, f"{name} must have shape {shape}")
+        _check(t.is_contiguous(), f"{name} must be contiguous")
+        _check(t.device == dev, "all tensors must be on one device")
+    _check(target_logits.device == dev, "all tensors must be on one device")
+    if outputs is None:
+        outputs = new_outputs(B, dev)
+    _check(len(outputs) == 5, "Expected accept/commit/bonus/output/new_seq buffers")
+    for t, (dt, shape) in zip(outputs, ((torch.int32, (B,)), (torch.int32, (B,)),
+                                        (torch.int64, (B,)), (torch.int64, (B, T)),
+                                        (torch.int32, (B,)))):
+        _check(t.dtype == dt and tuple(t.shape) == shape and t.is_contiguous() and t.device == dev,
+               "output buffers must be contiguous accept i32[B], commit i32[B], bonus i64[B], "
+               "output i64[B,16], new_seq i32[B]")
+    cstruct = None
+    if compact is not None:
+        _check(slots is not None and slot_rows is not None, "compaction needs slots and slot_rows")
+        _check(slots.dtype == torch.int32 and slot_rows.dtype == torch.int64, "slot dtypes")
+        _check(slot_rows.shape == (B,), "slot_rows must be [B]")
+        cstruct = _lib.CompactOut(slots.data_ptr(), slots.numel(), slot_rows.data_ptr(), compact.tokens.data_ptr(),
+                                  compact.kept_slots.data_ptr(), compact.offsets.data_ptr(),
+                                  compact.freed_slots.data_ptr(), compact.freed_offsets.data_ptr())
+    if workspace is None:
+        workspace = workspace_for(B, dev)
+    _check(workspace.batch >= B, "workspace is too small for this batch")
+    drows_n = draft_logits.shape[0] if draft_logits is not None else 0
+    _lib.call(
+        "dsv_verify_logits", B, V, _DTYPES[target_logits.dtype], candidates.data_ptr(),
+        target_logits.data_ptr(), target_rows.data_ptr(), target_logits.shape[0],
+        _lib.ptr(draft_logits), _lib.ptr(draft_rows), drows_n, stride, temperature.data_ptr(),
+        top_k.data_ptr(), top_p.data_ptr(), verify_lens.data_ptr(), uniforms.data_ptr(),
+        uniform_final.data_ptr(), prefix_lens.data_ptr(), *(o.data_ptr() for o in outputs),
+        ctypes.byref(cstruct) if cstruct is not None else None, workspace.buf.data_ptr(),
+        workspace.nbytes, _stream(dev))
+    return outputs

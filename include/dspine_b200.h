@@ -1,0 +1,96 @@
+/*
+ * dspine_b200.h -- C ABI of the B200 draft-block verification library (libdspine_b200.so).
+ *
+ * Every entry point takes device pointers, sizes and a cudaStream_t, enqueues its work on that
+ * stream and returns a dsv_status (0 = success).  Arguments are validated on the host before
+ * anything is launched; nothing here synchronizes the stream unless stated.  Outputs are
+ * caller-owned buffers; inputs are never modified.
+ *
+ * Each declaration names the reference interface it replaces (paths inside the reference
+ * project, package sglang_dspine).
+ */
+#ifndef DSPINE_B200_H
+#define DSPINE_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef struct CUstream_st* dsv_stream_t; /* == cudaStream_t */
+
+typedef enum {
+    DSV_OK = 0,
+    DSV_BAD_SHAPE = 1,
+    DSV_BAD_DTYPE = 2,
+    DSV_BAD_POINTER = 3,
+    DSV_BAD_ALIGNMENT = 4,
+    DSV_LAUNCH_FAILED = 5,
+    DSV_WORKSPACE_TOO_SMALL = 6,
+    DSV_DEVICE_TIMEOUT = 7,
+    DSV_UNSUPPORTED = 8
+} dsv_status;
+
+typedef enum { DSV_BF16 = 0, DSV_F32 = 1 } dsv_dtype;
+
+/* Library version string and a readable name for a status code. */
+const char* dsv_version(void);
+const char* dsv_status_string(int status);
+
+/* ---- workspace ----------------------------------------------------------------------------
+ * Scratch for dsv_verify_logits: task counters and per-row decisions.  Zero it once after
+ * allocation (dsv_workspace_init); every launch leaves it zeroed again. */
+int dsv_verify_workspace_size(int32_t batch, size_t* bytes);
+int dsv_workspace_init(void* workspace, size_t bytes, dsv_stream_t stream);
+/* Copy the device error word of a workspace to *err and clear it (synchronizes `stream`).
+ * bit 0: a shared-memory bulk copy did not complete within its time limit;
+ * bit 1: a request addressed a row outside the logit tensors. */
+int dsv_workspace_error(void* workspace, uint32_t* err, dsv_stream_t stream);
+/* bit 2 of the error word: a compaction read a KV slot position outside `slots_len`. */
+
+/* ---- accept-compact outputs (optional argument of dsv_verify_logits) ----------------------
+ * Restates SGLang's commit of accepted tokens and KV slots (wrapped by the reference at
+ * runtime/worker.py:745-777): request b keeps tokens output[b, :commit_b] and the KV slots of
+ * its verify positions [0, commit_b); positions [commit_b, verify_len_b) are freed. */
+typedef struct {
+    const int32_t* slots;     /* KV slot of verify position s of request b: slots[slot_row[b]+s] */
+    int64_t slots_len;        /* entries in `slots`; positions outside it read as -1 */
+    const int64_t* slot_row;  /* [B] */
+    int64_t* tokens;          /* [B*16] accepted tokens, request-major (first sum(commit) used) */
+    int32_t* kept_slots;      /* [B*16] */
+    int32_t* offsets;         /* [B+1] exclusive scan of commit */
+    int32_t* freed_slots;     /* [B*16] */
+    int32_t* freed_offsets;   /* [B+1] */
+} dsv_compact_out;
+
+/* ---- fused verification from logits -------------------------------------------------------
+ * Replaces runtime/worker.py:440-508 build_dspine_target_probs (flashinfer backend, min-p off:
+ * temperature softmax, joint top-k/top-p, greedy rows one-hot at the lowest-index argmax)
+ * followed by the capped chain rejection of sampling/rejection.py:12-98
+ * (_sample_capped_chain; the dense-q path of runtime/worker.py:511-581 dspine_accept_sampling).
+ *
+ * Target row of (request b, position s) is target_row[b] + s; its draft row (the distribution
+ * draft s+1 was sampled from: the same temperature/top-k/top-p applied to draft logits) is
+ * draft_row[b] + s.  draft_logits == NULL, or a greedy request (top_k <= 1 or temperature <= 0),
+ * means q is one-hot at the drafted token.  Rows hold `vocab` logits of `dtype`, `row_stride`
+ * elements apart.  Outputs as sample_capped_chain_from_probs (sampling/rejection.py:101-153):
+ * accept i32[B], commit i32[B], bonus i64[B], output i64[B,16], new_seq i32[B].
+ * Sums that feed decisions are exact (2^-40 fixed point), so results do not depend on launch
+ * shape.  `compact` may be NULL. */
+int dsv_verify_logits(int32_t batch, int32_t vocab, int32_t dtype, const int64_t* candidates,
+                      const void* target_logits, const int64_t* target_row, int64_t target_rows,
+                      const void* draft_logits, const int64_t* draft_row, int64_t draft_rows,
+                      int64_t row_stride, const float* temperature, const int32_t* top_k,
+                      const float* top_p, const int32_t* verify_lens, const float* uniforms,
+                      const float* uniform_final, const int32_t* prefix_lens, int32_t* accept,
+                      int32_t* commit, int64_t* bonus, int64_t* output, int32_t* new_seq,
+                      const dsv_compact_out* compact, void* workspace, size_t workspace_bytes,
+                      dsv_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* DSPINE_B200_H */

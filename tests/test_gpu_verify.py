@@ -1,0 +1,145 @@
+"""Parity of the fused CUDA verification (dsv_verify_logits) with the CPU oracle.
+
+Every case compares all five outputs (accept, commit, bonus, output, new_seq) bit-exactly:
+the kernel and the oracle use the same exact fixed-point sums, so no tolerance applies to
+these integer outputs.  Cases follow the reference's own parity tests
+(tests/test_sparse_accept_compact.py:56-130, tests/test_dynamic_sampling.py:222-338): ragged
+caps, all-accepted rows, zero-residual fallback, greedy ties, mixed filters.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle as O
+from dspine_b200 import verify, workloads
+from tests.helpers import assert_same, oracle_verify
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+
+
+def run_kernel(batch, compact=False):
+    kw = batch.kwargs()
+    out = verify.verify_logits(**kw)
+    torch.cuda.synchronize()
+    return out
+
+
+def random_batch(seed, B, V, dtype, quantize=False, with_draft=True, neg_inf=False):
+    g = torch.Generator().manual_seed(seed)
+    lens = torch.randint(1, 17, (B,), generator=g, dtype=torch.int32)
+    lens[0] = 16
+    temperature = torch.rand(B, generator=g) * 1.8
+    temperature[torch.rand(B, generator=g) < 0.2] = 0.0
+    ks = torch.tensor([workloads.TOPK_OFF, 1, 3, 7, 20, 50], dtype=torch.int32)
+    top_k = ks[torch.randint(0, len(ks), (B,), generator=g)]
+    top_p = torch.where(torch.rand(B, generator=g) < 0.3, torch.ones(B),
+                        0.5 + 0.5 * torch.rand(B, generator=g))
+    batch = workloads.build(lens, temperature, top_k, top_p, V=V, dtype=torch.float32,
+                            seed=seed, with_draft=with_draft)
+    if quantize:  # many exactly equal logits: ties at every boundary
+        batch.target_logits = (batch.target_logits * 2).round() / 2
+        if batch.draft_logits is not None:
+            batch.draft_logits = (batch.draft_logits * 2).round() / 2
+    if neg_inf:
+        batch.target_logits[:, ::5] = -float("inf")
+    batch.uniforms[0] = 0.0  # request 0: everything accepted when q agrees
+    batch.target_logits = batch.target_logits.to(dtype)
+    if batch.draft_logits is not None:
+        batch.draft_logits = batch.draft_logits.to(dtype)
+    return batch.to(DEV)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("V", [97, 257, 1031, 4099])
+def test_small_vocab_matches_oracle(dtype, V):
+    for seed in range(3):
+        batch = random_batch(1000 + seed * 7 + V, 9, V, dtype)
+        got = run_kernel(batch)
+        assert_same(got, oracle_verify(batch), f"V={V} seed={seed}")
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_ties_and_masked_logits(dtype):
+    for seed in range(3):
+        batch = random_batch(77 + seed, 12, 2053, dtype, quantize=True, neg_inf=seed == 1)
+        assert_same(run_kernel(batch), oracle_verify(batch), f"ties seed={seed}")
+
+
+def test_one_hot_q_without_draft_logits():
+    batch = random_batch(5, 17, 1031, torch.bfloat16, with_draft=False)
+    assert batch.draft_logits is None
+    assert_same(run_kernel(batch), oracle_verify(batch), "one-hot q")
+
+
+def test_zero_residual_falls_back_to_target():
+    """tests/test_sparse_accept_compact.py:77-86: p == q on the rejected row."""
+    batch = random_batch(9, 4, 257, torch.float32)
+    # draft == target for request 1 and a coin that rejects (u = 1 -> u*q < p fails)
+    b = 1
+    t0, d0 = int(batch.target_rows[b]), int(batch.draft_rows[b])
+    n = int(batch.verify_lens[b]) - 1
+    if n > 0:
+        batch.draft_logits[d0:d0 + n] = batch.target_logits[t0:t0 + n]
+    batch.uniforms[b] = 1.0
+    assert_same(run_kernel(batch), oracle_verify(batch), "zero residual")
+
+
+def test_repeated_launches_are_identical_and_reset_the_workspace():
+    batch = random_batch(31, 23, 4099, torch.bfloat16)
+    first = [t.clone() for t in run_kernel(batch)]
+    for _ in range(3):
+        again = run_kernel(batch)
+        for a, b in zip(first, again):
+            assert torch.equal(a, b)
+    ws = verify.workspace_for(batch.B, DEV)
+    assert ws.error_word() == 0
+    header = ws.buf[:16].view(torch.int32).cpu().tolist()
+    assert header[:3] == [0, 0, 0]
+
+
+def test_config0_full_vocab_fp32():
+    batch = workloads.config0(device=DEV)
+    assert_same(run_kernel(batch), oracle_verify(batch), "config0")
+
+
+def test_config1_full_size_bf16():
+    batch = workloads.config1(device=DEV)
+    assert_same(run_kernel(batch), oracle_verify(batch), "config1")
+
+
+def test_config4_full_size_bf16():
+    batch = workloads.config4(device=DEV)
+    assert_same(run_kernel(batch), oracle_verify(batch), "config4")
+
+
+def test_accept_compact_matches_oracle():
+    batch = workloads.config1(device=DEV, B=64, V=4099)
+    comp = verify.CompactOutputs.allocate(batch.B, DEV)
+    out = verify.verify_logits(**batch.kwargs(), slots=batch.slots, slot_rows=batch.slot_rows,
+                               compact=comp)
+    torch.cuda.synchronize()
+    acc, commit, bonus, output, new_seq = [t.cpu().numpy() for t in out]
+    tok, sl, off, fr, foff = O.accept_compact(commit, batch.verify_lens.cpu().numpy(), output,
+                                              batch.slots.cpu().numpy(),
+                                              batch.slot_rows.cpu().numpy())
+    n, nf = int(off[-1]), int(foff[-1])
+    np.testing.assert_array_equal(comp.offsets.cpu().numpy(), off)
+    np.testing.assert_array_equal(comp.freed_offsets.cpu().numpy(), foff)
+    np.testing.assert_array_equal(comp.tokens[:n].cpu().numpy(), tok)
+    np.testing.assert_array_equal(comp.kept_slots[:n].cpu().numpy(), sl)
+    np.testing.assert_array_equal(comp.freed_slots[:nf].cpu().numpy(), fr)
+    assert verify.workspace_for(batch.B, DEV).error_word() == 0
+
+
+def test_invalid_arguments_raise_before_launch():
+    batch = random_batch(3, 4, 257, torch.bfloat16)
+    kw = batch.kwargs()
+    with pytest.raises(ValueError):
+        verify.verify_logits(**{**kw, "candidates": kw["candidates"][:, :15]})
+    with pytest.raises(ValueError):
+        verify.verify_logits(**{**kw, "top_k": kw["top_k"].long()})
+    with pytest.raises(ValueError):
+        verify.verify_logits(**{**kw, "draft_logits": kw["draft_logits"].float()})
