@@ -1,0 +1,394 @@
+#!/usr/bin/env python
+"""Benchmark: fused draft-block verification on B200 (config 1 of the benchmark plan).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl dspine|reference]
+
+One step = one dsv_verify_logits launch over the whole ragged batch: temperature / top-k /
+top-p / softmax of every verify row of the target and of the draft, the capped chain rejection,
+the residual bonus draw and the accept-compact of tokens and KV slots.  Inputs are seeded
+synthetic logits (dspine_b200.workloads), resident in HBM for ``value``; ``e2e`` times the same
+call with the inputs copied from pinned host memory and the outputs read back every step.
+
+Multi-GPU: verification has no exchange step (requests are independent), so each rank runs an
+independent replica on its own requests (weak scaling); no collective touches the data path.
+The only collectives are the barrier around the timed region and the max/sum of the results.
+
+``--impl reference`` times the reference algorithm on the host cores instead: the CPU
+restatement under oracle/ (the reference itself is Python/Triton and cannot run on the GPU box)
+on a bounded sample of the same workload, with every host thread.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "verified draft tokens/s at B=64, block 16, V=151936"
+UNIT = "tokens/s"
+L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
+FALLBACK_HBM_GBS = 6650.0
+REF_SAMPLE_REQUESTS = 16
+
+WORKLOADS = {
+    "config1": "ragged continuous batch: 64 requests, verify length U{1..16}, V=151936, bf16 "
+               "logits N(0,2.5^2)+8 spike, draft = target + N(0,1); T U[0,1.5] (25% 0), "
+               "top_k {off,1,20,50}, top_p U[0.8,1]; accept-compact of tokens + int32 KV slots",
+    "config0": "4 requests x 16, V=151936, fp32 logits, 2 greedy + 2 T=1",
+    "config4": "256 requests, SPS-capped verify lengths + early stop 0.3, V=151936, bf16",
+}
+
+# NVML clock-event reason bits (nvml.h: nvmlClocksEventReason*)
+_REASONS = {
+    0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+    0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+    0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown",
+    0x100: "display_clock_setting",
+}
+
+
+def parse_args():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=50)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--impl", choices=("dspine", "reference"), default="dspine")
+    p.add_argument("--config", choices=tuple(WORKLOADS), default="config1")
+    p.add_argument("--no-cpu-baseline", action="store_true",
+                   help="skip the CPU baseline leg (it is reported by default at N=1)")
+    return p.parse_args()
+
+
+def log(*a):
+    print(*a, file=sys.stderr, flush=True)
+
+
+def dist_env():
+    return (int(os.environ.get("RANK", "0")), int(os.environ.get("LOCAL_RANK", "0")),
+            int(os.environ.get("WORLD_SIZE", "1")))
+
+
+def measured_hbm_peak():
+    f = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(f.read_text())["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def profiled_traffic(config: str):
+    """DRAM bytes per launch of the verify kernel from the committed ncu summary, or None."""
+    f = ROOT / "profiles" / f"verify_kernel_{config}.md"
+    if not f.exists():
+        return None
+    for line in f.read_text().splitlines():
+        if line.strip().startswith("dram_bytes_per_launch:"):
+            try:
+                return float(line.split(":", 1)[1].split()[0])
+            except ValueError:
+                return None
+    return None
+
+
+def make_batch(config: str, rank: int, device):
+    from dspine_b200 import workloads
+    fn = getattr(workloads, config)
+    seed = {"config0": 0, "config1": 1, "config4": 4}[config] + 1000 * rank
+    return fn(seed=seed, device=device)
+
+
+class ClockSampler:
+    """Polls NVML for SM clock and clock-event reasons of one GPU while running."""
+
+    def __init__(self, torch_device):
+        self.samples = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._thread = None
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            import torch
+            props = torch.cuda.get_device_properties(torch_device)
+            bus = f"{props.pci_domain_id:08x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+            try:
+                self._h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                self._h = pynvml.nvmlDeviceGetHandleByIndex(torch_device.index or 0)
+            self._nvml = pynvml
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception as e:  # no NVML: report no clocks rather than fail the bench
+            log(f"clock sampling unavailable: {e}")
+            self._nvml = None
+
+    def _run(self):
+        nv = self._nvml
+        while not self._stop.is_set():
+            try:
+                mhz = nv.nvmlDeviceGetClockInfo(self._h, nv.NVML_CLOCK_SM)
+                try:
+                    bits = nv.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+                except AttributeError:
+                    bits = nv.nvmlDeviceGetCurrentClocksThrottleReasons(self._h)
+                self.samples.append((mhz, int(bits)))
+            except Exception:
+                pass
+            self._stop.wait(0.002)
+
+    def __enter__(self):
+        if self._nvml is not None:
+            self._thread = threading.Thread(target=self._run, daemon=True)
+            self._thread.start()
+        return self
+
+    def __exit__(self, *exc):
+        self._stop.set()
+        if self._thread is not None:
+            self._thread.join()
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [], "samples": 0}
+        mhz = [m for m, _ in self.samples]
+        bits = 0
+        for _, b in self.samples:
+            bits |= b
+        reasons = sorted(name for bit, name in _REASONS.items() if bits & bit and bit != 0x1)
+        return {"sm_mhz": statistics.median(mhz), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(mhz)}
+
+
+def cpu_port_time(batch, n_requests=None, nthreads=None):
+    """Seconds of one oracle run (the CPU restatement) over the first n requests."""
+    import oracle as O
+
+    def np_f32(t):
+        return t.detach().float().cpu().numpy()
+
+    def np_i(t):
+        return t.detach().cpu().numpy()
+    n = batch.B if n_requests is None else min(n_requests, batch.B)
+    tgt = np_f32(batch.target_logits)
+    drf = None if batch.draft_logits is None else np_f32(batch.draft_logits)
+    args = (np_i(batch.candidates)[:n], tgt, np_i(batch.target_rows)[:n], drf,
+            None if batch.draft_rows is None else np_i(batch.draft_rows)[:n],
+            np_f32(batch.temperature)[:n], np_i(batch.top_k)[:n], np_f32(batch.top_p)[:n],
+            np_i(batch.verify_lens)[:n], np_f32(batch.uniforms)[:n],
+            np_f32(batch.uniform_final)[:n], np_i(batch.prefix_lens)[:n])
+    tokens = int(batch.verify_lens[:n].sum())
+
+    def once():
+        t0 = time.perf_counter()
+        O.verify_logits(*args, nthreads=nthreads)
+        return time.perf_counter() - t0
+    return once, tokens
+
+
+def host_cores():
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def run_reference(args):
+    rank, _, world = dist_env()
+    if rank != 0:
+        return  # the CPU reference arm runs once, on rank 0
+    import torch
+    cores = host_cores()
+    torch.set_num_threads(cores)
+    batch = make_batch(args.config, 0, "cpu")
+    n = min(REF_SAMPLE_REQUESTS, batch.B)
+    once, tokens = cpu_port_time(batch, n, nthreads=cores)
+    for _ in range(args.warmup):
+        once()
+    times = [once() for _ in range(args.steps)]
+    step_s = sum(times) / len(times)
+    value = tokens / step_s
+    sample = (f"requests 0-{n - 1} of {args.config} ({tokens} verified tokens) per step, "
+              f"oracle port with {cores} OpenMP threads")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32+i64", "data": "synthetic",
+        "config": {"workload": f"{args.config}: {WORKLOADS[args.config]}",
+                   "sample_requests": n, "parallelism": "host cores"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def run_dspine(args):
+    import torch
+    rank, local_rank, world = dist_env()
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device (there is no CPU fallback)")
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300),
+                                device_id=dev)
+
+    from dspine_b200 import _lib, verify
+
+    lib = _lib.load()
+    batch = make_batch(args.config, rank, dev)
+    kw = batch.kwargs()
+    B = batch.B
+    out = verify.new_outputs(B, dev)
+    comp = verify.CompactOutputs.allocate(B, dev)
+    ws = verify.workspace_for(B, dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+
+    def step():
+        verify.verify_logits(**kw, outputs=out, slots=batch.slots, slot_rows=batch.slot_rows,
+                             compact=comp, workspace=ws)
+
+    def barrier():
+        if dist is not None:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize(dev)
+
+    for _ in range(max(args.warmup, 3)):
+        flush.zero_()
+        step()
+    torch.cuda.synchronize(dev)
+    if ws.error_word() != 0:
+        raise SystemExit("device error word set during warm-up")
+
+    # ---- device-timed steps (inputs resident in HBM, L2 flushed before each step) ----
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    launches0 = lib.dsv_launch_count()
+    sampler = ClockSampler(dev)
+    barrier()
+    with sampler:
+        for i in range(args.steps):
+            flush.zero_()
+            starts[i].record()
+            step()
+            ends[i].record()
+        barrier()
+    launches = lib.dsv_launch_count() - launches0
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = sum(step_ms)
+    tokens = batch.verified_tokens()
+    if dist is not None:
+        t = torch.tensor([total_ms, float(tokens), float(launches)], dtype=torch.float64, device=dev)
+        tmax = t.clone()
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        total_ms, all_tokens, all_launches = float(tmax[0]), float(t[1]), int(t[2])
+    else:
+        all_tokens, all_launches = float(tokens), launches
+    ms_per_step = total_ms / args.steps
+    value = all_tokens / (ms_per_step * 1e-3)
+
+    # ---- end to end: pinned host inputs -> device, verify, outputs -> host, every step ----
+    inputs = {**kw, "slots": batch.slots, "slot_rows": batch.slot_rows}
+    dev_in = {k: v for k, v in inputs.items() if v is not None}
+    host_in = {k: v.cpu().pin_memory() for k, v in dev_in.items()}
+    host_out = [o.cpu().pin_memory() for o in out]
+    h2d = sum(v.numel() * v.element_size() for v in host_in.values())
+    d2h = sum(o.numel() * o.element_size() for o in host_out)
+    e2e_steps = max(3, min(args.steps, 20))
+
+    def e2e_step():
+        for k, v in host_in.items():
+            dev_in[k].copy_(v, non_blocking=True)
+        verify.verify_logits(**dev_in, outputs=out, compact=comp, workspace=ws)
+        for h, o in zip(host_out, out):
+            h.copy_(o, non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+
+    e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    if dist is not None:
+        t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t[0])
+    e2e_value = all_tokens / (e2e_ms * 1e-3)
+    if ws.error_word() != 0:
+        raise SystemExit("device error word set during the timed region")
+
+    line = None
+    if rank == 0:
+        alg_bytes = batch.algorithmic_bytes()
+        kernel_ms = statistics.mean(step_ms)
+        achieved = alg_bytes / (kernel_ms * 1e-3) / 1e9
+        peak, peak_src = measured_hbm_peak()
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32+i64", "data": "synthetic",
+            "config": {"workload": f"{args.config}: {WORKLOADS[args.config]}",
+                       "requests_per_gpu": B, "vocab": batch.V,
+                       "verified_tokens_per_gpu": tokens,
+                       "logits_dtype": str(batch.target_logits.dtype).replace("torch.", ""),
+                       "parallelism": f"dp{world} (independent replicas)",
+                       "l2": "flushed before every timed step (256 MiB memset, untimed)"},
+            "clocks": sampler.summary(),
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": all_launches,
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                         "frac": achieved / peak, "traffic": profiled_traffic(args.config),
+                         "peak_source": peak_src, "kernel": "dsv::verify_kernel",
+                         "algorithmic_bytes_per_launch": alg_bytes,
+                         "kernel_ms": kernel_ms},
+        }
+    if dist is not None:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+    if rank == 0:
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(batch)
+        print(json.dumps(line), flush=True)
+
+
+def cpu_baseline(batch):
+    """Oracle port over the whole workload on every host core, repeated for ~10 s."""
+    cores = host_cores()
+    once, tokens = cpu_port_time(batch, None, nthreads=cores)
+    t, reps = 0.0, 0
+    while reps < 1 or (t < 10.0 and reps < 10):
+        t += once()
+        reps += 1
+    return {"value": tokens * reps / t, "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"whole workload ({tokens} verified tokens) x {reps} runs, "
+                      f"oracle port with {cores} OpenMP threads"}
+
+
+def main():
+    args = parse_args()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_dspine(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -7,6 +7,7 @@ is missing every operator raises, so a CUDA run can never silently take another 
 from __future__ import annotations
 
 import ctypes
+import os
 import re
 import threading
 from pathlib import Path
@@ -52,6 +53,7 @@ class CompactOut(ctypes.Structure):
 # argument types of every entry point (restype is int unless listed in _RESTYPES)
 _SIGNATURES = {
     "dsv_version": [],
+    "dsv_launch_count": [],
     "dsv_status_string": [c_int32],
     "dsv_verify_workspace_size": [c_int32, ctypes.POINTER(c_size_t)],
     "dsv_workspace_init": [c_void_p, c_size_t, c_void_p],
@@ -62,7 +64,8 @@ _SIGNATURES = {
                           c_void_p, c_void_p, ctypes.POINTER(CompactOut), c_void_p, c_size_t,
                           c_void_p],
 }
-_RESTYPES = {"dsv_version": ctypes.c_char_p, "dsv_status_string": ctypes.c_char_p}
+_RESTYPES = {"dsv_version": ctypes.c_char_p, "dsv_status_string": ctypes.c_char_p,
+             "dsv_launch_count": ctypes.c_uint64}
 
 
 class DSVError(RuntimeError):
@@ -76,7 +79,7 @@ class DSVError(RuntimeError):
 def declared_symbols() -> list[str]:
     """Entry points declared in include/dspine_b200.h."""
     text = HEADER.read_text()
-    return sorted(set(re.findall(r"^\s*(?:int|const char\*)\s+(dsv_\w+)\s*\(", text, re.M)))
+    return sorted(set(re.findall(r"^\s*(?:int|uint64_t|const char\*)\s+(dsv_\w+)\s*\(", text, re.M)))
 
 
 def load():
@@ -86,11 +89,13 @@ def load():
     with _lock:
         if _lib is not None:
             return _lib
-        if not LIB_PATH.exists():
+        # DSV_LIBRARY selects another build of the same C ABI (e.g. the index-checking one)
+        path = Path(os.environ.get("DSV_LIBRARY", LIB_PATH))
+        if not path.exists():
             raise RuntimeError(
-                f"{LIB_PATH} is missing: build it with `python -m dspine_b200.build` "
+                f"{path} is missing: build it with `python -m dspine_b200.build` "
                 "(the CUDA library is required; there is no CPU fallback)")
-        lib = ctypes.CDLL(str(LIB_PATH))
+        lib = ctypes.CDLL(str(path))
         for name, argtypes in _SIGNATURES.items():
             fn = getattr(lib, name)
             fn.argtypes = argtypes

@@ -47,32 +47,37 @@ def headers():
     return sorted(CSRC.glob("*.h")) + sorted(CSRC.glob("*.cuh")) + sorted((ROOT / "include").glob("*.h"))
 
 
-def build(verbose: bool = False, ptxas_info: bool = False) -> Path:
-    OUT_DIR.mkdir(parents=True, exist_ok=True)
-    OBJ_DIR.mkdir(parents=True, exist_ok=True)
+def build(verbose: bool = False, ptxas_info: bool = False, checked: bool = False) -> Path:
+    """Compile every csrc/*.cu and link the shared library.  ``checked`` builds the index-
+    checking variant (-DDSV_CHECKS) into _build/checked/ instead of the product library."""
+    out_dir = (ROOT / "_build" / "checked") if checked else OUT_DIR
+    obj_dir = OBJ_DIR.parent / ("obj_checked" if checked else "obj")
+    lib = out_dir / LIB.name
+    out_dir.mkdir(parents=True, exist_ok=True)
+    obj_dir.mkdir(parents=True, exist_ok=True)
+    extra = ["-DDSV_CHECKS"] if checked else []
     cc = nvcc()
     hdr_mtime = max((p.stat().st_mtime for p in headers()), default=0)
     objs = []
     for src in sources():
-        obj = OBJ_DIR / (src.stem + ".o")
+        obj = obj_dir / (src.stem + ".o")
         objs.append(obj)
         if obj.exists() and obj.stat().st_mtime >= max(src.stat().st_mtime, hdr_mtime):
             continue
-        cmd = [cc, *ARCH, *FLAGS, *_host_compiler_args(), "-c", str(src), "-o", str(obj)]
+        cmd = [cc, *ARCH, *FLAGS, *extra, *_host_compiler_args(), "-c", str(src), "-o", str(obj)]
         if ptxas_info:
             cmd += ["-Xptxas", "-v"]
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)
     newest = max(o.stat().st_mtime for o in objs)
-    if not LIB.exists() or LIB.stat().st_mtime < newest:
-        cmd = [cc, *ARCH, *_host_compiler_args(), "-shared", "-o", str(LIB), *map(str, objs)]
+    if not lib.exists() or lib.stat().st_mtime < newest:
+        cmd = [cc, *ARCH, *_host_compiler_args(), "-shared", "-o", str(lib), *map(str, objs)]
         if verbose:
             print(" ".join(cmd), flush=True)
         subprocess.run(cmd, check=True)
-    return LIB
+    return lib
 
 
 if __name__ == "__main__":
-    build(verbose=True, ptxas_info="-v" in sys.argv)
-    print(LIB)
+    print(build(verbose=True, ptxas_info="-v" in sys.argv, checked="--checked" in sys.argv))

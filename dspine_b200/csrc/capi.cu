@@ -1,6 +1,8 @@
 // capi.cu -- extern "C" entry points: host-side validation, then the kernel launchers.
 #include <cuda_runtime.h>
 
+#include <atomic>
+
 #include "../../include/dspine_b200.h"
 #include "dsv_common.cuh"
 #include "dsv_kernels.h"
@@ -9,11 +11,21 @@ namespace {
 
 inline bool aligned(const void* p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
+std::atomic<uint64_t> g_launches{0};
+
+// count the kernels an entry point enqueued (only after a successful launch)
+inline int counted(int status, int kernels) {
+    if (status == DSV_OK) g_launches.fetch_add((uint64_t)kernels, std::memory_order_relaxed);
+    return status;
+}
+
 }  // namespace
 
 extern "C" {
 
 const char* dsv_version(void) { return "dspine_b200 0.1.0 (sm_100a)"; }
+
+uint64_t dsv_launch_count(void) { return g_launches.load(std::memory_order_relaxed); }
 
 const char* dsv_status_string(int s) {
     switch (s) {
@@ -121,7 +133,7 @@ int dsv_verify_logits(int32_t batch, int32_t vocab, int32_t dtype, const int64_t
     a.ws = reinterpret_cast<dsv::WsHeader*>(base);
     a.done = reinterpret_cast<unsigned int*>(base + 64);
     a.res = reinterpret_cast<dsv::TaskResult*>(base + 64 + ((((size_t)batch * 4) + 63) & ~(size_t)63));
-    return dsv::launch_verify(a, dtype, (cudaStream_t)stream);
+    return counted(dsv::launch_verify(a, dtype, (cudaStream_t)stream), 1);
 }
 
 }  // extern "C"

@@ -38,6 +38,9 @@ typedef enum { DSV_BF16 = 0, DSV_F32 = 1 } dsv_dtype;
 /* Library version string and a readable name for a status code. */
 const char* dsv_version(void);
 const char* dsv_status_string(int status);
+/* Kernels this process has enqueued through the library so far (all entry points, all
+ * devices); a diagnostic for benchmarks.  No counterpart in the reference. */
+uint64_t dsv_launch_count(void);
 
 /* ---- workspace ----------------------------------------------------------------------------
  * Scratch for dsv_verify_logits: task counters and per-row decisions.  Zero it once after

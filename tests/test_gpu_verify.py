@@ -24,6 +24,8 @@ def run_kernel(batch, compact=False):
     kw = batch.kwargs()
     out = verify.verify_logits(**kw)
     torch.cuda.synchronize()
+    # no bulk-copy timeout, bad row, bad slot or (index-checking builds) failed index check
+    assert verify.workspace_for(batch.B, DEV).error_word() == 0
     return out
 
 
@@ -66,6 +68,35 @@ def test_ties_and_masked_logits(dtype):
     for seed in range(3):
         batch = random_batch(77 + seed, 12, 2053, dtype, quantize=True, neg_inf=seed == 1)
         assert_same(run_kernel(batch), oracle_verify(batch), f"ties seed={seed}")
+
+
+@pytest.mark.parametrize("V", [4099, 151936])
+def test_every_selection_path(V):
+    """Rows that resolve in the top window, rows whose nucleus needs the histogram levels,
+    top_k beyond the window, a window overflow (all-equal logits) and unfiltered rows."""
+    off = workloads.TOPK_OFF
+    params = [  # (temperature, top_k, top_p)
+        (1.5, off, 0.95), (0.3, off, 0.9), (1.0, 500, 1.0), (1.0, 500, 0.5),
+        (1.0, 192, 0.99), (0.7, 20, 0.3), (1.0, 20, 0.9), (1.0, off, 1.0),
+        (2.0, off, 0.999), (0.05, off, 0.8), (1.2, 7, 1.0), (0.9, 50, 0.85),
+    ]
+    B = len(params)
+    g = torch.Generator().manual_seed(V)
+    lens = torch.randint(2, 17, (B,), generator=g, dtype=torch.int32)
+    temperature, top_k, top_p = (torch.tensor(x) for x in zip(*params))
+    batch = workloads.build(lens, temperature.float(), top_k.int(), top_p.float(), V=V,
+                            dtype=torch.float32, seed=V + 1)
+    # request 6: every logit equal -> every element enters the top window (overflow path)
+    b = 6
+    t0, n = int(batch.target_rows[b]), int(lens[b])
+    batch.target_logits[t0:t0 + n] = 1.0
+    d0 = int(batch.draft_rows[b])
+    batch.draft_logits[d0:d0 + n - 1] = 1.0
+    batch.target_logits = batch.target_logits.to(torch.bfloat16)
+    batch.draft_logits = batch.draft_logits.to(torch.bfloat16)
+    batch = batch.to(DEV)
+    assert_same(run_kernel(batch), oracle_verify(batch), f"paths V={V}")
+    assert verify.workspace_for(batch.B, DEV).error_word() == 0
 
 
 def test_one_hot_q_without_draft_logits():
