@@ -132,7 +132,10 @@ int dsv_verify_logits(int32_t batch, int32_t vocab, int32_t dtype, const int64_t
     char* base = reinterpret_cast<char*>(workspace);
     a.ws = reinterpret_cast<dsv::WsHeader*>(base);
     a.done = reinterpret_cast<unsigned int*>(base + 64);
-    a.res = reinterpret_cast<dsv::TaskResult*>(base + 64 + ((((size_t)batch * 4) + 63) & ~(size_t)63));
+    a.res = reinterpret_cast<dsv::TaskResult*>(base + 64 + dsv::verify_done_bytes(batch));
+    a.desc = reinterpret_cast<dsv::RowDesc*>(base + dsv::verify_desc_offset(batch));
+    if (dsv::stream_supported(a, dtype))
+        return counted(dsv::launch_stream(a, (cudaStream_t)stream), 2);
     return counted(dsv::launch_verify(a, dtype, (cudaStream_t)stream), 1);
 }
 

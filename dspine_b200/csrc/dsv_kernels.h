@@ -17,13 +17,33 @@ struct WsHeader {
     unsigned int next;       // dynamic task counter
     unsigned int exited;     // clusters that left the task loop
     unsigned int finalized;  // requests finalized in this launch
-    unsigned int err;        // bit 0: bulk copy timed out; bit 1: bad row; bit 2: bad slot
+    unsigned int err;        // bit 0: bulk copy timed out; bit 1: bad row; bit 2: bad slot;
+                             // bit 3: a selection found no boundary; bit 4: tie cut not found
 };
 
-// Workspace layout: [WsHeader (64 B)][done: u32 x B, padded to 64 B][TaskResult x 16B]
+// Descriptor of one processed logit row (streaming path): p_i = exp2c((l_i - m) c) * inv_s
+// for kept elements (key > kstar, or key == kstar and index <= tie_cut), else 0; greedy rows
+// are one-hot at argmax.
+constexpr uint32_t kDescGreedy = 1u;
+struct RowDesc {
+    float m;
+    float c;
+    float inv_s;
+    uint32_t kstar;      // ordered 16-bit key of the boundary value
+    int32_t tie_cut;
+    int32_t argmax;
+    uint32_t flags;
+    uint32_t pad;
+};
+
+// Workspace layout: [WsHeader (64 B)][done: u32 x B, padded to 64 B][TaskResult x B x 16]
+//                   [RowDesc x B x 16 x 2]
+inline size_t verify_done_bytes(int B) { return ((size_t)B * 4 + 63) & ~(size_t)63; }
+inline size_t verify_desc_offset(int B) {
+    return 64 + verify_done_bytes(B) + (size_t)B * 16 * sizeof(TaskResult);
+}
 inline size_t verify_workspace_bytes(int B) {
-    size_t done = ((size_t)B * 4 + 63) & ~(size_t)63;
-    return 64 + done + (size_t)B * 16 * sizeof(TaskResult);
+    return verify_desc_offset(B) + (size_t)B * 16 * 2 * sizeof(RowDesc);
 }
 
 struct VerifyArgs {
@@ -63,9 +83,13 @@ struct VerifyArgs {
     WsHeader* ws;
     unsigned int* done;
     TaskResult* res;
+    RowDesc* desc;             // [B,16,2] row descriptors (streaming path)
 };
 
 // launchers (return a dsv::Status)
 int launch_verify(const VerifyArgs& a, int dtype, cudaStream_t stream);
+// streaming path (bf16 rows, B <= 1024, V <= 163776): row kernel + chain kernel
+bool stream_supported(const VerifyArgs& a, int dtype);
+int launch_stream(VerifyArgs a, cudaStream_t stream);
 
 }  // namespace dsv

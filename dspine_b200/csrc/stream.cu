@@ -1,0 +1,1598 @@
+// stream.cu -- streaming verification of bf16 logit rows (sm_100a).
+//
+// Two kernels replace the reference's build_dspine_target_probs + chain rejection
+// (runtime/worker.py:440-508, sampling/rejection.py:12-153) for bf16 logits:
+//
+//   row_kernel    one row (a target row, or the draft row of a sampled request) per task;
+//                 a cluster of 8 CTAs holds the row in registers (one eighth per CTA, 16-byte
+//                 loads, the next task's slice prefetched into L2) and computes its descriptor:
+//                 max, exact 2^-40 fixed-point softmax sum, and the kept set of the joint
+//                 top-k / top-p filter as (boundary key, tie cut).  Passes:
+//                   P1  bf16x2 max                                   (every row)
+//                   P2  exp + fixed-point split, packed f32x2        (sampled rows)
+//                       + candidate window (top-k <= 64), or
+//                       + 32 y-bins with exact masses in thread-private shared accumulators
+//                   L2  31 sub-bins of the boundary bin (compacted list when it fits)
+//                   L3  per-key counts of the boundary sub-bin, walked with F(key)
+//                   tie the n-th occurrence of the boundary key in index order
+//   chain_kernel  one cluster per request: the capped chain from the descriptors (one logit
+//                 load per step), the residual (p - q)+ draw over target row a and draft row a,
+//                 the five outputs and, for the last request, the accept-compact.
+//
+// Arithmetic is the canonical one of dsv_common.cuh (exp2c, fix, scale_floor), so the result
+// equals the CPU oracle bit for bit.  Bulk passes clamp y at -64 before the exponent trick:
+// every y below -41.5 has fix(exp2(y)) = 0, so the clamp never changes a fix value; exact
+// probabilities (chain, residual) use the unclamped exp2c with its y < -125 -> 0 rule.
+#include <cooperative_groups.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "dsv_common.cuh"
+#include "dsv_kernels.h"
+
+namespace cg = cooperative_groups;
+
+namespace dsv {
+namespace st {
+
+constexpr int kCS = 8;           // CTAs per cluster: one row is split into 8 slices
+constexpr int kNT = 256;         // threads per CTA
+constexpr int kNW = kNT / 32;    // warps per CTA
+constexpr int kBins = 32;        // level-1 bins: min(rne(-0.75 y), 31)
+constexpr int kSub = 31;         // level-2 bins: rne(-22.5 y) - 30 b1 + 15, clamped to [0, 30]
+constexpr int kWinK = kCS * kNW; // top-k rows with k <= 64 select inside the candidate window
+constexpr int kWinCap = 128;     // window entries per CTA
+constexpr int kWinTotal = 512;   // window entries per row
+constexpr int kListCap = 4096;   // level-2 compaction list per CTA
+constexpr int kKeyChunk = 512;   // keys per level-3 histogram chunk
+constexpr int kMaxB = 1024;      // requests per launch handled by this path
+
+enum Cat : int { kGreedy = 0, kKeepAll = 1, kWindow = 2, kBinned = 3 };
+
+constexpr uint32_t kFill = 0xFF80FF80u;  // two bf16 -inf: slots outside the slice
+constexpr float kS1 = 0.75f;             // level-1 scale (exact)
+constexpr float kS2 = 22.5f;             // level-2 scale = 30 * kS1 (exact)
+constexpr float kTwo23 = 8388608.0f;
+
+// ---------------------------------------------------------------------------------------
+// small helpers
+
+__device__ __forceinline__ void cluster_barrier() {
+    // non-.aligned forms: correct even if a warp reaches the barrier diverged
+    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
+}
+
+__device__ __forceinline__ uint32_t okey(uint32_t u16) { return Elem<__nv_bfloat16>::key(u16); }
+__device__ __forceinline__ uint32_t key_bits(uint32_t k) {
+    return (k & 0x8000u) ? (k & 0x7FFFu) : (~k & 0xFFFFu);
+}
+__device__ __forceinline__ float bf(uint32_t u16) { return __uint_as_float(u16 << 16); }
+
+__device__ __forceinline__ uint32_t bf2_ge(uint32_t a, uint32_t b) {
+    return __hge2_mask(*reinterpret_cast<const __nv_bfloat162*>(&a),
+                       *reinterpret_cast<const __nv_bfloat162*>(&b));
+}
+__device__ __forceinline__ uint32_t bf2_le(uint32_t a, uint32_t b) {
+    return __hle2_mask(*reinterpret_cast<const __nv_bfloat162*>(&a),
+                       *reinterpret_cast<const __nv_bfloat162*>(&b));
+}
+__device__ __forceinline__ uint32_t bf2_eq(uint32_t a, uint32_t b) {
+    return __heq2_mask(*reinterpret_cast<const __nv_bfloat162*>(&a),
+                       *reinterpret_cast<const __nv_bfloat162*>(&b));
+}
+__device__ __forceinline__ uint32_t bf2_max(uint32_t a, uint32_t b) {
+    __nv_bfloat162 r = __hmax2(*reinterpret_cast<const __nv_bfloat162*>(&a),
+                               *reinterpret_cast<const __nv_bfloat162*>(&b));
+    return *reinterpret_cast<uint32_t*>(&r);
+}
+
+// y of one element, clamped at -64 (bulk passes; see file header)
+__device__ __forceinline__ float y_clamped(float l, float m, float c) {
+    return fmaxf(__fmul_rn(__fadd_rn(l, -m), c), -64.0f);
+}
+__device__ __forceinline__ int bin1_of(float yc) {
+    const float t = __fmaf_rn(yc, -kS1, kTwo23);
+    return (int)min(__float_as_uint(t) - 0x4B000000u, (uint32_t)(kBins - 1));
+}
+__device__ __forceinline__ int bin2_of(float yc, int b1) {
+    const float t = __fmaf_rn(yc, -kS2, kTwo23);
+    const int v = (int)(__float_as_uint(t) - 0x4B000000u) - 30 * b1 + 15;
+    return v < 0 ? 0 : (v > kSub - 1 ? kSub - 1 : v);
+}
+// fix(exp2(yc)) for yc in [-64, 0]: the split below, scalar form
+__device__ __forceinline__ uint64_t fix_of_y(float yc) {
+    const float M17 = 12582912.0f + 17.0f;
+    const float t = __fadd_rn(yc, M17);
+    const float f = __fsub_rn(yc, __fsub_rn(t, M17));
+    float p = __uint_as_float(0x3920fddcu);
+    p = __fmaf_rn(p, f, __uint_as_float(0x3aaf9f2bu));
+    p = __fmaf_rn(p, f, __uint_as_float(0x3c1d96a6u));
+    p = __fmaf_rn(p, f, __uint_as_float(0x3d635774u));
+    p = __fmaf_rn(p, f, __uint_as_float(0x3e75fdeeu));
+    p = __fmaf_rn(p, f, __uint_as_float(0x3f317218u));
+    p = __fmaf_rn(p, f, 1.0f);
+    const float x = __uint_as_float(__float_as_uint(p) + (__float_as_uint(t) << 23));  // e * 2^17
+    const float h = __fadd_rn(x, kTwo23);
+    const float r = __fsub_rn(x, __fsub_rn(h, kTwo23));
+    const float lo = __fmaf_rn(r, kTwo23, 12582912.0f);
+    const uint32_t hi = __float_as_uint(h) - 0x4B000000u;
+    const int32_t lv = (int32_t)(__float_as_uint(lo) - 0x4B400000u);
+    return (uint64_t)((int64_t)hi * 8388608 + lv);
+}
+
+// packed pair: yc (clamped y) and the raw float bits of h = 2^23 + rne(x), lo = 1.5*2^23 +
+// rne((x - rne(x)) * 2^23) for both halves of a bf16x2 word (x = exp2(yc) * 2^17)
+struct Pair {
+    float2 yc;
+    uint32_t h0, h1, l0, l1;
+};
+
+__device__ __forceinline__ Pair exp_pair(uint32_t w, float2 nm, float2 c2) {
+    const float2 l = make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
+    float2 y = __fmul2_rn(__fadd2_rn(l, nm), c2);
+    y.x = fmaxf(y.x, -64.0f);
+    y.y = fmaxf(y.y, -64.0f);
+    const float M17 = 12582912.0f + 17.0f;
+    const float2 t = __fadd2_rn(y, make_float2(M17, M17));
+    const float2 tm = __fadd2_rn(t, make_float2(-M17, -M17));
+    const float2 f = __ffma2_rn(tm, make_float2(-1.0f, -1.0f), y);
+    float2 p = make_float2(__uint_as_float(0x3920fddcu), __uint_as_float(0x3920fddcu));
+    p = __ffma2_rn(p, f, make_float2(__uint_as_float(0x3aaf9f2bu), __uint_as_float(0x3aaf9f2bu)));
+    p = __ffma2_rn(p, f, make_float2(__uint_as_float(0x3c1d96a6u), __uint_as_float(0x3c1d96a6u)));
+    p = __ffma2_rn(p, f, make_float2(__uint_as_float(0x3d635774u), __uint_as_float(0x3d635774u)));
+    p = __ffma2_rn(p, f, make_float2(__uint_as_float(0x3e75fdeeu), __uint_as_float(0x3e75fdeeu)));
+    p = __ffma2_rn(p, f, make_float2(__uint_as_float(0x3f317218u), __uint_as_float(0x3f317218u)));
+    p = __ffma2_rn(p, f, make_float2(1.0f, 1.0f));
+    const float2 x = make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
+                                 __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
+    const float2 h = __fadd2_rn(x, make_float2(kTwo23, kTwo23));
+    const float2 hm = __fadd2_rn(h, make_float2(-kTwo23, -kTwo23));
+    const float2 r = __ffma2_rn(hm, make_float2(-1.0f, -1.0f), x);
+    const float2 lo = __ffma2_rn(r, make_float2(kTwo23, kTwo23), make_float2(12582912.0f, 12582912.0f));
+    Pair o;
+    o.yc = y;
+    o.h0 = __float_as_uint(h.x);
+    o.h1 = __float_as_uint(h.y);
+    o.l0 = __float_as_uint(lo.x);
+    o.l1 = __float_as_uint(lo.y);
+    return o;
+}
+
+// exact probability of element value l under a row descriptor (oracle or_row_prob)
+__device__ __forceinline__ float row_prob(const RowDesc& d, float l, uint32_t u16, int i) {
+    if (d.flags & kDescGreedy) return i == d.argmax ? 1.0f : 0.0f;
+    const uint32_t k = okey(u16);
+    const bool kept = (k > d.kstar) || (k == d.kstar && i <= d.tie_cut);
+    if (!kept) return 0.0f;
+    return __fmul_rn(exp2c(__fmul_rn(__fadd_rn(l, -d.m), d.c)), d.inv_s);
+}
+
+// ---------------------------------------------------------------------------------------
+// shared memory of the row kernel
+
+struct Pub {                       // published at an exchange, read by the cluster (DSMEM)
+    uint32_t maxkey;               // CTA max key
+    int32_t first;                 // first index of the CTA max (greedy rows)
+    uint32_t wmax[kNW];            // warp max keys (window threshold)
+    uint32_t nwin;                 // window entries of this CTA (kWinCap + 1: overflow)
+    uint32_t flag;                 // per-exchange flag (tie: occurrences of the boundary key)
+    unsigned long long S;          // partial fixed-point sum
+    unsigned long long mass[kBins];
+    uint32_t cnt[kBins];
+};
+
+struct RowSmem {
+    Pub pub[2];
+    uint32_t win[kWinCap];         // window entries: key << 16 | slice-local index
+    uint32_t khist[kKeyChunk];     // level-3 key counts of this CTA
+    uint32_t bcnt[kBins];          // local bin counts (atomics)
+    unsigned long long red64[kNW];
+    uint32_t red32[kNW * 2];
+    int32_t task[8];               // decoded task (broadcast)
+    float taskf[4];
+    int32_t sel[16];               // selection state (broadcast inside the CTA)
+    unsigned long long self64[8];
+    uint32_t nlist;
+    int32_t first_min;
+    int pre[3][kMaxB + 1];         // task prefix per group (binned, keep-all/window, greedy)
+    uint32_t req[kMaxB];           // per request: cat | cap << 4
+    alignas(16) uint2 acc[kBins * kNT];  // thread-private bin accumulators / gather area
+    alignas(16) uint32_t list[kListCap]; // level-2 compaction list: bits << 16 | local index
+};
+// the accumulator region is cleared with 16-byte stores
+static_assert(offsetof(RowSmem, acc) % 16 == 0, "acc must be 16-byte aligned");
+
+struct TaskInfo {
+    int b, s, kind, cat, cap;
+    long long row;     // row index in its tensor (-1: invalid)
+    float T, p, c;
+    int k;
+};
+
+__device__ __forceinline__ int clamp_cap(int c) { return c < 1 ? 1 : (c > kT ? kT : c); }
+
+__device__ int request_cat(const VerifyArgs& a, int b, float& c_out) {
+    const float T = a.temperature[b];
+    const int k = a.top_k[b];
+    const float c = log2e_over(T);
+    c_out = c;
+    if (is_greedy(T, k, c)) return kGreedy;
+    if (k >= a.V && !(a.top_p[b] < 1.0f)) return kKeepAll;
+    if (k <= kWinK) return kWindow;
+    return kBinned;
+}
+
+// every CTA builds the same task table: binned rows first, then keep-all/window, then greedy
+__device__ void build_plan(const VerifyArgs& a, RowSmem* sh) {
+    const int tid = threadIdx.x;
+    for (int b = tid; b < a.B; b += kNT) {
+        float c;
+        const int cat = request_cat(a, b, c);
+        const int cap = clamp_cap(a.caps[b]);
+        sh->req[b] = (uint32_t)cat | ((uint32_t)cap << 4);
+    }
+    __syncthreads();
+    if (tid < 32) {
+        int run[3] = {0, 0, 0};
+        for (int b0 = 0; b0 < a.B; b0 += 32) {
+            const int b = b0 + tid;
+            int n[3] = {0, 0, 0};
+            if (b < a.B) {
+                const int cat = (int)(sh->req[b] & 15u);
+                const int cap = (int)(sh->req[b] >> 4);
+                const int rows = cap + ((cat != kGreedy && a.drf != nullptr) ? cap - 1 : 0);
+                const int g = cat == kBinned ? 0 : (cat == kGreedy ? 2 : 1);
+                n[g] = rows;
+            }
+#pragma unroll
+            for (int g = 0; g < 3; ++g) {
+                const int inc = (int)warp_incl_u32((uint32_t)n[g]);
+                if (b < a.B) sh->pre[g][b + 1] = run[g] + inc;
+                run[g] += __shfl_sync(0xffffffffu, inc, 31);
+            }
+        }
+        if (tid == 0) {
+            sh->pre[0][0] = 0;
+            sh->pre[1][0] = 0;
+            sh->pre[2][0] = 0;
+        }
+    }
+    __syncthreads();
+}
+
+__device__ int total_tasks(const VerifyArgs& a, const RowSmem* sh) {
+    return sh->pre[0][a.B] + sh->pre[1][a.B] + sh->pre[2][a.B];
+}
+
+__device__ TaskInfo decode_task(const VerifyArgs& a, const RowSmem* sh, int t) {
+    int g = 0;
+    int local = t;
+    while (g < 2 && local >= sh->pre[g][a.B]) {
+        local -= sh->pre[g][a.B];
+        ++g;
+    }
+    // largest b with pre[g][b] <= local
+    int lo = 0, hi = a.B - 1;
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (sh->pre[g][mid] <= local) lo = mid; else hi = mid - 1;
+    }
+    TaskInfo ti;
+    ti.b = lo;
+    const int r = local - sh->pre[g][lo];
+    ti.cat = (int)(sh->req[lo] & 15u);
+    ti.cap = (int)(sh->req[lo] >> 4);
+    ti.kind = r < ti.cap ? 0 : 1;
+    ti.s = ti.kind == 0 ? r : r - ti.cap;
+    const long long base = ti.kind == 0 ? a.tgt_row[ti.b] : a.drf_row[ti.b];
+    const long long lim = ti.kind == 0 ? a.tgt_rows : a.drf_rows;
+    const long long row = base + ti.s;
+    ti.row = (row >= 0 && row < lim) ? row : -1;
+    ti.T = a.temperature[ti.b];
+    ti.k = a.top_k[ti.b];
+    ti.p = a.top_p[ti.b];
+    ti.c = log2e_over(ti.T);
+    return ti;
+}
+
+// geometry of slice q of a row: elements [e0, e1), vector v covers [e0 - off + 8v, +8)
+struct Slice {
+    const uint16_t* rowp;
+    int e0, e1, off, nv;
+};
+
+__device__ __forceinline__ Slice slice_of(const VerifyArgs& a, const TaskInfo& ti, int q, int L) {
+    Slice sl;
+    const uint16_t* base = reinterpret_cast<const uint16_t*>(ti.kind == 0 ? a.tgt : a.drf);
+    sl.rowp = base + (ti.row < 0 ? 0 : ti.row) * a.stride;
+    sl.e0 = min(q * L, a.V);
+    sl.e1 = min(sl.e0 + L, a.V);
+    sl.off = (int)((reinterpret_cast<uintptr_t>(sl.rowp) & 15u) >> 1);
+    sl.nv = (ti.row < 0 || sl.e1 <= sl.e0) ? 0 : (sl.e1 - sl.e0 + sl.off + 7) >> 3;
+    return sl;
+}
+
+template <int NVT>
+__device__ __forceinline__ void load_slice(const Slice& sl, uint4 (&w)[NVT]) {
+    const int tid = threadIdx.x;
+    const uint4* src = reinterpret_cast<const uint4*>(sl.rowp + sl.e0 - sl.off);
+#pragma unroll
+    for (int j = 0; j < NVT; ++j) {
+        const int v = j * kNT + tid;
+        if (v < sl.nv) w[j] = __ldg(src + v);
+        else w[j] = make_uint4(kFill, kFill, kFill, kFill);
+    }
+    // mask the halves of the first and last vector that lie outside [e0, e1)
+#pragma unroll
+    for (int j = 0; j < NVT; ++j) {
+        const int v = j * kNT + tid;
+        if (v < sl.nv && (v == 0 || v == sl.nv - 1)) {
+            uint32_t* u = reinterpret_cast<uint32_t*>(&w[j]);
+#pragma unroll
+            for (int h = 0; h < 8; ++h) {
+                const int e = sl.e0 - sl.off + 8 * v + h;
+                if (e < sl.e0 || e >= sl.e1) {
+                    const uint32_t mask = (h & 1) ? 0xFFFF0000u : 0x0000FFFFu;
+                    u[h >> 1] = (u[h >> 1] & ~mask) | (kFill & mask);
+                }
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ void prefetch_l2(const Slice& sl) {
+    if (sl.nv <= 0) return;
+    const char* p = reinterpret_cast<const char*>(sl.rowp + sl.e0 - sl.off);
+    uint32_t bytes = (uint32_t)sl.nv * 16u;
+    // bulk prefetch: 16-byte aligned start, size a multiple of 16
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
+}
+
+// element index (within the row) of half h of register vector j of this thread
+__device__ __forceinline__ int elem_index(const Slice& sl, int j, int h) {
+    return sl.e0 - sl.off + 8 * (j * kNT + (int)threadIdx.x) + h;
+}
+__device__ __forceinline__ bool elem_valid(const Slice& sl, int e) { return e >= sl.e0 && e < sl.e1; }
+
+// ---- CTA reductions ---------------------------------------------------------------------
+
+__device__ __forceinline__ unsigned long long cta_sum_u64(unsigned long long v, RowSmem* sh) {
+    v = warp_sum_u64(v);
+    const int w = threadIdx.x >> 5;
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) sh->red64[w] = v;
+    __syncthreads();
+    unsigned long long s = 0;
+#pragma unroll
+    for (int i = 0; i < kNW; ++i) s += sh->red64[i];
+    return s;
+}
+
+// ---------------------------------------------------------------------------------------
+// selection walk over groups in rank order (bins, sub-bins): first group where the count
+// reaches k or the mass passes thr
+
+struct Walk {
+    int group;                 // -1: not found
+    unsigned long long cnt;    // elements ranked before the group
+    unsigned long long mass;   // their fixed-point mass
+};
+
+// one warp; cnt/mass arrays of n <= 32 groups
+__device__ Walk walk_groups(const uint32_t* cnt, const unsigned long long* mass, int n,
+                            unsigned long long cnt0, unsigned long long mass0, long long k,
+                            long long thr) {
+    const int lane = threadIdx.x & 31;
+    unsigned long long c = lane < n ? cnt[lane] : 0ull;
+    unsigned long long m = lane < n ? mass[lane] : 0ull;
+    unsigned long long ci = c, mi = m;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const unsigned long long a = __shfl_up_sync(0xffffffffu, ci, o);
+        const unsigned long long bm = __shfl_up_sync(0xffffffffu, mi, o);
+        if (lane >= o) { ci += a; mi += bm; }
+    }
+    const unsigned long long cb = cnt0 + ci - c, mb = mass0 + mi - m;  // before the group
+    const bool stop = lane < n && c > 0 &&
+                      ((long long)(cb + c) >= k || (long long)(mb + m) > thr);
+    const uint32_t bal = __ballot_sync(0xffffffffu, stop);
+    Walk wk;
+    if (bal == 0) {
+        wk.group = -1;
+        wk.cnt = cnt0 + __shfl_sync(0xffffffffu, ci, 31);
+        wk.mass = mass0 + __shfl_sync(0xffffffffu, mi, 31);
+        return wk;
+    }
+    const int g = __ffs(bal) - 1;
+    wk.group = g;
+    wk.cnt = __shfl_sync(0xffffffffu, cb, g);
+    wk.mass = __shfl_sync(0xffffffffu, mb, g);
+    return wk;
+}
+
+// ---------------------------------------------------------------------------------------
+// the row kernel
+
+template <int NVT>
+struct RowCtx {
+    const VerifyArgs* a;
+    RowSmem* sh;
+    cg::cluster_group* cl;
+    int rank;
+    int L;
+    unsigned ex;   // exchange counter (buffer parity)
+};
+
+template <int NVT>
+__device__ __forceinline__ Pub* remote_pub(RowCtx<NVT>& cx, int q, unsigned ex) {
+    return cx.cl->map_shared_rank(&cx.sh->pub[ex & 1], q);
+}
+
+// write a row descriptor
+__device__ __forceinline__ void put_desc(const VerifyArgs& a, const TaskInfo& ti, float m,
+                                         uint32_t kstar, int tie, unsigned long long skept,
+                                         int argmax, uint32_t flags) {
+    RowDesc d;
+    d.m = m;
+    d.c = ti.c;
+    d.inv_s = (flags & kDescGreedy) ? 1.0f : inv_from_fix(skept);
+    d.kstar = kstar;
+    d.tie_cut = tie;
+    d.argmax = argmax;
+    d.flags = flags;
+    d.pad = 0;
+    a.desc[(ti.b * kT + ti.s) * 2 + ti.kind] = d;
+}
+
+// exact kept-set resolution from per-key counts: walk keys hi..lo (one warp)
+struct KeyStop {
+    int found;
+    uint32_t key;
+    unsigned long long cnt;    // before the key
+    unsigned long long mass;   // before the key
+    uint32_t count;            // elements with this key
+    unsigned long long F;      // fix value of one element with this key
+};
+
+__device__ KeyStop walk_keys(const uint32_t* counts, uint32_t khi, int n, float m, float c,
+                             unsigned long long cnt0, unsigned long long mass0, long long k,
+                             long long thr) {
+    const int lane = threadIdx.x & 31;
+    KeyStop ks;
+    ks.found = 0;
+    ks.cnt = cnt0;
+    ks.mass = mass0;
+    for (int base = 0; base < n; base += 32) {
+        const int i = base + lane;                 // i-th key from the top
+        const uint32_t key = khi - (uint32_t)i;
+        const uint32_t cc = i < n ? counts[i] : 0u;
+        unsigned long long F = 0;
+        if (cc) F = fix_of_y(y_clamped(bf(key_bits(key)), m, c));
+        const unsigned long long mm = F * cc;
+        unsigned long long ci = cc, mi = mm;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned long long a = __shfl_up_sync(0xffffffffu, ci, o);
+            const unsigned long long b = __shfl_up_sync(0xffffffffu, mi, o);
+            if (lane >= o) { ci += a; mi += b; }
+        }
+        const unsigned long long cb = ks.cnt + ci - cc, mb = ks.mass + mi - mm;
+        const bool stop = cc > 0 && ((long long)(cb + cc) >= k || (long long)(mb + mm) > thr);
+        const uint32_t bal = __ballot_sync(0xffffffffu, stop);
+        if (bal) {
+            const int g = __ffs(bal) - 1;
+            ks.found = 1;
+            ks.key = __shfl_sync(0xffffffffu, key, g);
+            ks.cnt = __shfl_sync(0xffffffffu, cb, g);
+            ks.mass = __shfl_sync(0xffffffffu, mb, g);
+            ks.count = __shfl_sync(0xffffffffu, cc, g);
+            ks.F = __shfl_sync(0xffffffffu, F, g);
+            return ks;
+        }
+        ks.cnt += __shfl_sync(0xffffffffu, ci, 31);
+        ks.mass += __shfl_sync(0xffffffffu, mi, 31);
+    }
+    return ks;
+}
+
+// composite bin index of a key (level 1 and level 2); over keys of values in [-inf, m] it is
+// non-increasing in the key (y is non-decreasing in the value and both bins round -0.75 y)
+__device__ __forceinline__ int composite_bin(uint32_t key, float m, float c) {
+    const float yc = y_clamped(bf(key_bits(key)), m, c);
+    const int b1 = bin1_of(yc);
+    return b1 * kSub + bin2_of(yc, b1);
+}
+
+// keys in [klo, khi] within [kmin, kmax] (the keys of -inf and of the row max) are exactly
+// those whose composite bin equals target
+__device__ void key_range(int target, uint32_t kmin, uint32_t kmax, float m, float c,
+                          uint32_t& klo, uint32_t& khi) {
+    // largest key with bin >= target
+    uint32_t lo = kmin, hi = kmax;
+    while (lo < hi) {
+        const uint32_t mid = (lo + hi + 1) >> 1;
+        if (composite_bin(mid, m, c) >= target) lo = mid; else hi = mid - 1;
+    }
+    khi = lo;
+    // smallest key with bin <= target
+    lo = kmin;
+    hi = kmax;
+    while (lo < hi) {
+        const uint32_t mid = (lo + hi) >> 1;
+        if (composite_bin(mid, m, c) <= target) hi = mid; else lo = mid + 1;
+    }
+    klo = lo;
+}
+
+template <int NVT>
+__global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    RowSmem* sh = reinterpret_cast<RowSmem*>(smem_raw);
+    cg::cluster_group cluster = cg::this_cluster();
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    RowCtx<NVT> cx;
+    cx.a = &a;
+    cx.sh = sh;
+    cx.cl = &cluster;
+    cx.rank = (int)cluster.block_rank();
+    cx.L = a.slice;
+    cx.ex = 0;
+    const int cid = blockIdx.x / kCS;
+
+    build_plan(a, sh);
+    const int ntask = total_tasks(a, sh);
+
+    uint4 w[NVT];
+    int it = 0;
+    for (int t = cid; t < ntask; t += a.num_clusters, ++it) {
+        const TaskInfo ti = decode_task(a, sh, t);
+        const int leader = it % kCS;
+        const bool lead = cx.rank == leader;
+        if (ti.row < 0 && tid == 0 && cx.rank == 0) atomicOr(&a.ws->err, 2u);
+        const Slice sl = slice_of(a, ti, cx.rank, cx.L);
+        load_slice<NVT>(sl, w);
+        if (tid == 0 && t + a.num_clusters < ntask) {
+            const TaskInfo tn = decode_task(a, sh, t + a.num_clusters);
+            if (tn.row >= 0) prefetch_l2(slice_of(a, tn, cx.rank, cx.L));
+        }
+
+        // ---- P1: max ----------------------------------------------------------------------
+        uint32_t mx = kFill;
+#pragma unroll
+        for (int j = 0; j < NVT; ++j) {
+            mx = bf2_max(mx, w[j].x);
+            mx = bf2_max(mx, w[j].y);
+            mx = bf2_max(mx, w[j].z);
+            mx = bf2_max(mx, w[j].w);
+        }
+        const uint32_t k0 = okey(mx & 0xFFFFu), k1 = okey(mx >> 16);
+        const uint32_t tkey = k0 > k1 ? k0 : k1;
+        const uint32_t wkey = __reduce_max_sync(0xffffffffu, tkey);
+        Pub& pb = sh->pub[cx.ex & 1];
+        if (lane == 0) sh->red32[wid] = wkey;
+        if (tid == 0) sh->first_min = 0x7fffffff;
+        __syncthreads();
+        uint32_t ckey = 0;
+#pragma unroll
+        for (int i = 0; i < kNW; ++i) ckey = max(ckey, sh->red32[i]);
+        if (ti.cat == kGreedy && tkey == ckey) {
+            // first element of this thread equal to the CTA max, in index order (j, half)
+            const uint32_t cb = key_bits(ckey);
+            const uint32_t c2 = cb | (cb << 16);
+            int best = 0x7fffffff;
+#pragma unroll
+            for (int j = 0; j < NVT; ++j) {
+                const uint32_t* u = reinterpret_cast<const uint32_t*>(&w[j]);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const uint32_t eq = bf2_eq(u[q], c2);
+                    if (eq && best == 0x7fffffff) {
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const int e = elem_index(sl, j, 2 * q + h);
+                            if ((eq & (h ? 0xFFFF0000u : 0x0000FFFFu)) && best == 0x7fffffff &&
+                                elem_valid(sl, e))
+                                best = e;
+                        }
+                    }
+                }
+            }
+            if (best != 0x7fffffff) atomicMin(&sh->first_min, best);
+        }
+        __syncthreads();
+        if (tid == 0) {
+            pb.maxkey = ckey;
+            pb.first = sh->first_min;
+        }
+        if (tid < kNW) pb.wmax[tid] = sh->red32[tid];
+        cluster_barrier();  // exchange 1
+        const unsigned ex1 = cx.ex++;
+        if (tid < 32) {
+            // lanes 0..7 read one CTA each; the max key and the first index among its holders
+            uint32_t k = 0;
+            int f = 0x7fffffff;
+            if (lane < kCS) {
+                const Pub* rp = remote_pub(cx, lane, ex1);
+                k = rp->maxkey;
+                f = rp->first;
+            }
+            const uint32_t mk = __reduce_max_sync(0xffffffffu, k);
+            const int fa = __reduce_min_sync(0xffffffffu, k == mk ? f : 0x7fffffff);
+            if (lane == 0) {
+                sh->sel[10] = (int)mk;
+                sh->sel[11] = fa;
+            }
+        }
+        __syncthreads();
+        const uint32_t mkey = (uint32_t)sh->sel[10];
+        const int argmax = sh->sel[11];
+        const float m = bf(key_bits(mkey));
+
+        if (ti.cat == kGreedy) {
+            if (lead && tid == 0) put_desc(a, ti, m, mkey, argmax, 1ull << kFixBits,
+                                           argmax == 0x7fffffff ? 0 : argmax, kDescGreedy);
+            continue;
+        }
+
+        // ---- window threshold (k-th largest warp maximum of the cluster) -----------------
+        int cat = ti.cat;
+        const long long kk = ti.k < a.V ? (long long)ti.k : (long long)a.V;
+        uint32_t tau = 0;
+        if (cat == kWindow) {
+            if (tid < 32) {
+                // 64 warp maxima, two per lane
+                const Pub* r0 = remote_pub(cx, lane >> 3, ex1);
+                const Pub* r1 = remote_pub(cx, 4 + (lane >> 3), ex1);
+                const uint32_t x0 = r0->wmax[lane & 7], x1 = r1->wmax[lane & 7];
+                int ge0 = 0, ge1 = 0;
+                for (int i = 0; i < 32; ++i) {
+                    const uint32_t y0 = __shfl_sync(0xffffffffu, x0, i);
+                    const uint32_t y1 = __shfl_sync(0xffffffffu, x1, i);
+                    ge0 += (y0 >= x0) + (y1 >= x0);
+                    ge1 += (y0 >= x1) + (y1 >= x1);
+                }
+                uint32_t cand = 0;
+                if (ge0 >= kk) cand = x0;
+                if (ge1 >= kk && x1 > cand) cand = x1;
+                cand = __reduce_max_sync(0xffffffffu, cand);
+                if (lane == 0) sh->sel[0] = (int)cand;
+            }
+            if (tid == 0) sh->nlist = 0;
+            __syncthreads();
+            tau = (uint32_t)sh->sel[0];
+        }
+
+        // ---- P2: exp pass -------------------------------------------------------------------
+        const float2 nm = make_float2(-m, -m), c2 = make_float2(ti.c, ti.c);
+        const uint32_t taub = key_bits(tau);
+        const uint32_t tau2 = taub | (taub << 16);
+        if (cat == kBinned) {
+            uint4* az = reinterpret_cast<uint4*>(sh->acc);
+            for (int i = tid; i < kBins * kNT / 2; i += kNT) az[i] = make_uint4(0, 0, 0, 0);
+            if (tid < kBins) sh->bcnt[tid] = 0;
+            __syncthreads();
+        }
+        uint32_t hs = 0, ls = 0;
+#pragma unroll
+        for (int j = 0; j < NVT; ++j) {
+            const uint32_t* u = reinterpret_cast<const uint32_t*>(&w[j]);
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const Pair pr = exp_pair(u[q], nm, c2);
+                hs += pr.h0 + pr.h1;
+                ls += pr.l0 + pr.l1;
+                if (cat == kWindow) {
+                    const uint32_t ge = bf2_ge(u[q], tau2);
+                    if (ge) {
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            if (!(ge & (h ? 0xFFFF0000u : 0x0000FFFFu))) continue;
+                            const int e = elem_index(sl, j, 2 * q + h);
+                            if (!elem_valid(sl, e)) continue;
+                            const uint32_t bits = h ? (u[q] >> 16) : (u[q] & 0xFFFFu);
+                            const uint32_t pos = atomicAdd(&sh->nlist, 1u);
+                            if (pos < kWinCap) sh->win[pos] = (okey(bits) << 16) | (uint32_t)(e - sl.e0);
+                        }
+                    }
+                } else if (cat == kBinned) {
+                    const int b0 = bin1_of(pr.yc.x), b1 = bin1_of(pr.yc.y);
+                    uint2* p0 = &sh->acc[b0 * kNT + tid];
+                    uint2 v0 = *p0;
+                    v0.x += pr.h0 - 0x4B000000u;
+                    v0.y += pr.l0 - 0x4B400000u;
+                    *p0 = v0;
+                    uint2* p1 = &sh->acc[b1 * kNT + tid];
+                    uint2 v1 = *p1;
+                    v1.x += pr.h1 - 0x4B000000u;
+                    v1.y += pr.l1 - 0x4B400000u;
+                    *p1 = v1;
+                    atomicAdd(&sh->bcnt[b0], 1u);
+                    atomicAdd(&sh->bcnt[b1], 1u);
+                }
+            }
+        }
+        const uint32_t nel = (uint32_t)NVT * 8u;
+        const uint32_t hi_t = hs - nel * 0x4B000000u;
+        const int32_t lo_t = (int32_t)(ls - nel * 0x4B400000u);
+        const unsigned long long s_thr = (unsigned long long)((long long)hi_t * 8388608 + lo_t);
+        const unsigned long long s_cta = cta_sum_u64(s_thr, sh);
+        Pub& pb2 = sh->pub[cx.ex & 1];
+        if (tid == 0) {
+            pb2.S = s_cta;
+            pb2.nwin = sh->nlist;
+        }
+        if (cat == kBinned) {
+            // reduce the private accumulators: warp w sums bins 4w..4w+3
+            __syncthreads();
+            for (int bb = 0; bb < kBins / kNW; ++bb) {
+                const int bin = wid * (kBins / kNW) + bb;
+                long long s = 0;
+                for (int i = lane; i < kNT; i += 32) {
+                    const uint2 v = sh->acc[bin * kNT + i];
+                    s += (long long)v.x * 8388608 + (int32_t)v.y;
+                }
+                s = (long long)warp_sum_u64((unsigned long long)s);
+                if (lane == 0) {
+                    pb2.mass[bin] = (unsigned long long)s;
+                    // fill slots (outside the slice) are -inf: they fall into the last bin
+                    const uint32_t fill = nel * kNT - (uint32_t)(sl.e1 > sl.e0 ? sl.e1 - sl.e0 : 0);
+                    pb2.cnt[bin] = sh->bcnt[bin] - (bin == kBins - 1 ? fill : 0u);
+                }
+            }
+        }
+        cluster_barrier();  // exchange 2
+        const unsigned ex2 = cx.ex++;
+        if (tid < 32) {
+            unsigned long long sp = 0;
+            uint32_t nw = 0;
+            if (lane < kCS) {
+                const Pub* rp = remote_pub(cx, lane, ex2);
+                sp = rp->S;
+                nw = rp->nwin;
+            }
+            sp = warp_sum_u64(sp);
+            const uint32_t tot = warp_sum_u32(nw);
+            const uint32_t over = __ballot_sync(0xffffffffu, nw > (uint32_t)kWinCap);
+            if (lane == 0) {
+                sh->self64[7] = sp;
+                sh->sel[12] = (int)tot;
+                sh->sel[13] = over != 0;
+            }
+        }
+        __syncthreads();
+        const unsigned long long S = sh->self64[7];
+        const uint32_t win_total = (uint32_t)sh->sel[12];
+        const bool win_over = sh->sel[13] != 0;
+        const long long thr = (ti.p < 1.0f) ? scale_floor(ti.p, S) : 0x7fffffffffffffffll;
+
+        if (cat == kKeepAll) {
+            if (lead && tid == 0) put_desc(a, ti, m, 0u, 0x7fffffff, S, 0, 0u);
+            continue;
+        }
+
+        if (cat == kWindow && !win_over && win_total <= (uint32_t)kWinTotal) {
+            if (lead) {
+                // gather every CTA's entries (key << 16 | local index) as (key, global index)
+                uint2* g = sh->acc;  // reuse: up to kWinTotal entries
+                __syncthreads();
+                if (tid == 0) sh->sel[1] = 0;
+                __syncthreads();
+                for (int q = 0; q < kCS; ++q) {
+                    const Pub* rp = remote_pub(cx, q, ex2);
+                    const uint32_t nw = rp->nwin;
+                    const uint32_t* rw = cluster.map_shared_rank(sh->win, q);
+                    const int qe0 = min(q * cx.L, a.V);
+                    int basepos = 0;
+                    for (int p2 = 0; p2 < q; ++p2) basepos += (int)remote_pub(cx, p2, ex2)->nwin;
+                    for (int i = tid; i < (int)nw; i += kNT) {
+                        const uint32_t e = rw[i];
+                        g[basepos + i] = make_uint2(e >> 16, (uint32_t)(qe0 + (int)(e & 0xFFFFu)));
+                    }
+                }
+                __syncthreads();
+                const int n = (int)win_total;
+                // rank by (key desc, index asc); place into sorted slots [kWinTotal, 2*kWinTotal)
+                for (int i = tid; i < n; i += kNT) {
+                    const uint2 me = g[i];
+                    int r = 0;
+                    for (int j2 = 0; j2 < n; ++j2) {
+                        const uint2 o = g[j2];
+                        r += (o.x > me.x) || (o.x == me.x && o.y < me.y);
+                    }
+                    g[kWinTotal + r] = me;
+                }
+                __syncthreads();
+                if (tid < 32) {
+                    // walk ranks with exact F; n' = min(k, n_p)
+                    unsigned long long A = 0;
+                    int nsel = -1;
+                    for (int base = 0; base < n && nsel < 0; base += 32) {
+                        const int r = base + lane;
+                        unsigned long long F = 0;
+                        if (r < n) F = fix_of_y(y_clamped(bf(key_bits(g[kWinTotal + r].x)), m, ti.c));
+                        unsigned long long inc = F;
+#pragma unroll
+                        for (int o = 1; o < 32; o <<= 1) {
+                            const unsigned long long v = __shfl_up_sync(0xffffffffu, inc, o);
+                            if (lane >= o) inc += v;
+                        }
+                        const unsigned long long Ar = A + inc - F;  // mass ranked ahead of r
+                        // rank r is kept iff r < k and A_r <= thr (r = 0 always)
+                        const bool out = r < n && (r >= kk || (long long)Ar > thr) && r > 0;
+                        const uint32_t bal = __ballot_sync(0xffffffffu, out);
+                        if (bal) nsel = base + __ffs(bal) - 1;
+                        A += __shfl_sync(0xffffffffu, inc, 31);
+                    }
+                    if (nsel < 0) nsel = n < kk ? n : (int)kk;  // window exhausted: rank k-1 is last
+                    // kept ranks 0..nsel-1
+                    unsigned long long sk = 0;
+                    for (int r = lane; r < nsel; r += 32)
+                        sk += fix_of_y(y_clamped(bf(key_bits(g[kWinTotal + r].x)), m, ti.c));
+                    sk = warp_sum_u64(sk);
+                    if (lane == 0) {
+                        const uint2 last = g[kWinTotal + nsel - 1];
+                        put_desc(a, ti, m, last.x, (int)last.y, sk, 0, 0u);
+                    }
+                }
+            }
+            continue;
+        }
+
+        // ---- binned selection (also the fallback of an overflowing window) -------------------
+        unsigned ex_bins = ex2;
+        if (cat == kWindow) {
+            // window overflow: a binned pass over the same registers
+            uint4* az = reinterpret_cast<uint4*>(sh->acc);
+            __syncthreads();
+            for (int i = tid; i < kBins * kNT / 2; i += kNT) az[i] = make_uint4(0, 0, 0, 0);
+            if (tid < kBins) sh->bcnt[tid] = 0;
+            __syncthreads();
+#pragma unroll
+            for (int j = 0; j < NVT; ++j) {
+                const uint32_t* u = reinterpret_cast<const uint32_t*>(&w[j]);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const Pair pr = exp_pair(u[q], nm, c2);
+                    const int b0 = bin1_of(pr.yc.x), b1 = bin1_of(pr.yc.y);
+                    uint2* p0 = &sh->acc[b0 * kNT + tid];
+                    uint2 v0 = *p0;
+                    v0.x += pr.h0 - 0x4B000000u;
+                    v0.y += pr.l0 - 0x4B400000u;
+                    *p0 = v0;
+                    uint2* p1 = &sh->acc[b1 * kNT + tid];
+                    uint2 v1 = *p1;
+                    v1.x += pr.h1 - 0x4B000000u;
+                    v1.y += pr.l1 - 0x4B400000u;
+                    *p1 = v1;
+                    atomicAdd(&sh->bcnt[b0], 1u);
+                    atomicAdd(&sh->bcnt[b1], 1u);
+                }
+            }
+            __syncthreads();
+            Pub& pbw = sh->pub[cx.ex & 1];
+            for (int bb = 0; bb < kBins / kNW; ++bb) {
+                const int bin = wid * (kBins / kNW) + bb;
+                long long s = 0;
+                for (int i = lane; i < kNT; i += 32) {
+                    const uint2 v = sh->acc[bin * kNT + i];
+                    s += (long long)v.x * 8388608 + (int32_t)v.y;
+                }
+                s = (long long)warp_sum_u64((unsigned long long)s);
+                if (lane == 0) {
+                    pbw.mass[bin] = (unsigned long long)s;
+                    const uint32_t fill = nel * kNT - (uint32_t)(sl.e1 > sl.e0 ? sl.e1 - sl.e0 : 0);
+                    pbw.cnt[bin] = sh->bcnt[bin] - (bin == kBins - 1 ? fill : 0u);
+                }
+            }
+            cluster_barrier();  // exchange 2b
+            ex_bins = cx.ex++;
+            cat = kBinned;
+        }
+
+        // level-1 walk (every CTA, identical inputs)
+        __syncthreads();
+        if (tid < 32) {
+            __shared__ uint32_t tc[kBins];
+            __shared__ unsigned long long tm[kBins];
+            uint32_t cs = 0;
+            unsigned long long ms = 0;
+            for (int q = 0; q < kCS; ++q) {
+                const Pub* rp = remote_pub(cx, q, ex_bins);
+                cs += rp->cnt[lane];
+                ms += rp->mass[lane];
+            }
+            tc[lane] = cs;
+            tm[lane] = ms;
+            __syncwarp();
+            const Walk wk = walk_groups(tc, tm, kBins, 0ull, 0ull, kk, thr);
+            if (lane == 0) {
+                sh->sel[0] = wk.group;
+                sh->self64[0] = wk.cnt;
+                sh->self64[1] = wk.mass;
+                sh->sel[2] = wk.group >= 0 ? (int)tc[wk.group] : 0;
+            }
+        }
+        __syncthreads();
+        const int b1 = sh->sel[0];
+        if (b1 < 0) {
+            // no boundary: every element is kept
+            if (lead && tid == 0) put_desc(a, ti, m, 0u, 0x7fffffff, S, 0, 0u);
+            continue;
+        }
+        unsigned long long cum_cnt = sh->self64[0], cum_mass = sh->self64[1];
+
+        // ---- level 2: sub-bins of bin b1 ---------------------------------------------------
+        {
+            // valid elements of bin b1 in this CTA (fill slots are excluded from the list)
+            const uint32_t my_cnt = sh->pub[ex_bins & 1].cnt[b1];
+            const bool compact = my_cnt <= (uint32_t)kListCap;
+            __syncthreads();
+            uint4* az = reinterpret_cast<uint4*>(sh->acc);
+            for (int i = tid; i < kSub * kNT / 2; i += kNT) az[i] = make_uint4(0, 0, 0, 0);
+            if (tid < kBins) sh->bcnt[tid] = 0;
+            if (tid == 0) sh->nlist = 0;
+            __syncthreads();
+            if (compact) {
+#pragma unroll
+                for (int j = 0; j < NVT; ++j) {
+                    const uint32_t* u = reinterpret_cast<const uint32_t*>(&w[j]);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const uint32_t bits = h ? (u[q] >> 16) : (u[q] & 0xFFFFu);
+                            const float yc = y_clamped(bf(bits), m, ti.c);
+                            if (bin1_of(yc) != b1) continue;
+                            const int e = elem_index(sl, j, 2 * q + h);
+                            if (!elem_valid(sl, e)) continue;
+                            const uint32_t pos = atomicAdd(&sh->nlist, 1u);
+                            if (pos < kListCap) sh->list[pos] = (bits << 16) | (uint32_t)(e - sl.e0);
+                        }
+                    }
+                }
+                __syncthreads();
+                const int n = (int)min(sh->nlist, (uint32_t)kListCap);
+                for (int i = tid; i < n; i += kNT) {
+                    const uint32_t bits = sh->list[i] >> 16;
+                    const float yc = y_clamped(bf(bits), m, ti.c);
+                    const int b2 = bin2_of(yc, b1);
+                    const unsigned long long F = fix_of_y(yc);
+                    uint2* p = &sh->acc[b2 * kNT + tid];
+                    uint2 v = *p;
+                    // F = hi * 2^23 + lo with hi <= 2^17, |lo| <= 2^22 (per-thread sums stay exact)
+                    const uint32_t fh = (uint32_t)((F + 4194304ull) >> 23);
+                    const int32_t fl = (int32_t)((long long)F - (long long)fh * 8388608);
+                    v.x += fh;
+                    v.y += (uint32_t)fl;
+                    *p = v;
+                    atomicAdd(&sh->bcnt[b2], 1u);
+                }
+            } else {
+#pragma unroll
+                for (int j = 0; j < NVT; ++j) {
+                    const uint32_t* u = reinterpret_cast<const uint32_t*>(&w[j]);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const Pair pr = exp_pair(u[q], nm, c2);
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const float yc = h ? pr.yc.y : pr.yc.x;
+                            if (bin1_of(yc) != b1) continue;
+                            const int e = elem_index(sl, j, 2 * q + h);
+                            if (!elem_valid(sl, e)) continue;
+                            const int b2 = bin2_of(yc, b1);
+                            uint2* p = &sh->acc[b2 * kNT + tid];
+                            uint2 v = *p;
+                            v.x += (h ? pr.h1 : pr.h0) - 0x4B000000u;
+                            v.y += (h ? pr.l1 : pr.l0) - 0x4B400000u;
+                            *p = v;
+                            atomicAdd(&sh->bcnt[b2], 1u);
+                        }
+                    }
+                }
+            }
+            __syncthreads();
+            Pub& pb3 = sh->pub[cx.ex & 1];
+            for (int bb = wid; bb < kSub; bb += kNW) {
+                long long s = 0;
+                for (int i = lane; i < kNT; i += 32) {
+                    const uint2 v = sh->acc[bb * kNT + i];
+                    s += (long long)v.x * 8388608 + (int32_t)v.y;
+                }
+                s = (long long)warp_sum_u64((unsigned long long)s);
+                if (lane == 0) {
+                    pb3.mass[bb] = (unsigned long long)s;
+                    pb3.cnt[bb] = sh->bcnt[bb];
+                }
+            }
+            cluster_barrier();  // exchange 3
+            const unsigned ex3 = cx.ex++;
+            __syncthreads();
+            if (tid < 32) {
+                __shared__ uint32_t tc2[kBins];
+                __shared__ unsigned long long tm2[kBins];
+                uint32_t cs = 0;
+                unsigned long long ms = 0;
+                if (lane < kSub) {
+                    for (int q = 0; q < kCS; ++q) {
+                        const Pub* rp = remote_pub(cx, q, ex3);
+                        cs += rp->cnt[lane];
+                        ms += rp->mass[lane];
+                    }
+                }
+                tc2[lane] = cs;
+                tm2[lane] = ms;
+                __syncwarp();
+                const Walk wk = walk_groups(tc2, tm2, kSub, cum_cnt, cum_mass, kk, thr);
+                if (lane == 0) {
+                    sh->sel[3] = wk.group;
+                    sh->self64[2] = wk.cnt;
+                    sh->self64[3] = wk.mass;
+                }
+            }
+            __syncthreads();
+        }
+        const int b2 = sh->sel[3];
+        if (b2 < 0) {
+            // cannot happen when level 1 found a boundary; keep everything defensively
+            if (lead && tid == 0) {
+                atomicOr(&a.ws->err, 8u);
+                put_desc(a, ti, m, 0u, 0x7fffffff, S, 0, 0u);
+            }
+            continue;
+        }
+        cum_cnt = sh->self64[2];
+        cum_mass = sh->self64[3];
+
+        // ---- level 3: per-key counts of the boundary sub-bin, in chunks from the top --------
+        if (tid == 0) {
+            uint32_t klo, khi;
+            key_range(b1 * kSub + b2, okey(0xFF80u), mkey, m, ti.c, klo, khi);
+            sh->sel[4] = (int)klo;
+            sh->sel[5] = (int)khi;
+        }
+        __syncthreads();
+        const uint32_t klo = (uint32_t)sh->sel[4], khi = (uint32_t)sh->sel[5];
+        KeyStop ks;
+        ks.found = 0;
+        for (uint32_t top = khi; top >= klo && top <= 0xFFFFu;) {
+            const uint32_t bot = (top - klo + 1 > (uint32_t)kKeyChunk) ? top - kKeyChunk + 1 : klo;
+            const int nk = (int)(top - bot + 1);
+            __syncthreads();
+            for (int i = tid; i < kKeyChunk; i += kNT) sh->khist[i] = 0;
+            __syncthreads();
+            const uint32_t vlo = key_bits(bot), vhi = key_bits(top);
+            const uint32_t vlo2 = vlo | (vlo << 16), vhi2 = vhi | (vhi << 16);
+#pragma unroll
+            for (int j = 0; j < NVT; ++j) {
+                const uint32_t* u = reinterpret_cast<const uint32_t*>(&w[j]);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const uint32_t in = bf2_ge(u[q], vlo2) & bf2_le(u[q], vhi2);
+                    if (!in) continue;
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        if (!(in & (h ? 0xFFFF0000u : 0x0000FFFFu))) continue;
+                        const int e = elem_index(sl, j, 2 * q + h);
+                        if (!elem_valid(sl, e)) continue;
+                        const uint32_t bits = h ? (u[q] >> 16) : (u[q] & 0xFFFFu);
+                        const uint32_t kkey = okey(bits);
+                        if (kkey >= bot && kkey <= top) atomicAdd(&sh->khist[top - kkey], 1u);
+                    }
+                }
+            }
+            cluster_barrier();  // exchange 4 (chunk)
+            cx.ex++;
+            // sum the cluster's counts into acc (as u32) and walk
+            uint32_t* tot = reinterpret_cast<uint32_t*>(sh->acc);
+            for (int i = tid; i < nk; i += kNT) {
+                uint32_t s = 0;
+                for (int q = 0; q < kCS; ++q) s += cluster.map_shared_rank(sh->khist, q)[i];
+                tot[i] = s;
+            }
+            __syncthreads();
+            if (tid < 32) {
+                const KeyStop r = walk_keys(tot, top, nk, m, ti.c, cum_cnt, cum_mass, kk, thr);
+                if (lane == 0) {
+                    sh->sel[6] = r.found;
+                    sh->sel[7] = (int)r.key;
+                    sh->sel[8] = (int)r.count;
+                    sh->self64[4] = r.cnt;
+                    sh->self64[5] = r.mass;
+                    sh->self64[6] = r.F;
+                }
+            }
+            // no CTA may clear its chunk counts while a peer still reads them
+            cluster_barrier();
+            cx.ex++;
+            ks.found = sh->sel[6];
+            if (ks.found) {
+                ks.key = (uint32_t)sh->sel[7];
+                ks.count = (uint32_t)sh->sel[8];
+                ks.cnt = sh->self64[4];
+                ks.mass = sh->self64[5];
+                ks.F = sh->self64[6];
+                break;
+            }
+            cum_cnt = sh->self64[4];
+            cum_mass = sh->self64[5];
+            if (bot == klo) break;
+            top = bot - 1;
+        }
+        if (!ks.found) {
+            if (lead && tid == 0) {
+                atomicOr(&a.ws->err, 8u);
+                put_desc(a, ti, m, 0u, 0x7fffffff, S, 0, 0u);
+            }
+            continue;
+        }
+        // kept among the ks.count elements with the boundary key
+        unsigned long long ntie = ks.count;
+        if ((long long)(ks.cnt + ntie) > kk) ntie = (unsigned long long)(kk - (long long)ks.cnt);
+        if (ks.F > 0 && (long long)(ks.mass) <= thr) {
+            const unsigned long long pb_ = (unsigned long long)((thr - (long long)ks.mass)) / ks.F + 1ull;
+            if (pb_ < ntie) ntie = pb_;
+        }
+        if (ntie < 1) ntie = 1;
+        const unsigned long long skept = ks.mass + ntie * ks.F;
+
+        if (ntie >= ks.count) {
+            if (lead && tid == 0) put_desc(a, ti, m, ks.key, 0x7fffffff, skept, 0, 0u);
+            continue;
+        }
+        // ---- tie cut: the ntie-th occurrence (index order) of the boundary key ----------------
+        const uint32_t kb = key_bits(ks.key);
+        const uint32_t kb2 = kb | (kb << 16);
+        uint32_t cj[NVT];
+        uint32_t mine = 0;
+#pragma unroll
+        for (int j = 0; j < NVT; ++j) {
+            const uint32_t* u = reinterpret_cast<const uint32_t*>(&w[j]);
+            uint32_t c = 0;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const uint32_t eq = bf2_eq(u[q], kb2);
+                if (eq) {
+#pragma unroll
+                    for (int h = 0; h < 2; ++h)
+                        if ((eq & (h ? 0xFFFF0000u : 0x0000FFFFu)) &&
+                            elem_valid(sl, elem_index(sl, j, 2 * q + h)))
+                            ++c;
+                }
+            }
+            cj[j] = c;
+            mine += c;
+        }
+        // per vector-row j totals of the CTA
+        __syncthreads();
+        uint32_t* rowtot = reinterpret_cast<uint32_t*>(sh->acc);  // [NVT][kNW]
+#pragma unroll
+        for (int j = 0; j < NVT; ++j) {
+            const uint32_t s = warp_sum_u32(cj[j]);
+            if (lane == 0) rowtot[j * kNW + wid] = s;
+        }
+        const uint32_t cta_occ = (uint32_t)cta_sum_u64(mine, sh);
+        Pub& pb5 = sh->pub[cx.ex & 1];
+        if (tid == 0) pb5.flag = cta_occ;
+        cluster_barrier();  // exchange 5
+        const unsigned ex5 = cx.ex++;
+        unsigned long long before = 0;
+        for (int q = 0; q < cx.rank; ++q) before += remote_pub(cx, q, ex5)->flag;
+        // the CTA holding occurrence number ntie (1-based) finds it and writes the descriptor
+        if (before < ntie && before + cta_occ >= ntie) {
+            uint32_t need = (uint32_t)(ntie - before);  // 1-based within this CTA
+            int jstar = 0;
+            uint32_t acc_rows = 0;
+            for (int j = 0; j < NVT; ++j) {
+                uint32_t rt = 0;
+                for (int i = 0; i < kNW; ++i) rt += rowtot[j * kNW + i];
+                if (acc_rows + rt >= need) { jstar = j; break; }
+                acc_rows += rt;
+            }
+            need -= acc_rows;
+            // within vector-row jstar: warps in order, lanes in order
+            uint32_t cme = 0;
+#pragma unroll
+            for (int j = 0; j < NVT; ++j) if (j == jstar) cme = cj[j];
+            const uint32_t incl = warp_incl_u32(cme);
+            uint32_t wbefore = 0;
+            for (int i = 0; i < wid; ++i) wbefore += rowtot[jstar * kNW + i];
+            const uint32_t lo_ = wbefore + incl - cme;
+            if (cme > 0 && lo_ < need && lo_ + cme >= need) {
+                uint32_t k2 = need - lo_;  // 1-based within this thread's vector
+                int tie = -1;
+#pragma unroll
+                for (int j = 0; j < NVT; ++j) {
+                    if (j != jstar) continue;
+                    const uint32_t* u = reinterpret_cast<const uint32_t*>(&w[j]);
+                    for (int hh = 0; hh < 8 && tie < 0; ++hh) {
+                        const uint32_t bits = (hh & 1) ? (u[hh >> 1] >> 16) : (u[hh >> 1] & 0xFFFFu);
+                        const int e = elem_index(sl, j, hh);
+                        if (!elem_valid(sl, e)) continue;
+                        if (okey(bits) == ks.key) {
+                            if (--k2 == 0) tie = e;
+                        }
+                    }
+                }
+                if (tie < 0) atomicOr(&a.ws->err, 16u);
+                put_desc(a, ti, m, ks.key, tie, skept, 0, 0u);
+            }
+        }
+    }
+    // no CTA may leave while a peer can still read its shared memory
+    cluster_barrier();
+}
+
+// ---------------------------------------------------------------------------------------
+// chain + bonus + outputs (one cluster per request)
+
+struct ChainSmem {
+    unsigned long long tsum[kNT];
+    unsigned long long pub[2][2];  // per exchange: CTA total
+    int32_t sel[8];
+    unsigned long long red64[kNW];
+    uint32_t red_a[kNW], red_b[kNW];
+    int flag;
+};
+
+__device__ __forceinline__ uint64_t fix_w(float w) {
+    if (!(w > 0.0f)) return 0;
+    return fix01(fminf(w, 1.0f));
+}
+
+// residual weight of element i (oracle logit_w): pure p, or max(p - clamp01(q), 0)
+__device__ __forceinline__ float resid_w(const RowDesc& dp, const RowDesc* dq, long long onehot,
+                                         bool pure, uint32_t pbits, uint32_t qbits, int i) {
+    const float p = row_prob(dp, bf(pbits), pbits, i);
+    if (pure) return p;
+    float q;
+    if (dq) q = row_prob(*dq, bf(qbits), qbits, i);
+    else q = (i == onehot) ? 1.0f : 0.0f;
+    const float qq = (q >= 0.0f && q <= 1.0f) ? q : 0.0f;
+    return fmaxf(__fsub_rn(p, qq), 0.0f);
+}
+
+__device__ void compact_all(const VerifyArgs& a, ChainSmem* sh) {
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    int run_c = 0, run_f = 0;
+    if (tid == 0) { a.offsets[0] = 0; a.free_offsets[0] = 0; }
+    for (int b0 = 0; b0 < a.B; b0 += kNT) {
+        const int b = b0 + tid;
+        int cm = 0, fr = 0;
+        if (b < a.B) {
+            const int cap = clamp_cap(a.caps[b]);
+            cm = __ldcg(&a.commit[b]);
+            fr = cap - cm;
+            if (fr < 0) fr = 0;
+        }
+        const uint32_t ic = warp_incl_u32((uint32_t)cm);
+        const uint32_t iff = warp_incl_u32((uint32_t)fr);
+        if (lane == 31) { sh->red_a[w] = ic; sh->red_b[w] = iff; }
+        __syncthreads();
+        int wc = 0, wf = 0, tc = 0, tf = 0;
+        for (int q = 0; q < kNW; ++q) {
+            if (q < w) { wc += (int)sh->red_a[q]; wf += (int)sh->red_b[q]; }
+            tc += (int)sh->red_a[q];
+            tf += (int)sh->red_b[q];
+        }
+        __syncthreads();
+        if (b < a.B) {
+            const int oc = run_c + wc + (int)ic - cm;
+            const int of = run_f + wf + (int)iff - fr;
+            a.offsets[b + 1] = oc + cm;
+            a.free_offsets[b + 1] = of + fr;
+            const long long srow = a.slot_row[b];
+            bool bad = false;
+            for (int i = 0; i < cm; ++i) {
+                a.tok_out[oc + i] = __ldcg(&a.output[b * kT + i]);
+                const long long si = srow + i;
+                const bool in = si >= 0 && si < a.slots_len;
+                bad |= !in;
+                a.slot_out[oc + i] = in ? a.slots[si] : -1;
+            }
+            for (int j = 0; j < fr; ++j) {
+                const long long si = srow + cm + j;
+                const bool in = si >= 0 && si < a.slots_len;
+                bad |= !in;
+                a.free_out[of + j] = in ? a.slots[si] : -1;
+            }
+            if (bad) atomicOr(&a.ws->err, 4u);
+        }
+        run_c += tc;
+        run_f += tf;
+    }
+}
+
+__device__ void write_request(const VerifyArgs& a, int b, int acc, long long bonus) {
+    a.accept[b] = acc;
+    a.commit[b] = acc + 1;
+    a.bonus[b] = bonus;
+    for (int i = 0; i < kT; ++i) {
+        long long v = 0;
+        if (i < acc) v = a.cand[b * kT + i + 1];
+        else if (i == acc) v = bonus;
+        a.output[b * kT + i] = v;
+    }
+    a.new_seq[b] = a.prefix[b] + acc + 1;
+}
+
+// contiguous element range of thread t inside slice [e0, e1)
+__device__ __forceinline__ void thread_range(int e0, int e1, int& lo, int& hi) {
+    const int n = e1 - e0;
+    const int per = (n + kNT - 1) / kNT;
+    lo = min(e0 + (int)threadIdx.x * per, e1);
+    hi = min(lo + per, e1);
+}
+
+__global__ void __launch_bounds__(kNT) chain_kernel(VerifyArgs a) {
+    __shared__ ChainSmem shm;
+    ChainSmem* sh = &shm;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int tid = threadIdx.x, lane = tid & 31;
+    const int rank = (int)cluster.block_rank();
+    const int b = blockIdx.x / kCS;  // gridDim = B * kCS: one cluster per request
+
+    const int cap = clamp_cap(a.caps[b]);
+    const float T = a.temperature[b];
+    const int kq = a.top_k[b];
+    const float c = log2e_over(T);
+    const bool greedy = is_greedy(T, kq, c);
+    const bool onehot_q = greedy || a.drf == nullptr;
+    const uint16_t* tgt = reinterpret_cast<const uint16_t*>(a.tgt);
+    const uint16_t* drf = reinterpret_cast<const uint16_t*>(a.drf);
+
+    // ---- chain: step s compares draft s+1 with target row s (warp 0, one lane per step) ----
+    if (tid < 32) {
+        bool acc = false;
+        const int s = lane;
+        if (s < cap - 1) {
+            const long long tok = a.cand[b * kT + s + 1];
+            const bool valid = tok >= 0 && tok < a.V;
+            float p = 0.0f, q = 0.0f;
+            if (valid) {
+                const RowDesc dt = a.desc[(b * kT + s) * 2 + 0];
+                const long long tr = a.tgt_row[b] + s;
+                if (tr >= 0 && tr < a.tgt_rows) {
+                    const uint32_t pb = tgt[tr * a.stride + tok];
+                    p = row_prob(dt, bf(pb), pb, (int)tok);
+                }
+                if (onehot_q) {
+                    q = 1.0f;
+                } else {
+                    const RowDesc dd = a.desc[(b * kT + s) * 2 + 1];
+                    const long long dr = a.drf_row[b] + s;
+                    if (dr >= 0 && dr < a.drf_rows) {
+                        const uint32_t qb = drf[dr * a.stride + tok];
+                        q = row_prob(dd, bf(qb), qb, (int)tok);
+                    }
+                }
+            }
+            acc = q > 0.0f && q <= 1.0f && __fmul_rn(a.u[b * 15 + s], q) < p;
+        }
+        const uint32_t rej = __ballot_sync(0xffffffffu, !acc) & ((cap - 1 >= 32) ? 0xffffffffu : ((1u << (cap - 1)) - 1u));
+        const int na = rej ? __ffs(rej) - 1 : cap - 1;
+        if (lane == 0) sh->sel[0] = na;
+    }
+    __syncthreads();
+    const int acc = sh->sel[0];
+    const bool pure = acc == cap - 1;
+    const float uf = a.uf[b];
+
+    const RowDesc dt = a.desc[(b * kT + acc) * 2 + 0];
+    if (greedy) {
+        // one-hot p at the argmax; the residual against a one-hot q is the same one-hot or
+        // empty (then the fallback to p): the draw is the argmax unless u is out of [0, 1)
+        if (rank == 0 && tid == 0) {
+            const long long thr = scale_floor(uf, 1ull << kFixBits);
+            const long long bo = thr == -2 ? (long long)a.V - 1 : (thr < 0 ? 0ll : (long long)dt.argmax);
+            write_request(a, b, acc, bo);
+        }
+    } else {
+        const long long tr = a.tgt_row[b] + acc;
+        const bool trow_ok = tr >= 0 && tr < a.tgt_rows;
+        const RowDesc* dq = nullptr;
+        RowDesc dd;
+        long long onehot = -1;
+        const uint16_t* qrow = nullptr;
+        if (!pure) {
+            if (onehot_q) {
+                onehot = a.cand[b * kT + acc + 1];
+            } else {
+                dd = a.desc[(b * kT + acc) * 2 + 1];
+                dq = &dd;
+                const long long dr = a.drf_row[b] + acc;
+                if (dr >= 0 && dr < a.drf_rows) qrow = drf + dr * a.stride;
+            }
+        }
+        const uint16_t* prow = trow_ok ? tgt + tr * a.stride : nullptr;
+        int L = (a.V + kCS - 1) / kCS;
+        const int e0 = min(rank * L, a.V), e1 = min(e0 + L, a.V);
+        int lo, hi;
+        thread_range(e0, e1, lo, hi);
+        unsigned ex = 0;
+        bool use_pure = pure;
+        unsigned long long M = 0, cum = 0, tot = 0, mine = 0;
+        for (int attempt = 0; attempt < 2; ++attempt) {
+            mine = 0;
+            for (int i = lo; i < hi; ++i) {
+                const uint32_t pb = prow ? prow[i] : 0xFF80u;
+                const uint32_t qb = qrow ? qrow[i] : 0xFF80u;
+                mine += fix_w(resid_w(dt, dq, onehot, use_pure, pb, qb, i));
+            }
+            // CTA exclusive scan of thread sums
+            sh->tsum[tid] = mine;
+            __syncthreads();
+            if (tid < 32) {
+                unsigned long long s = 0;
+                for (int i = 0; i < kNT / 32; ++i) s += sh->tsum[lane * (kNT / 32) + i];
+                unsigned long long inc = s;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const unsigned long long v = __shfl_up_sync(0xffffffffu, inc, o);
+                    if (lane >= o) inc += v;
+                }
+                unsigned long long run = inc - s;
+                for (int i = 0; i < kNT / 32; ++i) {
+                    const unsigned long long x = sh->tsum[lane * (kNT / 32) + i];
+                    sh->tsum[lane * (kNT / 32) + i] = run;  // exclusive prefix
+                    run += x;
+                }
+                if (lane == 31) sh->pub[ex & 1][0] = inc;
+            }
+            __syncthreads();
+            cluster_barrier();
+            const unsigned exn = ex++;
+            M = 0;
+            cum = 0;
+            for (int q = 0; q < kCS; ++q) {
+                const unsigned long long v = cluster.map_shared_rank(&sh->pub[exn & 1][0], q)[0];
+                if (q < rank) cum += v;
+                if (q == rank) tot = v;
+                M += v;
+            }
+            if (!use_pure && M == 0) { use_pure = true; continue; }
+            break;
+        }
+        const long long thr = scale_floor(uf, M);
+        if (thr == -2) {
+            if (rank == 0 && tid == 0) write_request(a, b, acc, (long long)a.V - 1);
+        } else if ((long long)(cum + tot) > thr && (rank == 0 || (long long)cum <= thr)) {
+            // this CTA holds the crossing: the first CTA whose running total passes thr
+            const long long rel = thr - (long long)cum;
+            const unsigned long long pre = sh->tsum[tid];
+            if ((long long)(pre + mine) > rel && (tid == 0 || (long long)pre <= rel)) {
+                unsigned long long run = pre;
+                long long bonus = (long long)a.V - 1;
+                for (int i = lo; i < hi; ++i) {
+                    const uint32_t pb = prow ? prow[i] : 0xFF80u;
+                    const uint32_t qb = qrow ? qrow[i] : 0xFF80u;
+                    run += fix_w(resid_w(dt, dq, onehot, use_pure, pb, qb, i));
+                    if ((long long)run > rel) { bonus = i; break; }
+                }
+                write_request(a, b, acc, bonus);
+            }
+        } else if (rank == 0 && (long long)M <= thr) {
+            // no crossing (mass 0): the default of the reference loop
+            if (tid == 0) write_request(a, b, acc, (long long)a.V - 1);
+        }
+        cluster_barrier();  // peers may still read this CTA's totals
+    }
+
+    // ---- completion: the last request packs tokens and KV slots ---------------------------
+    if (rank == 0) {
+        __syncthreads();
+        if (tid == 0) {
+            __threadfence();
+            const unsigned old = atomicAdd(&a.ws->finalized, 1u);
+            sh->flag = old == (unsigned)(a.B - 1);
+        }
+        __syncthreads();
+        if (sh->flag) {
+            __threadfence();
+            if (a.tok_out != nullptr) compact_all(a, sh);
+            __syncthreads();
+            if (tid == 0) a.ws->finalized = 0;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// launcher
+
+template <int NVT>
+int launch_rows(VerifyArgs a, cudaStream_t stream) {
+    auto kern = row_kernel<NVT>;
+    const size_t smem = sizeof(RowSmem);
+    static int attr_done = 0;
+    if (!attr_done) {
+        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+            return kLaunchFailed;
+        cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
+        attr_done = 1;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kCS;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(kNT, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    static int cached_dev = -1, cached_n = 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    int nclus = 0;
+    if (cached_dev == dev) {
+        nclus = cached_n;
+    } else {
+        cfg.gridDim = dim3(kCS, 1, 1);
+        if (cudaOccupancyMaxActiveClusters(&nclus, kern, &cfg) != cudaSuccess || nclus <= 0)
+            return kLaunchFailed;
+        cached_dev = dev;
+        cached_n = nclus;
+    }
+    a.num_clusters = nclus;
+    cfg.gridDim = dim3(nclus * kCS, 1, 1);
+    if (cudaLaunchKernelEx(&cfg, kern, a) != cudaSuccess) return kLaunchFailed;
+    return kOk;
+}
+
+int launch_chain(VerifyArgs a, cudaStream_t stream) {
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kCS;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(kNT, 1, 1);
+    cfg.dynamicSmemBytes = 0;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cfg.gridDim = dim3(a.B * kCS, 1, 1);
+    if (cudaLaunchKernelEx(&cfg, chain_kernel, a) != cudaSuccess) return kLaunchFailed;
+    return kOk;
+}
+
+}  // namespace st
+
+size_t stream_smem_bytes() { return sizeof(st::RowSmem); }
+
+// vocabulary elements per CTA slice for a given V (multiple of 8)
+static int stream_slice(int V) {
+    int L = (V + st::kCS - 1) / st::kCS;
+    return (L + 7) & ~7;
+}
+
+int stream_nvt(int V) {
+    const int L = stream_slice(V);
+    const int nv = L / 8 + 1;
+    return (nv + st::kNT - 1) / st::kNT;
+}
+
+bool stream_supported(const VerifyArgs& a, int dtype) {
+    if (dtype != 0) return false;
+    if (a.B > st::kMaxB || a.desc == nullptr) return false;
+    if ((reinterpret_cast<uintptr_t>(a.tgt) & 1u) || (a.drf && (reinterpret_cast<uintptr_t>(a.drf) & 1u)))
+        return false;
+    return stream_nvt(a.V) <= 10;
+}
+
+int launch_stream(VerifyArgs a, cudaStream_t stream) {
+    a.slice = stream_slice(a.V);
+    const int nvt = stream_nvt(a.V);
+    int st_ = kUnsupported;
+    if (nvt <= 1) st_ = st::launch_rows<1>(a, stream);
+    else if (nvt <= 2) st_ = st::launch_rows<2>(a, stream);
+    else if (nvt <= 4) st_ = st::launch_rows<4>(a, stream);
+    else if (nvt <= 10) st_ = st::launch_rows<10>(a, stream);
+    if (st_ != kOk) return st_;
+    return st::launch_chain(a, stream);
+}
+
+}  // namespace dsv
