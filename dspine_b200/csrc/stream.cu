@@ -48,6 +48,7 @@ constexpr int kWinTotal = 512;   // window entries per row
 constexpr int kListCap = 4096;   // level-2 compaction list per CTA
 constexpr int kKeyChunk = 512;   // keys per level-3 histogram chunk
 constexpr int kMaxB = 1024;      // requests per launch handled by this path
+constexpr int kTaskCap = 256;    // decoded tasks of one cluster held in shared memory at a time
 
 enum Cat : int { kGreedy = 0, kKeepAll = 1, kWindow = 2, kBinned = 3 };
 
@@ -172,6 +173,13 @@ __device__ __forceinline__ float row_prob(const RowDesc& d, float l, uint32_t u1
 // ---------------------------------------------------------------------------------------
 // shared memory of the row kernel
 
+struct TaskInfo {
+    int b, s, kind, cat, cap;
+    long long row;     // row index in its tensor (-1: invalid)
+    float T, p, c;
+    int k;
+};
+
 struct Pub {                       // published at an exchange, read by the cluster (DSMEM)
     uint32_t maxkey;               // CTA max key
     int32_t first;                 // first index of the CTA max (greedy rows)
@@ -197,19 +205,13 @@ struct RowSmem {
     uint32_t nlist;
     int32_t first_min;
     int pre[3][kMaxB + 1];         // task prefix per group (binned, keep-all/window, greedy)
+    TaskInfo tasks[kTaskCap];      // this cluster's next tasks, decoded once
     uint32_t req[kMaxB];           // per request: cat | cap << 4
     alignas(16) uint2 acc[kBins * kNT];  // thread-private bin accumulators / gather area
     alignas(16) uint32_t list[kListCap]; // level-2 compaction list: bits << 16 | local index
 };
 // the accumulator region is cleared with 16-byte stores
 static_assert(offsetof(RowSmem, acc) % 16 == 0, "acc must be 16-byte aligned");
-
-struct TaskInfo {
-    int b, s, kind, cat, cap;
-    long long row;     // row index in its tensor (-1: invalid)
-    float T, p, c;
-    int k;
-};
 
 __device__ __forceinline__ int clamp_cap(int c) { return c < 1 ? 1 : (c > kT ? kT : c); }
 
@@ -526,6 +528,45 @@ __device__ void key_range(int target, uint32_t kmin, uint32_t kmax, float m, flo
     klo = lo;
 }
 
+
+// Rare follow-up pass (window overflow -> level-1 bins of every valid element; level-2 sub-bins
+// of bin b1 that do not fit the compaction list): re-reads the slice from global memory (L2-hot)
+// so that the row slice held in registers by the caller is not touched.  Accumulates into the
+// thread-private columns acc[slot * kNT + tid] and the slot counts.
+__device__ __noinline__ void reread_bins(const Slice sl, float m, float c, int sub, int b1,
+                                         RowSmem* sh) {
+    const int tid = threadIdx.x;
+    const float2 nm = make_float2(-m, -m), c2 = make_float2(c, c);
+    const uint4* src = reinterpret_cast<const uint4*>(sl.rowp + sl.e0 - sl.off);
+#pragma unroll 1
+    for (int v = tid; v < sl.nv; v += kNT) {
+        const uint4 x = __ldg(src + v);
+        const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            const Pair pr = exp_pair(xs[q], nm, c2);
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const float yc = h ? pr.yc.y : pr.yc.x;
+                const int e = sl.e0 - sl.off + 8 * v + 2 * q + h;
+                if (!elem_valid(sl, e)) continue;
+                const int bb = bin1_of(yc);
+                int slot = bb;
+                if (sub) {
+                    if (bb != b1) continue;
+                    slot = bin2_of(yc, b1);
+                }
+                uint2* pa = &sh->acc[slot * kNT + tid];
+                uint2 va = *pa;
+                va.x += (h ? pr.h1 : pr.h0) - 0x4B000000u;
+                va.y += (h ? pr.l1 : pr.l0) - 0x4B400000u;
+                *pa = va;
+                atomicAdd(&sh->bcnt[slot], 1u);
+            }
+        }
+    }
+}
+
 template <int NVT>
 __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
@@ -545,16 +586,24 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
     const int ntask = total_tasks(a, sh);
 
     uint4 w[NVT];
-    int it = 0;
-    for (int t = cid; t < ntask; t += a.num_clusters, ++it) {
-        const TaskInfo ti = decode_task(a, sh, t);
+    // this cluster's tasks are cid, cid + NC, ...; decode them into shared memory in parallel
+    // (kTaskCap at a time) so that no task waits on its own metadata loads
+    const int nmine = ntask > cid ? (ntask - cid + a.num_clusters - 1) / a.num_clusters : 0;
+    for (int it = 0; it < nmine; ++it) {
+        if (it % kTaskCap == 0) {
+            __syncthreads();
+            for (int i = tid; i < kTaskCap && it + i < nmine; i += kNT)
+                sh->tasks[i] = decode_task(a, sh, cid + (it + i) * a.num_clusters);
+            __syncthreads();
+        }
+        const TaskInfo ti = sh->tasks[it % kTaskCap];
         const int leader = it % kCS;
         const bool lead = cx.rank == leader;
         if (ti.row < 0 && tid == 0 && cx.rank == 0) atomicOr(&a.ws->err, 2u);
         const Slice sl = slice_of(a, ti, cx.rank, cx.L);
         load_slice<NVT>(sl, w);
-        if (tid == 0 && t + a.num_clusters < ntask) {
-            const TaskInfo tn = decode_task(a, sh, t + a.num_clusters);
+        if (tid == 0 && it + 1 < nmine && (it + 1) % kTaskCap != 0) {
+            const TaskInfo& tn = sh->tasks[(it + 1) % kTaskCap];
             if (tn.row >= 0) prefetch_l2(slice_of(a, tn, cx.rank, cx.L));
         }
 
@@ -849,27 +898,7 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
             for (int i = tid; i < kBins * kNT / 2; i += kNT) az[i] = make_uint4(0, 0, 0, 0);
             if (tid < kBins) sh->bcnt[tid] = 0;
             __syncthreads();
-#pragma unroll
-            for (int j = 0; j < NVT; ++j) {
-                const uint32_t* u = reinterpret_cast<const uint32_t*>(&w[j]);
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const Pair pr = exp_pair(u[q], nm, c2);
-                    const int b0 = bin1_of(pr.yc.x), b1 = bin1_of(pr.yc.y);
-                    uint2* p0 = &sh->acc[b0 * kNT + tid];
-                    uint2 v0 = *p0;
-                    v0.x += pr.h0 - 0x4B000000u;
-                    v0.y += pr.l0 - 0x4B400000u;
-                    *p0 = v0;
-                    uint2* p1 = &sh->acc[b1 * kNT + tid];
-                    uint2 v1 = *p1;
-                    v1.x += pr.h1 - 0x4B000000u;
-                    v1.y += pr.l1 - 0x4B400000u;
-                    *p1 = v1;
-                    atomicAdd(&sh->bcnt[b0], 1u);
-                    atomicAdd(&sh->bcnt[b1], 1u);
-                }
-            }
+            reread_bins(sl, m, ti.c, 0, 0, sh);
             __syncthreads();
             Pub& pbw = sh->pub[cx.ex & 1];
             for (int bb = 0; bb < kBins / kNW; ++bb) {
@@ -882,8 +911,7 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
                 s = (long long)warp_sum_u64((unsigned long long)s);
                 if (lane == 0) {
                     pbw.mass[bin] = (unsigned long long)s;
-                    const uint32_t fill = nel * kNT - (uint32_t)(sl.e1 > sl.e0 ? sl.e1 - sl.e0 : 0);
-                    pbw.cnt[bin] = sh->bcnt[bin] - (bin == kBins - 1 ? fill : 0u);
+                    pbw.cnt[bin] = sh->bcnt[bin];
                 }
             }
             cluster_barrier();  // exchange 2b
@@ -970,28 +998,7 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
                     atomicAdd(&sh->bcnt[b2], 1u);
                 }
             } else {
-#pragma unroll
-                for (int j = 0; j < NVT; ++j) {
-                    const uint32_t* u = reinterpret_cast<const uint32_t*>(&w[j]);
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const Pair pr = exp_pair(u[q], nm, c2);
-#pragma unroll
-                        for (int h = 0; h < 2; ++h) {
-                            const float yc = h ? pr.yc.y : pr.yc.x;
-                            if (bin1_of(yc) != b1) continue;
-                            const int e = elem_index(sl, j, 2 * q + h);
-                            if (!elem_valid(sl, e)) continue;
-                            const int b2 = bin2_of(yc, b1);
-                            uint2* p = &sh->acc[b2 * kNT + tid];
-                            uint2 v = *p;
-                            v.x += (h ? pr.h1 : pr.h0) - 0x4B000000u;
-                            v.y += (h ? pr.l1 : pr.l0) - 0x4B400000u;
-                            *p = v;
-                            atomicAdd(&sh->bcnt[b2], 1u);
-                        }
-                    }
-                }
+                reread_bins(sl, m, ti.c, 1, b1, sh);
             }
             __syncthreads();
             Pub& pb3 = sh->pub[cx.ex & 1];
@@ -1143,37 +1150,28 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
             continue;
         }
         // ---- tie cut: the ntie-th occurrence (index order) of the boundary key ----------------
-        const uint32_t kb = key_bits(ks.key);
-        const uint32_t kb2 = kb | (kb << 16);
-        uint32_t cj[NVT];
+        // index order inside a CTA is (vector-row j, thread, half); per-row totals go to shared
+        // memory so that no per-row array stays in registers next to the row slice
+        uint32_t* rowcnt = reinterpret_cast<uint32_t*>(sh->acc);          // [NVT]
+        uint32_t* wrow = reinterpret_cast<uint32_t*>(sh->acc) + 64;       // [kNW]
+        __syncthreads();
+        if (tid < NVT) rowcnt[tid] = 0;
+        __syncthreads();
         uint32_t mine = 0;
 #pragma unroll
         for (int j = 0; j < NVT; ++j) {
             const uint32_t* u = reinterpret_cast<const uint32_t*>(&w[j]);
             uint32_t c = 0;
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const uint32_t eq = bf2_eq(u[q], kb2);
-                if (eq) {
-#pragma unroll
-                    for (int h = 0; h < 2; ++h)
-                        if ((eq & (h ? 0xFFFF0000u : 0x0000FFFFu)) &&
-                            elem_valid(sl, elem_index(sl, j, 2 * q + h)))
-                            ++c;
-                }
+            for (int hh = 0; hh < 8; ++hh) {
+                const uint32_t bits = (hh & 1) ? (u[hh >> 1] >> 16) : (u[hh >> 1] & 0xFFFFu);
+                c += (okey(bits) == ks.key && elem_valid(sl, elem_index(sl, j, hh))) ? 1u : 0u;
             }
-            cj[j] = c;
+            const uint32_t ws_ = warp_sum_u32(c);
+            if (lane == 0 && ws_) atomicAdd(&rowcnt[j], ws_);
             mine += c;
         }
-        // per vector-row j totals of the CTA
-        __syncthreads();
-        uint32_t* rowtot = reinterpret_cast<uint32_t*>(sh->acc);  // [NVT][kNW]
-#pragma unroll
-        for (int j = 0; j < NVT; ++j) {
-            const uint32_t s = warp_sum_u32(cj[j]);
-            if (lane == 0) rowtot[j * kNW + wid] = s;
-        }
-        const uint32_t cta_occ = (uint32_t)cta_sum_u64(mine, sh);
+        const uint32_t cta_occ = (uint32_t)cta_sum_u64(mine, sh);  // includes __syncthreads
         Pub& pb5 = sh->pub[cx.ex & 1];
         if (tid == 0) pb5.flag = cta_occ;
         cluster_barrier();  // exchange 5
@@ -1182,23 +1180,29 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
         for (int q = 0; q < cx.rank; ++q) before += remote_pub(cx, q, ex5)->flag;
         // the CTA holding occurrence number ntie (1-based) finds it and writes the descriptor
         if (before < ntie && before + cta_occ >= ntie) {
-            uint32_t need = (uint32_t)(ntie - before);  // 1-based within this CTA
-            int jstar = 0;
-            uint32_t acc_rows = 0;
+            uint32_t need = (uint32_t)(ntie - before);
+            int jstar = NVT - 1;
             for (int j = 0; j < NVT; ++j) {
-                uint32_t rt = 0;
-                for (int i = 0; i < kNW; ++i) rt += rowtot[j * kNW + i];
-                if (acc_rows + rt >= need) { jstar = j; break; }
-                acc_rows += rt;
+                if (rowcnt[j] >= need) { jstar = j; break; }
+                need -= rowcnt[j];
             }
-            need -= acc_rows;
-            // within vector-row jstar: warps in order, lanes in order
+            // recount vector-row jstar for this thread
             uint32_t cme = 0;
 #pragma unroll
-            for (int j = 0; j < NVT; ++j) if (j == jstar) cme = cj[j];
+            for (int j = 0; j < NVT; ++j) {
+                if (j != jstar) continue;
+                const uint32_t* u = reinterpret_cast<const uint32_t*>(&w[j]);
+#pragma unroll
+                for (int hh = 0; hh < 8; ++hh) {
+                    const uint32_t bits = (hh & 1) ? (u[hh >> 1] >> 16) : (u[hh >> 1] & 0xFFFFu);
+                    cme += (okey(bits) == ks.key && elem_valid(sl, elem_index(sl, j, hh))) ? 1u : 0u;
+                }
+            }
             const uint32_t incl = warp_incl_u32(cme);
+            if (lane == 31) wrow[wid] = incl;
+            __syncthreads();
             uint32_t wbefore = 0;
-            for (int i = 0; i < wid; ++i) wbefore += rowtot[jstar * kNW + i];
+            for (int i = 0; i < wid; ++i) wbefore += wrow[i];
             const uint32_t lo_ = wbefore + incl - cme;
             if (cme > 0 && lo_ < need && lo_ + cme >= need) {
                 uint32_t k2 = need - lo_;  // 1-based within this thread's vector
@@ -1207,11 +1211,11 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
                 for (int j = 0; j < NVT; ++j) {
                     if (j != jstar) continue;
                     const uint32_t* u = reinterpret_cast<const uint32_t*>(&w[j]);
-                    for (int hh = 0; hh < 8 && tie < 0; ++hh) {
+#pragma unroll
+                    for (int hh = 0; hh < 8; ++hh) {
                         const uint32_t bits = (hh & 1) ? (u[hh >> 1] >> 16) : (u[hh >> 1] & 0xFFFFu);
                         const int e = elem_index(sl, j, hh);
-                        if (!elem_valid(sl, e)) continue;
-                        if (okey(bits) == ks.key) {
+                        if (tie < 0 && elem_valid(sl, e) && okey(bits) == ks.key) {
                             if (--k2 == 0) tie = e;
                         }
                     }
@@ -1229,7 +1233,7 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
 // chain + bonus + outputs (one cluster per request)
 
 struct ChainSmem {
-    unsigned long long tsum[kNT];
+    unsigned long long tsum[kNW];  // warp sums
     unsigned long long pub[2][2];  // per exchange: CTA total
     int32_t sel[8];
     unsigned long long red64[kNW];
@@ -1318,15 +1322,8 @@ __device__ void write_request(const VerifyArgs& a, int b, int acc, long long bon
     a.new_seq[b] = a.prefix[b] + acc + 1;
 }
 
-// contiguous element range of thread t inside slice [e0, e1)
-__device__ __forceinline__ void thread_range(int e0, int e1, int& lo, int& hi) {
-    const int n = e1 - e0;
-    const int per = (n + kNT - 1) / kNT;
-    lo = min(e0 + (int)threadIdx.x * per, e1);
-    hi = min(lo + per, e1);
-}
-
 __global__ void __launch_bounds__(kNT) chain_kernel(VerifyArgs a) {
+    extern __shared__ __align__(16) unsigned char chain_smem[];
     __shared__ ChainSmem shm;
     ChainSmem* sh = &shm;
     cg::cluster_group cluster = cg::this_cluster();
@@ -1407,41 +1404,50 @@ __global__ void __launch_bounds__(kNT) chain_kernel(VerifyArgs a) {
             }
         }
         const uint16_t* prow = trow_ok ? tgt + tr * a.stride : nullptr;
-        int L = (a.V + kCS - 1) / kCS;
+        const int L = ((a.V + kCS - 1) / kCS + 7) & ~7;
         const int e0 = min(rank * L, a.V), e1 = min(e0 + L, a.V);
-        int lo, hi;
-        thread_range(e0, e1, lo, hi);
+        // stage this CTA's slice of both rows in shared memory (16-byte loads; element e sits
+        // at position e - e0 + off, off = the row's misalignment in elements)
+        uint16_t* sp = reinterpret_cast<uint16_t*>(chain_smem);
+        uint16_t* sq = sp + (L + 16);
+        const int poff = prow ? (int)((reinterpret_cast<uintptr_t>(prow) & 15u) >> 1) : 0;
+        const int qoff = qrow ? (int)((reinterpret_cast<uintptr_t>(qrow) & 15u) >> 1) : 0;
+        if (e1 > e0) {
+            if (prow) {
+                const uint4* src = reinterpret_cast<const uint4*>(prow + e0 - poff);
+                const int nv = (e1 - e0 + poff + 7) >> 3;
+                for (int v = tid; v < nv; v += kNT) reinterpret_cast<uint4*>(sp)[v] = __ldg(src + v);
+            }
+            if (qrow) {
+                const uint4* src = reinterpret_cast<const uint4*>(qrow + e0 - qoff);
+                const int nv = (e1 - e0 + qoff + 7) >> 3;
+                for (int v = tid; v < nv; v += kNT) reinterpret_cast<uint4*>(sq)[v] = __ldg(src + v);
+            }
+        }
+        __syncthreads();
+        // warp w scans elements [e0 + w*Lw, ...) in groups of 32 consecutive elements
+        const int n = e1 - e0;
+        const int Lw = (((n + kNW - 1) / kNW) + 31) & ~31;
+        const int wid = tid >> 5;
+        const int w0 = min(e0 + wid * Lw, e1), w1 = min(w0 + Lw, e1);
         unsigned ex = 0;
         bool use_pure = pure;
-        unsigned long long M = 0, cum = 0, tot = 0, mine = 0;
+        unsigned long long M = 0, cum = 0, tot = 0;
         for (int attempt = 0; attempt < 2; ++attempt) {
-            mine = 0;
-            for (int i = lo; i < hi; ++i) {
-                const uint32_t pb = prow ? prow[i] : 0xFF80u;
-                const uint32_t qb = qrow ? qrow[i] : 0xFF80u;
+            unsigned long long mine = 0;
+            for (int i = w0 + lane; i < w1; i += 32) {
+                const uint32_t pb = prow ? sp[i - e0 + poff] : 0xFF80u;
+                const uint32_t qb = qrow ? sq[i - e0 + qoff] : 0xFF80u;
                 mine += fix_w(resid_w(dt, dq, onehot, use_pure, pb, qb, i));
             }
-            // CTA exclusive scan of thread sums
-            sh->tsum[tid] = mine;
+            mine = warp_sum_u64(mine);
+            if (lane == 0) sh->tsum[wid] = mine;
             __syncthreads();
-            if (tid < 32) {
-                unsigned long long s = 0;
-                for (int i = 0; i < kNT / 32; ++i) s += sh->tsum[lane * (kNT / 32) + i];
-                unsigned long long inc = s;
-#pragma unroll
-                for (int o = 1; o < 32; o <<= 1) {
-                    const unsigned long long v = __shfl_up_sync(0xffffffffu, inc, o);
-                    if (lane >= o) inc += v;
-                }
-                unsigned long long run = inc - s;
-                for (int i = 0; i < kNT / 32; ++i) {
-                    const unsigned long long x = sh->tsum[lane * (kNT / 32) + i];
-                    sh->tsum[lane * (kNT / 32) + i] = run;  // exclusive prefix
-                    run += x;
-                }
-                if (lane == 31) sh->pub[ex & 1][0] = inc;
+            if (tid == 0) {
+                unsigned long long t_ = 0;
+                for (int i = 0; i < kNW; ++i) t_ += sh->tsum[i];
+                sh->pub[ex & 1][0] = t_;
             }
-            __syncthreads();
             cluster_barrier();
             const unsigned exn = ex++;
             M = 0;
@@ -1452,26 +1458,50 @@ __global__ void __launch_bounds__(kNT) chain_kernel(VerifyArgs a) {
                 if (q == rank) tot = v;
                 M += v;
             }
-            if (!use_pure && M == 0) { use_pure = true; continue; }
+            if (!use_pure && M == 0) {
+                use_pure = true;
+                __syncthreads();
+                continue;
+            }
             break;
         }
         const long long thr = scale_floor(uf, M);
         if (thr == -2) {
             if (rank == 0 && tid == 0) write_request(a, b, acc, (long long)a.V - 1);
         } else if ((long long)(cum + tot) > thr && (rank == 0 || (long long)cum <= thr)) {
-            // this CTA holds the crossing: the first CTA whose running total passes thr
-            const long long rel = thr - (long long)cum;
-            const unsigned long long pre = sh->tsum[tid];
-            if ((long long)(pre + mine) > rel && (tid == 0 || (long long)pre <= rel)) {
-                unsigned long long run = pre;
+            // this CTA holds the crossing: the first CTA whose running total passes thr;
+            // then the first warp, the first group of 32 and the first lane
+            long long rel = thr - (long long)cum;
+            int wstar = kNW - 1;
+            for (int i = 0; i < kNW; ++i) {
+                const long long ws_ = (long long)sh->tsum[i];
+                if (ws_ > rel) { wstar = i; break; }
+                rel -= ws_;
+            }
+            if (wid == wstar) {
                 long long bonus = (long long)a.V - 1;
-                for (int i = lo; i < hi; ++i) {
-                    const uint32_t pb = prow ? prow[i] : 0xFF80u;
-                    const uint32_t qb = qrow ? qrow[i] : 0xFF80u;
-                    run += fix_w(resid_w(dt, dq, onehot, use_pure, pb, qb, i));
-                    if ((long long)run > rel) { bonus = i; break; }
+                for (int g0 = w0; g0 < w1; g0 += 32) {
+                    const int i = g0 + lane;
+                    unsigned long long F = 0;
+                    if (i < w1) {
+                        const uint32_t pb = prow ? sp[i - e0 + poff] : 0xFF80u;
+                        const uint32_t qb = qrow ? sq[i - e0 + qoff] : 0xFF80u;
+                        F = fix_w(resid_w(dt, dq, onehot, use_pure, pb, qb, i));
+                    }
+                    unsigned long long inc = F;
+#pragma unroll
+                    for (int o = 1; o < 32; o <<= 1) {
+                        const unsigned long long v = __shfl_up_sync(0xffffffffu, inc, o);
+                        if (lane >= o) inc += v;
+                    }
+                    const uint32_t bal = __ballot_sync(0xffffffffu, i < w1 && (long long)inc > rel);
+                    if (bal) {
+                        bonus = g0 + __ffs(bal) - 1;
+                        break;
+                    }
+                    rel -= (long long)__shfl_sync(0xffffffffu, inc, 31);
                 }
-                write_request(a, b, acc, bonus);
+                if (lane == 0) write_request(a, b, acc, bonus);
             }
         } else if (rank == 0 && (long long)M <= thr) {
             // no crossing (mass 0): the default of the reference loop
@@ -1549,8 +1579,16 @@ int launch_chain(VerifyArgs a, cudaStream_t stream) {
     attr[0].val.clusterDim.x = kCS;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
+    const int L = ((a.V + kCS - 1) / kCS + 7) & ~7;
+    const size_t smem = (size_t)2 * (L + 16) * sizeof(uint16_t);
+    static size_t attr_smem = 0;
+    if (smem > 48 * 1024 && smem > attr_smem) {
+        if (cudaFuncSetAttribute(chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+            return kLaunchFailed;
+        attr_smem = smem;
+    }
     cfg.blockDim = dim3(kNT, 1, 1);
-    cfg.dynamicSmemBytes = 0;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
