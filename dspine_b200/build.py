@@ -47,15 +47,18 @@ def headers():
     return sorted(CSRC.glob("*.h")) + sorted(CSRC.glob("*.cuh")) + sorted((ROOT / "include").glob("*.h"))
 
 
-def build(verbose: bool = False, ptxas_info: bool = False, checked: bool = False) -> Path:
+def build(verbose: bool = False, ptxas_info: bool = False, checked: bool = False,
+          profile: bool = False) -> Path:
     """Compile every csrc/*.cu and link the shared library.  ``checked`` builds the index-
-    checking variant (-DDSV_CHECKS) into _build/checked/ instead of the product library."""
-    out_dir = (ROOT / "_build" / "checked") if checked else OUT_DIR
-    obj_dir = OBJ_DIR.parent / ("obj_checked" if checked else "obj")
+    checking variant (-DDSV_CHECKS) into _build/checked/, ``profile`` the phase-timing variant
+    (-DDSV_PROFILE) into _build/profile/, instead of the product library."""
+    variant = "checked" if checked else ("profile" if profile else None)
+    out_dir = (ROOT / "_build" / variant) if variant else OUT_DIR
+    obj_dir = OBJ_DIR.parent / (f"obj_{variant}" if variant else "obj")
     lib = out_dir / LIB.name
     out_dir.mkdir(parents=True, exist_ok=True)
     obj_dir.mkdir(parents=True, exist_ok=True)
-    extra = ["-DDSV_CHECKS"] if checked else []
+    extra = (["-DDSV_CHECKS"] if checked else []) + (["-DDSV_PROFILE"] if profile else [])
     cc = nvcc()
     hdr_mtime = max((p.stat().st_mtime for p in headers()), default=0)
     objs = []
@@ -80,4 +83,5 @@ def build(verbose: bool = False, ptxas_info: bool = False, checked: bool = False
 
 
 if __name__ == "__main__":
-    print(build(verbose=True, ptxas_info="-v" in sys.argv, checked="--checked" in sys.argv))
+    print(build(verbose=True, ptxas_info="-v" in sys.argv, checked="--checked" in sys.argv,
+                profile="--profile" in sys.argv))

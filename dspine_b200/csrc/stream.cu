@@ -58,6 +58,39 @@ constexpr float kS2 = 22.5f;             // level-2 scale = 30 * kS1 (exact)
 constexpr float kTwo23 = 8388608.0f;
 
 // ---------------------------------------------------------------------------------------
+// optional phase profiling (builds with -DDSV_PROFILE only): thread 0 of every CTA adds the
+// %globaltimer duration of each phase to u64 counters in the workspace's task-result area,
+// which this path does not otherwise use: counter [cat * 16 + phase], task count at phase 15
+
+#ifdef DSV_PROFILE
+#define PROF_START() unsigned long long prof_t = globaltimer_ns()
+#define PROF_MARK(cat_, ph)                                                              \
+    do {                                                                                 \
+        if (threadIdx.x == 0) {                                                          \
+            const unsigned long long prof_n = globaltimer_ns();                          \
+            atomicAdd(reinterpret_cast<unsigned long long*>(a.res) + (cat_) * 16 + (ph), \
+                      prof_n - prof_t);                                                  \
+            prof_t = prof_n;                                                             \
+        }                                                                                \
+    } while (0)
+#define PROF_END(cat_, ph)                                                                  \
+    do {                                                                                    \
+        PROF_MARK(cat_, ph);                                                                \
+        if (threadIdx.x == 0) atomicAdd(reinterpret_cast<unsigned long long*>(a.res) + (cat_) * 16 + 15, 1ull); \
+    } while (0)
+#else
+#define PROF_START() \
+    do {             \
+    } while (0)
+#define PROF_MARK(cat_, ph) \
+    do {                    \
+    } while (0)
+#define PROF_END(cat_, ph) \
+    do {                   \
+    } while (0)
+#endif
+
+// ---------------------------------------------------------------------------------------
 // small helpers
 
 __device__ __forceinline__ void cluster_barrier() {
@@ -596,6 +629,7 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
                 sh->tasks[i] = decode_task(a, sh, cid + (it + i) * a.num_clusters);
             __syncthreads();
         }
+        PROF_START();
         const TaskInfo ti = sh->tasks[it % kTaskCap];
         const int leader = it % kCS;
         const bool lead = cx.rank == leader;
@@ -656,6 +690,7 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
             pb.first = sh->first_min;
         }
         if (tid < kNW) pb.wmax[tid] = sh->red32[tid];
+        PROF_MARK(ti.cat, 0);
         cluster_barrier();  // exchange 1
         const unsigned ex1 = cx.ex++;
         if (tid < 32) {
@@ -678,10 +713,12 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
         const uint32_t mkey = (uint32_t)sh->sel[10];
         const int argmax = sh->sel[11];
         const float m = bf(key_bits(mkey));
+        PROF_MARK(ti.cat, 1);
 
         if (ti.cat == kGreedy) {
             if (lead && tid == 0) put_desc(a, ti, m, mkey, argmax, 1ull << kFixBits,
                                            argmax == 0x7fffffff ? 0 : argmax, kDescGreedy);
+            PROF_END(ti.cat, 2);
             continue;
         }
 
@@ -791,6 +828,7 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
                 }
             }
         }
+        PROF_MARK(ti.cat, 2);
         cluster_barrier();  // exchange 2
         const unsigned ex2 = cx.ex++;
         if (tid < 32) {
@@ -816,8 +854,10 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
         const bool win_over = sh->sel[13] != 0;
         const long long thr = (ti.p < 1.0f) ? scale_floor(ti.p, S) : 0x7fffffffffffffffll;
 
+        PROF_MARK(ti.cat, 3);
         if (cat == kKeepAll) {
             if (lead && tid == 0) put_desc(a, ti, m, 0u, 0x7fffffff, S, 0, 0u);
+            PROF_END(ti.cat, 4);
             continue;
         }
 
@@ -886,6 +926,7 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
                     }
                 }
             }
+            PROF_END(ti.cat, 4);
             continue;
         }
 
@@ -917,6 +958,7 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
             cluster_barrier();  // exchange 2b
             ex_bins = cx.ex++;
             cat = kBinned;
+            PROF_MARK(ti.cat, 5);
         }
 
         // level-1 walk (every CTA, identical inputs)
@@ -944,9 +986,11 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
         }
         __syncthreads();
         const int b1 = sh->sel[0];
+        PROF_MARK(ti.cat, 6);
         if (b1 < 0) {
             // no boundary: every element is kept
             if (lead && tid == 0) put_desc(a, ti, m, 0u, 0x7fffffff, S, 0, 0u);
+            PROF_END(ti.cat, 14);
             continue;
         }
         unsigned long long cum_cnt = sh->self64[0], cum_mass = sh->self64[1];
@@ -1042,6 +1086,7 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
             __syncthreads();
         }
         const int b2 = sh->sel[3];
+        PROF_MARK(ti.cat, 7);
         if (b2 < 0) {
             // cannot happen when level 1 found a boundary; keep everything defensively
             if (lead && tid == 0) {
@@ -1090,6 +1135,9 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
                     }
                 }
             }
+#ifdef DSV_PROFILE
+            if (tid == 0) atomicAdd(reinterpret_cast<unsigned long long*>(a.res) + ti.cat * 16 + 11, 1ull);
+#endif
             cluster_barrier();  // exchange 4 (chunk)
             cx.ex++;
             // sum the cluster's counts into acc (as u32) and walk
@@ -1135,6 +1183,7 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
             }
             continue;
         }
+        PROF_MARK(ti.cat, 8);
         // kept among the ks.count elements with the boundary key
         unsigned long long ntie = ks.count;
         if ((long long)(ks.cnt + ntie) > kk) ntie = (unsigned long long)(kk - (long long)ks.cnt);
@@ -1147,6 +1196,7 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
 
         if (ntie >= ks.count) {
             if (lead && tid == 0) put_desc(a, ti, m, ks.key, 0x7fffffff, skept, 0, 0u);
+            PROF_END(ti.cat, 9);
             continue;
         }
         // ---- tie cut: the ntie-th occurrence (index order) of the boundary key ----------------
@@ -1224,6 +1274,7 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
                 put_desc(a, ti, m, ks.key, tie, skept, 0, 0u);
             }
         }
+        PROF_END(ti.cat, 10);
     }
     // no CTA may leave while a peer can still read its shared memory
     cluster_barrier();
