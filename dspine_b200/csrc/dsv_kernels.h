@@ -42,8 +42,12 @@ inline size_t verify_done_bytes(int B) { return ((size_t)B * 4 + 63) & ~(size_t)
 inline size_t verify_desc_offset(int B) {
     return 64 + verify_done_bytes(B) + (size_t)B * 16 * sizeof(TaskResult);
 }
-inline size_t verify_workspace_bytes(int B) {
+inline size_t verify_gmax_offset(int B) {
     return verify_desc_offset(B) + (size_t)B * 16 * 2 * sizeof(RowDesc);
+}
+// [u64 x B x 16]: greedy rows' packed (max key << 32 | ~first index), reset after use
+inline size_t verify_workspace_bytes(int B) {
+    return verify_gmax_offset(B) + (size_t)B * 16 * sizeof(unsigned long long);
 }
 
 struct VerifyArgs {
@@ -84,6 +88,7 @@ struct VerifyArgs {
     unsigned int* done;
     TaskResult* res;
     RowDesc* desc;             // [B,16,2] row descriptors (streaming path)
+    unsigned long long* gmax;  // [B,16] greedy rows: max key << 32 | (0xFFFFFFFF - first index)
 };
 
 // launchers (return a dsv::Status)

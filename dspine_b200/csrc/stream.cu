@@ -48,7 +48,7 @@ constexpr int kWinTotal = 512;   // window entries per row
 constexpr int kListCap = 4096;   // level-2 compaction list per CTA
 constexpr int kKeyChunk = 512;   // keys per level-3 histogram chunk
 constexpr int kMaxB = 1024;      // requests per launch handled by this path
-constexpr int kTaskCap = 256;    // decoded tasks of one cluster held in shared memory at a time
+constexpr int kTaskCap = 64;     // decoded tasks of one cluster held in shared memory at a time
 
 enum Cat : int { kGreedy = 0, kKeepAll = 1, kWindow = 2, kBinned = 3 };
 
@@ -540,27 +540,41 @@ __device__ __forceinline__ int composite_bin(uint32_t key, float m, float c) {
     return b1 * kSub + bin2_of(yc, b1);
 }
 
-// keys in [klo, khi] within [kmin, kmax] (the keys of -inf and of the row max) are exactly
-// those whose composite bin equals target
-__device__ void key_range(int target, uint32_t kmin, uint32_t kmax, float m, float c,
-                          uint32_t& klo, uint32_t& khi) {
-    // largest key with bin >= target
-    uint32_t lo = kmin, hi = kmax;
-    while (lo < hi) {
-        const uint32_t mid = (lo + hi + 1) >> 1;
-        if (composite_bin(mid, m, c) >= target) lo = mid; else hi = mid - 1;
-    }
-    khi = lo;
-    // smallest key with bin <= target
-    lo = kmin;
-    hi = kmax;
-    while (lo < hi) {
-        const uint32_t mid = (lo + hi) >> 1;
-        if (composite_bin(mid, m, c) <= target) hi = mid; else lo = mid + 1;
-    }
-    klo = lo;
+// largest key in [kmin, kmax] whose composite bin is >= target, given bin(kmin) >= target (one
+// warp, 32 probes per step; bins are non-increasing in the key, so the probes that pass form a
+// prefix)
+__device__ __forceinline__ int level_bin(uint32_t key, float m, float c, int lvl) {
+    return lvl == 1 ? bin1_of(y_clamped(bf(key_bits(key)), m, c)) : composite_bin(key, m, c);
 }
 
+__device__ uint32_t largest_key_ge(int target, uint32_t kmin, uint32_t kmax, float m, float c,
+                                   int lvl) {
+    const int lane = threadIdx.x & 31;
+    uint32_t lo = kmin, hi = kmax;  // invariant: bin(lo) >= target, answer in [lo, hi]
+    while (lo < hi) {
+        const uint32_t step = (hi - lo + 31) / 32;
+        const uint32_t probe = lo + (uint32_t)(lane + 1) * step;
+        const bool ok = probe <= hi && level_bin(probe, m, c, lvl) >= target;
+        const int nt = __popc(__ballot_sync(0xffffffffu, ok));
+        const uint32_t nlo = lo + (uint32_t)nt * step;
+        const uint32_t nhi = min(hi, lo + (uint32_t)(nt + 1) * step - 1u);
+        lo = nlo;
+        hi = nhi;
+    }
+    return lo;
+}
+
+// keys in [klo, khi] within [kmin, kmax] (the keys of -inf and of the row max) are exactly
+// those whose composite bin equals target (one warp)
+__device__ void key_range(int target, uint32_t kmin, uint32_t kmax, float m, float c, int lvl,
+                          uint32_t& klo, uint32_t& khi) {
+    khi = largest_key_ge(target, kmin, kmax, m, c, lvl);
+    // smallest key with bin <= target = 1 + largest key with bin >= target + 1
+    if (level_bin(kmin, m, c, lvl) >= target + 1)
+        klo = largest_key_ge(target + 1, kmin, kmax, m, c, lvl) + 1u;
+    else
+        klo = kmin;
+}
 
 // Rare follow-up pass (window overflow -> level-1 bins of every valid element; level-2 sub-bins
 // of bin b1 that do not fit the compaction list): re-reads the slice from global memory (L2-hot)
@@ -684,6 +698,18 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
             }
             if (best != 0x7fffffff) atomicMin(&sh->first_min, best);
         }
+        if (ti.cat == kGreedy) {
+            // greedy rows need only the max and its first index: combine the slices with one
+            // global atomicMax on (key << 32 | ~index); no cluster exchange
+            __syncthreads();
+            if (tid == 0 && sh->first_min != 0x7fffffff) {
+                const unsigned long long packed =
+                    ((unsigned long long)ckey << 32) | (0xFFFFFFFFull - (unsigned)sh->first_min);
+                atomicMax(&a.gmax[ti.b * kT + ti.s], packed);
+            }
+            PROF_END(ti.cat, 2);
+            continue;
+        }
         __syncthreads();
         if (tid == 0) {
             pb.maxkey = ckey;
@@ -711,16 +737,9 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
         }
         __syncthreads();
         const uint32_t mkey = (uint32_t)sh->sel[10];
-        const int argmax = sh->sel[11];
         const float m = bf(key_bits(mkey));
         PROF_MARK(ti.cat, 1);
 
-        if (ti.cat == kGreedy) {
-            if (lead && tid == 0) put_desc(a, ti, m, mkey, argmax, 1ull << kFixBits,
-                                           argmax == 0x7fffffff ? 0 : argmax, kDescGreedy);
-            PROF_END(ti.cat, 2);
-            continue;
-        }
 
         // ---- window threshold (k-th largest warp maximum of the cluster) -----------------
         int cat = ti.cat;
@@ -769,20 +788,7 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
                 const Pair pr = exp_pair(u[q], nm, c2);
                 hs += pr.h0 + pr.h1;
                 ls += pr.l0 + pr.l1;
-                if (cat == kWindow) {
-                    const uint32_t ge = bf2_ge(u[q], tau2);
-                    if (ge) {
-#pragma unroll
-                        for (int h = 0; h < 2; ++h) {
-                            if (!(ge & (h ? 0xFFFF0000u : 0x0000FFFFu))) continue;
-                            const int e = elem_index(sl, j, 2 * q + h);
-                            if (!elem_valid(sl, e)) continue;
-                            const uint32_t bits = h ? (u[q] >> 16) : (u[q] & 0xFFFFu);
-                            const uint32_t pos = atomicAdd(&sh->nlist, 1u);
-                            if (pos < kWinCap) sh->win[pos] = (okey(bits) << 16) | (uint32_t)(e - sl.e0);
-                        }
-                    }
-                } else if (cat == kBinned) {
+                if (cat == kBinned) {
                     const int b0 = bin1_of(pr.yc.x), b1 = bin1_of(pr.yc.y);
                     uint2* p0 = &sh->acc[b0 * kNT + tid];
                     uint2 v0 = *p0;
@@ -796,6 +802,29 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
                     *p1 = v1;
                     atomicAdd(&sh->bcnt[b0], 1u);
                     atomicAdd(&sh->bcnt[b1], 1u);
+                }
+            }
+        }
+        if (cat == kWindow) {
+            // candidates (value >= tau) in a separate cheap scan: a branch inside the exp loop
+            // would cut it into blocks the compiler cannot interleave
+#pragma unroll
+            for (int j = 0; j < NVT; ++j) {
+                const uint32_t* u = reinterpret_cast<const uint32_t*>(&w[j]);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const uint32_t ge = bf2_ge(u[q], tau2);
+                    if (ge) {
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const int e = elem_index(sl, j, 2 * q + h);
+                            if ((ge & (h ? 0xFFFF0000u : 0x0000FFFFu)) && elem_valid(sl, e)) {
+                                const uint32_t bits = h ? (u[q] >> 16) : (u[q] & 0xFFFFu);
+                                const uint32_t pos = atomicAdd(&sh->nlist, 1u);
+                                if (pos < kWinCap) sh->win[pos] = (okey(bits) << 16) | (uint32_t)(e - sl.e0);
+                            }
+                        }
+                    }
                 }
             }
         }
@@ -863,22 +892,22 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
 
         if (cat == kWindow && !win_over && win_total <= (uint32_t)kWinTotal) {
             if (lead) {
-                // gather every CTA's entries (key << 16 | local index) as (key, global index)
+                // gather every CTA's entries (key << 16 | local index) as (key, global index):
+                // counts of all CTAs in one DSMEM round, then every entry in parallel
                 uint2* g = sh->acc;  // reuse: up to kWinTotal entries
                 __syncthreads();
-                if (tid == 0) sh->sel[1] = 0;
+                if (tid < 32) {
+                    const uint32_t nw = lane < kCS ? remote_pub(cx, lane, ex2)->nwin : 0u;
+                    const uint32_t incl = warp_incl_u32(nw);
+                    if (lane < kCS) sh->sel[1 + lane] = (int)(incl - nw);  // sel[1..8]: offsets
+                }
                 __syncthreads();
-                for (int q = 0; q < kCS; ++q) {
-                    const Pub* rp = remote_pub(cx, q, ex2);
-                    const uint32_t nw = rp->nwin;
-                    const uint32_t* rw = cluster.map_shared_rank(sh->win, q);
+                for (int f = tid; f < (int)win_total; f += kNT) {
+                    int q = 0;
+                    while (q + 1 < kCS && sh->sel[2 + q] <= f) ++q;
+                    const uint32_t e = cluster.map_shared_rank(sh->win, q)[f - sh->sel[1 + q]];
                     const int qe0 = min(q * cx.L, a.V);
-                    int basepos = 0;
-                    for (int p2 = 0; p2 < q; ++p2) basepos += (int)remote_pub(cx, p2, ex2)->nwin;
-                    for (int i = tid; i < (int)nw; i += kNT) {
-                        const uint32_t e = rw[i];
-                        g[basepos + i] = make_uint2(e >> 16, (uint32_t)(qe0 + (int)(e & 0xFFFFu)));
-                    }
+                    g[f] = make_uint2(e >> 16, (uint32_t)(qe0 + (int)(e & 0xFFFFu)));
                 }
                 __syncthreads();
                 const int n = (int)win_total;
@@ -995,6 +1024,18 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
         }
         unsigned long long cum_cnt = sh->self64[0], cum_mass = sh->self64[1];
 
+        // keys of bin b1: when they fit one key chunk, count keys directly (no level 2)
+        if (tid < 32) {
+            uint32_t klo1, khi1;
+            key_range(b1, okey(0xFF80u), mkey, m, ti.c, 1, klo1, khi1);
+            if (lane == 0) {
+                sh->sel[4] = (int)klo1;
+                sh->sel[5] = (int)khi1;
+            }
+        }
+        __syncthreads();
+        int b2 = -2;  // -2: level 2 skipped
+        if ((uint32_t)sh->sel[5] - (uint32_t)sh->sel[4] + 1u > (uint32_t)kKeyChunk) {
         // ---- level 2: sub-bins of bin b1 ---------------------------------------------------
         {
             // valid elements of bin b1 in this CTA (fill slots are excluded from the list)
@@ -1007,20 +1048,39 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
             if (tid == 0) sh->nlist = 0;
             __syncthreads();
             if (compact) {
+                // positions by a block-wide exclusive scan of per-thread counts (no atomics)
+                uint32_t cnt_me = 0;
 #pragma unroll
                 for (int j = 0; j < NVT; ++j) {
                     const uint32_t* u = reinterpret_cast<const uint32_t*>(&w[j]);
 #pragma unroll
-                    for (int q = 0; q < 4; ++q) {
+                    for (int hh = 0; hh < 8; ++hh) {
+                        const uint32_t bits = (hh & 1) ? (u[hh >> 1] >> 16) : (u[hh >> 1] & 0xFFFFu);
+                        cnt_me += (bin1_of(y_clamped(bf(bits), m, ti.c)) == b1 &&
+                                   elem_valid(sl, elem_index(sl, j, hh))) ? 1u : 0u;
+                    }
+                }
+                const uint32_t incl = warp_incl_u32(cnt_me);
+                if (lane == 31) sh->red32[wid] = incl;
+                __syncthreads();
+                uint32_t pos = incl - cnt_me, total = 0;
+                for (int i = 0; i < kNW; ++i) {
+                    if (i < wid) pos += sh->red32[i];
+                    total += sh->red32[i];
+                }
+                if (tid == 0) sh->nlist = total;
+                if (cnt_me) {
 #pragma unroll
-                        for (int h = 0; h < 2; ++h) {
-                            const uint32_t bits = h ? (u[q] >> 16) : (u[q] & 0xFFFFu);
-                            const float yc = y_clamped(bf(bits), m, ti.c);
-                            if (bin1_of(yc) != b1) continue;
-                            const int e = elem_index(sl, j, 2 * q + h);
-                            if (!elem_valid(sl, e)) continue;
-                            const uint32_t pos = atomicAdd(&sh->nlist, 1u);
-                            if (pos < kListCap) sh->list[pos] = (bits << 16) | (uint32_t)(e - sl.e0);
+                    for (int j = 0; j < NVT; ++j) {
+                        const uint32_t* u = reinterpret_cast<const uint32_t*>(&w[j]);
+#pragma unroll
+                        for (int hh = 0; hh < 8; ++hh) {
+                            const uint32_t bits = (hh & 1) ? (u[hh >> 1] >> 16) : (u[hh >> 1] & 0xFFFFu);
+                            const int e = elem_index(sl, j, hh);
+                            if (bin1_of(y_clamped(bf(bits), m, ti.c)) == b1 && elem_valid(sl, e)) {
+                                if (pos < kListCap) sh->list[pos] = (bits << 16) | (uint32_t)(e - sl.e0);
+                                ++pos;
+                            }
                         }
                     }
                 }
@@ -1085,7 +1145,7 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
             }
             __syncthreads();
         }
-        const int b2 = sh->sel[3];
+        b2 = sh->sel[3];
         PROF_MARK(ti.cat, 7);
         if (b2 < 0) {
             // cannot happen when level 1 found a boundary; keep everything defensively
@@ -1097,15 +1157,18 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
         }
         cum_cnt = sh->self64[2];
         cum_mass = sh->self64[3];
-
-        // ---- level 3: per-key counts of the boundary sub-bin, in chunks from the top --------
-        if (tid == 0) {
-            uint32_t klo, khi;
-            key_range(b1 * kSub + b2, okey(0xFF80u), mkey, m, ti.c, klo, khi);
-            sh->sel[4] = (int)klo;
-            sh->sel[5] = (int)khi;
+        if (tid < 32) {
+            uint32_t klo2, khi2;
+            key_range(b1 * kSub + b2, okey(0xFF80u), mkey, m, ti.c, 2, klo2, khi2);
+            if (lane == 0) {
+                sh->sel[4] = (int)klo2;
+                sh->sel[5] = (int)khi2;
+            }
         }
         __syncthreads();
+        }  // level 2
+
+        // ---- level 3: per-key counts of the boundary (sub-)bin, in chunks from the top ------
         const uint32_t klo = (uint32_t)sh->sel[4], khi = (uint32_t)sh->sel[5];
         KeyStop ks;
         ks.found = 0;
@@ -1159,6 +1222,19 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
                     sh->self64[6] = r.F;
                 }
             }
+            __syncthreads();
+            if (sh->sel[6]) {
+                // occurrences of the boundary key in the CTAs before this one, and in this one
+                const uint32_t kidx = top - (uint32_t)sh->sel[7];
+                if (tid < 32) {
+                    const uint32_t f = lane < cx.rank ? cluster.map_shared_rank(sh->khist, lane)[kidx] : 0u;
+                    const uint32_t sum_ = warp_sum_u32(f);
+                    if (lane == 0) {
+                        sh->sel[9] = (int)sum_;
+                        sh->sel[14] = (int)sh->khist[kidx];
+                    }
+                }
+            }
             // no CTA may clear its chunk counts while a peer still reads them
             cluster_barrier();
             cx.ex++;
@@ -1200,36 +1276,30 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
             continue;
         }
         // ---- tie cut: the ntie-th occurrence (index order) of the boundary key ----------------
-        // index order inside a CTA is (vector-row j, thread, half); per-row totals go to shared
-        // memory so that no per-row array stays in registers next to the row slice
-        uint32_t* rowcnt = reinterpret_cast<uint32_t*>(sh->acc);          // [NVT]
-        uint32_t* wrow = reinterpret_cast<uint32_t*>(sh->acc) + 64;       // [kNW]
-        __syncthreads();
-        if (tid < NVT) rowcnt[tid] = 0;
-        __syncthreads();
-        uint32_t mine = 0;
-#pragma unroll
-        for (int j = 0; j < NVT; ++j) {
-            const uint32_t* u = reinterpret_cast<const uint32_t*>(&w[j]);
-            uint32_t c = 0;
-#pragma unroll
-            for (int hh = 0; hh < 8; ++hh) {
-                const uint32_t bits = (hh & 1) ? (u[hh >> 1] >> 16) : (u[hh >> 1] & 0xFFFFu);
-                c += (okey(bits) == ks.key && elem_valid(sl, elem_index(sl, j, hh))) ? 1u : 0u;
-            }
-            const uint32_t ws_ = warp_sum_u32(c);
-            if (lane == 0 && ws_) atomicAdd(&rowcnt[j], ws_);
-            mine += c;
-        }
-        const uint32_t cta_occ = (uint32_t)cta_sum_u64(mine, sh);  // includes __syncthreads
-        Pub& pb5 = sh->pub[cx.ex & 1];
-        if (tid == 0) pb5.flag = cta_occ;
-        cluster_barrier();  // exchange 5
-        const unsigned ex5 = cx.ex++;
-        unsigned long long before = 0;
-        for (int q = 0; q < cx.rank; ++q) before += remote_pub(cx, q, ex5)->flag;
-        // the CTA holding occurrence number ntie (1-based) finds it and writes the descriptor
+        // the CTA holding it is known from the per-CTA key counts of the last chunk
+        const unsigned long long before = (unsigned)sh->sel[9];
+        const unsigned long long cta_occ = (unsigned)sh->sel[14];
         if (before < ntie && before + cta_occ >= ntie) {
+            // index order inside a CTA is (vector-row j, thread, half); per-row totals go to
+            // shared memory so that no per-row array stays in registers next to the row slice
+            uint32_t* rowcnt = reinterpret_cast<uint32_t*>(sh->acc);          // [NVT]
+            uint32_t* wrow = reinterpret_cast<uint32_t*>(sh->acc) + 64;       // [kNW]
+            __syncthreads();
+            if (tid < NVT) rowcnt[tid] = 0;
+            __syncthreads();
+#pragma unroll
+            for (int j = 0; j < NVT; ++j) {
+                const uint32_t* u = reinterpret_cast<const uint32_t*>(&w[j]);
+                uint32_t c = 0;
+#pragma unroll
+                for (int hh = 0; hh < 8; ++hh) {
+                    const uint32_t bits = (hh & 1) ? (u[hh >> 1] >> 16) : (u[hh >> 1] & 0xFFFFu);
+                    c += (okey(bits) == ks.key && elem_valid(sl, elem_index(sl, j, hh))) ? 1u : 0u;
+                }
+                const uint32_t ws_ = warp_sum_u32(c);
+                if (lane == 0 && ws_) atomicAdd(&rowcnt[j], ws_);
+            }
+            __syncthreads();
             uint32_t need = (uint32_t)(ntie - before);
             int jstar = NVT - 1;
             for (int j = 0; j < NVT; ++j) {
@@ -1391,6 +1461,38 @@ __global__ void __launch_bounds__(kNT) chain_kernel(VerifyArgs a) {
     const uint16_t* tgt = reinterpret_cast<const uint16_t*>(a.tgt);
     const uint16_t* drf = reinterpret_cast<const uint16_t*>(a.drf);
 
+    if (greedy) {
+        // one-hot p at each target row's first argmax (packed by the row kernel), one-hot q at
+        // the drafted token: rank 0 decides alone and resets the packed maxima for the next launch
+        if (rank == 0 && tid < 32) {
+            const int s = lane;
+            bool accp = false;
+            long long am = 0;
+            if (s < cap) {
+                const unsigned long long g = a.gmax[b * kT + s];
+                am = g ? (long long)(0xFFFFFFFFull - (g & 0xFFFFFFFFull)) : 0ll;
+            }
+            if (s < cap - 1) {
+                const long long tok = a.cand[b * kT + s + 1];
+                const bool valid = tok >= 0 && tok < a.V;
+                const float p = (valid && tok == am) ? 1.0f : 0.0f;
+                const float q = valid ? 1.0f : 0.0f;
+                accp = q > 0.0f && q <= 1.0f && __fmul_rn(a.u[b * 15 + s], q) < p;
+            }
+            const uint32_t rej = __ballot_sync(0xffffffffu, !accp) & ((1u << (cap - 1)) - 1u);
+            const int acc = rej ? __ffs(rej) - 1 : cap - 1;
+            const long long ga = __shfl_sync(0xffffffffu, am, acc);
+            __syncwarp();
+            if (s < cap) a.gmax[b * kT + s] = 0ull;
+            if (lane == 0) {
+                // the residual against a one-hot q is the same one-hot or empty (then the
+                // fallback to p): the draw is the argmax unless u is outside [0, 1)
+                const long long thr = scale_floor(a.uf[b], 1ull << kFixBits);
+                const long long bo = thr == -2 ? (long long)a.V - 1 : (thr < 0 ? 0ll : ga);
+                write_request(a, b, acc, bo);
+            }
+        }
+    } else {
     // ---- chain: step s compares draft s+1 with target row s (warp 0, one lane per step) ----
     if (tid < 32) {
         bool acc = false;
@@ -1429,15 +1531,7 @@ __global__ void __launch_bounds__(kNT) chain_kernel(VerifyArgs a) {
     const float uf = a.uf[b];
 
     const RowDesc dt = a.desc[(b * kT + acc) * 2 + 0];
-    if (greedy) {
-        // one-hot p at the argmax; the residual against a one-hot q is the same one-hot or
-        // empty (then the fallback to p): the draw is the argmax unless u is out of [0, 1)
-        if (rank == 0 && tid == 0) {
-            const long long thr = scale_floor(uf, 1ull << kFixBits);
-            const long long bo = thr == -2 ? (long long)a.V - 1 : (thr < 0 ? 0ll : (long long)dt.argmax);
-            write_request(a, b, acc, bo);
-        }
-    } else {
+    {
         const long long tr = a.tgt_row[b] + acc;
         const bool trow_ok = tr >= 0 && tr < a.tgt_rows;
         const RowDesc* dq = nullptr;
@@ -1559,6 +1653,7 @@ __global__ void __launch_bounds__(kNT) chain_kernel(VerifyArgs a) {
             if (tid == 0) write_request(a, b, acc, (long long)a.V - 1);
         }
         cluster_barrier();  // peers may still read this CTA's totals
+    }
     }
 
     // ---- completion: the last request packs tokens and KV slots ---------------------------
