@@ -40,12 +40,12 @@ namespace st {
 constexpr int kCS = 8;           // CTAs per cluster: one row is split into 8 slices
 constexpr int kNT = 256;         // threads per CTA
 constexpr int kNW = kNT / 32;    // warps per CTA
-constexpr int kBins = 32;        // level-1 bins: min(rne(-0.75 y), 31)
-constexpr int kSub = 31;         // level-2 bins: rne(-22.5 y) - 30 b1 + 15, clamped to [0, 30]
+constexpr int kBins = 24;        // level-1 bins: min(rne(-0.75 y), 23)
+constexpr int kSub = 23;         // level-2 bins: rne(-16.5 y) - 22 b1 + 11, clamped to [0, 22]
 constexpr int kWinK = kCS * kNW; // top-k rows with k <= 64 select inside the candidate window
 constexpr int kWinCap = 128;     // window entries per CTA
 constexpr int kWinTotal = 512;   // window entries per row
-constexpr int kListCap = 4096;   // level-2 compaction list per CTA
+constexpr int kListCap = 2048;   // level-2 compaction list per CTA
 constexpr int kKeyChunk = 512;   // keys per level-3 histogram chunk
 constexpr int kMaxB = 1024;      // requests per launch handled by this path
 constexpr int kTaskCap = 64;     // decoded tasks of one cluster held in shared memory at a time
@@ -54,7 +54,7 @@ enum Cat : int { kGreedy = 0, kKeepAll = 1, kWindow = 2, kBinned = 3 };
 
 constexpr uint32_t kFill = 0xFF80FF80u;  // two bf16 -inf: slots outside the slice
 constexpr float kS1 = 0.75f;             // level-1 scale (exact)
-constexpr float kS2 = 22.5f;             // level-2 scale = 30 * kS1 (exact)
+constexpr float kS2 = 16.5f;             // level-2 scale = (kSub - 1) * kS1 (exact)
 constexpr float kTwo23 = 8388608.0f;
 
 // ---------------------------------------------------------------------------------------
@@ -132,7 +132,7 @@ __device__ __forceinline__ int bin1_of(float yc) {
 }
 __device__ __forceinline__ int bin2_of(float yc, int b1) {
     const float t = __fmaf_rn(yc, -kS2, kTwo23);
-    const int v = (int)(__float_as_uint(t) - 0x4B000000u) - 30 * b1 + 15;
+    const int v = (int)(__float_as_uint(t) - 0x4B000000u) - (kSub - 1) * b1 + (kSub - 1) / 2;
     return v < 0 ? 0 : (v > kSub - 1 ? kSub - 1 : v);
 }
 // fix(exp2(yc)) for yc in [-64, 0]: the split below, scalar form
@@ -237,9 +237,10 @@ struct RowSmem {
     unsigned long long self64[8];
     uint32_t nlist;
     int32_t first_min;
-    int pre[3][kMaxB + 1];         // task prefix per group (binned, keep-all/window, greedy)
+    alignas(8) uint64_t stage_bar;  // mbarrier of the staged next slice
+    uint16_t pre[3][kMaxB + 1];    // task prefix per group (binned, keep-all/window, greedy)
     TaskInfo tasks[kTaskCap];      // this cluster's next tasks, decoded once
-    uint32_t req[kMaxB];           // per request: cat | cap << 4
+    uint8_t req[kMaxB];            // per request: cat | cap << 3
     alignas(16) uint2 acc[kBins * kNT];  // thread-private bin accumulators / gather area
     alignas(16) uint32_t list[kListCap]; // level-2 compaction list: bits << 16 | local index
 };
@@ -266,7 +267,7 @@ __device__ void build_plan(const VerifyArgs& a, RowSmem* sh) {
         float c;
         const int cat = request_cat(a, b, c);
         const int cap = clamp_cap(a.caps[b]);
-        sh->req[b] = (uint32_t)cat | ((uint32_t)cap << 4);
+        sh->req[b] = (uint8_t)(cat | (cap << 3));
     }
     __syncthreads();
     if (tid < 32) {
@@ -275,8 +276,8 @@ __device__ void build_plan(const VerifyArgs& a, RowSmem* sh) {
             const int b = b0 + tid;
             int n[3] = {0, 0, 0};
             if (b < a.B) {
-                const int cat = (int)(sh->req[b] & 15u);
-                const int cap = (int)(sh->req[b] >> 4);
+                const int cat = (int)(sh->req[b] & 7u);
+                const int cap = (int)(sh->req[b] >> 3);
                 const int rows = cap + ((cat != kGreedy && a.drf != nullptr) ? cap - 1 : 0);
                 const int g = cat == kBinned ? 0 : (cat == kGreedy ? 2 : 1);
                 n[g] = rows;
@@ -284,7 +285,7 @@ __device__ void build_plan(const VerifyArgs& a, RowSmem* sh) {
 #pragma unroll
             for (int g = 0; g < 3; ++g) {
                 const int inc = (int)warp_incl_u32((uint32_t)n[g]);
-                if (b < a.B) sh->pre[g][b + 1] = run[g] + inc;
+                if (b < a.B) sh->pre[g][b + 1] = (uint16_t)(run[g] + inc);
                 run[g] += __shfl_sync(0xffffffffu, inc, 31);
             }
         }
@@ -317,8 +318,8 @@ __device__ TaskInfo decode_task(const VerifyArgs& a, const RowSmem* sh, int t) {
     TaskInfo ti;
     ti.b = lo;
     const int r = local - sh->pre[g][lo];
-    ti.cat = (int)(sh->req[lo] & 15u);
-    ti.cap = (int)(sh->req[lo] >> 4);
+    ti.cat = (int)(sh->req[lo] & 7u);
+    ti.cap = (int)(sh->req[lo] >> 3);
     ti.kind = r < ti.cap ? 0 : 1;
     ti.s = ti.kind == 0 ? r : r - ti.cap;
     const long long base = ti.kind == 0 ? a.tgt_row[ti.b] : a.drf_row[ti.b];
@@ -349,17 +350,29 @@ __device__ __forceinline__ Slice slice_of(const VerifyArgs& a, const TaskInfo& t
     return sl;
 }
 
+// Bulk-copy the 16-byte vectors of a slice into the staging buffer (thread 0; completion on
+// the stage mbarrier).  Vector v of the slice lands at stage[v].
+__device__ __forceinline__ void stage_issue(const Slice& sl, uint4* stage, uint64_t* bar) {
+    const uint32_t bytes = (uint32_t)sl.nv * 16u;
+    fence_proxy_async_smem();  // earlier generic reads of the buffer precede the async writes
+    mbar_arrive_expect_tx(bar, bytes);
+    if (bytes == 0) return;
+    const char* src = reinterpret_cast<const char*>(sl.rowp + sl.e0 - sl.off);
+    char* dst = reinterpret_cast<char*>(stage);
+    for (uint32_t off = 0; off < bytes; off += 32768u)
+        bulk_g2s(dst + off, src + off, min(32768u, bytes - off), bar);
+}
+
+// staged slice -> registers (vector j*kNT + tid), with the halves outside [e0, e1) set to -inf
 template <int NVT>
-__device__ __forceinline__ void load_slice(const Slice& sl, uint4 (&w)[NVT]) {
+__device__ __forceinline__ void stage_to_regs(const Slice& sl, const uint4* stage, uint4 (&w)[NVT]) {
     const int tid = threadIdx.x;
-    const uint4* src = reinterpret_cast<const uint4*>(sl.rowp + sl.e0 - sl.off);
 #pragma unroll
     for (int j = 0; j < NVT; ++j) {
         const int v = j * kNT + tid;
-        if (v < sl.nv) w[j] = __ldg(src + v);
+        if (v < sl.nv) w[j] = stage[v];
         else w[j] = make_uint4(kFill, kFill, kFill, kFill);
     }
-    // mask the halves of the first and last vector that lie outside [e0, e1)
 #pragma unroll
     for (int j = 0; j < NVT; ++j) {
         const int v = j * kNT + tid;
@@ -375,14 +388,6 @@ __device__ __forceinline__ void load_slice(const Slice& sl, uint4 (&w)[NVT]) {
             }
         }
     }
-}
-
-__device__ __forceinline__ void prefetch_l2(const Slice& sl) {
-    if (sl.nv <= 0) return;
-    const char* p = reinterpret_cast<const char*>(sl.rowp + sl.e0 - sl.off);
-    uint32_t bytes = (uint32_t)sl.nv * 16u;
-    // bulk prefetch: 16-byte aligned start, size a multiple of 16
-    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(p), "r"(bytes) : "memory");
 }
 
 // element index (within the row) of half h of register vector j of this thread
@@ -633,9 +638,19 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
     const int ntask = total_tasks(a, sh);
 
     uint4 w[NVT];
+    uint4* stage = reinterpret_cast<uint4*>(smem_raw + ((sizeof(RowSmem) + 15) & ~(size_t)15));
     // this cluster's tasks are cid, cid + NC, ...; decode them into shared memory in parallel
     // (kTaskCap at a time) so that no task waits on its own metadata loads
     const int nmine = ntask > cid ? (ntask - cid + a.num_clusters - 1) / a.num_clusters : 0;
+    // the next task's slice is bulk-copied into the staging buffer while this one is processed
+    if (tid == 0) {
+        mbar_init(&sh->stage_bar, 1);
+        fence_mbar_init();
+    }
+    __syncthreads();
+    uint32_t stage_phase = 0;
+    if (tid == 0 && nmine > 0)
+        stage_issue(slice_of(a, decode_task(a, sh, cid), cx.rank, cx.L), stage, &sh->stage_bar);
     for (int it = 0; it < nmine; ++it) {
         if (it % kTaskCap == 0) {
             __syncthreads();
@@ -649,10 +664,16 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
         const bool lead = cx.rank == leader;
         if (ti.row < 0 && tid == 0 && cx.rank == 0) atomicOr(&a.ws->err, 2u);
         const Slice sl = slice_of(a, ti, cx.rank, cx.L);
-        load_slice<NVT>(sl, w);
-        if (tid == 0 && it + 1 < nmine && (it + 1) % kTaskCap != 0) {
-            const TaskInfo& tn = sh->tasks[(it + 1) % kTaskCap];
-            if (tn.row >= 0) prefetch_l2(slice_of(a, tn, cx.rank, cx.L));
+        if (!mbar_wait_bounded(&sh->stage_bar, stage_phase)) {
+            if (tid == 0) atomicOr(&a.ws->err, 1u);
+        }
+        stage_phase ^= 1u;
+        stage_to_regs<NVT>(sl, stage, w);
+        __syncthreads();  // every thread has its slice: the buffer takes the next one
+        if (tid == 0 && it + 1 < nmine) {
+            const TaskInfo tn = ((it + 1) % kTaskCap != 0) ? sh->tasks[(it + 1) % kTaskCap]
+                                                           : decode_task(a, sh, cid + (it + 1) * a.num_clusters);
+            stage_issue(slice_of(a, tn, cx.rank, cx.L), stage, &sh->stage_bar);
         }
 
         // ---- P1: max ----------------------------------------------------------------------
@@ -993,14 +1014,16 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
         // level-1 walk (every CTA, identical inputs)
         __syncthreads();
         if (tid < 32) {
-            __shared__ uint32_t tc[kBins];
-            __shared__ unsigned long long tm[kBins];
+            __shared__ uint32_t tc[32];
+            __shared__ unsigned long long tm[32];
             uint32_t cs = 0;
             unsigned long long ms = 0;
-            for (int q = 0; q < kCS; ++q) {
-                const Pub* rp = remote_pub(cx, q, ex_bins);
-                cs += rp->cnt[lane];
-                ms += rp->mass[lane];
+            if (lane < kBins) {
+                for (int q = 0; q < kCS; ++q) {
+                    const Pub* rp = remote_pub(cx, q, ex_bins);
+                    cs += rp->cnt[lane];
+                    ms += rp->mass[lane];
+                }
             }
             tc[lane] = cs;
             tm[lane] = ms;
@@ -1122,8 +1145,8 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
             const unsigned ex3 = cx.ex++;
             __syncthreads();
             if (tid < 32) {
-                __shared__ uint32_t tc2[kBins];
-                __shared__ unsigned long long tm2[kBins];
+                __shared__ uint32_t tc2[32];
+                __shared__ unsigned long long tm2[32];
                 uint32_t cs = 0;
                 unsigned long long ms = 0;
                 if (lane < kSub) {
@@ -1680,7 +1703,7 @@ __global__ void __launch_bounds__(kNT) chain_kernel(VerifyArgs a) {
 template <int NVT>
 int launch_rows(VerifyArgs a, cudaStream_t stream) {
     auto kern = row_kernel<NVT>;
-    const size_t smem = sizeof(RowSmem);
+    const size_t smem = ((sizeof(RowSmem) + 15) & ~(size_t)15) + (size_t)NVT * kNT * sizeof(uint4);
     static int attr_done = 0;
     if (!attr_done) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
