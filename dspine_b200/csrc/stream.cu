@@ -38,14 +38,14 @@ namespace dsv {
 namespace st {
 
 constexpr int kCS = 8;           // CTAs per cluster: one row is split into 8 slices
-constexpr int kNT = 256;         // threads per CTA
+constexpr int kNT = 512;         // threads per CTA (one CTA per SM)
 constexpr int kNW = kNT / 32;    // warps per CTA
 constexpr int kBins = 24;        // level-1 bins: min(rne(-0.75 y), 23)
 constexpr int kSub = 23;         // level-2 bins: rne(-16.5 y) - 22 b1 + 11, clamped to [0, 22]
-constexpr int kWinK = kCS * kNW; // top-k rows with k <= 64 select inside the candidate window
+constexpr int kWinK = kCS * kNW; // top-k rows with k <= 128 select inside the candidate window
 constexpr int kWinCap = 128;     // window entries per CTA
 constexpr int kWinTotal = 512;   // window entries per row
-constexpr int kListCap = 2048;   // level-2 compaction list per CTA
+constexpr int kListCap = 4096;   // level-2 compaction list per CTA
 constexpr int kKeyChunk = 512;   // keys per level-3 histogram chunk
 constexpr int kMaxB = 1024;      // requests per launch handled by this path
 constexpr int kTaskCap = 64;     // decoded tasks of one cluster held in shared memory at a time
@@ -78,7 +78,21 @@ constexpr float kTwo23 = 8388608.0f;
         PROF_MARK(cat_, ph);                                                                \
         if (threadIdx.x == 0) atomicAdd(reinterpret_cast<unsigned long long*>(a.res) + (cat_) * 16 + 15, 1ull); \
     } while (0)
+#define PROF_SCAN(cat_, ph)                                                              \
+    do {                                                                                 \
+        if (threadIdx.x == 0) {                                                          \
+            const unsigned long long prof_n = globaltimer_ns();                          \
+            atomicAdd(reinterpret_cast<unsigned long long*>(a.res) + 64 + (cat_) * 16 + (ph), \
+                      prof_n - prof_t);                                                  \
+            if ((ph) == 0)                                                               \
+                atomicAdd(reinterpret_cast<unsigned long long*>(a.res) + 64 + (cat_) * 16 + 15, 1ull); \
+            prof_t = prof_n;                                                             \
+        }                                                                                \
+    } while (0)
 #else
+#define PROF_SCAN(cat_, ph) \
+    do {                    \
+    } while (0)
 #define PROF_START() \
     do {             \
     } while (0)
@@ -238,6 +252,7 @@ struct RowSmem {
     uint32_t nlist;
     int32_t first_min;
     alignas(8) uint64_t stage_bar;  // mbarrier of the staged next slice
+    alignas(8) uint64_t stage_bar2[2];  // scan kernel: mbarriers of its two staging buffers
     uint16_t pre[3][kMaxB + 1];    // task prefix per group (binned, keep-all/window, greedy)
     TaskInfo tasks[kTaskCap];      // this cluster's next tasks, decoded once
     uint8_t req[kMaxB];            // per request: cat | cap << 3
@@ -619,8 +634,422 @@ __device__ __noinline__ void reread_bins(const Slice sl, float m, float c, int s
     }
 }
 
+
 template <int NVT>
-__global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
+__device__ __forceinline__ void load_slice(const Slice& sl, uint4 (&w)[NVT]) {
+    const int tid = threadIdx.x;
+    const uint4* src = reinterpret_cast<const uint4*>(sl.rowp + sl.e0 - sl.off);
+#pragma unroll
+    for (int j = 0; j < NVT; ++j) {
+        const int v = j * kNT + tid;
+        if (v < sl.nv) w[j] = __ldg(src + v);
+        else w[j] = make_uint4(kFill, kFill, kFill, kFill);
+    }
+    // mask the halves of the first and last vector that lie outside [e0, e1)
+#pragma unroll
+    for (int j = 0; j < NVT; ++j) {
+        const int v = j * kNT + tid;
+        if (v < sl.nv && (v == 0 || v == sl.nv - 1)) {
+            uint32_t* u = reinterpret_cast<uint32_t*>(&w[j]);
+#pragma unroll
+            for (int h = 0; h < 8; ++h) {
+                const int e = sl.e0 - sl.off + 8 * v + h;
+                if (e < sl.e0 || e >= sl.e1) {
+                    const uint32_t mask = (h & 1) ? 0xFFFF0000u : 0x0000FFFFu;
+                    u[h >> 1] = (u[h >> 1] & ~mask) | (kFill & mask);
+                }
+            }
+        }
+    }
+}
+
+// the leader's exact resolution inside the candidate window, from the scan results: gather
+// the entries of all CTAs, rank them by (key desc, index asc), walk the exact masses
+__device__ void window_resolve_area(const VerifyArgs& a, const TaskInfo& ti, const TaskArea* ar,
+                                    RowSmem* sh, uint32_t win_total, int L, float m, long long kk,
+                                    long long thr) {
+    const int tid = threadIdx.x, lane = tid & 31;
+    uint2* g = sh->acc;  // [0, kWinTotal): gathered, [kWinTotal, 2 kWinTotal): sorted
+    __syncthreads();
+    for (int f = tid; f < (int)win_total; f += kNT) {
+        int q = 0, off = 0;
+        while (q + 1 < kCS && off + (int)ar->wcnt[q] <= f) {
+            off += (int)ar->wcnt[q];
+            ++q;
+        }
+        const uint32_t e = ar->went[q][f - off];
+        const int qe0 = min(q * L, a.V);
+        g[f] = make_uint2(e >> 16, (uint32_t)(qe0 + (int)(e & 0xFFFFu)));
+    }
+    __syncthreads();
+    const int n = (int)win_total;
+    for (int i = tid; i < n; i += kNT) {
+        const uint2 me = g[i];
+        int r = 0;
+        for (int j = 0; j < n; ++j) {
+            const uint2 o = g[j];
+            r += (o.x > me.x) || (o.x == me.x && o.y < me.y);
+        }
+        g[kWinTotal + r] = me;
+    }
+    __syncthreads();
+    if (tid < 32) {
+        // first rank that is not kept: r >= k, or mass ranked ahead > thr (rank 0 always kept)
+        unsigned long long A = 0;
+        int nsel = -1;
+        for (int base = 0; base < n && nsel < 0; base += 32) {
+            const int r = base + lane;
+            unsigned long long F = 0;
+            if (r < n) F = fix_of_y(y_clamped(bf(key_bits(g[kWinTotal + r].x)), m, ti.c));
+            unsigned long long inc = F;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const unsigned long long v = __shfl_up_sync(0xffffffffu, inc, o);
+                if (lane >= o) inc += v;
+            }
+            const unsigned long long Ar = A + inc - F;
+            const bool out = r < n && r > 0 && (r >= kk || (long long)Ar > thr);
+            const uint32_t bal = __ballot_sync(0xffffffffu, out);
+            if (bal) nsel = base + __ffs(bal) - 1;
+            A += __shfl_sync(0xffffffffu, inc, 31);
+        }
+        if (nsel < 0) nsel = n < kk ? n : (int)kk;
+        unsigned long long sk = 0;
+        for (int r = lane; r < nsel; r += 32)
+            sk += fix_of_y(y_clamped(bf(key_bits(g[kWinTotal + r].x)), m, ti.c));
+        sk = warp_sum_u64(sk);
+        if (lane == 0) {
+            const uint2 last = g[kWinTotal + nsel - 1];
+            put_desc(a, ti, m, last.x, (int)last.y, sk, 0, 0u);
+        }
+    }
+}
+
+
+__device__ __forceinline__ void cluster_arrive() {
+    asm volatile("barrier.cluster.arrive.release;" ::: "memory");
+}
+__device__ __forceinline__ void cluster_wait() {
+    asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
+}
+
+static_assert(kBins == kAreaBins && kCS == kAreaCS, "scan area layout");
+
+// Scan kernel: max and exact exp pass of every row, pipelined across tasks.  While the row of
+// task A sits in registers, P1 of the next task B runs from the staging buffer and its max is
+// exchanged across the cluster (split arrive/wait) during P2 of A, so the exchange latency is
+// hidden.  Results go to the row's TaskArea (sum, level-1 bins, candidate window) and, for
+// greedy rows, to the packed argmax; the select kernel finishes the kept sets.
+template <int NVT>
+__global__ void __launch_bounds__(kNT, 1) scan_kernel(VerifyArgs a) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    RowSmem* sh = reinterpret_cast<RowSmem*>(smem_raw);
+    cg::cluster_group cluster = cg::this_cluster();
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    RowCtx<NVT> cx;
+    cx.a = &a;
+    cx.sh = sh;
+    cx.cl = &cluster;
+    cx.rank = (int)cluster.block_rank();
+    cx.L = a.slice;
+    cx.ex = 0;
+    const int cid = blockIdx.x / kCS;
+
+    build_plan(a, sh);
+    const int ntask = total_tasks(a, sh);
+    const int nmine = ntask > cid ? (ntask - cid + a.num_clusters - 1) / a.num_clusters : 0;
+    // two staging buffers: task i+1 is copied into one while task i's slice (in the other) is
+    // read by its P1 and then moved to the registers
+    uint4* stage_base = reinterpret_cast<uint4*>(smem_raw + ((sizeof(RowSmem) + 15) & ~(size_t)15));
+    if (tid == 0) {
+        mbar_init(&sh->stage_bar2[0], 1);
+        mbar_init(&sh->stage_bar2[1], 1);
+        fence_mbar_init();
+        sh->nlist = 0;
+    }
+    __syncthreads();
+    uint32_t stage_ph0 = 0, stage_ph1 = 0;
+    if (tid == 0 && nmine > 0)
+        stage_issue(slice_of(a, decode_task(a, sh, cid), cx.rank, cx.L), stage_base, &sh->stage_bar2[0]);
+
+    uint4 w[NVT];
+    bool haveA = false;
+    TaskInfo tA;
+    Slice sA;
+    float mA = 0.0f;
+    uint32_t tauA = 0;
+    tA.b = tA.s = tA.kind = tA.cat = tA.cap = tA.k = 0;
+    tA.row = -1;
+    tA.T = tA.p = tA.c = 0.0f;
+    sA.rowp = nullptr;
+    sA.e0 = sA.e1 = sA.off = sA.nv = 0;
+
+    for (int it = 0; it <= nmine; ++it) {
+        PROF_START();
+        const bool haveB = it < nmine;
+        TaskInfo tB = tA;
+        Slice sB = sA;
+        bool sampledB = false;
+        // ---- P1 of task B from the staging buffer; sampled rows start the max exchange ------
+        if (haveB) {
+            if (it % kTaskCap == 0) {
+                __syncthreads();
+                for (int i = tid; i < kTaskCap && it + i < nmine; i += kNT)
+                    sh->tasks[i] = decode_task(a, sh, cid + (it + i) * a.num_clusters);
+                __syncthreads();
+            }
+            tB = sh->tasks[it % kTaskCap];
+            sB = slice_of(a, tB, cx.rank, cx.L);
+            sampledB = tB.cat != kGreedy;
+            if (tB.row < 0 && tid == 0 && cx.rank == 0) atomicOr(&a.ws->err, 2u);
+            // the next task's slice goes into the other buffer (its previous task has moved on)
+            if (tid == 0 && it + 1 < nmine) {
+                const TaskInfo tn = ((it + 1) % kTaskCap != 0) ? sh->tasks[(it + 1) % kTaskCap]
+                                                               : decode_task(a, sh, cid + (it + 1) * a.num_clusters);
+                stage_issue(slice_of(a, tn, cx.rank, cx.L), stage_base + ((it + 1) & 1) * NVT * kNT,
+                            &sh->stage_bar2[(it + 1) & 1]);
+            }
+            uint4* stage = stage_base + (it & 1) * NVT * kNT;
+            const uint32_t ph = (it & 1) ? stage_ph1 : stage_ph0;
+            if (!mbar_wait_bounded(&sh->stage_bar2[it & 1], ph)) {
+                if (tid == 0) atomicOr(&a.ws->err, 1u);
+            }
+            if (it & 1) stage_ph1 ^= 1u; else stage_ph0 ^= 1u;
+            PROF_SCAN(tB.cat, 0);
+            uint32_t mx = kFill;
+#pragma unroll
+            for (int j = 0; j < NVT; ++j) {
+                const int v = j * kNT + tid;
+                if (v < sB.nv) {
+                    uint4 x = stage[v];
+                    if (v == 0 || v == sB.nv - 1) {
+                        uint32_t* u = reinterpret_cast<uint32_t*>(&x);
+#pragma unroll
+                        for (int h = 0; h < 8; ++h) {
+                            const int e = sB.e0 - sB.off + 8 * v + h;
+                            if (e < sB.e0 || e >= sB.e1) {
+                                const uint32_t msk = (h & 1) ? 0xFFFF0000u : 0x0000FFFFu;
+                                u[h >> 1] = (u[h >> 1] & ~msk) | (kFill & msk);
+                            }
+                        }
+                    }
+                    mx = bf2_max(mx, x.x);
+                    mx = bf2_max(mx, x.y);
+                    mx = bf2_max(mx, x.z);
+                    mx = bf2_max(mx, x.w);
+                }
+            }
+            const uint32_t k0 = okey(mx & 0xFFFFu), k1 = okey(mx >> 16);
+            const uint32_t tkey = k0 > k1 ? k0 : k1;
+            const uint32_t wkey = __reduce_max_sync(0xffffffffu, tkey);
+            if (lane == 0) sh->red32[wid] = wkey;
+            if (tid == 0) sh->first_min = 0x7fffffff;
+            __syncthreads();
+            uint32_t ckey = 0;
+#pragma unroll
+            for (int i = 0; i < kNW; ++i) ckey = max(ckey, sh->red32[i]);
+            if (!sampledB) {
+                // greedy row: the first index of the CTA max, combined across the slices by one
+                // global atomicMax on (key << 32 | ~index); no cluster exchange
+                if (tkey == ckey) {
+                    const uint32_t cb = key_bits(ckey);
+                    const uint32_t c2 = cb | (cb << 16);
+                    int best = 0x7fffffff;
+                    for (int j = 0; j < NVT && best == 0x7fffffff; ++j) {
+                        const int v = j * kNT + tid;
+                        if (v >= sB.nv) break;
+                        const uint4 x = stage[v];
+                        const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+                        for (int h = 0; h < 8; ++h) {
+                            const uint32_t eq = bf2_eq(xs[h >> 1], c2) & ((h & 1) ? 0xFFFF0000u : 0x0000FFFFu);
+                            const int e = sB.e0 - sB.off + 8 * v + h;
+                            if (eq && best == 0x7fffffff && e >= sB.e0 && e < sB.e1) best = e;
+                        }
+                    }
+                    if (best != 0x7fffffff) atomicMin(&sh->first_min, best);
+                }
+                __syncthreads();
+                if (tid == 0 && sh->first_min != 0x7fffffff) {
+                    const unsigned long long packed =
+                        ((unsigned long long)ckey << 32) | (0xFFFFFFFFull - (unsigned)sh->first_min);
+                    atomicMax(&a.gmax[tB.b * kT + tB.s], packed);
+                }
+            } else {
+                Pub& pb = sh->pub[cx.ex & 1];
+                if (tid == 0) pb.maxkey = ckey;
+                if (tid < kNW) pb.wmax[tid] = sh->red32[tid];
+                cluster_arrive();
+            }
+        }
+
+        if (haveB) PROF_SCAN(tB.cat, 1);
+        // ---- P2 of task A from the registers (overlaps the exchange of B) -------------------
+        if (haveA) {
+            TaskArea* ar = &a.area[(tA.b * kT + tA.s) * 2 + tA.kind];
+            const int cat = tA.cat;
+            const float2 nm = make_float2(-mA, -mA), c2 = make_float2(tA.c, tA.c);
+            if (cat == kBinned) {
+                __syncthreads();
+                uint4* az = reinterpret_cast<uint4*>(sh->acc);
+                for (int i = tid; i < kBins * kNT / 2; i += kNT) az[i] = make_uint4(0, 0, 0, 0);
+                if (tid < kBins) sh->bcnt[tid] = 0;
+                __syncthreads();
+            }
+            uint32_t hs = 0, ls = 0;
+#pragma unroll
+            for (int j = 0; j < NVT; ++j) {
+                const uint32_t* u = reinterpret_cast<const uint32_t*>(&w[j]);
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const Pair pr = exp_pair(u[q], nm, c2);
+                    hs += pr.h0 + pr.h1;
+                    ls += pr.l0 + pr.l1;
+                    if (cat == kBinned) {
+                        const int bx = bin1_of(pr.yc.x), by = bin1_of(pr.yc.y);
+                        uint2* px = &sh->acc[bx * kNT + tid];
+                        uint2 vx = *px;
+                        vx.x += pr.h0 - 0x4B000000u;
+                        vx.y += pr.l0 - 0x4B400000u;
+                        *px = vx;
+                        uint2* py = &sh->acc[by * kNT + tid];
+                        uint2 vy = *py;
+                        vy.x += pr.h1 - 0x4B000000u;
+                        vy.y += pr.l1 - 0x4B400000u;
+                        *py = vy;
+                        atomicAdd(&sh->bcnt[bx], 1u);
+                        atomicAdd(&sh->bcnt[by], 1u);
+                    }
+                }
+            }
+            if (cat == kWindow) {
+                const uint32_t taub = key_bits(tauA);
+                const uint32_t tau2 = taub | (taub << 16);
+#pragma unroll
+                for (int j = 0; j < NVT; ++j) {
+                    const uint32_t* u = reinterpret_cast<const uint32_t*>(&w[j]);
+#pragma unroll
+                    for (int q = 0; q < 4; ++q) {
+                        const uint32_t ge = bf2_ge(u[q], tau2);
+                        if (ge) {
+#pragma unroll
+                            for (int h = 0; h < 2; ++h) {
+                                const int e = elem_index(sA, j, 2 * q + h);
+                                if ((ge & (h ? 0xFFFF0000u : 0x0000FFFFu)) && elem_valid(sA, e)) {
+                                    const uint32_t bits = h ? (u[q] >> 16) : (u[q] & 0xFFFFu);
+                                    const uint32_t pos = atomicAdd(&sh->nlist, 1u);
+                                    if (pos < kWinCap) sh->win[pos] = (okey(bits) << 16) | (uint32_t)(e - sA.e0);
+                                }
+                            }
+                        }
+                    }
+                }
+            }
+            const uint32_t nel = (uint32_t)NVT * 8u;
+            const uint32_t hi_t = hs - nel * 0x4B000000u;
+            const int32_t lo_t = (int32_t)(ls - nel * 0x4B400000u);
+            const unsigned long long s_cta =
+                cta_sum_u64((unsigned long long)((long long)hi_t * 8388608 + lo_t), sh);
+            if (tid == 0) atomicAdd(&ar->S, s_cta);
+            if (cat == kWindow) {
+                const uint32_t nw = sh->nlist;
+                for (int i = tid; i < (int)min(nw, (uint32_t)kAreaWin); i += kNT)
+                    ar->went[cx.rank][i] = sh->win[i];
+                if (tid == 0) ar->wcnt[cx.rank] = nw;
+                __syncthreads();
+                if (tid == 0) sh->nlist = 0;  // the next window row appends after later barriers
+            }
+            if (cat == kBinned) {
+                const uint32_t nfill = nel * kNT - (uint32_t)(sA.e1 > sA.e0 ? sA.e1 - sA.e0 : 0);
+                for (int bin = wid; bin < kBins; bin += kNW) {
+                    long long sm = 0;
+                    for (int i = lane; i < kNT; i += 32) {
+                        const uint2 v = sh->acc[bin * kNT + i];
+                        sm += (long long)v.x * 8388608 + (int32_t)v.y;
+                    }
+                    sm = (long long)warp_sum_u64((unsigned long long)sm);
+                    if (lane == 0) {
+                        if (sm) atomicAdd(&ar->mass[bin], (unsigned long long)sm);
+                        // fill slots (outside the slice) are -inf and fall into the last bin
+                        const uint32_t cnt = sh->bcnt[bin] - (bin == kBins - 1 ? nfill : 0u);
+                        if (cnt) atomicAdd(&ar->cnt[bin], cnt);
+                    }
+                }
+            }
+        }
+
+        if (haveA) PROF_SCAN(tA.cat, 2);
+        // ---- finish B's exchange, then move B into the registers ----------------------------
+        if (haveB) {
+            uint32_t tauB = 0;
+            uint32_t mkeyB = 0;
+            if (sampledB) {
+                cluster_wait();
+                const unsigned exB = cx.ex++;
+                if (tid < 32) {
+                    uint32_t k = lane < kCS ? remote_pub(cx, lane, exB)->maxkey : 0u;
+                    const uint32_t mk = __reduce_max_sync(0xffffffffu, k);
+                    uint32_t cand = 0;
+                    if (tB.cat == kWindow) {
+                        const long long kk = tB.k < a.V ? (long long)tB.k : (long long)a.V;
+                        // tau = the k-th largest of the cluster's kCS * kNW warp maxima: at least
+                        // k elements are >= tau (one per warp whose maximum is >= tau)
+                        constexpr int R = kCS * kNW / 32;
+                        uint32_t x[R];
+#pragma unroll
+                        for (int r = 0; r < R; ++r) {
+                            const int g = lane + 32 * r;
+                            x[r] = remote_pub(cx, g / kNW, exB)->wmax[g % kNW];
+                        }
+                        int ge[R];
+#pragma unroll
+                        for (int r = 0; r < R; ++r) ge[r] = 0;
+                        for (int i = 0; i < 32; ++i) {
+#pragma unroll
+                            for (int r2 = 0; r2 < R; ++r2) {
+                                const uint32_t y = __shfl_sync(0xffffffffu, x[r2], i);
+#pragma unroll
+                                for (int r = 0; r < R; ++r) ge[r] += (y >= x[r]);
+                            }
+                        }
+#pragma unroll
+                        for (int r = 0; r < R; ++r)
+                            if (ge[r] >= kk && x[r] > cand) cand = x[r];
+                        cand = __reduce_max_sync(0xffffffffu, cand);
+                    }
+                    if (lane == 0) {
+                        sh->sel[10] = (int)mk;
+                        sh->sel[0] = (int)cand;
+                        if (cx.rank == 0) a.area[(tB.b * kT + tB.s) * 2 + tB.kind].mkey = mk;
+                    }
+                }
+            }
+            __syncthreads();  // P2 of A is done with the registers, P1 of B with the buffer
+            PROF_SCAN(tB.cat, 3);
+            if (sampledB) {
+                mkeyB = (uint32_t)sh->sel[10];
+                tauB = (uint32_t)sh->sel[0];
+                stage_to_regs<NVT>(sB, stage_base + (it & 1) * NVT * kNT, w);
+            }
+            __syncthreads();  // B's buffer is free for the task after next
+            PROF_SCAN(tB.cat, 4);
+            haveA = sampledB;
+            tA = tB;
+            sA = sB;
+            mA = bf(key_bits(mkeyB));
+            tauA = tauB;
+        } else {
+            haveA = false;
+        }
+    }
+    // no CTA may leave while a peer can still read its shared memory
+    cluster_barrier();
+}
+
+// Select kernel: the kept sets of sampled rows from the scan results.  Keep-all and window
+// rows need no row data; binned rows reload their slice and walk bins, keys and the tie.
+template <int NVT>
+__global__ void __launch_bounds__(kNT, 1) select_kernel(VerifyArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     RowSmem* sh = reinterpret_cast<RowSmem*>(smem_raw);
     cg::cluster_group cluster = cg::this_cluster();
@@ -637,20 +1066,11 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
     build_plan(a, sh);
     const int ntask = total_tasks(a, sh);
 
+    // sampled rows only (binned first, then keep-all / window), in the scan kernel's order
     uint4 w[NVT];
-    uint4* stage = reinterpret_cast<uint4*>(smem_raw + ((sizeof(RowSmem) + 15) & ~(size_t)15));
-    // this cluster's tasks are cid, cid + NC, ...; decode them into shared memory in parallel
-    // (kTaskCap at a time) so that no task waits on its own metadata loads
-    const int nmine = ntask > cid ? (ntask - cid + a.num_clusters - 1) / a.num_clusters : 0;
-    // the next task's slice is bulk-copied into the staging buffer while this one is processed
-    if (tid == 0) {
-        mbar_init(&sh->stage_bar, 1);
-        fence_mbar_init();
-    }
-    __syncthreads();
-    uint32_t stage_phase = 0;
-    if (tid == 0 && nmine > 0)
-        stage_issue(slice_of(a, decode_task(a, sh, cid), cx.rank, cx.L), stage, &sh->stage_bar);
+    const int nsampled = (int)sh->pre[0][a.B] + (int)sh->pre[1][a.B];
+    (void)ntask;
+    const int nmine = nsampled > cid ? (nsampled - cid + a.num_clusters - 1) / a.num_clusters : 0;
     for (int it = 0; it < nmine; ++it) {
         if (it % kTaskCap == 0) {
             __syncthreads();
@@ -662,328 +1082,45 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
         const TaskInfo ti = sh->tasks[it % kTaskCap];
         const int leader = it % kCS;
         const bool lead = cx.rank == leader;
-        if (ti.row < 0 && tid == 0 && cx.rank == 0) atomicOr(&a.ws->err, 2u);
         const Slice sl = slice_of(a, ti, cx.rank, cx.L);
-        if (!mbar_wait_bounded(&sh->stage_bar, stage_phase)) {
-            if (tid == 0) atomicOr(&a.ws->err, 1u);
-        }
-        stage_phase ^= 1u;
-        stage_to_regs<NVT>(sl, stage, w);
-        __syncthreads();  // every thread has its slice: the buffer takes the next one
-        if (tid == 0 && it + 1 < nmine) {
-            const TaskInfo tn = ((it + 1) % kTaskCap != 0) ? sh->tasks[(it + 1) % kTaskCap]
-                                                           : decode_task(a, sh, cid + (it + 1) * a.num_clusters);
-            stage_issue(slice_of(a, tn, cx.rank, cx.L), stage, &sh->stage_bar);
-        }
-
-        // ---- P1: max ----------------------------------------------------------------------
-        uint32_t mx = kFill;
-#pragma unroll
-        for (int j = 0; j < NVT; ++j) {
-            mx = bf2_max(mx, w[j].x);
-            mx = bf2_max(mx, w[j].y);
-            mx = bf2_max(mx, w[j].z);
-            mx = bf2_max(mx, w[j].w);
-        }
-        const uint32_t k0 = okey(mx & 0xFFFFu), k1 = okey(mx >> 16);
-        const uint32_t tkey = k0 > k1 ? k0 : k1;
-        const uint32_t wkey = __reduce_max_sync(0xffffffffu, tkey);
-        Pub& pb = sh->pub[cx.ex & 1];
-        if (lane == 0) sh->red32[wid] = wkey;
-        if (tid == 0) sh->first_min = 0x7fffffff;
-        __syncthreads();
-        uint32_t ckey = 0;
-#pragma unroll
-        for (int i = 0; i < kNW; ++i) ckey = max(ckey, sh->red32[i]);
-        if (ti.cat == kGreedy && tkey == ckey) {
-            // first element of this thread equal to the CTA max, in index order (j, half)
-            const uint32_t cb = key_bits(ckey);
-            const uint32_t c2 = cb | (cb << 16);
-            int best = 0x7fffffff;
-#pragma unroll
-            for (int j = 0; j < NVT; ++j) {
-                const uint32_t* u = reinterpret_cast<const uint32_t*>(&w[j]);
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const uint32_t eq = bf2_eq(u[q], c2);
-                    if (eq && best == 0x7fffffff) {
-#pragma unroll
-                        for (int h = 0; h < 2; ++h) {
-                            const int e = elem_index(sl, j, 2 * q + h);
-                            if ((eq & (h ? 0xFFFF0000u : 0x0000FFFFu)) && best == 0x7fffffff &&
-                                elem_valid(sl, e))
-                                best = e;
-                        }
-                    }
-                }
-            }
-            if (best != 0x7fffffff) atomicMin(&sh->first_min, best);
-        }
-        if (ti.cat == kGreedy) {
-            // greedy rows need only the max and its first index: combine the slices with one
-            // global atomicMax on (key << 32 | ~index); no cluster exchange
-            __syncthreads();
-            if (tid == 0 && sh->first_min != 0x7fffffff) {
-                const unsigned long long packed =
-                    ((unsigned long long)ckey << 32) | (0xFFFFFFFFull - (unsigned)sh->first_min);
-                atomicMax(&a.gmax[ti.b * kT + ti.s], packed);
-            }
-            PROF_END(ti.cat, 2);
-            continue;
-        }
-        __syncthreads();
-        if (tid == 0) {
-            pb.maxkey = ckey;
-            pb.first = sh->first_min;
-        }
-        if (tid < kNW) pb.wmax[tid] = sh->red32[tid];
-        PROF_MARK(ti.cat, 0);
-        cluster_barrier();  // exchange 1
-        const unsigned ex1 = cx.ex++;
-        if (tid < 32) {
-            // lanes 0..7 read one CTA each; the max key and the first index among its holders
-            uint32_t k = 0;
-            int f = 0x7fffffff;
-            if (lane < kCS) {
-                const Pub* rp = remote_pub(cx, lane, ex1);
-                k = rp->maxkey;
-                f = rp->first;
-            }
-            const uint32_t mk = __reduce_max_sync(0xffffffffu, k);
-            const int fa = __reduce_min_sync(0xffffffffu, k == mk ? f : 0x7fffffff);
-            if (lane == 0) {
-                sh->sel[10] = (int)mk;
-                sh->sel[11] = fa;
-            }
-        }
-        __syncthreads();
-        const uint32_t mkey = (uint32_t)sh->sel[10];
+        const TaskArea* ar = &a.area[(ti.b * kT + ti.s) * 2 + ti.kind];
+        const uint32_t mkey = ar->mkey;
         const float m = bf(key_bits(mkey));
-        PROF_MARK(ti.cat, 1);
-
-
-        // ---- window threshold (k-th largest warp maximum of the cluster) -----------------
+        const unsigned long long S = ar->S;
+        const long long thr = (ti.p < 1.0f) ? scale_floor(ti.p, S) : 0x7fffffffffffffffll;
         int cat = ti.cat;
         const long long kk = ti.k < a.V ? (long long)ti.k : (long long)a.V;
-        uint32_t tau = 0;
-        if (cat == kWindow) {
-            if (tid < 32) {
-                // 64 warp maxima, two per lane
-                const Pub* r0 = remote_pub(cx, lane >> 3, ex1);
-                const Pub* r1 = remote_pub(cx, 4 + (lane >> 3), ex1);
-                const uint32_t x0 = r0->wmax[lane & 7], x1 = r1->wmax[lane & 7];
-                int ge0 = 0, ge1 = 0;
-                for (int i = 0; i < 32; ++i) {
-                    const uint32_t y0 = __shfl_sync(0xffffffffu, x0, i);
-                    const uint32_t y1 = __shfl_sync(0xffffffffu, x1, i);
-                    ge0 += (y0 >= x0) + (y1 >= x0);
-                    ge1 += (y0 >= x1) + (y1 >= x1);
-                }
-                uint32_t cand = 0;
-                if (ge0 >= kk) cand = x0;
-                if (ge1 >= kk && x1 > cand) cand = x1;
-                cand = __reduce_max_sync(0xffffffffu, cand);
-                if (lane == 0) sh->sel[0] = (int)cand;
-            }
-            if (tid == 0) sh->nlist = 0;
-            __syncthreads();
-            tau = (uint32_t)sh->sel[0];
-        }
-
-        // ---- P2: exp pass -------------------------------------------------------------------
         const float2 nm = make_float2(-m, -m), c2 = make_float2(ti.c, ti.c);
-        const uint32_t taub = key_bits(tau);
-        const uint32_t tau2 = taub | (taub << 16);
-        if (cat == kBinned) {
-            uint4* az = reinterpret_cast<uint4*>(sh->acc);
-            for (int i = tid; i < kBins * kNT / 2; i += kNT) az[i] = make_uint4(0, 0, 0, 0);
-            if (tid < kBins) sh->bcnt[tid] = 0;
-            __syncthreads();
-        }
-        uint32_t hs = 0, ls = 0;
-#pragma unroll
-        for (int j = 0; j < NVT; ++j) {
-            const uint32_t* u = reinterpret_cast<const uint32_t*>(&w[j]);
-#pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const Pair pr = exp_pair(u[q], nm, c2);
-                hs += pr.h0 + pr.h1;
-                ls += pr.l0 + pr.l1;
-                if (cat == kBinned) {
-                    const int b0 = bin1_of(pr.yc.x), b1 = bin1_of(pr.yc.y);
-                    uint2* p0 = &sh->acc[b0 * kNT + tid];
-                    uint2 v0 = *p0;
-                    v0.x += pr.h0 - 0x4B000000u;
-                    v0.y += pr.l0 - 0x4B400000u;
-                    *p0 = v0;
-                    uint2* p1 = &sh->acc[b1 * kNT + tid];
-                    uint2 v1 = *p1;
-                    v1.x += pr.h1 - 0x4B000000u;
-                    v1.y += pr.l1 - 0x4B400000u;
-                    *p1 = v1;
-                    atomicAdd(&sh->bcnt[b0], 1u);
-                    atomicAdd(&sh->bcnt[b1], 1u);
-                }
-            }
-        }
-        if (cat == kWindow) {
-            // candidates (value >= tau) in a separate cheap scan: a branch inside the exp loop
-            // would cut it into blocks the compiler cannot interleave
-#pragma unroll
-            for (int j = 0; j < NVT; ++j) {
-                const uint32_t* u = reinterpret_cast<const uint32_t*>(&w[j]);
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const uint32_t ge = bf2_ge(u[q], tau2);
-                    if (ge) {
-#pragma unroll
-                        for (int h = 0; h < 2; ++h) {
-                            const int e = elem_index(sl, j, 2 * q + h);
-                            if ((ge & (h ? 0xFFFF0000u : 0x0000FFFFu)) && elem_valid(sl, e)) {
-                                const uint32_t bits = h ? (u[q] >> 16) : (u[q] & 0xFFFFu);
-                                const uint32_t pos = atomicAdd(&sh->nlist, 1u);
-                                if (pos < kWinCap) sh->win[pos] = (okey(bits) << 16) | (uint32_t)(e - sl.e0);
-                            }
-                        }
-                    }
-                }
-            }
-        }
         const uint32_t nel = (uint32_t)NVT * 8u;
-        const uint32_t hi_t = hs - nel * 0x4B000000u;
-        const int32_t lo_t = (int32_t)(ls - nel * 0x4B400000u);
-        const unsigned long long s_thr = (unsigned long long)((long long)hi_t * 8388608 + lo_t);
-        const unsigned long long s_cta = cta_sum_u64(s_thr, sh);
-        Pub& pb2 = sh->pub[cx.ex & 1];
-        if (tid == 0) {
-            pb2.S = s_cta;
-            pb2.nwin = sh->nlist;
-        }
-        if (cat == kBinned) {
-            // reduce the private accumulators: warp w sums bins 4w..4w+3
-            __syncthreads();
-            for (int bb = 0; bb < kBins / kNW; ++bb) {
-                const int bin = wid * (kBins / kNW) + bb;
-                long long s = 0;
-                for (int i = lane; i < kNT; i += 32) {
-                    const uint2 v = sh->acc[bin * kNT + i];
-                    s += (long long)v.x * 8388608 + (int32_t)v.y;
-                }
-                s = (long long)warp_sum_u64((unsigned long long)s);
-                if (lane == 0) {
-                    pb2.mass[bin] = (unsigned long long)s;
-                    // fill slots (outside the slice) are -inf: they fall into the last bin
-                    const uint32_t fill = nel * kNT - (uint32_t)(sl.e1 > sl.e0 ? sl.e1 - sl.e0 : 0);
-                    pb2.cnt[bin] = sh->bcnt[bin] - (bin == kBins - 1 ? fill : 0u);
-                }
-            }
-        }
-        PROF_MARK(ti.cat, 2);
-        cluster_barrier();  // exchange 2
-        const unsigned ex2 = cx.ex++;
-        if (tid < 32) {
-            unsigned long long sp = 0;
-            uint32_t nw = 0;
-            if (lane < kCS) {
-                const Pub* rp = remote_pub(cx, lane, ex2);
-                sp = rp->S;
-                nw = rp->nwin;
-            }
-            sp = warp_sum_u64(sp);
-            const uint32_t tot = warp_sum_u32(nw);
-            const uint32_t over = __ballot_sync(0xffffffffu, nw > (uint32_t)kWinCap);
-            if (lane == 0) {
-                sh->self64[7] = sp;
-                sh->sel[12] = (int)tot;
-                sh->sel[13] = over != 0;
-            }
-        }
-        __syncthreads();
-        const unsigned long long S = sh->self64[7];
-        const uint32_t win_total = (uint32_t)sh->sel[12];
-        const bool win_over = sh->sel[13] != 0;
-        const long long thr = (ti.p < 1.0f) ? scale_floor(ti.p, S) : 0x7fffffffffffffffll;
-
-        PROF_MARK(ti.cat, 3);
+        (void)nm;
+        (void)c2;
+        (void)nel;
         if (cat == kKeepAll) {
             if (lead && tid == 0) put_desc(a, ti, m, 0u, 0x7fffffff, S, 0, 0u);
             PROF_END(ti.cat, 4);
             continue;
         }
-
-        if (cat == kWindow && !win_over && win_total <= (uint32_t)kWinTotal) {
-            if (lead) {
-                // gather every CTA's entries (key << 16 | local index) as (key, global index):
-                // counts of all CTAs in one DSMEM round, then every entry in parallel
-                uint2* g = sh->acc;  // reuse: up to kWinTotal entries
-                __syncthreads();
-                if (tid < 32) {
-                    const uint32_t nw = lane < kCS ? remote_pub(cx, lane, ex2)->nwin : 0u;
-                    const uint32_t incl = warp_incl_u32(nw);
-                    if (lane < kCS) sh->sel[1 + lane] = (int)(incl - nw);  // sel[1..8]: offsets
-                }
-                __syncthreads();
-                for (int f = tid; f < (int)win_total; f += kNT) {
-                    int q = 0;
-                    while (q + 1 < kCS && sh->sel[2 + q] <= f) ++q;
-                    const uint32_t e = cluster.map_shared_rank(sh->win, q)[f - sh->sel[1 + q]];
-                    const int qe0 = min(q * cx.L, a.V);
-                    g[f] = make_uint2(e >> 16, (uint32_t)(qe0 + (int)(e & 0xFFFFu)));
-                }
-                __syncthreads();
-                const int n = (int)win_total;
-                // rank by (key desc, index asc); place into sorted slots [kWinTotal, 2*kWinTotal)
-                for (int i = tid; i < n; i += kNT) {
-                    const uint2 me = g[i];
-                    int r = 0;
-                    for (int j2 = 0; j2 < n; ++j2) {
-                        const uint2 o = g[j2];
-                        r += (o.x > me.x) || (o.x == me.x && o.y < me.y);
-                    }
-                    g[kWinTotal + r] = me;
-                }
-                __syncthreads();
-                if (tid < 32) {
-                    // walk ranks with exact F; n' = min(k, n_p)
-                    unsigned long long A = 0;
-                    int nsel = -1;
-                    for (int base = 0; base < n && nsel < 0; base += 32) {
-                        const int r = base + lane;
-                        unsigned long long F = 0;
-                        if (r < n) F = fix_of_y(y_clamped(bf(key_bits(g[kWinTotal + r].x)), m, ti.c));
-                        unsigned long long inc = F;
-#pragma unroll
-                        for (int o = 1; o < 32; o <<= 1) {
-                            const unsigned long long v = __shfl_up_sync(0xffffffffu, inc, o);
-                            if (lane >= o) inc += v;
-                        }
-                        const unsigned long long Ar = A + inc - F;  // mass ranked ahead of r
-                        // rank r is kept iff r < k and A_r <= thr (r = 0 always)
-                        const bool out = r < n && (r >= kk || (long long)Ar > thr) && r > 0;
-                        const uint32_t bal = __ballot_sync(0xffffffffu, out);
-                        if (bal) nsel = base + __ffs(bal) - 1;
-                        A += __shfl_sync(0xffffffffu, inc, 31);
-                    }
-                    if (nsel < 0) nsel = n < kk ? n : (int)kk;  // window exhausted: rank k-1 is last
-                    // kept ranks 0..nsel-1
-                    unsigned long long sk = 0;
-                    for (int r = lane; r < nsel; r += 32)
-                        sk += fix_of_y(y_clamped(bf(key_bits(g[kWinTotal + r].x)), m, ti.c));
-                    sk = warp_sum_u64(sk);
-                    if (lane == 0) {
-                        const uint2 last = g[kWinTotal + nsel - 1];
-                        put_desc(a, ti, m, last.x, (int)last.y, sk, 0, 0u);
-                    }
-                }
-            }
-            PROF_END(ti.cat, 4);
-            continue;
-        }
-
-        // ---- binned selection (also the fallback of an overflowing window) -------------------
-        unsigned ex_bins = ex2;
         if (cat == kWindow) {
-            // window overflow: a binned pass over the same registers
+            uint32_t win_total = 0;
+            bool win_over = false;
+            for (int q = 0; q < kCS; ++q) {
+                const uint32_t n = ar->wcnt[q];
+                win_total += n;
+                win_over |= n > (uint32_t)kAreaWin;
+            }
+            if (!win_over && win_total <= (uint32_t)kWinTotal) {
+                if (lead) window_resolve_area(a, ti, ar, sh, win_total, cx.L, m, kk, thr);
+                PROF_END(ti.cat, 4);
+                continue;
+            }
+        }
+        // binned rows and overflowing windows need the row slice
+        load_slice<NVT>(sl, w);
+        unsigned ex_bins = 0;
+        bool bins_remote = false;
+        if (cat == kWindow) {
+            // window overflow: level-1 bins of the slice here (the scan kernel binned only
+            // binned rows), exchanged across the cluster
             uint4* az = reinterpret_cast<uint4*>(sh->acc);
             __syncthreads();
             for (int i = tid; i < kBins * kNT / 2; i += kNT) az[i] = make_uint4(0, 0, 0, 0);
@@ -992,21 +1129,21 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
             reread_bins(sl, m, ti.c, 0, 0, sh);
             __syncthreads();
             Pub& pbw = sh->pub[cx.ex & 1];
-            for (int bb = 0; bb < kBins / kNW; ++bb) {
-                const int bin = wid * (kBins / kNW) + bb;
-                long long s = 0;
+            for (int bin = wid; bin < kBins; bin += kNW) {
+                long long sm = 0;
                 for (int i = lane; i < kNT; i += 32) {
                     const uint2 v = sh->acc[bin * kNT + i];
-                    s += (long long)v.x * 8388608 + (int32_t)v.y;
+                    sm += (long long)v.x * 8388608 + (int32_t)v.y;
                 }
-                s = (long long)warp_sum_u64((unsigned long long)s);
+                sm = (long long)warp_sum_u64((unsigned long long)sm);
                 if (lane == 0) {
-                    pbw.mass[bin] = (unsigned long long)s;
+                    pbw.mass[bin] = (unsigned long long)sm;
                     pbw.cnt[bin] = sh->bcnt[bin];
                 }
             }
-            cluster_barrier();  // exchange 2b
+            cluster_barrier();  // exchange of the overflow bins
             ex_bins = cx.ex++;
+            bins_remote = true;
             cat = kBinned;
             PROF_MARK(ti.cat, 5);
         }
@@ -1019,10 +1156,15 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
             uint32_t cs = 0;
             unsigned long long ms = 0;
             if (lane < kBins) {
-                for (int q = 0; q < kCS; ++q) {
-                    const Pub* rp = remote_pub(cx, q, ex_bins);
-                    cs += rp->cnt[lane];
-                    ms += rp->mass[lane];
+                if (bins_remote) {
+                    for (int q = 0; q < kCS; ++q) {
+                        const Pub* rp = remote_pub(cx, q, ex_bins);
+                        cs += rp->cnt[lane];
+                        ms += rp->mass[lane];
+                    }
+                } else {
+                    cs = ar->cnt[lane];
+                    ms = ar->mass[lane];
                 }
             }
             tc[lane] = cs;
@@ -1033,7 +1175,6 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
                 sh->sel[0] = wk.group;
                 sh->self64[0] = wk.cnt;
                 sh->self64[1] = wk.mass;
-                sh->sel[2] = wk.group >= 0 ? (int)tc[wk.group] : 0;
             }
         }
         __syncthreads();
@@ -1061,36 +1202,34 @@ __global__ void __launch_bounds__(kNT, 2) row_kernel(VerifyArgs a) {
         if ((uint32_t)sh->sel[5] - (uint32_t)sh->sel[4] + 1u > (uint32_t)kKeyChunk) {
         // ---- level 2: sub-bins of bin b1 ---------------------------------------------------
         {
-            // valid elements of bin b1 in this CTA (fill slots are excluded from the list)
-            const uint32_t my_cnt = sh->pub[ex_bins & 1].cnt[b1];
-            const bool compact = my_cnt <= (uint32_t)kListCap;
             __syncthreads();
             uint4* az = reinterpret_cast<uint4*>(sh->acc);
             for (int i = tid; i < kSub * kNT / 2; i += kNT) az[i] = make_uint4(0, 0, 0, 0);
             if (tid < kBins) sh->bcnt[tid] = 0;
             if (tid == 0) sh->nlist = 0;
+            // this CTA's valid elements of bin b1: positions by a block-wide exclusive scan of
+            // per-thread counts (no atomics); compacted into the list when they fit
+            uint32_t cnt_me = 0;
+#pragma unroll
+            for (int j = 0; j < NVT; ++j) {
+                const uint32_t* u = reinterpret_cast<const uint32_t*>(&w[j]);
+#pragma unroll
+                for (int hh = 0; hh < 8; ++hh) {
+                    const uint32_t bits = (hh & 1) ? (u[hh >> 1] >> 16) : (u[hh >> 1] & 0xFFFFu);
+                    cnt_me += (bin1_of(y_clamped(bf(bits), m, ti.c)) == b1 &&
+                               elem_valid(sl, elem_index(sl, j, hh))) ? 1u : 0u;
+                }
+            }
+            const uint32_t incl = warp_incl_u32(cnt_me);
+            if (lane == 31) sh->red32[wid] = incl;
             __syncthreads();
+            uint32_t pos = incl - cnt_me, total = 0;
+            for (int i = 0; i < kNW; ++i) {
+                if (i < wid) pos += sh->red32[i];
+                total += sh->red32[i];
+            }
+            const bool compact = total <= (uint32_t)kListCap;
             if (compact) {
-                // positions by a block-wide exclusive scan of per-thread counts (no atomics)
-                uint32_t cnt_me = 0;
-#pragma unroll
-                for (int j = 0; j < NVT; ++j) {
-                    const uint32_t* u = reinterpret_cast<const uint32_t*>(&w[j]);
-#pragma unroll
-                    for (int hh = 0; hh < 8; ++hh) {
-                        const uint32_t bits = (hh & 1) ? (u[hh >> 1] >> 16) : (u[hh >> 1] & 0xFFFFu);
-                        cnt_me += (bin1_of(y_clamped(bf(bits), m, ti.c)) == b1 &&
-                                   elem_valid(sl, elem_index(sl, j, hh))) ? 1u : 0u;
-                    }
-                }
-                const uint32_t incl = warp_incl_u32(cnt_me);
-                if (lane == 31) sh->red32[wid] = incl;
-                __syncthreads();
-                uint32_t pos = incl - cnt_me, total = 0;
-                for (int i = 0; i < kNW; ++i) {
-                    if (i < wid) pos += sh->red32[i];
-                    total += sh->red32[i];
-                }
                 if (tid == 0) sh->nlist = total;
                 if (cnt_me) {
 #pragma unroll
@@ -1474,6 +1613,20 @@ __global__ void __launch_bounds__(kNT) chain_kernel(VerifyArgs a) {
     const int tid = threadIdx.x, lane = tid & 31;
     const int rank = (int)cluster.block_rank();
     const int b = blockIdx.x / kCS;  // gridDim = B * kCS: one cluster per request
+    if (rank == 0) {
+        // the scan areas of this request's rows start the next launch at zero
+        for (int i = tid; i < kT * 2; i += kNT) {
+            TaskArea* ar = &a.area[b * kT * 2 + i];
+            ar->S = 0ull;
+            ar->wcnt[0] = ar->wcnt[1] = ar->wcnt[2] = ar->wcnt[3] = 0u;
+            ar->wcnt[4] = ar->wcnt[5] = ar->wcnt[6] = ar->wcnt[7] = 0u;
+        }
+        for (int i = tid; i < kT * 2 * kBins; i += kNT) {
+            TaskArea* ar = &a.area[b * kT * 2 + i / kBins];
+            ar->mass[i % kBins] = 0ull;
+            ar->cnt[i % kBins] = 0u;
+        }
+    }
 
     const int cap = clamp_cap(a.caps[b]);
     const float T = a.temperature[b];
@@ -1701,15 +1854,14 @@ __global__ void __launch_bounds__(kNT) chain_kernel(VerifyArgs a) {
 // launcher
 
 template <int NVT>
-int launch_rows(VerifyArgs a, cudaStream_t stream) {
-    auto kern = row_kernel<NVT>;
-    const size_t smem = ((sizeof(RowSmem) + 15) & ~(size_t)15) + (size_t)NVT * kNT * sizeof(uint4);
-    static int attr_done = 0;
-    if (!attr_done) {
+int launch_cluster_kernel(void (*kern)(VerifyArgs), VerifyArgs a, cudaStream_t stream, int which) {
+    const size_t smem = ((sizeof(RowSmem) + 15) & ~(size_t)15) +
+                        (which == 0 ? (size_t)2 * NVT * kNT * sizeof(uint4) : (size_t)0);
+    static int attr_done[2] = {0, 0};
+    if (!attr_done[which]) {
         if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
             return kLaunchFailed;
-        cudaFuncSetAttribute(kern, cudaFuncAttributeNonPortableClusterSizeAllowed, 0);
-        attr_done = 1;
+        attr_done[which] = 1;
     }
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
@@ -1722,23 +1874,30 @@ int launch_rows(VerifyArgs a, cudaStream_t stream) {
     cfg.stream = stream;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    static int cached_dev = -1, cached_n = 0;
+    static int cached_dev[2] = {-1, -1}, cached_n[2] = {0, 0};
     int dev = 0;
     cudaGetDevice(&dev);
     int nclus = 0;
-    if (cached_dev == dev) {
-        nclus = cached_n;
+    if (cached_dev[which] == dev) {
+        nclus = cached_n[which];
     } else {
         cfg.gridDim = dim3(kCS, 1, 1);
         if (cudaOccupancyMaxActiveClusters(&nclus, kern, &cfg) != cudaSuccess || nclus <= 0)
             return kLaunchFailed;
-        cached_dev = dev;
-        cached_n = nclus;
+        cached_dev[which] = dev;
+        cached_n[which] = nclus;
     }
     a.num_clusters = nclus;
     cfg.gridDim = dim3(nclus * kCS, 1, 1);
     if (cudaLaunchKernelEx(&cfg, kern, a) != cudaSuccess) return kLaunchFailed;
     return kOk;
+}
+
+template <int NVT>
+int launch_rows(VerifyArgs a, cudaStream_t stream) {
+    int st = launch_cluster_kernel<NVT>(scan_kernel<NVT>, a, stream, 0);
+    if (st != kOk) return st;
+    return launch_cluster_kernel<NVT>(select_kernel<NVT>, a, stream, 1);
 }
 
 int launch_chain(VerifyArgs a, cudaStream_t stream) {
@@ -1787,7 +1946,7 @@ bool stream_supported(const VerifyArgs& a, int dtype) {
     if (a.B > st::kMaxB || a.desc == nullptr) return false;
     if ((reinterpret_cast<uintptr_t>(a.tgt) & 1u) || (a.drf && (reinterpret_cast<uintptr_t>(a.drf) & 1u)))
         return false;
-    return stream_nvt(a.V) <= 10;
+    return stream_nvt(a.V) <= 5;
 }
 
 int launch_stream(VerifyArgs a, cudaStream_t stream) {
@@ -1796,8 +1955,7 @@ int launch_stream(VerifyArgs a, cudaStream_t stream) {
     int st_ = kUnsupported;
     if (nvt <= 1) st_ = st::launch_rows<1>(a, stream);
     else if (nvt <= 2) st_ = st::launch_rows<2>(a, stream);
-    else if (nvt <= 4) st_ = st::launch_rows<4>(a, stream);
-    else if (nvt <= 10) st_ = st::launch_rows<10>(a, stream);
+    else if (nvt <= 5) st_ = st::launch_rows<5>(a, stream);
     if (st_ != kOk) return st_;
     return st::launch_chain(a, stream);
 }
