@@ -264,23 +264,24 @@ static_assert(offsetof(RowSmem, acc) % 16 == 0, "acc must be 16-byte aligned");
 
 __device__ __forceinline__ int clamp_cap(int c) { return c < 1 ? 1 : (c > kT ? kT : c); }
 
-__device__ int request_cat(const VerifyArgs& a, int b, float& c_out) {
+__device__ int request_cat(const VerifyArgs& a, int b, float& c_out, int wink = kWinK) {
     const float T = a.temperature[b];
     const int k = a.top_k[b];
     const float c = log2e_over(T);
     c_out = c;
     if (is_greedy(T, k, c)) return kGreedy;
     if (k >= a.V && !(a.top_p[b] < 1.0f)) return kKeepAll;
-    if (k <= kWinK) return kWindow;
+    if (k <= wink) return kWindow;
     return kBinned;
 }
 
 // every CTA builds the same task table: binned rows first, then keep-all/window, then greedy
-__device__ void build_plan(const VerifyArgs& a, RowSmem* sh) {
+template <typename Sm>
+__device__ void build_plan(const VerifyArgs& a, Sm* sh, int wink = kWinK) {
     const int tid = threadIdx.x;
-    for (int b = tid; b < a.B; b += kNT) {
+    for (int b = tid; b < a.B; b += blockDim.x) {
         float c;
-        const int cat = request_cat(a, b, c);
+        const int cat = request_cat(a, b, c, wink);
         const int cap = clamp_cap(a.caps[b]);
         sh->req[b] = (uint8_t)(cat | (cap << 3));
     }
@@ -313,11 +314,13 @@ __device__ void build_plan(const VerifyArgs& a, RowSmem* sh) {
     __syncthreads();
 }
 
-__device__ int total_tasks(const VerifyArgs& a, const RowSmem* sh) {
+template <typename Sm>
+__device__ int total_tasks(const VerifyArgs& a, const Sm* sh) {
     return sh->pre[0][a.B] + sh->pre[1][a.B] + sh->pre[2][a.B];
 }
 
-__device__ TaskInfo decode_task(const VerifyArgs& a, const RowSmem* sh, int t) {
+template <typename Sm>
+__device__ TaskInfo decode_task(const VerifyArgs& a, const Sm* sh, int t) {
     int g = 0;
     int local = t;
     while (g < 2 && local >= sh->pre[g][a.B]) {
@@ -1512,6 +1515,653 @@ __global__ void __launch_bounds__(kNT, 1) select_kernel(VerifyArgs a) {
     cluster_barrier();
 }
 
+
+// =======================================================================================
+// Row kernel: ONE CTA per row, no clusters.  Each CTA streams its whole row from global
+// memory with 16-byte loads: pass 1 (max; greedy rows finish here) reads HBM, pass 2 (exact
+// exp, fixed-point sum and either the candidate window or the level-1 bins) and the few
+// selection passes re-read the row from L2.  All selection is CTA-local (no cross-SM
+// exchange); two CTAs per SM overlap a memory-bound pass with an ALU-bound one.  Rows are
+// handed out by a global counter, most expensive first.
+
+constexpr int kRT = 256;           // threads per CTA
+constexpr int kRW = kRT / 32;      // warps
+constexpr int kRWinK = kRT;        // top-k rows with k <= 256 select inside the window
+constexpr int kRWinCap = 1024;     // window candidates per row
+constexpr int kRKeyCap = 4096;     // keys per level-3 histogram chunk
+
+struct RSmem {
+    uint16_t pre[3][kMaxB + 1];
+    uint8_t req[kMaxB];
+    int task;
+    int first_min;
+    uint32_t nlist;
+    uint32_t red32[32];
+    unsigned long long red64[32];
+    int sel[16];
+    unsigned long long self64[8];
+    uint32_t wc[32];
+    unsigned long long wm[32];
+    uint32_t bcnt[kBins];
+    uint32_t wkey[kRWinCap];       // window candidates: key
+    uint32_t widx[kRWinCap];       //                    element index
+    alignas(16) uint2 acc[kBins * kRT];     // private bin accumulators / window sort area
+    alignas(16) uint32_t khist[kRKeyCap];   // key counts / level-2 list
+};
+
+struct RowGeo {
+    const uint16_t* rowp;
+    int off, nv;   // element e is half (e + off) % 8 of vector (e + off) / 8
+};
+
+__device__ __forceinline__ RowGeo row_geo(const VerifyArgs& a, const TaskInfo& ti) {
+    RowGeo g;
+    const uint16_t* base = reinterpret_cast<const uint16_t*>(ti.kind == 0 ? a.tgt : a.drf);
+    g.rowp = base + (ti.row < 0 ? 0 : ti.row) * a.stride;
+    g.off = (int)((reinterpret_cast<uintptr_t>(g.rowp) & 15u) >> 1);
+    g.nv = ti.row < 0 ? 0 : (a.V + g.off + 7) >> 3;
+    return g;
+}
+
+// vector v of the row with the halves outside [0, V) set to -inf
+__device__ __forceinline__ uint4 row_vec(const RowGeo& g, int V, const uint4* src, int v, uint4 x) {
+    if (v == 0 || v == g.nv - 1) {
+        uint32_t* u = reinterpret_cast<uint32_t*>(&x);
+#pragma unroll
+        for (int h = 0; h < 8; ++h) {
+            const int e = 8 * v + h - g.off;
+            if (e < 0 || e >= V) {
+                const uint32_t msk = (h & 1) ? 0xFFFF0000u : 0x0000FFFFu;
+                u[h >> 1] = (u[h >> 1] & ~msk) | (kFill & msk);
+            }
+        }
+    }
+    return x;
+}
+
+// stream the row through fn(vector, v): four 16-byte loads in flight per thread
+template <typename F>
+__device__ __forceinline__ void stream_row(const RowGeo& g, int V, F&& fn) {
+    const uint4* src = reinterpret_cast<const uint4*>(g.rowp - g.off);
+    int v = threadIdx.x;
+    for (; v + 3 * kRT < g.nv; v += 4 * kRT) {
+        uint4 x[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) x[u] = __ldg(src + v + u * kRT);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) fn(row_vec(g, V, src, v + u * kRT, x[u]), v + u * kRT);
+    }
+    for (; v < g.nv; v += kRT) fn(row_vec(g, V, src, v, __ldg(src + v)), v);
+}
+
+__device__ __forceinline__ unsigned long long rcta_sum_u64(unsigned long long v, RSmem* sh) {
+    v = warp_sum_u64(v);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) sh->red64[threadIdx.x >> 5] = v;
+    __syncthreads();
+    unsigned long long s = 0;
+#pragma unroll
+    for (int i = 0; i < kRW; ++i) s += sh->red64[i];
+    return s;
+}
+
+// reduce the private accumulators of nb bins into (mass, count) pairs in wm/wc
+__device__ void reduce_bins(RSmem* sh, int nb, uint32_t fill_last) {
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    __syncthreads();
+    for (int bin = wid; bin < nb; bin += kRW) {
+        long long sm = 0;
+        for (int i = lane; i < kRT; i += 32) {
+            const uint2 v = sh->acc[bin * kRT + i];
+            sm += (long long)v.x * 8388608 + (int32_t)v.y;
+        }
+        sm = (long long)warp_sum_u64((unsigned long long)sm);
+        if (lane == 0) {
+            sh->wm[bin] = (unsigned long long)sm;
+            sh->wc[bin] = sh->bcnt[bin] - (bin == nb - 1 ? fill_last : 0u);
+        }
+    }
+    if (tid < 32 && tid >= nb) {
+        sh->wm[tid] = 0ull;
+        sh->wc[tid] = 0u;
+    }
+    __syncthreads();
+}
+
+__device__ __forceinline__ void clear_bins(RSmem* sh, int nb) {
+    __syncthreads();
+    uint4* az = reinterpret_cast<uint4*>(sh->acc);
+    for (int i = threadIdx.x; i < nb * kRT / 2; i += kRT) az[i] = make_uint4(0, 0, 0, 0);
+    if (threadIdx.x < kBins) sh->bcnt[threadIdx.x] = 0;
+    __syncthreads();
+}
+
+__device__ __forceinline__ void acc_add(RSmem* sh, int slot, uint32_t hbits, uint32_t lbits) {
+    uint2* p = &sh->acc[slot * kRT + threadIdx.x];
+    uint2 v = *p;
+    v.x += hbits - 0x4B000000u;
+    v.y += lbits - 0x4B400000u;
+    *p = v;
+    atomicAdd(&sh->bcnt[slot], 1u);
+}
+
+// CTA-wide walk over the per-key counts of keys khi, khi-1, ... (n keys, thread t owns a
+// contiguous run): the first key where the count reaches k or the mass passes thr
+__device__ KeyStop cta_walk_keys(RSmem* sh, const uint32_t* counts, uint32_t khi, int n, float m,
+                                 float c, unsigned long long cnt0, unsigned long long mass0,
+                                 long long k, long long thr) {
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const int per = (n + kRT - 1) / kRT;
+    const int i0 = min(tid * per, n), i1 = min(i0 + per, n);
+    unsigned long long cs = 0, ms = 0;
+    for (int i = i0; i < i1; ++i) {
+        const uint32_t cc = counts[i];
+        if (cc) {
+            cs += cc;
+            ms += (unsigned long long)cc * fix_of_y(y_clamped(bf(key_bits(khi - (uint32_t)i)), m, c));
+        }
+    }
+    // block exclusive scan of (cs, ms)
+    unsigned long long ci = cs, mi = ms;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const unsigned long long a = __shfl_up_sync(0xffffffffu, ci, o);
+        const unsigned long long b = __shfl_up_sync(0xffffffffu, mi, o);
+        if (lane >= o) { ci += a; mi += b; }
+    }
+    __syncthreads();
+    if (lane == 31) {
+        sh->wc[wid] = (uint32_t)0;
+        sh->red64[wid] = ci;
+        sh->wm[wid] = mi;
+    }
+    if (tid == 0) sh->sel[6] = 0x7fffffff;
+    __syncthreads();
+    unsigned long long cb = cnt0 + ci - cs, mb = mass0 + mi - ms;
+    for (int w = 0; w < wid; ++w) {
+        cb += sh->red64[w];
+        mb += sh->wm[w];
+    }
+    // my first stopping key, if any
+    for (int i = i0; i < i1; ++i) {
+        const uint32_t cc = counts[i];
+        if (!cc) continue;
+        const unsigned long long F = fix_of_y(y_clamped(bf(key_bits(khi - (uint32_t)i)), m, c));
+        if ((long long)(cb + cc) >= k || (long long)(mb + cc * F) > thr) {
+            atomicMin(&sh->sel[6], i);
+            break;
+        }
+        cb += cc;
+        mb += cc * F;
+    }
+    __syncthreads();
+    KeyStop ks;
+    ks.found = sh->sel[6] != 0x7fffffff;
+    const int istop = sh->sel[6];
+    __syncthreads();
+    if (ks.found && istop >= i0 && istop < i1) {
+        // the owner of the stopping key recomputes its prefix and publishes the stop
+        unsigned long long cb2 = cnt0 + ci - cs, mb2 = mass0 + mi - ms;
+        for (int w = 0; w < wid; ++w) {
+            cb2 += sh->red64[w];
+            mb2 += sh->wm[w];
+        }
+        for (int i = i0; i < istop; ++i) {
+            const uint32_t cc = counts[i];
+            if (!cc) continue;
+            cb2 += cc;
+            mb2 += cc * fix_of_y(y_clamped(bf(key_bits(khi - (uint32_t)i)), m, c));
+        }
+        sh->self64[4] = cb2;
+        sh->self64[5] = mb2;
+        sh->self64[6] = fix_of_y(y_clamped(bf(key_bits(khi - (uint32_t)istop)), m, c));
+        sh->sel[7] = (int)(khi - (uint32_t)istop);
+        sh->sel[8] = (int)counts[istop];
+    }
+    // totals of the whole range (for a continuation into the next chunk)
+    if (tid == 0) {
+        unsigned long long ct = cnt0, mt = mass0;
+        for (int w = 0; w < kRW; ++w) {
+            ct += sh->red64[w];
+            mt += sh->wm[w];
+        }
+        sh->self64[2] = ct;
+        sh->self64[3] = mt;
+    }
+    __syncthreads();
+    if (ks.found) {
+        ks.key = (uint32_t)sh->sel[7];
+        ks.count = (uint32_t)sh->sel[8];
+        ks.cnt = sh->self64[4];
+        ks.mass = sh->self64[5];
+        ks.F = sh->self64[6];
+    } else {
+        ks.cnt = sh->self64[2];
+        ks.mass = sh->self64[3];
+    }
+    __syncthreads();
+    return ks;
+}
+
+__global__ void __launch_bounds__(kRT, 2) rows_kernel(VerifyArgs a) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    RSmem* sh = reinterpret_cast<RSmem*>(smem_raw);
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    build_plan(a, sh, kRWinK);
+    const int ntask = total_tasks(a, sh);
+    const int V = a.V;
+
+    for (;;) {
+        __syncthreads();
+        if (tid == 0) sh->task = (int)atomicAdd(&a.ws->next, 1u);
+        __syncthreads();
+        const int t = sh->task;
+        if (t >= ntask) break;
+        PROF_START();
+        const TaskInfo ti = decode_task(a, sh, t);
+        if (ti.row < 0 && tid == 0) atomicOr(&a.ws->err, 2u);
+        const RowGeo g = row_geo(a, ti);
+        const bool greedy = ti.cat == kGreedy;
+        const uint32_t nfill = (uint32_t)g.nv * 8u - (uint32_t)(g.nv ? V : 0);
+
+        // ---- pass 1: max (greedy rows: and the first index of the max) -------------------
+        uint32_t tkey = 0;
+        int tfirst = 0x7fffffff;
+        stream_row(g, V, [&](const uint4& x, int v) {
+            uint32_t mx = bf2_max(bf2_max(x.x, x.y), bf2_max(x.z, x.w));
+            const uint32_t k0 = okey(mx & 0xFFFFu), k1 = okey(mx >> 16);
+            const uint32_t vk = k0 > k1 ? k0 : k1;
+            if (vk > tkey) {
+                tkey = vk;
+                if (greedy) {
+                    // first half of this vector with the new maximum (vectors arrive in order)
+                    const uint32_t b = key_bits(vk);
+                    const uint32_t b2 = b | (b << 16);
+                    const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+                    int f = 0x7fffffff;
+#pragma unroll
+                    for (int h = 7; h >= 0; --h) {
+                        const uint32_t eq = bf2_eq(xs[h >> 1], b2) & ((h & 1) ? 0xFFFF0000u : 0x0000FFFFu);
+                        const int e = 8 * v + h - g.off;
+                        if (eq && e >= 0 && e < V) f = e;
+                    }
+                    tfirst = f;
+                }
+            }
+        });
+        PROF_MARK(ti.cat, 0);
+        const uint32_t wk = __reduce_max_sync(0xffffffffu, tkey);
+        if (lane == 0) sh->red32[wid] = wk;
+        if (tid == 0) sh->first_min = 0x7fffffff;
+        __syncthreads();
+        uint32_t mkey = 0;
+#pragma unroll
+        for (int i = 0; i < kRW; ++i) mkey = max(mkey, sh->red32[i]);
+        if (greedy) {
+            if (tkey == mkey && tfirst != 0x7fffffff) atomicMin(&sh->first_min, tfirst);
+            __syncthreads();
+            if (tid == 0) {
+                const int f = sh->first_min;
+                if (f != 0x7fffffff)
+                    a.gmax[ti.b * kT + ti.s] = ((unsigned long long)mkey << 32) | (0xFFFFFFFFull - (unsigned)f);
+                put_desc(a, ti, bf(key_bits(mkey)), mkey, f, 1ull << kFixBits, f == 0x7fffffff ? 0 : f,
+                         kDescGreedy);
+            }
+            PROF_END(ti.cat, 1);
+            continue;
+        }
+        const float m = bf(key_bits(mkey));
+        const long long kk = ti.k < V ? (long long)ti.k : (long long)V;
+        int cat = ti.cat;
+        // window threshold: the largest tau with at least k thread maxima >= tau (each such
+        // thread holds an element >= tau)
+        uint32_t tau = 0;
+        if (cat == kWindow) {
+            for (int bit = 15; bit >= 0; --bit) {
+                const uint32_t cand = tau | (1u << bit);
+                if (__syncthreads_count(tkey >= cand) >= kk) tau = cand;
+            }
+            // fewer than k threads hold data (tiny vocabularies): take every element >= -inf
+            const uint32_t kneg = okey(0xFF80u);
+            if (tau < kneg) tau = kneg;
+            if (tid == 0) sh->nlist = 0;
+        }
+        if (cat == kBinned) clear_bins(sh, kBins);
+        __syncthreads();
+
+        // ---- pass 2: exact exp, fixed-point sum, window candidates or level-1 bins --------
+        const float2 nm = make_float2(-m, -m), c2 = make_float2(ti.c, ti.c);
+        const uint32_t taub = key_bits(tau);
+        const uint32_t tau2 = taub | (taub << 16);
+        uint32_t hs = 0, ls = 0, nel = 0;
+        stream_row(g, V, [&](const uint4& x, int v) {
+            const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+            nel += 8;
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const Pair pr = exp_pair(xs[q], nm, c2);
+                hs += pr.h0 + pr.h1;
+                ls += pr.l0 + pr.l1;
+                if (cat == kBinned) {
+                    acc_add(sh, bin1_of(pr.yc.x), pr.h0, pr.l0);
+                    acc_add(sh, bin1_of(pr.yc.y), pr.h1, pr.l1);
+                } else if (cat == kWindow) {
+                    const uint32_t ge = bf2_ge(xs[q], tau2);
+                    if (ge) {
+#pragma unroll
+                        for (int h = 0; h < 2; ++h) {
+                            const int e = 8 * v + 2 * q + h - g.off;
+                            if ((ge & (h ? 0xFFFF0000u : 0x0000FFFFu)) && e >= 0 && e < V) {
+                                const uint32_t pos = atomicAdd(&sh->nlist, 1u);
+                                if (pos < kRWinCap) {
+                                    sh->wkey[pos] = okey(h ? (xs[q] >> 16) : (xs[q] & 0xFFFFu));
+                                    sh->widx[pos] = (uint32_t)e;
+                                }
+                            }
+                        }
+                    }
+                }
+            }
+        });
+        const uint32_t hi_t = hs - nel * 0x4B000000u;
+        const int32_t lo_t = (int32_t)(ls - nel * 0x4B400000u);
+        PROF_MARK(ti.cat, 2);
+        const unsigned long long S = rcta_sum_u64((unsigned long long)((long long)hi_t * 8388608 + lo_t), sh);
+        const long long thr = (ti.p < 1.0f) ? scale_floor(ti.p, S) : 0x7fffffffffffffffll;
+
+        if (cat == kKeepAll) {
+            if (tid == 0) put_desc(a, ti, m, 0u, 0x7fffffff, S, 0, 0u);
+            PROF_END(ti.cat, 3);
+            continue;
+        }
+        if (cat == kWindow) {
+            const int n = (int)sh->nlist;
+            if (n >= 1 && n <= kRWinCap) {
+                // rank the candidates by (key desc, index asc) into acc (as uint2)
+                uint2* srt = sh->acc;
+                for (int i = tid; i < n; i += kRT) {
+                    const uint32_t ki = sh->wkey[i], xi = sh->widx[i];
+                    int r = 0;
+                    for (int j = 0; j < n; ++j) {
+                        const uint32_t kj = sh->wkey[j];
+                        r += (kj > ki) || (kj == ki && sh->widx[j] < xi);
+                    }
+                    srt[r] = make_uint2(ki, xi);
+                }
+                __syncthreads();
+                if (tid < 32) {
+                    unsigned long long A = 0;
+                    int nsel = -1;
+                    for (int base = 0; base < n && nsel < 0; base += 32) {
+                        const int r = base + lane;
+                        unsigned long long F = 0;
+                        if (r < n) F = fix_of_y(y_clamped(bf(key_bits(srt[r].x)), m, ti.c));
+                        unsigned long long inc = F;
+#pragma unroll
+                        for (int o = 1; o < 32; o <<= 1) {
+                            const unsigned long long vv = __shfl_up_sync(0xffffffffu, inc, o);
+                            if (lane >= o) inc += vv;
+                        }
+                        const unsigned long long Ar = A + inc - F;
+                        const bool out = r < n && r > 0 && (r >= kk || (long long)Ar > thr);
+                        const uint32_t bal = __ballot_sync(0xffffffffu, out);
+                        if (bal) nsel = base + __ffs(bal) - 1;
+                        A += __shfl_sync(0xffffffffu, inc, 31);
+                    }
+                    if (nsel < 0) nsel = n < kk ? n : (int)kk;
+                    unsigned long long sk = 0;
+                    for (int r = lane; r < nsel; r += 32)
+                        sk += fix_of_y(y_clamped(bf(key_bits(srt[r].x)), m, ti.c));
+                    sk = warp_sum_u64(sk);
+                    if (lane == 0) put_desc(a, ti, m, srt[nsel - 1].x, (int)srt[nsel - 1].y, sk, 0, 0u);
+                }
+                PROF_END(ti.cat, 3);
+                continue;
+            }
+            // the window overflowed: level-1 bins in another pass
+            clear_bins(sh, kBins);
+            stream_row(g, V, [&](const uint4& x, int) {
+                const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const Pair pr = exp_pair(xs[q], nm, c2);
+                    acc_add(sh, bin1_of(pr.yc.x), pr.h0, pr.l0);
+                    acc_add(sh, bin1_of(pr.yc.y), pr.h1, pr.l1);
+                }
+            });
+            cat = kBinned;
+        }
+
+        // ---- binned selection --------------------------------------------------------------
+        PROF_MARK(ti.cat, 4);
+        reduce_bins(sh, kBins, nfill);
+        if (tid < 32) {
+            const Walk wk1 = walk_groups(sh->wc, sh->wm, kBins, 0ull, 0ull, kk, thr);
+            if (lane == 0) {
+                sh->sel[0] = wk1.group;
+                sh->self64[0] = wk1.cnt;
+                sh->self64[1] = wk1.mass;
+            }
+        }
+        __syncthreads();
+        const int b1 = sh->sel[0];
+        if (b1 < 0) {
+            if (tid == 0) put_desc(a, ti, m, 0u, 0x7fffffff, S, 0, 0u);
+            continue;
+        }
+        unsigned long long cum_cnt = sh->self64[0], cum_mass = sh->self64[1];
+        if (tid < 32) {
+            uint32_t klo1, khi1;
+            key_range(b1, okey(0xFF80u), mkey, m, ti.c, 1, klo1, khi1);
+            if (lane == 0) {
+                sh->sel[4] = (int)klo1;
+                sh->sel[5] = (int)khi1;
+            }
+        }
+        __syncthreads();
+        uint32_t klo = (uint32_t)sh->sel[4], khi = (uint32_t)sh->sel[5];
+        if (khi - klo + 1u > (uint32_t)kRKeyCap) {
+            // level 2: sub-bins of bin b1 (exp again, only elements of the bin accumulate)
+            clear_bins(sh, kSub);
+            stream_row(g, V, [&](const uint4& x, int v) {
+                const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const Pair pr = exp_pair(xs[q], nm, c2);
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const float yc = h ? pr.yc.y : pr.yc.x;
+                        const int e = 8 * v + 2 * q + h - g.off;
+                        if (bin1_of(yc) == b1 && e >= 0 && e < V)
+                            acc_add(sh, bin2_of(yc, b1), h ? pr.h1 : pr.h0, h ? pr.l1 : pr.l0);
+                    }
+                }
+            });
+            reduce_bins(sh, kSub, 0u);
+            if (tid < 32) {
+                const Walk wk2 = walk_groups(sh->wc, sh->wm, kSub, cum_cnt, cum_mass, kk, thr);
+                if (lane == 0) {
+                    sh->sel[3] = wk2.group;
+                    sh->self64[0] = wk2.cnt;
+                    sh->self64[1] = wk2.mass;
+                }
+            }
+            __syncthreads();
+            const int b2 = sh->sel[3];
+            if (b2 < 0) {
+                if (tid == 0) {
+                    atomicOr(&a.ws->err, 8u);
+                    put_desc(a, ti, m, 0u, 0x7fffffff, S, 0, 0u);
+                }
+                continue;
+            }
+            cum_cnt = sh->self64[0];
+            cum_mass = sh->self64[1];
+            if (tid < 32) {
+                uint32_t klo2, khi2;
+                key_range(b1 * kSub + b2, okey(0xFF80u), mkey, m, ti.c, 2, klo2, khi2);
+                if (lane == 0) {
+                    sh->sel[4] = (int)klo2;
+                    sh->sel[5] = (int)khi2;
+                }
+            }
+            __syncthreads();
+            klo = (uint32_t)sh->sel[4];
+            khi = (uint32_t)sh->sel[5];
+        }
+
+        PROF_MARK(ti.cat, 5);
+        // ---- level 3: per-key counts of the boundary (sub-)bin, in chunks from the top -----
+        KeyStop ks;
+        ks.found = 0;
+        for (uint32_t top = khi; top >= klo && top <= 0xFFFFu;) {
+            const uint32_t bot = (top - klo + 1u > (uint32_t)kRKeyCap) ? top - kRKeyCap + 1 : klo;
+            const int nk = (int)(top - bot + 1);
+            __syncthreads();
+            for (int i = tid; i < nk; i += kRT) sh->khist[i] = 0;
+            __syncthreads();
+            const uint32_t vlo = key_bits(bot), vhi = key_bits(top);
+            const uint32_t vlo2 = vlo | (vlo << 16), vhi2 = vhi | (vhi << 16);
+            stream_row(g, V, [&](const uint4& x, int v) {
+                const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const uint32_t in = bf2_ge(xs[q], vlo2) & bf2_le(xs[q], vhi2);
+                    if (!in) continue;
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int e = 8 * v + 2 * q + h - g.off;
+                        if (!(in & (h ? 0xFFFF0000u : 0x0000FFFFu)) || e < 0 || e >= V) continue;
+                        const uint32_t kkey = okey(h ? (xs[q] >> 16) : (xs[q] & 0xFFFFu));
+                        if (kkey >= bot && kkey <= top) atomicAdd(&sh->khist[top - kkey], 1u);
+                    }
+                }
+            });
+            __syncthreads();
+            ks = cta_walk_keys(sh, sh->khist, top, nk, m, ti.c, cum_cnt, cum_mass, kk, thr);
+            if (ks.found) break;
+            cum_cnt = ks.cnt;
+            cum_mass = ks.mass;
+            if (bot == klo) break;
+            top = bot - 1;
+        }
+        if (!ks.found) {
+            if (tid == 0) {
+                atomicOr(&a.ws->err, 8u);
+                put_desc(a, ti, m, 0u, 0x7fffffff, S, 0, 0u);
+            }
+            continue;
+        }
+        PROF_MARK(ti.cat, 6);
+        unsigned long long ntie = ks.count;
+        if ((long long)(ks.cnt + ntie) > kk) ntie = (unsigned long long)(kk - (long long)ks.cnt);
+        if (ks.F > 0 && (long long)ks.mass <= thr) {
+            const unsigned long long pb_ = (unsigned long long)(thr - (long long)ks.mass) / ks.F + 1ull;
+            if (pb_ < ntie) ntie = pb_;
+        }
+        if (ntie < 1) ntie = 1;
+        const unsigned long long skept = ks.mass + ntie * ks.F;
+        if (ntie >= ks.count) {
+            if (tid == 0) put_desc(a, ti, m, ks.key, 0x7fffffff, skept, 0, 0u);
+            PROF_END(ti.cat, 7);
+            continue;
+        }
+
+        // ---- tie cut: occurrence number ntie of the boundary key in index order ------------
+        // warp w owns the contiguous vector range [w*nvw, (w+1)*nvw); lanes read consecutive
+        // vectors, so index order inside a warp is (group of 32 vectors, lane, half)
+        const uint32_t kb = key_bits(ks.key);
+        const uint32_t kb2 = kb | (kb << 16);
+        const int nvw = (((g.nv + kRW - 1) / kRW) + 31) & ~31;
+        const int v0 = min(wid * nvw, g.nv), v1 = min(v0 + nvw, g.nv);
+        const uint4* src = reinterpret_cast<const uint4*>(g.rowp - g.off);
+        auto count_vec = [&](int v) -> uint32_t {
+            const uint4 x = row_vec(g, V, src, v, __ldg(src + v));
+            const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+            uint32_t c = 0;
+#pragma unroll
+            for (int h = 0; h < 8; ++h) {
+                const uint32_t eq = bf2_eq(xs[h >> 1], kb2) & ((h & 1) ? 0xFFFF0000u : 0x0000FFFFu);
+                const int e = 8 * v + h - g.off;
+                c += (eq && e >= 0 && e < V) ? 1u : 0u;
+            }
+            return c;
+        };
+        uint32_t wcount = 0;
+        for (int v = v0 + lane; v < v1; v += 32) wcount += count_vec(v);
+        wcount = warp_sum_u32(wcount);
+        __syncthreads();
+        if (lane == 0) sh->red32[wid] = wcount;
+        __syncthreads();
+        uint32_t before = 0;
+        for (int i = 0; i < wid; ++i) before += sh->red32[i];
+        if (before < ntie && before + wcount >= ntie) {
+            uint32_t need = (uint32_t)(ntie - before);
+            int tie = -1;
+            for (int gv = v0; gv < v1 && tie < 0; gv += 32) {
+                const int v = gv + lane;
+                const uint32_t c = v < v1 ? count_vec(v) : 0u;
+                const uint32_t incl = warp_incl_u32(c);
+                const uint32_t tot = __shfl_sync(0xffffffffu, incl, 31);
+                if (tot >= need) {
+                    const bool mine = c > 0 && incl - c < need && incl >= need;
+                    if (mine) {
+                        uint32_t k2 = need - (incl - c);
+                        const uint4 x = row_vec(g, V, src, v, __ldg(src + v));
+                        const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+                        for (int h = 0; h < 8; ++h) {
+                            const uint32_t eq = bf2_eq(xs[h >> 1], kb2) & ((h & 1) ? 0xFFFF0000u : 0x0000FFFFu);
+                            const int e = 8 * v + h - g.off;
+                            if (tie < 0 && eq && e >= 0 && e < V && --k2 == 0) tie = e;
+                        }
+                        put_desc(a, ti, m, ks.key, tie, skept, 0, 0u);
+                        if (tie < 0) atomicOr(&a.ws->err, 16u);
+                    }
+                    tie = 0;  // found by the owning lane: the warp stops
+                } else {
+                    need -= tot;
+                }
+            }
+        }
+        PROF_END(ti.cat, 8);
+    }
+    // the last CTA out resets the row counter for the next launch
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        const unsigned old = atomicAdd(&a.ws->exited, 1u);
+        if (old == gridDim.x - 1) {
+            a.ws->next = 0;
+            a.ws->exited = 0;
+            __threadfence();
+        }
+    }
+}
+
+int launch_rows_cta(VerifyArgs a, cudaStream_t stream) {
+    const size_t smem = sizeof(RSmem);
+    static int attr_done = 0;
+    static int cached_dev = -1, cached_blocks = 0;
+    if (!attr_done) {
+        if (cudaFuncSetAttribute(rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+            return kLaunchFailed;
+        attr_done = 1;
+    }
+    int dev = 0;
+    cudaGetDevice(&dev);
+    if (cached_dev != dev) {
+        int per_sm = 0, sms = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rows_kernel, kRT, smem) != cudaSuccess || per_sm < 1)
+            return kLaunchFailed;
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return kLaunchFailed;
+        cached_dev = dev;
+        cached_blocks = per_sm * sms;
+    }
+    rows_kernel<<<cached_blocks, kRT, smem, stream>>>(a);
+    return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
+}
+
 // ---------------------------------------------------------------------------------------
 // chain + bonus + outputs (one cluster per request)
 
@@ -1953,9 +2603,8 @@ int launch_stream(VerifyArgs a, cudaStream_t stream) {
     a.slice = stream_slice(a.V);
     const int nvt = stream_nvt(a.V);
     int st_ = kUnsupported;
-    if (nvt <= 1) st_ = st::launch_rows<1>(a, stream);
-    else if (nvt <= 2) st_ = st::launch_rows<2>(a, stream);
-    else if (nvt <= 5) st_ = st::launch_rows<5>(a, stream);
+    (void)nvt;
+    st_ = st::launch_rows_cta(a, stream);
     if (st_ != kOk) return st_;
     return st::launch_chain(a, stream);
 }
