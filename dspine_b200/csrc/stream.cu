@@ -1528,7 +1528,9 @@ constexpr int kRT = 256;           // threads per CTA
 constexpr int kRW = kRT / 32;      // warps
 constexpr int kRWinK = kRT;        // top-k rows with k <= 256 select inside the window
 constexpr int kRWinCap = 1024;     // window candidates per row
-constexpr int kRKeyCap = 4096;     // keys per level-3 histogram chunk
+constexpr int kRKeyCap = 2048;     // keys per level-3 histogram chunk
+constexpr int kRingS = 4;          // streaming ring: slots
+constexpr int kRingCW = 512;       // vectors (16 B) per slot: 8 KB
 
 struct RSmem {
     uint16_t pre[3][kMaxB + 1];
@@ -1546,7 +1548,10 @@ struct RSmem {
     uint32_t wkey[kRWinCap];       // window candidates: key
     uint32_t widx[kRWinCap];       //                    element index
     alignas(16) uint2 acc[kBins * kRT];     // private bin accumulators / window sort area
-    alignas(16) uint32_t khist[kRKeyCap];   // key counts / level-2 list
+    alignas(16) uint32_t khist[kRKeyCap];   // key counts
+    alignas(16) uint4 ring[kRingS][kRingCW];  // streaming ring filled by bulk copies
+    alignas(8) uint64_t ring_bar[kRingS];
+    uint32_t ring_cnt;                      // chunks consumed so far (slot, phase)
 };
 
 struct RowGeo {
@@ -1579,19 +1584,51 @@ __device__ __forceinline__ uint4 row_vec(const RowGeo& g, int V, const uint4* sr
     return x;
 }
 
-// stream the row through fn(vector, v): four 16-byte loads in flight per thread
+// Stream the row through fn(vector, v) via the ring: thread 0 keeps kRingS chunks of kRingCW
+// vectors in flight with bulk copies (one mbarrier per slot, bounded waits); every thread
+// handles vectors tid and tid + kRT of each chunk.  All threads must call it.
 template <typename F>
-__device__ __forceinline__ void stream_row(const RowGeo& g, int V, F&& fn) {
-    const uint4* src = reinterpret_cast<const uint4*>(g.rowp - g.off);
-    int v = threadIdx.x;
-    for (; v + 3 * kRT < g.nv; v += 4 * kRT) {
-        uint4 x[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) x[u] = __ldg(src + v + u * kRT);
-#pragma unroll
-        for (int u = 0; u < 4; ++u) fn(row_vec(g, V, src, v + u * kRT, x[u]), v + u * kRT);
+__device__ __forceinline__ void stream_row(RSmem* sh, const VerifyArgs& a, const RowGeo& g, int V,
+                                           F&& fn) {
+    const int tid = threadIdx.x;
+    const char* src = reinterpret_cast<const char*>(g.rowp - g.off);
+    const int nch = (g.nv + kRingCW - 1) / kRingCW;
+    const uint32_t base = sh->ring_cnt;  // uniform: read before any thread updates it
+    __syncthreads();
+    if (tid == 0) {
+        for (int c = 0; c < nch && c < kRingS; ++c) {
+            const uint32_t slot = (base + c) % kRingS;
+            const int nvec = min(kRingCW, g.nv - c * kRingCW);
+            fence_proxy_async_smem();
+            mbar_arrive_expect_tx(&sh->ring_bar[slot], (uint32_t)nvec * 16u);
+            bulk_g2s(sh->ring[slot], src + (size_t)c * kRingCW * 16, (uint32_t)nvec * 16u, &sh->ring_bar[slot]);
+        }
     }
-    for (; v < g.nv; v += kRT) fn(row_vec(g, V, src, v, __ldg(src + v)), v);
+    for (int c = 0; c < nch; ++c) {
+        const uint32_t k = base + c;
+        const uint32_t slot = k % kRingS;
+        if (!mbar_wait_bounded(&sh->ring_bar[slot], (k / kRingS) & 1u)) {
+            if (tid == 0) atomicOr(&a.ws->err, 1u);
+        }
+        const int v0 = c * kRingCW;
+        const int nvec = min(kRingCW, g.nv - v0);
+#pragma unroll
+        for (int u = 0; u < kRingCW / kRT; ++u) {
+            const int i = tid + u * kRT;
+            if (i < nvec) fn(row_vec(g, V, nullptr, v0 + i, sh->ring[slot][i]), v0 + i);
+        }
+        __syncthreads();  // the slot is consumed
+        if (tid == 0 && c + kRingS < nch) {
+            const int cn = c + kRingS;
+            const int nv2 = min(kRingCW, g.nv - cn * kRingCW);
+            fence_proxy_async_smem();
+            mbar_arrive_expect_tx(&sh->ring_bar[slot], (uint32_t)nv2 * 16u);
+            bulk_g2s(sh->ring[slot], src + (size_t)cn * kRingCW * 16, (uint32_t)nv2 * 16u, &sh->ring_bar[slot]);
+        }
+    }
+    __syncthreads();
+    if (tid == 0) sh->ring_cnt = base + (uint32_t)nch;
+    __syncthreads();
 }
 
 __device__ __forceinline__ unsigned long long rcta_sum_u64(unsigned long long v, RSmem* sh) {
@@ -1743,10 +1780,131 @@ __device__ KeyStop cta_walk_keys(RSmem* sh, const uint32_t* counts, uint32_t khi
     return ks;
 }
 
+
+// index of occurrence number `need` (1-based) of the key in index order, streaming the row
+// through the ring; chunks already issued when it is found are drained, none is left in flight
+__device__ int tie_scan(RSmem* sh, const VerifyArgs& a, const RowGeo& g, int V, uint32_t key,
+                        unsigned long long need_total) {
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const uint32_t kb = key_bits(key);
+    const uint32_t kb2 = kb | (kb << 16);
+    const char* src = reinterpret_cast<const char*>(g.rowp - g.off);
+    const int nch = (g.nv + kRingCW - 1) / kRingCW;
+    const uint32_t base = sh->ring_cnt;
+    __syncthreads();
+    if (tid == 0) {
+        sh->sel[12] = -1;
+        for (int c = 0; c < nch && c < kRingS; ++c) {
+            const uint32_t slot = (base + c) % kRingS;
+            const int nvec = min(kRingCW, g.nv - c * kRingCW);
+            fence_proxy_async_smem();
+            mbar_arrive_expect_tx(&sh->ring_bar[slot], (uint32_t)nvec * 16u);
+            bulk_g2s(sh->ring[slot], src + (size_t)c * kRingCW * 16, (uint32_t)nvec * 16u, &sh->ring_bar[slot]);
+        }
+    }
+    __syncthreads();
+    int issued = nch < kRingS ? nch : kRingS;
+    unsigned long long run = 0;
+    int found = -1;
+    auto count_in = [&](uint4 x, int v) -> uint32_t {
+        x = row_vec(g, V, nullptr, v, x);
+        const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+        uint32_t c = 0;
+#pragma unroll
+        for (int h = 0; h < 8; ++h) {
+            const uint32_t eq = bf2_eq(xs[h >> 1], kb2) & ((h & 1) ? 0xFFFF0000u : 0x0000FFFFu);
+            const int e = 8 * v + h - g.off;
+            c += (eq && e >= 0 && e < V) ? 1u : 0u;
+        }
+        return c;
+    };
+    for (int c = 0; c < issued; ++c) {
+        const uint32_t k = base + c;
+        const uint32_t slot = k % kRingS;
+        if (!mbar_wait_bounded(&sh->ring_bar[slot], (k / kRingS) & 1u)) {
+            if (tid == 0) atomicOr(&a.ws->err, 1u);
+        }
+        if (found < 0) {
+            const int v0 = c * kRingCW;
+            const int nvec = min(kRingCW, g.nv - v0);
+            uint32_t cu[kRingCW / kRT];
+#pragma unroll
+            for (int u = 0; u < kRingCW / kRT; ++u) {
+                const int i = tid + u * kRT;
+                cu[u] = i < nvec ? count_in(sh->ring[slot][i], v0 + i) : 0u;
+                const uint32_t ws_ = warp_sum_u32(cu[u]);
+                if (lane == 0) sh->red32[u * kRW + wid] = ws_;
+            }
+            __syncthreads();
+            uint32_t tot[kRingCW / kRT];
+            uint32_t all = 0;
+#pragma unroll
+            for (int u = 0; u < kRingCW / kRT; ++u) {
+                tot[u] = 0;
+                for (int w = 0; w < kRW; ++w) tot[u] += sh->red32[u * kRW + w];
+                all += tot[u];
+            }
+            if (run + all >= need_total) {
+                // in this chunk: vectors are in index order u-major, then thread
+                uint32_t need = (uint32_t)(need_total - run);
+#pragma unroll
+                for (int u = 0; u < kRingCW / kRT; ++u) {
+                    if (need == 0u) break;
+                    if (need > tot[u]) {
+                        need -= tot[u];
+                        continue;
+                    }
+                    const uint32_t incl = warp_incl_u32(cu[u]);
+                    uint32_t wpre = 0;
+                    for (int w = 0; w < wid; ++w) wpre += sh->red32[u * kRW + w];
+                    const uint32_t lo = wpre + incl - cu[u];
+                    if (cu[u] > 0 && lo < need && lo + cu[u] >= need) {
+                        uint32_t k2 = need - lo;
+                        const int v = v0 + tid + u * kRT;
+                        const uint4 x = row_vec(g, V, nullptr, v, sh->ring[slot][tid + u * kRT]);
+                        const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+                        int e_found = -1;
+#pragma unroll
+                        for (int h = 0; h < 8; ++h) {
+                            const uint32_t eq = bf2_eq(xs[h >> 1], kb2) & ((h & 1) ? 0xFFFF0000u : 0x0000FFFFu);
+                            const int e = 8 * v + h - g.off;
+                            if (e_found < 0 && eq && e >= 0 && e < V && --k2 == 0u) e_found = e;
+                        }
+                        sh->sel[12] = e_found;
+                    }
+                    need = 0u;
+                }
+            }
+            run += all;
+        }
+        __syncthreads();  // the slot is consumed; sel[12] is visible
+        found = sh->sel[12];
+        const bool more = found < 0 && issued < nch;
+        if (tid == 0 && more) {
+            const int cn = issued;
+            const uint32_t slot2 = (base + cn) % kRingS;
+            const int nv2 = min(kRingCW, g.nv - cn * kRingCW);
+            fence_proxy_async_smem();
+            mbar_arrive_expect_tx(&sh->ring_bar[slot2], (uint32_t)nv2 * 16u);
+            bulk_g2s(sh->ring[slot2], src + (size_t)cn * kRingCW * 16, (uint32_t)nv2 * 16u, &sh->ring_bar[slot2]);
+        }
+        if (more) ++issued;
+    }
+    __syncthreads();
+    if (tid == 0) sh->ring_cnt = base + (uint32_t)issued;
+    __syncthreads();
+    return found;
+}
+
 __global__ void __launch_bounds__(kRT, 2) rows_kernel(VerifyArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     RSmem* sh = reinterpret_cast<RSmem*>(smem_raw);
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    if (tid == 0) {
+        for (int i = 0; i < kRingS; ++i) mbar_init(&sh->ring_bar[i], 1);
+        fence_mbar_init();
+        sh->ring_cnt = 0;
+    }
     build_plan(a, sh, kRWinK);
     const int ntask = total_tasks(a, sh);
     const int V = a.V;
@@ -1767,7 +1925,7 @@ __global__ void __launch_bounds__(kRT, 2) rows_kernel(VerifyArgs a) {
         // ---- pass 1: max (greedy rows: and the first index of the max) -------------------
         uint32_t tkey = 0;
         int tfirst = 0x7fffffff;
-        stream_row(g, V, [&](const uint4& x, int v) {
+        stream_row(sh, a, g, V, [&](const uint4& x, int v) {
             uint32_t mx = bf2_max(bf2_max(x.x, x.y), bf2_max(x.z, x.w));
             const uint32_t k0 = okey(mx & 0xFFFFu), k1 = okey(mx >> 16);
             const uint32_t vk = k0 > k1 ? k0 : k1;
@@ -1834,7 +1992,7 @@ __global__ void __launch_bounds__(kRT, 2) rows_kernel(VerifyArgs a) {
         const uint32_t taub = key_bits(tau);
         const uint32_t tau2 = taub | (taub << 16);
         uint32_t hs = 0, ls = 0, nel = 0;
-        stream_row(g, V, [&](const uint4& x, int v) {
+        stream_row(sh, a, g, V, [&](const uint4& x, int v) {
             const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
             nel += 8;
 #pragma unroll
@@ -1920,7 +2078,7 @@ __global__ void __launch_bounds__(kRT, 2) rows_kernel(VerifyArgs a) {
             }
             // the window overflowed: level-1 bins in another pass
             clear_bins(sh, kBins);
-            stream_row(g, V, [&](const uint4& x, int) {
+            stream_row(sh, a, g, V, [&](const uint4& x, int) {
                 const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
@@ -1963,7 +2121,7 @@ __global__ void __launch_bounds__(kRT, 2) rows_kernel(VerifyArgs a) {
         if (khi - klo + 1u > (uint32_t)kRKeyCap) {
             // level 2: sub-bins of bin b1 (exp again, only elements of the bin accumulate)
             clear_bins(sh, kSub);
-            stream_row(g, V, [&](const uint4& x, int v) {
+            stream_row(sh, a, g, V, [&](const uint4& x, int v) {
                 const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
@@ -2022,7 +2180,7 @@ __global__ void __launch_bounds__(kRT, 2) rows_kernel(VerifyArgs a) {
             __syncthreads();
             const uint32_t vlo = key_bits(bot), vhi = key_bits(top);
             const uint32_t vlo2 = vlo | (vlo << 16), vhi2 = vhi | (vhi << 16);
-            stream_row(g, V, [&](const uint4& x, int v) {
+            stream_row(sh, a, g, V, [&](const uint4& x, int v) {
                 const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
                 for (int q = 0; q < 4; ++q) {
@@ -2068,60 +2226,11 @@ __global__ void __launch_bounds__(kRT, 2) rows_kernel(VerifyArgs a) {
         }
 
         // ---- tie cut: occurrence number ntie of the boundary key in index order ------------
-        // warp w owns the contiguous vector range [w*nvw, (w+1)*nvw); lanes read consecutive
-        // vectors, so index order inside a warp is (group of 32 vectors, lane, half)
-        const uint32_t kb = key_bits(ks.key);
-        const uint32_t kb2 = kb | (kb << 16);
-        const int nvw = (((g.nv + kRW - 1) / kRW) + 31) & ~31;
-        const int v0 = min(wid * nvw, g.nv), v1 = min(v0 + nvw, g.nv);
-        const uint4* src = reinterpret_cast<const uint4*>(g.rowp - g.off);
-        auto count_vec = [&](int v) -> uint32_t {
-            const uint4 x = row_vec(g, V, src, v, __ldg(src + v));
-            const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
-            uint32_t c = 0;
-#pragma unroll
-            for (int h = 0; h < 8; ++h) {
-                const uint32_t eq = bf2_eq(xs[h >> 1], kb2) & ((h & 1) ? 0xFFFF0000u : 0x0000FFFFu);
-                const int e = 8 * v + h - g.off;
-                c += (eq && e >= 0 && e < V) ? 1u : 0u;
-            }
-            return c;
-        };
-        uint32_t wcount = 0;
-        for (int v = v0 + lane; v < v1; v += 32) wcount += count_vec(v);
-        wcount = warp_sum_u32(wcount);
-        __syncthreads();
-        if (lane == 0) sh->red32[wid] = wcount;
-        __syncthreads();
-        uint32_t before = 0;
-        for (int i = 0; i < wid; ++i) before += sh->red32[i];
-        if (before < ntie && before + wcount >= ntie) {
-            uint32_t need = (uint32_t)(ntie - before);
-            int tie = -1;
-            for (int gv = v0; gv < v1 && tie < 0; gv += 32) {
-                const int v = gv + lane;
-                const uint32_t c = v < v1 ? count_vec(v) : 0u;
-                const uint32_t incl = warp_incl_u32(c);
-                const uint32_t tot = __shfl_sync(0xffffffffu, incl, 31);
-                if (tot >= need) {
-                    const bool mine = c > 0 && incl - c < need && incl >= need;
-                    if (mine) {
-                        uint32_t k2 = need - (incl - c);
-                        const uint4 x = row_vec(g, V, src, v, __ldg(src + v));
-                        const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-                        for (int h = 0; h < 8; ++h) {
-                            const uint32_t eq = bf2_eq(xs[h >> 1], kb2) & ((h & 1) ? 0xFFFF0000u : 0x0000FFFFu);
-                            const int e = 8 * v + h - g.off;
-                            if (tie < 0 && eq && e >= 0 && e < V && --k2 == 0) tie = e;
-                        }
-                        put_desc(a, ti, m, ks.key, tie, skept, 0, 0u);
-                        if (tie < 0) atomicOr(&a.ws->err, 16u);
-                    }
-                    tie = 0;  // found by the owning lane: the warp stops
-                } else {
-                    need -= tot;
-                }
+        {
+            const int tie = tie_scan(sh, a, g, V, ks.key, ntie);
+            if (tid == 0) {
+                if (tie < 0) atomicOr(&a.ws->err, 16u);
+                put_desc(a, ti, m, ks.key, tie, skept, 0, 0u);
             }
         }
         PROF_END(ti.cat, 8);
