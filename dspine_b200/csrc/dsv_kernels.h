@@ -45,27 +45,9 @@ inline size_t verify_desc_offset(int B) {
 inline size_t verify_gmax_offset(int B) {
     return verify_desc_offset(B) + (size_t)B * 16 * 2 * sizeof(RowDesc);
 }
-// Per-row results of the streaming scan kernel, consumed by the select kernel and cleared by
-// the chain kernel (streaming path): fixed-point sum, level-1 bins, candidate windows.
-constexpr int kAreaBins = 24;
-constexpr int kAreaCS = 8;
-constexpr int kAreaWin = 32;
-struct TaskArea {
-    unsigned long long S;
-    unsigned long long mass[kAreaBins];
-    unsigned int cnt[kAreaBins];
-    unsigned int wcnt[kAreaCS];            // window entries per CTA (> kAreaWin: overflow)
-    unsigned int mkey;                     // ordered key of the row max
-    unsigned int pad;
-    unsigned int went[kAreaCS][kAreaWin];  // key << 16 | slice-local index
-};
 // [u64 x B x 16]: greedy rows' packed (max key << 32 | ~first index), reset after use
-inline size_t verify_area_offset(int B) {
-    return verify_gmax_offset(B) + (size_t)B * 16 * sizeof(unsigned long long);
-}
-// [TaskArea x B x 16 x 2]
 inline size_t verify_workspace_bytes(int B) {
-    return verify_area_offset(B) + (size_t)B * 16 * 2 * sizeof(TaskArea);
+    return verify_gmax_offset(B) + (size_t)B * 16 * sizeof(unsigned long long);
 }
 
 struct VerifyArgs {
@@ -107,12 +89,11 @@ struct VerifyArgs {
     TaskResult* res;
     RowDesc* desc;             // [B,16,2] row descriptors (streaming path)
     unsigned long long* gmax;  // [B,16] greedy rows: max key << 32 | (0xFFFFFFFF - first index)
-    TaskArea* area;            // [B,16,2] scan results of sampled rows
 };
 
 // launchers (return a dsv::Status)
 int launch_verify(const VerifyArgs& a, int dtype, cudaStream_t stream);
-// streaming path (bf16 rows, B <= 1024, V <= 163776): row kernel + chain kernel
+// streaming path (bf16 rows, B <= 1024, V <= 262144): rows kernel + chain kernel
 bool stream_supported(const VerifyArgs& a, int dtype);
 int launch_stream(VerifyArgs a, cudaStream_t stream);
 

@@ -3,21 +3,20 @@
 // Two kernels replace the reference's build_dspine_target_probs + chain rejection
 // (runtime/worker.py:440-508, sampling/rejection.py:12-153) for bf16 logits:
 //
-//   row_kernel    one row (a target row, or the draft row of a sampled request) per task;
-//                 a cluster of 8 CTAs holds the row in registers (one eighth per CTA, 16-byte
-//                 loads, the next task's slice prefetched into L2) and computes its descriptor:
-//                 max, exact 2^-40 fixed-point softmax sum, and the kept set of the joint
-//                 top-k / top-p filter as (boundary key, tie cut).  Passes:
-//                   P1  bf16x2 max                                   (every row)
-//                   P2  exp + fixed-point split, packed f32x2        (sampled rows)
-//                       + candidate window (top-k <= 64), or
-//                       + 32 y-bins with exact masses in thread-private shared accumulators
-//                   L2  31 sub-bins of the boundary bin (compacted list when it fits)
-//                   L3  per-key counts of the boundary sub-bin, walked with F(key)
-//                   tie the n-th occurrence of the boundary key in index order
-//   chain_kernel  one cluster per request: the capped chain from the descriptors (one logit
-//                 load per step), the residual (p - q)+ draw over target row a and draft row a,
-//                 the five outputs and, for the last request, the accept-compact.
+//   rows_kernel   one CTA per logit row (a target row, or the draft row of a sampled request);
+//                 rows are handed out by a global counter, most expensive first.  The CTA
+//                 streams its row through a shared-memory ring filled by cp.async.bulk copies
+//                 and computes the row's descriptor: max, exact 2^-40 fixed-point softmax sum,
+//                 and the kept set of the joint top-k / top-p filter as (boundary key, tie cut).
+//                   pass 1  bf16x2 max (greedy rows: and the first index of the max) -- HBM
+//                   pass 2  exp + fixed-point split with packed f32x2 FMA, and either the
+//                           candidate window (top-k <= 256) or 24 y-bins with exact masses in
+//                           thread-private shared accumulators                       -- L2
+//                   then, binned rows only: per-key counts of the boundary bin (sub-bins first
+//                   when it spans many keys) and the tie cut in index order
+//   chain_kernel  one 8-CTA cluster per request: the capped chain from the descriptors (one
+//                 logit load per step), the residual (p - q)+ draw over target row a and draft
+//                 row a, the five outputs and, for the last request, the accept-compact.
 //
 // Arithmetic is the canonical one of dsv_common.cuh (exp2c, fix, scale_floor), so the result
 // equals the CPU oracle bit for bit.  Bulk passes clamp y at -64 before the exponent trick:
@@ -37,18 +36,12 @@ namespace cg = cooperative_groups;
 namespace dsv {
 namespace st {
 
-constexpr int kCS = 8;           // CTAs per cluster: one row is split into 8 slices
-constexpr int kNT = 512;         // threads per CTA (one CTA per SM)
-constexpr int kNW = kNT / 32;    // warps per CTA
+constexpr int kCS = 8;           // chain kernel: CTAs per request cluster
+constexpr int kNT = 512;         // chain kernel: threads per CTA
+constexpr int kNW = kNT / 32;
 constexpr int kBins = 24;        // level-1 bins: min(rne(-0.75 y), 23)
 constexpr int kSub = 23;         // level-2 bins: rne(-16.5 y) - 22 b1 + 11, clamped to [0, 22]
-constexpr int kWinK = kCS * kNW; // top-k rows with k <= 128 select inside the candidate window
-constexpr int kWinCap = 128;     // window entries per CTA
-constexpr int kWinTotal = 512;   // window entries per row
-constexpr int kListCap = 4096;   // level-2 compaction list per CTA
-constexpr int kKeyChunk = 512;   // keys per level-3 histogram chunk
 constexpr int kMaxB = 1024;      // requests per launch handled by this path
-constexpr int kTaskCap = 64;     // decoded tasks of one cluster held in shared memory at a time
 
 enum Cat : int { kGreedy = 0, kKeepAll = 1, kWindow = 2, kBinned = 3 };
 
@@ -78,21 +71,7 @@ constexpr float kTwo23 = 8388608.0f;
         PROF_MARK(cat_, ph);                                                                \
         if (threadIdx.x == 0) atomicAdd(reinterpret_cast<unsigned long long*>(a.res) + (cat_) * 16 + 15, 1ull); \
     } while (0)
-#define PROF_SCAN(cat_, ph)                                                              \
-    do {                                                                                 \
-        if (threadIdx.x == 0) {                                                          \
-            const unsigned long long prof_n = globaltimer_ns();                          \
-            atomicAdd(reinterpret_cast<unsigned long long*>(a.res) + 64 + (cat_) * 16 + (ph), \
-                      prof_n - prof_t);                                                  \
-            if ((ph) == 0)                                                               \
-                atomicAdd(reinterpret_cast<unsigned long long*>(a.res) + 64 + (cat_) * 16 + 15, 1ull); \
-            prof_t = prof_n;                                                             \
-        }                                                                                \
-    } while (0)
 #else
-#define PROF_SCAN(cat_, ph) \
-    do {                    \
-    } while (0)
 #define PROF_START() \
     do {             \
     } while (0)
@@ -227,44 +206,9 @@ struct TaskInfo {
     int k;
 };
 
-struct Pub {                       // published at an exchange, read by the cluster (DSMEM)
-    uint32_t maxkey;               // CTA max key
-    int32_t first;                 // first index of the CTA max (greedy rows)
-    uint32_t wmax[kNW];            // warp max keys (window threshold)
-    uint32_t nwin;                 // window entries of this CTA (kWinCap + 1: overflow)
-    uint32_t flag;                 // per-exchange flag (tie: occurrences of the boundary key)
-    unsigned long long S;          // partial fixed-point sum
-    unsigned long long mass[kBins];
-    uint32_t cnt[kBins];
-};
-
-struct RowSmem {
-    Pub pub[2];
-    uint32_t win[kWinCap];         // window entries: key << 16 | slice-local index
-    uint32_t khist[kKeyChunk];     // level-3 key counts of this CTA
-    uint32_t bcnt[kBins];          // local bin counts (atomics)
-    unsigned long long red64[kNW];
-    uint32_t red32[kNW * 2];
-    int32_t task[8];               // decoded task (broadcast)
-    float taskf[4];
-    int32_t sel[16];               // selection state (broadcast inside the CTA)
-    unsigned long long self64[8];
-    uint32_t nlist;
-    int32_t first_min;
-    alignas(8) uint64_t stage_bar;  // mbarrier of the staged next slice
-    alignas(8) uint64_t stage_bar2[2];  // scan kernel: mbarriers of its two staging buffers
-    uint16_t pre[3][kMaxB + 1];    // task prefix per group (binned, keep-all/window, greedy)
-    TaskInfo tasks[kTaskCap];      // this cluster's next tasks, decoded once
-    uint8_t req[kMaxB];            // per request: cat | cap << 3
-    alignas(16) uint2 acc[kBins * kNT];  // thread-private bin accumulators / gather area
-    alignas(16) uint32_t list[kListCap]; // level-2 compaction list: bits << 16 | local index
-};
-// the accumulator region is cleared with 16-byte stores
-static_assert(offsetof(RowSmem, acc) % 16 == 0, "acc must be 16-byte aligned");
-
 __device__ __forceinline__ int clamp_cap(int c) { return c < 1 ? 1 : (c > kT ? kT : c); }
 
-__device__ int request_cat(const VerifyArgs& a, int b, float& c_out, int wink = kWinK) {
+__device__ int request_cat(const VerifyArgs& a, int b, float& c_out, int wink) {
     const float T = a.temperature[b];
     const int k = a.top_k[b];
     const float c = log2e_over(T);
@@ -277,7 +221,7 @@ __device__ int request_cat(const VerifyArgs& a, int b, float& c_out, int wink = 
 
 // every CTA builds the same task table: binned rows first, then keep-all/window, then greedy
 template <typename Sm>
-__device__ void build_plan(const VerifyArgs& a, Sm* sh, int wink = kWinK) {
+__device__ void build_plan(const VerifyArgs& a, Sm* sh, int wink) {
     const int tid = threadIdx.x;
     for (int b = tid; b < a.B; b += blockDim.x) {
         float c;
@@ -351,83 +295,6 @@ __device__ TaskInfo decode_task(const VerifyArgs& a, const Sm* sh, int t) {
     return ti;
 }
 
-// geometry of slice q of a row: elements [e0, e1), vector v covers [e0 - off + 8v, +8)
-struct Slice {
-    const uint16_t* rowp;
-    int e0, e1, off, nv;
-};
-
-__device__ __forceinline__ Slice slice_of(const VerifyArgs& a, const TaskInfo& ti, int q, int L) {
-    Slice sl;
-    const uint16_t* base = reinterpret_cast<const uint16_t*>(ti.kind == 0 ? a.tgt : a.drf);
-    sl.rowp = base + (ti.row < 0 ? 0 : ti.row) * a.stride;
-    sl.e0 = min(q * L, a.V);
-    sl.e1 = min(sl.e0 + L, a.V);
-    sl.off = (int)((reinterpret_cast<uintptr_t>(sl.rowp) & 15u) >> 1);
-    sl.nv = (ti.row < 0 || sl.e1 <= sl.e0) ? 0 : (sl.e1 - sl.e0 + sl.off + 7) >> 3;
-    return sl;
-}
-
-// Bulk-copy the 16-byte vectors of a slice into the staging buffer (thread 0; completion on
-// the stage mbarrier).  Vector v of the slice lands at stage[v].
-__device__ __forceinline__ void stage_issue(const Slice& sl, uint4* stage, uint64_t* bar) {
-    const uint32_t bytes = (uint32_t)sl.nv * 16u;
-    fence_proxy_async_smem();  // earlier generic reads of the buffer precede the async writes
-    mbar_arrive_expect_tx(bar, bytes);
-    if (bytes == 0) return;
-    const char* src = reinterpret_cast<const char*>(sl.rowp + sl.e0 - sl.off);
-    char* dst = reinterpret_cast<char*>(stage);
-    for (uint32_t off = 0; off < bytes; off += 32768u)
-        bulk_g2s(dst + off, src + off, min(32768u, bytes - off), bar);
-}
-
-// staged slice -> registers (vector j*kNT + tid), with the halves outside [e0, e1) set to -inf
-template <int NVT>
-__device__ __forceinline__ void stage_to_regs(const Slice& sl, const uint4* stage, uint4 (&w)[NVT]) {
-    const int tid = threadIdx.x;
-#pragma unroll
-    for (int j = 0; j < NVT; ++j) {
-        const int v = j * kNT + tid;
-        if (v < sl.nv) w[j] = stage[v];
-        else w[j] = make_uint4(kFill, kFill, kFill, kFill);
-    }
-#pragma unroll
-    for (int j = 0; j < NVT; ++j) {
-        const int v = j * kNT + tid;
-        if (v < sl.nv && (v == 0 || v == sl.nv - 1)) {
-            uint32_t* u = reinterpret_cast<uint32_t*>(&w[j]);
-#pragma unroll
-            for (int h = 0; h < 8; ++h) {
-                const int e = sl.e0 - sl.off + 8 * v + h;
-                if (e < sl.e0 || e >= sl.e1) {
-                    const uint32_t mask = (h & 1) ? 0xFFFF0000u : 0x0000FFFFu;
-                    u[h >> 1] = (u[h >> 1] & ~mask) | (kFill & mask);
-                }
-            }
-        }
-    }
-}
-
-// element index (within the row) of half h of register vector j of this thread
-__device__ __forceinline__ int elem_index(const Slice& sl, int j, int h) {
-    return sl.e0 - sl.off + 8 * (j * kNT + (int)threadIdx.x) + h;
-}
-__device__ __forceinline__ bool elem_valid(const Slice& sl, int e) { return e >= sl.e0 && e < sl.e1; }
-
-// ---- CTA reductions ---------------------------------------------------------------------
-
-__device__ __forceinline__ unsigned long long cta_sum_u64(unsigned long long v, RowSmem* sh) {
-    v = warp_sum_u64(v);
-    const int w = threadIdx.x >> 5;
-    __syncthreads();
-    if ((threadIdx.x & 31) == 0) sh->red64[w] = v;
-    __syncthreads();
-    unsigned long long s = 0;
-#pragma unroll
-    for (int i = 0; i < kNW; ++i) s += sh->red64[i];
-    return s;
-}
-
 // ---------------------------------------------------------------------------------------
 // selection walk over groups in rank order (bins, sub-bins): first group where the count
 // reaches k or the mass passes thr
@@ -470,24 +337,6 @@ __device__ Walk walk_groups(const uint32_t* cnt, const unsigned long long* mass,
     return wk;
 }
 
-// ---------------------------------------------------------------------------------------
-// the row kernel
-
-template <int NVT>
-struct RowCtx {
-    const VerifyArgs* a;
-    RowSmem* sh;
-    cg::cluster_group* cl;
-    int rank;
-    int L;
-    unsigned ex;   // exchange counter (buffer parity)
-};
-
-template <int NVT>
-__device__ __forceinline__ Pub* remote_pub(RowCtx<NVT>& cx, int q, unsigned ex) {
-    return cx.cl->map_shared_rank(&cx.sh->pub[ex & 1], q);
-}
-
 // write a row descriptor
 __device__ __forceinline__ void put_desc(const VerifyArgs& a, const TaskInfo& ti, float m,
                                          uint32_t kstar, int tie, unsigned long long skept,
@@ -513,47 +362,6 @@ struct KeyStop {
     uint32_t count;            // elements with this key
     unsigned long long F;      // fix value of one element with this key
 };
-
-__device__ KeyStop walk_keys(const uint32_t* counts, uint32_t khi, int n, float m, float c,
-                             unsigned long long cnt0, unsigned long long mass0, long long k,
-                             long long thr) {
-    const int lane = threadIdx.x & 31;
-    KeyStop ks;
-    ks.found = 0;
-    ks.cnt = cnt0;
-    ks.mass = mass0;
-    for (int base = 0; base < n; base += 32) {
-        const int i = base + lane;                 // i-th key from the top
-        const uint32_t key = khi - (uint32_t)i;
-        const uint32_t cc = i < n ? counts[i] : 0u;
-        unsigned long long F = 0;
-        if (cc) F = fix_of_y(y_clamped(bf(key_bits(key)), m, c));
-        const unsigned long long mm = F * cc;
-        unsigned long long ci = cc, mi = mm;
-#pragma unroll
-        for (int o = 1; o < 32; o <<= 1) {
-            const unsigned long long a = __shfl_up_sync(0xffffffffu, ci, o);
-            const unsigned long long b = __shfl_up_sync(0xffffffffu, mi, o);
-            if (lane >= o) { ci += a; mi += b; }
-        }
-        const unsigned long long cb = ks.cnt + ci - cc, mb = ks.mass + mi - mm;
-        const bool stop = cc > 0 && ((long long)(cb + cc) >= k || (long long)(mb + mm) > thr);
-        const uint32_t bal = __ballot_sync(0xffffffffu, stop);
-        if (bal) {
-            const int g = __ffs(bal) - 1;
-            ks.found = 1;
-            ks.key = __shfl_sync(0xffffffffu, key, g);
-            ks.cnt = __shfl_sync(0xffffffffu, cb, g);
-            ks.mass = __shfl_sync(0xffffffffu, mb, g);
-            ks.count = __shfl_sync(0xffffffffu, cc, g);
-            ks.F = __shfl_sync(0xffffffffu, F, g);
-            return ks;
-        }
-        ks.cnt += __shfl_sync(0xffffffffu, ci, 31);
-        ks.mass += __shfl_sync(0xffffffffu, mi, 31);
-    }
-    return ks;
-}
 
 // composite bin index of a key (level 1 and level 2); over keys of values in [-inf, m] it is
 // non-increasing in the key (y is non-decreasing in the value and both bins round -0.75 y)
@@ -598,923 +406,6 @@ __device__ void key_range(int target, uint32_t kmin, uint32_t kmax, float m, flo
     else
         klo = kmin;
 }
-
-// Rare follow-up pass (window overflow -> level-1 bins of every valid element; level-2 sub-bins
-// of bin b1 that do not fit the compaction list): re-reads the slice from global memory (L2-hot)
-// so that the row slice held in registers by the caller is not touched.  Accumulates into the
-// thread-private columns acc[slot * kNT + tid] and the slot counts.
-__device__ __noinline__ void reread_bins(const Slice sl, float m, float c, int sub, int b1,
-                                         RowSmem* sh) {
-    const int tid = threadIdx.x;
-    const float2 nm = make_float2(-m, -m), c2 = make_float2(c, c);
-    const uint4* src = reinterpret_cast<const uint4*>(sl.rowp + sl.e0 - sl.off);
-#pragma unroll 1
-    for (int v = tid; v < sl.nv; v += kNT) {
-        const uint4 x = __ldg(src + v);
-        const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            const Pair pr = exp_pair(xs[q], nm, c2);
-#pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const float yc = h ? pr.yc.y : pr.yc.x;
-                const int e = sl.e0 - sl.off + 8 * v + 2 * q + h;
-                if (!elem_valid(sl, e)) continue;
-                const int bb = bin1_of(yc);
-                int slot = bb;
-                if (sub) {
-                    if (bb != b1) continue;
-                    slot = bin2_of(yc, b1);
-                }
-                uint2* pa = &sh->acc[slot * kNT + tid];
-                uint2 va = *pa;
-                va.x += (h ? pr.h1 : pr.h0) - 0x4B000000u;
-                va.y += (h ? pr.l1 : pr.l0) - 0x4B400000u;
-                *pa = va;
-                atomicAdd(&sh->bcnt[slot], 1u);
-            }
-        }
-    }
-}
-
-
-template <int NVT>
-__device__ __forceinline__ void load_slice(const Slice& sl, uint4 (&w)[NVT]) {
-    const int tid = threadIdx.x;
-    const uint4* src = reinterpret_cast<const uint4*>(sl.rowp + sl.e0 - sl.off);
-#pragma unroll
-    for (int j = 0; j < NVT; ++j) {
-        const int v = j * kNT + tid;
-        if (v < sl.nv) w[j] = __ldg(src + v);
-        else w[j] = make_uint4(kFill, kFill, kFill, kFill);
-    }
-    // mask the halves of the first and last vector that lie outside [e0, e1)
-#pragma unroll
-    for (int j = 0; j < NVT; ++j) {
-        const int v = j * kNT + tid;
-        if (v < sl.nv && (v == 0 || v == sl.nv - 1)) {
-            uint32_t* u = reinterpret_cast<uint32_t*>(&w[j]);
-#pragma unroll
-            for (int h = 0; h < 8; ++h) {
-                const int e = sl.e0 - sl.off + 8 * v + h;
-                if (e < sl.e0 || e >= sl.e1) {
-                    const uint32_t mask = (h & 1) ? 0xFFFF0000u : 0x0000FFFFu;
-                    u[h >> 1] = (u[h >> 1] & ~mask) | (kFill & mask);
-                }
-            }
-        }
-    }
-}
-
-// the leader's exact resolution inside the candidate window, from the scan results: gather
-// the entries of all CTAs, rank them by (key desc, index asc), walk the exact masses
-__device__ void window_resolve_area(const VerifyArgs& a, const TaskInfo& ti, const TaskArea* ar,
-                                    RowSmem* sh, uint32_t win_total, int L, float m, long long kk,
-                                    long long thr) {
-    const int tid = threadIdx.x, lane = tid & 31;
-    uint2* g = sh->acc;  // [0, kWinTotal): gathered, [kWinTotal, 2 kWinTotal): sorted
-    __syncthreads();
-    for (int f = tid; f < (int)win_total; f += kNT) {
-        int q = 0, off = 0;
-        while (q + 1 < kCS && off + (int)ar->wcnt[q] <= f) {
-            off += (int)ar->wcnt[q];
-            ++q;
-        }
-        const uint32_t e = ar->went[q][f - off];
-        const int qe0 = min(q * L, a.V);
-        g[f] = make_uint2(e >> 16, (uint32_t)(qe0 + (int)(e & 0xFFFFu)));
-    }
-    __syncthreads();
-    const int n = (int)win_total;
-    for (int i = tid; i < n; i += kNT) {
-        const uint2 me = g[i];
-        int r = 0;
-        for (int j = 0; j < n; ++j) {
-            const uint2 o = g[j];
-            r += (o.x > me.x) || (o.x == me.x && o.y < me.y);
-        }
-        g[kWinTotal + r] = me;
-    }
-    __syncthreads();
-    if (tid < 32) {
-        // first rank that is not kept: r >= k, or mass ranked ahead > thr (rank 0 always kept)
-        unsigned long long A = 0;
-        int nsel = -1;
-        for (int base = 0; base < n && nsel < 0; base += 32) {
-            const int r = base + lane;
-            unsigned long long F = 0;
-            if (r < n) F = fix_of_y(y_clamped(bf(key_bits(g[kWinTotal + r].x)), m, ti.c));
-            unsigned long long inc = F;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const unsigned long long v = __shfl_up_sync(0xffffffffu, inc, o);
-                if (lane >= o) inc += v;
-            }
-            const unsigned long long Ar = A + inc - F;
-            const bool out = r < n && r > 0 && (r >= kk || (long long)Ar > thr);
-            const uint32_t bal = __ballot_sync(0xffffffffu, out);
-            if (bal) nsel = base + __ffs(bal) - 1;
-            A += __shfl_sync(0xffffffffu, inc, 31);
-        }
-        if (nsel < 0) nsel = n < kk ? n : (int)kk;
-        unsigned long long sk = 0;
-        for (int r = lane; r < nsel; r += 32)
-            sk += fix_of_y(y_clamped(bf(key_bits(g[kWinTotal + r].x)), m, ti.c));
-        sk = warp_sum_u64(sk);
-        if (lane == 0) {
-            const uint2 last = g[kWinTotal + nsel - 1];
-            put_desc(a, ti, m, last.x, (int)last.y, sk, 0, 0u);
-        }
-    }
-}
-
-
-__device__ __forceinline__ void cluster_arrive() {
-    asm volatile("barrier.cluster.arrive.release;" ::: "memory");
-}
-__device__ __forceinline__ void cluster_wait() {
-    asm volatile("barrier.cluster.wait.acquire;" ::: "memory");
-}
-
-static_assert(kBins == kAreaBins && kCS == kAreaCS, "scan area layout");
-
-// Scan kernel: max and exact exp pass of every row, pipelined across tasks.  While the row of
-// task A sits in registers, P1 of the next task B runs from the staging buffer and its max is
-// exchanged across the cluster (split arrive/wait) during P2 of A, so the exchange latency is
-// hidden.  Results go to the row's TaskArea (sum, level-1 bins, candidate window) and, for
-// greedy rows, to the packed argmax; the select kernel finishes the kept sets.
-template <int NVT>
-__global__ void __launch_bounds__(kNT, 1) scan_kernel(VerifyArgs a) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    RowSmem* sh = reinterpret_cast<RowSmem*>(smem_raw);
-    cg::cluster_group cluster = cg::this_cluster();
-    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-    RowCtx<NVT> cx;
-    cx.a = &a;
-    cx.sh = sh;
-    cx.cl = &cluster;
-    cx.rank = (int)cluster.block_rank();
-    cx.L = a.slice;
-    cx.ex = 0;
-    const int cid = blockIdx.x / kCS;
-
-    build_plan(a, sh);
-    const int ntask = total_tasks(a, sh);
-    const int nmine = ntask > cid ? (ntask - cid + a.num_clusters - 1) / a.num_clusters : 0;
-    // two staging buffers: task i+1 is copied into one while task i's slice (in the other) is
-    // read by its P1 and then moved to the registers
-    uint4* stage_base = reinterpret_cast<uint4*>(smem_raw + ((sizeof(RowSmem) + 15) & ~(size_t)15));
-    if (tid == 0) {
-        mbar_init(&sh->stage_bar2[0], 1);
-        mbar_init(&sh->stage_bar2[1], 1);
-        fence_mbar_init();
-        sh->nlist = 0;
-    }
-    __syncthreads();
-    uint32_t stage_ph0 = 0, stage_ph1 = 0;
-    if (tid == 0 && nmine > 0)
-        stage_issue(slice_of(a, decode_task(a, sh, cid), cx.rank, cx.L), stage_base, &sh->stage_bar2[0]);
-
-    uint4 w[NVT];
-    bool haveA = false;
-    TaskInfo tA;
-    Slice sA;
-    float mA = 0.0f;
-    uint32_t tauA = 0;
-    tA.b = tA.s = tA.kind = tA.cat = tA.cap = tA.k = 0;
-    tA.row = -1;
-    tA.T = tA.p = tA.c = 0.0f;
-    sA.rowp = nullptr;
-    sA.e0 = sA.e1 = sA.off = sA.nv = 0;
-
-    for (int it = 0; it <= nmine; ++it) {
-        PROF_START();
-        const bool haveB = it < nmine;
-        TaskInfo tB = tA;
-        Slice sB = sA;
-        bool sampledB = false;
-        // ---- P1 of task B from the staging buffer; sampled rows start the max exchange ------
-        if (haveB) {
-            if (it % kTaskCap == 0) {
-                __syncthreads();
-                for (int i = tid; i < kTaskCap && it + i < nmine; i += kNT)
-                    sh->tasks[i] = decode_task(a, sh, cid + (it + i) * a.num_clusters);
-                __syncthreads();
-            }
-            tB = sh->tasks[it % kTaskCap];
-            sB = slice_of(a, tB, cx.rank, cx.L);
-            sampledB = tB.cat != kGreedy;
-            if (tB.row < 0 && tid == 0 && cx.rank == 0) atomicOr(&a.ws->err, 2u);
-            // the next task's slice goes into the other buffer (its previous task has moved on)
-            if (tid == 0 && it + 1 < nmine) {
-                const TaskInfo tn = ((it + 1) % kTaskCap != 0) ? sh->tasks[(it + 1) % kTaskCap]
-                                                               : decode_task(a, sh, cid + (it + 1) * a.num_clusters);
-                stage_issue(slice_of(a, tn, cx.rank, cx.L), stage_base + ((it + 1) & 1) * NVT * kNT,
-                            &sh->stage_bar2[(it + 1) & 1]);
-            }
-            uint4* stage = stage_base + (it & 1) * NVT * kNT;
-            const uint32_t ph = (it & 1) ? stage_ph1 : stage_ph0;
-            if (!mbar_wait_bounded(&sh->stage_bar2[it & 1], ph)) {
-                if (tid == 0) atomicOr(&a.ws->err, 1u);
-            }
-            if (it & 1) stage_ph1 ^= 1u; else stage_ph0 ^= 1u;
-            PROF_SCAN(tB.cat, 0);
-            uint32_t mx = kFill;
-#pragma unroll
-            for (int j = 0; j < NVT; ++j) {
-                const int v = j * kNT + tid;
-                if (v < sB.nv) {
-                    uint4 x = stage[v];
-                    if (v == 0 || v == sB.nv - 1) {
-                        uint32_t* u = reinterpret_cast<uint32_t*>(&x);
-#pragma unroll
-                        for (int h = 0; h < 8; ++h) {
-                            const int e = sB.e0 - sB.off + 8 * v + h;
-                            if (e < sB.e0 || e >= sB.e1) {
-                                const uint32_t msk = (h & 1) ? 0xFFFF0000u : 0x0000FFFFu;
-                                u[h >> 1] = (u[h >> 1] & ~msk) | (kFill & msk);
-                            }
-                        }
-                    }
-                    mx = bf2_max(mx, x.x);
-                    mx = bf2_max(mx, x.y);
-                    mx = bf2_max(mx, x.z);
-                    mx = bf2_max(mx, x.w);
-                }
-            }
-            const uint32_t k0 = okey(mx & 0xFFFFu), k1 = okey(mx >> 16);
-            const uint32_t tkey = k0 > k1 ? k0 : k1;
-            const uint32_t wkey = __reduce_max_sync(0xffffffffu, tkey);
-            if (lane == 0) sh->red32[wid] = wkey;
-            if (tid == 0) sh->first_min = 0x7fffffff;
-            __syncthreads();
-            uint32_t ckey = 0;
-#pragma unroll
-            for (int i = 0; i < kNW; ++i) ckey = max(ckey, sh->red32[i]);
-            if (!sampledB) {
-                // greedy row: the first index of the CTA max, combined across the slices by one
-                // global atomicMax on (key << 32 | ~index); no cluster exchange
-                if (tkey == ckey) {
-                    const uint32_t cb = key_bits(ckey);
-                    const uint32_t c2 = cb | (cb << 16);
-                    int best = 0x7fffffff;
-                    for (int j = 0; j < NVT && best == 0x7fffffff; ++j) {
-                        const int v = j * kNT + tid;
-                        if (v >= sB.nv) break;
-                        const uint4 x = stage[v];
-                        const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-                        for (int h = 0; h < 8; ++h) {
-                            const uint32_t eq = bf2_eq(xs[h >> 1], c2) & ((h & 1) ? 0xFFFF0000u : 0x0000FFFFu);
-                            const int e = sB.e0 - sB.off + 8 * v + h;
-                            if (eq && best == 0x7fffffff && e >= sB.e0 && e < sB.e1) best = e;
-                        }
-                    }
-                    if (best != 0x7fffffff) atomicMin(&sh->first_min, best);
-                }
-                __syncthreads();
-                if (tid == 0 && sh->first_min != 0x7fffffff) {
-                    const unsigned long long packed =
-                        ((unsigned long long)ckey << 32) | (0xFFFFFFFFull - (unsigned)sh->first_min);
-                    atomicMax(&a.gmax[tB.b * kT + tB.s], packed);
-                }
-            } else {
-                Pub& pb = sh->pub[cx.ex & 1];
-                if (tid == 0) pb.maxkey = ckey;
-                if (tid < kNW) pb.wmax[tid] = sh->red32[tid];
-                cluster_arrive();
-            }
-        }
-
-        if (haveB) PROF_SCAN(tB.cat, 1);
-        // ---- P2 of task A from the registers (overlaps the exchange of B) -------------------
-        if (haveA) {
-            TaskArea* ar = &a.area[(tA.b * kT + tA.s) * 2 + tA.kind];
-            const int cat = tA.cat;
-            const float2 nm = make_float2(-mA, -mA), c2 = make_float2(tA.c, tA.c);
-            if (cat == kBinned) {
-                __syncthreads();
-                uint4* az = reinterpret_cast<uint4*>(sh->acc);
-                for (int i = tid; i < kBins * kNT / 2; i += kNT) az[i] = make_uint4(0, 0, 0, 0);
-                if (tid < kBins) sh->bcnt[tid] = 0;
-                __syncthreads();
-            }
-            uint32_t hs = 0, ls = 0;
-#pragma unroll
-            for (int j = 0; j < NVT; ++j) {
-                const uint32_t* u = reinterpret_cast<const uint32_t*>(&w[j]);
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const Pair pr = exp_pair(u[q], nm, c2);
-                    hs += pr.h0 + pr.h1;
-                    ls += pr.l0 + pr.l1;
-                    if (cat == kBinned) {
-                        const int bx = bin1_of(pr.yc.x), by = bin1_of(pr.yc.y);
-                        uint2* px = &sh->acc[bx * kNT + tid];
-                        uint2 vx = *px;
-                        vx.x += pr.h0 - 0x4B000000u;
-                        vx.y += pr.l0 - 0x4B400000u;
-                        *px = vx;
-                        uint2* py = &sh->acc[by * kNT + tid];
-                        uint2 vy = *py;
-                        vy.x += pr.h1 - 0x4B000000u;
-                        vy.y += pr.l1 - 0x4B400000u;
-                        *py = vy;
-                        atomicAdd(&sh->bcnt[bx], 1u);
-                        atomicAdd(&sh->bcnt[by], 1u);
-                    }
-                }
-            }
-            if (cat == kWindow) {
-                const uint32_t taub = key_bits(tauA);
-                const uint32_t tau2 = taub | (taub << 16);
-#pragma unroll
-                for (int j = 0; j < NVT; ++j) {
-                    const uint32_t* u = reinterpret_cast<const uint32_t*>(&w[j]);
-#pragma unroll
-                    for (int q = 0; q < 4; ++q) {
-                        const uint32_t ge = bf2_ge(u[q], tau2);
-                        if (ge) {
-#pragma unroll
-                            for (int h = 0; h < 2; ++h) {
-                                const int e = elem_index(sA, j, 2 * q + h);
-                                if ((ge & (h ? 0xFFFF0000u : 0x0000FFFFu)) && elem_valid(sA, e)) {
-                                    const uint32_t bits = h ? (u[q] >> 16) : (u[q] & 0xFFFFu);
-                                    const uint32_t pos = atomicAdd(&sh->nlist, 1u);
-                                    if (pos < kWinCap) sh->win[pos] = (okey(bits) << 16) | (uint32_t)(e - sA.e0);
-                                }
-                            }
-                        }
-                    }
-                }
-            }
-            const uint32_t nel = (uint32_t)NVT * 8u;
-            const uint32_t hi_t = hs - nel * 0x4B000000u;
-            const int32_t lo_t = (int32_t)(ls - nel * 0x4B400000u);
-            const unsigned long long s_cta =
-                cta_sum_u64((unsigned long long)((long long)hi_t * 8388608 + lo_t), sh);
-            if (tid == 0) atomicAdd(&ar->S, s_cta);
-            if (cat == kWindow) {
-                const uint32_t nw = sh->nlist;
-                for (int i = tid; i < (int)min(nw, (uint32_t)kAreaWin); i += kNT)
-                    ar->went[cx.rank][i] = sh->win[i];
-                if (tid == 0) ar->wcnt[cx.rank] = nw;
-                __syncthreads();
-                if (tid == 0) sh->nlist = 0;  // the next window row appends after later barriers
-            }
-            if (cat == kBinned) {
-                const uint32_t nfill = nel * kNT - (uint32_t)(sA.e1 > sA.e0 ? sA.e1 - sA.e0 : 0);
-                for (int bin = wid; bin < kBins; bin += kNW) {
-                    long long sm = 0;
-                    for (int i = lane; i < kNT; i += 32) {
-                        const uint2 v = sh->acc[bin * kNT + i];
-                        sm += (long long)v.x * 8388608 + (int32_t)v.y;
-                    }
-                    sm = (long long)warp_sum_u64((unsigned long long)sm);
-                    if (lane == 0) {
-                        if (sm) atomicAdd(&ar->mass[bin], (unsigned long long)sm);
-                        // fill slots (outside the slice) are -inf and fall into the last bin
-                        const uint32_t cnt = sh->bcnt[bin] - (bin == kBins - 1 ? nfill : 0u);
-                        if (cnt) atomicAdd(&ar->cnt[bin], cnt);
-                    }
-                }
-            }
-        }
-
-        if (haveA) PROF_SCAN(tA.cat, 2);
-        // ---- finish B's exchange, then move B into the registers ----------------------------
-        if (haveB) {
-            uint32_t tauB = 0;
-            uint32_t mkeyB = 0;
-            if (sampledB) {
-                cluster_wait();
-                const unsigned exB = cx.ex++;
-                if (tid < 32) {
-                    uint32_t k = lane < kCS ? remote_pub(cx, lane, exB)->maxkey : 0u;
-                    const uint32_t mk = __reduce_max_sync(0xffffffffu, k);
-                    uint32_t cand = 0;
-                    if (tB.cat == kWindow) {
-                        const long long kk = tB.k < a.V ? (long long)tB.k : (long long)a.V;
-                        // tau = the k-th largest of the cluster's kCS * kNW warp maxima: at least
-                        // k elements are >= tau (one per warp whose maximum is >= tau)
-                        constexpr int R = kCS * kNW / 32;
-                        uint32_t x[R];
-#pragma unroll
-                        for (int r = 0; r < R; ++r) {
-                            const int g = lane + 32 * r;
-                            x[r] = remote_pub(cx, g / kNW, exB)->wmax[g % kNW];
-                        }
-                        int ge[R];
-#pragma unroll
-                        for (int r = 0; r < R; ++r) ge[r] = 0;
-                        for (int i = 0; i < 32; ++i) {
-#pragma unroll
-                            for (int r2 = 0; r2 < R; ++r2) {
-                                const uint32_t y = __shfl_sync(0xffffffffu, x[r2], i);
-#pragma unroll
-                                for (int r = 0; r < R; ++r) ge[r] += (y >= x[r]);
-                            }
-                        }
-#pragma unroll
-                        for (int r = 0; r < R; ++r)
-                            if (ge[r] >= kk && x[r] > cand) cand = x[r];
-                        cand = __reduce_max_sync(0xffffffffu, cand);
-                    }
-                    if (lane == 0) {
-                        sh->sel[10] = (int)mk;
-                        sh->sel[0] = (int)cand;
-                        if (cx.rank == 0) a.area[(tB.b * kT + tB.s) * 2 + tB.kind].mkey = mk;
-                    }
-                }
-            }
-            __syncthreads();  // P2 of A is done with the registers, P1 of B with the buffer
-            PROF_SCAN(tB.cat, 3);
-            if (sampledB) {
-                mkeyB = (uint32_t)sh->sel[10];
-                tauB = (uint32_t)sh->sel[0];
-                stage_to_regs<NVT>(sB, stage_base + (it & 1) * NVT * kNT, w);
-            }
-            __syncthreads();  // B's buffer is free for the task after next
-            PROF_SCAN(tB.cat, 4);
-            haveA = sampledB;
-            tA = tB;
-            sA = sB;
-            mA = bf(key_bits(mkeyB));
-            tauA = tauB;
-        } else {
-            haveA = false;
-        }
-    }
-    // no CTA may leave while a peer can still read its shared memory
-    cluster_barrier();
-}
-
-// Select kernel: the kept sets of sampled rows from the scan results.  Keep-all and window
-// rows need no row data; binned rows reload their slice and walk bins, keys and the tie.
-template <int NVT>
-__global__ void __launch_bounds__(kNT, 1) select_kernel(VerifyArgs a) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    RowSmem* sh = reinterpret_cast<RowSmem*>(smem_raw);
-    cg::cluster_group cluster = cg::this_cluster();
-    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-    RowCtx<NVT> cx;
-    cx.a = &a;
-    cx.sh = sh;
-    cx.cl = &cluster;
-    cx.rank = (int)cluster.block_rank();
-    cx.L = a.slice;
-    cx.ex = 0;
-    const int cid = blockIdx.x / kCS;
-
-    build_plan(a, sh);
-    const int ntask = total_tasks(a, sh);
-
-    // sampled rows only (binned first, then keep-all / window), in the scan kernel's order
-    uint4 w[NVT];
-    const int nsampled = (int)sh->pre[0][a.B] + (int)sh->pre[1][a.B];
-    (void)ntask;
-    const int nmine = nsampled > cid ? (nsampled - cid + a.num_clusters - 1) / a.num_clusters : 0;
-    for (int it = 0; it < nmine; ++it) {
-        if (it % kTaskCap == 0) {
-            __syncthreads();
-            for (int i = tid; i < kTaskCap && it + i < nmine; i += kNT)
-                sh->tasks[i] = decode_task(a, sh, cid + (it + i) * a.num_clusters);
-            __syncthreads();
-        }
-        PROF_START();
-        const TaskInfo ti = sh->tasks[it % kTaskCap];
-        const int leader = it % kCS;
-        const bool lead = cx.rank == leader;
-        const Slice sl = slice_of(a, ti, cx.rank, cx.L);
-        const TaskArea* ar = &a.area[(ti.b * kT + ti.s) * 2 + ti.kind];
-        const uint32_t mkey = ar->mkey;
-        const float m = bf(key_bits(mkey));
-        const unsigned long long S = ar->S;
-        const long long thr = (ti.p < 1.0f) ? scale_floor(ti.p, S) : 0x7fffffffffffffffll;
-        int cat = ti.cat;
-        const long long kk = ti.k < a.V ? (long long)ti.k : (long long)a.V;
-        const float2 nm = make_float2(-m, -m), c2 = make_float2(ti.c, ti.c);
-        const uint32_t nel = (uint32_t)NVT * 8u;
-        (void)nm;
-        (void)c2;
-        (void)nel;
-        if (cat == kKeepAll) {
-            if (lead && tid == 0) put_desc(a, ti, m, 0u, 0x7fffffff, S, 0, 0u);
-            PROF_END(ti.cat, 4);
-            continue;
-        }
-        if (cat == kWindow) {
-            uint32_t win_total = 0;
-            bool win_over = false;
-            for (int q = 0; q < kCS; ++q) {
-                const uint32_t n = ar->wcnt[q];
-                win_total += n;
-                win_over |= n > (uint32_t)kAreaWin;
-            }
-            if (!win_over && win_total <= (uint32_t)kWinTotal) {
-                if (lead) window_resolve_area(a, ti, ar, sh, win_total, cx.L, m, kk, thr);
-                PROF_END(ti.cat, 4);
-                continue;
-            }
-        }
-        // binned rows and overflowing windows need the row slice
-        load_slice<NVT>(sl, w);
-        unsigned ex_bins = 0;
-        bool bins_remote = false;
-        if (cat == kWindow) {
-            // window overflow: level-1 bins of the slice here (the scan kernel binned only
-            // binned rows), exchanged across the cluster
-            uint4* az = reinterpret_cast<uint4*>(sh->acc);
-            __syncthreads();
-            for (int i = tid; i < kBins * kNT / 2; i += kNT) az[i] = make_uint4(0, 0, 0, 0);
-            if (tid < kBins) sh->bcnt[tid] = 0;
-            __syncthreads();
-            reread_bins(sl, m, ti.c, 0, 0, sh);
-            __syncthreads();
-            Pub& pbw = sh->pub[cx.ex & 1];
-            for (int bin = wid; bin < kBins; bin += kNW) {
-                long long sm = 0;
-                for (int i = lane; i < kNT; i += 32) {
-                    const uint2 v = sh->acc[bin * kNT + i];
-                    sm += (long long)v.x * 8388608 + (int32_t)v.y;
-                }
-                sm = (long long)warp_sum_u64((unsigned long long)sm);
-                if (lane == 0) {
-                    pbw.mass[bin] = (unsigned long long)sm;
-                    pbw.cnt[bin] = sh->bcnt[bin];
-                }
-            }
-            cluster_barrier();  // exchange of the overflow bins
-            ex_bins = cx.ex++;
-            bins_remote = true;
-            cat = kBinned;
-            PROF_MARK(ti.cat, 5);
-        }
-
-        // level-1 walk (every CTA, identical inputs)
-        __syncthreads();
-        if (tid < 32) {
-            __shared__ uint32_t tc[32];
-            __shared__ unsigned long long tm[32];
-            uint32_t cs = 0;
-            unsigned long long ms = 0;
-            if (lane < kBins) {
-                if (bins_remote) {
-                    for (int q = 0; q < kCS; ++q) {
-                        const Pub* rp = remote_pub(cx, q, ex_bins);
-                        cs += rp->cnt[lane];
-                        ms += rp->mass[lane];
-                    }
-                } else {
-                    cs = ar->cnt[lane];
-                    ms = ar->mass[lane];
-                }
-            }
-            tc[lane] = cs;
-            tm[lane] = ms;
-            __syncwarp();
-            const Walk wk = walk_groups(tc, tm, kBins, 0ull, 0ull, kk, thr);
-            if (lane == 0) {
-                sh->sel[0] = wk.group;
-                sh->self64[0] = wk.cnt;
-                sh->self64[1] = wk.mass;
-            }
-        }
-        __syncthreads();
-        const int b1 = sh->sel[0];
-        PROF_MARK(ti.cat, 6);
-        if (b1 < 0) {
-            // no boundary: every element is kept
-            if (lead && tid == 0) put_desc(a, ti, m, 0u, 0x7fffffff, S, 0, 0u);
-            PROF_END(ti.cat, 14);
-            continue;
-        }
-        unsigned long long cum_cnt = sh->self64[0], cum_mass = sh->self64[1];
-
-        // keys of bin b1: when they fit one key chunk, count keys directly (no level 2)
-        if (tid < 32) {
-            uint32_t klo1, khi1;
-            key_range(b1, okey(0xFF80u), mkey, m, ti.c, 1, klo1, khi1);
-            if (lane == 0) {
-                sh->sel[4] = (int)klo1;
-                sh->sel[5] = (int)khi1;
-            }
-        }
-        __syncthreads();
-        int b2 = -2;  // -2: level 2 skipped
-        if ((uint32_t)sh->sel[5] - (uint32_t)sh->sel[4] + 1u > (uint32_t)kKeyChunk) {
-        // ---- level 2: sub-bins of bin b1 ---------------------------------------------------
-        {
-            __syncthreads();
-            uint4* az = reinterpret_cast<uint4*>(sh->acc);
-            for (int i = tid; i < kSub * kNT / 2; i += kNT) az[i] = make_uint4(0, 0, 0, 0);
-            if (tid < kBins) sh->bcnt[tid] = 0;
-            if (tid == 0) sh->nlist = 0;
-            // this CTA's valid elements of bin b1: positions by a block-wide exclusive scan of
-            // per-thread counts (no atomics); compacted into the list when they fit
-            uint32_t cnt_me = 0;
-#pragma unroll
-            for (int j = 0; j < NVT; ++j) {
-                const uint32_t* u = reinterpret_cast<const uint32_t*>(&w[j]);
-#pragma unroll
-                for (int hh = 0; hh < 8; ++hh) {
-                    const uint32_t bits = (hh & 1) ? (u[hh >> 1] >> 16) : (u[hh >> 1] & 0xFFFFu);
-                    cnt_me += (bin1_of(y_clamped(bf(bits), m, ti.c)) == b1 &&
-                               elem_valid(sl, elem_index(sl, j, hh))) ? 1u : 0u;
-                }
-            }
-            const uint32_t incl = warp_incl_u32(cnt_me);
-            if (lane == 31) sh->red32[wid] = incl;
-            __syncthreads();
-            uint32_t pos = incl - cnt_me, total = 0;
-            for (int i = 0; i < kNW; ++i) {
-                if (i < wid) pos += sh->red32[i];
-                total += sh->red32[i];
-            }
-            const bool compact = total <= (uint32_t)kListCap;
-            if (compact) {
-                if (tid == 0) sh->nlist = total;
-                if (cnt_me) {
-#pragma unroll
-                    for (int j = 0; j < NVT; ++j) {
-                        const uint32_t* u = reinterpret_cast<const uint32_t*>(&w[j]);
-#pragma unroll
-                        for (int hh = 0; hh < 8; ++hh) {
-                            const uint32_t bits = (hh & 1) ? (u[hh >> 1] >> 16) : (u[hh >> 1] & 0xFFFFu);
-                            const int e = elem_index(sl, j, hh);
-                            if (bin1_of(y_clamped(bf(bits), m, ti.c)) == b1 && elem_valid(sl, e)) {
-                                if (pos < kListCap) sh->list[pos] = (bits << 16) | (uint32_t)(e - sl.e0);
-                                ++pos;
-                            }
-                        }
-                    }
-                }
-                __syncthreads();
-                const int n = (int)min(sh->nlist, (uint32_t)kListCap);
-                for (int i = tid; i < n; i += kNT) {
-                    const uint32_t bits = sh->list[i] >> 16;
-                    const float yc = y_clamped(bf(bits), m, ti.c);
-                    const int b2 = bin2_of(yc, b1);
-                    const unsigned long long F = fix_of_y(yc);
-                    uint2* p = &sh->acc[b2 * kNT + tid];
-                    uint2 v = *p;
-                    // F = hi * 2^23 + lo with hi <= 2^17, |lo| <= 2^22 (per-thread sums stay exact)
-                    const uint32_t fh = (uint32_t)((F + 4194304ull) >> 23);
-                    const int32_t fl = (int32_t)((long long)F - (long long)fh * 8388608);
-                    v.x += fh;
-                    v.y += (uint32_t)fl;
-                    *p = v;
-                    atomicAdd(&sh->bcnt[b2], 1u);
-                }
-            } else {
-                reread_bins(sl, m, ti.c, 1, b1, sh);
-            }
-            __syncthreads();
-            Pub& pb3 = sh->pub[cx.ex & 1];
-            for (int bb = wid; bb < kSub; bb += kNW) {
-                long long s = 0;
-                for (int i = lane; i < kNT; i += 32) {
-                    const uint2 v = sh->acc[bb * kNT + i];
-                    s += (long long)v.x * 8388608 + (int32_t)v.y;
-                }
-                s = (long long)warp_sum_u64((unsigned long long)s);
-                if (lane == 0) {
-                    pb3.mass[bb] = (unsigned long long)s;
-                    pb3.cnt[bb] = sh->bcnt[bb];
-                }
-            }
-            cluster_barrier();  // exchange 3
-            const unsigned ex3 = cx.ex++;
-            __syncthreads();
-            if (tid < 32) {
-                __shared__ uint32_t tc2[32];
-                __shared__ unsigned long long tm2[32];
-                uint32_t cs = 0;
-                unsigned long long ms = 0;
-                if (lane < kSub) {
-                    for (int q = 0; q < kCS; ++q) {
-                        const Pub* rp = remote_pub(cx, q, ex3);
-                        cs += rp->cnt[lane];
-                        ms += rp->mass[lane];
-                    }
-                }
-                tc2[lane] = cs;
-                tm2[lane] = ms;
-                __syncwarp();
-                const Walk wk = walk_groups(tc2, tm2, kSub, cum_cnt, cum_mass, kk, thr);
-                if (lane == 0) {
-                    sh->sel[3] = wk.group;
-                    sh->self64[2] = wk.cnt;
-                    sh->self64[3] = wk.mass;
-                }
-            }
-            __syncthreads();
-        }
-        b2 = sh->sel[3];
-        PROF_MARK(ti.cat, 7);
-        if (b2 < 0) {
-            // cannot happen when level 1 found a boundary; keep everything defensively
-            if (lead && tid == 0) {
-                atomicOr(&a.ws->err, 8u);
-                put_desc(a, ti, m, 0u, 0x7fffffff, S, 0, 0u);
-            }
-            continue;
-        }
-        cum_cnt = sh->self64[2];
-        cum_mass = sh->self64[3];
-        if (tid < 32) {
-            uint32_t klo2, khi2;
-            key_range(b1 * kSub + b2, okey(0xFF80u), mkey, m, ti.c, 2, klo2, khi2);
-            if (lane == 0) {
-                sh->sel[4] = (int)klo2;
-                sh->sel[5] = (int)khi2;
-            }
-        }
-        __syncthreads();
-        }  // level 2
-
-        // ---- level 3: per-key counts of the boundary (sub-)bin, in chunks from the top ------
-        const uint32_t klo = (uint32_t)sh->sel[4], khi = (uint32_t)sh->sel[5];
-        KeyStop ks;
-        ks.found = 0;
-        for (uint32_t top = khi; top >= klo && top <= 0xFFFFu;) {
-            const uint32_t bot = (top - klo + 1 > (uint32_t)kKeyChunk) ? top - kKeyChunk + 1 : klo;
-            const int nk = (int)(top - bot + 1);
-            __syncthreads();
-            for (int i = tid; i < kKeyChunk; i += kNT) sh->khist[i] = 0;
-            __syncthreads();
-            const uint32_t vlo = key_bits(bot), vhi = key_bits(top);
-            const uint32_t vlo2 = vlo | (vlo << 16), vhi2 = vhi | (vhi << 16);
-#pragma unroll
-            for (int j = 0; j < NVT; ++j) {
-                const uint32_t* u = reinterpret_cast<const uint32_t*>(&w[j]);
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const uint32_t in = bf2_ge(u[q], vlo2) & bf2_le(u[q], vhi2);
-                    if (!in) continue;
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        if (!(in & (h ? 0xFFFF0000u : 0x0000FFFFu))) continue;
-                        const int e = elem_index(sl, j, 2 * q + h);
-                        if (!elem_valid(sl, e)) continue;
-                        const uint32_t bits = h ? (u[q] >> 16) : (u[q] & 0xFFFFu);
-                        const uint32_t kkey = okey(bits);
-                        if (kkey >= bot && kkey <= top) atomicAdd(&sh->khist[top - kkey], 1u);
-                    }
-                }
-            }
-#ifdef DSV_PROFILE
-            if (tid == 0) atomicAdd(reinterpret_cast<unsigned long long*>(a.res) + ti.cat * 16 + 11, 1ull);
-#endif
-            cluster_barrier();  // exchange 4 (chunk)
-            cx.ex++;
-            // sum the cluster's counts into acc (as u32) and walk
-            uint32_t* tot = reinterpret_cast<uint32_t*>(sh->acc);
-            for (int i = tid; i < nk; i += kNT) {
-                uint32_t s = 0;
-                for (int q = 0; q < kCS; ++q) s += cluster.map_shared_rank(sh->khist, q)[i];
-                tot[i] = s;
-            }
-            __syncthreads();
-            if (tid < 32) {
-                const KeyStop r = walk_keys(tot, top, nk, m, ti.c, cum_cnt, cum_mass, kk, thr);
-                if (lane == 0) {
-                    sh->sel[6] = r.found;
-                    sh->sel[7] = (int)r.key;
-                    sh->sel[8] = (int)r.count;
-                    sh->self64[4] = r.cnt;
-                    sh->self64[5] = r.mass;
-                    sh->self64[6] = r.F;
-                }
-            }
-            __syncthreads();
-            if (sh->sel[6]) {
-                // occurrences of the boundary key in the CTAs before this one, and in this one
-                const uint32_t kidx = top - (uint32_t)sh->sel[7];
-                if (tid < 32) {
-                    const uint32_t f = lane < cx.rank ? cluster.map_shared_rank(sh->khist, lane)[kidx] : 0u;
-                    const uint32_t sum_ = warp_sum_u32(f);
-                    if (lane == 0) {
-                        sh->sel[9] = (int)sum_;
-                        sh->sel[14] = (int)sh->khist[kidx];
-                    }
-                }
-            }
-            // no CTA may clear its chunk counts while a peer still reads them
-            cluster_barrier();
-            cx.ex++;
-            ks.found = sh->sel[6];
-            if (ks.found) {
-                ks.key = (uint32_t)sh->sel[7];
-                ks.count = (uint32_t)sh->sel[8];
-                ks.cnt = sh->self64[4];
-                ks.mass = sh->self64[5];
-                ks.F = sh->self64[6];
-                break;
-            }
-            cum_cnt = sh->self64[4];
-            cum_mass = sh->self64[5];
-            if (bot == klo) break;
-            top = bot - 1;
-        }
-        if (!ks.found) {
-            if (lead && tid == 0) {
-                atomicOr(&a.ws->err, 8u);
-                put_desc(a, ti, m, 0u, 0x7fffffff, S, 0, 0u);
-            }
-            continue;
-        }
-        PROF_MARK(ti.cat, 8);
-        // kept among the ks.count elements with the boundary key
-        unsigned long long ntie = ks.count;
-        if ((long long)(ks.cnt + ntie) > kk) ntie = (unsigned long long)(kk - (long long)ks.cnt);
-        if (ks.F > 0 && (long long)(ks.mass) <= thr) {
-            const unsigned long long pb_ = (unsigned long long)((thr - (long long)ks.mass)) / ks.F + 1ull;
-            if (pb_ < ntie) ntie = pb_;
-        }
-        if (ntie < 1) ntie = 1;
-        const unsigned long long skept = ks.mass + ntie * ks.F;
-
-        if (ntie >= ks.count) {
-            if (lead && tid == 0) put_desc(a, ti, m, ks.key, 0x7fffffff, skept, 0, 0u);
-            PROF_END(ti.cat, 9);
-            continue;
-        }
-        // ---- tie cut: the ntie-th occurrence (index order) of the boundary key ----------------
-        // the CTA holding it is known from the per-CTA key counts of the last chunk
-        const unsigned long long before = (unsigned)sh->sel[9];
-        const unsigned long long cta_occ = (unsigned)sh->sel[14];
-        if (before < ntie && before + cta_occ >= ntie) {
-            // index order inside a CTA is (vector-row j, thread, half); per-row totals go to
-            // shared memory so that no per-row array stays in registers next to the row slice
-            uint32_t* rowcnt = reinterpret_cast<uint32_t*>(sh->acc);          // [NVT]
-            uint32_t* wrow = reinterpret_cast<uint32_t*>(sh->acc) + 64;       // [kNW]
-            __syncthreads();
-            if (tid < NVT) rowcnt[tid] = 0;
-            __syncthreads();
-#pragma unroll
-            for (int j = 0; j < NVT; ++j) {
-                const uint32_t* u = reinterpret_cast<const uint32_t*>(&w[j]);
-                uint32_t c = 0;
-#pragma unroll
-                for (int hh = 0; hh < 8; ++hh) {
-                    const uint32_t bits = (hh & 1) ? (u[hh >> 1] >> 16) : (u[hh >> 1] & 0xFFFFu);
-                    c += (okey(bits) == ks.key && elem_valid(sl, elem_index(sl, j, hh))) ? 1u : 0u;
-                }
-                const uint32_t ws_ = warp_sum_u32(c);
-                if (lane == 0 && ws_) atomicAdd(&rowcnt[j], ws_);
-            }
-            __syncthreads();
-            uint32_t need = (uint32_t)(ntie - before);
-            int jstar = NVT - 1;
-            for (int j = 0; j < NVT; ++j) {
-                if (rowcnt[j] >= need) { jstar = j; break; }
-                need -= rowcnt[j];
-            }
-            // recount vector-row jstar for this thread
-            uint32_t cme = 0;
-#pragma unroll
-            for (int j = 0; j < NVT; ++j) {
-                if (j != jstar) continue;
-                const uint32_t* u = reinterpret_cast<const uint32_t*>(&w[j]);
-#pragma unroll
-                for (int hh = 0; hh < 8; ++hh) {
-                    const uint32_t bits = (hh & 1) ? (u[hh >> 1] >> 16) : (u[hh >> 1] & 0xFFFFu);
-                    cme += (okey(bits) == ks.key && elem_valid(sl, elem_index(sl, j, hh))) ? 1u : 0u;
-                }
-            }
-            const uint32_t incl = warp_incl_u32(cme);
-            if (lane == 31) wrow[wid] = incl;
-            __syncthreads();
-            uint32_t wbefore = 0;
-            for (int i = 0; i < wid; ++i) wbefore += wrow[i];
-            const uint32_t lo_ = wbefore + incl - cme;
-            if (cme > 0 && lo_ < need && lo_ + cme >= need) {
-                uint32_t k2 = need - lo_;  // 1-based within this thread's vector
-                int tie = -1;
-#pragma unroll
-                for (int j = 0; j < NVT; ++j) {
-                    if (j != jstar) continue;
-                    const uint32_t* u = reinterpret_cast<const uint32_t*>(&w[j]);
-#pragma unroll
-                    for (int hh = 0; hh < 8; ++hh) {
-                        const uint32_t bits = (hh & 1) ? (u[hh >> 1] >> 16) : (u[hh >> 1] & 0xFFFFu);
-                        const int e = elem_index(sl, j, hh);
-                        if (tie < 0 && elem_valid(sl, e) && okey(bits) == ks.key) {
-                            if (--k2 == 0) tie = e;
-                        }
-                    }
-                }
-                if (tie < 0) atomicOr(&a.ws->err, 16u);
-                put_desc(a, ti, m, ks.key, tie, skept, 0, 0u);
-            }
-        }
-        PROF_END(ti.cat, 10);
-    }
-    // no CTA may leave while a peer can still read its shared memory
-    cluster_barrier();
-}
-
 
 // =======================================================================================
 // Row kernel: ONE CTA per row, no clusters.  Each CTA streams its whole row from global
@@ -2372,21 +1263,6 @@ __global__ void __launch_bounds__(kNT) chain_kernel(VerifyArgs a) {
     const int tid = threadIdx.x, lane = tid & 31;
     const int rank = (int)cluster.block_rank();
     const int b = blockIdx.x / kCS;  // gridDim = B * kCS: one cluster per request
-    if (rank == 0) {
-        // the scan areas of this request's rows start the next launch at zero
-        for (int i = tid; i < kT * 2; i += kNT) {
-            TaskArea* ar = &a.area[b * kT * 2 + i];
-            ar->S = 0ull;
-            ar->wcnt[0] = ar->wcnt[1] = ar->wcnt[2] = ar->wcnt[3] = 0u;
-            ar->wcnt[4] = ar->wcnt[5] = ar->wcnt[6] = ar->wcnt[7] = 0u;
-        }
-        for (int i = tid; i < kT * 2 * kBins; i += kNT) {
-            TaskArea* ar = &a.area[b * kT * 2 + i / kBins];
-            ar->mass[i % kBins] = 0ull;
-            ar->cnt[i % kBins] = 0u;
-        }
-    }
-
     const int cap = clamp_cap(a.caps[b]);
     const float T = a.temperature[b];
     const int kq = a.top_k[b];
@@ -2612,53 +1488,6 @@ __global__ void __launch_bounds__(kNT) chain_kernel(VerifyArgs a) {
 // ---------------------------------------------------------------------------------------
 // launcher
 
-template <int NVT>
-int launch_cluster_kernel(void (*kern)(VerifyArgs), VerifyArgs a, cudaStream_t stream, int which) {
-    const size_t smem = ((sizeof(RowSmem) + 15) & ~(size_t)15) +
-                        (which == 0 ? (size_t)2 * NVT * kNT * sizeof(uint4) : (size_t)0);
-    static int attr_done[2] = {0, 0};
-    if (!attr_done[which]) {
-        if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-            return kLaunchFailed;
-        attr_done[which] = 1;
-    }
-    cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = kCS;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.blockDim = dim3(kNT, 1, 1);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = stream;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    static int cached_dev[2] = {-1, -1}, cached_n[2] = {0, 0};
-    int dev = 0;
-    cudaGetDevice(&dev);
-    int nclus = 0;
-    if (cached_dev[which] == dev) {
-        nclus = cached_n[which];
-    } else {
-        cfg.gridDim = dim3(kCS, 1, 1);
-        if (cudaOccupancyMaxActiveClusters(&nclus, kern, &cfg) != cudaSuccess || nclus <= 0)
-            return kLaunchFailed;
-        cached_dev[which] = dev;
-        cached_n[which] = nclus;
-    }
-    a.num_clusters = nclus;
-    cfg.gridDim = dim3(nclus * kCS, 1, 1);
-    if (cudaLaunchKernelEx(&cfg, kern, a) != cudaSuccess) return kLaunchFailed;
-    return kOk;
-}
-
-template <int NVT>
-int launch_rows(VerifyArgs a, cudaStream_t stream) {
-    int st = launch_cluster_kernel<NVT>(scan_kernel<NVT>, a, stream, 0);
-    if (st != kOk) return st;
-    return launch_cluster_kernel<NVT>(select_kernel<NVT>, a, stream, 1);
-}
-
 int launch_chain(VerifyArgs a, cudaStream_t stream) {
     cudaLaunchConfig_t cfg = {};
     cudaLaunchAttribute attr[1];
@@ -2686,34 +1515,16 @@ int launch_chain(VerifyArgs a, cudaStream_t stream) {
 
 }  // namespace st
 
-size_t stream_smem_bytes() { return sizeof(st::RowSmem); }
-
-// vocabulary elements per CTA slice for a given V (multiple of 8)
-static int stream_slice(int V) {
-    int L = (V + st::kCS - 1) / st::kCS;
-    return (L + 7) & ~7;
-}
-
-int stream_nvt(int V) {
-    const int L = stream_slice(V);
-    const int nv = L / 8 + 1;
-    return (nv + st::kNT - 1) / st::kNT;
-}
-
 bool stream_supported(const VerifyArgs& a, int dtype) {
     if (dtype != 0) return false;
-    if (a.B > st::kMaxB || a.desc == nullptr) return false;
+    if (a.B > st::kMaxB || a.desc == nullptr || a.gmax == nullptr) return false;
     if ((reinterpret_cast<uintptr_t>(a.tgt) & 1u) || (a.drf && (reinterpret_cast<uintptr_t>(a.drf) & 1u)))
         return false;
-    return stream_nvt(a.V) <= 5;
+    return a.V <= 262144;
 }
 
 int launch_stream(VerifyArgs a, cudaStream_t stream) {
-    a.slice = stream_slice(a.V);
-    const int nvt = stream_nvt(a.V);
-    int st_ = kUnsupported;
-    (void)nvt;
-    st_ = st::launch_rows_cta(a, stream);
+    const int st_ = st::launch_rows_cta(a, stream);
     if (st_ != kOk) return st_;
     return st::launch_chain(a, stream);
 }
