@@ -22,6 +22,7 @@ from __future__ import annotations
 
 import argparse
 import json
+import re
 import os
 import statistics
 import sys
@@ -85,17 +86,20 @@ def measured_hbm_peak():
 
 
 def profiled_traffic(config: str):
-    """DRAM bytes per launch of the verify kernel from the committed ncu summary, or None."""
-    f = ROOT / "profiles" / f"verify_kernel_{config}.md"
+    """DRAM bytes per verification call from the committed ncu summary, or (None, []).
+
+    The summary holds one `dram_bytes_per_launch_<kernel>: N` line per captured kernel; the
+    call's traffic is their sum, reported with the kernels it covers."""
+    f = ROOT / "profiles" / f"rows_kernel_{config}.md"
     if not f.exists():
-        return None
+        return None, []
+    total, kernels = 0.0, []
     for line in f.read_text().splitlines():
-        if line.strip().startswith("dram_bytes_per_launch:"):
-            try:
-                return float(line.split(":", 1)[1].split()[0])
-            except ValueError:
-                return None
-    return None
+        m = re.match(r"\s*dram_bytes_per_launch_(\w+):\s*([0-9.eE+]+)", line)
+        if m:
+            kernels.append("dsv::" + m.group(1))
+            total += float(m.group(2))
+    return (total if kernels else None), kernels
 
 
 def make_batch(config: str, rank: int, device):
@@ -339,6 +343,7 @@ def run_dspine(args):
         kernel_ms = statistics.mean(step_ms)
         achieved = alg_bytes / (kernel_ms * 1e-3) / 1e9
         peak, peak_src = measured_hbm_peak()
+        traffic, traffic_kernels = profiled_traffic(args.config)
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
@@ -355,8 +360,9 @@ def run_dspine(args):
                     "d2h_bytes_per_step": d2h},
             "gpu_launches": all_launches,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
-                         "frac": achieved / peak, "traffic": profiled_traffic(args.config),
-                         "peak_source": peak_src, "kernel": "dsv::verify_kernel",
+                         "frac": achieved / peak, "traffic": traffic,
+                         "traffic_kernels": traffic_kernels, "peak_source": peak_src,
+                         "kernel": "dsv::rows_kernel + dsv::chain_kernel (one dsv_verify_logits call)",
                          "algorithmic_bytes_per_launch": alg_bytes,
                          "kernel_ms": kernel_ms},
         }
