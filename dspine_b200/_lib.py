@@ -63,6 +63,11 @@ _SIGNATURES = {
                           c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                           c_void_p, c_void_p, ctypes.POINTER(CompactOut), c_void_p, c_size_t,
                           c_void_p],
+    "dsv_verify_logits_noalloc": [c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p,
+                                  c_int64, c_void_p, c_void_p, c_int64, c_int64, c_void_p,
+                                  c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                  c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                                  ctypes.POINTER(CompactOut), c_void_p, c_void_p],
 }
 _RESTYPES = {"dsv_version": ctypes.c_char_p, "dsv_status_string": ctypes.c_char_p,
              "dsv_launch_count": ctypes.c_uint64}

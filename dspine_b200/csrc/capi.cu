@@ -2,6 +2,8 @@
 #include <cuda_runtime.h>
 
 #include <atomic>
+#include <cstddef>
+#include <mutex>
 
 #include "../../include/dspine_b200.h"
 #include "dsv_common.cuh"
@@ -17,6 +19,31 @@ std::atomic<uint64_t> g_launches{0};
 inline int counted(int status, int kernels) {
     if (status == DSV_OK) g_launches.fetch_add((uint64_t)kernels, std::memory_order_relaxed);
     return status;
+}
+
+// ---- scratch of dsv_verify_logits_noalloc -------------------------------------------------
+// A file-scope device array sized for kNoAllocMaxBatch requests (225 KB).  It is part of the
+// module image: the driver places it when the library's kernels are loaded on a device, and it
+// starts zeroed.  Its address is looked up once per device and cached.
+constexpr int kNoAllocMaxBatch = 256;
+constexpr size_t kNoAllocBytes = dsv::verify_workspace_bytes(kNoAllocMaxBatch);
+__device__ __align__(256) unsigned char g_noalloc_ws[kNoAllocBytes];
+
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+void* g_noalloc_addr[kMaxDevices] = {};
+
+// address of g_noalloc_ws on the current device, or nullptr if it cannot be obtained
+void* noalloc_scratch() {
+    int dev = -1;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) return nullptr;
+    std::lock_guard<std::mutex> g(g_noalloc_mu);
+    if (g_noalloc_addr[dev] == nullptr) {
+        void* p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_noalloc_ws) != cudaSuccess) return nullptr;
+        g_noalloc_addr[dev] = p;
+    }
+    return g_noalloc_addr[dev];
 }
 
 }  // namespace
@@ -138,6 +165,40 @@ int dsv_verify_logits(int32_t batch, int32_t vocab, int32_t dtype, const int64_t
     if (dsv::stream_supported(a, dtype))
         return counted(dsv::launch_stream(a, (cudaStream_t)stream), 2);
     return counted(dsv::launch_verify(a, dtype, (cudaStream_t)stream), 1);
+}
+
+int dsv_verify_logits_noalloc(int32_t batch, int32_t vocab, int32_t dtype,
+                              const int64_t* candidates, const void* target_logits,
+                              const int64_t* target_row, int64_t target_rows,
+                              const void* draft_logits, const int64_t* draft_row,
+                              int64_t draft_rows, int64_t row_stride, const float* temperature,
+                              const int32_t* top_k, const float* top_p,
+                              const int32_t* verify_lens, const float* uniforms,
+                              const float* uniform_final, const int32_t* prefix_lens,
+                              int32_t* accept, int32_t* commit, int64_t* bonus, int64_t* output,
+                              int32_t* new_seq, const dsv_compact_out* compact,
+                              uint32_t* device_error, dsv_stream_t stream) {
+    if (batch < 0) return DSV_BAD_SHAPE;
+    if (batch > kNoAllocMaxBatch) return DSV_WORKSPACE_TOO_SMALL;
+    if (batch == 0) return DSV_OK;
+    char* ws = static_cast<char*>(noalloc_scratch());
+    if (ws == nullptr) return DSV_LAUNCH_FAILED;
+    const size_t used = dsv::verify_workspace_bytes(batch);
+    cudaStream_t st = (cudaStream_t)stream;
+    // counters, the error word and the greedy maxima must start at zero; clearing the whole
+    // used prefix also drops whatever an earlier call that failed on the device left behind
+    if (cudaMemsetAsync(ws, 0, used, st) != cudaSuccess) return DSV_LAUNCH_FAILED;
+    const int status = dsv_verify_logits(
+        batch, vocab, dtype, candidates, target_logits, target_row, target_rows, draft_logits,
+        draft_row, draft_rows, row_stride, temperature, top_k, top_p, verify_lens, uniforms,
+        uniform_final, prefix_lens, accept, commit, bonus, output, new_seq, compact, ws, used,
+        stream);
+    if (status != DSV_OK) return status;
+    if (device_error != nullptr &&
+        cudaMemcpyAsync(device_error, ws + offsetof(dsv::WsHeader, err), sizeof(uint32_t),
+                        cudaMemcpyDeviceToDevice, st) != cudaSuccess)
+        return DSV_LAUNCH_FAILED;
+    return DSV_OK;
 }
 
 }  // extern "C"

@@ -38,15 +38,15 @@ struct RowDesc {
 
 // Workspace layout: [WsHeader (64 B)][done: u32 x B, padded to 64 B][TaskResult x B x 16]
 //                   [RowDesc x B x 16 x 2]
-inline size_t verify_done_bytes(int B) { return ((size_t)B * 4 + 63) & ~(size_t)63; }
-inline size_t verify_desc_offset(int B) {
+constexpr inline size_t verify_done_bytes(int B) { return ((size_t)B * 4 + 63) & ~(size_t)63; }
+constexpr inline size_t verify_desc_offset(int B) {
     return 64 + verify_done_bytes(B) + (size_t)B * 16 * sizeof(TaskResult);
 }
-inline size_t verify_gmax_offset(int B) {
+constexpr inline size_t verify_gmax_offset(int B) {
     return verify_desc_offset(B) + (size_t)B * 16 * 2 * sizeof(RowDesc);
 }
 // [u64 x B x 16]: greedy rows' packed (max key << 32 | ~first index), reset after use
-inline size_t verify_workspace_bytes(int B) {
+constexpr inline size_t verify_workspace_bytes(int B) {
     return verify_gmax_offset(B) + (size_t)B * 16 * sizeof(unsigned long long);
 }
 

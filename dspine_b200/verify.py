@@ -95,20 +95,12 @@ def _check(cond, msg):
         raise ValueError(msg)
 
 
-def verify_logits(*, candidates, target_logits, target_rows, temperature, top_k, top_p,
-                  verify_lens, uniforms, uniform_final, prefix_lens, draft_logits=None,
-                  draft_rows=None, outputs=None, slots=None, slot_rows=None, compact=None,
-                  workspace: Workspace | None = None):
-    """Verify a ragged batch of 16-token draft blocks directly from logits.
-
-    candidates [B,16] int64 (anchor + 15 drafts); target_logits [R,V] bf16/fp32 rows;
-    target_rows [B] int64: request b's verify position s uses target row target_rows[b]+s;
-    draft_logits [R',V] (same dtype) with draft_rows [B], or None for one-hot q;
-    temperature [B] f32, top_k [B] i32 (>= V: off, <= 1: greedy), top_p [B] f32;
-    verify_lens [B] i32 in [1,16]; uniforms [B,15] f32; uniform_final [B] f32;
-    prefix_lens [B] i32.  Optional ``slots`` [*] i32 with ``slot_rows`` [B] i64 and a
-    ``compact`` CompactOutputs receive the packed accepted tokens and KV slots.
-    Returns (accept, commit, bonus, output, new_seq)."""
+def _prepare(candidates, target_logits, target_rows, temperature, top_k, top_p, verify_lens,
+             uniforms, uniform_final, prefix_lens, draft_logits, draft_rows, outputs, slots,
+             slot_rows, compact):
+    """Validate the arguments of verify_logits (ValueError before launch, as
+    sampling/rejection.py:113-138) and marshal the C-ABI arguments shared by
+    dsv_verify_logits and dsv_verify_logits_noalloc (everything before the scratch)."""
     _check(candidates.dim() == 2 and candidates.shape[1] == T, "candidates must be [B,16]")
     B = candidates.shape[0]
     dev = candidates.device
@@ -160,16 +152,63 @@ def verify_logits(*, candidates, target_logits, target_rows, temperature, top_k,
         cstruct = _lib.CompactOut(slots.data_ptr(), slots.numel(), slot_rows.data_ptr(), compact.tokens.data_ptr(),
                                   compact.kept_slots.data_ptr(), compact.offsets.data_ptr(),
                                   compact.freed_slots.data_ptr(), compact.freed_offsets.data_ptr())
+    drows_n = draft_logits.shape[0] if draft_logits is not None else 0
+    args = (B, V, _DTYPES[target_logits.dtype], candidates.data_ptr(),
+            target_logits.data_ptr(), target_rows.data_ptr(), target_logits.shape[0],
+            _lib.ptr(draft_logits), _lib.ptr(draft_rows), drows_n, stride,
+            temperature.data_ptr(), top_k.data_ptr(), top_p.data_ptr(), verify_lens.data_ptr(),
+            uniforms.data_ptr(), uniform_final.data_ptr(), prefix_lens.data_ptr(),
+            *(o.data_ptr() for o in outputs),
+            ctypes.byref(cstruct) if cstruct is not None else None)
+    return B, dev, outputs, args, cstruct
+
+
+def verify_logits(*, candidates, target_logits, target_rows, temperature, top_k, top_p,
+                  verify_lens, uniforms, uniform_final, prefix_lens, draft_logits=None,
+                  draft_rows=None, outputs=None, slots=None, slot_rows=None, compact=None,
+                  workspace: Workspace | None = None):
+    """Verify a ragged batch of 16-token draft blocks directly from logits.
+
+    candidates [B,16] int64 (anchor + 15 drafts); target_logits [R,V] bf16/fp32 rows;
+    target_rows [B] int64: request b's verify position s uses target row target_rows[b]+s;
+    draft_logits [R',V] (same dtype) with draft_rows [B], or None for one-hot q;
+    temperature [B] f32, top_k [B] i32 (>= V: off, <= 1: greedy), top_p [B] f32;
+    verify_lens [B] i32 in [1,16]; uniforms [B,15] f32; uniform_final [B] f32;
+    prefix_lens [B] i32.  Optional ``slots`` [*] i32 with ``slot_rows`` [B] i64 and a
+    ``compact`` CompactOutputs receive the packed accepted tokens and KV slots.
+    Returns (accept, commit, bonus, output, new_seq)."""
+    B, dev, outputs, args, _keep = _prepare(
+        candidates, target_logits, target_rows, temperature, top_k, top_p, verify_lens,
+        uniforms, uniform_final, prefix_lens, draft_logits, draft_rows, outputs, slots,
+        slot_rows, compact)
     if workspace is None:
         workspace = workspace_for(B, dev)
     _check(workspace.batch >= B, "workspace is too small for this batch")
-    drows_n = draft_logits.shape[0] if draft_logits is not None else 0
-    _lib.call(
-        "dsv_verify_logits", B, V, _DTYPES[target_logits.dtype], candidates.data_ptr(),
-        target_logits.data_ptr(), target_rows.data_ptr(), target_logits.shape[0],
-        _lib.ptr(draft_logits), _lib.ptr(draft_rows), drows_n, stride, temperature.data_ptr(),
-        top_k.data_ptr(), top_p.data_ptr(), verify_lens.data_ptr(), uniforms.data_ptr(),
-        uniform_final.data_ptr(), prefix_lens.data_ptr(), *(o.data_ptr() for o in outputs),
-        ctypes.byref(cstruct) if cstruct is not None else None, workspace.buf.data_ptr(),
-        workspace.nbytes, _stream(dev))
+    _lib.call("dsv_verify_logits", *args, workspace.buf.data_ptr(), workspace.nbytes,
+              _stream(dev))
+    return outputs
+
+
+NOALLOC_MAX_BATCH = 256
+
+
+def verify_logits_noalloc(*, candidates, target_logits, target_rows, temperature, top_k, top_p,
+                          verify_lens, uniforms, uniform_final, prefix_lens, draft_logits=None,
+                          draft_rows=None, outputs, slots=None, slot_rows=None, compact=None,
+                          device_error=None):
+    """verify_logits for callers that cannot allocate at verification time
+    (C ABI: dsv_verify_logits_noalloc).  No workspace: the library's fixed device scratch
+    serves up to NOALLOC_MAX_BATCH requests; ``outputs`` (and ``compact``) must be given.
+    ``device_error`` (optional int32 [1] CUDA tensor) receives the call's device error word.
+    Calls that may overlap on one device (other streams or threads) must be serialised."""
+    _check(outputs is not None, "verify_logits_noalloc needs caller-owned outputs")
+    B, dev, outputs, args, _keep = _prepare(
+        candidates, target_logits, target_rows, temperature, top_k, top_p, verify_lens,
+        uniforms, uniform_final, prefix_lens, draft_logits, draft_rows, outputs, slots,
+        slot_rows, compact)
+    _check(B <= NOALLOC_MAX_BATCH, f"verify_logits_noalloc serves at most {NOALLOC_MAX_BATCH} requests")
+    if device_error is not None:
+        _check(device_error.device == dev and device_error.numel() >= 1 and
+               device_error.element_size() == 4, "device_error must be a 4-byte CUDA tensor")
+    _lib.call("dsv_verify_logits_noalloc", *args, _lib.ptr(device_error), _stream(dev))
     return outputs

@@ -92,6 +92,33 @@ int dsv_verify_logits(int32_t batch, int32_t vocab, int32_t dtype, const int64_t
                       const dsv_compact_out* compact, void* workspace, size_t workspace_bytes,
                       dsv_stream_t stream);
 
+/* ---- the same verification without a caller workspace ------------------------------------
+ * No counterpart in the reference: for callers that cannot allocate device memory (or hand out
+ * scratch) at verification time.  Same arguments, outputs and results as dsv_verify_logits,
+ * without `workspace`/`workspace_bytes`; its scratch is a fixed 225 KB device array inside the
+ * library (sized for 256 requests), and the call performs no cudaMalloc/cudaFree and no
+ * allocating library call.
+ *  - batch > 256 returns DSV_WORKSPACE_TOO_SMALL before anything is enqueued.
+ *  - each call clears the scratch it uses (cudaMemsetAsync on `stream`) before its kernels.
+ *  - device_error (optional, a device pointer to one uint32) receives this call's error word
+ *    (bits as for dsv_workspace_error), copied on `stream` after the kernels.
+ *  - the scratch is shared by every call on a device: calls that can overlap (other streams,
+ *    other host threads) race on it and must be serialised by the caller.
+ *  - the first call on each device looks up the scratch address (cudaGetSymbolAddress, which
+ *    may load the module); make that first call outside any stream capture.
+ *  - the current device must be the device of `stream` and of the tensors. */
+int dsv_verify_logits_noalloc(int32_t batch, int32_t vocab, int32_t dtype,
+                              const int64_t* candidates, const void* target_logits,
+                              const int64_t* target_row, int64_t target_rows,
+                              const void* draft_logits, const int64_t* draft_row,
+                              int64_t draft_rows, int64_t row_stride, const float* temperature,
+                              const int32_t* top_k, const float* top_p,
+                              const int32_t* verify_lens, const float* uniforms,
+                              const float* uniform_final, const int32_t* prefix_lens,
+                              int32_t* accept, int32_t* commit, int64_t* bonus, int64_t* output,
+                              int32_t* new_seq, const dsv_compact_out* compact,
+                              uint32_t* device_error, dsv_stream_t stream);
+
 #ifdef __cplusplus
 }
 #endif
