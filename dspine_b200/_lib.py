@@ -63,6 +63,12 @@ _SIGNATURES = {
                           c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                           c_void_p, c_void_p, ctypes.POINTER(CompactOut), c_void_p, c_size_t,
                           c_void_p],
+    "dsv_lmhead_workspace_size": [c_int32, c_int32, c_int32, ctypes.POINTER(c_size_t)],
+    "dsv_lmhead_topk": [c_int32, c_int32, c_int32, c_int32, c_void_p, c_int64, c_void_p, c_int64,
+                        c_int64, c_int64, c_int32, c_void_p, c_void_p, c_void_p, c_void_p,
+                        c_size_t, c_void_p],
+    "dsv_tp_merge": [c_int32, c_int32, c_int32, c_void_p, c_int64, c_void_p, c_int64, c_void_p,
+                     c_int64, c_int64, c_int32, c_void_p, c_void_p, c_void_p, c_void_p],
     "dsv_verify_logits_noalloc": [c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p,
                                   c_int64, c_void_p, c_void_p, c_int64, c_int64, c_void_p,
                                   c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

@@ -167,6 +167,76 @@ int dsv_verify_logits(int32_t batch, int32_t vocab, int32_t dtype, const int64_t
     return counted(dsv::launch_verify(a, dtype, (cudaStream_t)stream), 1);
 }
 
+int dsv_lmhead_workspace_size(int32_t rows, int32_t vocab, int32_t k, size_t* bytes) {
+    if (bytes == nullptr) return DSV_BAD_POINTER;
+    if (rows < 0 || vocab < 1 || k < 1 || k > 32) return DSV_BAD_SHAPE;
+    *bytes = dsv::lmhead_workspace_bytes(rows, vocab, k);
+    return DSV_OK;
+}
+
+int dsv_lmhead_topk(int32_t rows, int32_t vocab, int32_t hidden, int32_t k,
+                    const void* hidden_states, int64_t hidden_stride, const void* weight,
+                    int64_t weight_stride, int64_t id_offset, int64_t pad_id, int32_t sort_ids,
+                    int64_t* ids, float* values, float* lse, void* workspace,
+                    size_t workspace_bytes, dsv_stream_t stream) {
+    if (rows < 0 || vocab < 1 || k < 1 || k > 32) return DSV_BAD_SHAPE;
+    if (hidden < 64 || hidden % 64 != 0) return DSV_BAD_SHAPE;
+    if (hidden_stride < hidden || weight_stride < hidden) return DSV_BAD_SHAPE;
+    if (rows == 0) return DSV_OK;
+    if (!hidden_states || !weight || !ids || !values || !workspace) return DSV_BAD_POINTER;
+    // tensor maps: 16-byte aligned bases and row pitches
+    if (!aligned(hidden_states, 16) || !aligned(weight, 16) || hidden_stride % 8 != 0 ||
+        weight_stride % 8 != 0 || !aligned(workspace, 16))
+        return DSV_BAD_ALIGNMENT;
+    if (workspace_bytes < dsv::lmhead_workspace_bytes(rows, vocab, k)) return DSV_WORKSPACE_TOO_SMALL;
+    dsv::LmHeadArgs h = {};
+    h.M = rows;
+    h.N = vocab;
+    h.K = hidden;
+    h.k = k;
+    h.x = hidden_states;
+    h.x_stride = hidden_stride;
+    h.w = weight;
+    h.w_stride = weight_stride;
+    h.id_offset = id_offset;
+    h.pad_id = pad_id;
+    h.sort_ids = sort_ids != 0;
+    h.out_ids = ids;
+    h.out_val = values;
+    h.out_lse = lse;
+    h.workspace = workspace;
+    return counted(dsv::launch_lmhead(h, (cudaStream_t)stream), 2);
+}
+
+int dsv_tp_merge(int32_t rows, int32_t shards, int32_t k, const float* values,
+                 int64_t values_shard_stride, const int64_t* ids, int64_t ids_shard_stride,
+                 const float* lse, int64_t lse_shard_stride, int64_t pad_id, int32_t sort_ids,
+                 int64_t* out_ids, float* out_values, float* out_lse, dsv_stream_t stream) {
+    if (rows < 0 || shards < 1 || shards > 256 || k < 1 || k > 32) return DSV_BAD_SHAPE;
+    if (values_shard_stride < (int64_t)rows * k || ids_shard_stride < (int64_t)rows * k ||
+        lse_shard_stride < rows)
+        return DSV_BAD_SHAPE;
+    if (rows == 0) return DSV_OK;
+    if (!values || !ids || !lse || !out_ids || !out_values) return DSV_BAD_POINTER;
+    if (!aligned(ids, 8) || !aligned(values, 4) || !aligned(lse, 4)) return DSV_BAD_ALIGNMENT;
+    dsv::TopkMergeArgs m = {};
+    m.M = rows;
+    m.P = shards;
+    m.k = k;
+    m.val = values;
+    m.val_ps = values_shard_stride;
+    m.ids = ids;
+    m.id_ps = ids_shard_stride;
+    m.lse = lse;
+    m.lse_ps = lse_shard_stride;
+    m.pad_id = pad_id;
+    m.sort_ids = sort_ids != 0;
+    m.out_ids = out_ids;
+    m.out_val = out_values;
+    m.out_lse = out_lse;
+    return counted(dsv::launch_topk_merge(m, (cudaStream_t)stream), 1);
+}
+
 int dsv_verify_logits_noalloc(int32_t batch, int32_t vocab, int32_t dtype,
                               const int64_t* candidates, const void* target_logits,
                               const int64_t* target_row, int64_t target_rows,

@@ -97,4 +97,41 @@ int launch_verify(const VerifyArgs& a, int dtype, cudaStream_t stream);
 bool stream_supported(const VerifyArgs& a, int dtype);
 int launch_stream(VerifyArgs a, cudaStream_t stream);
 
+// ---- LM head fused with top-k (lmhead.cu) ---------------------------------------------------
+struct LmHeadArgs {
+    int M, N, K, k;            // rows, vocabulary columns of this weight, hidden, top-k (<= 32)
+    const void* x;             // [M, K] bf16, rows x_stride elements apart
+    long long x_stride;
+    const void* w;             // [N, K] bf16, rows w_stride elements apart
+    long long w_stride;
+    long long id_offset;       // added to every column index (first vocabulary id of a shard)
+    long long pad_id;          // id written for empty slots (k > N)
+    int sort_ids;              // 0: rank order (value desc, id asc); 1: ids ascending
+    int64_t* out_ids;          // [M, k]
+    float* out_val;            // [M, k] bf16-rounded logits
+    float* out_lse;            // [M] or null
+    void* workspace;           // lmhead_workspace_bytes(M, N, k), 16-byte aligned
+};
+int lmhead_tk(int k);  // register list length serving k (0: unsupported)
+size_t lmhead_workspace_bytes(int M, int N, int k);
+int launch_lmhead(const LmHeadArgs& h, cudaStream_t stream);
+
+// merge of P per-shard lists (value desc, id asc) + their logsumexps: list p of row r at
+// val[p * val_ps + r * k], ids[p * id_ps + r * k], lse[p * lse_ps + r]
+struct TopkMergeArgs {
+    int M, P, k;
+    const float* val;
+    long long val_ps;
+    const int64_t* ids;
+    long long id_ps;
+    const float* lse;
+    long long lse_ps;
+    long long pad_id;
+    int sort_ids;
+    int64_t* out_ids;
+    float* out_val;
+    float* out_lse;
+};
+int launch_topk_merge(const TopkMergeArgs& m, cudaStream_t stream);
+
 }  // namespace dsv

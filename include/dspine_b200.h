@@ -92,6 +92,36 @@ int dsv_verify_logits(int32_t batch, int32_t vocab, int32_t dtype, const int64_t
                       const dsv_compact_out* compact, void* workspace, size_t workspace_bytes,
                       dsv_stream_t stream);
 
+/* ---- draft LM head fused with top-k and logsumexp --------------------------------------------
+ * Replaces the materialised `torch.matmul(rows, W.T)` of runtime/worker.py:283-285 followed by
+ * kernels/dspine.py:165-207 topk_ids (and, per vocabulary shard, the local candidates that
+ * sampling/tp_head.py:76-82 TPHead.global_topk merges).  hidden_states [rows, hidden] and
+ * weight [vocab, hidden] are bf16 (hidden a multiple of 64, row pitches multiples of 8
+ * elements, 16-byte aligned bases); the [rows, vocab] logits are never written.
+ * Per row: the k (<= 32) largest logits ranked by their bf16 value (the value torch.matmul
+ * materialises), ties to the lower index, as ids (column + id_offset; pad_id where vocab < k)
+ * and values (fp32 holding the bf16-rounded logit); lse (optional) = logsumexp of the fp32
+ * logits.  sort_ids = 0 gives rank order, 1 ids ascending (topk_ids order).  The workspace
+ * (dsv_lmhead_workspace_size) holds per-CTA partial lists and the error word of
+ * dsv_workspace_error; zero it once (dsv_workspace_init). */
+int dsv_lmhead_workspace_size(int32_t rows, int32_t vocab, int32_t k, size_t* bytes);
+int dsv_lmhead_topk(int32_t rows, int32_t vocab, int32_t hidden, int32_t k,
+                    const void* hidden_states, int64_t hidden_stride, const void* weight,
+                    int64_t weight_stride, int64_t id_offset, int64_t pad_id, int32_t sort_ids,
+                    int64_t* ids, float* values, float* lse, void* workspace,
+                    size_t workspace_bytes, dsv_stream_t stream);
+
+/* ---- vocab-parallel merge --------------------------------------------------------------------
+ * Replaces sampling/tp_head.py:9-14 merge_topk over the all-gathered shard candidates: shard s
+ * contributes, for row r, k candidates (rank order) at values[s * values_shard_stride + r * k],
+ * ids[s * ids_shard_stride + r * k] and its logsumexp lse[s * lse_shard_stride + r].  Output per
+ * row: the global top-k by (value desc, id asc) and the global logsumexp; identical on every
+ * rank that merges the same gathered buffer. */
+int dsv_tp_merge(int32_t rows, int32_t shards, int32_t k, const float* values,
+                 int64_t values_shard_stride, const int64_t* ids, int64_t ids_shard_stride,
+                 const float* lse, int64_t lse_shard_stride, int64_t pad_id, int32_t sort_ids,
+                 int64_t* out_ids, float* out_values, float* out_lse, dsv_stream_t stream);
+
 /* ---- the same verification without a caller workspace ------------------------------------
  * No counterpart in the reference: for callers that cannot allocate device memory (or hand out
  * scratch) at verification time.  Same arguments, outputs and results as dsv_verify_logits,

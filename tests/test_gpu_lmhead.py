@@ -1,0 +1,133 @@
+"""Parity of the fused LM head + top-k + logsumexp (dsv_lmhead_topk, dsv_tp_merge).
+
+Reference semantics (runtime/worker.py:283-285 then kernels/dspine.py:165-207 topk_ids, and
+sampling/tp_head.py:9-14 merge_topk): logits = hidden @ W.T materialised in bf16, top-k by
+value with ties to the lower id.  This is a floating-point contraction, so the oracle is a
+torch reference: the exact (fp64) products rounded to bf16 give the reference ranking keys.
+The kernel accumulates in fp32 on the tensor cores; its bf16 key can differ from the exact
+one only for a logit within the accumulation error of a bf16 rounding midpoint.  Rows whose
+top-k boundary involves no such logit must match exactly (ids bit-exact, values equal); the
+test also requires such rows to be the large majority.  The logsumexp is compared with the
+fp64 logsumexp within 2e-4 absolute (the bf16-input tolerance of the spec is 2e-2).
+"""
+
+import pytest
+import torch
+
+from dspine_b200 import lmhead
+
+pytestmark = pytest.mark.gpu
+
+DEV = "cuda"
+REL_ERR = 2.0 ** -18  # bound on |fp32 tensor-core sum - exact| relative to sum |x_i w_i|
+
+
+def make(M, N, H, seed, wscale=0.02):
+    g = torch.Generator(device=DEV).manual_seed(seed)
+    x = torch.randn(M, H, generator=g, device=DEV).to(torch.bfloat16)
+    w = (torch.randn(N, H, generator=g, device=DEV) * wscale).to(torch.bfloat16)
+    return x, w
+
+
+def bf16(t):
+    return t.float().to(torch.bfloat16).double()
+
+
+def top_by_key(key, k):
+    """(key desc, id asc) order: a stable descending sort keeps ascending ids among ties."""
+    order = torch.sort(key, dim=1, descending=True, stable=True).indices[:, :k]
+    return order, key.gather(1, order)
+
+
+def check_against_exact(x, w, k, ids, vals, lse):
+    """The kernel's fp32 logit f_i lies within d_i = REL_ERR * sum_h |x_h w_ih| of the exact
+    logit L_i, so its ranking key lies in [bf16(L_i - d_i), bf16(L_i + d_i)] (a single value
+    except near a rounding midpoint or for logits near zero).  Checks: every returned value is an admissible key of its id; with
+    the returned keys on the returned ids and the lowest admissible key everywhere else, the
+    top-k by (key desc, id asc) is exactly the returned list; rows with no admissible
+    ambiguity near the cut equal the exact reference; lse within 2e-4 of the fp64 one."""
+    L = x.double() @ w.double().T
+    d = (x.double().abs() @ w.double().abs().T) * REL_ERR
+    lo, hi = bf16(L - d), bf16(L + d)
+    del d
+    M, N = L.shape
+    kk = min(k, N)
+    got_ids, got_val = ids[:, :kk], vals[:, :kk].double()
+    assert ((got_ids >= 0) & (got_ids < N)).all(), "ids out of range"
+    glo, ghi = lo.gather(1, got_ids), hi.gather(1, got_ids)
+    assert ((got_val >= glo) & (got_val <= ghi)).all(), "a returned value is not an admissible key"
+    key = lo.clone()
+    key.scatter_(1, got_ids, got_val)
+    a_ids, _ = top_by_key(key, kk)
+    bad = (a_ids != got_ids).any(dim=1)
+    assert not bad.any(), f"{int(bad.sum())} rows are not a top-{kk} list, first {bad.nonzero()[:4].flatten().tolist()}"
+    # exact comparison where the cut is unambiguous
+    e_ids, e_val = top_by_key(bf16(L), kk)
+    kth = e_val[:, -1:]
+    region = hi >= kth - 1e-30
+    unambiguous = ~((lo != hi) & region).any(dim=1)
+    assert unambiguous.float().mean().item() >= 0.5
+    diff = unambiguous & ((e_ids != got_ids).any(dim=1) | (e_val != got_val).any(dim=1))
+    assert not diff.any(), f"{int(diff.sum())} unambiguous rows differ from the exact top-{kk}"
+    torch.testing.assert_close(lse.double(), torch.logsumexp(L, dim=1), atol=2e-4, rtol=0)
+
+
+def check(M, N, H, k, seed, sort_ids=False):
+    x, w = make(M, N, H, seed)
+    ids, vals, lse = lmhead.lmhead_topk(x, w, k, sort_ids=sort_ids)
+    torch.cuda.synchronize()
+    assert lmhead.workspace_for(M, N, k, DEV).error_word() == 0
+    if sort_ids:
+        r_ids, r_vals, _ = lmhead.lmhead_topk(x, w, k)
+        s_ids, perm = torch.sort(r_ids, dim=1)
+        assert torch.equal(ids, s_ids) and torch.equal(vals, r_vals.gather(1, perm))
+        ids, vals = r_ids, r_vals
+    check_against_exact(x, w, k, ids, vals, lse)
+    return ids, vals, lse
+
+
+@pytest.mark.parametrize("M,N,H,k", [(128, 4096, 64, 8), (128, 5000, 256, 8), (200, 12345, 512, 20),
+                                     (256, 151936, 4096, 8), (384, 33000, 5120, 20),
+                                     (130, 700, 128, 32), (128, 300, 64, 16)])
+def test_lmhead_topk_matches_reference(M, N, H, k):
+    check(M, N, H, k, seed=M * 7 + N)
+
+
+def test_lmhead_sorted_ids_mode():
+    check(128, 9000, 256, 8, seed=3, sort_ids=True)
+
+
+def test_lmhead_config2_full():
+    """Config 2: hidden [1024, 4096] ~ N(0,1), W [151936, 4096] ~ N(0, 0.02^2), top-8 + lse."""
+    check(1024, 151936, 4096, 8, seed=2)
+
+
+def test_lmhead_vocab_smaller_than_k_pads():
+    x, w = make(128, 5, 64, seed=11)
+    ids, vals, lse = lmhead.lmhead_topk(x, w, 8, id_offset=100, pad_id=-1)
+    torch.cuda.synchronize()
+    assert (ids[:, 5:] == -1).all() and torch.isinf(vals[:, 5:]).all()
+    check_against_exact(x, w, 8, ids[:, :5] - 100, vals, lse)
+
+
+@pytest.mark.parametrize("shards", [2, 4, 8])
+def test_shard_merge_equals_full_head(shards):
+    """Vocab-parallel head: per-shard fused heads + dsv_tp_merge == the unsharded head, and
+    merge_topk (the reference's merge, sampling/tp_head.py:9-14) agrees with the merge kernel."""
+    M, N, H, k = 256, 151936, 1024, 20
+    x, w = make(M, N, H, seed=shards)
+    full_ids, full_val, full_lse = lmhead.lmhead_topk(x, w, k)
+    bounds = [N * s // shards for s in range(shards + 1)]
+    parts = [lmhead.lmhead_topk(x, w[bounds[s]:bounds[s + 1]], k, id_offset=bounds[s], pad_id=N)
+             for s in range(shards)]
+    v = torch.stack([p[1] for p in parts])
+    i = torch.stack([p[0] for p in parts])
+    l = torch.stack([p[2] for p in parts])
+    m_ids, m_val, m_lse = lmhead.merge_shards(v, i, l, k, pad_id=N)
+    torch.cuda.synchronize()
+    assert torch.equal(m_ids, full_ids)
+    assert torch.equal(m_val, full_val)
+    torch.testing.assert_close(m_lse, full_lse, atol=1e-5, rtol=0)
+    ref_val, ref_ids = lmhead.merge_topk(v.permute(1, 0, 2).reshape(M, -1),
+                                         i.permute(1, 0, 2).reshape(M, -1), k)
+    assert torch.equal(ref_ids, m_ids) and torch.equal(ref_val, m_val)
