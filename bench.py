@@ -37,6 +37,7 @@ METRIC = "verified draft tokens/s at B=64, block 16, V=151936"
 UNIT = "tokens/s"
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
 FALLBACK_HBM_GBS = 6650.0
+FALLBACK_BF16_TFLOPS = 1590.0
 REF_SAMPLE_REQUESTS = 16
 
 WORKLOADS = {
@@ -45,7 +46,17 @@ WORKLOADS = {
                "top_k {off,1,20,50}, top_p U[0.8,1]; accept-compact of tokens + int32 KV slots",
     "config0": "4 requests x 16, V=151936, fp32 logits, 2 greedy + 2 T=1",
     "config4": "256 requests, SPS-capped verify lengths + early stop 0.3, V=151936, bf16",
+    "config2": "fused draft LM head + top-8 + logsumexp, Qwen3-8B draft shapes: hidden bf16 "
+               "[1024, 4096] ~ N(0,1), W bf16 [151936, 4096] ~ N(0, 0.02^2); logits never written",
+    "config3": "vocab-parallel TP head, TP = --gpus: hidden bf16 [512, 5120] (32 requests x 16), "
+               "W [151936, 5120] ~ N(0, 0.02^2) sharded contiguously; per rank fused top-20 + "
+               "logsumexp, one all-gather, replicated merge and greedy accept on every rank",
 }
+HEAD_SHAPES = {"config2": (1024, 4096, 8, 64), "config3": (512, 5120, 20, 32)}  # rows, H, k, B
+VOCAB = 151936
+HEAD_METRIC = {"config2": "fused LM head + top-8 + logsumexp: hidden rows/s (1024 x 4096 x 151936)",
+               "config3": "vocab-parallel TP head top-20 + logsumexp + accept: draft rows/s "
+                          "(512 x 5120 x 151936)"}
 
 # NVML clock-event reason bits (nvml.h: nvmlClocksEventReason*)
 _REASONS = {
@@ -388,9 +399,229 @@ def cpu_baseline(batch):
                       f"oracle port with {cores} OpenMP threads"}
 
 
+def measured_tensor_peak():
+    f = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(f.read_text())["bf16_tflops"]), "measured (burst)"
+    except Exception:
+        return FALLBACK_BF16_TFLOPS, "fallback"
+
+
+def head_inputs(config, rank, world, device):
+    """Seeded synthetic hidden states and this rank's contiguous weight shard."""
+    import torch
+    rows, H, k, _ = HEAD_SHAPES[config]
+    g = torch.Generator(device="cpu").manual_seed(2 if config == "config2" else 3)
+    hidden = torch.randn(rows, H, generator=g).to(torch.bfloat16)
+    start, end = VOCAB * rank // world, VOCAB * (rank + 1) // world
+    # every rank draws the full weight stream in the same order and keeps its rows, so the
+    # shards of all ranks partition one seeded weight (chunked to bound host memory)
+    shard = torch.empty(end - start, H, dtype=torch.bfloat16)
+    gw = torch.Generator(device="cpu").manual_seed(7)
+    step = 8192
+    for r0 in range(0, VOCAB, step):
+        r1 = min(VOCAB, r0 + step)
+        block = (torch.randn(r1 - r0, H, generator=gw) * 0.02).to(torch.bfloat16)
+        lo, hi = max(r0, start), min(r1, end)
+        if lo < hi:
+            shard[lo - start:hi - start] = block[lo - r0:hi - r0]
+    return hidden.to(device), shard.to(device), start, end
+
+
+def head_cpu_time(config, n_rows, cores):
+    """torch CPU reference: matmul + topk + logsumexp over a row subset (the whole vocab)."""
+    import torch
+    torch.set_num_threads(cores)
+    rows, H, k, _ = HEAD_SHAPES[config]
+    g = torch.Generator(device="cpu").manual_seed(5)
+    x = torch.randn(n_rows, H, generator=g).to(torch.bfloat16)
+    w = (torch.randn(VOCAB, H, generator=g) * 0.02).to(torch.bfloat16)
+
+    def once():
+        t0 = time.perf_counter()
+        logits = torch.matmul(x, w.T)
+        torch.topk(logits.float(), k, dim=1)
+        torch.logsumexp(logits.float(), dim=1)
+        return time.perf_counter() - t0
+    return once
+
+
+def run_head(args):
+    """Configs 2 and 3: the fused LM head (and, for config 3, the vocab-parallel TP head)."""
+    import torch
+    from dspine_b200 import lmhead, _lib, accept
+    rank, local_rank, world = dist_env()
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device (there is no CPU fallback)")
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    rows, H, k, B = HEAD_SHAPES[args.config]
+    dist = None
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    tp = world if args.config == "config3" else 1
+    lib = _lib.load()
+    hidden, shard, start, end = head_inputs(args.config, rank if tp > 1 else 0, tp, dev)
+    group = lmhead.TorchGroup() if tp > 1 else None
+    g = torch.Generator(device="cpu").manual_seed(9)
+    cand = torch.randint(0, VOCAB, (B, 16), generator=g).to(dev)
+    caps = torch.randint(1, 17, (B,), generator=g, dtype=torch.int32).to(dev)
+    outs = accept.new_outputs(B, dev)
+
+    if tp > 1:
+        head = lmhead.TPHead(shard, start, end, VOCAB, group)
+
+        def step():
+            ids, vals, lse = head.topk_lse(hidden, k)
+            accept.accept_greedy(cand, ids[:, 0].view(B, 16), caps, outputs=outs)
+            return ids
+    else:
+        out = (torch.empty(rows, k, dtype=torch.int64, device=dev),
+               torch.empty(rows, k, dtype=torch.float32, device=dev),
+               torch.empty(rows, dtype=torch.float32, device=dev))
+
+        def step():
+            lmhead.lmhead_topk(hidden, shard, k, out=out)
+            if args.config == "config3":
+                accept.accept_greedy(cand, out[0][:, 0].view(B, 16), caps, outputs=outs)
+            return out[0]
+
+    def barrier():
+        if dist is not None:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize(dev)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    barrier()
+    starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
+    launches0 = lib.dsv_launch_count()
+    sampler = ClockSampler(dev)
+    with sampler:
+        for i in range(args.steps):
+            starts[i].record()
+            step()
+            ends[i].record()
+        barrier()
+    launches = lib.dsv_launch_count() - launches0
+    step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
+    total_ms = sum(step_ms)
+    if dist is not None:
+        t = torch.tensor([total_ms, float(launches)], dtype=torch.float64, device=dev)
+        tmax = t.clone()
+        dist.all_reduce(tmax, op=dist.ReduceOp.MAX)
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        total_ms, all_launches = float(tmax[0]), int(t[1])
+    else:
+        all_launches = launches
+    ms_per_step = total_ms / args.steps
+    value = rows / (ms_per_step * 1e-3)
+
+    # end to end: hidden states from pinned host memory, top-k/lse (and accept) read back
+    host_x = hidden.cpu().pin_memory()
+    res = step()
+    host_ids = torch.empty(res.shape, dtype=res.dtype).pin_memory()
+    e2e_steps = max(3, min(args.steps, 20))
+
+    def e2e_step():
+        hidden.copy_(host_x, non_blocking=True)
+        r = step()
+        host_ids.copy_(r, non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+    e2e_step()
+    barrier()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record()
+    barrier()
+    e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    if dist is not None:
+        t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t[0])
+    err = lmhead.workspace_for(rows, end - start, k, dev).error_word()
+    if err:
+        raise SystemExit(f"device error word {err:#x}")
+
+    line = None
+    if rank == 0:
+        flops = 2.0 * rows * (end - start) * H          # this rank's share
+        kernel_ms = statistics.mean(step_ms)
+        achieved = flops / (kernel_ms * 1e-3) / 1e12
+        peak, src = measured_tensor_peak()
+        line = {
+            "metric": HEAD_METRIC[args.config], "value": value, "unit": "rows/s",
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "strong" if tp > 1 else "weak", "vs_baseline": None,
+            "dtype": "bf16 (fp32 accumulate)", "data": "synthetic",
+            "config": {"workload": f"{args.config}: {WORKLOADS[args.config]}",
+                       "rows": rows, "hidden": H, "vocab": VOCAB, "k": k, "tp": tp,
+                       "parallelism": f"tp{tp}" if tp > 1 else "dp1",
+                       "l2": "inputs larger than L2 (weight shard streamed every step)"},
+            "clocks": sampler.summary(),
+            "e2e": {"value": rows / (e2e_ms * 1e-3), "unit": "rows/s",
+                    "h2d_bytes_per_step": host_x.numel() * 2,
+                    "d2h_bytes_per_step": host_ids.numel() * host_ids.element_size()},
+            "gpu_launches": all_launches,
+            "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak,
+                         "unit": "TFLOP/s", "frac": achieved / peak, "traffic": None,
+                         "peak_source": src, "kernel": "dsv::lm::lmhead_kernel (+ merge)",
+                         "flops_per_launch": flops, "kernel_ms": kernel_ms},
+        }
+    if dist is not None:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+    if rank == 0:
+        if world == 1 and not args.no_cpu_baseline:
+            cores = host_cores()
+            n_rows = 16
+            once = head_cpu_time(args.config, n_rows, cores)
+            once()
+            t = min(once() for _ in range(2))
+            line["cpu_baseline"] = {"value": n_rows / t, "unit": "rows/s", "cores": cores,
+                                    "kind": "port",
+                                    "sample": f"{n_rows} rows x full vocab: torch CPU matmul + "
+                                              f"topk + logsumexp, {cores} threads"}
+        print(json.dumps(line), flush=True)
+
+
+def run_head_reference(args):
+    rank, _, world = dist_env()
+    if rank != 0:
+        return
+    cores = host_cores()
+    n_rows = 16
+    once = head_cpu_time(args.config, n_rows, cores)
+    for _ in range(min(args.warmup, 1)):
+        once()
+    times = [once() for _ in range(min(args.steps, 3))]
+    step_s = sum(times) / len(times)
+    value = n_rows / step_s
+    print(json.dumps({
+        "impl": "reference", "metric": HEAD_METRIC[args.config], "value": value, "unit": "rows/s",
+        "n_gpus": args.gpus, "steps": len(times), "warmup": args.warmup,
+        "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "config": {"workload": f"{args.config}: {WORKLOADS[args.config]}", "sample_rows": n_rows,
+                   "parallelism": "host cores"},
+        "cpu_baseline": {"value": value, "unit": "rows/s", "cores": cores, "kind": "port",
+                         "sample": f"{n_rows} rows x full vocab per step: torch CPU matmul + "
+                                   f"topk + logsumexp"},
+        "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }), flush=True)
+
+
 def main():
     args = parse_args()
-    if args.impl == "reference":
+    if args.config in HEAD_SHAPES:
+        run_head_reference(args) if args.impl == "reference" else run_head(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_dspine(args)

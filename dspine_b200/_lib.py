@@ -69,6 +69,13 @@ _SIGNATURES = {
                         c_size_t, c_void_p],
     "dsv_tp_merge": [c_int32, c_int32, c_int32, c_void_p, c_int64, c_void_p, c_int64, c_void_p,
                      c_int64, c_int64, c_int32, c_void_p, c_void_p, c_void_p, c_void_p],
+    "dsv_accept_greedy": [c_int32, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p,
+                          c_void_p, c_void_p, c_void_p, c_void_p, c_void_p],
+    "dsv_uniforms": [c_int32, c_int32, c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_void_p],
+    "dsv_sps_plan": [c_int32, c_void_p, c_void_p, c_int32, c_void_p, c_int32, c_int32, c_void_p,
+                     c_void_p, c_void_p, c_void_p],
+    "dsv_accept_compact": [c_int32, c_void_p, c_void_p, c_void_p, ctypes.POINTER(CompactOut),
+                           c_void_p, c_void_p],
     "dsv_verify_logits_noalloc": [c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p,
                                   c_int64, c_void_p, c_void_p, c_int64, c_int64, c_void_p,
                                   c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

@@ -237,6 +237,63 @@ int dsv_tp_merge(int32_t rows, int32_t shards, int32_t k, const float* values,
     return counted(dsv::launch_topk_merge(m, (cudaStream_t)stream), 1);
 }
 
+int dsv_accept_greedy(int32_t batch, const int64_t* candidates, const int64_t* top1,
+                      int64_t top1_stride, const int32_t* verify_lens, const int32_t* prefix_lens,
+                      int32_t* accept, int32_t* commit, int64_t* bonus, int64_t* output,
+                      int32_t* new_seq, dsv_stream_t stream) {
+    if (batch < 0 || top1_stride < 1) return DSV_BAD_SHAPE;
+    if (batch == 0) return DSV_OK;
+    if (!candidates || !top1 || !verify_lens || !prefix_lens || !accept || !commit || !bonus ||
+        !output || !new_seq)
+        return DSV_BAD_POINTER;
+    dsv::GreedyArgs g = {batch, candidates, top1, top1_stride, verify_lens, prefix_lens,
+                         accept, commit, bonus, output, new_seq};
+    return counted(dsv::launch_greedy(g, (cudaStream_t)stream), 1);
+}
+
+int dsv_uniforms(int32_t n, int32_t width, const int64_t* seeds, const void* positions,
+                 int32_t positions_int64, int32_t stream_id, float* out, dsv_stream_t stream) {
+    if (n < 0 || width < 1 || width >= 65536 || stream_id < 0 || stream_id > 3) return DSV_BAD_SHAPE;
+    if (n == 0) return DSV_OK;
+    if (!seeds || !positions || !out) return DSV_BAD_POINTER;
+    return counted(dsv::launch_uniforms(n, width, seeds, positions, positions_int64 != 0,
+                                        stream_id, out, (cudaStream_t)stream),
+                   1);
+}
+
+int dsv_sps_plan(int32_t batch, const float* raw, const float* table, int32_t nbins,
+                 const float* boundaries, int32_t nbound, int32_t budget, int32_t* verify_lens,
+                 int64_t* qo_indptr, int64_t* index, dsv_stream_t stream) {
+    if (batch < 1 || batch > dsv::sps_max_batch() || nbins < 1) return DSV_BAD_SHAPE;
+    if (budget < batch || budget > batch * 16) return DSV_BAD_SHAPE;
+    if (boundaries && nbound < 0) return DSV_BAD_SHAPE;
+    if (!raw || !table || !verify_lens || !qo_indptr || !index) return DSV_BAD_POINTER;
+    return counted(dsv::launch_sps(batch, raw, table, nbins, boundaries, boundaries ? nbound : 0,
+                                   budget, verify_lens, qo_indptr, index, (cudaStream_t)stream),
+                   1);
+}
+
+int dsv_accept_compact(int32_t batch, const int32_t* commit, const int32_t* verify_lens,
+                       const int64_t* output, const dsv_compact_out* compact, void* workspace,
+                       dsv_stream_t stream) {
+    if (batch < 0) return DSV_BAD_SHAPE;
+    if (batch == 0) return DSV_OK;
+    if (!commit || !verify_lens || !output || !compact || !workspace) return DSV_BAD_POINTER;
+    if (compact->slots_len < 0) return DSV_BAD_SHAPE;
+    if (!compact->slots || !compact->slot_row || !compact->tokens || !compact->kept_slots ||
+        !compact->offsets || !compact->freed_slots || !compact->freed_offsets)
+        return DSV_BAD_POINTER;
+    if (!aligned(workspace, 16)) return DSV_BAD_ALIGNMENT;
+    unsigned int* err = reinterpret_cast<unsigned int*>(static_cast<char*>(workspace) +
+                                                        offsetof(dsv::WsHeader, err));
+    return counted(dsv::launch_compact(batch, commit, verify_lens, output, compact->slots,
+                                       compact->slots_len, compact->slot_row, compact->tokens,
+                                       compact->kept_slots, compact->offsets,
+                                       compact->freed_slots, compact->freed_offsets, err,
+                                       (cudaStream_t)stream),
+                   1);
+}
+
 int dsv_verify_logits_noalloc(int32_t batch, int32_t vocab, int32_t dtype,
                               const int64_t* candidates, const void* target_logits,
                               const int64_t* target_row, int64_t target_rows,

@@ -134,4 +134,30 @@ struct TopkMergeArgs {
 };
 int launch_topk_merge(const TopkMergeArgs& m, cudaStream_t stream);
 
+// ---- per-request steps (small.cu) -----------------------------------------------------------
+struct GreedyArgs {
+    int B;
+    const int64_t* cand;       // [B,16]
+    const int64_t* top1;       // top-1 id of (b, s) at top1[(b * 16 + s) * top1_stride]
+    long long top1_stride;
+    const int32_t* caps;       // [B]
+    const int32_t* prefix;     // [B]
+    int32_t* accept;
+    int32_t* commit;
+    int64_t* bonus;
+    int64_t* output;           // [B,16]
+    int32_t* new_seq;
+};
+int launch_greedy(const GreedyArgs& g, cudaStream_t stream);
+int launch_uniforms(int n, int width, const int64_t* seeds, const void* positions, int pos64,
+                    int stream_id, float* out, cudaStream_t stream);
+int sps_max_batch();
+int launch_sps(int B, const float* raw, const float* table, int nbins, const float* bounds,
+               int nbound, int budget, int32_t* lens, int64_t* qo, int64_t* index,
+               cudaStream_t stream);
+int launch_compact(int B, const int32_t* commit, const int32_t* lens, const int64_t* output,
+                   const int32_t* slots, long long slots_len, const int64_t* slot_row,
+                   int64_t* tok_out, int32_t* slot_out, int32_t* offsets, int32_t* free_out,
+                   int32_t* free_offsets, unsigned int* err, cudaStream_t stream);
+
 }  // namespace dsv

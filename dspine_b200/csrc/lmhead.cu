@@ -529,13 +529,10 @@ void geometry(int M, int N, int* mt, int* nsplit, int* ntiles) {
 
 template <int TK>
 int launch_tk(const CUtensorMap& mx, const CUtensorMap& mw, const LmArgs& a, cudaStream_t st) {
-    static std::once_flag once;
-    static cudaError_t attr = cudaSuccess;
-    std::call_once(once, [] {
-        attr = cudaFuncSetAttribute(lmhead_kernel<TK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    kSmemBytes);
-    });
-    if (attr != cudaSuccess) return kLaunchFailed;
+    // per launch: the attribute belongs to the current device, and the call is cheap
+    if (cudaFuncSetAttribute(lmhead_kernel<TK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             kSmemBytes) != cudaSuccess)
+        return kLaunchFailed;
     lmhead_kernel<TK><<<a.mt * a.nsplit, kThreads, kSmemBytes, st>>>(mx, mw, a);
     return cudaGetLastError() == cudaSuccess ? 0 : kLaunchFailed;
 }

@@ -1,0 +1,291 @@
+// small.cu -- the per-request (not per-logit) steps around verification (sm_100a).
+//
+//   greedy_kernel    capped greedy accept from target top-1 ids
+//                    (verification/caps.py:32-59 _accept_capped, verification/ragged.py:51-76)
+//   uniforms_kernel  request-seeded uniforms: MurmurHash3 (x86_32) mixing of the seed's two
+//                    32-bit halves, the position and (column + stream << 16), finalised with
+//                    fmix32(h ^ 16), value = (bits >> 8) * 2^-24
+//                    (sampling/random.py:22-91 seeded_uniforms / _cpu_uniforms)
+//   sps_kernel       SPS verify lengths: conditional acceptance per (request, depth) from a bin
+//                    table, survival = cumulative product then running minimum, stable
+//                    descending rank of all B x 15 survivals, lens = 1 + selected per request,
+//                    plus qo_indptr and the token index (verification/sps.py:27-58)
+//   compact_kernel   accept-compact of tokens and KV slots by the exclusive scan of commit
+//                    (SGLang's _commit_accept, wrapped at runtime/worker.py:745-777)
+//
+// Every kernel is small (B requests, at most a few thousand entries); the cost is launch
+// latency, so each is one launch with no host synchronisation.
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "dsv_common.cuh"
+#include "dsv_kernels.h"
+
+namespace dsv {
+namespace sm {
+
+constexpr int kT = 16;  // draft block: anchor + 15 drafts
+
+__device__ __forceinline__ int clamp_cap(int c) { return c < 1 ? 1 : (c > kT ? kT : c); }
+
+__global__ void greedy_kernel(int B, const int64_t* __restrict__ cand, const int64_t* __restrict__ top1,
+                              long long top1_stride, const int32_t* __restrict__ caps,
+                              const int32_t* __restrict__ prefix, int32_t* accept, int32_t* commit,
+                              int64_t* bonus, int64_t* output, int32_t* new_seq) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= B) return;
+    const int cap = clamp_cap(caps[b]);
+    const int64_t* c = cand + (int64_t)b * kT;
+    const int64_t* t = top1 + (int64_t)b * kT * top1_stride;
+    int a = cap - 1;
+    for (int i = 0; i < cap - 1; ++i)
+        if (c[i + 1] != t[i * top1_stride]) {
+            a = i;
+            break;
+        }
+    const int64_t bo = t[a * top1_stride];
+    accept[b] = a;
+    commit[b] = a + 1;
+    bonus[b] = bo;
+    for (int i = 0; i < kT; ++i) output[(int64_t)b * kT + i] = (i == a) ? bo : (i < kT - 1 ? c[i + 1] : 0);
+    new_seq[b] = prefix[b] + a + 1;
+}
+
+__device__ __forceinline__ uint32_t rotl32(uint32_t x, int r) { return (x << r) | (x >> (32 - r)); }
+
+__device__ __forceinline__ uint32_t murmur_block(uint32_t h, uint32_t k) {
+    k *= 0xCC9E2D51u;
+    k = rotl32(k, 15);
+    k *= 0x1B873593u;
+    h ^= k;
+    h = rotl32(h, 13);
+    return h * 5u + 0xE6546B64u;
+}
+
+__device__ __forceinline__ uint32_t fmix32(uint32_t h) {
+    h ^= h >> 16;
+    h *= 0x85EBCA6Bu;
+    h ^= h >> 13;
+    h *= 0xC2B2AE35u;
+    h ^= h >> 16;
+    return h;
+}
+
+template <typename PosT>
+__global__ void uniforms_kernel(int n, int width, const int64_t* __restrict__ seeds,
+                                const PosT* __restrict__ positions, uint32_t stream, float* out) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= (int64_t)n * width) return;
+    const int r = (int)(i / width), col = (int)(i % width);
+    const uint64_t s = (uint64_t)seeds[r];
+    uint32_t h = 0;
+    h = murmur_block(h, (uint32_t)(s & 0xFFFFFFFFu));
+    h = murmur_block(h, (uint32_t)(s >> 32));
+    h = murmur_block(h, (uint32_t)((uint64_t)(int64_t)positions[r] & 0xFFFFFFFFu));
+    h = murmur_block(h, (uint32_t)col + (stream << 16));
+    const uint32_t bits = fmix32(h ^ 16u);
+    out[i] = (float)(bits >> 8) * 5.9604644775390625e-08f;  // 2^-24
+}
+
+constexpr int kSpsThreads = 1024;
+constexpr int kSpsMaxB = 1024;
+constexpr int kSpsG = kT - 1;                  // drafted depths per request
+constexpr int kSpsSort = 16384;                // >= kSpsMaxB * kSpsG, power of two
+
+// one CTA: survivals -> stable descending order -> lens, qo_indptr, index
+__global__ void __launch_bounds__(kSpsThreads, 1)
+    sps_kernel(int B, const float* __restrict__ raw, const float* __restrict__ table, int nbins,
+               const float* __restrict__ bounds, int nbound, int budget, int32_t* lens,
+               int64_t* qo, int64_t* index) {
+    extern __shared__ uint64_t keys[];         // [kSpsSort]: (~survival bits) << 32 | d * B + b
+    __shared__ int32_t cnt[kSpsMaxB];
+    __shared__ int64_t scan[kSpsThreads];
+    const int tid = threadIdx.x;
+    const int n = B * kSpsG;
+    int sort_n = 1;
+    while (sort_n < n) sort_n <<= 1;
+    for (int b = tid; b < B; b += kSpsThreads) {
+        // survival of request b at every depth, position-major index d * B + b
+        double run = 1.0;
+        float mn = INFINITY;
+        for (int d = 0; d < kSpsG; ++d) {
+            const float x = raw[b * kSpsG + d];
+            int bin;
+            if (bounds) {
+                bin = 0;
+                while (bin < nbound && bounds[bin] < x) ++bin;
+            } else {
+                const float sc = x * (float)nbins;
+                long long t = (sc != sc) ? 0 : (long long)sc;
+                if (sc != sc) t = 0;
+                t = t < 0 ? 0 : (t > nbins - 1 ? nbins - 1 : t);
+                bin = (int)t;
+            }
+            const float cond = table[d * nbins + bin];
+            run = (d == 0) ? (double)cond : run * (double)cond;
+            const float pre = (float)run;
+            mn = (d == 0 || pre < mn) ? pre : mn;
+            // survival is >= 0: its float bits order like the value; descending -> complement
+            const uint32_t okey = 0xFFFFFFFFu - __float_as_uint(mn);
+            keys[d * B + b] = ((uint64_t)okey << 32) | (uint32_t)(d * B + b);
+        }
+        cnt[b] = 1;
+    }
+    for (int i = n + tid; i < sort_n; i += kSpsThreads) keys[i] = ~0ull;
+    __syncthreads();
+    // bitonic sort, ascending
+    for (int size = 2; size <= sort_n; size <<= 1) {
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            for (int i = tid; i < sort_n; i += kSpsThreads) {
+                const int j = i ^ stride;
+                if (j > i) {
+                    const bool up = (i & size) == 0;
+                    const uint64_t a = keys[i], c = keys[j];
+                    if ((a > c) == up) {
+                        keys[i] = c;
+                        keys[j] = a;
+                    }
+                }
+            }
+            __syncthreads();
+        }
+    }
+    for (int j = tid; j < budget - B; j += kSpsThreads) {
+        const uint32_t idx = (uint32_t)keys[j];
+        atomicAdd(&cnt[idx % B], 1);
+    }
+    __syncthreads();
+    // exclusive scan of lens -> qo (B <= 1024: one entry per thread)
+    const int64_t my = tid < B ? cnt[tid] : 0;
+    scan[tid] = my;
+    __syncthreads();
+    for (int o = 1; o < kSpsThreads; o <<= 1) {
+        const int64_t v = tid >= o ? scan[tid - o] : 0;
+        __syncthreads();
+        scan[tid] += v;
+        __syncthreads();
+    }
+    if (tid < B) {
+        lens[tid] = (int32_t)my;
+        const int64_t start = scan[tid] - my;
+        qo[tid + 1] = scan[tid];
+        for (int t = 0; t < my; ++t) index[start + t] = (int64_t)tid * kT + t;
+    }
+    if (tid == 0) qo[0] = 0;
+}
+
+constexpr int kCompactThreads = 1024;
+
+// one CTA: exclusive scans of commit and of the freed counts, then the packed copies
+__global__ void __launch_bounds__(kCompactThreads, 1)
+    compact_kernel(int B, const int32_t* __restrict__ commit, const int32_t* __restrict__ lens,
+                   const int64_t* __restrict__ output, const int32_t* __restrict__ slots,
+                   long long slots_len, const int64_t* __restrict__ slot_row, int64_t* tok_out,
+                   int32_t* slot_out, int32_t* offsets, int32_t* free_out, int32_t* free_offsets,
+                   unsigned int* err) {
+    __shared__ int32_t sc[kCompactThreads], sf[kCompactThreads];
+    __shared__ int32_t carry_c, carry_f;
+    const int tid = threadIdx.x;
+    if (tid == 0) {
+        carry_c = 0;
+        carry_f = 0;
+        offsets[0] = 0;
+        free_offsets[0] = 0;
+    }
+    __syncthreads();
+    for (int base = 0; base < B; base += kCompactThreads) {
+        const int b = base + tid;
+        int c = 0, f = 0;
+        if (b < B) {
+            c = commit[b];
+            f = lens[b] - c;
+            f = f < 0 ? 0 : f;
+        }
+        sc[tid] = c;
+        sf[tid] = f;
+        __syncthreads();
+        for (int o = 1; o < kCompactThreads; o <<= 1) {
+            const int vc = tid >= o ? sc[tid - o] : 0, vf = tid >= o ? sf[tid - o] : 0;
+            __syncthreads();
+            sc[tid] += vc;
+            sf[tid] += vf;
+            __syncthreads();
+        }
+        if (b < B) {
+            const int oc = carry_c + sc[tid] - c, of = carry_f + sf[tid] - f;
+            offsets[b + 1] = oc + c;
+            free_offsets[b + 1] = of + f;
+            const int64_t row = slot_row[b];
+            for (int i = 0; i < c; ++i) {
+                tok_out[oc + i] = output[(int64_t)b * kT + i];
+                const long long p = row + i;
+                int32_t sl = -1;
+                if (p >= 0 && p < slots_len) sl = slots[p];
+                else atomicOr(err, 4u);
+                slot_out[oc + i] = sl;
+            }
+            for (int j = 0; j < f; ++j) {
+                const long long p = row + c + j;
+                int32_t sl = -1;
+                if (p >= 0 && p < slots_len) sl = slots[p];
+                else atomicOr(err, 4u);
+                free_out[of + j] = sl;
+            }
+        }
+        __syncthreads();
+        if (tid == kCompactThreads - 1) {
+            carry_c += sc[tid];
+            carry_f += sf[tid];
+        }
+        __syncthreads();
+    }
+}
+
+}  // namespace sm
+
+int launch_greedy(const GreedyArgs& g, cudaStream_t st) {
+    const int threads = 128;
+    sm::greedy_kernel<<<(g.B + threads - 1) / threads, threads, 0, st>>>(
+        g.B, g.cand, g.top1, g.top1_stride, g.caps, g.prefix, g.accept, g.commit, g.bonus,
+        g.output, g.new_seq);
+    return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
+}
+
+int launch_uniforms(int n, int width, const int64_t* seeds, const void* positions, int pos64,
+                    int stream_id, float* out, cudaStream_t st) {
+    const int64_t total = (int64_t)n * width;
+    const int threads = 256;
+    const unsigned blocks = (unsigned)((total + threads - 1) / threads);
+    if (pos64)
+        sm::uniforms_kernel<int64_t><<<blocks, threads, 0, st>>>(
+            n, width, seeds, static_cast<const int64_t*>(positions), (uint32_t)stream_id, out);
+    else
+        sm::uniforms_kernel<int32_t><<<blocks, threads, 0, st>>>(
+            n, width, seeds, static_cast<const int32_t*>(positions), (uint32_t)stream_id, out);
+    return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
+}
+
+int sps_max_batch() { return sm::kSpsMaxB; }
+
+int launch_sps(int B, const float* raw, const float* table, int nbins, const float* bounds,
+               int nbound, int budget, int32_t* lens, int64_t* qo, int64_t* index,
+               cudaStream_t st) {
+    if (cudaFuncSetAttribute(sm::sps_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             sm::kSpsSort * 8) != cudaSuccess)
+        return kLaunchFailed;
+    sm::sps_kernel<<<1, sm::kSpsThreads, sm::kSpsSort * 8, st>>>(B, raw, table, nbins, bounds,
+                                                                 nbound, budget, lens, qo, index);
+    return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
+}
+
+int launch_compact(int B, const int32_t* commit, const int32_t* lens, const int64_t* output,
+                   const int32_t* slots, long long slots_len, const int64_t* slot_row,
+                   int64_t* tok_out, int32_t* slot_out, int32_t* offsets, int32_t* free_out,
+                   int32_t* free_offsets, unsigned int* err, cudaStream_t st) {
+    sm::compact_kernel<<<1, sm::kCompactThreads, 0, st>>>(B, commit, lens, output, slots, slots_len,
+                                                           slot_row, tok_out, slot_out, offsets,
+                                                           free_out, free_offsets, err);
+    return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
+}
+
+}  // namespace dsv

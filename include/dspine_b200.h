@@ -122,6 +122,43 @@ int dsv_tp_merge(int32_t rows, int32_t shards, int32_t k, const float* values,
                  const float* lse, int64_t lse_shard_stride, int64_t pad_id, int32_t sort_ids,
                  int64_t* out_ids, float* out_values, float* out_lse, dsv_stream_t stream);
 
+/* ---- greedy capped accept ----------------------------------------------------------------------
+ * Replaces verification/caps.py:32-59 _accept_capped (and verification/ragged.py:51-76 _accept):
+ * with top1 of (b, s) at top1[(b * 16 + s) * top1_stride] (e.g. column 0 of a [B*16, k] top-k
+ * id array with top1_stride = k), accepted = first s < cap-1 with cand[b, s+1] != top1(b, s),
+ * else cap-1; bonus = top1(b, accepted); output keeps the proposed tokens around the bonus.
+ * Same five outputs as dsv_verify_logits. */
+int dsv_accept_greedy(int32_t batch, const int64_t* candidates, const int64_t* top1,
+                      int64_t top1_stride, const int32_t* verify_lens, const int32_t* prefix_lens,
+                      int32_t* accept, int32_t* commit, int64_t* bonus, int64_t* output,
+                      int32_t* new_seq, dsv_stream_t stream);
+
+/* ---- request-seeded uniforms -------------------------------------------------------------------
+ * Replaces sampling/random.py:22-91 seeded_uniforms (bit-exact with its _cpu_uniforms):
+ * out[r, c] for r < n, c < width from seeds[r] (int64), positions[r] (int32, or int64 when
+ * positions_int64) and stream_id (DRAFT 0, ACCEPT 1, BONUS 2, PREFILL 3). */
+int dsv_uniforms(int32_t n, int32_t width, const int64_t* seeds, const void* positions,
+                 int32_t positions_int64, int32_t stream_id, float* out, dsv_stream_t stream);
+
+/* ---- SPS verify-length plan --------------------------------------------------------------------
+ * Replaces verification/sps.py:35-58 allocate_verify_lens and the index of sps.py:61-99
+ * device_plan: raw [B, 15] draft confidences, table [15, nbins] conditional acceptance,
+ * optional boundaries [nbound] (bucketize; NULL: linear bins), budget in [B, 16 B].
+ * Outputs verify_lens [B], qo_indptr [B+1] and index [budget] (index[qo[b] + t] = b * 16 + t).
+ * B <= 1024; one launch. */
+int dsv_sps_plan(int32_t batch, const float* raw, const float* table, int32_t nbins,
+                 const float* boundaries, int32_t nbound, int32_t budget, int32_t* verify_lens,
+                 int64_t* qo_indptr, int64_t* index, dsv_stream_t stream);
+
+/* ---- accept-compact on its own -----------------------------------------------------------------
+ * The compaction of dsv_compact_out after any accept step (e.g. dsv_accept_greedy): tokens
+ * output[b, :commit_b] and KV slots of positions [0, commit_b) packed by the exclusive scan of
+ * commit; positions [commit_b, verify_len_b) freed.  Slot positions outside slots_len read as
+ * -1 and set bit 2 of the error word of `workspace` (any zeroed dsv workspace). */
+int dsv_accept_compact(int32_t batch, const int32_t* commit, const int32_t* verify_lens,
+                       const int64_t* output, const dsv_compact_out* compact, void* workspace,
+                       dsv_stream_t stream);
+
 /* ---- the same verification without a caller workspace ------------------------------------
  * No counterpart in the reference: for callers that cannot allocate device memory (or hand out
  * scratch) at verification time.  Same arguments, outputs and results as dsv_verify_logits,
