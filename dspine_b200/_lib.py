@@ -69,6 +69,9 @@ _SIGNATURES = {
                         c_size_t, c_void_p],
     "dsv_tp_merge": [c_int32, c_int32, c_int32, c_void_p, c_int64, c_void_p, c_int64, c_void_p,
                      c_int64, c_int64, c_int32, c_void_p, c_void_p, c_void_p, c_void_p],
+    "dsv_chain_from_probs": [c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                             c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                             c_void_p],
     "dsv_accept_greedy": [c_int32, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p,
                           c_void_p, c_void_p, c_void_p, c_void_p, c_void_p],
     "dsv_uniforms": [c_int32, c_int32, c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_void_p],

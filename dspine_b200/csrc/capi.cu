@@ -237,6 +237,24 @@ int dsv_tp_merge(int32_t rows, int32_t shards, int32_t k, const float* values,
     return counted(dsv::launch_topk_merge(m, (cudaStream_t)stream), 1);
 }
 
+int dsv_chain_from_probs(int32_t batch, int32_t vocab, const int64_t* candidates,
+                         const float* target_probs, const float* draft_probs,
+                         const int32_t* verify_lens, const float* uniforms,
+                         const float* uniform_final, const int32_t* prefix_lens, int32_t* accept,
+                         int32_t* commit, int64_t* bonus, int64_t* output, int32_t* new_seq,
+                         dsv_stream_t stream) {
+    if (batch < 0 || vocab < 1 || vocab > dsv::chain_probs_max_vocab()) return DSV_BAD_SHAPE;
+    if (batch == 0) return DSV_OK;
+    if (!candidates || !target_probs || !draft_probs || !verify_lens || !uniforms ||
+        !uniform_final || !prefix_lens || !accept || !commit || !bonus || !output || !new_seq)
+        return DSV_BAD_POINTER;
+    if (!aligned(target_probs, 4) || !aligned(draft_probs, 4)) return DSV_BAD_ALIGNMENT;
+    dsv::ChainProbsArgs c = {batch, vocab, candidates, target_probs, draft_probs, verify_lens,
+                             uniforms, uniform_final, prefix_lens, accept, commit, bonus,
+                             output, new_seq};
+    return counted(dsv::launch_chain_probs(c, (cudaStream_t)stream), 1);
+}
+
 int dsv_accept_greedy(int32_t batch, const int64_t* candidates, const int64_t* top1,
                       int64_t top1_stride, const int32_t* verify_lens, const int32_t* prefix_lens,
                       int32_t* accept, int32_t* commit, int64_t* bonus, int64_t* output,

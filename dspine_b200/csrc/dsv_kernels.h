@@ -134,6 +134,25 @@ struct TopkMergeArgs {
 };
 int launch_topk_merge(const TopkMergeArgs& m, cudaStream_t stream);
 
+// ---- chain rejection from dense probabilities (probs.cu) -------------------------------------
+struct ChainProbsArgs {
+    int B, V;
+    const int64_t* cand;   // [B,16]
+    const float* target;   // [B,16,V]
+    const float* draft;    // [B,15,V]
+    const int32_t* caps;   // [B]
+    const float* u;        // [B,15]
+    const float* uf;       // [B]
+    const int32_t* prefix; // [B]
+    int32_t* accept;
+    int32_t* commit;
+    int64_t* bonus;
+    int64_t* output;
+    int32_t* new_seq;
+};
+int chain_probs_max_vocab();
+int launch_chain_probs(const ChainProbsArgs& c, cudaStream_t stream);
+
 // ---- per-request steps (small.cu) -----------------------------------------------------------
 struct GreedyArgs {
     int B;

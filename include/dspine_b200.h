@@ -122,6 +122,20 @@ int dsv_tp_merge(int32_t rows, int32_t shards, int32_t k, const float* values,
                  const float* lse, int64_t lse_shard_stride, int64_t pad_id, int32_t sort_ids,
                  int64_t* out_ids, float* out_values, float* out_lse, dsv_stream_t stream);
 
+/* ---- capped chain rejection from dense probabilities ---------------------------------------
+ * Replaces sampling/rejection.py:101-153 sample_capped_chain_from_probs (_sample_capped_chain,
+ * :12-98): target_probs [B,16,V] and draft_probs [B,15,V] fp32, contiguous.  Draft s+1 is
+ * accepted while q in (0,1] and uniforms[b,s] * q < p (at most verify_lens[b]-1 drafts); the
+ * bonus is the first index whose running exact (2^-40 fixed point) mass of max(p - clamp01(q), 0)
+ * exceeds floor(uniform_final * total) (p itself after a fully accepted block or a zero
+ * residual; V-1 when no index does).  Same five outputs as dsv_verify_logits.  V <= 2^20. */
+int dsv_chain_from_probs(int32_t batch, int32_t vocab, const int64_t* candidates,
+                         const float* target_probs, const float* draft_probs,
+                         const int32_t* verify_lens, const float* uniforms,
+                         const float* uniform_final, const int32_t* prefix_lens, int32_t* accept,
+                         int32_t* commit, int64_t* bonus, int64_t* output, int32_t* new_seq,
+                         dsv_stream_t stream);
+
 /* ---- greedy capped accept ----------------------------------------------------------------------
  * Replaces verification/caps.py:32-59 _accept_capped (and verification/ragged.py:51-76 _accept):
  * with top1 of (b, s) at top1[(b * 16 + s) * top1_stride] (e.g. column 0 of a [B*16, k] top-k
