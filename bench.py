@@ -408,24 +408,19 @@ def measured_tensor_peak():
 
 
 def head_inputs(config, rank, world, device):
-    """Seeded synthetic hidden states and this rank's contiguous weight shard."""
+    """Seeded synthetic hidden states and this rank's contiguous weight shard.  Every rank
+    draws the same full weight on its GPU (one seeded generator) and keeps its rows, so the
+    shards of all ranks partition one weight."""
     import torch
     rows, H, k, _ = HEAD_SHAPES[config]
-    g = torch.Generator(device="cpu").manual_seed(2 if config == "config2" else 3)
-    hidden = torch.randn(rows, H, generator=g).to(torch.bfloat16)
+    g = torch.Generator(device=device).manual_seed(2 if config == "config2" else 3)
+    hidden = torch.randn(rows, H, generator=g, device=device).to(torch.bfloat16)
     start, end = VOCAB * rank // world, VOCAB * (rank + 1) // world
-    # every rank draws the full weight stream in the same order and keeps its rows, so the
-    # shards of all ranks partition one seeded weight (chunked to bound host memory)
-    shard = torch.empty(end - start, H, dtype=torch.bfloat16)
-    gw = torch.Generator(device="cpu").manual_seed(7)
-    step = 8192
-    for r0 in range(0, VOCAB, step):
-        r1 = min(VOCAB, r0 + step)
-        block = (torch.randn(r1 - r0, H, generator=gw) * 0.02).to(torch.bfloat16)
-        lo, hi = max(r0, start), min(r1, end)
-        if lo < hi:
-            shard[lo - start:hi - start] = block[lo - r0:hi - r0]
-    return hidden.to(device), shard.to(device), start, end
+    full = (torch.randn(VOCAB, H, generator=g, device=device) * 0.02).to(torch.bfloat16)
+    shard = full[start:end].contiguous()
+    del full
+    torch.cuda.empty_cache()
+    return hidden, shard, start, end
 
 
 def head_cpu_time(config, n_rows, cores):
