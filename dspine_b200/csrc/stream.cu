@@ -214,9 +214,10 @@ __device__ int request_cat(const VerifyArgs& a, int b, float& c_out, int wink) {
     const float c = log2e_over(T);
     c_out = c;
     if (is_greedy(T, k, c)) return kGreedy;
-    if (k >= a.V && !(a.top_p[b] < 1.0f)) return kKeepAll;
-    if (k <= wink) return kWindow;
-    return kBinned;
+    if (a.top_p[b] < 1.0f) return kBinned;    // nucleus (any k): per-key histogram walk
+    if (k >= a.V) return kKeepAll;
+    if (k <= wink) return kWindow;            // pure top-k, small k: candidate window
+    return kBinned;                           // pure top-k, large k: exact counts from the top
 }
 
 // every CTA builds the same task table: binned rows first, then keep-all/window, then greedy
@@ -419,7 +420,20 @@ constexpr int kRT = 256;           // threads per CTA
 constexpr int kRW = kRT / 32;      // warps
 constexpr int kRWinK = kRT;        // top-k rows with k <= 256 select inside the window
 constexpr int kRWinCap = 1024;     // window candidates per row
-constexpr int kRKeyCap = 2048;     // keys per level-3 histogram chunk
+constexpr int kRKeyCap = 2048;     // keys per chunk of an exact count walk (count_walk)
+constexpr int kHCap = 8192;        // per-key histogram bins (32 KB)
+// one-pass histogram: fine bins for 2^-20 <= |v| < 2^12 (4096 keys per sign), the band
+// |v| < 2^-20 listed element by element (at most kBandCap), -inf ignored, anything else
+// (|v| >= 2^12, +inf, NaN) falls back to the max pass + adaptive histogram
+constexpr uint32_t kFB = 0xB580u;     // key of +2^-20
+constexpr uint32_t kFTop = 0xC57Fu;   // key of the largest bf16 below +2^12
+constexpr uint32_t kFNB = 0x4A7Fu;    // key of -2^-20
+constexpr uint32_t kFNLow = 0x3A80u;  // key of the smallest bf16 above -2^12
+constexpr uint32_t kFPos = kFTop - kFB + 1u;  // 4096
+constexpr uint32_t kNInfRaw = 0x007Fu;        // key of -inf
+constexpr int kBandCap = 512;
+static_assert(kFPos == 4096u && kFNB - kFNLow + 1u == 4096u && 2 * kFPos == (uint32_t)kHCap,
+              "fixed histogram geometry");
 constexpr int kRingS = 4;          // streaming ring: slots
 constexpr int kRingCW = 512;       // vectors (16 B) per slot: 8 KB
 
@@ -435,11 +449,14 @@ struct RSmem {
     unsigned long long self64[8];
     uint32_t wc[32];
     unsigned long long wm[32];
-    uint32_t bcnt[kBins];
+    uint32_t nband;                // one-pass histogram: band elements listed
+    uint32_t outside;              //                     a value outside the fixed range
+    uint16_t band[kBandCap];       //                     the band's raw values
+    uint32_t zcnt;                 // histogram band: elements
+    unsigned long long zmass;      //                 exact mass
     uint32_t wkey[kRWinCap];       // window candidates: key
     uint32_t widx[kRWinCap];       //                    element index
-    alignas(16) uint2 acc[kBins * kRT];     // private bin accumulators / window sort area
-    alignas(16) uint32_t khist[kRKeyCap];   // key counts
+    alignas(16) uint32_t hist[kHCap];       // per-key counts / window sort area / count chunks
     alignas(16) uint4 ring[kRingS][kRingCW];  // streaming ring filled by bulk copies
     alignas(8) uint64_t ring_bar[kRingS];
     uint32_t ring_cnt;                      // chunks consumed so far (slot, phase)
@@ -531,46 +548,6 @@ __device__ __forceinline__ unsigned long long rcta_sum_u64(unsigned long long v,
 #pragma unroll
     for (int i = 0; i < kRW; ++i) s += sh->red64[i];
     return s;
-}
-
-// reduce the private accumulators of nb bins into (mass, count) pairs in wm/wc
-__device__ void reduce_bins(RSmem* sh, int nb, uint32_t fill_last) {
-    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-    __syncthreads();
-    for (int bin = wid; bin < nb; bin += kRW) {
-        long long sm = 0;
-        for (int i = lane; i < kRT; i += 32) {
-            const uint2 v = sh->acc[bin * kRT + i];
-            sm += (long long)v.x * 8388608 + (int32_t)v.y;
-        }
-        sm = (long long)warp_sum_u64((unsigned long long)sm);
-        if (lane == 0) {
-            sh->wm[bin] = (unsigned long long)sm;
-            sh->wc[bin] = sh->bcnt[bin] - (bin == nb - 1 ? fill_last : 0u);
-        }
-    }
-    if (tid < 32 && tid >= nb) {
-        sh->wm[tid] = 0ull;
-        sh->wc[tid] = 0u;
-    }
-    __syncthreads();
-}
-
-__device__ __forceinline__ void clear_bins(RSmem* sh, int nb) {
-    __syncthreads();
-    uint4* az = reinterpret_cast<uint4*>(sh->acc);
-    for (int i = threadIdx.x; i < nb * kRT / 2; i += kRT) az[i] = make_uint4(0, 0, 0, 0);
-    if (threadIdx.x < kBins) sh->bcnt[threadIdx.x] = 0;
-    __syncthreads();
-}
-
-__device__ __forceinline__ void acc_add(RSmem* sh, int slot, uint32_t hbits, uint32_t lbits) {
-    uint2* p = &sh->acc[slot * kRT + threadIdx.x];
-    uint2 v = *p;
-    v.x += hbits - 0x4B000000u;
-    v.y += lbits - 0x4B400000u;
-    *p = v;
-    atomicAdd(&sh->bcnt[slot], 1u);
 }
 
 // CTA-wide walk over the per-key counts of keys khi, khi-1, ... (n keys, thread t owns a
@@ -787,6 +764,52 @@ __device__ int tie_scan(RSmem* sh, const VerifyArgs& a, const RowGeo& g, int V, 
     return found;
 }
 
+// Exact walk over the keys top, top-1, ..., bottom from counts gathered by streaming the row
+// (kRKeyCap keys per pass, from the top): the first key where the count reaches k or the mass
+// passes thr, starting from (cnt0, mass0) ranked ahead.  All threads must call it.
+__device__ KeyStop count_walk(RSmem* sh, const VerifyArgs& a, const RowGeo& g, int V, uint32_t top,
+                              uint32_t bottom, float m, float c, unsigned long long cnt0,
+                              unsigned long long mass0, long long k, long long thr) {
+    const int tid = threadIdx.x;
+    KeyStop ks;
+    ks.found = 0;
+    ks.cnt = cnt0;
+    ks.mass = mass0;
+    unsigned long long cum_cnt = cnt0, cum_mass = mass0;
+    for (uint32_t t = top; t >= bottom && t <= 0xFFFFu;) {
+        const uint32_t bot = (t - bottom + 1u > (uint32_t)kRKeyCap) ? t - kRKeyCap + 1 : bottom;
+        const int nk = (int)(t - bot + 1);
+        __syncthreads();
+        for (int i = tid; i < nk; i += kRT) sh->hist[i] = 0;
+        __syncthreads();
+        const uint32_t vlo = key_bits(bot), vhi = key_bits(t);
+        const uint32_t vlo2 = vlo | (vlo << 16), vhi2 = vhi | (vhi << 16);
+        stream_row(sh, a, g, V, [&](const uint4& x, int v) {
+            const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const uint32_t in = bf2_ge(xs[q], vlo2) & bf2_le(xs[q], vhi2);
+                if (!in) continue;
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int e = 8 * v + 2 * q + h - g.off;
+                    if (!(in & (h ? 0xFFFF0000u : 0x0000FFFFu)) || e < 0 || e >= V) continue;
+                    const uint32_t kkey = okey(h ? (xs[q] >> 16) : (xs[q] & 0xFFFFu));
+                    if (kkey >= bot && kkey <= t) atomicAdd(&sh->hist[t - kkey], 1u);
+                }
+            }
+        });
+        __syncthreads();
+        ks = cta_walk_keys(sh, sh->hist, t, nk, m, c, cum_cnt, cum_mass, k, thr);
+        if (ks.found) break;
+        cum_cnt = ks.cnt;
+        cum_mass = ks.mass;
+        if (bot == bottom) break;
+        t = bot - 1;
+    }
+    return ks;
+}
+
 __global__ void __launch_bounds__(kRT, 2) rows_kernel(VerifyArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     RSmem* sh = reinterpret_cast<RSmem*>(smem_raw);
@@ -811,123 +834,156 @@ __global__ void __launch_bounds__(kRT, 2) rows_kernel(VerifyArgs a) {
         if (ti.row < 0 && tid == 0) atomicOr(&a.ws->err, 2u);
         const RowGeo g = row_geo(a, ti);
         const bool greedy = ti.cat == kGreedy;
-        const uint32_t nfill = (uint32_t)g.nv * 8u - (uint32_t)(g.nv ? V : 0);
 
-        // ---- pass 1: max (greedy rows: and the first index of the max) -------------------
-        uint32_t tkey = 0;
-        int tfirst = 0x7fffffff;
-        stream_row(sh, a, g, V, [&](const uint4& x, int v) {
-            uint32_t mx = bf2_max(bf2_max(x.x, x.y), bf2_max(x.z, x.w));
-            const uint32_t k0 = okey(mx & 0xFFFFu), k1 = okey(mx >> 16);
-            const uint32_t vk = k0 > k1 ? k0 : k1;
-            if (vk > tkey) {
-                tkey = vk;
-                if (greedy) {
-                    // first half of this vector with the new maximum (vectors arrive in order)
-                    const uint32_t b = key_bits(vk);
-                    const uint32_t b2 = b | (b << 16);
-                    const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
-                    int f = 0x7fffffff;
-#pragma unroll
-                    for (int h = 7; h >= 0; --h) {
-                        const uint32_t eq = bf2_eq(xs[h >> 1], b2) & ((h & 1) ? 0xFFFF0000u : 0x0000FFFFu);
-                        const int e = 8 * v + h - g.off;
-                        if (eq && e >= 0 && e < V) f = e;
-                    }
-                    tfirst = f;
-                }
-            }
-        });
-        PROF_MARK(ti.cat, 0);
-        const uint32_t wk = __reduce_max_sync(0xffffffffu, tkey);
-        if (lane == 0) sh->red32[wid] = wk;
-        if (tid == 0) sh->first_min = 0x7fffffff;
-        __syncthreads();
-        uint32_t mkey = 0;
-#pragma unroll
-        for (int i = 0; i < kRW; ++i) mkey = max(mkey, sh->red32[i]);
-        if (greedy) {
-            if (tkey == mkey && tfirst != 0x7fffffff) atomicMin(&sh->first_min, tfirst);
+        // Nucleus and keep-all rows start with the fixed-range histogram (one pass, no max
+        // pass); the other rows, and rows with values outside that range, start with the max.
+        const bool onepass = ti.cat == kKeepAll || (ti.cat == kBinned && ti.p < 1.0f);
+        uint32_t tkey = 0, mkey = 0;
+        bool fixed_hist = false;
+        if (onepass) {
             __syncthreads();
+            for (int i = tid; i < kHCap; i += kRT) sh->hist[i] = 0u;
             if (tid == 0) {
-                const int f = sh->first_min;
-                if (f != 0x7fffffff)
-                    a.gmax[ti.b * kT + ti.s] = ((unsigned long long)mkey << 32) | (0xFFFFFFFFull - (unsigned)f);
-                put_desc(a, ti, bf(key_bits(mkey)), mkey, f, 1ull << kFixBits, f == 0x7fffffff ? 0 : f,
-                         kDescGreedy);
+                sh->nband = 0u;
+                sh->outside = 0u;
             }
-            PROF_END(ti.cat, 1);
-            continue;
+            __syncthreads();
+            stream_row(sh, a, g, V, [&](const uint4& x, int) {
+                const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+                uint32_t rare = 0;  // bit h: element h is outside the fine bins
+#pragma unroll
+                for (int h = 0; h < 8; ++h) {
+                    const uint32_t u16 = (h & 1) ? (xs[h >> 1] >> 16) : (xs[h >> 1] & 0xFFFFu);
+                    const uint32_t key = u16 ^ ((u16 & 0x8000u) ? 0xFFFFu : 0x8000u);
+                    tkey = key > tkey ? key : tkey;
+                    const bool pos = key >= kFB;
+                    const uint32_t idx = pos ? kFTop - key : (kFPos + kFNB) - key;
+                    const bool fine = key >= kFNLow && key <= kFTop && (pos || key <= kFNB);
+                    if (fine) atomicAdd(&sh->hist[idx], 1u);
+                    rare |= fine ? 0u : (1u << h);
+                }
+                if (rare) {
+#pragma unroll 1
+                    for (int h = 0; h < 8; ++h) {
+                        if (!(rare & (1u << h))) continue;
+                        const uint32_t u16 = (h & 1) ? (xs[h >> 1] >> 16) : (xs[h >> 1] & 0xFFFFu);
+                        const uint32_t key = u16 ^ ((u16 & 0x8000u) ? 0xFFFFu : 0x8000u);
+                        if (key == kNInfRaw) continue;             // -inf (and the row's fill)
+                        if (key > kFNB && key < kFB) {             // the band |v| < 2^-20
+                            const uint32_t p = atomicAdd(&sh->nband, 1u);
+                            if (p < (uint32_t)kBandCap) sh->band[p] = (uint16_t)u16;
+                        } else {
+                            sh->outside = 1u;                      // |v| >= 2^12, +inf, NaN
+                        }
+                    }
+                }
+            });
+            PROF_MARK(ti.cat, 2);
+            const uint32_t wk0 = __reduce_max_sync(0xffffffffu, tkey);
+            if (lane == 0) sh->red32[wid] = wk0;
+            __syncthreads();
+#pragma unroll
+            for (int i = 0; i < kRW; ++i) mkey = max(mkey, sh->red32[i]);
+            fixed_hist = sh->outside == 0u && sh->nband <= (uint32_t)kBandCap && mkey > kNInfRaw &&
+                         mkey <= kFTop;
+            __syncthreads();
+        }
+        if (!fixed_hist) {
+            // ---- pass 1: max (greedy rows: and the first index of the max) ---------------
+            tkey = 0;
+            int tfirst = 0x7fffffff;
+            stream_row(sh, a, g, V, [&](const uint4& x, int v) {
+                uint32_t mx = bf2_max(bf2_max(x.x, x.y), bf2_max(x.z, x.w));
+                const uint32_t k0 = okey(mx & 0xFFFFu), k1 = okey(mx >> 16);
+                const uint32_t vk = k0 > k1 ? k0 : k1;
+                if (vk > tkey) {
+                    tkey = vk;
+                    if (greedy) {
+                        // first half of this vector with the new maximum (vectors arrive in order)
+                        const uint32_t b = key_bits(vk);
+                        const uint32_t b2 = b | (b << 16);
+                        const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+                        int f = 0x7fffffff;
+#pragma unroll
+                        for (int h = 7; h >= 0; --h) {
+                            const uint32_t eq = bf2_eq(xs[h >> 1], b2) & ((h & 1) ? 0xFFFF0000u : 0x0000FFFFu);
+                            const int e = 8 * v + h - g.off;
+                            if (eq && e >= 0 && e < V) f = e;
+                        }
+                        tfirst = f;
+                    }
+                }
+            });
+            PROF_MARK(ti.cat, 0);
+            const uint32_t wk = __reduce_max_sync(0xffffffffu, tkey);
+            if (lane == 0) sh->red32[wid] = wk;
+            if (tid == 0) sh->first_min = 0x7fffffff;
+            __syncthreads();
+            mkey = 0;
+#pragma unroll
+            for (int i = 0; i < kRW; ++i) mkey = max(mkey, sh->red32[i]);
+            if (greedy) {
+                if (tkey == mkey && tfirst != 0x7fffffff) atomicMin(&sh->first_min, tfirst);
+                __syncthreads();
+                if (tid == 0) {
+                    const int f = sh->first_min;
+                    if (f != 0x7fffffff)
+                        a.gmax[ti.b * kT + ti.s] = ((unsigned long long)mkey << 32) | (0xFFFFFFFFull - (unsigned)f);
+                    put_desc(a, ti, bf(key_bits(mkey)), mkey, f, 1ull << kFixBits, f == 0x7fffffff ? 0 : f,
+                             kDescGreedy);
+                }
+                PROF_END(ti.cat, 1);
+                continue;
+            }
         }
         const float m = bf(key_bits(mkey));
         const long long kk = ti.k < V ? (long long)ti.k : (long long)V;
-        int cat = ti.cat;
-        // window threshold: the largest tau with at least k thread maxima >= tau (each such
-        // thread holds an element >= tau)
-        uint32_t tau = 0;
+        const int cat = ti.cat;
+        const bool nucleus = ti.p < 1.0f;
+        const uint32_t kninf = okey(0xFF80u);  // key of -inf
+        KeyStop ks;
+        ks.found = 0;
+        unsigned long long S = 0;
+        long long thr = 0x7fffffffffffffffll;
+
         if (cat == kWindow) {
+            // ---- pure top-k, k <= 256: candidates >= tau, ranked exactly -------------------
+            // tau = the largest value with at least k thread maxima >= tau (each such thread
+            // holds an element >= tau)
+            uint32_t tau = 0;
             for (int bit = 15; bit >= 0; --bit) {
                 const uint32_t cand = tau | (1u << bit);
                 if (__syncthreads_count(tkey >= cand) >= kk) tau = cand;
             }
-            // fewer than k threads hold data (tiny vocabularies): take every element >= -inf
-            const uint32_t kneg = okey(0xFF80u);
-            if (tau < kneg) tau = kneg;
+            if (tau < kninf) tau = kninf;  // fewer than k threads hold data (tiny vocabularies)
             if (tid == 0) sh->nlist = 0;
-        }
-        if (cat == kBinned) clear_bins(sh, kBins);
-        __syncthreads();
-
-        // ---- pass 2: exact exp, fixed-point sum, window candidates or level-1 bins --------
-        const float2 nm = make_float2(-m, -m), c2 = make_float2(ti.c, ti.c);
-        const uint32_t taub = key_bits(tau);
-        const uint32_t tau2 = taub | (taub << 16);
-        uint32_t hs = 0, ls = 0, nel = 0;
-        stream_row(sh, a, g, V, [&](const uint4& x, int v) {
-            const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
-            nel += 8;
+            __syncthreads();
+            const uint32_t taub = key_bits(tau);
+            const uint32_t tau2 = taub | (taub << 16);
+            stream_row(sh, a, g, V, [&](const uint4& x, int v) {
+                const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
 #pragma unroll
-            for (int q = 0; q < 4; ++q) {
-                const Pair pr = exp_pair(xs[q], nm, c2);
-                hs += pr.h0 + pr.h1;
-                ls += pr.l0 + pr.l1;
-                if (cat == kBinned) {
-                    acc_add(sh, bin1_of(pr.yc.x), pr.h0, pr.l0);
-                    acc_add(sh, bin1_of(pr.yc.y), pr.h1, pr.l1);
-                } else if (cat == kWindow) {
+                for (int q = 0; q < 4; ++q) {
                     const uint32_t ge = bf2_ge(xs[q], tau2);
-                    if (ge) {
+                    if (!ge) continue;
 #pragma unroll
-                        for (int h = 0; h < 2; ++h) {
-                            const int e = 8 * v + 2 * q + h - g.off;
-                            if ((ge & (h ? 0xFFFF0000u : 0x0000FFFFu)) && e >= 0 && e < V) {
-                                const uint32_t pos = atomicAdd(&sh->nlist, 1u);
-                                if (pos < kRWinCap) {
-                                    sh->wkey[pos] = okey(h ? (xs[q] >> 16) : (xs[q] & 0xFFFFu));
-                                    sh->widx[pos] = (uint32_t)e;
-                                }
+                    for (int h = 0; h < 2; ++h) {
+                        const int e = 8 * v + 2 * q + h - g.off;
+                        if ((ge & (h ? 0xFFFF0000u : 0x0000FFFFu)) && e >= 0 && e < V) {
+                            const uint32_t pos = atomicAdd(&sh->nlist, 1u);
+                            if (pos < kRWinCap) {
+                                sh->wkey[pos] = okey(h ? (xs[q] >> 16) : (xs[q] & 0xFFFFu));
+                                sh->widx[pos] = (uint32_t)e;
                             }
                         }
                     }
                 }
-            }
-        });
-        const uint32_t hi_t = hs - nel * 0x4B000000u;
-        const int32_t lo_t = (int32_t)(ls - nel * 0x4B400000u);
-        PROF_MARK(ti.cat, 2);
-        const unsigned long long S = rcta_sum_u64((unsigned long long)((long long)hi_t * 8388608 + lo_t), sh);
-        const long long thr = (ti.p < 1.0f) ? scale_floor(ti.p, S) : 0x7fffffffffffffffll;
-
-        if (cat == kKeepAll) {
-            if (tid == 0) put_desc(a, ti, m, 0u, 0x7fffffff, S, 0, 0u);
-            PROF_END(ti.cat, 3);
-            continue;
-        }
-        if (cat == kWindow) {
+            });
+            PROF_MARK(ti.cat, 2);
             const int n = (int)sh->nlist;
             if (n >= 1 && n <= kRWinCap) {
-                // rank the candidates by (key desc, index asc) into acc (as uint2)
-                uint2* srt = sh->acc;
+                // rank the candidates by (key desc, index asc); the first k are kept
+                uint2* srt = reinterpret_cast<uint2*>(sh->hist);
                 for (int i = tid; i < n; i += kRT) {
                     const uint32_t ki = sh->wkey[i], xi = sh->widx[i];
                     int r = 0;
@@ -939,25 +995,7 @@ __global__ void __launch_bounds__(kRT, 2) rows_kernel(VerifyArgs a) {
                 }
                 __syncthreads();
                 if (tid < 32) {
-                    unsigned long long A = 0;
-                    int nsel = -1;
-                    for (int base = 0; base < n && nsel < 0; base += 32) {
-                        const int r = base + lane;
-                        unsigned long long F = 0;
-                        if (r < n) F = fix_of_y(y_clamped(bf(key_bits(srt[r].x)), m, ti.c));
-                        unsigned long long inc = F;
-#pragma unroll
-                        for (int o = 1; o < 32; o <<= 1) {
-                            const unsigned long long vv = __shfl_up_sync(0xffffffffu, inc, o);
-                            if (lane >= o) inc += vv;
-                        }
-                        const unsigned long long Ar = A + inc - F;
-                        const bool out = r < n && r > 0 && (r >= kk || (long long)Ar > thr);
-                        const uint32_t bal = __ballot_sync(0xffffffffu, out);
-                        if (bal) nsel = base + __ffs(bal) - 1;
-                        A += __shfl_sync(0xffffffffu, inc, 31);
-                    }
-                    if (nsel < 0) nsel = n < kk ? n : (int)kk;
+                    const int nsel = n < kk ? n : (int)kk;
                     unsigned long long sk = 0;
                     for (int r = lane; r < nsel; r += 32)
                         sk += fix_of_y(y_clamped(bf(key_bits(srt[r].x)), m, ti.c));
@@ -967,132 +1005,130 @@ __global__ void __launch_bounds__(kRT, 2) rows_kernel(VerifyArgs a) {
                 PROF_END(ti.cat, 3);
                 continue;
             }
-            // the window overflowed: level-1 bins in another pass
-            clear_bins(sh, kBins);
-            stream_row(sh, a, g, V, [&](const uint4& x, int) {
-                const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const Pair pr = exp_pair(xs[q], nm, c2);
-                    acc_add(sh, bin1_of(pr.yc.x), pr.h0, pr.l0);
-                    acc_add(sh, bin1_of(pr.yc.y), pr.h1, pr.l1);
-                }
-            });
-            cat = kBinned;
-        }
-
-        // ---- binned selection --------------------------------------------------------------
-        PROF_MARK(ti.cat, 4);
-        reduce_bins(sh, kBins, nfill);
-        if (tid < 32) {
-            const Walk wk1 = walk_groups(sh->wc, sh->wm, kBins, 0ull, 0ull, kk, thr);
-            if (lane == 0) {
-                sh->sel[0] = wk1.group;
-                sh->self64[0] = wk1.cnt;
-                sh->self64[1] = wk1.mass;
+            // the window overflowed (many equal values): exact counts from the top instead
+            ks = count_walk(sh, a, g, V, mkey, kninf, m, ti.c, 0ull, 0ull, kk, thr);
+        } else if (cat == kKeepAll || nucleus) {
+            // ---- exact per-key histogram of every element with nonzero fixed-point mass -----
+            // key < klo: y < -42 so fix(exp2(y)) = 0; such elements are never in a nucleus
+            // (their mass ranked ahead is S > floor(top_p S)) and add nothing to S.
+            const float vlo = m - 42.5f / ti.c;
+            uint32_t klo = kninf + 1u;
+            if (vlo > -INFINITY) {
+                const uint32_t vb = __float_as_uint(vlo) >> 16;  // truncated toward zero
+                const uint32_t kt = okey(vb);
+                klo = kt > kninf + 1u ? kt - 1u : kninf + 1u;      // one bf16 step below vlo
             }
-        }
-        __syncthreads();
-        const int b1 = sh->sel[0];
-        if (b1 < 0) {
-            if (tid == 0) put_desc(a, ti, m, 0u, 0x7fffffff, S, 0, 0u);
-            continue;
-        }
-        unsigned long long cum_cnt = sh->self64[0], cum_mass = sh->self64[1];
-        if (tid < 32) {
-            uint32_t klo1, khi1;
-            key_range(b1, okey(0xFF80u), mkey, m, ti.c, 1, klo1, khi1);
-            if (lane == 0) {
-                sh->sel[4] = (int)klo1;
-                sh->sel[5] = (int)khi1;
-            }
-        }
-        __syncthreads();
-        uint32_t klo = (uint32_t)sh->sel[4], khi = (uint32_t)sh->sel[5];
-        if (khi - klo + 1u > (uint32_t)kRKeyCap) {
-            // level 2: sub-bins of bin b1 (exp again, only elements of the bin accumulate)
-            clear_bins(sh, kSub);
-            stream_row(sh, a, g, V, [&](const uint4& x, int v) {
-                const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const Pair pr = exp_pair(xs[q], nm, c2);
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const float yc = h ? pr.yc.y : pr.yc.x;
-                        const int e = 8 * v + 2 * q + h - g.off;
-                        if (bin1_of(yc) == b1 && e >= 0 && e < V)
-                            acc_add(sh, bin2_of(yc, b1), h ? pr.h1 : pr.h0, h ? pr.l1 : pr.l0);
-                    }
-                }
-            });
-            reduce_bins(sh, kSub, 0u);
-            if (tid < 32) {
-                const Walk wk2 = walk_groups(sh->wc, sh->wm, kSub, cum_cnt, cum_mass, kk, thr);
-                if (lane == 0) {
-                    sh->sel[3] = wk2.group;
-                    sh->self64[0] = wk2.cnt;
-                    sh->self64[1] = wk2.mass;
-                }
-            }
-            __syncthreads();
-            const int b2 = sh->sel[3];
-            if (b2 < 0) {
+            if (klo > mkey) klo = mkey;
+            uint32_t kB = 0x8000u, kNB = 0x7FFFu, npos = 0, nneg = 0, negtop = 0, topkey = 0;
+            if (fixed_hist) {
+                // the one-pass histogram: fixed bins, the band's elements listed
+                kB = kFB;
+                kNB = kFNB;
+                npos = kFPos;
+                nneg = kFPos;
+                negtop = kFNB;
+                topkey = kFTop;
                 if (tid == 0) {
-                    atomicOr(&a.ws->err, 8u);
-                    put_desc(a, ti, m, 0u, 0x7fffffff, S, 0, 0u);
+                    sh->zcnt = 0u;
+                    sh->zmass = 0ull;
                 }
+                __syncthreads();
+                const uint32_t nb = sh->nband;
+                for (uint32_t i = tid; i < nb; i += kRT) {
+                    const uint32_t u16 = sh->band[i];
+                    const uint32_t key = okey(u16);
+                    if (key < klo || key > mkey) continue;
+                    atomicAdd(&sh->zcnt, 1u);
+                    const unsigned long long F = fix_of_y(y_clamped(bf(u16), m, ti.c));
+                    if (F) atomicAdd(&sh->zmass, F);
+                }
+                __syncthreads();
+            } else {
+                // the band |v| < 2^zb is left out of the histogram (exact per element, usually
+                // empty): the smallest band for which the rest fits kHCap bins
+                for (int zb = -126; zb <= 127; ++zb) {
+                    const uint32_t bits = (uint32_t)(127 + zb) << 7;
+                    kB = 0x8000u | bits;          // key of +2^zb
+                    kNB = 0x7FFFu - bits;         // key of -2^zb
+                    npos = mkey >= kB ? mkey - kB + 1u : 0u;
+                    const uint32_t ntop = kNB < mkey ? kNB : mkey;
+                    nneg = ntop >= klo ? ntop - klo + 1u : 0u;
+                    if (npos + nneg <= (uint32_t)kHCap) break;
+                }
+                negtop = kNB < mkey ? kNB : mkey;
+                topkey = mkey;
+                __syncthreads();
+                for (uint32_t i = tid; i < npos + nneg; i += kRT) sh->hist[i] = 0u;
+                if (tid == 0) {
+                    sh->zcnt = 0u;
+                    sh->zmass = 0ull;
+                }
+                __syncthreads();
+                const float mz = m, cz = ti.c;
+                const uint32_t nposv = npos, negv = npos + negtop, mk = mkey, kl = klo, kb = kB, knb = kNB;
+                stream_row(sh, a, g, V, [&](const uint4& x, int) {
+                    const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+                    uint32_t band = 0;  // bit h: element h of this vector is in the band
+#pragma unroll
+                    for (int h = 0; h < 8; ++h) {
+                        const uint32_t u16 = (h & 1) ? (xs[h >> 1] >> 16) : (xs[h >> 1] & 0xFFFFu);
+                        // ordered key (-0 joins +0 inside the band, which is handled exactly below)
+                        const uint32_t key = u16 ^ ((u16 & 0x8000u) ? 0xFFFFu : 0x8000u);
+                        const bool pos = key >= kb;
+                        const uint32_t idx = pos ? mk - key : negv - key;
+                        const bool fine = key >= kl && key <= mk && (pos || key <= knb);
+                        if (fine) atomicAdd(&sh->hist[idx], 1u);
+                        band |= (key >= kl && key <= mk && !pos && key > knb) ? (1u << h) : 0u;
+                    }
+                    if (band) {
+#pragma unroll 1
+                        for (int h = 0; h < 8; ++h) {
+                            if (!(band & (1u << h))) continue;
+                            const uint32_t u16 = (h & 1) ? (xs[h >> 1] >> 16) : (xs[h >> 1] & 0xFFFFu);
+                            const unsigned long long F = fix_of_y(y_clamped(bf(u16), mz, cz));
+                            atomicAdd(&sh->zcnt, 1u);
+                            if (F) atomicAdd(&sh->zmass, F);
+                        }
+                    }
+                });
+                (void)nposv;
+            }
+            const uint32_t nfine = npos + nneg;
+            PROF_MARK(ti.cat, 2);
+            // S = sum over bins of count * F(key) + the band's exact mass
+            unsigned long long part = 0;
+            for (uint32_t i = tid; i < nfine; i += kRT) {
+                const uint32_t cnt = sh->hist[i];
+                const uint32_t key = i < npos ? topkey - i : negtop - (i - npos);
+                if (cnt && key >= klo)
+                    part += (unsigned long long)cnt * fix_of_y(y_clamped(bf(key_bits(key)), m, ti.c));
+            }
+            S = rcta_sum_u64(part, sh) + sh->zmass;
+            if (cat == kKeepAll || !nucleus) {
+                if (tid == 0) put_desc(a, ti, m, 0u, 0x7fffffff, S, 0, 0u);
+                PROF_END(ti.cat, 3);
                 continue;
             }
-            cum_cnt = sh->self64[0];
-            cum_mass = sh->self64[1];
-            if (tid < 32) {
-                uint32_t klo2, khi2;
-                key_range(b1 * kSub + b2, okey(0xFF80u), mkey, m, ti.c, 2, klo2, khi2);
-                if (lane == 0) {
-                    sh->sel[4] = (int)klo2;
-                    sh->sel[5] = (int)khi2;
+            thr = scale_floor(ti.p, S);
+            PROF_MARK(ti.cat, 4);
+            // walk: positive bins, the band, negative bins (rank order)
+            ks = cta_walk_keys(sh, sh->hist, topkey, (int)npos, m, ti.c, 0ull, 0ull, kk, thr);
+            if (!ks.found) {
+                const unsigned long long zc = sh->zcnt, zm = sh->zmass;
+                const unsigned long long c0 = ks.cnt, m0 = ks.mass;
+                if (zc > 0 && ((long long)(c0 + zc) >= kk || (long long)(m0 + zm) > thr)) {
+                    // the boundary is inside the band: exact counts of its keys
+                    const uint32_t btop = (kB - 1u) < mkey ? kB - 1u : mkey;
+                    const uint32_t bbot = (kNB + 1u) > klo ? kNB + 1u : klo;
+                    ks = count_walk(sh, a, g, V, btop, bbot, m, ti.c, c0, m0, kk, thr);
+                } else {
+                    ks = cta_walk_keys(sh, sh->hist + npos, negtop, (int)nneg, m, ti.c, c0 + zc,
+                                       m0 + zm, kk, thr);
                 }
             }
-            __syncthreads();
-            klo = (uint32_t)sh->sel[4];
-            khi = (uint32_t)sh->sel[5];
-        }
-
-        PROF_MARK(ti.cat, 5);
-        // ---- level 3: per-key counts of the boundary (sub-)bin, in chunks from the top -----
-        KeyStop ks;
-        ks.found = 0;
-        for (uint32_t top = khi; top >= klo && top <= 0xFFFFu;) {
-            const uint32_t bot = (top - klo + 1u > (uint32_t)kRKeyCap) ? top - kRKeyCap + 1 : klo;
-            const int nk = (int)(top - bot + 1);
-            __syncthreads();
-            for (int i = tid; i < nk; i += kRT) sh->khist[i] = 0;
-            __syncthreads();
-            const uint32_t vlo = key_bits(bot), vhi = key_bits(top);
-            const uint32_t vlo2 = vlo | (vlo << 16), vhi2 = vhi | (vhi << 16);
-            stream_row(sh, a, g, V, [&](const uint4& x, int v) {
-                const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const uint32_t in = bf2_ge(xs[q], vlo2) & bf2_le(xs[q], vhi2);
-                    if (!in) continue;
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const int e = 8 * v + 2 * q + h - g.off;
-                        if (!(in & (h ? 0xFFFF0000u : 0x0000FFFFu)) || e < 0 || e >= V) continue;
-                        const uint32_t kkey = okey(h ? (xs[q] >> 16) : (xs[q] & 0xFFFFu));
-                        if (kkey >= bot && kkey <= top) atomicAdd(&sh->khist[top - kkey], 1u);
-                    }
-                }
-            });
-            __syncthreads();
-            ks = cta_walk_keys(sh, sh->khist, top, nk, m, ti.c, cum_cnt, cum_mass, kk, thr);
-            if (ks.found) break;
-            cum_cnt = ks.cnt;
-            cum_mass = ks.mass;
-            if (bot == klo) break;
-            top = bot - 1;
+        } else {
+            // ---- pure top-k with k > 256: exact counts from the top ------------------------
+            ks = count_walk(sh, a, g, V, mkey, kninf, m, ti.c, 0ull, 0ull, kk, thr);
         }
         if (!ks.found) {
             if (tid == 0) {
