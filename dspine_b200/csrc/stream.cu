@@ -434,7 +434,7 @@ constexpr uint32_t kNInfRaw = 0x007Fu;        // key of -inf
 constexpr int kBandCap = 512;
 static_assert(kFPos == 4096u && kFNB - kFNLow + 1u == 4096u && 2 * kFPos == (uint32_t)kHCap,
               "fixed histogram geometry");
-constexpr int kRingS = 4;          // streaming ring: slots
+constexpr int kRingS = 3;          // streaming ring: slots
 constexpr int kRingCW = 512;       // vectors (16 B) per slot: 8 KB
 
 struct RSmem {
@@ -452,15 +452,20 @@ struct RSmem {
     uint32_t nband;                // one-pass histogram: band elements listed
     uint32_t outside;              //                     a value outside the fixed range
     uint16_t band[kBandCap];       //                     the band's raw values
+    uint32_t gcnt[kHCap / 32];     // histogram groups of 32 bins: counts
+    unsigned long long gmass[kHCap / 32];  //                       masses
     uint32_t zcnt;                 // histogram band: elements
     unsigned long long zmass;      //                 exact mass
-    uint32_t wkey[kRWinCap];       // window candidates: key
-    uint32_t widx[kRWinCap];       //                    element index
-    alignas(16) uint32_t hist[kHCap];       // per-key counts / window sort area / count chunks
+    alignas(16) uint32_t hist[kHCap];       // per-key counts / window candidates / count chunks
     alignas(16) uint4 ring[kRingS][kRingCW];  // streaming ring filled by bulk copies
     alignas(8) uint64_t ring_bar[kRingS];
     uint32_t ring_cnt;                      // chunks consumed so far (slot, phase)
 };
+
+// three CTAs per SM: 3 x (this + 1 KB reserved) within the SM's 228 KB
+static_assert(sizeof(RSmem) <= 74 * 1024, "row kernel shared memory");
+static_assert(2 * kRWinCap * 4 <= kHCap * 4 && kRWinCap * 8 <= kRingS * kRingCW * 16,
+              "window candidates fit the histogram, the ranked list the ring");
 
 struct RowGeo {
     const uint16_t* rowp;
@@ -810,7 +815,10 @@ __device__ KeyStop count_walk(RSmem* sh, const VerifyArgs& a, const RowGeo& g, i
     return ks;
 }
 
-__global__ void __launch_bounds__(kRT, 2) rows_kernel(VerifyArgs a) {
+#ifndef DSV_ROWS_MIN_CTAS
+#define DSV_ROWS_MIN_CTAS 3
+#endif
+__global__ void __launch_bounds__(kRT, DSV_ROWS_MIN_CTAS) rows_kernel(VerifyArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     RSmem* sh = reinterpret_cast<RSmem*>(smem_raw);
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
@@ -848,36 +856,48 @@ __global__ void __launch_bounds__(kRT, 2) rows_kernel(VerifyArgs a) {
                 sh->outside = 0u;
             }
             __syncthreads();
+            uint32_t vmax2 = 0xFF80FF80u;  // running bf16x2 maximum (-inf, -inf)
             stream_row(sh, a, g, V, [&](const uint4& x, int) {
                 const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
-                uint32_t rare = 0;  // bit h: element h is outside the fine bins
+                vmax2 = bf2_max(vmax2, bf2_max(bf2_max(xs[0], xs[1]), bf2_max(xs[2], xs[3])));
+                uint32_t rare = 0;  // bit q: word q has an element outside the fine bins
 #pragma unroll
-                for (int h = 0; h < 8; ++h) {
-                    const uint32_t u16 = (h & 1) ? (xs[h >> 1] >> 16) : (xs[h >> 1] & 0xFFFFu);
-                    const uint32_t key = u16 ^ ((u16 & 0x8000u) ? 0xFFFFu : 0x8000u);
-                    tkey = key > tkey ? key : tkey;
-                    const bool pos = key >= kFB;
-                    const uint32_t idx = pos ? kFTop - key : (kFPos + kFNB) - key;
-                    const bool fine = key >= kFNLow && key <= kFTop && (pos || key <= kFNB);
-                    if (fine) atomicAdd(&sh->hist[idx], 1u);
-                    rare |= fine ? 0u : (1u << h);
+                for (int q = 0; q < 4; ++q) {
+                    const uint32_t w = xs[q];
+                    // fine iff 2^-20 <= |v| < 2^12, i.e. 0x3580 <= |bits| <= 0x457F: bit 15 of
+                    // |bits| + 0x4A80 says ">= 0x3580", of |bits| + 0x3A80 says ">= 0x4580"
+                    const uint32_t a2 = w & 0x7FFF7FFFu;
+                    const uint32_t f2 = (a2 + 0x4A804A80u) & ~(a2 + 0x3A803A80u) & 0x80008000u;
+                    // bin: positive v -> 0x457F - |bits| (descending key), negative v ->
+                    // |bits| - 0x2580 (4096 + descending key of the negative part)
+                    const uint32_t lo = w & 0xFFFFu, hi = w >> 16;
+                    const uint32_t ilo = (lo & 0x8000u) ? (lo & 0x7FFFu) - 0x2580u : 0x457Fu - lo;
+                    const uint32_t ihi = (hi & 0x8000u) ? (hi & 0x7FFFu) - 0x2580u : 0x457Fu - hi;
+                    if (f2 & 0x00008000u) atomicAdd(&sh->hist[ilo], 1u);
+                    if (f2 & 0x80000000u) atomicAdd(&sh->hist[ihi], 1u);
+                    rare |= (f2 != 0x80008000u) ? (1u << q) : 0u;
                 }
                 if (rare) {
 #pragma unroll 1
                     for (int h = 0; h < 8; ++h) {
-                        if (!(rare & (1u << h))) continue;
+                        if (!(rare & (1u << (h >> 1)))) continue;
                         const uint32_t u16 = (h & 1) ? (xs[h >> 1] >> 16) : (xs[h >> 1] & 0xFFFFu);
-                        const uint32_t key = u16 ^ ((u16 & 0x8000u) ? 0xFFFFu : 0x8000u);
-                        if (key == kNInfRaw) continue;             // -inf (and the row's fill)
-                        if (key > kFNB && key < kFB) {             // the band |v| < 2^-20
+                        const uint32_t ab = u16 & 0x7FFFu;
+                        if (ab >= 0x3580u && ab <= 0x457Fu) continue;  // a fine element
+                        if (u16 == 0xFF80u) continue;                   // -inf (and the row's fill)
+                        if (ab < 0x3580u) {                             // the band |v| < 2^-20
                             const uint32_t p = atomicAdd(&sh->nband, 1u);
                             if (p < (uint32_t)kBandCap) sh->band[p] = (uint16_t)u16;
                         } else {
-                            sh->outside = 1u;                      // |v| >= 2^12, +inf, NaN
+                            sh->outside = 1u;                           // |v| >= 2^12, inf, NaN
                         }
                     }
                 }
             });
+            {
+                const uint32_t k0 = okey(vmax2 & 0xFFFFu), k1 = okey(vmax2 >> 16);
+                tkey = k0 > k1 ? k0 : k1;
+            }
             PROF_MARK(ti.cat, 2);
             const uint32_t wk0 = __reduce_max_sync(0xffffffffu, tkey);
             if (lane == 0) sh->red32[wid] = wk0;
@@ -972,8 +992,8 @@ __global__ void __launch_bounds__(kRT, 2) rows_kernel(VerifyArgs a) {
                         if ((ge & (h ? 0xFFFF0000u : 0x0000FFFFu)) && e >= 0 && e < V) {
                             const uint32_t pos = atomicAdd(&sh->nlist, 1u);
                             if (pos < kRWinCap) {
-                                sh->wkey[pos] = okey(h ? (xs[q] >> 16) : (xs[q] & 0xFFFFu));
-                                sh->widx[pos] = (uint32_t)e;
+                                sh->hist[pos] = okey(h ? (xs[q] >> 16) : (xs[q] & 0xFFFFu));
+                                sh->hist[kRWinCap + pos] = (uint32_t)e;
                             }
                         }
                     }
@@ -983,13 +1003,17 @@ __global__ void __launch_bounds__(kRT, 2) rows_kernel(VerifyArgs a) {
             const int n = (int)sh->nlist;
             if (n >= 1 && n <= kRWinCap) {
                 // rank the candidates by (key desc, index asc); the first k are kept
-                uint2* srt = reinterpret_cast<uint2*>(sh->hist);
+                // candidates: keys hist[0, n), indices hist[kRWinCap, kRWinCap + n); the ranked
+                // list goes to the ring (idle after the pass)
+                const uint32_t* wkey = sh->hist;
+                const uint32_t* widx = sh->hist + kRWinCap;
+                uint2* srt = reinterpret_cast<uint2*>(&sh->ring[0][0]);
                 for (int i = tid; i < n; i += kRT) {
-                    const uint32_t ki = sh->wkey[i], xi = sh->widx[i];
+                    const uint32_t ki = wkey[i], xi = widx[i];
                     int r = 0;
                     for (int j = 0; j < n; ++j) {
-                        const uint32_t kj = sh->wkey[j];
-                        r += (kj > ki) || (kj == ki && sh->widx[j] < xi);
+                        const uint32_t kj = wkey[j];
+                        r += (kj > ki) || (kj == ki && widx[j] < xi);
                     }
                     srt[r] = make_uint2(ki, xi);
                 }
@@ -1053,7 +1077,7 @@ __global__ void __launch_bounds__(kRT, 2) rows_kernel(VerifyArgs a) {
                     npos = mkey >= kB ? mkey - kB + 1u : 0u;
                     const uint32_t ntop = kNB < mkey ? kNB : mkey;
                     nneg = ntop >= klo ? ntop - klo + 1u : 0u;
-                    if (npos + nneg <= (uint32_t)kHCap) break;
+                    if (npos + nneg <= (uint32_t)kHCap - 64u) break;  // ceil/32 of both parts <= 256
                 }
                 negtop = kNB < mkey ? kNB : mkey;
                 topkey = mkey;
@@ -1093,17 +1117,70 @@ __global__ void __launch_bounds__(kRT, 2) rows_kernel(VerifyArgs a) {
                 });
                 (void)nposv;
             }
-            const uint32_t nfine = npos + nneg;
             PROF_MARK(ti.cat, 2);
-            // S = sum over bins of count * F(key) + the band's exact mass
-            unsigned long long part = 0;
-            for (uint32_t i = tid; i < nfine; i += kRT) {
-                const uint32_t cnt = sh->hist[i];
-                const uint32_t key = i < npos ? topkey - i : negtop - (i - npos);
-                if (cnt && key >= klo)
-                    part += (unsigned long long)cnt * fix_of_y(y_clamped(bf(key_bits(key)), m, ti.c));
+            // ---- S and the walk over groups of 32 bins: positive groups, the band, negative
+            // groups (rank order).  Each warp sums its groups (one bin per lane), thread g scans
+            // group g, and the warp of the stopping group finds the bin.
+            const uint32_t ngp = (npos + 31u) >> 5, ngn = (nneg + 31u) >> 5, ng = ngp + ngn;
+            for (uint32_t gi = wid; gi < ng; gi += kRW) {
+                const bool neg = gi >= ngp;
+                const uint32_t j = neg ? gi - ngp : gi;
+                const uint32_t i = (j << 5) + lane;            // bin within its part
+                const uint32_t lim = neg ? nneg : npos;
+                uint32_t cnt = 0;
+                unsigned long long ms = 0;
+                if (i < lim) {
+                    cnt = sh->hist[(neg ? npos : 0u) + i];
+                    const uint32_t key = (neg ? negtop : topkey) - i;
+                    if (cnt && key >= klo)
+                        ms = (unsigned long long)cnt * fix_of_y(y_clamped(bf(key_bits(key)), m, ti.c));
+                }
+                // warp sums with single-instruction reductions: the mass (< 2^59) in three
+                // 21-bit parts, each summing below 2^26
+                const uint32_t gc = __reduce_add_sync(0xffffffffu, cnt);
+                const uint32_t s0 = __reduce_add_sync(0xffffffffu, (uint32_t)(ms & 0x1FFFFFu));
+                const uint32_t s1 = __reduce_add_sync(0xffffffffu, (uint32_t)((ms >> 21) & 0x1FFFFFu));
+                const uint32_t s2 = __reduce_add_sync(0xffffffffu, (uint32_t)(ms >> 42));
+                if (lane == 0) {
+                    sh->gcnt[gi] = gc;
+                    sh->gmass[gi] = (unsigned long long)s0 + ((unsigned long long)s1 << 21) +
+                                    ((unsigned long long)s2 << 42);
+                }
             }
-            S = rcta_sum_u64(part, sh) + sh->zmass;
+            __syncthreads();
+            const unsigned long long zc = sh->zcnt, zm = sh->zmass;
+            const uint32_t gme = (uint32_t)tid;
+            const unsigned long long ct = gme < ng ? sh->gcnt[gme] : 0ull;
+            const unsigned long long mt = gme < ng ? sh->gmass[gme] : 0ull;
+            unsigned long long ci = ct, mi = mt;
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const unsigned long long x1 = __shfl_up_sync(0xffffffffu, ci, o);
+                const unsigned long long x2 = __shfl_up_sync(0xffffffffu, mi, o);
+                if (lane >= o) {
+                    ci += x1;
+                    mi += x2;
+                }
+            }
+            if (lane == 31) {
+                sh->red64[wid] = ci;
+                sh->wm[wid] = mi;
+            }
+            if (tid == 0) sh->sel[6] = 0x7fffffff;
+            __syncthreads();
+            unsigned long long cb = ci - ct, mb = mi - mt, Sall = 0;
+            for (int w = 0; w < kRW; ++w) {
+                if (w < wid) {
+                    cb += sh->red64[w];
+                    mb += sh->wm[w];
+                }
+                Sall += sh->wm[w];
+            }
+            if (gme >= ngp) {
+                cb += zc;
+                mb += zm;
+            }
+            S = Sall + zm;
             if (cat == kKeepAll || !nucleus) {
                 if (tid == 0) put_desc(a, ti, m, 0u, 0x7fffffff, S, 0, 0u);
                 PROF_END(ti.cat, 3);
@@ -1111,20 +1188,71 @@ __global__ void __launch_bounds__(kRT, 2) rows_kernel(VerifyArgs a) {
             }
             thr = scale_floor(ti.p, S);
             PROF_MARK(ti.cat, 4);
-            // walk: positive bins, the band, negative bins (rank order)
-            ks = cta_walk_keys(sh, sh->hist, topkey, (int)npos, m, ti.c, 0ull, 0ull, kk, thr);
-            if (!ks.found) {
-                const unsigned long long zc = sh->zcnt, zm = sh->zmass;
-                const unsigned long long c0 = ks.cnt, m0 = ks.mass;
-                if (zc > 0 && ((long long)(c0 + zc) >= kk || (long long)(m0 + zm) > thr)) {
-                    // the boundary is inside the band: exact counts of its keys
-                    const uint32_t btop = (kB - 1u) < mkey ? kB - 1u : mkey;
-                    const uint32_t bbot = (kNB + 1u) > klo ? kNB + 1u : klo;
-                    ks = count_walk(sh, a, g, V, btop, bbot, m, ti.c, c0, m0, kk, thr);
-                } else {
-                    ks = cta_walk_keys(sh, sh->hist + npos, negtop, (int)nneg, m, ti.c, c0 + zc,
-                                       m0 + zm, kk, thr);
+            if (gme < ng && ct > 0 && ((long long)(cb + ct) >= kk || (long long)(mb + mt) > thr))
+                atomicMin(&sh->sel[6], tid);
+            if (gme + 1u == ngp || (ngp == 0u && tid == 0)) {
+                // the band, between the positive and the negative groups
+                const unsigned long long c0 = ngp ? cb + ct : 0ull, m0 = ngp ? mb + mt : 0ull;
+                const bool bstop = zc > 0 && ((long long)(c0 + zc) >= kk || (long long)(m0 + zm) > thr);
+                sh->sel[9] = bstop ? 1 : 0;
+                sh->self64[7] = c0;
+                sh->self64[6] = m0;
+            }
+            __syncthreads();
+            const int owner = sh->sel[6];
+            const bool band_stop = sh->sel[9] != 0 && (owner == 0x7fffffff || (uint32_t)owner >= ngp);
+            if (tid == 0) sh->sel[10] = owner;
+            if (owner != 0x7fffffff && !band_stop) {
+                // the owner group's prefix, then the first bin of it that stops
+                if (tid == owner) {
+                    sh->self64[4] = cb;
+                    sh->self64[5] = mb;
                 }
+                __syncthreads();
+                const uint32_t go = (uint32_t)owner;
+                if (wid == 0) {
+                    const bool neg = go >= ngp;
+                    const uint32_t j = neg ? go - ngp : go;
+                    const uint32_t i = (j << 5) + lane;
+                    const uint32_t lim = neg ? nneg : npos;
+                    uint32_t cnt = 0;
+                    unsigned long long F = 0;
+                    uint32_t key = 0;
+                    if (i < lim) {
+                        cnt = sh->hist[(neg ? npos : 0u) + i];
+                        key = (neg ? negtop : topkey) - i;
+                        if (cnt && key >= klo) F = fix_of_y(y_clamped(bf(key_bits(key)), m, ti.c));
+                    }
+                    const unsigned long long c0 = sh->self64[4], m0 = sh->self64[5];
+                    const unsigned long long mm = (unsigned long long)cnt * F;
+                    const unsigned long long cin = warp_incl_u64(cnt), min_ = warp_incl_u64(mm);
+                    const unsigned long long cbl = c0 + cin - cnt, mbl = m0 + min_ - mm;
+                    const bool stop = cnt > 0 && ((long long)(cbl + cnt) >= kk || (long long)(mbl + mm) > thr);
+                    const uint32_t bal = __ballot_sync(0xffffffffu, stop);
+                    const int sl = bal ? __ffs(bal) - 1 : 0;
+                    if (lane == sl) {
+                        sh->sel[7] = (int)key;
+                        sh->sel[8] = (int)cnt;
+                        sh->self64[4] = cbl;
+                        sh->self64[5] = mbl;
+                        sh->self64[3] = F;
+                        sh->sel[11] = bal ? 1 : 0;
+                    }
+                }
+                __syncthreads();
+                ks.found = sh->sel[11];
+                ks.key = (uint32_t)sh->sel[7];
+                ks.count = (uint32_t)sh->sel[8];
+                ks.cnt = sh->self64[4];
+                ks.mass = sh->self64[5];
+                ks.F = sh->self64[3];
+                __syncthreads();
+            } else if (band_stop) {
+                const unsigned long long c0 = sh->self64[7], m0 = sh->self64[6];
+                __syncthreads();
+                const uint32_t btop = (kB - 1u) < mkey ? kB - 1u : mkey;
+                const uint32_t bbot = (kNB + 1u) > klo ? kNB + 1u : klo;
+                ks = count_walk(sh, a, g, V, btop, bbot, m, ti.c, c0, m0, kk, thr);
             }
         } else {
             // ---- pure top-k with k > 256: exact counts from the top ------------------------
