@@ -162,6 +162,7 @@ int dsv_verify_logits(int32_t batch, int32_t vocab, int32_t dtype, const int64_t
     a.res = reinterpret_cast<dsv::TaskResult*>(base + 64 + dsv::verify_done_bytes(batch));
     a.desc = reinterpret_cast<dsv::RowDesc*>(base + dsv::verify_desc_offset(batch));
     a.gmax = reinterpret_cast<unsigned long long*>(base + dsv::verify_gmax_offset(batch));
+    a.prof = reinterpret_cast<unsigned long long*>(base + dsv::verify_prof_offset(batch));
     if (dsv::stream_supported(a, dtype))
         return counted(dsv::launch_stream(a, (cudaStream_t)stream), 2);
     return counted(dsv::launch_verify(a, dtype, (cudaStream_t)stream), 1);

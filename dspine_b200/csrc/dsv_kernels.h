@@ -46,8 +46,12 @@ constexpr inline size_t verify_gmax_offset(int B) {
     return verify_desc_offset(B) + (size_t)B * 16 * 2 * sizeof(RowDesc);
 }
 // [u64 x B x 16]: greedy rows' packed (max key << 32 | ~first index), reset after use
-constexpr inline size_t verify_workspace_bytes(int B) {
+// [2 KB]: phase timers of profiling builds (-DDSV_PROFILE); unused otherwise
+constexpr inline size_t verify_prof_offset(int B) {
     return verify_gmax_offset(B) + (size_t)B * 16 * sizeof(unsigned long long);
+}
+constexpr inline size_t verify_workspace_bytes(int B) {
+    return verify_prof_offset(B) + 2048;
 }
 
 struct VerifyArgs {
@@ -89,6 +93,7 @@ struct VerifyArgs {
     TaskResult* res;
     RowDesc* desc;             // [B,16,2] row descriptors (streaming path)
     unsigned long long* gmax;  // [B,16] greedy rows: max key << 32 | (0xFFFFFFFF - first index)
+    unsigned long long* prof;  // profiling builds: phase timers
 };
 
 // launchers (return a dsv::Status)

@@ -52,8 +52,8 @@ constexpr float kTwo23 = 8388608.0f;
 
 // ---------------------------------------------------------------------------------------
 // optional phase profiling (builds with -DDSV_PROFILE only): thread 0 of every CTA adds the
-// %globaltimer duration of each phase to u64 counters in the workspace's task-result area,
-// which this path does not otherwise use: counter [cat * 16 + phase], task count at phase 15
+// %globaltimer duration of each phase to u64 counters in the workspace's profiling area:
+// counter [cat * 16 + phase], task count at phase 15; the chain kernel at [64 + phase]
 
 #ifdef DSV_PROFILE
 #define PROF_START() unsigned long long prof_t = globaltimer_ns()
@@ -61,7 +61,7 @@ constexpr float kTwo23 = 8388608.0f;
     do {                                                                                 \
         if (threadIdx.x == 0) {                                                          \
             const unsigned long long prof_n = globaltimer_ns();                          \
-            atomicAdd(reinterpret_cast<unsigned long long*>(a.res) + (cat_) * 16 + (ph), \
+            atomicAdd(a.prof + (cat_) * 16 + (ph), \
                       prof_n - prof_t);                                                  \
             prof_t = prof_n;                                                             \
         }                                                                                \
@@ -69,7 +69,7 @@ constexpr float kTwo23 = 8388608.0f;
 #define PROF_END(cat_, ph)                                                                  \
     do {                                                                                    \
         PROF_MARK(cat_, ph);                                                                \
-        if (threadIdx.x == 0) atomicAdd(reinterpret_cast<unsigned long long*>(a.res) + (cat_) * 16 + 15, 1ull); \
+        if (threadIdx.x == 0) atomicAdd(a.prof + (cat_) * 16 + 15, 1ull); \
     } while (0)
 #else
 #define PROF_START() \
@@ -1122,6 +1122,7 @@ __global__ void __launch_bounds__(kRT, DSV_ROWS_MIN_CTAS) rows_kernel(VerifyArgs
             // groups (rank order).  Each warp sums its groups (one bin per lane), thread g scans
             // group g, and the warp of the stopping group finds the bin.
             const uint32_t ngp = (npos + 31u) >> 5, ngn = (nneg + 31u) >> 5, ng = ngp + ngn;
+#pragma unroll 2
             for (uint32_t gi = wid; gi < ng; gi += kRW) {
                 const bool neg = gi >= ngp;
                 const uint32_t j = neg ? gi - ngp : gi;
@@ -1129,8 +1130,15 @@ __global__ void __launch_bounds__(kRT, DSV_ROWS_MIN_CTAS) rows_kernel(VerifyArgs
                 const uint32_t lim = neg ? nneg : npos;
                 uint32_t cnt = 0;
                 unsigned long long ms = 0;
-                if (i < lim) {
-                    cnt = sh->hist[(neg ? npos : 0u) + i];
+                if (i < lim) cnt = sh->hist[(neg ? npos : 0u) + i];
+                if (!__any_sync(0xffffffffu, cnt != 0u)) {     // empty group
+                    if (lane == 0) {
+                        sh->gcnt[gi] = 0u;
+                        sh->gmass[gi] = 0ull;
+                    }
+                    continue;
+                }
+                {
                     const uint32_t key = (neg ? negtop : topkey) - i;
                     if (cnt && key >= klo)
                         ms = (unsigned long long)cnt * fix_of_y(y_clamped(bf(key_bits(key)), m, ti.c));
@@ -1347,7 +1355,7 @@ __device__ __forceinline__ uint64_t fix_w(float w) {
 __device__ __forceinline__ float resid_w(const RowDesc& dp, const RowDesc* dq, long long onehot,
                                          bool pure, uint32_t pbits, uint32_t qbits, int i) {
     const float p = row_prob(dp, bf(pbits), pbits, i);
-    if (pure) return p;
+    if (pure || !(p > 0.0f)) return pure ? p : 0.0f;  // p = 0: max(0 - clamp01(q), 0) = 0
     float q;
     if (dq) q = row_prob(*dq, bf(qbits), qbits, i);
     else q = (i == onehot) ? 1.0f : 0.0f;
@@ -1468,6 +1476,21 @@ __global__ void __launch_bounds__(kNT) chain_kernel(VerifyArgs a) {
             }
         }
     } else {
+#ifdef DSV_PROFILE
+    unsigned long long cprof = globaltimer_ns();
+#define CPROF(ph)                                                                               \
+    do {                                                                                        \
+        if (rank == 0 && tid == 0) {                                                            \
+            const unsigned long long n_ = globaltimer_ns();                                    \
+            atomicAdd(a.prof + 64 + (ph), n_ - cprof);   \
+            cprof = n_;                                                                         \
+        }                                                                                       \
+    } while (0)
+#else
+#define CPROF(ph) \
+    do {          \
+    } while (0)
+#endif
     // ---- chain: step s compares draft s+1 with target row s (warp 0, one lane per step) ----
     if (tid < 32) {
         bool acc = false;
@@ -1501,6 +1524,7 @@ __global__ void __launch_bounds__(kNT) chain_kernel(VerifyArgs a) {
         if (lane == 0) sh->sel[0] = na;
     }
     __syncthreads();
+    CPROF(0);
     const int acc = sh->sel[0];
     const bool pure = acc == cap - 1;
     const float uf = a.uf[b];
@@ -1545,6 +1569,7 @@ __global__ void __launch_bounds__(kNT) chain_kernel(VerifyArgs a) {
             }
         }
         __syncthreads();
+        CPROF(1);
         // warp w scans elements [e0 + w*Lw, ...) in groups of 32 consecutive elements
         const int n = e1 - e0;
         const int Lw = (((n + kNW - 1) / kNW) + 31) & ~31;
@@ -1568,7 +1593,9 @@ __global__ void __launch_bounds__(kNT) chain_kernel(VerifyArgs a) {
                 for (int i = 0; i < kNW; ++i) t_ += sh->tsum[i];
                 sh->pub[ex & 1][0] = t_;
             }
+            CPROF(2);
             cluster_barrier();
+            CPROF(3);
             const unsigned exn = ex++;
             M = 0;
             cum = 0;
@@ -1627,7 +1654,12 @@ __global__ void __launch_bounds__(kNT) chain_kernel(VerifyArgs a) {
             // no crossing (mass 0): the default of the reference loop
             if (tid == 0) write_request(a, b, acc, (long long)a.V - 1);
         }
+        CPROF(4);
         cluster_barrier();  // peers may still read this CTA's totals
+        CPROF(5);
+#ifdef DSV_PROFILE
+        if (rank == 0 && tid == 0) atomicAdd(a.prof + 64 + 15, 1ull);
+#endif
     }
     }
 
@@ -1650,31 +1682,524 @@ __global__ void __launch_bounds__(kNT) chain_kernel(VerifyArgs a) {
 }
 
 // ---------------------------------------------------------------------------------------
+// chain + bonus + outputs: kCP CTAs per request, no cluster
+//
+// Every CTA of a request decides the chain (warp 0, one lane per step), then takes one slice
+// of the bonus row: the slice's exact residual mass goes to the request's spare greedy-maximum
+// slots in the workspace (unused by sampled requests).  The last CTA of the request (a done
+// counter) forms the threshold from the slice totals, rescans only the crossing slice tile by
+// tile (block scans) and writes the five outputs; the last request packs tokens and KV slots.
+// p is evaluated only for kept elements and q only where p > 0 (the residual is 0 elsewhere).
+
+constexpr int kCP = 16;                   // CTAs (slices) per request
+constexpr int kCT = 256;                  // threads per CTA (4 CTAs per SM: one wave)
+constexpr int kCTW = kCT / 32;
+static_assert(kCP <= kT, "slice totals live in the request's kT greedy-maximum slots");
+static_assert(kCP * 2 <= 2 * kT, "tile masses live in the request's task-result area (32 u64)");
+
+struct Chain3Smem {
+    uint2 queue[kCTW][256];        // per warp: kept elements of one vector per lane
+    unsigned long long own[kCT];   // crossing tile: mass per owner thread
+    unsigned long long wsum[kCTW];
+    uint32_t red_a[kCTW], red_b[kCTW];
+    unsigned long long slice[kCP];
+    long long thr, base;
+    int acc, bonus, flag, last, cross;
+    unsigned long long total;
+};
+
+template <int NT>
+__device__ void compact_all_nt(const VerifyArgs& a, uint32_t* red_a, uint32_t* red_b) {
+    constexpr int NW = NT / 32;
+    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
+    int run_c = 0, run_f = 0;
+    if (tid == 0) {
+        a.offsets[0] = 0;
+        a.free_offsets[0] = 0;
+    }
+    for (int b0 = 0; b0 < a.B; b0 += NT) {
+        const int b = b0 + tid;
+        int cm = 0, fr = 0;
+        if (b < a.B) {
+            const int cap = clamp_cap(a.caps[b]);
+            cm = __ldcg(&a.commit[b]);
+            fr = cap - cm;
+            if (fr < 0) fr = 0;
+        }
+        const uint32_t ic = warp_incl_u32((uint32_t)cm);
+        const uint32_t iff = warp_incl_u32((uint32_t)fr);
+        if (lane == 31) {
+            red_a[w] = ic;
+            red_b[w] = iff;
+        }
+        __syncthreads();
+        int wc = 0, wf = 0, tc = 0, tf = 0;
+        for (int q = 0; q < NW; ++q) {
+            if (q < w) {
+                wc += (int)red_a[q];
+                wf += (int)red_b[q];
+            }
+            tc += (int)red_a[q];
+            tf += (int)red_b[q];
+        }
+        __syncthreads();
+        if (b < a.B) {
+            const int oc = run_c + wc + (int)ic - cm;
+            const int of = run_f + wf + (int)iff - fr;
+            a.offsets[b + 1] = oc + cm;
+            a.free_offsets[b + 1] = of + fr;
+            const long long srow = a.slot_row[b];
+            bool bad = false;
+            for (int i = 0; i < cm; ++i) {
+                a.tok_out[oc + i] = __ldcg(&a.output[b * kT + i]);
+                const long long si = srow + i;
+                const bool in = si >= 0 && si < a.slots_len;
+                bad |= !in;
+                a.slot_out[oc + i] = in ? a.slots[si] : -1;
+            }
+            for (int j = 0; j < fr; ++j) {
+                const long long si = srow + cm + j;
+                const bool in = si >= 0 && si < a.slots_len;
+                bad |= !in;
+                a.free_out[of + j] = in ? a.slots[si] : -1;
+            }
+            if (bad) atomicOr(&a.ws->err, 4u);
+        }
+        run_c += tc;
+        run_f += tf;
+    }
+}
+
+// the bonus row of one request: p row (target), q (draft row, one-hot or none)
+struct BonusRow {
+    RowDesc dt, dd;
+    bool has_dq;
+    const uint16_t* prow;
+    const uint16_t* qrow;
+    long long onehot;
+    int poff;     // misalignment of prow in elements
+    int nvp;      // 16-byte vectors covering the p row
+    bool qvec;    // q row has the same alignment: load q vectors alongside
+};
+
+constexpr int kCTileV = 4 * kCT;           // vectors per tile: 4 consecutive per thread
+constexpr int kCMaxTiles = 2;              // tiles per slice (kCP x kCMaxTiles <= 32): V <= kMaxV
+constexpr int kMaxV = 8 * (kCP * kCMaxTiles * kCTileV - kCP) - 16;  // vectors of every slice fit
+
+__device__ __forceinline__ bool kept_in(const RowDesc& d, uint32_t u16, int i) {
+    const uint32_t k = okey(u16);
+    return (k > d.kstar) || (k == d.kstar && i <= d.tie_cut);
+}
+
+// residual fixed-point weight of one kept p element (p bits pb, q bits qb, index i)
+__device__ __forceinline__ unsigned long long resid_kept(const BonusRow& r, bool pure, uint32_t pb,
+                                                         uint32_t qb, int i) {
+    const float p = __fmul_rn(exp2c(__fmul_rn(__fadd_rn(bf(pb), -r.dt.m), r.dt.c)), r.dt.inv_s);
+    if (!(p > 0.0f)) return 0ull;
+    float w = p;
+    if (!pure) {
+        float q;
+        if (r.has_dq) q = row_prob(r.dd, bf(qb), qb, i);
+        else q = (i == r.onehot) ? 1.0f : 0.0f;
+        const float qq = (q >= 0.0f && q <= 1.0f) ? q : 0.0f;
+        w = fmaxf(__fsub_rn(p, qq), 0.0f);
+    }
+    return fix_w(w);
+}
+
+// p and q bits of the 8 elements of p-row vector v
+__device__ __forceinline__ void load8(const BonusRow& r, int v, bool pure, uint4& x, uint4& y) {
+    x = __ldg(reinterpret_cast<const uint4*>(r.prow - r.poff) + v);
+    y = make_uint4(0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u);
+    if (!pure && r.has_dq && r.qvec) y = __ldg(reinterpret_cast<const uint4*>(r.qrow - r.poff) + v);
+}
+
+__device__ __forceinline__ uint32_t half16(const uint4& x, int h) {
+    const uint32_t w = h < 2 ? x.x : (h < 4 ? x.y : (h < 6 ? x.z : x.w));
+    return (h & 1) ? (w >> 16) : (w & 0xFFFFu);
+}
+
+// Residual mass of tile [tv0, tv1) (vectors; thread t owns 4 consecutive vectors).  Kept p
+// elements are queued per warp (shared memory) and evaluated 32 at a time, so the exps are
+// not serialised by lanes whose elements are outside the kept set.  Returns this thread's sum.
+__device__ unsigned long long tile_mass(const BonusRow& r, int V, int tv0, int tv1, bool pure,
+                                        uint2* queue) {
+    const int tid = threadIdx.x, lane = tid & 31;
+    unsigned long long mine = 0;
+    // the thread's 4 vectors (p and q) are loaded before any is used
+    uint4 xa[4], ya[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        const int v = tv0 + 4 * tid + u;
+        xa[u] = make_uint4(0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u);
+        ya[u] = xa[u];
+        if (v < tv1) load8(r, v, pure, xa[u], ya[u]);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+        const int v = tv0 + 4 * tid + u;
+        const uint4 x = xa[u], y = ya[u];
+        uint32_t keep = 0;
+#pragma unroll
+        for (int h = 0; h < 8; ++h) {
+            const int i = 8 * v + h - r.poff;
+            if (v < tv1 && i >= 0 && i < V && kept_in(r.dt, half16(x, h), i)) keep |= 1u << h;
+        }
+        const uint32_t n = __popc(keep);
+        const uint32_t incl = warp_incl_u32(n);
+        const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
+        uint32_t slot = incl - n;
+        while (keep) {
+            const int h = __ffs(keep) - 1;
+            keep &= keep - 1;
+            const int i = 8 * v + h - r.poff;
+            uint32_t qb = half16(y, h);
+            if (!pure && r.has_dq && !r.qvec) qb = r.qrow ? (uint32_t)__ldg(r.qrow + i) : 0xFF80u;
+            queue[slot++] = make_uint2(half16(x, h) | (qb << 16), (uint32_t)i);
+        }
+        __syncwarp();
+        for (uint32_t e = lane; e < total; e += 32) {
+            const uint2 q = queue[e];
+            mine += resid_kept(r, pure, q.x & 0xFFFFu, q.x >> 16, (int)q.y);
+        }
+        __syncwarp();
+    }
+    return mine;
+}
+
+__device__ __forceinline__ unsigned long long block_sum_u64(unsigned long long v,
+                                                            unsigned long long* wsum) {
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    v = warp_sum_u64(v);
+    __syncthreads();
+    if (lane == 0) wsum[wid] = v;
+    __syncthreads();
+    unsigned long long t = 0;
+#pragma unroll
+    for (int w = 0; w < kCTW; ++w) t += wsum[w];
+    __syncthreads();
+    return t;
+}
+
+// per-thread residual masses of tile [tv0, tv1) (thread t owns vectors tv0 + 4t .. +3): kept
+// elements are queued per warp and evaluated 32 at a time; each mass is added to its owner
+__device__ unsigned long long tile_owner_mass(const BonusRow& r, int V, int tv0, int tv1, bool pure,
+                                              Chain3Smem* sh) {
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    uint2* queue = sh->queue[wid];
+    sh->own[tid] = 0ull;
+    __syncthreads();
+#pragma unroll 1
+    for (int u = 0; u < 4; ++u) {
+        const int v = tv0 + 4 * tid + u;
+        uint4 x = make_uint4(0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u), y = x;
+        if (v < tv1) load8(r, v, pure, x, y);
+        uint32_t keep = 0;
+#pragma unroll
+        for (int h = 0; h < 8; ++h) {
+            const int i = 8 * v + h - r.poff;
+            if (v < tv1 && i >= 0 && i < V && kept_in(r.dt, half16(x, h), i)) keep |= 1u << h;
+        }
+        const uint32_t n = __popc(keep);
+        const uint32_t incl = warp_incl_u32(n);
+        const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
+        uint32_t slot = incl - n;
+        while (keep) {
+            const int h = __ffs(keep) - 1;
+            keep &= keep - 1;
+            const int i = 8 * v + h - r.poff;
+            uint32_t qb = half16(y, h);
+            if (!pure && r.has_dq && !r.qvec) qb = r.qrow ? (uint32_t)__ldg(r.qrow + i) : 0xFF80u;
+            queue[slot++] = make_uint2(half16(x, h) | (qb << 16), (uint32_t)i | ((uint32_t)lane << 27));
+        }
+        __syncwarp();
+        for (uint32_t e = lane; e < total; e += 32) {
+            const uint2 q = queue[e];
+            const int i = (int)(q.y & 0x07FFFFFFu);
+            const unsigned long long f = resid_kept(r, pure, q.x & 0xFFFFu, q.x >> 16, i);
+            if (f) atomicAdd(&sh->own[(wid << 5) | (q.y >> 27)], f);
+        }
+        __syncwarp();
+    }
+    __syncthreads();
+    return sh->own[tid];
+}
+
+__global__ void __launch_bounds__(kCT, 4) chain3_kernel(VerifyArgs a) {
+    __shared__ Chain3Smem shm;
+    Chain3Smem* sh = &shm;
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const int b = blockIdx.x / kCP, rank = blockIdx.x % kCP;
+    const int cap = clamp_cap(a.caps[b]);
+    const float T = a.temperature[b];
+    const int kq = a.top_k[b];
+    const float c = log2e_over(T);
+    const bool greedy = is_greedy(T, kq, c);
+    const bool onehot_q = greedy || a.drf == nullptr;
+    const uint16_t* tgt = reinterpret_cast<const uint16_t*>(a.tgt);
+    const uint16_t* drf = reinterpret_cast<const uint16_t*>(a.drf);
+    bool finished = false;  // this CTA wrote the request's outputs
+#ifdef DSV_PROFILE
+    unsigned long long cp3 = globaltimer_ns();
+    if (tid == 0) atomicMin(a.prof + 80, cp3);  // kernel start (host presets it to ~0)
+#define CP3(cond, ph)                                                                          \
+    do {                                                                                       \
+        if ((cond) && tid == 0) {                                                              \
+            const unsigned long long n_ = globaltimer_ns();                                   \
+            atomicAdd(a.prof + 64 + (ph), n_ - cp3);    \
+            cp3 = n_;                                                                          \
+        }                                                                                      \
+    } while (0)
+#else
+#define CP3(cond, ph) \
+    do {              \
+    } while (0)
+#endif
+
+    if (greedy) {
+        // one-hot p at each target row's first argmax (packed by the row kernel), one-hot q at
+        // the drafted token: rank 0 decides alone and resets the packed maxima
+        if (rank == 0 && tid < 32) {
+            const int s = lane;
+            bool accp = false;
+            long long am = 0;
+            if (s < cap) {
+                const unsigned long long g = a.gmax[b * kT + s];
+                am = g ? (long long)(0xFFFFFFFFull - (g & 0xFFFFFFFFull)) : 0ll;
+            }
+            if (s < cap - 1) {
+                const long long tok = a.cand[b * kT + s + 1];
+                const bool valid = tok >= 0 && tok < a.V;
+                const float p = (valid && tok == am) ? 1.0f : 0.0f;
+                const float q = valid ? 1.0f : 0.0f;
+                accp = q > 0.0f && q <= 1.0f && __fmul_rn(a.u[b * 15 + s], q) < p;
+            }
+            const uint32_t rej = __ballot_sync(0xffffffffu, !accp) & ((1u << (cap - 1)) - 1u);
+            const int acc = rej ? __ffs(rej) - 1 : cap - 1;
+            const long long ga = __shfl_sync(0xffffffffu, am, acc);
+            __syncwarp();
+            if (s < cap) a.gmax[b * kT + s] = 0ull;
+            if (lane == 0) {
+                // the residual against a one-hot q is the same one-hot or empty (then the
+                // fallback to p): the draw is the argmax unless u is outside [0, 1)
+                const long long thr = scale_floor(a.uf[b], 1ull << kFixBits);
+                const long long bo = thr == -2 ? (long long)a.V - 1 : (thr < 0 ? 0ll : ga);
+                write_request(a, b, acc, bo);
+            }
+        }
+        finished = rank == 0;
+    } else {
+        // ---- chain: step s compares draft s+1 with target row s (warp 0, one lane per step)
+        if (tid < 32) {
+            bool acc = false;
+            const int s = lane;
+            if (s < cap - 1) {
+                const long long tok = a.cand[b * kT + s + 1];
+                const bool valid = tok >= 0 && tok < a.V;
+                float p = 0.0f, q = 0.0f;
+                if (valid) {
+                    const RowDesc dt = a.desc[(b * kT + s) * 2 + 0];
+                    const long long tr = a.tgt_row[b] + s;
+                    if (tr >= 0 && tr < a.tgt_rows) {
+                        const uint32_t pb = tgt[tr * a.stride + tok];
+                        p = row_prob(dt, bf(pb), pb, (int)tok);
+                    }
+                    if (onehot_q) {
+                        q = 1.0f;
+                    } else {
+                        const RowDesc dd = a.desc[(b * kT + s) * 2 + 1];
+                        const long long dr = a.drf_row[b] + s;
+                        if (dr >= 0 && dr < a.drf_rows) {
+                            const uint32_t qb = drf[dr * a.stride + tok];
+                            q = row_prob(dd, bf(qb), qb, (int)tok);
+                        }
+                    }
+                }
+                acc = q > 0.0f && q <= 1.0f && __fmul_rn(a.u[b * 15 + s], q) < p;
+            }
+            const uint32_t rej = __ballot_sync(0xffffffffu, !acc) &
+                                 ((cap - 1 >= 32) ? 0xffffffffu : ((1u << (cap - 1)) - 1u));
+            if (lane == 0) sh->acc = rej ? __ffs(rej) - 1 : cap - 1;
+        }
+        __syncthreads();
+        CP3(true, 0);
+        const int acc = sh->acc;
+        const bool pure0 = acc == cap - 1;
+        const int V = a.V;
+        BonusRow r;
+        r.dt = a.desc[(b * kT + acc) * 2 + 0];
+        const long long tr = a.tgt_row[b] + acc;
+        r.prow = (tr >= 0 && tr < a.tgt_rows) ? tgt + tr * a.stride : nullptr;
+        r.has_dq = false;
+        r.qrow = nullptr;
+        r.onehot = -1;
+        if (!pure0) {
+            if (onehot_q) {
+                r.onehot = a.cand[b * kT + acc + 1];
+            } else {
+                r.dd = a.desc[(b * kT + acc) * 2 + 1];
+                r.has_dq = true;
+                const long long dr = a.drf_row[b] + acc;
+                if (dr >= 0 && dr < a.drf_rows) r.qrow = drf + dr * a.stride;
+            }
+        }
+        r.poff = r.prow ? (int)((reinterpret_cast<uintptr_t>(r.prow) & 15u) >> 1) : 0;
+        r.nvp = r.prow ? (V + r.poff + 7) >> 3 : 0;
+        r.qvec = r.qrow && (int)((reinterpret_cast<uintptr_t>(r.qrow) & 15u) >> 1) == r.poff;
+        // this CTA's slice of vectors, in tiles of kCTileV; tile masses go to the request's
+        // task-result area (kCP x kCMaxTiles u64), slice totals to the spare maximum slots
+        const int per = (r.nvp + kCP - 1) / kCP;
+        const int v0 = min(rank * per, r.nvp), v1 = min(v0 + per, r.nvp);
+        unsigned long long* slots = a.gmax + (size_t)b * kT;  // spare for sampled requests
+        unsigned long long* tmass = reinterpret_cast<unsigned long long*>(a.res) + (size_t)b * kT * 2;
+        auto slice_tiles = [&](int q, bool pure_) -> unsigned long long {
+            const int u0 = min(q * per, r.nvp), u1 = min(u0 + per, r.nvp);
+            unsigned long long tot = 0;
+            for (int t = 0; u0 + t * kCTileV < u1 && t < kCMaxTiles; ++t) {
+                const int tv0 = u0 + t * kCTileV, tv1 = min(tv0 + kCTileV, u1);
+                const unsigned long long m =
+                    block_sum_u64(tile_mass(r, V, tv0, tv1, pure_, sh->queue[wid]), sh->wsum);
+                if (tid == 0) tmass[q * kCMaxTiles + t] = m;
+                tot += m;
+            }
+            return tot;
+        };
+        const unsigned long long mine = slice_tiles(rank, pure0);
+        (void)v0;
+        (void)v1;
+        CP3(true, 1);
+        if (tid == 0) {
+            slots[rank] = mine;
+            __threadfence();
+            const unsigned old = atomicAdd(&a.done[b], 1u);
+            sh->last = old == (unsigned)(kCP - 1);
+        }
+        __syncthreads();
+        if (sh->last) {
+            __threadfence();
+            bool pure = pure0;
+            if (tid < kCP) sh->slice[tid] = __ldcg(&slots[tid]);
+            __syncthreads();
+            unsigned long long M = 0;
+#pragma unroll
+            for (int q = 0; q < kCP; ++q) M += sh->slice[q];
+            if (!pure && M == 0) {
+                // zero residual mass: draw from p (this CTA recomputes every slice)
+                pure = true;
+                M = 0;
+                for (int q = 0; q < kCP; ++q) {
+                    const unsigned long long t = slice_tiles(q, true);
+                    if (tid == 0) sh->slice[q] = t;
+                    M += t;
+                }
+                __syncthreads();
+            }
+            CP3(true, 2);
+            const long long thr = scale_floor(a.uf[b], M);
+            long long bonus = (long long)V - 1;
+            if (thr == -1) {
+                bonus = 0;  // u < 0: the first running sum already exceeds it
+            } else if (thr != -2 && M != 0) {
+                // the crossing slice and tile from the totals, then the tile element by element
+                long long base = 0;
+                int qs = -1, tq = -1;
+                for (int q = 0; q < kCP && qs < 0; ++q) {
+                    const long long t = (long long)sh->slice[q];
+                    if (base + t > thr) {
+                        qs = q;
+                        const int u0 = min(q * per, r.nvp), u1 = min(u0 + per, r.nvp);
+                        for (int t2 = 0; u0 + t2 * kCTileV < u1 && t2 < kCMaxTiles; ++t2) {
+                            const long long tm = (long long)__ldcg(&tmass[q * kCMaxTiles + t2]);
+                            if (base + tm > thr) {
+                                tq = t2;
+                                break;
+                            }
+                            base += tm;
+                        }
+                    } else {
+                        base += t;
+                    }
+                }
+                if (qs >= 0 && tq >= 0) {
+                    const int u0 = min(qs * per, r.nvp), u1 = min(u0 + per, r.nvp);
+                    const int tv0 = u0 + tq * kCTileV, tv1 = min(tv0 + kCTileV, u1);
+                    // per-thread masses of the tile (4 consecutive vectors per thread, so thread
+                    // order is index order): queued kept elements add into their owner's slot
+                    __syncthreads();
+                    const unsigned long long own = tile_owner_mass(r, V, tv0, tv1, pure, sh);
+                    const unsigned long long incl = warp_incl_u64(own);
+                    if (lane == 31) sh->wsum[wid] = incl;
+                    __syncthreads();
+                    unsigned long long before = 0;
+#pragma unroll
+                    for (int w = 0; w < kCTW; ++w)
+                        if (w < wid) before += sh->wsum[w];
+                    long long run = base + (long long)(before + incl - own);
+                    if (tid == 0) sh->bonus = -1;
+                    __syncthreads();
+                    if (run <= thr && run + (long long)own > thr) {
+                        // this thread's 32 elements in order
+                        for (int u = 0; u < 4 && sh->bonus < 0; ++u) {
+                            const int v = tv0 + 4 * tid + u;
+                            if (v >= tv1) break;
+                            uint4 x, y;
+                            load8(r, v, pure, x, y);
+                            for (int h = 0; h < 8; ++h) {
+                                const int i = 8 * v + h - r.poff;
+                                if (i < 0 || i >= V || !kept_in(r.dt, half16(x, h), i)) continue;
+                                uint32_t qb = half16(y, h);
+                                if (!pure && r.has_dq && !r.qvec)
+                                    qb = r.qrow ? (uint32_t)__ldg(r.qrow + i) : 0xFF80u;
+                                run += (long long)resid_kept(r, pure, half16(x, h), qb, i);
+                                if (run > thr) {
+                                    sh->bonus = i;
+                                    break;
+                                }
+                            }
+                        }
+                    }
+                    __syncthreads();
+                    if (sh->bonus >= 0) bonus = sh->bonus;
+                }
+            }
+            CP3(true, 3);
+#ifdef DSV_PROFILE
+            if (tid == 0) atomicAdd(a.prof + 64 + 15, 1ull);
+            if (tid == 0 && b < 128) a.prof[128 + b] = globaltimer_ns();
+#endif
+            if (tid == 0) {
+                write_request(a, b, acc, bonus);
+                for (int q = 0; q < kCP; ++q) slots[q] = 0ull;
+                a.done[b] = 0u;
+            }
+            finished = true;
+        }
+    }
+
+    // ---- completion: the last request packs tokens and KV slots ---------------------------
+    if (finished) {
+        __syncthreads();
+        if (tid == 0) {
+            __threadfence();
+            const unsigned old = atomicAdd(&a.ws->finalized, 1u);
+            sh->flag = old == (unsigned)(a.B - 1);
+        }
+        __syncthreads();
+        if (sh->flag) {
+            __threadfence();
+            if (a.tok_out != nullptr) compact_all_nt<kCT>(a, sh->red_a, sh->red_b);
+            __syncthreads();
+            if (tid == 0) a.ws->finalized = 0;
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------
 // launcher
 
 int launch_chain(VerifyArgs a, cudaStream_t stream) {
-    cudaLaunchConfig_t cfg = {};
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = kCS;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    const int L = ((a.V + kCS - 1) / kCS + 7) & ~7;
-    const size_t smem = (size_t)2 * (L + 16) * sizeof(uint16_t);
-    static size_t attr_smem = 0;
-    if (smem > 48 * 1024 && smem > attr_smem) {
-        if (cudaFuncSetAttribute(chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-            return kLaunchFailed;
-        attr_smem = smem;
-    }
-    cfg.blockDim = dim3(kNT, 1, 1);
-    cfg.dynamicSmemBytes = smem;
-    cfg.stream = stream;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
-    cfg.gridDim = dim3(a.B * kCS, 1, 1);
-    if (cudaLaunchKernelEx(&cfg, chain_kernel, a) != cudaSuccess) return kLaunchFailed;
-    return kOk;
+    chain3_kernel<<<a.B * kCP, kCT, 0, stream>>>(a);
+    return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
 }
 
 }  // namespace st
@@ -1684,7 +2209,7 @@ bool stream_supported(const VerifyArgs& a, int dtype) {
     if (a.B > st::kMaxB || a.desc == nullptr || a.gmax == nullptr) return false;
     if ((reinterpret_cast<uintptr_t>(a.tgt) & 1u) || (a.drf && (reinterpret_cast<uintptr_t>(a.drf) & 1u)))
         return false;
-    return a.V <= 262144;
+    return a.V <= st::kMaxV;
 }
 
 int launch_stream(VerifyArgs a, cudaStream_t stream) {
