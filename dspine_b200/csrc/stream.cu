@@ -22,7 +22,6 @@
 // equals the CPU oracle bit for bit.  Bulk passes clamp y at -64 before the exponent trick:
 // every y below -41.5 has fix(exp2(y)) = 0, so the clamp never changes a fix value; exact
 // probabilities (chain, residual) use the unclamped exp2c with its y < -125 -> 0 rule.
-#include <cooperative_groups.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stddef.h>
@@ -31,14 +30,10 @@
 #include "dsv_common.cuh"
 #include "dsv_kernels.h"
 
-namespace cg = cooperative_groups;
 
 namespace dsv {
 namespace st {
 
-constexpr int kCS = 8;           // chain kernel: CTAs per request cluster
-constexpr int kNT = 512;         // chain kernel: threads per CTA
-constexpr int kNW = kNT / 32;
 constexpr int kBins = 24;        // level-1 bins: min(rne(-0.75 y), 23)
 constexpr int kSub = 23;         // level-2 bins: rne(-16.5 y) - 22 b1 + 11, clamped to [0, 22]
 constexpr int kMaxB = 1024;      // requests per launch handled by this path
@@ -85,11 +80,6 @@ constexpr float kTwo23 = 8388608.0f;
 
 // ---------------------------------------------------------------------------------------
 // small helpers
-
-__device__ __forceinline__ void cluster_barrier() {
-    // non-.aligned forms: correct even if a warp reaches the barrier diverged
-    asm volatile("barrier.cluster.arrive.release;\n\tbarrier.cluster.wait.acquire;" ::: "memory");
-}
 
 __device__ __forceinline__ uint32_t okey(uint32_t u16) { return Elem<__nv_bfloat16>::key(u16); }
 __device__ __forceinline__ uint32_t key_bits(uint32_t k) {
@@ -1334,86 +1324,12 @@ int launch_rows_cta(VerifyArgs a, cudaStream_t stream) {
     return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
 }
 
-// ---------------------------------------------------------------------------------------
-// chain + bonus + outputs (one cluster per request)
-
-struct ChainSmem {
-    unsigned long long tsum[kNW];  // warp sums
-    unsigned long long pub[2][2];  // per exchange: CTA total
-    int32_t sel[8];
-    unsigned long long red64[kNW];
-    uint32_t red_a[kNW], red_b[kNW];
-    int flag;
-};
-
 __device__ __forceinline__ uint64_t fix_w(float w) {
     if (!(w > 0.0f)) return 0;
     return fix01(fminf(w, 1.0f));
 }
 
-// residual weight of element i (oracle logit_w): pure p, or max(p - clamp01(q), 0)
-__device__ __forceinline__ float resid_w(const RowDesc& dp, const RowDesc* dq, long long onehot,
-                                         bool pure, uint32_t pbits, uint32_t qbits, int i) {
-    const float p = row_prob(dp, bf(pbits), pbits, i);
-    if (pure || !(p > 0.0f)) return pure ? p : 0.0f;  // p = 0: max(0 - clamp01(q), 0) = 0
-    float q;
-    if (dq) q = row_prob(*dq, bf(qbits), qbits, i);
-    else q = (i == onehot) ? 1.0f : 0.0f;
-    const float qq = (q >= 0.0f && q <= 1.0f) ? q : 0.0f;
-    return fmaxf(__fsub_rn(p, qq), 0.0f);
-}
-
-__device__ void compact_all(const VerifyArgs& a, ChainSmem* sh) {
-    const int tid = threadIdx.x, lane = tid & 31, w = tid >> 5;
-    int run_c = 0, run_f = 0;
-    if (tid == 0) { a.offsets[0] = 0; a.free_offsets[0] = 0; }
-    for (int b0 = 0; b0 < a.B; b0 += kNT) {
-        const int b = b0 + tid;
-        int cm = 0, fr = 0;
-        if (b < a.B) {
-            const int cap = clamp_cap(a.caps[b]);
-            cm = __ldcg(&a.commit[b]);
-            fr = cap - cm;
-            if (fr < 0) fr = 0;
-        }
-        const uint32_t ic = warp_incl_u32((uint32_t)cm);
-        const uint32_t iff = warp_incl_u32((uint32_t)fr);
-        if (lane == 31) { sh->red_a[w] = ic; sh->red_b[w] = iff; }
-        __syncthreads();
-        int wc = 0, wf = 0, tc = 0, tf = 0;
-        for (int q = 0; q < kNW; ++q) {
-            if (q < w) { wc += (int)sh->red_a[q]; wf += (int)sh->red_b[q]; }
-            tc += (int)sh->red_a[q];
-            tf += (int)sh->red_b[q];
-        }
-        __syncthreads();
-        if (b < a.B) {
-            const int oc = run_c + wc + (int)ic - cm;
-            const int of = run_f + wf + (int)iff - fr;
-            a.offsets[b + 1] = oc + cm;
-            a.free_offsets[b + 1] = of + fr;
-            const long long srow = a.slot_row[b];
-            bool bad = false;
-            for (int i = 0; i < cm; ++i) {
-                a.tok_out[oc + i] = __ldcg(&a.output[b * kT + i]);
-                const long long si = srow + i;
-                const bool in = si >= 0 && si < a.slots_len;
-                bad |= !in;
-                a.slot_out[oc + i] = in ? a.slots[si] : -1;
-            }
-            for (int j = 0; j < fr; ++j) {
-                const long long si = srow + cm + j;
-                const bool in = si >= 0 && si < a.slots_len;
-                bad |= !in;
-                a.free_out[of + j] = in ? a.slots[si] : -1;
-            }
-            if (bad) atomicOr(&a.ws->err, 4u);
-        }
-        run_c += tc;
-        run_f += tf;
-    }
-}
-
+// the five outputs of request b (sampling/rejection.py:66-98 output convention)
 __device__ void write_request(const VerifyArgs& a, int b, int acc, long long bonus) {
     a.accept[b] = acc;
     a.commit[b] = acc + 1;
@@ -1425,260 +1341,6 @@ __device__ void write_request(const VerifyArgs& a, int b, int acc, long long bon
         a.output[b * kT + i] = v;
     }
     a.new_seq[b] = a.prefix[b] + acc + 1;
-}
-
-__global__ void __launch_bounds__(kNT) chain_kernel(VerifyArgs a) {
-    extern __shared__ __align__(16) unsigned char chain_smem[];
-    __shared__ ChainSmem shm;
-    ChainSmem* sh = &shm;
-    cg::cluster_group cluster = cg::this_cluster();
-    const int tid = threadIdx.x, lane = tid & 31;
-    const int rank = (int)cluster.block_rank();
-    const int b = blockIdx.x / kCS;  // gridDim = B * kCS: one cluster per request
-    const int cap = clamp_cap(a.caps[b]);
-    const float T = a.temperature[b];
-    const int kq = a.top_k[b];
-    const float c = log2e_over(T);
-    const bool greedy = is_greedy(T, kq, c);
-    const bool onehot_q = greedy || a.drf == nullptr;
-    const uint16_t* tgt = reinterpret_cast<const uint16_t*>(a.tgt);
-    const uint16_t* drf = reinterpret_cast<const uint16_t*>(a.drf);
-
-    if (greedy) {
-        // one-hot p at each target row's first argmax (packed by the row kernel), one-hot q at
-        // the drafted token: rank 0 decides alone and resets the packed maxima for the next launch
-        if (rank == 0 && tid < 32) {
-            const int s = lane;
-            bool accp = false;
-            long long am = 0;
-            if (s < cap) {
-                const unsigned long long g = a.gmax[b * kT + s];
-                am = g ? (long long)(0xFFFFFFFFull - (g & 0xFFFFFFFFull)) : 0ll;
-            }
-            if (s < cap - 1) {
-                const long long tok = a.cand[b * kT + s + 1];
-                const bool valid = tok >= 0 && tok < a.V;
-                const float p = (valid && tok == am) ? 1.0f : 0.0f;
-                const float q = valid ? 1.0f : 0.0f;
-                accp = q > 0.0f && q <= 1.0f && __fmul_rn(a.u[b * 15 + s], q) < p;
-            }
-            const uint32_t rej = __ballot_sync(0xffffffffu, !accp) & ((1u << (cap - 1)) - 1u);
-            const int acc = rej ? __ffs(rej) - 1 : cap - 1;
-            const long long ga = __shfl_sync(0xffffffffu, am, acc);
-            __syncwarp();
-            if (s < cap) a.gmax[b * kT + s] = 0ull;
-            if (lane == 0) {
-                // the residual against a one-hot q is the same one-hot or empty (then the
-                // fallback to p): the draw is the argmax unless u is outside [0, 1)
-                const long long thr = scale_floor(a.uf[b], 1ull << kFixBits);
-                const long long bo = thr == -2 ? (long long)a.V - 1 : (thr < 0 ? 0ll : ga);
-                write_request(a, b, acc, bo);
-            }
-        }
-    } else {
-#ifdef DSV_PROFILE
-    unsigned long long cprof = globaltimer_ns();
-#define CPROF(ph)                                                                               \
-    do {                                                                                        \
-        if (rank == 0 && tid == 0) {                                                            \
-            const unsigned long long n_ = globaltimer_ns();                                    \
-            atomicAdd(a.prof + 64 + (ph), n_ - cprof);   \
-            cprof = n_;                                                                         \
-        }                                                                                       \
-    } while (0)
-#else
-#define CPROF(ph) \
-    do {          \
-    } while (0)
-#endif
-    // ---- chain: step s compares draft s+1 with target row s (warp 0, one lane per step) ----
-    if (tid < 32) {
-        bool acc = false;
-        const int s = lane;
-        if (s < cap - 1) {
-            const long long tok = a.cand[b * kT + s + 1];
-            const bool valid = tok >= 0 && tok < a.V;
-            float p = 0.0f, q = 0.0f;
-            if (valid) {
-                const RowDesc dt = a.desc[(b * kT + s) * 2 + 0];
-                const long long tr = a.tgt_row[b] + s;
-                if (tr >= 0 && tr < a.tgt_rows) {
-                    const uint32_t pb = tgt[tr * a.stride + tok];
-                    p = row_prob(dt, bf(pb), pb, (int)tok);
-                }
-                if (onehot_q) {
-                    q = 1.0f;
-                } else {
-                    const RowDesc dd = a.desc[(b * kT + s) * 2 + 1];
-                    const long long dr = a.drf_row[b] + s;
-                    if (dr >= 0 && dr < a.drf_rows) {
-                        const uint32_t qb = drf[dr * a.stride + tok];
-                        q = row_prob(dd, bf(qb), qb, (int)tok);
-                    }
-                }
-            }
-            acc = q > 0.0f && q <= 1.0f && __fmul_rn(a.u[b * 15 + s], q) < p;
-        }
-        const uint32_t rej = __ballot_sync(0xffffffffu, !acc) & ((cap - 1 >= 32) ? 0xffffffffu : ((1u << (cap - 1)) - 1u));
-        const int na = rej ? __ffs(rej) - 1 : cap - 1;
-        if (lane == 0) sh->sel[0] = na;
-    }
-    __syncthreads();
-    CPROF(0);
-    const int acc = sh->sel[0];
-    const bool pure = acc == cap - 1;
-    const float uf = a.uf[b];
-
-    const RowDesc dt = a.desc[(b * kT + acc) * 2 + 0];
-    {
-        const long long tr = a.tgt_row[b] + acc;
-        const bool trow_ok = tr >= 0 && tr < a.tgt_rows;
-        const RowDesc* dq = nullptr;
-        RowDesc dd;
-        long long onehot = -1;
-        const uint16_t* qrow = nullptr;
-        if (!pure) {
-            if (onehot_q) {
-                onehot = a.cand[b * kT + acc + 1];
-            } else {
-                dd = a.desc[(b * kT + acc) * 2 + 1];
-                dq = &dd;
-                const long long dr = a.drf_row[b] + acc;
-                if (dr >= 0 && dr < a.drf_rows) qrow = drf + dr * a.stride;
-            }
-        }
-        const uint16_t* prow = trow_ok ? tgt + tr * a.stride : nullptr;
-        const int L = ((a.V + kCS - 1) / kCS + 7) & ~7;
-        const int e0 = min(rank * L, a.V), e1 = min(e0 + L, a.V);
-        // stage this CTA's slice of both rows in shared memory (16-byte loads; element e sits
-        // at position e - e0 + off, off = the row's misalignment in elements)
-        uint16_t* sp = reinterpret_cast<uint16_t*>(chain_smem);
-        uint16_t* sq = sp + (L + 16);
-        const int poff = prow ? (int)((reinterpret_cast<uintptr_t>(prow) & 15u) >> 1) : 0;
-        const int qoff = qrow ? (int)((reinterpret_cast<uintptr_t>(qrow) & 15u) >> 1) : 0;
-        if (e1 > e0) {
-            if (prow) {
-                const uint4* src = reinterpret_cast<const uint4*>(prow + e0 - poff);
-                const int nv = (e1 - e0 + poff + 7) >> 3;
-                for (int v = tid; v < nv; v += kNT) reinterpret_cast<uint4*>(sp)[v] = __ldg(src + v);
-            }
-            if (qrow) {
-                const uint4* src = reinterpret_cast<const uint4*>(qrow + e0 - qoff);
-                const int nv = (e1 - e0 + qoff + 7) >> 3;
-                for (int v = tid; v < nv; v += kNT) reinterpret_cast<uint4*>(sq)[v] = __ldg(src + v);
-            }
-        }
-        __syncthreads();
-        CPROF(1);
-        // warp w scans elements [e0 + w*Lw, ...) in groups of 32 consecutive elements
-        const int n = e1 - e0;
-        const int Lw = (((n + kNW - 1) / kNW) + 31) & ~31;
-        const int wid = tid >> 5;
-        const int w0 = min(e0 + wid * Lw, e1), w1 = min(w0 + Lw, e1);
-        unsigned ex = 0;
-        bool use_pure = pure;
-        unsigned long long M = 0, cum = 0, tot = 0;
-        for (int attempt = 0; attempt < 2; ++attempt) {
-            unsigned long long mine = 0;
-            for (int i = w0 + lane; i < w1; i += 32) {
-                const uint32_t pb = prow ? sp[i - e0 + poff] : 0xFF80u;
-                const uint32_t qb = qrow ? sq[i - e0 + qoff] : 0xFF80u;
-                mine += fix_w(resid_w(dt, dq, onehot, use_pure, pb, qb, i));
-            }
-            mine = warp_sum_u64(mine);
-            if (lane == 0) sh->tsum[wid] = mine;
-            __syncthreads();
-            if (tid == 0) {
-                unsigned long long t_ = 0;
-                for (int i = 0; i < kNW; ++i) t_ += sh->tsum[i];
-                sh->pub[ex & 1][0] = t_;
-            }
-            CPROF(2);
-            cluster_barrier();
-            CPROF(3);
-            const unsigned exn = ex++;
-            M = 0;
-            cum = 0;
-            for (int q = 0; q < kCS; ++q) {
-                const unsigned long long v = cluster.map_shared_rank(&sh->pub[exn & 1][0], q)[0];
-                if (q < rank) cum += v;
-                if (q == rank) tot = v;
-                M += v;
-            }
-            if (!use_pure && M == 0) {
-                use_pure = true;
-                __syncthreads();
-                continue;
-            }
-            break;
-        }
-        const long long thr = scale_floor(uf, M);
-        if (thr == -2) {
-            if (rank == 0 && tid == 0) write_request(a, b, acc, (long long)a.V - 1);
-        } else if ((long long)(cum + tot) > thr && (rank == 0 || (long long)cum <= thr)) {
-            // this CTA holds the crossing: the first CTA whose running total passes thr;
-            // then the first warp, the first group of 32 and the first lane
-            long long rel = thr - (long long)cum;
-            int wstar = kNW - 1;
-            for (int i = 0; i < kNW; ++i) {
-                const long long ws_ = (long long)sh->tsum[i];
-                if (ws_ > rel) { wstar = i; break; }
-                rel -= ws_;
-            }
-            if (wid == wstar) {
-                long long bonus = (long long)a.V - 1;
-                for (int g0 = w0; g0 < w1; g0 += 32) {
-                    const int i = g0 + lane;
-                    unsigned long long F = 0;
-                    if (i < w1) {
-                        const uint32_t pb = prow ? sp[i - e0 + poff] : 0xFF80u;
-                        const uint32_t qb = qrow ? sq[i - e0 + qoff] : 0xFF80u;
-                        F = fix_w(resid_w(dt, dq, onehot, use_pure, pb, qb, i));
-                    }
-                    unsigned long long inc = F;
-#pragma unroll
-                    for (int o = 1; o < 32; o <<= 1) {
-                        const unsigned long long v = __shfl_up_sync(0xffffffffu, inc, o);
-                        if (lane >= o) inc += v;
-                    }
-                    const uint32_t bal = __ballot_sync(0xffffffffu, i < w1 && (long long)inc > rel);
-                    if (bal) {
-                        bonus = g0 + __ffs(bal) - 1;
-                        break;
-                    }
-                    rel -= (long long)__shfl_sync(0xffffffffu, inc, 31);
-                }
-                if (lane == 0) write_request(a, b, acc, bonus);
-            }
-        } else if (rank == 0 && (long long)M <= thr) {
-            // no crossing (mass 0): the default of the reference loop
-            if (tid == 0) write_request(a, b, acc, (long long)a.V - 1);
-        }
-        CPROF(4);
-        cluster_barrier();  // peers may still read this CTA's totals
-        CPROF(5);
-#ifdef DSV_PROFILE
-        if (rank == 0 && tid == 0) atomicAdd(a.prof + 64 + 15, 1ull);
-#endif
-    }
-    }
-
-    // ---- completion: the last request packs tokens and KV slots ---------------------------
-    if (rank == 0) {
-        __syncthreads();
-        if (tid == 0) {
-            __threadfence();
-            const unsigned old = atomicAdd(&a.ws->finalized, 1u);
-            sh->flag = old == (unsigned)(a.B - 1);
-        }
-        __syncthreads();
-        if (sh->flag) {
-            __threadfence();
-            if (a.tok_out != nullptr) compact_all(a, sh);
-            __syncthreads();
-            if (tid == 0) a.ws->finalized = 0;
-        }
-    }
 }
 
 // ---------------------------------------------------------------------------------------
