@@ -163,6 +163,7 @@ int dsv_verify_logits(int32_t batch, int32_t vocab, int32_t dtype, const int64_t
     a.desc = reinterpret_cast<dsv::RowDesc*>(base + dsv::verify_desc_offset(batch));
     a.gmax = reinterpret_cast<unsigned long long*>(base + dsv::verify_gmax_offset(batch));
     a.prof = reinterpret_cast<unsigned long long*>(base + dsv::verify_prof_offset(batch));
+    a.order = reinterpret_cast<unsigned int*>(base + dsv::verify_order_offset(batch));
     if (dsv::stream_supported(a, dtype))
         return counted(dsv::launch_stream(a, (cudaStream_t)stream), 2);
     return counted(dsv::launch_verify(a, dtype, (cudaStream_t)stream), 1);

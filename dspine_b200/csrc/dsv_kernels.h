@@ -46,9 +46,13 @@ constexpr inline size_t verify_gmax_offset(int B) {
     return verify_desc_offset(B) + (size_t)B * 16 * 2 * sizeof(RowDesc);
 }
 // [u64 x B x 16]: greedy rows' packed (max key << 32 | ~first index), reset after use
+// [u32 x B]: streaming path: requests in chain-kernel dispatch order (costliest first)
+constexpr inline size_t verify_order_offset(int B) {
+    return verify_gmax_offset(B) + (size_t)B * 16 * sizeof(unsigned long long);
+}
 // [2 KB]: phase timers of profiling builds (-DDSV_PROFILE); unused otherwise
 constexpr inline size_t verify_prof_offset(int B) {
-    return verify_gmax_offset(B) + (size_t)B * 16 * sizeof(unsigned long long);
+    return verify_order_offset(B) + (((size_t)B * 4 + 63) & ~(size_t)63);
 }
 constexpr inline size_t verify_workspace_bytes(int B) {
     return verify_prof_offset(B) + 2048;
@@ -94,6 +98,7 @@ struct VerifyArgs {
     RowDesc* desc;             // [B,16,2] row descriptors (streaming path)
     unsigned long long* gmax;  // [B,16] greedy rows: max key << 32 | (0xFFFFFFFF - first index)
     unsigned long long* prof;  // profiling builds: phase timers
+    unsigned int* order;       // [B] streaming path: chain-kernel dispatch order
 };
 
 // launchers (return a dsv::Status)

@@ -820,6 +820,38 @@ __global__ void __launch_bounds__(kRT, DSV_ROWS_MIN_CTAS) rows_kernel(VerifyArgs
     build_plan(a, sh, kRWinK);
     const int ntask = total_tasks(a, sh);
     const int V = a.V;
+    if (blockIdx.x == 0 && tid < 32) {
+        // chain-kernel dispatch order: large-k sampled requests (big kept sets), then small-k
+        // sampled requests, then greedy ones (a counting sort, request order inside a class)
+        int base_[3] = {0, 0, 0};
+        int tot[3] = {0, 0, 0};
+        for (int b0 = 0; b0 < a.B; b0 += 32) {
+            const int b = b0 + lane;
+            int g = -1;
+            if (b < a.B) {
+                const int cat = (int)(sh->req[b] & 7u);
+                g = cat == kGreedy ? 2 : (a.top_k[b] > kRWinK ? 0 : 1);
+            }
+#pragma unroll
+            for (int q = 0; q < 3; ++q) tot[q] += __popc(__ballot_sync(0xffffffffu, g == q));
+        }
+        base_[1] = tot[0];
+        base_[2] = tot[0] + tot[1];
+        for (int b0 = 0; b0 < a.B; b0 += 32) {
+            const int b = b0 + lane;
+            int g = -1;
+            if (b < a.B) {
+                const int cat = (int)(sh->req[b] & 7u);
+                g = cat == kGreedy ? 2 : (a.top_k[b] > kRWinK ? 0 : 1);
+            }
+#pragma unroll
+            for (int q = 0; q < 3; ++q) {
+                const unsigned m = __ballot_sync(0xffffffffu, g == q);
+                if (g == q) a.order[base_[q] + __popc(m & ((1u << lane) - 1u))] = (unsigned)b;
+                base_[q] += __popc(m);
+            }
+        }
+    }
 
     for (;;) {
         __syncthreads();
@@ -1347,17 +1379,16 @@ __device__ void write_request(const VerifyArgs& a, int b, int acc, long long bon
 // chain + bonus + outputs: kCP CTAs per request, no cluster
 //
 // Every CTA of a request decides the chain (warp 0, one lane per step), then takes one slice
-// of the bonus row: the slice's exact residual mass goes to the request's spare greedy-maximum
-// slots in the workspace (unused by sampled requests).  The last CTA of the request (a done
+// of the bonus row: the slice's exact residual mass goes to the request's task-result area in
+// the workspace (unused by this path otherwise).  The last CTA of the request (a done
 // counter) forms the threshold from the slice totals, rescans only the crossing slice tile by
 // tile (block scans) and writes the five outputs; the last request packs tokens and KV slots.
 // p is evaluated only for kept elements and q only where p > 0 (the residual is 0 elsewhere).
 
-constexpr int kCP = 16;                   // CTAs (slices) per request
+constexpr int kCP = 32;                   // CTAs (slices) per request
 constexpr int kCT = 256;                  // threads per CTA (4 CTAs per SM: one wave)
 constexpr int kCTW = kCT / 32;
-static_assert(kCP <= kT, "slice totals live in the request's kT greedy-maximum slots");
-static_assert(kCP * 2 <= 2 * kT, "tile masses live in the request's task-result area (32 u64)");
+static_assert(kCP * 1 <= 2 * kT, "slice masses live in the request's task-result area (32 u64)");
 
 struct Chain3Smem {
     uint2 queue[kCTW][256];        // per warp: kept elements of one vector per lane
@@ -1445,7 +1476,7 @@ struct BonusRow {
 };
 
 constexpr int kCTileV = 4 * kCT;           // vectors per tile: 4 consecutive per thread
-constexpr int kCMaxTiles = 2;              // tiles per slice (kCP x kCMaxTiles <= 32): V <= kMaxV
+constexpr int kCMaxTiles = 1;              // tiles per slice (kCP x kCMaxTiles <= 32): V <= kMaxV
 constexpr int kMaxV = 8 * (kCP * kCMaxTiles * kCTileV - kCP) - 16;  // vectors of every slice fit
 
 __device__ __forceinline__ bool kept_in(const RowDesc& d, uint32_t u16, int i) {
@@ -1591,7 +1622,7 @@ __global__ void __launch_bounds__(kCT, 4) chain3_kernel(VerifyArgs a) {
     __shared__ Chain3Smem shm;
     Chain3Smem* sh = &shm;
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-    const int b = blockIdx.x / kCP, rank = blockIdx.x % kCP;
+    const int b = (int)a.order[blockIdx.x / kCP], rank = blockIdx.x % kCP;
     const int cap = clamp_cap(a.caps[b]);
     const float T = a.temperature[b];
     const int kq = a.top_k[b];
@@ -1709,14 +1740,14 @@ __global__ void __launch_bounds__(kCT, 4) chain3_kernel(VerifyArgs a) {
         r.nvp = r.prow ? (V + r.poff + 7) >> 3 : 0;
         r.qvec = r.qrow && (int)((reinterpret_cast<uintptr_t>(r.qrow) & 15u) >> 1) == r.poff;
         // this CTA's slice of vectors, in tiles of kCTileV; tile masses go to the request's
-        // task-result area (kCP x kCMaxTiles u64), slice totals to the spare maximum slots
+        // task-result area (kCP x kCMaxTiles u64)
         const int per = (r.nvp + kCP - 1) / kCP;
         const int v0 = min(rank * per, r.nvp), v1 = min(v0 + per, r.nvp);
-        unsigned long long* slots = a.gmax + (size_t)b * kT;  // spare for sampled requests
         unsigned long long* tmass = reinterpret_cast<unsigned long long*>(a.res) + (size_t)b * kT * 2;
         auto slice_tiles = [&](int q, bool pure_) -> unsigned long long {
             const int u0 = min(q * per, r.nvp), u1 = min(u0 + per, r.nvp);
             unsigned long long tot = 0;
+            if (tid == 0 && u0 >= u1) tmass[q * kCMaxTiles] = 0ull;  // an empty slice
             for (int t = 0; u0 + t * kCTileV < u1 && t < kCMaxTiles; ++t) {
                 const int tv0 = u0 + t * kCTileV, tv1 = min(tv0 + kCTileV, u1);
                 const unsigned long long m =
@@ -1730,8 +1761,8 @@ __global__ void __launch_bounds__(kCT, 4) chain3_kernel(VerifyArgs a) {
         (void)v0;
         (void)v1;
         CP3(true, 1);
+        (void)mine;
         if (tid == 0) {
-            slots[rank] = mine;
             __threadfence();
             const unsigned old = atomicAdd(&a.done[b], 1u);
             sh->last = old == (unsigned)(kCP - 1);
@@ -1740,7 +1771,7 @@ __global__ void __launch_bounds__(kCT, 4) chain3_kernel(VerifyArgs a) {
         if (sh->last) {
             __threadfence();
             bool pure = pure0;
-            if (tid < kCP) sh->slice[tid] = __ldcg(&slots[tid]);
+            if (tid < kCP) sh->slice[tid] = __ldcg(&tmass[tid * kCMaxTiles]);  // one tile per slice
             __syncthreads();
             unsigned long long M = 0;
 #pragma unroll
@@ -1831,7 +1862,6 @@ __global__ void __launch_bounds__(kCT, 4) chain3_kernel(VerifyArgs a) {
 #endif
             if (tid == 0) {
                 write_request(a, b, acc, bonus);
-                for (int q = 0; q < kCP; ++q) slots[q] = 0ull;
                 a.done[b] = 0u;
             }
             finished = true;
