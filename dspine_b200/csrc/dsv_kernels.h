@@ -50,9 +50,17 @@ constexpr inline size_t verify_gmax_offset(int B) {
 constexpr inline size_t verify_order_offset(int B) {
     return verify_gmax_offset(B) + (size_t)B * 16 * sizeof(unsigned long long);
 }
+// [u32 x 2 x B]: streaming path: rows finished per request (reset after use), accepted length
+constexpr inline size_t verify_racc_offset(int B) {
+    return verify_order_offset(B) + (((size_t)B * 4 + 63) & ~(size_t)63);
+}
+// [u64 x 32 x 8 x B]: streaming path: residual mass per (request, slice, warp)
+constexpr inline size_t verify_wmass_offset(int B) {
+    return verify_racc_offset(B) + (((size_t)B * 8 + 63) & ~(size_t)63);
+}
 // [2 KB]: phase timers of profiling builds (-DDSV_PROFILE); unused otherwise
 constexpr inline size_t verify_prof_offset(int B) {
-    return verify_order_offset(B) + (((size_t)B * 4 + 63) & ~(size_t)63);
+    return verify_wmass_offset(B) + (size_t)B * 32 * 8 * 8;
 }
 constexpr inline size_t verify_workspace_bytes(int B) {
     return verify_prof_offset(B) + 2048;
@@ -99,6 +107,8 @@ struct VerifyArgs {
     unsigned long long* gmax;  // [B,16] greedy rows: max key << 32 | (0xFFFFFFFF - first index)
     unsigned long long* prof;  // profiling builds: phase timers
     unsigned int* order;       // [B] streaming path: chain-kernel dispatch order
+    unsigned int* racc;        // [B,2] streaming path: rows finished, accepted length
+    unsigned long long* wmass; // [B,32,8] streaming path: residual mass per slice and warp
 };
 
 // launchers (return a dsv::Status)

@@ -808,10 +808,546 @@ __device__ KeyStop count_walk(RSmem* sh, const VerifyArgs& a, const RowGeo& g, i
 #ifndef DSV_ROWS_MIN_CTAS
 #define DSV_ROWS_MIN_CTAS 3
 #endif
+// One row task: its descriptor (and, for greedy rows, its packed first argmax).  All threads.
+__device__ void process_row(RSmem* sh, const VerifyArgs& a, const TaskInfo& ti) {
+    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const int V = a.V;
+    PROF_START();
+    if (ti.row < 0 && tid == 0) atomicOr(&a.ws->err, 2u);
+    const RowGeo g = row_geo(a, ti);
+    const bool greedy = ti.cat == kGreedy;
+
+    // Nucleus and keep-all rows start with the fixed-range histogram (one pass, no max
+    // pass); the other rows, and rows with values outside that range, start with the max.
+    const bool onepass = ti.cat == kKeepAll || (ti.cat == kBinned && ti.p < 1.0f);
+    uint32_t tkey = 0, mkey = 0;
+    bool fixed_hist = false;
+    if (onepass) {
+        __syncthreads();
+        for (int i = tid; i < kHCap; i += kRT) sh->hist[i] = 0u;
+        if (tid == 0) {
+            sh->nband = 0u;
+            sh->outside = 0u;
+        }
+        __syncthreads();
+        uint32_t vmax2 = 0xFF80FF80u;  // running bf16x2 maximum (-inf, -inf)
+        stream_row(sh, a, g, V, [&](const uint4& x, int) {
+            const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+            vmax2 = bf2_max(vmax2, bf2_max(bf2_max(xs[0], xs[1]), bf2_max(xs[2], xs[3])));
+            uint32_t rare = 0;  // bit q: word q has an element outside the fine bins
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const uint32_t w = xs[q];
+                // fine iff 2^-20 <= |v| < 2^12, i.e. 0x3580 <= |bits| <= 0x457F: bit 15 of
+                // |bits| + 0x4A80 says ">= 0x3580", of |bits| + 0x3A80 says ">= 0x4580"
+                const uint32_t a2 = w & 0x7FFF7FFFu;
+                const uint32_t f2 = (a2 + 0x4A804A80u) & ~(a2 + 0x3A803A80u) & 0x80008000u;
+                // bin: positive v -> 0x457F - |bits| (descending key), negative v ->
+                // |bits| - 0x2580 (4096 + descending key of the negative part)
+                const uint32_t lo = w & 0xFFFFu, hi = w >> 16;
+                const uint32_t ilo = (lo & 0x8000u) ? (lo & 0x7FFFu) - 0x2580u : 0x457Fu - lo;
+                const uint32_t ihi = (hi & 0x8000u) ? (hi & 0x7FFFu) - 0x2580u : 0x457Fu - hi;
+                if (f2 & 0x00008000u) atomicAdd(&sh->hist[ilo], 1u);
+                if (f2 & 0x80000000u) atomicAdd(&sh->hist[ihi], 1u);
+                rare |= (f2 != 0x80008000u) ? (1u << q) : 0u;
+            }
+            if (rare) {
+#pragma unroll 1
+                for (int h = 0; h < 8; ++h) {
+                    if (!(rare & (1u << (h >> 1)))) continue;
+                    const uint32_t u16 = (h & 1) ? (xs[h >> 1] >> 16) : (xs[h >> 1] & 0xFFFFu);
+                    const uint32_t ab = u16 & 0x7FFFu;
+                    if (ab >= 0x3580u && ab <= 0x457Fu) continue;  // a fine element
+                    if (u16 == 0xFF80u) continue;                   // -inf (and the row's fill)
+                    if (ab < 0x3580u) {                             // the band |v| < 2^-20
+                        const uint32_t p = atomicAdd(&sh->nband, 1u);
+                        if (p < (uint32_t)kBandCap) sh->band[p] = (uint16_t)u16;
+                    } else {
+                        sh->outside = 1u;                           // |v| >= 2^12, inf, NaN
+                    }
+                }
+            }
+        });
+        {
+            const uint32_t k0 = okey(vmax2 & 0xFFFFu), k1 = okey(vmax2 >> 16);
+            tkey = k0 > k1 ? k0 : k1;
+        }
+        PROF_MARK(ti.cat, 2);
+        const uint32_t wk0 = __reduce_max_sync(0xffffffffu, tkey);
+        if (lane == 0) sh->red32[wid] = wk0;
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < kRW; ++i) mkey = max(mkey, sh->red32[i]);
+        fixed_hist = sh->outside == 0u && sh->nband <= (uint32_t)kBandCap && mkey > kNInfRaw &&
+                     mkey <= kFTop;
+        __syncthreads();
+    }
+    if (!fixed_hist) {
+        // ---- pass 1: max (greedy rows: and the first index of the max) ---------------
+        tkey = 0;
+        int tfirst = 0x7fffffff;
+        stream_row(sh, a, g, V, [&](const uint4& x, int v) {
+            uint32_t mx = bf2_max(bf2_max(x.x, x.y), bf2_max(x.z, x.w));
+            const uint32_t k0 = okey(mx & 0xFFFFu), k1 = okey(mx >> 16);
+            const uint32_t vk = k0 > k1 ? k0 : k1;
+            if (vk > tkey) {
+                tkey = vk;
+                if (greedy) {
+                    // first half of this vector with the new maximum (vectors arrive in order)
+                    const uint32_t b = key_bits(vk);
+                    const uint32_t b2 = b | (b << 16);
+                    const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+                    int f = 0x7fffffff;
+#pragma unroll
+                    for (int h = 7; h >= 0; --h) {
+                        const uint32_t eq = bf2_eq(xs[h >> 1], b2) & ((h & 1) ? 0xFFFF0000u : 0x0000FFFFu);
+                        const int e = 8 * v + h - g.off;
+                        if (eq && e >= 0 && e < V) f = e;
+                    }
+                    tfirst = f;
+                }
+            }
+        });
+        PROF_MARK(ti.cat, 0);
+        const uint32_t wk = __reduce_max_sync(0xffffffffu, tkey);
+        if (lane == 0) sh->red32[wid] = wk;
+        if (tid == 0) sh->first_min = 0x7fffffff;
+        __syncthreads();
+        mkey = 0;
+#pragma unroll
+        for (int i = 0; i < kRW; ++i) mkey = max(mkey, sh->red32[i]);
+        if (greedy) {
+            if (tkey == mkey && tfirst != 0x7fffffff) atomicMin(&sh->first_min, tfirst);
+            __syncthreads();
+            if (tid == 0) {
+                const int f = sh->first_min;
+                if (f != 0x7fffffff)
+                    a.gmax[ti.b * kT + ti.s] = ((unsigned long long)mkey << 32) | (0xFFFFFFFFull - (unsigned)f);
+                put_desc(a, ti, bf(key_bits(mkey)), mkey, f, 1ull << kFixBits, f == 0x7fffffff ? 0 : f,
+                         kDescGreedy);
+            }
+            PROF_END(ti.cat, 1);
+            return;
+        }
+    }
+    const float m = bf(key_bits(mkey));
+    const long long kk = ti.k < V ? (long long)ti.k : (long long)V;
+    const int cat = ti.cat;
+    const bool nucleus = ti.p < 1.0f;
+    const uint32_t kninf = okey(0xFF80u);  // key of -inf
+    KeyStop ks;
+    ks.found = 0;
+    unsigned long long S = 0;
+    long long thr = 0x7fffffffffffffffll;
+
+    if (cat == kWindow) {
+        // ---- pure top-k, k <= 256: candidates >= tau, ranked exactly -------------------
+        // tau = the largest value with at least k thread maxima >= tau (each such thread
+        // holds an element >= tau)
+        uint32_t tau = 0;
+        for (int bit = 15; bit >= 0; --bit) {
+            const uint32_t cand = tau | (1u << bit);
+            if (__syncthreads_count(tkey >= cand) >= kk) tau = cand;
+        }
+        if (tau < kninf) tau = kninf;  // fewer than k threads hold data (tiny vocabularies)
+        if (tid == 0) sh->nlist = 0;
+        __syncthreads();
+        const uint32_t taub = key_bits(tau);
+        const uint32_t tau2 = taub | (taub << 16);
+        stream_row(sh, a, g, V, [&](const uint4& x, int v) {
+            const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+#pragma unroll
+            for (int q = 0; q < 4; ++q) {
+                const uint32_t ge = bf2_ge(xs[q], tau2);
+                if (!ge) continue;
+#pragma unroll
+                for (int h = 0; h < 2; ++h) {
+                    const int e = 8 * v + 2 * q + h - g.off;
+                    if ((ge & (h ? 0xFFFF0000u : 0x0000FFFFu)) && e >= 0 && e < V) {
+                        const uint32_t pos = atomicAdd(&sh->nlist, 1u);
+                        if (pos < kRWinCap) {
+                            sh->hist[pos] = okey(h ? (xs[q] >> 16) : (xs[q] & 0xFFFFu));
+                            sh->hist[kRWinCap + pos] = (uint32_t)e;
+                        }
+                    }
+                }
+            }
+        });
+        PROF_MARK(ti.cat, 2);
+        const int n = (int)sh->nlist;
+        if (n >= 1 && n <= kRWinCap) {
+            // rank the candidates by (key desc, index asc); the first k are kept
+            // candidates: keys hist[0, n), indices hist[kRWinCap, kRWinCap + n); the ranked
+            // list goes to the ring (idle after the pass)
+            const uint32_t* wkey = sh->hist;
+            const uint32_t* widx = sh->hist + kRWinCap;
+            uint2* srt = reinterpret_cast<uint2*>(&sh->ring[0][0]);
+            for (int i = tid; i < n; i += kRT) {
+                const uint32_t ki = wkey[i], xi = widx[i];
+                int r = 0;
+                for (int j = 0; j < n; ++j) {
+                    const uint32_t kj = wkey[j];
+                    r += (kj > ki) || (kj == ki && widx[j] < xi);
+                }
+                srt[r] = make_uint2(ki, xi);
+            }
+            __syncthreads();
+            if (tid < 32) {
+                const int nsel = n < kk ? n : (int)kk;
+                unsigned long long sk = 0;
+                for (int r = lane; r < nsel; r += 32)
+                    sk += fix_of_y(y_clamped(bf(key_bits(srt[r].x)), m, ti.c));
+                sk = warp_sum_u64(sk);
+                if (lane == 0) put_desc(a, ti, m, srt[nsel - 1].x, (int)srt[nsel - 1].y, sk, 0, 0u);
+            }
+            PROF_END(ti.cat, 3);
+            return;
+        }
+        // the window overflowed (many equal values): exact counts from the top instead
+        ks = count_walk(sh, a, g, V, mkey, kninf, m, ti.c, 0ull, 0ull, kk, thr);
+    } else if (cat == kKeepAll || nucleus) {
+        // ---- exact per-key histogram of every element with nonzero fixed-point mass -----
+        // key < klo: y < -42 so fix(exp2(y)) = 0; such elements are never in a nucleus
+        // (their mass ranked ahead is S > floor(top_p S)) and add nothing to S.
+        const float vlo = m - 42.5f / ti.c;
+        uint32_t klo = kninf + 1u;
+        if (vlo > -INFINITY) {
+            const uint32_t vb = __float_as_uint(vlo) >> 16;  // truncated toward zero
+            const uint32_t kt = okey(vb);
+            klo = kt > kninf + 1u ? kt - 1u : kninf + 1u;      // one bf16 step below vlo
+        }
+        if (klo > mkey) klo = mkey;
+        uint32_t kB = 0x8000u, kNB = 0x7FFFu, npos = 0, nneg = 0, negtop = 0, topkey = 0;
+        if (fixed_hist) {
+            // the one-pass histogram: fixed bins, the band's elements listed
+            kB = kFB;
+            kNB = kFNB;
+            npos = kFPos;
+            nneg = kFPos;
+            negtop = kFNB;
+            topkey = kFTop;
+            if (tid == 0) {
+                sh->zcnt = 0u;
+                sh->zmass = 0ull;
+            }
+            __syncthreads();
+            const uint32_t nb = sh->nband;
+            for (uint32_t i = tid; i < nb; i += kRT) {
+                const uint32_t u16 = sh->band[i];
+                const uint32_t key = okey(u16);
+                if (key < klo || key > mkey) continue;
+                atomicAdd(&sh->zcnt, 1u);
+                const unsigned long long F = fix_of_y(y_clamped(bf(u16), m, ti.c));
+                if (F) atomicAdd(&sh->zmass, F);
+            }
+            __syncthreads();
+        } else {
+            // the band |v| < 2^zb is left out of the histogram (exact per element, usually
+            // empty): the smallest band for which the rest fits kHCap bins
+            for (int zb = -126; zb <= 127; ++zb) {
+                const uint32_t bits = (uint32_t)(127 + zb) << 7;
+                kB = 0x8000u | bits;          // key of +2^zb
+                kNB = 0x7FFFu - bits;         // key of -2^zb
+                npos = mkey >= kB ? mkey - kB + 1u : 0u;
+                const uint32_t ntop = kNB < mkey ? kNB : mkey;
+                nneg = ntop >= klo ? ntop - klo + 1u : 0u;
+                if (npos + nneg <= (uint32_t)kHCap - 64u) break;  // ceil/32 of both parts <= 256
+            }
+            negtop = kNB < mkey ? kNB : mkey;
+            topkey = mkey;
+            __syncthreads();
+            for (uint32_t i = tid; i < npos + nneg; i += kRT) sh->hist[i] = 0u;
+            if (tid == 0) {
+                sh->zcnt = 0u;
+                sh->zmass = 0ull;
+            }
+            __syncthreads();
+            const float mz = m, cz = ti.c;
+            const uint32_t nposv = npos, negv = npos + negtop, mk = mkey, kl = klo, kb = kB, knb = kNB;
+            stream_row(sh, a, g, V, [&](const uint4& x, int) {
+                const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
+                uint32_t band = 0;  // bit h: element h of this vector is in the band
+#pragma unroll
+                for (int h = 0; h < 8; ++h) {
+                    const uint32_t u16 = (h & 1) ? (xs[h >> 1] >> 16) : (xs[h >> 1] & 0xFFFFu);
+                    // ordered key (-0 joins +0 inside the band, which is handled exactly below)
+                    const uint32_t key = u16 ^ ((u16 & 0x8000u) ? 0xFFFFu : 0x8000u);
+                    const bool pos = key >= kb;
+                    const uint32_t idx = pos ? mk - key : negv - key;
+                    const bool fine = key >= kl && key <= mk && (pos || key <= knb);
+                    if (fine) atomicAdd(&sh->hist[idx], 1u);
+                    band |= (key >= kl && key <= mk && !pos && key > knb) ? (1u << h) : 0u;
+                }
+                if (band) {
+#pragma unroll 1
+                    for (int h = 0; h < 8; ++h) {
+                        if (!(band & (1u << h))) continue;
+                        const uint32_t u16 = (h & 1) ? (xs[h >> 1] >> 16) : (xs[h >> 1] & 0xFFFFu);
+                        const unsigned long long F = fix_of_y(y_clamped(bf(u16), mz, cz));
+                        atomicAdd(&sh->zcnt, 1u);
+                        if (F) atomicAdd(&sh->zmass, F);
+                    }
+                }
+            });
+            (void)nposv;
+        }
+        PROF_MARK(ti.cat, 2);
+        // ---- S and the walk over groups of 32 bins: positive groups, the band, negative
+        // groups (rank order).  Each warp sums its groups (one bin per lane), thread g scans
+        // group g, and the warp of the stopping group finds the bin.
+        const uint32_t ngp = (npos + 31u) >> 5, ngn = (nneg + 31u) >> 5, ng = ngp + ngn;
+#pragma unroll 2
+        for (uint32_t gi = wid; gi < ng; gi += kRW) {
+            const bool neg = gi >= ngp;
+            const uint32_t j = neg ? gi - ngp : gi;
+            const uint32_t i = (j << 5) + lane;            // bin within its part
+            const uint32_t lim = neg ? nneg : npos;
+            uint32_t cnt = 0;
+            unsigned long long ms = 0;
+            if (i < lim) cnt = sh->hist[(neg ? npos : 0u) + i];
+            if (!__any_sync(0xffffffffu, cnt != 0u)) {     // empty group
+                if (lane == 0) {
+                    sh->gcnt[gi] = 0u;
+                    sh->gmass[gi] = 0ull;
+                }
+                continue;
+            }
+            {
+                const uint32_t key = (neg ? negtop : topkey) - i;
+                if (cnt && key >= klo)
+                    ms = (unsigned long long)cnt * fix_of_y(y_clamped(bf(key_bits(key)), m, ti.c));
+            }
+            // warp sums with single-instruction reductions: the mass (< 2^59) in three
+            // 21-bit parts, each summing below 2^26
+            const uint32_t gc = __reduce_add_sync(0xffffffffu, cnt);
+            const uint32_t s0 = __reduce_add_sync(0xffffffffu, (uint32_t)(ms & 0x1FFFFFu));
+            const uint32_t s1 = __reduce_add_sync(0xffffffffu, (uint32_t)((ms >> 21) & 0x1FFFFFu));
+            const uint32_t s2 = __reduce_add_sync(0xffffffffu, (uint32_t)(ms >> 42));
+            if (lane == 0) {
+                sh->gcnt[gi] = gc;
+                sh->gmass[gi] = (unsigned long long)s0 + ((unsigned long long)s1 << 21) +
+                                ((unsigned long long)s2 << 42);
+            }
+        }
+        __syncthreads();
+        const unsigned long long zc = sh->zcnt, zm = sh->zmass;
+        const uint32_t gme = (uint32_t)tid;
+        const unsigned long long ct = gme < ng ? sh->gcnt[gme] : 0ull;
+        const unsigned long long mt = gme < ng ? sh->gmass[gme] : 0ull;
+        unsigned long long ci = ct, mi = mt;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const unsigned long long x1 = __shfl_up_sync(0xffffffffu, ci, o);
+            const unsigned long long x2 = __shfl_up_sync(0xffffffffu, mi, o);
+            if (lane >= o) {
+                ci += x1;
+                mi += x2;
+            }
+        }
+        if (lane == 31) {
+            sh->red64[wid] = ci;
+            sh->wm[wid] = mi;
+        }
+        if (tid == 0) sh->sel[6] = 0x7fffffff;
+        __syncthreads();
+        unsigned long long cb = ci - ct, mb = mi - mt, Sall = 0;
+        for (int w = 0; w < kRW; ++w) {
+            if (w < wid) {
+                cb += sh->red64[w];
+                mb += sh->wm[w];
+            }
+            Sall += sh->wm[w];
+        }
+        if (gme >= ngp) {
+            cb += zc;
+            mb += zm;
+        }
+        S = Sall + zm;
+        if (cat == kKeepAll || !nucleus) {
+            if (tid == 0) put_desc(a, ti, m, 0u, 0x7fffffff, S, 0, 0u);
+            PROF_END(ti.cat, 3);
+            return;
+        }
+        thr = scale_floor(ti.p, S);
+        PROF_MARK(ti.cat, 4);
+        if (gme < ng && ct > 0 && ((long long)(cb + ct) >= kk || (long long)(mb + mt) > thr))
+            atomicMin(&sh->sel[6], tid);
+        if (gme + 1u == ngp || (ngp == 0u && tid == 0)) {
+            // the band, between the positive and the negative groups
+            const unsigned long long c0 = ngp ? cb + ct : 0ull, m0 = ngp ? mb + mt : 0ull;
+            const bool bstop = zc > 0 && ((long long)(c0 + zc) >= kk || (long long)(m0 + zm) > thr);
+            sh->sel[9] = bstop ? 1 : 0;
+            sh->self64[7] = c0;
+            sh->self64[6] = m0;
+        }
+        __syncthreads();
+        const int owner = sh->sel[6];
+        const bool band_stop = sh->sel[9] != 0 && (owner == 0x7fffffff || (uint32_t)owner >= ngp);
+        if (tid == 0) sh->sel[10] = owner;
+        if (owner != 0x7fffffff && !band_stop) {
+            // the owner group's prefix, then the first bin of it that stops
+            if (tid == owner) {
+                sh->self64[4] = cb;
+                sh->self64[5] = mb;
+            }
+            __syncthreads();
+            const uint32_t go = (uint32_t)owner;
+            if (wid == 0) {
+                const bool neg = go >= ngp;
+                const uint32_t j = neg ? go - ngp : go;
+                const uint32_t i = (j << 5) + lane;
+                const uint32_t lim = neg ? nneg : npos;
+                uint32_t cnt = 0;
+                unsigned long long F = 0;
+                uint32_t key = 0;
+                if (i < lim) {
+                    cnt = sh->hist[(neg ? npos : 0u) + i];
+                    key = (neg ? negtop : topkey) - i;
+                    if (cnt && key >= klo) F = fix_of_y(y_clamped(bf(key_bits(key)), m, ti.c));
+                }
+                const unsigned long long c0 = sh->self64[4], m0 = sh->self64[5];
+                const unsigned long long mm = (unsigned long long)cnt * F;
+                const unsigned long long cin = warp_incl_u64(cnt), min_ = warp_incl_u64(mm);
+                const unsigned long long cbl = c0 + cin - cnt, mbl = m0 + min_ - mm;
+                const bool stop = cnt > 0 && ((long long)(cbl + cnt) >= kk || (long long)(mbl + mm) > thr);
+                const uint32_t bal = __ballot_sync(0xffffffffu, stop);
+                const int sl = bal ? __ffs(bal) - 1 : 0;
+                if (lane == sl) {
+                    sh->sel[7] = (int)key;
+                    sh->sel[8] = (int)cnt;
+                    sh->self64[4] = cbl;
+                    sh->self64[5] = mbl;
+                    sh->self64[3] = F;
+                    sh->sel[11] = bal ? 1 : 0;
+                }
+            }
+            __syncthreads();
+            ks.found = sh->sel[11];
+            ks.key = (uint32_t)sh->sel[7];
+            ks.count = (uint32_t)sh->sel[8];
+            ks.cnt = sh->self64[4];
+            ks.mass = sh->self64[5];
+            ks.F = sh->self64[3];
+            __syncthreads();
+        } else if (band_stop) {
+            const unsigned long long c0 = sh->self64[7], m0 = sh->self64[6];
+            __syncthreads();
+            const uint32_t btop = (kB - 1u) < mkey ? kB - 1u : mkey;
+            const uint32_t bbot = (kNB + 1u) > klo ? kNB + 1u : klo;
+            ks = count_walk(sh, a, g, V, btop, bbot, m, ti.c, c0, m0, kk, thr);
+        }
+    } else {
+        // ---- pure top-k with k > 256: exact counts from the top ------------------------
+        ks = count_walk(sh, a, g, V, mkey, kninf, m, ti.c, 0ull, 0ull, kk, thr);
+    }
+    if (!ks.found) {
+        if (tid == 0) {
+            atomicOr(&a.ws->err, 8u);
+            put_desc(a, ti, m, 0u, 0x7fffffff, S, 0, 0u);
+        }
+        return;
+    }
+    PROF_MARK(ti.cat, 6);
+    unsigned long long ntie = ks.count;
+    if ((long long)(ks.cnt + ntie) > kk) ntie = (unsigned long long)(kk - (long long)ks.cnt);
+    if (ks.F > 0 && (long long)ks.mass <= thr) {
+        const unsigned long long pb_ = (unsigned long long)(thr - (long long)ks.mass) / ks.F + 1ull;
+        if (pb_ < ntie) ntie = pb_;
+    }
+    if (ntie < 1) ntie = 1;
+    const unsigned long long skept = ks.mass + ntie * ks.F;
+    if (ntie >= ks.count) {
+        if (tid == 0) put_desc(a, ti, m, ks.key, 0x7fffffff, skept, 0, 0u);
+        PROF_END(ti.cat, 7);
+        return;
+    }
+
+    // ---- tie cut: occurrence number ntie of the boundary key in index order ------------
+    {
+        const int tie = tie_scan(sh, a, g, V, ks.key, ntie);
+        if (tid == 0) {
+            if (tie < 0) atomicOr(&a.ws->err, 16u);
+            put_desc(a, ti, m, ks.key, tie, skept, 0, 0u);
+        }
+    }
+    PROF_END(ti.cat, 8);
+}
+
+// a row descriptor written by another CTA of this launch (L2, not a stale L1 line)
+__device__ __forceinline__ RowDesc load_desc_cg(const RowDesc* p) {
+    static_assert(sizeof(RowDesc) == 32, "row descriptor: two 16-byte words");
+    const uint4 w0 = __ldcg(reinterpret_cast<const uint4*>(p));
+    const uint4 w1 = __ldcg(reinterpret_cast<const uint4*>(p) + 1);
+    RowDesc d;
+    d.m = __uint_as_float(w0.x);
+    d.c = __uint_as_float(w0.y);
+    d.inv_s = __uint_as_float(w0.z);
+    d.kstar = w0.w;
+    d.tie_cut = (int32_t)w1.x;
+    d.argmax = (int32_t)w1.y;
+    d.flags = w1.z;
+    d.pad = w1.w;
+    return d;
+}
+
+// After a row of sampled request b: the CTA that completes the request's rows decides the
+// chain (warp 0, one lane per step: draft s+1 against target row s) and leaves the accepted
+// length for the chain kernel.  Greedy requests are decided there from the packed maxima.
+__device__ void row_done(RSmem* sh, const VerifyArgs& a, int b) {
+    const int tid = threadIdx.x, lane = tid & 31;
+    const int cat = (int)(sh->req[b] & 7u), cap = (int)(sh->req[b] >> 3);
+    if (cat == kGreedy) return;
+    const unsigned nrows = (unsigned)(cap + (a.drf != nullptr ? cap - 1 : 0));
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        const unsigned old = atomicAdd(&a.racc[2 * b], 1u);
+        sh->first_min = old == nrows - 1u;
+    }
+    __syncthreads();
+    if (!sh->first_min || tid >= 32) return;
+    __threadfence();
+    const bool onehot_q = a.drf == nullptr;
+    const uint16_t* tgt = reinterpret_cast<const uint16_t*>(a.tgt);
+    const uint16_t* drf = reinterpret_cast<const uint16_t*>(a.drf);
+    bool acc = false;
+    const int s = lane;
+    if (s < cap - 1) {
+        const long long tok = a.cand[b * kT + s + 1];
+        const bool valid = tok >= 0 && tok < a.V;
+        float p = 0.0f, q = 0.0f;
+        if (valid) {
+            const RowDesc dt = load_desc_cg(&a.desc[(b * kT + s) * 2 + 0]);
+            const long long tr = a.tgt_row[b] + s;
+            if (tr >= 0 && tr < a.tgt_rows) {
+                const uint32_t pb = tgt[tr * a.stride + tok];
+                p = row_prob(dt, bf(pb), pb, (int)tok);
+            }
+            if (onehot_q) {
+                q = 1.0f;
+            } else {
+                const RowDesc dd = load_desc_cg(&a.desc[(b * kT + s) * 2 + 1]);
+                const long long dr = a.drf_row[b] + s;
+                if (dr >= 0 && dr < a.drf_rows) {
+                    const uint32_t qb = drf[dr * a.stride + tok];
+                    q = row_prob(dd, bf(qb), qb, (int)tok);
+                }
+            }
+        }
+        acc = q > 0.0f && q <= 1.0f && __fmul_rn(a.u[b * 15 + s], q) < p;
+    }
+    const uint32_t rej = __ballot_sync(0xffffffffu, !acc) &
+                         ((cap - 1 >= 32) ? 0xffffffffu : ((1u << (cap - 1)) - 1u));
+    if (lane == 0) {
+        a.racc[2 * b + 1] = (unsigned)(rej ? __ffs(rej) - 1 : cap - 1);
+        a.racc[2 * b] = 0u;  // for the next launch
+    }
+}
+
 __global__ void __launch_bounds__(kRT, DSV_ROWS_MIN_CTAS) rows_kernel(VerifyArgs a) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     RSmem* sh = reinterpret_cast<RSmem*>(smem_raw);
-    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+    const int tid = threadIdx.x, lane = tid & 31;
     if (tid == 0) {
         for (int i = 0; i < kRingS; ++i) mbar_init(&sh->ring_bar[i], 1);
         fence_mbar_init();
@@ -819,7 +1355,6 @@ __global__ void __launch_bounds__(kRT, DSV_ROWS_MIN_CTAS) rows_kernel(VerifyArgs
     }
     build_plan(a, sh, kRWinK);
     const int ntask = total_tasks(a, sh);
-    const int V = a.V;
     if (blockIdx.x == 0 && tid < 32) {
         // chain-kernel dispatch order: large-k sampled requests (big kept sets), then small-k
         // sampled requests, then greedy ones (a counting sort, request order inside a class)
@@ -859,466 +1394,9 @@ __global__ void __launch_bounds__(kRT, DSV_ROWS_MIN_CTAS) rows_kernel(VerifyArgs
         __syncthreads();
         const int t = sh->task;
         if (t >= ntask) break;
-        PROF_START();
         const TaskInfo ti = decode_task(a, sh, t);
-        if (ti.row < 0 && tid == 0) atomicOr(&a.ws->err, 2u);
-        const RowGeo g = row_geo(a, ti);
-        const bool greedy = ti.cat == kGreedy;
-
-        // Nucleus and keep-all rows start with the fixed-range histogram (one pass, no max
-        // pass); the other rows, and rows with values outside that range, start with the max.
-        const bool onepass = ti.cat == kKeepAll || (ti.cat == kBinned && ti.p < 1.0f);
-        uint32_t tkey = 0, mkey = 0;
-        bool fixed_hist = false;
-        if (onepass) {
-            __syncthreads();
-            for (int i = tid; i < kHCap; i += kRT) sh->hist[i] = 0u;
-            if (tid == 0) {
-                sh->nband = 0u;
-                sh->outside = 0u;
-            }
-            __syncthreads();
-            uint32_t vmax2 = 0xFF80FF80u;  // running bf16x2 maximum (-inf, -inf)
-            stream_row(sh, a, g, V, [&](const uint4& x, int) {
-                const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
-                vmax2 = bf2_max(vmax2, bf2_max(bf2_max(xs[0], xs[1]), bf2_max(xs[2], xs[3])));
-                uint32_t rare = 0;  // bit q: word q has an element outside the fine bins
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const uint32_t w = xs[q];
-                    // fine iff 2^-20 <= |v| < 2^12, i.e. 0x3580 <= |bits| <= 0x457F: bit 15 of
-                    // |bits| + 0x4A80 says ">= 0x3580", of |bits| + 0x3A80 says ">= 0x4580"
-                    const uint32_t a2 = w & 0x7FFF7FFFu;
-                    const uint32_t f2 = (a2 + 0x4A804A80u) & ~(a2 + 0x3A803A80u) & 0x80008000u;
-                    // bin: positive v -> 0x457F - |bits| (descending key), negative v ->
-                    // |bits| - 0x2580 (4096 + descending key of the negative part)
-                    const uint32_t lo = w & 0xFFFFu, hi = w >> 16;
-                    const uint32_t ilo = (lo & 0x8000u) ? (lo & 0x7FFFu) - 0x2580u : 0x457Fu - lo;
-                    const uint32_t ihi = (hi & 0x8000u) ? (hi & 0x7FFFu) - 0x2580u : 0x457Fu - hi;
-                    if (f2 & 0x00008000u) atomicAdd(&sh->hist[ilo], 1u);
-                    if (f2 & 0x80000000u) atomicAdd(&sh->hist[ihi], 1u);
-                    rare |= (f2 != 0x80008000u) ? (1u << q) : 0u;
-                }
-                if (rare) {
-#pragma unroll 1
-                    for (int h = 0; h < 8; ++h) {
-                        if (!(rare & (1u << (h >> 1)))) continue;
-                        const uint32_t u16 = (h & 1) ? (xs[h >> 1] >> 16) : (xs[h >> 1] & 0xFFFFu);
-                        const uint32_t ab = u16 & 0x7FFFu;
-                        if (ab >= 0x3580u && ab <= 0x457Fu) continue;  // a fine element
-                        if (u16 == 0xFF80u) continue;                   // -inf (and the row's fill)
-                        if (ab < 0x3580u) {                             // the band |v| < 2^-20
-                            const uint32_t p = atomicAdd(&sh->nband, 1u);
-                            if (p < (uint32_t)kBandCap) sh->band[p] = (uint16_t)u16;
-                        } else {
-                            sh->outside = 1u;                           // |v| >= 2^12, inf, NaN
-                        }
-                    }
-                }
-            });
-            {
-                const uint32_t k0 = okey(vmax2 & 0xFFFFu), k1 = okey(vmax2 >> 16);
-                tkey = k0 > k1 ? k0 : k1;
-            }
-            PROF_MARK(ti.cat, 2);
-            const uint32_t wk0 = __reduce_max_sync(0xffffffffu, tkey);
-            if (lane == 0) sh->red32[wid] = wk0;
-            __syncthreads();
-#pragma unroll
-            for (int i = 0; i < kRW; ++i) mkey = max(mkey, sh->red32[i]);
-            fixed_hist = sh->outside == 0u && sh->nband <= (uint32_t)kBandCap && mkey > kNInfRaw &&
-                         mkey <= kFTop;
-            __syncthreads();
-        }
-        if (!fixed_hist) {
-            // ---- pass 1: max (greedy rows: and the first index of the max) ---------------
-            tkey = 0;
-            int tfirst = 0x7fffffff;
-            stream_row(sh, a, g, V, [&](const uint4& x, int v) {
-                uint32_t mx = bf2_max(bf2_max(x.x, x.y), bf2_max(x.z, x.w));
-                const uint32_t k0 = okey(mx & 0xFFFFu), k1 = okey(mx >> 16);
-                const uint32_t vk = k0 > k1 ? k0 : k1;
-                if (vk > tkey) {
-                    tkey = vk;
-                    if (greedy) {
-                        // first half of this vector with the new maximum (vectors arrive in order)
-                        const uint32_t b = key_bits(vk);
-                        const uint32_t b2 = b | (b << 16);
-                        const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
-                        int f = 0x7fffffff;
-#pragma unroll
-                        for (int h = 7; h >= 0; --h) {
-                            const uint32_t eq = bf2_eq(xs[h >> 1], b2) & ((h & 1) ? 0xFFFF0000u : 0x0000FFFFu);
-                            const int e = 8 * v + h - g.off;
-                            if (eq && e >= 0 && e < V) f = e;
-                        }
-                        tfirst = f;
-                    }
-                }
-            });
-            PROF_MARK(ti.cat, 0);
-            const uint32_t wk = __reduce_max_sync(0xffffffffu, tkey);
-            if (lane == 0) sh->red32[wid] = wk;
-            if (tid == 0) sh->first_min = 0x7fffffff;
-            __syncthreads();
-            mkey = 0;
-#pragma unroll
-            for (int i = 0; i < kRW; ++i) mkey = max(mkey, sh->red32[i]);
-            if (greedy) {
-                if (tkey == mkey && tfirst != 0x7fffffff) atomicMin(&sh->first_min, tfirst);
-                __syncthreads();
-                if (tid == 0) {
-                    const int f = sh->first_min;
-                    if (f != 0x7fffffff)
-                        a.gmax[ti.b * kT + ti.s] = ((unsigned long long)mkey << 32) | (0xFFFFFFFFull - (unsigned)f);
-                    put_desc(a, ti, bf(key_bits(mkey)), mkey, f, 1ull << kFixBits, f == 0x7fffffff ? 0 : f,
-                             kDescGreedy);
-                }
-                PROF_END(ti.cat, 1);
-                continue;
-            }
-        }
-        const float m = bf(key_bits(mkey));
-        const long long kk = ti.k < V ? (long long)ti.k : (long long)V;
-        const int cat = ti.cat;
-        const bool nucleus = ti.p < 1.0f;
-        const uint32_t kninf = okey(0xFF80u);  // key of -inf
-        KeyStop ks;
-        ks.found = 0;
-        unsigned long long S = 0;
-        long long thr = 0x7fffffffffffffffll;
-
-        if (cat == kWindow) {
-            // ---- pure top-k, k <= 256: candidates >= tau, ranked exactly -------------------
-            // tau = the largest value with at least k thread maxima >= tau (each such thread
-            // holds an element >= tau)
-            uint32_t tau = 0;
-            for (int bit = 15; bit >= 0; --bit) {
-                const uint32_t cand = tau | (1u << bit);
-                if (__syncthreads_count(tkey >= cand) >= kk) tau = cand;
-            }
-            if (tau < kninf) tau = kninf;  // fewer than k threads hold data (tiny vocabularies)
-            if (tid == 0) sh->nlist = 0;
-            __syncthreads();
-            const uint32_t taub = key_bits(tau);
-            const uint32_t tau2 = taub | (taub << 16);
-            stream_row(sh, a, g, V, [&](const uint4& x, int v) {
-                const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
-#pragma unroll
-                for (int q = 0; q < 4; ++q) {
-                    const uint32_t ge = bf2_ge(xs[q], tau2);
-                    if (!ge) continue;
-#pragma unroll
-                    for (int h = 0; h < 2; ++h) {
-                        const int e = 8 * v + 2 * q + h - g.off;
-                        if ((ge & (h ? 0xFFFF0000u : 0x0000FFFFu)) && e >= 0 && e < V) {
-                            const uint32_t pos = atomicAdd(&sh->nlist, 1u);
-                            if (pos < kRWinCap) {
-                                sh->hist[pos] = okey(h ? (xs[q] >> 16) : (xs[q] & 0xFFFFu));
-                                sh->hist[kRWinCap + pos] = (uint32_t)e;
-                            }
-                        }
-                    }
-                }
-            });
-            PROF_MARK(ti.cat, 2);
-            const int n = (int)sh->nlist;
-            if (n >= 1 && n <= kRWinCap) {
-                // rank the candidates by (key desc, index asc); the first k are kept
-                // candidates: keys hist[0, n), indices hist[kRWinCap, kRWinCap + n); the ranked
-                // list goes to the ring (idle after the pass)
-                const uint32_t* wkey = sh->hist;
-                const uint32_t* widx = sh->hist + kRWinCap;
-                uint2* srt = reinterpret_cast<uint2*>(&sh->ring[0][0]);
-                for (int i = tid; i < n; i += kRT) {
-                    const uint32_t ki = wkey[i], xi = widx[i];
-                    int r = 0;
-                    for (int j = 0; j < n; ++j) {
-                        const uint32_t kj = wkey[j];
-                        r += (kj > ki) || (kj == ki && widx[j] < xi);
-                    }
-                    srt[r] = make_uint2(ki, xi);
-                }
-                __syncthreads();
-                if (tid < 32) {
-                    const int nsel = n < kk ? n : (int)kk;
-                    unsigned long long sk = 0;
-                    for (int r = lane; r < nsel; r += 32)
-                        sk += fix_of_y(y_clamped(bf(key_bits(srt[r].x)), m, ti.c));
-                    sk = warp_sum_u64(sk);
-                    if (lane == 0) put_desc(a, ti, m, srt[nsel - 1].x, (int)srt[nsel - 1].y, sk, 0, 0u);
-                }
-                PROF_END(ti.cat, 3);
-                continue;
-            }
-            // the window overflowed (many equal values): exact counts from the top instead
-            ks = count_walk(sh, a, g, V, mkey, kninf, m, ti.c, 0ull, 0ull, kk, thr);
-        } else if (cat == kKeepAll || nucleus) {
-            // ---- exact per-key histogram of every element with nonzero fixed-point mass -----
-            // key < klo: y < -42 so fix(exp2(y)) = 0; such elements are never in a nucleus
-            // (their mass ranked ahead is S > floor(top_p S)) and add nothing to S.
-            const float vlo = m - 42.5f / ti.c;
-            uint32_t klo = kninf + 1u;
-            if (vlo > -INFINITY) {
-                const uint32_t vb = __float_as_uint(vlo) >> 16;  // truncated toward zero
-                const uint32_t kt = okey(vb);
-                klo = kt > kninf + 1u ? kt - 1u : kninf + 1u;      // one bf16 step below vlo
-            }
-            if (klo > mkey) klo = mkey;
-            uint32_t kB = 0x8000u, kNB = 0x7FFFu, npos = 0, nneg = 0, negtop = 0, topkey = 0;
-            if (fixed_hist) {
-                // the one-pass histogram: fixed bins, the band's elements listed
-                kB = kFB;
-                kNB = kFNB;
-                npos = kFPos;
-                nneg = kFPos;
-                negtop = kFNB;
-                topkey = kFTop;
-                if (tid == 0) {
-                    sh->zcnt = 0u;
-                    sh->zmass = 0ull;
-                }
-                __syncthreads();
-                const uint32_t nb = sh->nband;
-                for (uint32_t i = tid; i < nb; i += kRT) {
-                    const uint32_t u16 = sh->band[i];
-                    const uint32_t key = okey(u16);
-                    if (key < klo || key > mkey) continue;
-                    atomicAdd(&sh->zcnt, 1u);
-                    const unsigned long long F = fix_of_y(y_clamped(bf(u16), m, ti.c));
-                    if (F) atomicAdd(&sh->zmass, F);
-                }
-                __syncthreads();
-            } else {
-                // the band |v| < 2^zb is left out of the histogram (exact per element, usually
-                // empty): the smallest band for which the rest fits kHCap bins
-                for (int zb = -126; zb <= 127; ++zb) {
-                    const uint32_t bits = (uint32_t)(127 + zb) << 7;
-                    kB = 0x8000u | bits;          // key of +2^zb
-                    kNB = 0x7FFFu - bits;         // key of -2^zb
-                    npos = mkey >= kB ? mkey - kB + 1u : 0u;
-                    const uint32_t ntop = kNB < mkey ? kNB : mkey;
-                    nneg = ntop >= klo ? ntop - klo + 1u : 0u;
-                    if (npos + nneg <= (uint32_t)kHCap - 64u) break;  // ceil/32 of both parts <= 256
-                }
-                negtop = kNB < mkey ? kNB : mkey;
-                topkey = mkey;
-                __syncthreads();
-                for (uint32_t i = tid; i < npos + nneg; i += kRT) sh->hist[i] = 0u;
-                if (tid == 0) {
-                    sh->zcnt = 0u;
-                    sh->zmass = 0ull;
-                }
-                __syncthreads();
-                const float mz = m, cz = ti.c;
-                const uint32_t nposv = npos, negv = npos + negtop, mk = mkey, kl = klo, kb = kB, knb = kNB;
-                stream_row(sh, a, g, V, [&](const uint4& x, int) {
-                    const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
-                    uint32_t band = 0;  // bit h: element h of this vector is in the band
-#pragma unroll
-                    for (int h = 0; h < 8; ++h) {
-                        const uint32_t u16 = (h & 1) ? (xs[h >> 1] >> 16) : (xs[h >> 1] & 0xFFFFu);
-                        // ordered key (-0 joins +0 inside the band, which is handled exactly below)
-                        const uint32_t key = u16 ^ ((u16 & 0x8000u) ? 0xFFFFu : 0x8000u);
-                        const bool pos = key >= kb;
-                        const uint32_t idx = pos ? mk - key : negv - key;
-                        const bool fine = key >= kl && key <= mk && (pos || key <= knb);
-                        if (fine) atomicAdd(&sh->hist[idx], 1u);
-                        band |= (key >= kl && key <= mk && !pos && key > knb) ? (1u << h) : 0u;
-                    }
-                    if (band) {
-#pragma unroll 1
-                        for (int h = 0; h < 8; ++h) {
-                            if (!(band & (1u << h))) continue;
-                            const uint32_t u16 = (h & 1) ? (xs[h >> 1] >> 16) : (xs[h >> 1] & 0xFFFFu);
-                            const unsigned long long F = fix_of_y(y_clamped(bf(u16), mz, cz));
-                            atomicAdd(&sh->zcnt, 1u);
-                            if (F) atomicAdd(&sh->zmass, F);
-                        }
-                    }
-                });
-                (void)nposv;
-            }
-            PROF_MARK(ti.cat, 2);
-            // ---- S and the walk over groups of 32 bins: positive groups, the band, negative
-            // groups (rank order).  Each warp sums its groups (one bin per lane), thread g scans
-            // group g, and the warp of the stopping group finds the bin.
-            const uint32_t ngp = (npos + 31u) >> 5, ngn = (nneg + 31u) >> 5, ng = ngp + ngn;
-#pragma unroll 2
-            for (uint32_t gi = wid; gi < ng; gi += kRW) {
-                const bool neg = gi >= ngp;
-                const uint32_t j = neg ? gi - ngp : gi;
-                const uint32_t i = (j << 5) + lane;            // bin within its part
-                const uint32_t lim = neg ? nneg : npos;
-                uint32_t cnt = 0;
-                unsigned long long ms = 0;
-                if (i < lim) cnt = sh->hist[(neg ? npos : 0u) + i];
-                if (!__any_sync(0xffffffffu, cnt != 0u)) {     // empty group
-                    if (lane == 0) {
-                        sh->gcnt[gi] = 0u;
-                        sh->gmass[gi] = 0ull;
-                    }
-                    continue;
-                }
-                {
-                    const uint32_t key = (neg ? negtop : topkey) - i;
-                    if (cnt && key >= klo)
-                        ms = (unsigned long long)cnt * fix_of_y(y_clamped(bf(key_bits(key)), m, ti.c));
-                }
-                // warp sums with single-instruction reductions: the mass (< 2^59) in three
-                // 21-bit parts, each summing below 2^26
-                const uint32_t gc = __reduce_add_sync(0xffffffffu, cnt);
-                const uint32_t s0 = __reduce_add_sync(0xffffffffu, (uint32_t)(ms & 0x1FFFFFu));
-                const uint32_t s1 = __reduce_add_sync(0xffffffffu, (uint32_t)((ms >> 21) & 0x1FFFFFu));
-                const uint32_t s2 = __reduce_add_sync(0xffffffffu, (uint32_t)(ms >> 42));
-                if (lane == 0) {
-                    sh->gcnt[gi] = gc;
-                    sh->gmass[gi] = (unsigned long long)s0 + ((unsigned long long)s1 << 21) +
-                                    ((unsigned long long)s2 << 42);
-                }
-            }
-            __syncthreads();
-            const unsigned long long zc = sh->zcnt, zm = sh->zmass;
-            const uint32_t gme = (uint32_t)tid;
-            const unsigned long long ct = gme < ng ? sh->gcnt[gme] : 0ull;
-            const unsigned long long mt = gme < ng ? sh->gmass[gme] : 0ull;
-            unsigned long long ci = ct, mi = mt;
-#pragma unroll
-            for (int o = 1; o < 32; o <<= 1) {
-                const unsigned long long x1 = __shfl_up_sync(0xffffffffu, ci, o);
-                const unsigned long long x2 = __shfl_up_sync(0xffffffffu, mi, o);
-                if (lane >= o) {
-                    ci += x1;
-                    mi += x2;
-                }
-            }
-            if (lane == 31) {
-                sh->red64[wid] = ci;
-                sh->wm[wid] = mi;
-            }
-            if (tid == 0) sh->sel[6] = 0x7fffffff;
-            __syncthreads();
-            unsigned long long cb = ci - ct, mb = mi - mt, Sall = 0;
-            for (int w = 0; w < kRW; ++w) {
-                if (w < wid) {
-                    cb += sh->red64[w];
-                    mb += sh->wm[w];
-                }
-                Sall += sh->wm[w];
-            }
-            if (gme >= ngp) {
-                cb += zc;
-                mb += zm;
-            }
-            S = Sall + zm;
-            if (cat == kKeepAll || !nucleus) {
-                if (tid == 0) put_desc(a, ti, m, 0u, 0x7fffffff, S, 0, 0u);
-                PROF_END(ti.cat, 3);
-                continue;
-            }
-            thr = scale_floor(ti.p, S);
-            PROF_MARK(ti.cat, 4);
-            if (gme < ng && ct > 0 && ((long long)(cb + ct) >= kk || (long long)(mb + mt) > thr))
-                atomicMin(&sh->sel[6], tid);
-            if (gme + 1u == ngp || (ngp == 0u && tid == 0)) {
-                // the band, between the positive and the negative groups
-                const unsigned long long c0 = ngp ? cb + ct : 0ull, m0 = ngp ? mb + mt : 0ull;
-                const bool bstop = zc > 0 && ((long long)(c0 + zc) >= kk || (long long)(m0 + zm) > thr);
-                sh->sel[9] = bstop ? 1 : 0;
-                sh->self64[7] = c0;
-                sh->self64[6] = m0;
-            }
-            __syncthreads();
-            const int owner = sh->sel[6];
-            const bool band_stop = sh->sel[9] != 0 && (owner == 0x7fffffff || (uint32_t)owner >= ngp);
-            if (tid == 0) sh->sel[10] = owner;
-            if (owner != 0x7fffffff && !band_stop) {
-                // the owner group's prefix, then the first bin of it that stops
-                if (tid == owner) {
-                    sh->self64[4] = cb;
-                    sh->self64[5] = mb;
-                }
-                __syncthreads();
-                const uint32_t go = (uint32_t)owner;
-                if (wid == 0) {
-                    const bool neg = go >= ngp;
-                    const uint32_t j = neg ? go - ngp : go;
-                    const uint32_t i = (j << 5) + lane;
-                    const uint32_t lim = neg ? nneg : npos;
-                    uint32_t cnt = 0;
-                    unsigned long long F = 0;
-                    uint32_t key = 0;
-                    if (i < lim) {
-                        cnt = sh->hist[(neg ? npos : 0u) + i];
-                        key = (neg ? negtop : topkey) - i;
-                        if (cnt && key >= klo) F = fix_of_y(y_clamped(bf(key_bits(key)), m, ti.c));
-                    }
-                    const unsigned long long c0 = sh->self64[4], m0 = sh->self64[5];
-                    const unsigned long long mm = (unsigned long long)cnt * F;
-                    const unsigned long long cin = warp_incl_u64(cnt), min_ = warp_incl_u64(mm);
-                    const unsigned long long cbl = c0 + cin - cnt, mbl = m0 + min_ - mm;
-                    const bool stop = cnt > 0 && ((long long)(cbl + cnt) >= kk || (long long)(mbl + mm) > thr);
-                    const uint32_t bal = __ballot_sync(0xffffffffu, stop);
-                    const int sl = bal ? __ffs(bal) - 1 : 0;
-                    if (lane == sl) {
-                        sh->sel[7] = (int)key;
-                        sh->sel[8] = (int)cnt;
-                        sh->self64[4] = cbl;
-                        sh->self64[5] = mbl;
-                        sh->self64[3] = F;
-                        sh->sel[11] = bal ? 1 : 0;
-                    }
-                }
-                __syncthreads();
-                ks.found = sh->sel[11];
-                ks.key = (uint32_t)sh->sel[7];
-                ks.count = (uint32_t)sh->sel[8];
-                ks.cnt = sh->self64[4];
-                ks.mass = sh->self64[5];
-                ks.F = sh->self64[3];
-                __syncthreads();
-            } else if (band_stop) {
-                const unsigned long long c0 = sh->self64[7], m0 = sh->self64[6];
-                __syncthreads();
-                const uint32_t btop = (kB - 1u) < mkey ? kB - 1u : mkey;
-                const uint32_t bbot = (kNB + 1u) > klo ? kNB + 1u : klo;
-                ks = count_walk(sh, a, g, V, btop, bbot, m, ti.c, c0, m0, kk, thr);
-            }
-        } else {
-            // ---- pure top-k with k > 256: exact counts from the top ------------------------
-            ks = count_walk(sh, a, g, V, mkey, kninf, m, ti.c, 0ull, 0ull, kk, thr);
-        }
-        if (!ks.found) {
-            if (tid == 0) {
-                atomicOr(&a.ws->err, 8u);
-                put_desc(a, ti, m, 0u, 0x7fffffff, S, 0, 0u);
-            }
-            continue;
-        }
-        PROF_MARK(ti.cat, 6);
-        unsigned long long ntie = ks.count;
-        if ((long long)(ks.cnt + ntie) > kk) ntie = (unsigned long long)(kk - (long long)ks.cnt);
-        if (ks.F > 0 && (long long)ks.mass <= thr) {
-            const unsigned long long pb_ = (unsigned long long)(thr - (long long)ks.mass) / ks.F + 1ull;
-            if (pb_ < ntie) ntie = pb_;
-        }
-        if (ntie < 1) ntie = 1;
-        const unsigned long long skept = ks.mass + ntie * ks.F;
-        if (ntie >= ks.count) {
-            if (tid == 0) put_desc(a, ti, m, ks.key, 0x7fffffff, skept, 0, 0u);
-            PROF_END(ti.cat, 7);
-            continue;
-        }
-
-        // ---- tie cut: occurrence number ntie of the boundary key in index order ------------
-        {
-            const int tie = tie_scan(sh, a, g, V, ks.key, ntie);
-            if (tid == 0) {
-                if (tie < 0) atomicOr(&a.ws->err, 16u);
-                put_desc(a, ti, m, ks.key, tie, skept, 0, 0u);
-            }
-        }
-        PROF_END(ti.cat, 8);
+        process_row(sh, a, ti);
+        row_done(sh, a, ti.b);
     }
     // the last CTA out resets the row counter for the next launch
     __syncthreads();
@@ -1389,10 +1467,10 @@ constexpr int kCP = 32;                   // CTAs (slices) per request
 constexpr int kCT = 256;                  // threads per CTA (4 CTAs per SM: one wave)
 constexpr int kCTW = kCT / 32;
 static_assert(kCP * 1 <= 2 * kT, "slice masses live in the request's task-result area (32 u64)");
+static_assert(kCP <= 32 && kCTW <= 8, "per-warp slice masses: [B][32][8] in the workspace");
 
 struct Chain3Smem {
     uint2 queue[kCTW][256];        // per warp: kept elements of one vector per lane
-    unsigned long long own[kCT];   // crossing tile: mass per owner thread
     unsigned long long wsum[kCTW];
     uint32_t red_a[kCTW], red_b[kCTW];
     unsigned long long slice[kCP];
@@ -1477,6 +1555,7 @@ struct BonusRow {
 
 constexpr int kCTileV = 4 * kCT;           // vectors per tile: 4 consecutive per thread
 constexpr int kCMaxTiles = 1;              // tiles per slice (kCP x kCMaxTiles <= 32): V <= kMaxV
+static_assert(kCMaxTiles == 1, "the crossing search takes the slice as its tile");
 constexpr int kMaxV = 8 * (kCP * kCMaxTiles * kCTileV - kCP) - 16;  // vectors of every slice fit
 
 __device__ __forceinline__ bool kept_in(const RowDesc& d, uint32_t u16, int i) {
@@ -1574,50 +1653,6 @@ __device__ __forceinline__ unsigned long long block_sum_u64(unsigned long long v
     return t;
 }
 
-// per-thread residual masses of tile [tv0, tv1) (thread t owns vectors tv0 + 4t .. +3): kept
-// elements are queued per warp and evaluated 32 at a time; each mass is added to its owner
-__device__ unsigned long long tile_owner_mass(const BonusRow& r, int V, int tv0, int tv1, bool pure,
-                                              Chain3Smem* sh) {
-    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-    uint2* queue = sh->queue[wid];
-    sh->own[tid] = 0ull;
-    __syncthreads();
-#pragma unroll 1
-    for (int u = 0; u < 4; ++u) {
-        const int v = tv0 + 4 * tid + u;
-        uint4 x = make_uint4(0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u), y = x;
-        if (v < tv1) load8(r, v, pure, x, y);
-        uint32_t keep = 0;
-#pragma unroll
-        for (int h = 0; h < 8; ++h) {
-            const int i = 8 * v + h - r.poff;
-            if (v < tv1 && i >= 0 && i < V && kept_in(r.dt, half16(x, h), i)) keep |= 1u << h;
-        }
-        const uint32_t n = __popc(keep);
-        const uint32_t incl = warp_incl_u32(n);
-        const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
-        uint32_t slot = incl - n;
-        while (keep) {
-            const int h = __ffs(keep) - 1;
-            keep &= keep - 1;
-            const int i = 8 * v + h - r.poff;
-            uint32_t qb = half16(y, h);
-            if (!pure && r.has_dq && !r.qvec) qb = r.qrow ? (uint32_t)__ldg(r.qrow + i) : 0xFF80u;
-            queue[slot++] = make_uint2(half16(x, h) | (qb << 16), (uint32_t)i | ((uint32_t)lane << 27));
-        }
-        __syncwarp();
-        for (uint32_t e = lane; e < total; e += 32) {
-            const uint2 q = queue[e];
-            const int i = (int)(q.y & 0x07FFFFFFu);
-            const unsigned long long f = resid_kept(r, pure, q.x & 0xFFFFu, q.x >> 16, i);
-            if (f) atomicAdd(&sh->own[(wid << 5) | (q.y >> 27)], f);
-        }
-        __syncwarp();
-    }
-    __syncthreads();
-    return sh->own[tid];
-}
-
 __global__ void __launch_bounds__(kCT, 4) chain3_kernel(VerifyArgs a) {
     __shared__ Chain3Smem shm;
     Chain3Smem* sh = &shm;
@@ -1682,38 +1717,8 @@ __global__ void __launch_bounds__(kCT, 4) chain3_kernel(VerifyArgs a) {
         }
         finished = rank == 0;
     } else {
-        // ---- chain: step s compares draft s+1 with target row s (warp 0, one lane per step)
-        if (tid < 32) {
-            bool acc = false;
-            const int s = lane;
-            if (s < cap - 1) {
-                const long long tok = a.cand[b * kT + s + 1];
-                const bool valid = tok >= 0 && tok < a.V;
-                float p = 0.0f, q = 0.0f;
-                if (valid) {
-                    const RowDesc dt = a.desc[(b * kT + s) * 2 + 0];
-                    const long long tr = a.tgt_row[b] + s;
-                    if (tr >= 0 && tr < a.tgt_rows) {
-                        const uint32_t pb = tgt[tr * a.stride + tok];
-                        p = row_prob(dt, bf(pb), pb, (int)tok);
-                    }
-                    if (onehot_q) {
-                        q = 1.0f;
-                    } else {
-                        const RowDesc dd = a.desc[(b * kT + s) * 2 + 1];
-                        const long long dr = a.drf_row[b] + s;
-                        if (dr >= 0 && dr < a.drf_rows) {
-                            const uint32_t qb = drf[dr * a.stride + tok];
-                            q = row_prob(dd, bf(qb), qb, (int)tok);
-                        }
-                    }
-                }
-                acc = q > 0.0f && q <= 1.0f && __fmul_rn(a.u[b * 15 + s], q) < p;
-            }
-            const uint32_t rej = __ballot_sync(0xffffffffu, !acc) &
-                                 ((cap - 1 >= 32) ? 0xffffffffu : ((1u << (cap - 1)) - 1u));
-            if (lane == 0) sh->acc = rej ? __ffs(rej) - 1 : cap - 1;
-        }
+        // the accepted length, decided by the row kernel when the request's rows completed
+        if (tid == 0) sh->acc = (int)a.racc[2 * b + 1];
         __syncthreads();
         CP3(true, 0);
         const int acc = sh->acc;
@@ -1753,6 +1758,8 @@ __global__ void __launch_bounds__(kCT, 4) chain3_kernel(VerifyArgs a) {
                 const unsigned long long m =
                     block_sum_u64(tile_mass(r, V, tv0, tv1, pure_, sh->queue[wid]), sh->wsum);
                 if (tid == 0) tmass[q * kCMaxTiles + t] = m;
+                // per-warp masses (still in shared memory) for the crossing search
+                if (tid < kCTW) a.wmass[((size_t)b * kCP + q) * kCTW + tid] = sh->wsum[tid];
                 tot += m;
             }
             return tot;
@@ -1800,15 +1807,7 @@ __global__ void __launch_bounds__(kCT, 4) chain3_kernel(VerifyArgs a) {
                     const long long t = (long long)sh->slice[q];
                     if (base + t > thr) {
                         qs = q;
-                        const int u0 = min(q * per, r.nvp), u1 = min(u0 + per, r.nvp);
-                        for (int t2 = 0; u0 + t2 * kCTileV < u1 && t2 < kCMaxTiles; ++t2) {
-                            const long long tm = (long long)__ldcg(&tmass[q * kCMaxTiles + t2]);
-                            if (base + tm > thr) {
-                                tq = t2;
-                                break;
-                            }
-                            base += tm;
-                        }
+                        tq = 0;  // one tile per slice (kCMaxTiles == 1)
                     } else {
                         base += t;
                     }
@@ -1816,36 +1815,64 @@ __global__ void __launch_bounds__(kCT, 4) chain3_kernel(VerifyArgs a) {
                 if (qs >= 0 && tq >= 0) {
                     const int u0 = min(qs * per, r.nvp), u1 = min(u0 + per, r.nvp);
                     const int tv0 = u0 + tq * kCTileV, tv1 = min(tv0 + kCTileV, u1);
-                    // per-thread masses of the tile (4 consecutive vectors per thread, so thread
-                    // order is index order): queued kept elements add into their owner's slot
-                    __syncthreads();
-                    const unsigned long long own = tile_owner_mass(r, V, tv0, tv1, pure, sh);
-                    const unsigned long long incl = warp_incl_u64(own);
-                    if (lane == 31) sh->wsum[wid] = incl;
-                    __syncthreads();
-                    unsigned long long before = 0;
+                    // the crossing warp from the slice's per-warp masses (warp w owns vectors
+                    // tv0 + 128 w ..., so warp order is index order), then that warp alone:
+                    // lane masses (4 consecutive vectors per lane), a warp scan, and the lane
+                    // holding the crossing walks its 32 elements
+                    const unsigned long long* wm = a.wmass + ((size_t)b * kCP + qs) * kCTW;
+                    unsigned long long wv[kCTW];
 #pragma unroll
-                    for (int w = 0; w < kCTW; ++w)
-                        if (w < wid) before += sh->wsum[w];
-                    long long run = base + (long long)(before + incl - own);
+                    for (int w = 0; w < kCTW; ++w) wv[w] = __ldcg(&wm[w]);  // independent loads
+                    int ws_ = kCTW - 1;
+#pragma unroll
+                    for (int w = 0; w < kCTW; ++w) {
+                        const long long m_ = (long long)wv[w];
+                        if (base + m_ > thr) {
+                            ws_ = w;
+                            break;
+                        }
+                        base += m_;
+                    }
                     if (tid == 0) sh->bonus = -1;
                     __syncthreads();
-                    if (run <= thr && run + (long long)own > thr) {
-                        // this thread's 32 elements in order
-                        for (int u = 0; u < 4 && sh->bonus < 0; ++u) {
-                            const int v = tv0 + 4 * tid + u;
-                            if (v >= tv1) break;
-                            uint4 x, y;
-                            load8(r, v, pure, x, y);
+                    if (wid == ws_) {
+                        // element masses of the warp's 1024 elements go to shared memory (the
+                        // idle queue area), lane l's 32 elements at [32 l, 32 l + 32)
+                        unsigned long long* fm = reinterpret_cast<unsigned long long*>(&sh->queue[0][0]);
+                        const int t_ = ws_ * 32 + lane;
+                        uint4 xa[4], ya[4];
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const int v = tv0 + 4 * t_ + u;
+                            xa[u] = make_uint4(0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u);
+                            ya[u] = xa[u];
+                            if (v < tv1) load8(r, v, pure, xa[u], ya[u]);
+                        }
+                        unsigned long long own = 0;
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const int v = tv0 + 4 * t_ + u;
+#pragma unroll
                             for (int h = 0; h < 8; ++h) {
                                 const int i = 8 * v + h - r.poff;
-                                if (i < 0 || i >= V || !kept_in(r.dt, half16(x, h), i)) continue;
-                                uint32_t qb = half16(y, h);
-                                if (!pure && r.has_dq && !r.qvec)
-                                    qb = r.qrow ? (uint32_t)__ldg(r.qrow + i) : 0xFF80u;
-                                run += (long long)resid_kept(r, pure, half16(x, h), qb, i);
+                                unsigned long long f = 0;
+                                if (v < tv1 && i >= 0 && i < V && kept_in(r.dt, half16(xa[u], h), i)) {
+                                    uint32_t qb = half16(ya[u], h);
+                                    if (!pure && r.has_dq && !r.qvec)
+                                        qb = r.qrow ? (uint32_t)__ldg(r.qrow + i) : 0xFF80u;
+                                    f = resid_kept(r, pure, half16(xa[u], h), qb, i);
+                                }
+                                fm[lane * 32 + u * 8 + h] = f;
+                                own += f;
+                            }
+                        }
+                        const unsigned long long incl = warp_incl_u64(own);
+                        long long run = base + (long long)(incl - own);
+                        if (run <= thr && run + (long long)own > thr) {
+                            for (int j = 0; j < 32; ++j) {
+                                run += (long long)fm[lane * 32 + j];
                                 if (run > thr) {
-                                    sh->bonus = i;
+                                    sh->bonus = 8 * (tv0 + 4 * t_) + j - r.poff;
                                     break;
                                 }
                             }
