@@ -22,7 +22,7 @@ inline int counted(int status, int kernels) {
 }
 
 // ---- scratch of dsv_verify_logits_noalloc -------------------------------------------------
-// A file-scope device array sized for kNoAllocMaxBatch requests (225 KB).  It is part of the
+// A file-scope device array sized for kNoAllocMaxBatch requests (870 KB).  It is part of the
 // module image: the driver places it when the library's kernels are loaded on a device, and it
 // starts zeroed.  Its address is looked up once per device and cached.
 constexpr int kNoAllocMaxBatch = 256;

@@ -176,7 +176,7 @@ int dsv_accept_compact(int32_t batch, const int32_t* commit, const int32_t* veri
 /* ---- the same verification without a caller workspace ------------------------------------
  * No counterpart in the reference: for callers that cannot allocate device memory (or hand out
  * scratch) at verification time.  Same arguments, outputs and results as dsv_verify_logits,
- * without `workspace`/`workspace_bytes`; its scratch is a fixed 225 KB device array inside the
+ * without `workspace`/`workspace_bytes`; its scratch is a fixed 870 KB device array inside the
  * library (sized for 256 requests), and the call performs no cudaMalloc/cudaFree and no
  * allocating library call.
  *  - batch > 256 returns DSV_WORKSPACE_TOO_SMALL before anything is enqueued.
