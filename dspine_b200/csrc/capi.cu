@@ -259,6 +259,59 @@ int dsv_chain_from_probs(int32_t batch, int32_t vocab, const int64_t* candidates
     return counted(dsv::launch_chain_probs(c, (cudaStream_t)stream), 1);
 }
 
+int dsv_accept_sparse(int32_t batch, int32_t vocab, int32_t width, const int64_t* candidates,
+                      const float* dense_p, const int32_t* p_ids, const float* p_values,
+                      const int32_t* p_lengths, const int32_t* p_overflow, const int64_t* q_ids,
+                      const float* q_values, const int32_t* verify_lens, const float* uniforms,
+                      const float* uniform_final, const int32_t* prefix_lens,
+                      const int64_t* row_offsets, const float* denominator, int32_t* accept,
+                      int32_t* commit, int64_t* bonus, int64_t* output, int32_t* new_seq,
+                      dsv_stream_t stream) {
+    if (batch < 0 || vocab < 1 || vocab > dsv::chain_probs_max_vocab()) return DSV_BAD_SHAPE;
+    if (p_ids && (width < 1 || width > 64)) return DSV_BAD_SHAPE;
+    if (batch == 0) return DSV_OK;
+    if (!candidates || !q_ids || !q_values || !verify_lens || !uniforms || !uniform_final ||
+        !prefix_lens || !accept || !commit || !bonus || !output || !new_seq)
+        return DSV_BAD_POINTER;
+    if (!dense_p && !p_ids) return DSV_BAD_POINTER;
+    if (p_ids && (!p_values || !p_lengths || !p_overflow)) return DSV_BAD_POINTER;
+    dsv::SparseAcceptArgs a = {};
+    a.B = batch;
+    a.V = vocab;
+    a.width = p_ids ? width : 0;
+    a.cand = candidates;
+    a.dense = dense_p;
+    a.p_ids = p_ids;
+    a.p_vals = p_values;
+    a.p_len = p_lengths;
+    a.overflow = p_overflow;
+    a.q_ids = q_ids;
+    a.q_vals = q_values;
+    a.caps = verify_lens;
+    a.u = uniforms;
+    a.uf = uniform_final;
+    a.prefix = prefix_lens;
+    a.row_offsets = row_offsets;
+    a.denom = denominator;
+    a.accept = accept;
+    a.commit = commit;
+    a.bonus = bonus;
+    a.output = output;
+    a.new_seq = new_seq;
+    return counted(dsv::launch_sparse_accept(a, (cudaStream_t)stream), 1);
+}
+
+int dsv_compress_probs(int64_t rows, int32_t vocab, int32_t capacity, const float* probs,
+                       int32_t* ids, float* values, int32_t* lengths, int32_t* overflow,
+                       dsv_stream_t stream) {
+    if (rows < 0 || vocab < 1 || capacity < 1 || rows > 0x7fffffff) return DSV_BAD_SHAPE;
+    if (rows == 0) return DSV_OK;
+    if (!probs || !ids || !values || !lengths || !overflow) return DSV_BAD_POINTER;
+    return counted(dsv::launch_compress(probs, rows, vocab, capacity, ids, values, lengths, overflow,
+                                        (cudaStream_t)stream),
+                   1);
+}
+
 int dsv_accept_greedy(int32_t batch, const int64_t* candidates, const int64_t* top1,
                       int64_t top1_stride, const int32_t* verify_lens, const int32_t* prefix_lens,
                       int32_t* accept, int32_t* commit, int64_t* bonus, int64_t* output,

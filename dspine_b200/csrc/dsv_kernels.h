@@ -171,6 +171,33 @@ struct ChainProbsArgs {
     int32_t* new_seq;
 };
 int chain_probs_max_vocab();
+
+// sparse-q chain rejection (probs.cu): dense, packed or overflow-mixed target rows
+struct SparseAcceptArgs {
+    int B, V, width;             // width: packed entries per row (0 without packed rows)
+    const int64_t* cand;         // [B,16]
+    const float* dense;          // [rows, V] or null
+    const int32_t* p_ids;        // [rows, width] or null
+    const float* p_vals;
+    const int32_t* p_len;        // [rows]
+    const int32_t* overflow;     // [rows]: the row is dense
+    const int64_t* q_ids;        // [B,15,16]
+    const float* q_vals;
+    const int32_t* caps;
+    const float* u;              // [B,15]
+    const float* uf;             // [B]
+    const int32_t* prefix;
+    const int64_t* row_offsets;  // [B] or null (b * 16)
+    const float* denom;          // [rows] or null: raw dense rows divided by it
+    int32_t* accept;
+    int32_t* commit;
+    int64_t* bonus;
+    int64_t* output;
+    int32_t* new_seq;
+};
+int launch_sparse_accept(const SparseAcceptArgs& a, cudaStream_t stream);
+int launch_compress(const float* p, long long rows, int V, int capacity, int32_t* ids, float* vals,
+                    int32_t* lens, int32_t* ovf, cudaStream_t stream);
 int launch_chain_probs(const ChainProbsArgs& c, cudaStream_t stream);
 
 // ---- per-request steps (small.cu) -----------------------------------------------------------

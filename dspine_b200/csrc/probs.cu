@@ -22,6 +22,7 @@ namespace pr {
 constexpr int kT = 16;
 constexpr int kThreads = 1024;
 constexpr int kMaxTiles = 1024;  // V <= 1M
+constexpr int kMaxPackedWidth = 64;  // packed target rows (compress_probs capacity)
 
 __device__ __forceinline__ float resid(const float* p, const float* q, int pure, int i) {
     const float pv = p[i];
@@ -157,9 +158,306 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// ---- sparse q: sampling/sparse/accept.py:94-543 (_accept_sparse, accept_sparse) --------------
+
+struct DrawSmem {
+    unsigned long long tile_mass[kMaxTiles];
+    unsigned long long wsum[kThreads / 32];
+    long long thr, base;
+    unsigned long long total;
+    int tile, bonus;
+};
+
+// First index whose running exact fixed-point mass of w(i) (i in [0, V)) exceeds
+// floor(u * M); V - 1 when none (also for u >= 1), 0 for u < 0.  Reports M.  All threads.
+template <typename W>
+__device__ int tile_draw(int V, float u, W w, DrawSmem* s, unsigned long long* mass_out) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int ntiles = (V + kThreads - 1) / kThreads;
+    for (int t = tid; t < kMaxTiles; t += kThreads) s->tile_mass[t] = 0;
+    __syncthreads();
+    for (int t = 0; t < ntiles; ++t) {
+        const int i = t * kThreads + tid;
+        uint64_t f = i < V ? fixv(w(i)) : 0;
+        f = warp_sum_u64(f);
+        if (lane == 0 && f) atomicAdd(&s->tile_mass[t], (unsigned long long)f);
+    }
+    __syncthreads();
+    if (warp == 0) {
+        unsigned long long run = 0;
+        for (int t0 = 0; t0 < ntiles; t0 += 32) {
+            const int t = t0 + lane;
+            uint64_t v = t < ntiles ? s->tile_mass[t] : 0;
+            v = warp_incl_u64(v);
+            if (t < ntiles) s->tile_mass[t] = run + v;
+            run += __shfl_sync(0xffffffffu, v, 31);
+        }
+        if (lane == 0) {
+            const long long thr = scale_floor(u, run);
+            int tile = -1, bo = V - 1;
+            if (thr == -1) {
+                bo = 0;
+            } else if (thr != -2 && run != 0) {
+                int lo = 0, hi = ntiles - 1;
+                while (lo < hi) {
+                    const int mid = (lo + hi) >> 1;
+                    if ((long long)s->tile_mass[mid] > thr) hi = mid;
+                    else lo = mid + 1;
+                }
+                tile = ((long long)s->tile_mass[lo] > thr) ? lo : -1;
+            }
+            s->thr = thr;
+            s->tile = tile;
+            s->bonus = bo;
+            s->base = tile > 0 ? (long long)s->tile_mass[tile - 1] : 0;
+            s->total = run;
+        }
+    }
+    __syncthreads();
+    *mass_out = s->total;
+    const int tile = s->tile;
+    if (tile >= 0) {
+        const int i = tile * kThreads + tid;
+        const uint64_t f = i < V ? fixv(w(i)) : 0;
+        const uint64_t incl = warp_incl_u64(f);
+        if (lane == 31) s->wsum[warp] = incl;
+        __syncthreads();
+        if (warp == 0) {
+            const uint64_t x = s->wsum[lane];
+            s->wsum[lane] = warp_incl_u64(x) - x;
+        }
+        __syncthreads();
+        const long long run = s->base + (long long)(s->wsum[warp] + incl);
+        const long long prev = run - (long long)f;
+        if (i < V && run > s->thr && prev <= s->thr) s->bonus = i;
+    }
+    __syncthreads();
+    const int bo = s->bonus;
+    __syncthreads();
+    return bo;
+}
+
+// sum of the q entries of a 16-entry sparse row equal to `token` (clamped to [0,1] when asked),
+// in entry order (sampling/sparse/accept.py:275-277)
+__device__ __forceinline__ float q_sparse(const int64_t* qid, const float* qv, long long token,
+                                          bool clamp) {
+    float s = 0.0f;
+#pragma unroll
+    for (int k = 0; k < 16; ++k) {
+        if (qid[k] != token) continue;
+        float v = qv[k];
+        if (clamp) v = (v >= 0.0f && v <= 1.0f) ? v : 0.0f;
+        s = __fadd_rn(s, v);
+    }
+    return s;
+}
+
+__device__ __forceinline__ float packed_p(const int32_t* ids, const float* vals, int len, int width,
+                                          long long token) {
+    float s = 0.0f;
+    for (int l = 0; l < width && l < len; ++l)
+        if ((long long)ids[l] == token) s = __fadd_rn(s, vals[l]);
+    return s;
+}
+
+__global__ void __launch_bounds__(kThreads, 1) sparse_accept_kernel(SparseAcceptArgs a) {
+    __shared__ DrawSmem ds;
+    __shared__ int64_t sq_id[16];
+    __shared__ float sq_v[16];
+    __shared__ int s_a;
+    const int b = blockIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int V = a.V;
+    int cap = a.caps[b];
+    cap = cap < 1 ? 1 : (cap > kT ? kT : cap);
+    const long long base = a.row_offsets ? a.row_offsets[b] : (long long)b * kT;
+    const bool packed = a.p_ids != nullptr;
+    const bool raw = a.denom != nullptr;
+
+    if (warp == 0) {
+        bool reject = true;
+        if (lane < cap - 1) {
+            const long long row = base + lane;
+            const long long qi = (long long)b * (kT - 1) + lane;
+            const long long tok = a.cand[(long long)b * kT + lane + 1];
+            const bool dense = packed ? (a.overflow[row] != 0) : true;
+            float p = 0.0f;
+            if (tok >= 0 && tok < V) {
+                if (dense) {
+                    p = a.dense ? a.dense[row * V + tok] : 0.0f;
+                    if (raw) p = __fdiv_rn(p, a.denom[row]);
+                } else {
+                    p = packed_p(a.p_ids + row * a.width, a.p_vals + row * a.width, a.p_len[row],
+                                 a.width, tok);
+                }
+            }
+            const float q = q_sparse(a.q_ids + qi * 16, a.q_vals + qi * 16, tok, false);
+            reject = !(q > 0.0f && q <= 1.0f && __fmul_rn(a.u[qi], q) < p);
+        }
+        const unsigned m = __ballot_sync(0xffffffffu, reject && lane < cap - 1);
+        if (lane == 0) s_a = m ? __ffs(m) - 1 : cap - 1;
+    }
+    __syncthreads();
+    const int acc = s_a;
+    const bool pure0 = acc == cap - 1;
+    const long long row = base + acc;
+    const long long qi = (long long)b * (kT - 1) + (acc < kT - 1 ? acc : 0);
+    const bool dense = packed ? (a.overflow[row] != 0) : true;
+    const float uf = a.uf[b];
+    long long bo = V - 1;
+    if (packed && !dense) {
+        // packed target row: its ids in ascending order (unused slots rank as V, the
+        // reference's padding), residual against q, exact CDF (accept.py:186-204)
+        if (tid == 0) {
+            const int32_t* ids = a.p_ids + row * a.width;
+            const float* vals = a.p_vals + row * a.width;
+            const int len = a.p_len[row];
+            const int n = a.width;
+            long long ord[kMaxPackedWidth];
+            for (int l = 0; l < n; ++l) ord[l] = l < len ? (long long)ids[l] : (long long)V;
+            for (int i = 1; i < n; ++i) {
+                const long long x = ord[i];
+                int j = i - 1;
+                while (j >= 0 && ord[j] > x) {
+                    ord[j + 1] = ord[j];
+                    --j;
+                }
+                ord[j + 1] = x;
+            }
+            const int64_t* qid = a.q_ids + qi * 16;
+            const float* qv = a.q_vals + qi * 16;
+            bool pure = pure0;
+            for (int attempt = 0; attempt < 2; ++attempt) {
+                unsigned long long M = 0;
+                for (int j = 0; j < n; ++j) {
+                    const float p = ord[j] < V ? packed_p(ids, vals, len, n, ord[j]) : 0.0f;
+                    const float r = pure ? p : fmaxf(__fsub_rn(p, q_sparse(qid, qv, ord[j], true)), 0.0f);
+                    M += fixv(r);
+                }
+                if (!pure && M == 0) {
+                    pure = true;
+                    continue;
+                }
+                const long long thr = scale_floor(uf, M);
+                if (thr != -2) {
+                    unsigned long long C = 0;
+                    for (int j = 0; j < n; ++j) {
+                        const float p = ord[j] < V ? packed_p(ids, vals, len, n, ord[j]) : 0.0f;
+                        const float r = pure ? p : fmaxf(__fsub_rn(p, q_sparse(qid, qv, ord[j], true)), 0.0f);
+                        C += fixv(r);
+                        if ((long long)C > thr) {
+                            if (ord[j] < V) bo = ord[j];
+                            break;
+                        }
+                    }
+                }
+                break;
+            }
+            ds.bonus = (int)bo;
+        }
+        __syncthreads();
+        bo = ds.bonus;
+    } else {
+        // dense target row (or the dense fallback of an overflowed packed row)
+        if (tid < 16) {
+            sq_id[tid] = a.q_ids[qi * 16 + tid];
+            sq_v[tid] = a.q_vals[qi * 16 + tid];
+        }
+        __syncthreads();
+        const float* prow = a.dense ? a.dense + row * V : nullptr;
+        const float den = raw ? a.denom[row] : 1.0f;
+        bool pure = pure0;
+        auto w = [&](int i) -> float {
+            float p = prow ? prow[i] : 0.0f;
+            if (raw) p = __fdiv_rn(p, den);
+            if (pure) return p;
+            return fmaxf(__fsub_rn(p, q_sparse(sq_id, sq_v, i, true)), 0.0f);
+        };
+        unsigned long long M = 0;
+        int draw = tile_draw(V, uf, w, &ds, &M);
+        if (!pure && M == 0) {  // zero residual: draw from p
+            pure = true;
+            draw = tile_draw(V, uf, w, &ds, &M);
+        }
+        bo = draw;
+    }
+    if (tid < kT) {
+        const int64_t v = tid < acc ? a.cand[(int64_t)b * kT + tid + 1] : (tid == acc ? bo : 0);
+        a.output[(int64_t)b * kT + tid] = v;
+    }
+    if (tid == 0) {
+        a.accept[b] = acc;
+        a.commit[b] = acc + 1;
+        a.bonus[b] = bo;
+        a.new_seq[b] = a.prefix[b] + acc + 1;
+    }
+}
+
+// ---- compress_probs: sampling/sparse/accept.py:422-460 --------------------------------------
+
+// One CTA per row: the first `capacity` positive entries in index order (ids, values), their
+// number (clamped) and the overflow flag (more than capacity, or a negative / NaN / inf entry).
+__global__ void __launch_bounds__(kThreads, 1)
+    compress_kernel(const float* __restrict__ p, int V, int capacity, int32_t* ids, float* vals,
+                    int32_t* lens, int32_t* ovf) {
+    __shared__ unsigned int wcnt[kThreads / 32];
+    __shared__ unsigned int s_run, s_bad;
+    const long long r = blockIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const float* x = p + r * V;
+    for (int l = tid; l < capacity; l += kThreads) {
+        ids[r * capacity + l] = -1;
+        vals[r * capacity + l] = 0.0f;
+    }
+    if (tid == 0) {
+        s_run = 0;
+        s_bad = 0;
+    }
+    __syncthreads();
+    bool bad = false;
+    for (int t0 = 0; t0 < V; t0 += kThreads) {
+        const int i = t0 + tid;
+        const float v = i < V ? x[i] : 0.0f;
+        bad |= (v < 0.0f) || (v != v) || (fabsf(v) == INFINITY);
+        const bool pos = v > 0.0f;
+        const unsigned m = __ballot_sync(0xffffffffu, pos);
+        if (lane == 0) wcnt[warp] = __popc(m);
+        __syncthreads();
+        unsigned before = s_run, all = 0;
+        for (int w = 0; w < kThreads / 32; ++w) {
+            if (w < warp) before += wcnt[w];
+            all += wcnt[w];
+        }
+        const unsigned slot = before + __popc(m & ((1u << lane) - 1u));
+        if (pos && slot < (unsigned)capacity) {
+            ids[r * capacity + slot] = i;
+            vals[r * capacity + slot] = v;
+        }
+        __syncthreads();
+        if (tid == 0) s_run += all;
+    }
+    if (bad) atomicOr(&s_bad, 1u);
+    __syncthreads();
+    if (tid == 0) {
+        lens[r] = (int32_t)(s_run < (unsigned)capacity ? s_run : (unsigned)capacity);
+        ovf[r] = (s_run > (unsigned)capacity || s_bad) ? 1 : 0;
+    }
+}
+
 }  // namespace pr
 
 int chain_probs_max_vocab() { return pr::kMaxTiles * pr::kThreads; }
+
+int launch_sparse_accept(const SparseAcceptArgs& a, cudaStream_t st) {
+    pr::sparse_accept_kernel<<<a.B, pr::kThreads, 0, st>>>(a);
+    return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
+}
+
+int launch_compress(const float* p, long long rows, int V, int capacity, int32_t* ids, float* vals,
+                    int32_t* lens, int32_t* ovf, cudaStream_t st) {
+    pr::compress_kernel<<<(unsigned)rows, pr::kThreads, 0, st>>>(p, V, capacity, ids, vals, lens, ovf);
+    return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
+}
 
 int launch_chain_probs(const ChainProbsArgs& c, cudaStream_t st) {
     pr::chain_probs_kernel<<<c.B, pr::kThreads, 0, st>>>(c.V, c.cand, c.target, c.draft, c.caps, c.u,

@@ -136,6 +136,33 @@ int dsv_chain_from_probs(int32_t batch, int32_t vocab, const int64_t* candidates
                          int32_t* commit, int64_t* bonus, int64_t* output, int32_t* new_seq,
                          dsv_stream_t stream);
 
+/* ---- capped chain rejection with sparse q ---------------------------------------------------
+ * Replaces sampling/sparse/accept.py:463-543 accept_sparse (_accept_sparse, _dense_bonus,
+ * _packed_bonus): q is sparse, q_ids/q_values [B,15,16] (q of a token = the sum of its
+ * entries); the target row of (b, s) is row_offsets[b] + s (b * 16 without row_offsets) of
+ * dense_p [rows, V] (divided by denominator[row] when given: the reference's raw fallback,
+ * IEEE division) or, with packed rows (p_ids/p_values [rows, width <= 64], p_lengths, and
+ * p_overflow != 0 meaning "use the dense row"), the packed entries (bonus over the row's ids in
+ * ascending order, as the reference).  Exact fixed-point residual CDF; same five outputs as
+ * dsv_verify_logits.  dense_p may be NULL when every packed row is used (pure packed). */
+int dsv_accept_sparse(int32_t batch, int32_t vocab, int32_t width, const int64_t* candidates,
+                      const float* dense_p, const int32_t* p_ids, const float* p_values,
+                      const int32_t* p_lengths, const int32_t* p_overflow, const int64_t* q_ids,
+                      const float* q_values, const int32_t* verify_lens, const float* uniforms,
+                      const float* uniform_final, const int32_t* prefix_lens,
+                      const int64_t* row_offsets, const float* denominator, int32_t* accept,
+                      int32_t* commit, int64_t* bonus, int64_t* output, int32_t* new_seq,
+                      dsv_stream_t stream);
+
+/* ---- compress_probs ------------------------------------------------------------------------
+ * Replaces sampling/sparse/accept.py:422-460 compress_probs: per row of probs [rows, V] the
+ * first `capacity` positive entries in index order (ids int32 / values, padded with -1 / 0),
+ * their clamped count and an overflow flag (more than capacity positives, or any negative,
+ * NaN or infinite entry). */
+int dsv_compress_probs(int64_t rows, int32_t vocab, int32_t capacity, const float* probs,
+                       int32_t* ids, float* values, int32_t* lengths, int32_t* overflow,
+                       dsv_stream_t stream);
+
 /* ---- greedy capped accept ----------------------------------------------------------------------
  * Replaces verification/caps.py:32-59 _accept_capped (and verification/ragged.py:51-76 _accept):
  * with top1 of (b, s) at top1[(b * 16 + s) * top1_stride] (e.g. column 0 of a [B*16, k] top-k
