@@ -72,6 +72,8 @@ _SIGNATURES = {
     "dsv_chain_from_probs": [c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                              c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                              c_void_p],
+    "dsv_target_probs": [c_int64, c_int32, c_int32, c_void_p, c_int64, c_void_p, c_void_p,
+                         c_void_p, c_void_p, c_void_p, c_size_t, c_void_p],
     "dsv_accept_sparse": [c_int32, c_int32, c_int32] + [c_void_p] * 19 + [c_void_p],
     "dsv_compress_probs": [c_int64, c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_void_p,
                            c_void_p, c_void_p],

@@ -369,6 +369,54 @@ int dsv_accept_compact(int32_t batch, const int32_t* commit, const int32_t* veri
                    1);
 }
 
+int dsv_target_probs(int64_t rows, int32_t vocab, int32_t rows_per_request, const void* logits,
+                     int64_t row_stride, const float* temperature, const int32_t* top_k,
+                     const float* top_p, float* probs, void* workspace, size_t workspace_bytes,
+                     dsv_stream_t stream) {
+    if (rows < 0 || vocab < 1 || vocab > 262000 || rows_per_request < 1 || rows_per_request > 16 ||
+        row_stride < vocab || rows % rows_per_request != 0)
+        return DSV_BAD_SHAPE;
+    if (rows == 0) return DSV_OK;
+    if (!logits || !temperature || !top_k || !top_p || !probs || !workspace) return DSV_BAD_POINTER;
+    if (!aligned(logits, 2) || !aligned(workspace, 16)) return DSV_BAD_ALIGNMENT;
+    const long long nreq = rows / rows_per_request;
+    const int chunk = 1024;
+    const int wsb = (int)(nreq < chunk ? nreq : chunk);
+    if (workspace_bytes < dsv::verify_workspace_bytes(wsb)) return DSV_WORKSPACE_TOO_SMALL;
+    char* base = reinterpret_cast<char*>(workspace);
+    int launched = 0;
+    for (long long r0 = 0; r0 < nreq; r0 += chunk) {
+        const int B = (int)((nreq - r0) < chunk ? (nreq - r0) : chunk);
+        dsv::VerifyArgs a = {};
+        a.B = B;
+        a.V = vocab;
+        a.tgt = static_cast<const uint16_t*>(logits) + r0 * rows_per_request * row_stride;
+        a.tgt_row = nullptr;
+        a.row_step = rows_per_request;
+        a.tgt_rows = (long long)B * rows_per_request;
+        a.stride = row_stride;
+        a.temperature = temperature + r0;
+        a.top_k = top_k + r0;
+        a.top_p = top_p + r0;
+        a.caps = nullptr;
+        a.cap_all = rows_per_request;
+        a.ws = reinterpret_cast<dsv::WsHeader*>(base);
+        a.done = reinterpret_cast<unsigned int*>(base + 64);
+        a.res = reinterpret_cast<dsv::TaskResult*>(base + 64 + dsv::verify_done_bytes(wsb));
+        a.desc = reinterpret_cast<dsv::RowDesc*>(base + dsv::verify_desc_offset(wsb));
+        a.gmax = reinterpret_cast<unsigned long long*>(base + dsv::verify_gmax_offset(wsb));
+        a.order = reinterpret_cast<unsigned int*>(base + dsv::verify_order_offset(wsb));
+        a.racc = reinterpret_cast<unsigned int*>(base + dsv::verify_racc_offset(wsb));
+        a.wmass = reinterpret_cast<unsigned long long*>(base + dsv::verify_wmass_offset(wsb));
+        a.prof = reinterpret_cast<unsigned long long*>(base + dsv::verify_prof_offset(wsb));
+        const int st = dsv::launch_target_probs(a, probs + r0 * rows_per_request * (long long)vocab,
+                                                (cudaStream_t)stream);
+        if (st != DSV_OK) return counted(st, launched);
+        launched += 2;
+    }
+    return counted(DSV_OK, launched);
+}
+
 int dsv_verify_logits_noalloc(int32_t batch, int32_t vocab, int32_t dtype,
                               const int64_t* candidates, const void* target_logits,
                               const int64_t* target_row, int64_t target_rows,

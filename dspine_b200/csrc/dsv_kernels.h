@@ -109,6 +109,11 @@ struct VerifyArgs {
     unsigned int* order;       // [B] streaming path: chain-kernel dispatch order
     unsigned int* racc;        // [B,2] streaming path: rows finished, accepted length
     unsigned long long* wmass; // [B,32,8] streaming path: residual mass per slice and warp
+    // standalone target probabilities (dsv_target_probs): caps == null means every request
+    // has cap_all rows, tgt_row == null means request b starts at row b * row_step, cand ==
+    // null skips the chain decision
+    int cap_all;
+    long long row_step;
 };
 
 // launchers (return a dsv::Status)
@@ -116,6 +121,8 @@ int launch_verify(const VerifyArgs& a, int dtype, cudaStream_t stream);
 // streaming path (bf16 rows, B <= 1024, V <= 262144): rows kernel + chain kernel
 bool stream_supported(const VerifyArgs& a, int dtype);
 int launch_stream(VerifyArgs a, cudaStream_t stream);
+// descriptors of every target row (rows kernel only) and the dense probabilities they define
+int launch_target_probs(VerifyArgs a, float* out, cudaStream_t stream);
 
 // ---- LM head fused with top-k (lmhead.cu) ---------------------------------------------------
 struct LmHeadArgs {

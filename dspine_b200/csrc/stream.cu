@@ -217,7 +217,7 @@ __device__ void build_plan(const VerifyArgs& a, Sm* sh, int wink) {
     for (int b = tid; b < a.B; b += blockDim.x) {
         float c;
         const int cat = request_cat(a, b, c, wink);
-        const int cap = clamp_cap(a.caps[b]);
+        const int cap = clamp_cap(a.caps ? a.caps[b] : a.cap_all);
         sh->req[b] = (uint8_t)(cat | (cap << 3));
     }
     __syncthreads();
@@ -275,7 +275,8 @@ __device__ TaskInfo decode_task(const VerifyArgs& a, const Sm* sh, int t) {
     ti.cap = (int)(sh->req[lo] >> 3);
     ti.kind = r < ti.cap ? 0 : 1;
     ti.s = ti.kind == 0 ? r : r - ti.cap;
-    const long long base = ti.kind == 0 ? a.tgt_row[ti.b] : a.drf_row[ti.b];
+    const long long base = ti.kind == 0 ? (a.tgt_row ? a.tgt_row[ti.b] : ti.b * a.row_step)
+                                        : a.drf_row[ti.b];
     const long long lim = ti.kind == 0 ? a.tgt_rows : a.drf_rows;
     const long long row = base + ti.s;
     ti.row = (row >= 0 && row < lim) ? row : -1;
@@ -1296,7 +1297,7 @@ __device__ __forceinline__ RowDesc load_desc_cg(const RowDesc* p) {
 __device__ void row_done(RSmem* sh, const VerifyArgs& a, int b) {
     const int tid = threadIdx.x, lane = tid & 31;
     const int cat = (int)(sh->req[b] & 7u), cap = (int)(sh->req[b] >> 3);
-    if (cat == kGreedy) return;
+    if (cat == kGreedy || a.cand == nullptr) return;
     const unsigned nrows = (unsigned)(cap + (a.drf != nullptr ? cap - 1 : 0));
     __syncthreads();
     if (tid == 0) {
@@ -1921,6 +1922,37 @@ int launch_chain(VerifyArgs a, cudaStream_t stream) {
     return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
 }
 
+// ---------------------------------------------------------------------------------------
+// dense target probabilities from the row descriptors (runtime/worker.py:440-508 output)
+
+constexpr int kPW = 256;  // threads per CTA of the writer
+constexpr int kPWChunk = 8192;  // elements per CTA
+
+__global__ void __launch_bounds__(kPW) probs_write_kernel(VerifyArgs a, float* out) {
+    const long long r = blockIdx.y;                 // row within the launch's requests
+    const int b = (int)(r / a.cap_all), s = (int)(r % a.cap_all);
+    const RowDesc d = a.desc[(b * kT + s) * 2 + 0];
+    const long long row = b * a.row_step + s;
+    const uint16_t* lr = reinterpret_cast<const uint16_t*>(a.tgt) + row * a.stride;
+    float* o = out + r * (long long)a.V;
+    const int i0 = blockIdx.x * kPWChunk;
+    const int i1 = min(i0 + kPWChunk, a.V);
+    for (int i = i0 + threadIdx.x; i < i1; i += kPW) {
+        const uint32_t u = lr[i];
+        o[i] = row_prob(d, bf(u), u, i);
+    }
+    // greedy rows packed their first argmax for the chain step; clear it for the next launch
+    if (blockIdx.x == 0 && threadIdx.x == 0 && (d.flags & kDescGreedy)) a.gmax[b * kT + s] = 0ull;
+}
+
+int launch_target_probs(VerifyArgs a, float* out, cudaStream_t stream) {
+    const int st_ = launch_rows_cta(a, stream);
+    if (st_ != kOk) return st_;
+    const dim3 grid((unsigned)((a.V + kPWChunk - 1) / kPWChunk), (unsigned)(a.B * a.cap_all));
+    probs_write_kernel<<<grid, kPW, 0, stream>>>(a, out);
+    return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
+}
+
 }  // namespace st
 
 bool stream_supported(const VerifyArgs& a, int dtype) {
@@ -1929,6 +1961,10 @@ bool stream_supported(const VerifyArgs& a, int dtype) {
     if ((reinterpret_cast<uintptr_t>(a.tgt) & 1u) || (a.drf && (reinterpret_cast<uintptr_t>(a.drf) & 1u)))
         return false;
     return a.V <= st::kMaxV;
+}
+
+int launch_target_probs(VerifyArgs a, float* out, cudaStream_t stream) {
+    return st::launch_target_probs(a, out, stream);
 }
 
 int launch_stream(VerifyArgs a, cudaStream_t stream) {

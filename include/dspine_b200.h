@@ -122,6 +122,19 @@ int dsv_tp_merge(int32_t rows, int32_t shards, int32_t k, const float* values,
                  const float* lse, int64_t lse_shard_stride, int64_t pad_id, int32_t sort_ids,
                  int64_t* out_ids, float* out_values, float* out_lse, dsv_stream_t stream);
 
+/* ---- target probabilities from logits --------------------------------------------------------
+ * Replaces runtime/worker.py:440-508 build_dspine_target_probs / filter_target_probs (SoftmaxTemp
+ * + joint top-k / top-p, greedy rows one-hot at the lowest-index argmax) as a standalone step:
+ * logits [rows, vocab] bf16 (rows row_stride elements apart), request r = rows
+ * [r * rows_per_request, (r+1) * rows_per_request) with temperature[r], top_k[r], top_p[r]
+ * (rows_per_request <= 16, rows a multiple of it); probs [rows, vocab] fp32 with the exact
+ * canonical kept set and p_i = exp2c((l_i - m) c) * (1 / S_kept).  The workspace is a
+ * dsv_verify_logits workspace for min(rows / rows_per_request, 1024) requests. */
+int dsv_target_probs(int64_t rows, int32_t vocab, int32_t rows_per_request, const void* logits,
+                     int64_t row_stride, const float* temperature, const int32_t* top_k,
+                     const float* top_p, float* probs, void* workspace, size_t workspace_bytes,
+                     dsv_stream_t stream);
+
 /* ---- capped chain rejection from dense probabilities ---------------------------------------
  * Replaces sampling/rejection.py:101-153 sample_capped_chain_from_probs (_sample_capped_chain,
  * :12-98): target_probs [B,16,V] and draft_probs [B,15,V] fp32, contiguous.  Draft s+1 is
