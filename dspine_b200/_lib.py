@@ -77,6 +77,8 @@ _SIGNATURES = {
     "dsv_accept_sparse": [c_int32, c_int32, c_int32] + [c_void_p] * 19 + [c_void_p],
     "dsv_compress_probs": [c_int64, c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_void_p,
                            c_void_p, c_void_p],
+    "dsv_adjust_logits": [c_void_p, c_int32, c_int64, c_int32, c_int64, c_void_p, c_int32,
+                          c_void_p, c_void_p, c_void_p, c_int32, c_void_p, c_void_p],
     "dsv_accept_greedy": [c_int32, c_void_p, c_void_p, c_int64, c_void_p, c_void_p, c_void_p,
                           c_void_p, c_void_p, c_void_p, c_void_p, c_void_p],
     "dsv_uniforms": [c_int32, c_int32, c_void_p, c_void_p, c_int32, c_int32, c_void_p, c_void_p],

@@ -312,6 +312,21 @@ int dsv_compress_probs(int64_t rows, int32_t vocab, int32_t capacity, const floa
                    1);
 }
 
+int dsv_adjust_logits(void* logits, int32_t dtype, int64_t rows, int32_t vocab, int64_t row_stride,
+                      const int64_t* row_to_request, int32_t rows_per_request,
+                      const float* additive, const float* scaling, const uint32_t* vocab_mask,
+                      int32_t mask_words, const float* bias, dsv_stream_t stream) {
+    if (rows < 0 || vocab < 1 || row_stride < vocab || rows > 0x7fffffff) return DSV_BAD_SHAPE;
+    if (dtype != DSV_BF16 && dtype != DSV_F32) return DSV_BAD_DTYPE;
+    if (!row_to_request && rows_per_request < 1) return DSV_BAD_SHAPE;
+    if (vocab_mask && mask_words * 32 < vocab) return DSV_BAD_SHAPE;
+    if (rows == 0) return DSV_OK;
+    if (!logits) return DSV_BAD_POINTER;
+    dsv::AdjustArgs a = {logits, rows, row_stride, vocab, row_to_request, rows_per_request,
+                         additive, scaling, vocab_mask, mask_words, bias};
+    return counted(dsv::launch_adjust(a, dtype, (cudaStream_t)stream), 1);
+}
+
 int dsv_accept_greedy(int32_t batch, const int64_t* candidates, const int64_t* top1,
                       int64_t top1_stride, const int32_t* verify_lens, const int32_t* prefix_lens,
                       int32_t* accept, int32_t* commit, int64_t* bonus, int64_t* output,

@@ -222,6 +222,21 @@ struct GreedyArgs {
     int32_t* new_seq;
 };
 int launch_greedy(const GreedyArgs& g, cudaStream_t stream);
+
+// in-place logit adjustments (small.cu)
+struct AdjustArgs {
+    void* logits;                  // [rows, V] bf16 or fp32, rows `stride` elements apart
+    long long rows, stride;
+    int V;
+    const int64_t* row_to_request; // [rows] or null: request = row / rows_per_request
+    int rows_per_request;
+    const float* additive;         // [requests, V] or null
+    const float* scaling;          // [requests, V] or null
+    const uint32_t* mask;          // [requests, mask_words] bitmask (1 = allowed) or null
+    int mask_words;
+    const float* bias;             // [requests, V] or null
+};
+int launch_adjust(const AdjustArgs& a, int dtype, cudaStream_t stream);
 int launch_uniforms(int n, int width, const int64_t* seeds, const void* positions, int pos64,
                     int stream_id, float* out, cudaStream_t stream);
 int sps_max_batch();

@@ -12,9 +12,12 @@
 //                    plus qo_indptr and the token index (verification/sps.py:27-58)
 //   compact_kernel   accept-compact of tokens and KV slots by the exclusive scan of commit
 //                    (SGLang's _commit_accept, wrapped at runtime/worker.py:745-777)
+//   adjust_kernel    in-place logit adjustments: penalties, grammar bitmask, logit bias
+//                    (sampling/compact.py:14-79 adjust_logits), one pass over the rows
 //
 // Every kernel is small (B requests, at most a few thousand entries); the cost is launch
 // latency, so each is one launch with no host synchronisation.
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -285,6 +288,64 @@ int launch_compact(int B, const int32_t* commit, const int32_t* lens, const int6
     sm::compact_kernel<<<1, sm::kCompactThreads, 0, st>>>(B, commit, lens, output, slots, slots_len,
                                                            slot_row, tok_out, slot_out, offsets,
                                                            free_out, free_offsets, err);
+    return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
+}
+
+}  // namespace dsv
+
+// ---- logit adjustments: sampling/compact.py:14-79 (adjust_logits) ------------------------------
+//
+// In place on bf16 or fp32 logit rows, in the reference's order: additive penalties, scaling
+// penalties (l < 0 ? l * s : l / s), the grammar bitmask (bit clear: -inf), the logit bias.
+// Each step rounds to the logit dtype like the torch ops it replaces (one pass over the rows).
+namespace dsv {
+namespace adj {
+
+template <typename T>
+__device__ __forceinline__ float ld(const T* p);
+template <>
+__device__ __forceinline__ float ld<float>(const float* p) { return *p; }
+template <>
+__device__ __forceinline__ float ld<__nv_bfloat16>(const __nv_bfloat16* p) { return __bfloat162float(*p); }
+
+template <typename T>
+__device__ __forceinline__ float rnd(float x);
+template <>
+__device__ __forceinline__ float rnd<float>(float x) { return x; }
+template <>
+__device__ __forceinline__ float rnd<__nv_bfloat16>(float x) { return __bfloat162float(__float2bfloat16_rn(x)); }
+
+template <typename T>
+__device__ __forceinline__ void st(T* p, float x);
+template <>
+__device__ __forceinline__ void st<float>(float* p, float x) { *p = x; }
+template <>
+__device__ __forceinline__ void st<__nv_bfloat16>(__nv_bfloat16* p, float x) { *p = __float2bfloat16_rn(x); }
+
+template <typename T>
+__global__ void adjust_kernel(AdjustArgs a) {
+    const long long r = blockIdx.y;
+    const long long req = a.row_to_request ? a.row_to_request[r] : r / a.rows_per_request;
+    T* row = reinterpret_cast<T*>(a.logits) + r * a.stride;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.V; i += gridDim.x * blockDim.x) {
+        float l = ld<T>(row + i);
+        if (a.additive) l = rnd<T>(__fadd_rn(l, a.additive[req * a.V + i]));
+        if (a.scaling) {
+            const float s = a.scaling[req * a.V + i];
+            l = rnd<T>(l < 0.0f ? __fmul_rn(l, s) : __fdiv_rn(l, s));
+        }
+        if (a.mask && !((a.mask[req * a.mask_words + (i >> 5)] >> (i & 31)) & 1u)) l = -INFINITY;
+        if (a.bias) l = rnd<T>(__fadd_rn(l, a.bias[req * a.V + i]));
+        st<T>(row + i, l);
+    }
+}
+
+}  // namespace adj
+
+int launch_adjust(const AdjustArgs& a, int dtype, cudaStream_t st) {
+    const dim3 grid((unsigned)((a.V + 255) / 256 < 64 ? (a.V + 255) / 256 : 64), (unsigned)a.rows);
+    if (dtype == 0) adj::adjust_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(a);
+    else adj::adjust_kernel<float><<<grid, 256, 0, st>>>(a);
     return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
 }
 

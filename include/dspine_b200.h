@@ -176,6 +176,20 @@ int dsv_compress_probs(int64_t rows, int32_t vocab, int32_t capacity, const floa
                        int32_t* ids, float* values, int32_t* lengths, int32_t* overflow,
                        dsv_stream_t stream);
 
+/* ---- logit adjustments ---------------------------------------------------------------------
+ * Replaces sampling/compact.py:14-79 adjust_logits (the native transforms of SGLang's
+ * SamplingBatchInfo, in its order) in place on logits [rows, vocab] (bf16 or fp32, rows
+ * row_stride elements apart): + additive[req] (acc_additive_penalties / acc_linear_penalties),
+ * then scaling[req] (l < 0 ? l * s : l / s, acc_scaling_penalties), then the grammar bitmask
+ * (vocab_mask[req] bit i clear: -inf; mask_words 32-bit words per request), then + bias[req]
+ * (logit_bias); each step rounded to the logit dtype as the torch op it replaces.  Request of
+ * row r: row_to_request[r], or r / rows_per_request when row_to_request is NULL.  Any of the
+ * four inputs may be NULL. */
+int dsv_adjust_logits(void* logits, int32_t dtype, int64_t rows, int32_t vocab, int64_t row_stride,
+                      const int64_t* row_to_request, int32_t rows_per_request,
+                      const float* additive, const float* scaling, const uint32_t* vocab_mask,
+                      int32_t mask_words, const float* bias, dsv_stream_t stream);
+
 /* ---- greedy capped accept ----------------------------------------------------------------------
  * Replaces verification/caps.py:32-59 _accept_capped (and verification/ragged.py:51-76 _accept):
  * with top1 of (b, s) at top1[(b * 16 + s) * top1_stride] (e.g. column 0 of a [B*16, k] top-k

@@ -73,3 +73,38 @@ def test_tp_head_host_logic_two_ranks():
     for p in procs:
         p.join(timeout=60)
     assert res == {0: "ok", 1: "ok"}, res
+
+
+def _sync_worker(rank, world, port, q):
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        from dspine_b200.runtime.tp_sync import TpCoordinator
+        tp = TpCoordinator()
+        acc = torch.full((4,), rank, dtype=torch.int32)
+        bonus = torch.full((4,), 100 + rank, dtype=torch.int64)
+        out = torch.full((4, 16), 7 * rank, dtype=torch.int64)
+        ptrs = (acc.data_ptr(), bonus.data_ptr(), out.data_ptr())
+        tp.sync_accept(acc, None, bonus, out)
+        ok = (acc == 0).all() and (bonus == 100).all() and (out == 0).all()
+        ok = ok and ptrs == (acc.data_ptr(), bonus.data_ptr(), out.data_ptr())
+        ok = ok and acc.dtype == torch.int32
+        dist.destroy_process_group()
+        q.put((rank, "ok" if ok else "mismatch"))
+    except Exception as e:
+        q.put((rank, repr(e)))
+
+
+def test_sync_accept_broadcasts_in_place_two_ranks():
+    """runtime/tp_sync.py:67-106: rank 0's accept buffers reach every rank, in place."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_sync_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert res == {0: "ok", 1: "ok"}, res
