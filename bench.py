@@ -491,6 +491,29 @@ def run_head(args):
     for _ in range(max(args.warmup, 3)):
         step()
     barrier()
+    # config 3: the step (shard head, all-gather, merge, accept) is a handful of short
+    # launches; it is captured once in a CUDA graph and replayed, so host launch overhead
+    # does not pace the GPU (every rank captures the same collective sequence)
+    graph = None
+    run = step
+    per_step = None
+    if args.config == "config3":
+        side = torch.cuda.Stream(device=dev)
+        side.wait_stream(torch.cuda.current_stream(dev))
+        with torch.cuda.stream(side):
+            step()
+        torch.cuda.current_stream(dev).wait_stream(side)
+        barrier()
+        graph = torch.cuda.CUDAGraph()
+        c0 = lib.dsv_launch_count()
+        with torch.cuda.graph(graph):
+            graph_res = step()
+        per_step = lib.dsv_launch_count() - c0
+        barrier()
+
+        def run():
+            graph.replay()
+            return graph_res
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     launches0 = lib.dsv_launch_count()
@@ -498,10 +521,12 @@ def run_head(args):
     with sampler:
         for i in range(args.steps):
             starts[i].record()
-            step()
+            run()
             ends[i].record()
         barrier()
     launches = lib.dsv_launch_count() - launches0
+    if per_step is not None:
+        launches = per_step * args.steps  # replays enqueue the captured kernels
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     total_ms = sum(step_ms)
     if dist is not None:
@@ -517,13 +542,13 @@ def run_head(args):
 
     # end to end: hidden states from pinned host memory, top-k/lse (and accept) read back
     host_x = hidden.cpu().pin_memory()
-    res = step()
+    res = run()
     host_ids = torch.empty(res.shape, dtype=res.dtype).pin_memory()
     e2e_steps = max(3, min(args.steps, 20))
 
     def e2e_step():
         hidden.copy_(host_x, non_blocking=True)
-        r = step()
+        r = run()
         host_ids.copy_(r, non_blocking=True)
         torch.cuda.current_stream(dev).synchronize()
     e2e_step()
@@ -557,6 +582,7 @@ def run_head(args):
             "dtype": "bf16 (fp32 accumulate)", "data": "synthetic",
             "config": {"workload": f"{args.config}: {WORKLOADS[args.config]}",
                        "rows": rows, "hidden": H, "vocab": VOCAB, "k": k, "tp": tp,
+                       "cuda_graph": graph is not None or per_step is not None,
                        "parallelism": f"tp{tp}" if tp > 1 else "dp1",
                        "l2": "inputs larger than L2 (weight shard streamed every step)"},
             "clocks": sampler.summary(),
@@ -569,6 +595,7 @@ def run_head(args):
                          "peak_source": src, "kernel": "dsv::lm::lmhead_kernel (+ merge)",
                          "flops_per_launch": flops, "kernel_ms": kernel_ms},
         }
+    del graph  # graphs holding NCCL calls go before the process group
     if dist is not None:
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()

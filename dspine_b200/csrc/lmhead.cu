@@ -529,10 +529,16 @@ void geometry(int M, int N, int* mt, int* nsplit, int* ntiles) {
 
 template <int TK>
 int launch_tk(const CUtensorMap& mx, const CUtensorMap& mw, const LmArgs& a, cudaStream_t st) {
-    // per launch: the attribute belongs to the current device, and the call is cheap
-    if (cudaFuncSetAttribute(lmhead_kernel<TK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             kSmemBytes) != cudaSuccess)
-        return kLaunchFailed;
+    // once per device (the attribute belongs to the current device; no call during capture)
+    static int attr_set[64] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return kLaunchFailed;
+    if (!attr_set[dev]) {
+        if (cudaFuncSetAttribute(lmhead_kernel<TK>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 kSmemBytes) != cudaSuccess)
+            return kLaunchFailed;
+        attr_set[dev] = 1;
+    }
     lmhead_kernel<TK><<<a.mt * a.nsplit, kThreads, kSmemBytes, st>>>(mx, mw, a);
     return cudaGetLastError() == cudaSuccess ? 0 : kLaunchFailed;
 }
