@@ -432,6 +432,78 @@ int dsv_target_probs(int64_t rows, int32_t vocab, int32_t rows_per_request, cons
     return counted(DSV_OK, launched);
 }
 
+int dsv_serial_sample_chain(int32_t batch, int32_t block_size, int32_t k, const float* table,
+                            const float* inv_temp, const int32_t* top_k, const float* top_p,
+                            const float* min_p, const int32_t* greedy, const float* u,
+                            const int64_t* candidates, const int64_t* greedy_tok,
+                            int64_t* out_tok, float* out_q, float* confidence_out,
+                            dsv_stream_t stream) {
+    if (batch < 0 || block_size < 2 || k < 1 || k > dsv::serial_max_k()) return DSV_BAD_SHAPE;
+    if ((int64_t)batch * (block_size - 1) > INT32_MAX) return DSV_BAD_SHAPE;
+    if (batch == 0) return DSV_OK;
+    if (!table || !inv_temp || !top_k || !top_p || !min_p || !greedy || !u || !candidates ||
+        !greedy_tok || !out_tok || !out_q)
+        return DSV_BAD_POINTER;
+    dsv::SampleChainArgs a = {batch, block_size - 1, k, table, inv_temp, top_k, top_p, min_p,
+                              greedy, u, candidates, greedy_tok, out_tok, out_q, confidence_out};
+    return counted(dsv::launch_sample_chain(a, (cudaStream_t)stream), 1);
+}
+
+int dsv_serial_table(int32_t batch, int32_t block_size, int32_t hidden, int32_t rk, int32_t k,
+                     int64_t vocab, const void* raw, int64_t raw_stride, const void* norm_w,
+                     const int64_t* candidates, const int64_t* input_ids, const void* lm_head,
+                     int64_t lm_stride, int32_t head_candidates, const void* tg, const void* tsv,
+                     const void* query, int64_t query_stride, const float* rms,
+                     const void* gate_b, int64_t* idx, float* confidence, dsv_stream_t stream) {
+    if (batch < 0 || block_size < 2) return DSV_BAD_SHAPE;
+    if (hidden < 512 || hidden % 512 || hidden > 16384) return DSV_BAD_SHAPE;
+    if (rk < 128 || rk % 128 || k < 2 || k > dsv::serial_max_k() || (k & (k - 1))) return DSV_BAD_SHAPE;
+    if (vocab < 1 || raw_stride < hidden || lm_stride < hidden || query_stride < rk) return DSV_BAD_SHAPE;
+    const int64_t n = (int64_t)batch * (block_size - 1);
+    if (n > INT32_MAX) return DSV_BAD_SHAPE;
+    if (batch == 0) return DSV_OK;
+    if (!raw || !norm_w || !candidates || !input_ids || !lm_head || !tg || !tsv || !query ||
+        !rms || !gate_b || !idx)
+        return DSV_BAD_POINTER;
+    if (!aligned(lm_head, 16) || lm_stride % 8) return DSV_BAD_ALIGNMENT;
+    dsv::TableArgs a;
+    a.n = (int)n;
+    a.t = block_size;
+    a.h = hidden;
+    a.rk = rk;
+    a.k = k;
+    a.vocab = vocab;
+    a.raw = static_cast<const __nv_bfloat16*>(raw);
+    a.raw_stride = raw_stride;
+    a.norm_w = static_cast<const __nv_bfloat16*>(norm_w);
+    a.cand = candidates;
+    a.input_ids = input_ids;
+    a.lm_w = static_cast<const __nv_bfloat16*>(lm_head);
+    a.w_stride = lm_stride;
+    a.head_candidates = head_candidates != 0;
+    a.tg = static_cast<const __nv_bfloat16*>(tg);
+    a.tsv = static_cast<const __nv_bfloat16*>(tsv);
+    a.query = static_cast<const __nv_bfloat16*>(query);
+    a.q_stride = query_stride;
+    a.rms = rms;
+    a.gate_b = static_cast<const __nv_bfloat16*>(gate_b);
+    a.idx = idx;
+    a.confidence = confidence;
+    return counted(dsv::launch_serial_table(a, (cudaStream_t)stream), 1);
+}
+
+int dsv_serial_chain(int32_t batch, int32_t block_size, int32_t k, const int64_t* idx,
+                     const int64_t* candidates, int64_t* out, const float* confidence,
+                     float* confidence_out, dsv_stream_t stream) {
+    if (batch < 0 || block_size < 2 || k < 1) return DSV_BAD_SHAPE;
+    if ((confidence == nullptr) != (confidence_out == nullptr)) return DSV_BAD_POINTER;
+    if (batch == 0) return DSV_OK;
+    if (!idx || !candidates || !out) return DSV_BAD_POINTER;
+    return counted(dsv::launch_serial_chain(batch, block_size - 1, k, idx, candidates, out,
+                                            confidence, confidence_out, (cudaStream_t)stream),
+                   1);
+}
+
 int dsv_verify_logits_noalloc(int32_t batch, int32_t vocab, int32_t dtype,
                               const int64_t* candidates, const void* target_logits,
                               const int64_t* target_row, int64_t target_rows,

@@ -1,6 +1,7 @@
 // dsv_kernels.h -- argument blocks and launchers shared by the kernels and the C ABI.
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -206,6 +207,49 @@ int launch_sparse_accept(const SparseAcceptArgs& a, cudaStream_t stream);
 int launch_compress(const float* p, long long rows, int V, int capacity, int32_t* ids, float* vals,
                     int32_t* lens, int32_t* ovf, cudaStream_t stream);
 int launch_chain_probs(const ChainProbsArgs& c, cudaStream_t stream);
+
+// ---- draft-side serial chains (serial.cu) ---------------------------------------------------
+struct SampleChainArgs {
+    int bs, tm1, k;               // requests, drafted rows per request (T-1), candidates per row
+    const float* table;           // [bs*tm1, k, k]
+    const float* inv_temp;        // [bs]
+    const int32_t* top_k;         // [bs]
+    const float* top_p;           // [bs]
+    const float* min_p;           // [bs]
+    const int32_t* greedy;        // [bs]
+    const float* u;               // [bs*tm1]
+    const int64_t* cand;          // [bs*tm1, k]
+    const int64_t* greedy_tok;    // [bs*tm1]
+    int64_t* out_tok;             // [bs*tm1]
+    float* out_q;                 // [bs*tm1, k]
+    float* confidence;            // [bs*tm1] or null
+};
+struct TableArgs {
+    int n, t, h, rk, k;           // drafted rows, block width T, hidden, RK, candidates per row
+    long long vocab;              // rows of tg / tsv (and of lm_w unless head_candidates)
+    const __nv_bfloat16* raw;     // [bs*T, h]
+    long long raw_stride;
+    const __nv_bfloat16* norm_w;  // [h]
+    const int64_t* cand;          // [n, k]
+    const int64_t* input_ids;     // [bs*T]
+    const __nv_bfloat16* lm_w;    // [vocab, h] or candidate head [n*k, h]
+    long long w_stride;
+    int head_candidates;
+    const __nv_bfloat16* tg;      // [vocab, rk]
+    const __nv_bfloat16* tsv;     // [vocab, 2*rk]
+    const __nv_bfloat16* query;   // [bs*T, >= rk]
+    long long q_stride;
+    const float* rms;             // [bs*T]
+    const __nv_bfloat16* gate_b;  // [rk]
+    int64_t* idx;                 // [n, k]
+    float* confidence;            // [n, k] or null
+};
+int serial_max_k();
+size_t serial_table_smem(int h, int k);
+int launch_sample_chain(const SampleChainArgs& a, cudaStream_t stream);
+int launch_serial_table(const TableArgs& a, cudaStream_t stream);
+int launch_serial_chain(int bs, int tm1, int k, const int64_t* idx, const int64_t* cand,
+                        int64_t* out, const float* conf, float* conf_out, cudaStream_t stream);
 
 // ---- per-request steps (small.cu) -----------------------------------------------------------
 struct GreedyArgs {

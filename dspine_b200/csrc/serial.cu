@@ -1,0 +1,333 @@
+// serial.cu -- the draft side of a block: the serial last-write refinement tables and chains
+// that produce the draft tokens, their q rows and their confidences (sm_100a).
+//
+//   sample_chain_kernel  sampled chain over a K x K table (kernels/dspine.py:616-772
+//                        _serial_sample_chain / serial_sample_chain): per request, row by row,
+//                        softmax(table[n, sender] * inv_temp), joint top-k / top-p / min-p
+//                        filter, inverse-CDF draw with u[n]; writes the token, the filtered q
+//                        row that verification consumes, the pre-filter confidence
+//   table_kernel         greedy refinement table (kernels/dspine.py:210-287 _serial_table /
+//                        serial_table): s[j, c] = base[c] + rms * sum_r m[j, r] TG[id_c, r],
+//                        best lane per sender lane j, confidence 1 / sum exp((s - best) / rms)
+//   chain_kernel         greedy walk of that table (kernels/dspine.py:290-324 _serial_chain)
+//
+// All three are per-request or per-row work on K <= 64 candidates: the cost is launch latency
+// and, for the table, reading K weight rows per drafted position.  Arithmetic is fp32 as in
+// the reference (exp through expf, sigmoid as 1 / (1 + exp(-x)), IEEE division).
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <math.h>
+#include <stdint.h>
+
+#include "dsv_common.cuh"
+#include "dsv_kernels.h"
+
+namespace dsv {
+namespace ser {
+
+constexpr int kMaxK = 64;
+constexpr int kChainWarps = 4;  // requests per CTA of the sampled chain
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+
+// ---- sampled chain -----------------------------------------------------------------------
+//
+// One warp per request; lane l holds candidates l and l + 32.  Per drafted row n:
+//   p      = softmax(table[n, sender, :] * inv_temp)            (max-shifted expf, IEEE /)
+//   rank_c = #{d : p_d > p_c or (p_d == p_c and d < c)}         (ties to the lower lane)
+//   before = sum of p over the lanes ranked ahead, added in rank order
+//   keep   = rank < top_k and before <= top_p and p >= min_p * max p
+//   q      = keep ? p / sum(kept p) : 0;  cdf = running sum of q in lane order
+//   choice = min(#{c : cdf_c <= u * cdf_{K-1}}, last kept lane)
+// The token is cand[n, choice] (greedy requests: greedy_tok[n] with a one-hot q on the
+// matching candidates); the next row's sender lane is choice in both cases.
+__global__ void __launch_bounds__(kChainWarps * 32)
+    sample_chain_kernel(SampleChainArgs a) {
+    __shared__ float s_p[kChainWarps][kMaxK];
+    __shared__ float s_q[kChainWarps][kMaxK];
+    __shared__ int s_ord[kChainWarps][kMaxK];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int b = blockIdx.x * kChainWarps + warp;
+    if (b >= a.bs) return;
+    const int K = a.k;
+    float* P = s_p[warp];
+    float* Q = s_q[warp];
+    int* ord = s_ord[warp];
+    const float inv_t = a.inv_temp[b];
+    const int top_k = a.top_k[b];
+    const float top_p = a.top_p[b], min_p = a.min_p[b];
+    const bool greedy = a.greedy[b] != 0;
+    const bool v0 = lane < K, v1 = lane + 32 < K;
+    int sender = 0;
+    for (int row = 0; row < a.tm1; ++row) {
+        const int64_t n = (int64_t)b * a.tm1 + row;
+        const float* tab = a.table + (n * K + sender) * K;
+        const float s0 = v0 ? tab[lane] * inv_t : -INFINITY;
+        const float s1 = v1 ? tab[lane + 32] * inv_t : -INFINITY;
+        const float mx = warp_max(fmaxf(s0, s1));
+        const float m0 = v0 ? expf(s0 - mx) : 0.0f;
+        const float m1 = v1 ? expf(s1 - mx) : 0.0f;
+        const float total = warp_sum(m0 + m1);
+        const float p0 = m0 / total, p1 = m1 / total;
+        const float pmax = warp_max(fmaxf(v0 ? p0 : -INFINITY, v1 ? p1 : -INFINITY));
+        if (a.confidence && !greedy && lane == 0) a.confidence[n] = pmax;
+        if (v0) P[lane] = p0;
+        if (v1) P[lane + 32] = p1;
+        __syncwarp();
+        int r0 = 0, r1 = 0;
+        for (int d = 0; d < K; ++d) {
+            const float pd = P[d];
+            r0 += (pd > p0) || (pd == p0 && d < lane);
+            r1 += (pd > p1) || (pd == p1 && d < lane + 32);
+        }
+        if (v0) ord[r0] = lane;
+        if (v1) ord[r1] = lane + 32;
+        __syncwarp();
+        float b0 = 0.0f, b1 = 0.0f;  // mass ranked ahead, added in rank order
+        for (int r = 0; r < (v0 ? r0 : 0); ++r) b0 += P[ord[r] & (kMaxK - 1)];
+        for (int r = 0; r < (v1 ? r1 : 0); ++r) b1 += P[ord[r] & (kMaxK - 1)];
+        const float floor_p = min_p * pmax;
+        const bool k0 = v0 && r0 < top_k && b0 <= top_p && p0 >= floor_p;
+        const bool k1 = v1 && r1 < top_k && b1 <= top_p && p1 >= floor_p;
+        const float w0 = k0 ? p0 : 0.0f, w1 = k1 ? p1 : 0.0f;
+        float wsum = 0.0f;  // kept mass in lane order
+        {
+            if (v0) Q[lane] = w0;
+            if (v1) Q[lane + 32] = w1;
+            __syncwarp();
+            for (int d = 0; d < K; ++d) wsum += Q[d];
+            __syncwarp();
+        }
+        const float q0 = w0 / wsum, q1 = w1 / wsum;
+        if (v0) Q[lane] = q0;
+        if (v1) Q[lane + 32] = q1;
+        __syncwarp();
+        float c0 = 0.0f, c1 = 0.0f;  // running sums in lane order
+        for (int d = 0; d <= lane && d < K; ++d) c0 += Q[d];
+        if (v1) {
+            c1 = c0;
+            for (int d = lane + 1; d <= lane + 32; ++d) c1 += Q[d];
+        }
+        // cdf of the last lane (the total the draw is scaled by)
+        const int last_lane = (K - 1) & 31;
+        const float ctot = __shfl_sync(0xffffffffu, K > 32 ? c1 : c0, last_lane);
+        const float thr = a.u[n] * ctot;
+        const unsigned under0 = __ballot_sync(0xffffffffu, v0 && c0 <= thr);
+        const unsigned under1 = __ballot_sync(0xffffffffu, v1 && c1 <= thr);
+        int choice = __popc(under0) + __popc(under1);
+        const unsigned kb0 = __ballot_sync(0xffffffffu, k0);
+        const unsigned kb1 = __ballot_sync(0xffffffffu, k1);
+        const int last = kb1 ? 32 + 31 - __clz(kb1) : (kb0 ? 31 - __clz(kb0) : 0);
+        choice = min(choice, last);
+        const int64_t* cand = a.cand + n * K;
+        const int64_t gtok = a.greedy_tok[n];
+        float* qo = a.out_q + n * K;
+        if (v0) qo[lane] = greedy ? (cand[lane] == gtok ? 1.0f : 0.0f) : q0;
+        if (v1) qo[lane + 32] = greedy ? (cand[lane + 32] == gtok ? 1.0f : 0.0f) : q1;
+        if (lane == 0) a.out_tok[n] = greedy ? gtok : cand[choice];
+        sender = choice;
+        __syncwarp();
+    }
+}
+
+// ---- greedy refinement table ---------------------------------------------------------------
+//
+// One CTA per drafted row n (request b = n / (T-1), block row r = n % (T-1), state row
+// b * T + 1 + r).  Candidate lanes c < K with ids id_c = cand[n, c]; sender lanes j carry the
+// anchor token on block row 0 and the previous row's candidates after it.
+//   u[h]    = raw[row, h] * norm_w[h]                                  (fp32)
+//   base[c] = sum_h W[id_c, h] u[h]      (W = lm_head rows by id, or candidate_head[n, c])
+//   m[j, r] = sigmoid(query[row, r] + TSV[sid_j, r] + gate_b[r]) * TSV[sid_j, RK + r]
+//   s[j, c] = base[c] + rms[row] * sum_r m[j, r] TG[id_c, r]
+//   idx[n, j] = first c of max_c s[j, c];  conf[n, j] = 1 / sum_c exp((s[j, c] - max) / max(rms, 1e-6))
+// The r sum runs in chunks of 128 columns staged in shared memory (row pitch 129 floats so the
+// K candidate rows of one column sit in distinct banks); each thread owns up to 16 (j, c) pairs.
+constexpr int kTabThreads = 256;
+constexpr int kRChunk = 128;
+constexpr int kRPitch = kRChunk + 1;
+constexpr int kMaxPairs = kMaxK * kMaxK / kTabThreads;  // 16
+
+__device__ __forceinline__ float bf(const __nv_bfloat16 x) { return __bfloat162float(x); }
+
+__device__ __forceinline__ float sigmoidf_(float x) { return 1.0f / (1.0f + expf(-x)); }
+
+size_t table_smem_bytes(int h, int k) {
+    return (size_t)h * 4 + (size_t)2 * k * kRPitch * 4 + (size_t)k * 4 + (size_t)2 * k * 8 + 16;
+}
+
+__global__ void __launch_bounds__(kTabThreads)
+    table_kernel(TableArgs a) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int K = a.k, H = a.h, RK = a.rk;
+    float* u = reinterpret_cast<float*>(smem);               // [H]
+    float* mch = u + H;                                      // [K][kRPitch]
+    float* gch = mch + K * kRPitch;                          // [K][kRPitch]
+    float* base = gch + K * kRPitch;                         // [K]
+    int64_t* ids = reinterpret_cast<int64_t*>(base + K + (K & 1));  // [K]
+    int64_t* sid = ids + K;                                  // [K]
+    __shared__ int s_bad;
+
+    const int n = blockIdx.x;
+    const int tm1 = a.t - 1;
+    const int b = n / tm1, r = n % tm1;
+    const int64_t row = (int64_t)b * a.t + 1 + r;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    if (tid == 0) s_bad = 0;
+    __syncthreads();
+    if (tid < K) {
+        const int64_t id = a.cand[(int64_t)n * K + tid];
+        const int64_t s = r == 0 ? a.input_ids[(int64_t)b * a.t] : a.cand[(int64_t)(n - 1) * K + tid];
+        ids[tid] = id;
+        sid[tid] = s;
+        if (id < 0 || id >= a.vocab || s < 0 || s >= a.vocab) atomicOr(&s_bad, 1);
+    }
+    const __nv_bfloat16* xr = a.raw + row * a.raw_stride;
+    for (int h = tid; h < H; h += kTabThreads) u[h] = bf(xr[h]) * bf(a.norm_w[h]);
+    __syncthreads();
+    if (s_bad) {  // a candidate or sender id outside the tables: no reads, flagged outputs
+        if (tid < K) {
+            a.idx[(int64_t)n * K + tid] = -1;
+            if (a.confidence) a.confidence[(int64_t)n * K + tid] = NAN;
+        }
+        return;
+    }
+    // base[c]: one warp per candidate row, 8 bf16 per lane per step
+    for (int c = warp; c < K; c += kTabThreads / 32) {
+        const __nv_bfloat16* w = a.head_candidates ? a.lm_w + ((int64_t)n * K + c) * a.w_stride
+                                                   : a.lm_w + ids[c] * a.w_stride;
+        float acc = 0.0f;
+        for (int h = lane * 8; h < H; h += 256) {
+            const uint4 v = *reinterpret_cast<const uint4*>(w + h);
+            const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&v);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                const float2 f = __bfloat1622float2(p2[e]);
+                acc = fmaf(f.x, u[h + 2 * e], acc);
+                acc = fmaf(f.y, u[h + 2 * e + 1], acc);
+            }
+        }
+        acc = warp_sum(acc);
+        if (lane == 0) base[c] = acc;
+    }
+    const int pairs = K * K;
+    float acc[kMaxPairs];
+#pragma unroll
+    for (int i = 0; i < kMaxPairs; ++i) acc[i] = 0.0f;
+    const __nv_bfloat16* q = a.query + row * a.q_stride;
+    for (int r0 = 0; r0 < RK; r0 += kRChunk) {
+        __syncthreads();  // previous chunk consumed
+        for (int e = tid; e < K * kRChunk; e += kTabThreads) {
+            const int j = e / kRChunk, rr = e % kRChunk, col = r0 + rr;
+            const __nv_bfloat16* t = a.tsv + sid[j] * (int64_t)(2 * RK);
+            const float gate = (bf(q[col]) + bf(t[col])) + bf(a.gate_b[col]);
+            mch[j * kRPitch + rr] = sigmoidf_(gate) * bf(t[RK + col]);
+            gch[j * kRPitch + rr] = bf(a.tg[ids[j] * (int64_t)RK + col]);
+        }
+        __syncthreads();
+#pragma unroll
+        for (int i = 0; i < kMaxPairs; ++i) {
+            const int pidx = tid + i * kTabThreads;
+            if (pidx < pairs) {
+                const int j = pidx / K, c = pidx % K;
+                const float* mr = mch + j * kRPitch;
+                const float* gr = gch + c * kRPitch;
+                float s = acc[i];
+                for (int rr = 0; rr < kRChunk; ++rr) s = fmaf(mr[rr], gr[rr], s);
+                acc[i] = s;
+            }
+        }
+    }
+    __syncthreads();
+    // s[j][c] into the m area (pitch K + 1), then one warp per sender lane j
+    float* sv = mch;
+    const float rms = a.rms[row];
+#pragma unroll
+    for (int i = 0; i < kMaxPairs; ++i) {
+        const int pidx = tid + i * kTabThreads;
+        if (pidx < pairs) {
+            const int j = pidx / K, c = pidx % K;
+            sv[j * (K + 1) + c] = base[c] + rms * acc[i];
+        }
+    }
+    __syncthreads();
+    const float scale = fmaxf(rms, 1e-6f);
+    for (int j = warp; j < K; j += kTabThreads / 32) {
+        const float* sr = sv + j * (K + 1);
+        const float x0 = lane < K ? sr[lane] : -INFINITY;
+        const float x1 = lane + 32 < K ? sr[lane + 32] : -INFINITY;
+        const float best = warp_max(fmaxf(x0, x1));
+        const unsigned at0 = __ballot_sync(0xffffffffu, lane < K && x0 == best);
+        const unsigned at1 = __ballot_sync(0xffffffffu, lane + 32 < K && x1 == best);
+        const int arg = at0 ? __ffs(at0) - 1 : (at1 ? 32 + __ffs(at1) - 1 : 0);
+        if (lane == 0) a.idx[(int64_t)n * K + j] = arg;
+        if (a.confidence) {
+            const float e0 = lane < K ? expf((x0 - best) / scale) : 0.0f;
+            const float e1 = lane + 32 < K ? expf((x1 - best) / scale) : 0.0f;
+            const float mass = warp_sum(e0 + e1);
+            if (lane == 0) a.confidence[(int64_t)n * K + j] = 1.0f / mass;
+        }
+    }
+}
+
+// ---- greedy chain ---------------------------------------------------------------------------
+// One thread per request: j = idx[first row, lane 0], then per row the candidate at lane j and
+// the next row's lane idx[next row, j].  A lane outside [0, K) selects nothing (value 0), as
+// the reference's masked selection does.
+__global__ void chain_kernel(int bs, int tm1, int K, const int64_t* __restrict__ idx,
+                             const int64_t* __restrict__ cand, int64_t* out,
+                             const float* __restrict__ conf, float* conf_out) {
+    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+    if (b >= bs) return;
+    const int64_t n0 = (int64_t)b * tm1;
+    int64_t j = idx[n0 * K];
+    int64_t prev = 0;
+    for (int r = 0; r < tm1; ++r) {
+        const int64_t n = n0 + r;
+        if (conf) conf_out[n] = (prev >= 0 && prev < K) ? conf[n * K + prev] : 0.0f;
+        out[n] = (j >= 0 && j < K) ? cand[n * K + j] : 0;
+        prev = j;
+        j = (r + 1 < tm1 && j >= 0 && j < K) ? idx[(n + 1) * K + j] : 0;
+    }
+}
+
+}  // namespace ser
+
+int launch_sample_chain(const SampleChainArgs& a, cudaStream_t st) {
+    const unsigned blocks = (unsigned)((a.bs + ser::kChainWarps - 1) / ser::kChainWarps);
+    ser::sample_chain_kernel<<<blocks, ser::kChainWarps * 32, 0, st>>>(a);
+    return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
+}
+
+int serial_max_k() { return ser::kMaxK; }
+
+size_t serial_table_smem(int h, int k) { return ser::table_smem_bytes(h, k); }
+
+int launch_serial_table(const TableArgs& a, cudaStream_t st) {
+    const size_t smem = ser::table_smem_bytes(a.h, a.k);
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(ser::table_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
+        return kLaunchFailed;
+    ser::table_kernel<<<(unsigned)a.n, ser::kTabThreads, smem, st>>>(a);
+    return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
+}
+
+int launch_serial_chain(int bs, int tm1, int k, const int64_t* idx, const int64_t* cand,
+                        int64_t* out, const float* conf, float* conf_out, cudaStream_t st) {
+    const int threads = 128;
+    ser::chain_kernel<<<(bs + threads - 1) / threads, threads, 0, st>>>(bs, tm1, k, idx, cand, out,
+                                                                      conf, conf_out);
+    return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
+}
+
+}  // namespace dsv

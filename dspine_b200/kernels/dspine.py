@@ -1,0 +1,166 @@
+"""Draft-side serial chains at the reference's ``sglang_dspine.kernels.dspine`` interface.
+
+`serial_sample_chain`, `serial_table` and `serial_chain` keep the reference's signatures,
+argument checks (ValueError before anything is launched) and caller-owned, in-place outputs
+(kernels/dspine.py:357-502, 677-772); each is one launch of the library's C ABI
+(dsv_serial_sample_chain, dsv_serial_table, dsv_serial_chain).  `build_serial_tables` is the
+offline table build (kernels/dspine.py:327-351): two plain bf16 library GEMMs per vocabulary
+chunk, run once per weight load, not per step.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from .. import _lib
+
+
+def _stream(t) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _cuda(*tensors):
+    for t in tensors:
+        if t is not None and t.device.type != "cuda":
+            raise ValueError("dspine_b200 runs the serial chains on CUDA tensors only")
+
+
+def build_serial_tables(lm_head_w, norm_w, write_w, pv_w, codebook, chunk: int = 8192):
+    """(TG [V, R] bf16, TSV [V, 2R] bf16) with TG[v] = bf16(LmHead[v] * norm_w) @ W_last and
+    TSV[v] = [G_p; A] @ bf16(sqrt(C) * Codebook[v]) (kernels/dspine.py:327-351)."""
+    (v, h) = lm_head_w.shape
+    r = write_w.shape[1]
+    c = codebook.shape[1]
+    if (codebook.shape[0] != v or tuple(write_w.shape) != (h, r) or tuple(pv_w.shape) != (2 * r, c)
+            or norm_w.shape != (h,)):
+        raise ValueError("build_serial_tables: shape contract violated")
+    tg = torch.empty((v, r), device=lm_head_w.device, dtype=torch.bfloat16)
+    tsv = torch.empty((v, 2 * r), device=lm_head_w.device, dtype=torch.bfloat16)
+    nwf, wb, scale = norm_w.float(), write_w.to(torch.bfloat16), float(c) ** 0.5
+    for s in range(0, v, chunk):
+        e = min(s + chunk, v)
+        tg[s:e] = torch.matmul((lm_head_w[s:e].float() * nwf).to(torch.bfloat16), wb)
+        tsv[s:e] = torch.nn.functional.linear((scale * codebook[s:e].float()).to(torch.bfloat16),
+                                              pv_w)
+    return (tg, tsv)
+
+
+def serial_table(raw, norm_w, cand, input_ids, lm_head_w, tg, tsv, packed, rms, gate_b,
+                 block_size: int, confidence=None, candidate_head=None):
+    """idx int64 [bs*(T-1), K]: idx[n, j] = the best candidate lane of row n when the previous
+    row chose lane j (kernels/dspine.py:357-471).  raw [bs*T, H] bf16, cand int64 [n, K],
+    input_ids [bs*T], packed [bs*T, >=R] bf16 (receiver query in columns :R), rms fp32 [bs*T];
+    optional confidence fp32 [n, K] output, optional candidate_head bf16 [n, K, H]."""
+    t = int(block_size)
+    (m, h) = raw.shape
+    (n, k) = cand.shape
+    rk = tg.shape[1]
+    if candidate_head is not None:
+        if (candidate_head.shape != (n, k, h) or candidate_head.dtype != torch.bfloat16
+                or not candidate_head.is_contiguous()):
+            raise ValueError("serial_table candidate head must be contiguous BF16 [N,K,H]")
+        lm_head_w = candidate_head.view(n * k, h)
+    if m % t or n != m // t * (t - 1) or input_ids.numel() != m or rms.numel() != m:
+        raise ValueError(f"serial_table row mismatch: raw {raw.shape}, cand {cand.shape}, T={t}")
+    if (raw.dtype != torch.bfloat16 or raw.stride(1) != 1 or packed.dtype != torch.bfloat16
+            or packed.stride(1) != 1):
+        raise ValueError("serial_table expects row-contiguous BF16 state and query")
+    if packed.shape[0] != m or packed.shape[1] < rk or rms.dtype != torch.float32 or not rms.is_contiguous():
+        raise ValueError("serial_table query/rms contract violated")
+    if (not cand.is_contiguous() or cand.dtype != torch.int64 or input_ids.dtype != torch.int64
+            or not input_ids.is_contiguous()):
+        raise ValueError("serial_table expects contiguous int64 candidates and input ids")
+    if lm_head_w.stride(1) != 1 or tuple(tsv.shape) != (tg.shape[0], 2 * rk) or not (
+            tg.is_contiguous() and tsv.is_contiguous()):
+        raise ValueError("serial_table table layout mismatch")
+    if h % 512 or rk % 128 or k & (k - 1) or not 2 <= k <= 64 or gate_b.numel() != rk or norm_w.numel() != h:
+        raise ValueError("serial_table size contract violated")
+    if (lm_head_w.dtype != torch.bfloat16 or tg.dtype != torch.bfloat16 or tsv.dtype != torch.bfloat16
+            or norm_w.dtype != torch.bfloat16 or gate_b.dtype != torch.bfloat16):
+        raise ValueError("serial_table expects BF16 weights, tables, norm and gate bias")
+    idx = torch.empty((n, k), dtype=torch.int64, device=raw.device)
+    if confidence is not None and (tuple(confidence.shape) != (n, k) or confidence.dtype != torch.float32
+                                   or not confidence.is_contiguous()):
+        raise ValueError("Confidence output must be contiguous float32 [N, K]")
+    _cuda(raw, norm_w, cand, input_ids, lm_head_w, tg, tsv, packed, rms, gate_b, confidence)
+    if n:
+        vocab = tg.shape[0]
+        if candidate_head is None and lm_head_w.shape[0] < vocab:
+            vocab = lm_head_w.shape[0]  # ids must address rows of every table
+        _lib.call("dsv_serial_table", m // t, t, h, rk, k, vocab, raw.data_ptr(), raw.stride(0),
+                  norm_w.contiguous().data_ptr(), cand.data_ptr(), input_ids.data_ptr(),
+                  lm_head_w.data_ptr(), lm_head_w.stride(0), int(candidate_head is not None),
+                  tg.data_ptr(), tsv.data_ptr(), packed.data_ptr(), packed.stride(0), rms.data_ptr(),
+                  gate_b.contiguous().data_ptr(), idx.data_ptr(), _lib.ptr(confidence), _stream(raw))
+    return idx
+
+
+def serial_chain(idx, cand, out, block_size: int, confidence=None, confidence_out=None):
+    """Walk every request's greedy table: out[:bs*(T-1)] written in place (int64)
+    (kernels/dspine.py:474-502)."""
+    t = int(block_size)
+    (n, k) = cand.shape
+    if n % (t - 1) or tuple(idx.shape) != (n, k) or not (idx.is_contiguous() and cand.is_contiguous()):
+        raise ValueError("serial_chain layout mismatch")
+    if out.dtype != torch.int64 or out.numel() < n or idx.dtype != torch.int64:
+        raise ValueError("serial_chain dtype/capacity contract violated")
+    if confidence is not None and (confidence_out is None or confidence_out.dtype != torch.float32
+                                   or confidence_out.numel() < n or tuple(confidence.shape) != (n, k)):
+        raise ValueError("Serial confidence needs a float32 [N, K] table and [N] output")
+    if not out.is_contiguous() or (confidence_out is not None and not confidence_out.is_contiguous()):
+        raise ValueError("serial_chain outputs must be contiguous")
+    if confidence is not None and (confidence.dtype != torch.float32 or not confidence.is_contiguous()):
+        raise ValueError("Serial confidence needs a float32 [N, K] table and [N] output")
+    _cuda(idx, cand, out, confidence, confidence_out)
+    if n:
+        conf_out = confidence_out if confidence is not None else None
+        _lib.call("dsv_serial_chain", n // (t - 1), t, k, idx.data_ptr(), cand.data_ptr(),
+                  out.data_ptr(), _lib.ptr(confidence), _lib.ptr(conf_out), _stream(idx))
+    return out
+
+
+def serial_sample_chain(table, inv_temp, top_k, top_p, min_p, greedy, u, cand, greedy_tok, out_tok,
+                        out_q, block_size: int, *, confidence_out=None):
+    """Sample every request's chain; fills out_tok[:n] / out_q[:n] in place
+    (kernels/dspine.py:677-772).  table fp32 [n, K, K]; inv_temp fp32 [>=bs]; top_k int32
+    [>=bs] (>= 1; >= K disables it); top_p fp32 [>=bs] in (0, 1]; min_p fp32 [>=bs] in [0, 1];
+    greedy int32 [>=bs]; u fp32 [>=n] in [0, 1); cand int64 [n, K]; greedy_tok int64 [>=n];
+    out_tok int64 [>=n]; out_q fp32 [>=n, K].  Optional confidence_out fp32 [>=n]: the maximum
+    temperature-softmax probability of each sampled row before filtering (greedy rows keep
+    their values)."""
+    t = int(block_size)
+    (n, k) = cand.shape
+    if n % (t - 1) or tuple(table.shape) != (n, k, k) or not table.is_contiguous():
+        raise ValueError("serial_sample_chain table layout mismatch")
+    bs = n // (t - 1)
+    staged = (inv_temp, top_k, top_p, min_p, greedy)
+    if any(x.numel() < bs for x in staged) or u.numel() < n or greedy_tok.numel() < n:
+        raise ValueError("serial_sample_chain staging buffers too small")
+    if out_tok.numel() < n or out_q.shape[0] < n or out_q.shape[1] != k:
+        raise ValueError("serial_sample_chain output buffers too small")
+    if not (cand.is_contiguous() and out_q.is_contiguous()):
+        raise ValueError("serial_sample_chain expects contiguous candidates and q")
+    if confidence_out is not None and (confidence_out.dtype != torch.float32
+                                       or confidence_out.numel() < n
+                                       or not confidence_out.is_contiguous()
+                                       or confidence_out.device != table.device):
+        raise ValueError(
+            "serial_sample_chain confidence needs contiguous float32 storage on the table device")
+    dtypes = (table.dtype, inv_temp.dtype, top_k.dtype, top_p.dtype, min_p.dtype, greedy.dtype,
+              u.dtype, cand.dtype, greedy_tok.dtype, out_tok.dtype, out_q.dtype)
+    expected = (torch.float32, torch.float32, torch.int32, torch.float32, torch.float32,
+                torch.int32, torch.float32, torch.int64, torch.int64, torch.int64, torch.float32)
+    if dtypes != expected:
+        raise ValueError(f"serial_sample_chain dtype contract violated: {dtypes}")
+    if k > 64:
+        raise ValueError("serial_sample_chain supports at most 64 candidates per row")
+    for x in (inv_temp, top_k, top_p, min_p, greedy, u, greedy_tok, out_tok):
+        if not x.is_contiguous():
+            raise ValueError("serial_sample_chain expects contiguous staging and output vectors")
+    _cuda(table, *staged, u, cand, greedy_tok, out_tok, out_q, confidence_out)
+    if bs:
+        _lib.call("dsv_serial_sample_chain", bs, t, k, table.data_ptr(), inv_temp.data_ptr(),
+                  top_k.data_ptr(), top_p.data_ptr(), min_p.data_ptr(), greedy.data_ptr(),
+                  u.data_ptr(), cand.data_ptr(), greedy_tok.data_ptr(), out_tok.data_ptr(),
+                  out_q.data_ptr(), _lib.ptr(confidence_out), _stream(table))
+    return (out_tok, out_q)

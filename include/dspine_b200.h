@@ -227,6 +227,55 @@ int dsv_accept_compact(int32_t batch, const int32_t* commit, const int32_t* veri
                        const int64_t* output, const dsv_compact_out* compact, void* workspace,
                        dsv_stream_t stream);
 
+/* ---- draft-side serial chains ------------------------------------------------------------------
+ * The kernels that produce a block's draft tokens, q rows and confidences from the serial
+ * last-write refinement (T = block_size, n = batch * (T - 1) drafted rows, K candidates each).
+ *
+ * dsv_serial_sample_chain replaces kernels/dspine.py:616-772 (_serial_sample_chain /
+ * serial_sample_chain): per request, row by row, p = softmax(table[n, sender] * inv_temp[b]),
+ * joint filter rank < top_k[b] (ties to the lower lane), mass ranked ahead <= top_p[b],
+ * p >= min_p[b] * max p, q = kept p renormalised, draw = first lane whose running sum of q
+ * exceeds u[n] * total (capped at the last kept lane); the drawn lane is the next row's sender.
+ * Writes out_tok[n] (cand[n, draw], or greedy_tok[n] when greedy[b]) and out_q[n, :] (q, or
+ * the one-hot of cand == greedy_tok for greedy requests).  confidence_out (optional, [n]):
+ * max p of each sampled row before filtering; rows of greedy requests are left untouched.
+ * table fp32 [n, K, K]; inv_temp, top_p, min_p fp32 [batch]; top_k, greedy int32 [batch];
+ * u fp32 [n]; candidates, greedy_tok int64 [n, K] / [n]; 1 <= K <= 64. */
+int dsv_serial_sample_chain(int32_t batch, int32_t block_size, int32_t k, const float* table,
+                            const float* inv_temp, const int32_t* top_k, const float* top_p,
+                            const float* min_p, const int32_t* greedy, const float* u,
+                            const int64_t* candidates, const int64_t* greedy_tok,
+                            int64_t* out_tok, float* out_q, float* confidence_out,
+                            dsv_stream_t stream);
+
+/* dsv_serial_table replaces kernels/dspine.py:210-287 _serial_table (serial_table :357-471):
+ * for drafted row n (request b, block row r, state row b*T + 1 + r), candidate lanes c with
+ * ids cand[n, c] and sender lanes j (the anchor input_ids[b*T] on block row 0, else
+ * cand[n-1, j]):
+ *   s[j, c] = W[c] . (raw[row] * norm_w) + rms[row] * sum_r sigmoid(query[row, r] + TSV[s_j, r]
+ *             + gate_b[r]) * TSV[s_j, RK + r] * TG[id_c, r]
+ * (W[c] = lm_head[id_c], or candidate_head[n*K + c] when head_candidates) and writes
+ * idx[n, j] = the first lane of max_c s[j, c]; confidence (optional, fp32 [n, K]) =
+ * 1 / sum_c exp((s[j, c] - max) / max(rms, 1e-6)).  bf16 raw [batch*T, hidden] (row pitch
+ * raw_stride), norm_w [hidden], lm_head (row pitch lm_stride, a multiple of 8, 16-byte aligned),
+ * tg [vocab, rk], tsv [vocab, 2 rk], query (pitch query_stride), gate_b [rk]; rms fp32 [batch*T].
+ * hidden a multiple of 512 up to 16384, rk a multiple of 128, K a power of two in [2, 64].
+ * A row whose candidate or sender id lies outside [0, vocab) writes idx -1 (confidence NaN). */
+int dsv_serial_table(int32_t batch, int32_t block_size, int32_t hidden, int32_t rk, int32_t k,
+                     int64_t vocab, const void* raw, int64_t raw_stride, const void* norm_w,
+                     const int64_t* candidates, const int64_t* input_ids, const void* lm_head,
+                     int64_t lm_stride, int32_t head_candidates, const void* tg, const void* tsv,
+                     const void* query, int64_t query_stride, const float* rms,
+                     const void* gate_b, int64_t* idx, float* confidence, dsv_stream_t stream);
+
+/* dsv_serial_chain replaces kernels/dspine.py:290-324 _serial_chain (serial_chain :474-502):
+ * per request, j = idx[first row, 0]; row r writes out[r] = cand[r, j] (and, with confidence,
+ * confidence_out[r] = confidence[r, previous j], previous starting at 0), then j = idx[r+1, j].
+ * A lane outside [0, K) selects the value 0.  confidence and confidence_out go together. */
+int dsv_serial_chain(int32_t batch, int32_t block_size, int32_t k, const int64_t* idx,
+                     const int64_t* candidates, int64_t* out, const float* confidence,
+                     float* confidence_out, dsv_stream_t stream);
+
 /* ---- the same verification without a caller workspace ------------------------------------
  * No counterpart in the reference: for callers that cannot allocate device memory (or hand out
  * scratch) at verification time.  Same arguments, outputs and results as dsv_verify_logits,

@@ -19,6 +19,9 @@ Fixture groups (reference function -> file):
   sps       verification/sps.py:35-58 allocate_verify_lens                 sps.npz
   merge     sampling/tp_head.py:9-14 merge_topk                            merge.npz
   greedy    verification/caps.py:32-59 _accept_capped, ragged.py:51-76     greedy.npz
+  serial    kernels/dspine.py:210-351,616-772 serial_table / serial_chain /
+            build_serial_tables / serial_sample_chain, and tests/ref_utils.py:12-76
+            ref_sample_chain / ref_refine_table                             serial.npz
 """
 
 import os
@@ -337,6 +340,147 @@ def gen_greedy(torch):
     return out
 
 
+def _serial_refine_inputs(torch, g, bs, T, H, R, C, V, k):
+    import math
+    bf = torch.bfloat16
+    m, n = bs * T, bs * (T - 1)
+    d = dict(
+        raw=torch.randn(m, H, generator=g).to(bf),
+        rms=(torch.rand(m, generator=g) + 0.5).float(),
+        packed=torch.randn(m, 3 * R, generator=g).to(bf),
+        codebook=(torch.randn(V, C, generator=g) / math.sqrt(C)).to(bf),
+        pg=(torch.randn(R, C, generator=g) / math.sqrt(C)).to(bf),
+        pv=(torch.randn(R, C, generator=g) / math.sqrt(C)).to(bf),
+        gb=(torch.randn(R, generator=g) * 0.1).to(bf),
+        w_last=(torch.randn(H, R, generator=g) / math.sqrt(R)).to(bf),
+        norm_w=(1.0 + 0.1 * torch.randn(H, generator=g)).to(bf),
+        lm=(torch.randn(V, H, generator=g) / math.sqrt(H)).to(bf),
+    )
+    d["cand"] = torch.stack([torch.randperm(V, generator=g)[:k].sort().values
+                             for _ in range(n)]).contiguous()
+    d["input_ids"] = torch.randint(0, V, (m,), generator=g)
+    d["anchors"] = d["input_ids"].view(bs, T)[:, 0].contiguous()
+    return d
+
+
+def gen_serial(torch, ref_dir):
+    """Sampled chain: the reference kernel (under the interpreter) and ref_sample_chain on the
+    same inputs.  Greedy table: build_serial_tables -> serial_table -> serial_chain (with
+    confidences), plus the fp64 refinement table ref_refine_table the chain approximates."""
+    sys.path.insert(0, str(Path(ref_dir) / "tests"))
+    from ref_utils import ref_refine_table, ref_sample_chain
+    from sglang_dspine.kernels import dspine as K
+
+    out = {}
+    g = torch.Generator().manual_seed(31)
+    ci = 0
+    chain_cases = [
+        # (T, k, per-request (temperature, top_k, top_p, min_p, greedy), table scale)
+        (5, 8, [(1.0, 8, 1.0, 0.0, 0), (0.7, 3, 0.8, 0.1, 0), (1.5, 8, 0.5, 0.0, 0),
+                (1.0, 8, 1.0, 0.3, 0), (0.3, 1, 1.0, 0.0, 0), (1.0, 1, 1.0, 0.0, 1)], 3.0),
+        (16, 16, [(1.0, 16, 1.0, 0.0, 0), (0.6, 4, 0.9, 0.05, 0), (1.3, 16, 0.7, 0.0, 0),
+                  (1.0, 2, 1.0, 0.0, 0), (0.8, 16, 0.95, 0.1, 0), (1.0, 1, 1.0, 0.0, 0),
+                  (2.0, 8, 0.5, 0.2, 0), (1.0, 1, 1.0, 0.0, 1)], 3.0),
+        (4, 32, [(1.0, 32, 1.0, 0.0, 0), (0.9, 10, 0.85, 0.02, 0), (1.0, 32, 0.6, 0.0, 1)], 2.0),
+        (3, 64, [(1.0, 64, 1.0, 0.0, 0), (0.7, 40, 0.9, 0.0, 0), (1.0, 5, 1.0, 0.0, 1)], 2.0),
+        (3, 4, [(1.0, 4, 1.0, 0.0, 0), (0.5, 2, 0.7, 0.05, 0), (1.0, 5, 0.65, 0.2, 0)], 2.0),
+    ]
+    for (T, k, params, scale) in chain_cases:
+        bs = len(params)
+        n = bs * (T - 1)
+        table = (torch.randn(n, k, k, generator=g) * scale).contiguous()
+        cand = torch.stack([torch.randperm(151936, generator=g)[:k].sort().values
+                            for _ in range(n)]).contiguous()
+        gtok = cand[torch.arange(n), torch.randint(0, k, (n,), generator=g)].contiguous()
+        u = torch.rand(n, generator=g)
+        staged = (torch.tensor([1.0 / p[0] for p in params], dtype=torch.float32),
+                  torch.tensor([p[1] for p in params], dtype=torch.int32),
+                  torch.tensor([p[2] for p in params], dtype=torch.float32),
+                  torch.tensor([p[3] for p in params], dtype=torch.float32),
+                  torch.tensor([p[4] for p in params], dtype=torch.int32))
+        tok = torch.full((n,), -1, dtype=torch.int64)
+        q = torch.full((n, k), -1.0)
+        conf = torch.full((n,), -0.25)
+        K.serial_sample_chain(table, *staged, u, cand, gtok, tok, q, T, confidence_out=conf)
+        rtok, rq = ref_sample_chain(table, *staged, u, cand, gtok, T)
+        for name, val in (("table", table), ("inv_t", staged[0]), ("top_k", staged[1]),
+                          ("top_p", staged[2]), ("min_p", staged[3]), ("greedy", staged[4]),
+                          ("u", u), ("cand", cand), ("gtok", gtok), ("tok", tok), ("q", q),
+                          ("conf", conf), ("ref_tok", rtok), ("ref_q", rq)):
+            out[f"c{ci}_{name}"] = _np(val)
+        out[f"c{ci}_T"] = np.array(T)
+        ci += 1
+    # exact tie between lanes 2 and 6 with top_k = 1: the lower lane wins
+    T, k = 3, 8
+    n = T - 1
+    table = torch.zeros(n, k, k)
+    table[:, :, 2] = 5.0
+    table[:, :, 6] = 5.0
+    cand = torch.arange(k, dtype=torch.int64).repeat(n, 1) + 100
+    gtok = cand[:, 0].clone()
+    staged = (torch.ones(1), torch.tensor([1], dtype=torch.int32), torch.ones(1), torch.zeros(1),
+              torch.zeros(1, dtype=torch.int32))
+    tok = torch.full((n,), -1, dtype=torch.int64)
+    q = torch.full((n, k), -1.0)
+    conf = torch.full((n,), -0.25)
+    u = torch.zeros(n)
+    K.serial_sample_chain(table, *staged, u, cand, gtok, tok, q, T, confidence_out=conf)
+    rtok, rq = ref_sample_chain(table, *staged, u, cand, gtok, T)
+    for name, val in (("table", table), ("inv_t", staged[0]), ("top_k", staged[1]),
+                      ("top_p", staged[2]), ("min_p", staged[3]), ("greedy", staged[4]),
+                      ("u", u), ("cand", cand), ("gtok", gtok), ("tok", tok), ("q", q),
+                      ("conf", conf), ("ref_tok", rtok), ("ref_q", rq)):
+        out[f"c{ci}_{name}"] = _np(val)
+    out[f"c{ci}_T"] = np.array(T)
+    ci += 1
+    out["n_chain"] = np.array(ci)
+
+    ti = 0
+    for (bs, T, H, R, C, V, k, head) in ((2, 4, 512, 128, 64, 1024, 8, False),
+                                         (2, 5, 1024, 256, 128, 2048, 16, False),
+                                         (3, 3, 512, 128, 64, 512, 2, False),
+                                         (1, 3, 512, 128, 64, 1024, 64, False),
+                                         (2, 4, 512, 128, 64, 1024, 8, True)):
+        d = _serial_refine_inputs(torch, g, bs, T, H, R, C, V, k)
+        n = bs * (T - 1)
+        tg, tsv = K.build_serial_tables(d["lm"], d["norm_w"], d["w_last"],
+                                        torch.cat((d["pg"], d["pv"]), 0), d["codebook"])
+        chead = d["lm"][d["cand"]].contiguous() if head else None
+        conf = torch.empty(n, k)
+        idx = K.serial_table(d["raw"], d["norm_w"], d["cand"], d["input_ids"], d["lm"], tg, tsv,
+                             d["packed"], d["rms"], d["gb"], T, confidence=conf,
+                             candidate_head=chead)
+        chain = torch.full((n,), -1, dtype=torch.int64)
+        cconf = torch.full((n,), -1.0)
+        K.serial_chain(idx, d["cand"], chain, T, confidence=conf, confidence_out=cconf)
+        ref = ref_refine_table(d["raw"], d["rms"], d["packed"][:, :R], d["anchors"], d["cand"],
+                               d["codebook"], d["pg"], d["pv"], d["gb"], d["w_last"], d["norm_w"],
+                               d["lm"], 1e-6, T)
+        # only the table rows the kernels read (candidate and sender ids) are stored; every
+        # other row of lm / tg / tsv may hold anything without changing a result
+        used = torch.unique(torch.cat((d["cand"].flatten(), d["anchors"])))
+
+        def bits(t):
+            return _np(t.contiguous().view(torch.int16))
+
+        out[f"t{ti}_dims"] = np.array([bs, T, H, R, C, V, k, int(head)])
+        out[f"t{ti}_used"] = _np(used)
+        for name in ("raw", "norm_w", "gb"):
+            out[f"t{ti}_{name}"] = bits(d[name])
+        out[f"t{ti}_query"] = bits(d["packed"][:, :R])
+        out[f"t{ti}_lm"] = bits(d["lm"][used])
+        out[f"t{ti}_tg"] = bits(tg[used])
+        out[f"t{ti}_tsv"] = bits(tsv[used])
+        for name in ("rms", "cand", "input_ids"):
+            out[f"t{ti}_{name}"] = _np(d[name])
+        for name, val in (("idx", idx), ("conf", conf), ("chain", chain), ("chain_conf", cconf),
+                          ("ref_table", ref)):
+            out[f"t{ti}_{name}"] = _np(val)
+        ti += 1
+    out["n_table"] = np.array(ti)
+    return out
+
+
 def main(ref_dir):
     os.environ.setdefault("TRITON_INTERPRET", "1")
     os.environ.setdefault("PYTHONDONTWRITEBYTECODE", "1")
@@ -355,6 +499,7 @@ def main(ref_dir):
         "sps": lambda: gen_sps(torch),
         "merge": lambda: gen_merge(torch),
         "greedy": lambda: gen_greedy(torch),
+        "serial": lambda: gen_serial(torch, ref_dir),
     }
     only = set(sys.argv[2:])
     for name, fn in groups.items():

@@ -191,3 +191,45 @@ def test_accept_compact_layout():
     assert sl.tolist() == [1000, 1016, 1017, 1018, 1032, 1033]
     assert foff.tolist() == [0, 3, 3, 17]
     assert fr.tolist() == [1001, 1002, 1003] + list(range(1034, 1048))
+
+
+# ---- draft-side serial chains (kernels/dspine.py:210-324, 616-772) -----------------------------
+
+def test_sample_chain_oracle_matches_reference_kernel():
+    """Tokens exact, q and confidence within fp32 rounding of the reference kernel (run under
+    the Triton interpreter); the reference's own test oracle agrees on the same inputs."""
+    import oracle.serial as OS
+    from tests.helpers import serial_chain_case
+
+    d = load("serial")
+    for ci in range(int(d["n_chain"])):
+        inp, ref = serial_chain_case(d, ci)
+        tok, q, conf = OS.sample_chain(**inp)
+        np.testing.assert_array_equal(tok, ref["tok"], err_msg=f"case {ci}")
+        np.testing.assert_array_equal(tok, ref["ref_tok"], err_msg=f"case {ci}")
+        np.testing.assert_allclose(q, ref["q"], rtol=1e-5, atol=1e-6, err_msg=f"case {ci}")
+        np.testing.assert_allclose(q, ref["ref_q"], rtol=1e-5, atol=1e-6, err_msg=f"case {ci}")
+        sampled = ~np.isnan(conf)
+        np.testing.assert_allclose(conf[sampled], ref["conf"][sampled], rtol=1e-5, atol=1e-6)
+        assert (ref["conf"][~sampled] == np.float32(-0.25)).all()  # greedy rows untouched
+
+
+def test_serial_table_oracle_pins_reference_kernel():
+    """The reference kernel's best lane is an argmax of the fp64 scores within the fp32
+    accumulation error, and its confidence matches; the greedy walk of its table is the
+    reference walk bit for bit."""
+    import oracle.serial as OS
+    from tests.helpers import serial_scores, serial_table_case
+
+    d = load("serial")
+    for ti in range(int(d["n_table"])):
+        case, ref = serial_table_case(d, ti)
+        s, bound = serial_scores(case)
+        tol = 2e-5 * bound.max(axis=2)
+        picked = np.take_along_axis(s, ref["idx"][..., None], axis=2)[..., 0]
+        assert (picked >= s.max(axis=2) - tol).all(), f"table case {ti}"
+        idx, conf = OS.table_idx_conf(s, case["rms"], case["T"])
+        np.testing.assert_allclose(conf, ref["conf"], rtol=2e-4, atol=1e-6, err_msg=f"case {ti}")
+        out, cout = OS.chain(ref["idx"], case["cand"], case["T"], ref["conf"])
+        np.testing.assert_array_equal(out, ref["chain"])
+        np.testing.assert_array_equal(cout, ref["chain_conf"])
