@@ -496,6 +496,7 @@ int dsv_serial_chain(int32_t batch, int32_t block_size, int32_t k, const int64_t
                      const int64_t* candidates, int64_t* out, const float* confidence,
                      float* confidence_out, dsv_stream_t stream) {
     if (batch < 0 || block_size < 2 || k < 1) return DSV_BAD_SHAPE;
+    if (dsv::serial_chain_smem(block_size - 1, k) > 200 * 1024) return DSV_UNSUPPORTED;
     if ((confidence == nullptr) != (confidence_out == nullptr)) return DSV_BAD_POINTER;
     if (batch == 0) return DSV_OK;
     if (!idx || !candidates || !out) return DSV_BAD_POINTER;

@@ -59,12 +59,18 @@ constexpr inline size_t verify_racc_offset(int B) {
 constexpr inline size_t verify_wmass_offset(int B) {
     return verify_racc_offset(B) + (((size_t)B * 8 + 63) & ~(size_t)63);
 }
-// [2 KB]: phase timers of profiling builds (-DDSV_PROFILE); unused otherwise
+// [2 KB]: phase timers of profiling builds (-DDSV_PROFILE); unused otherwise.  Profiling
+// builds add a 96 KB task trace after them.
+#ifdef DSV_PROFILE
+constexpr size_t kProfBytes = 2048 + 96 * 1024;
+#else
+constexpr size_t kProfBytes = 2048;
+#endif
 constexpr inline size_t verify_prof_offset(int B) {
     return verify_wmass_offset(B) + (size_t)B * 32 * 8 * 8;
 }
 constexpr inline size_t verify_workspace_bytes(int B) {
-    return verify_prof_offset(B) + 2048;
+    return verify_prof_offset(B) + kProfBytes;
 }
 
 struct VerifyArgs {
@@ -246,6 +252,7 @@ struct TableArgs {
 };
 int serial_max_k();
 size_t serial_table_smem(int h, int k);
+size_t serial_chain_smem(int tm1, int k);
 int launch_sample_chain(const SampleChainArgs& a, cudaStream_t stream);
 int launch_serial_table(const TableArgs& a, cudaStream_t stream);
 int launch_serial_chain(int bs, int tm1, int k, const int64_t* idx, const int64_t* cand,

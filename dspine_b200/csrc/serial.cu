@@ -43,26 +43,59 @@ __device__ __forceinline__ float warp_sum(float v) {
 // ---- sampled chain -----------------------------------------------------------------------
 //
 // One warp per request; lane l holds candidates l and l + 32.  Per drafted row n:
-//   p      = softmax(table[n, sender, :] * inv_temp)            (max-shifted expf, IEEE /)
-//   rank_c = #{d : p_d > p_c or (p_d == p_c and d < c)}         (ties to the lower lane)
-//   before = sum of p over the lanes ranked ahead, added in rank order
+//   p      = softmax(table[n, sender, :] * inv_temp)      (max-shifted expf, butterfly sum, IEEE /)
+//   rank_c = #{d : p_d > p_c or (p_d == p_c and d < c)}   (ties to the lower lane)
+//   before = exclusive prefix sum of p in rank order       (warp scan, see below)
 //   keep   = rank < top_k and before <= top_p and p >= min_p * max p
-//   q      = keep ? p / sum(kept p) : 0;  cdf = running sum of q in lane order
+//   q      = keep ? p / sum(kept p) : 0                    (butterfly sum)
+//   cdf    = inclusive prefix sum of q in lane order        (warp scan)
 //   choice = min(#{c : cdf_c <= u * cdf_{K-1}}, last kept lane)
 // The token is cand[n, choice] (greedy requests: greedy_tok[n] with a one-hot q on the
 // matching candidates); the next row's sender lane is choice in both cases.
+// Summation orders (fixed, so results do not depend on timing): butterfly sums add lane
+// l + 32 to lane l, then xor-shuffles 16, 8, 4, 2, 1; prefix sums are Kogge-Stone scans
+// (shifts 1, 2, 4, 8, 16) over positions 0..31 and 32..63, the second half plus the total
+// of the first.  The K x K block of the next row is copied to shared memory (cp.async)
+// while the current row is processed, so no row waits on a dependent global load.
+
+__device__ __forceinline__ float warp_scan(float x, int lane) {
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+        const float y = __shfl_up_sync(0xffffffffu, x, o);
+        if (lane >= o) x = x + y;
+    }
+    return x;
+}
+
+__device__ __forceinline__ void cp_async4(void* dst, const void* src) {
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"(smem_u32(dst)), "l"(src)
+                 : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+__device__ __forceinline__ void cp_async_wait_all() { asm volatile("cp.async.wait_all;" ::: "memory"); }
+
+size_t chain_smem_bytes(int k) { return (size_t)kChainWarps * 2 * k * k * sizeof(float); }
+
 __global__ void __launch_bounds__(kChainWarps * 32)
     sample_chain_kernel(SampleChainArgs a) {
-    __shared__ float s_p[kChainWarps][kMaxK];
-    __shared__ float s_q[kChainWarps][kMaxK];
-    __shared__ int s_ord[kChainWarps][kMaxK];
+    extern __shared__ __align__(16) float s_tab[];   // [warp][2][K * K] table blocks
+    __shared__ float s_p[kChainWarps][kMaxK];        // p by lane
+    __shared__ float s_r[kChainWarps][kMaxK];        // p by rank, then its prefix sums
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int b = blockIdx.x * kChainWarps + warp;
     if (b >= a.bs) return;
-    const int K = a.k;
+    const int K = a.k, KK = K * K;
+    float* tb = s_tab + (size_t)warp * 2 * KK;
     float* P = s_p[warp];
-    float* Q = s_q[warp];
-    int* ord = s_ord[warp];
+    float* R = s_r[warp];
+    const int64_t n0 = (int64_t)b * a.tm1;
+    auto prefetch = [&](int row) {
+        const float* src = a.table + (n0 + row) * KK;
+        float* dst = tb + (row & 1) * KK;
+        for (int i = lane; i < KK; i += 32) cp_async4(dst + i, src + i);
+        cp_async_commit();
+    };
+    prefetch(0);
     const float inv_t = a.inv_temp[b];
     const int top_k = a.top_k[b];
     const float top_p = a.top_p[b], min_p = a.min_p[b];
@@ -70,8 +103,16 @@ __global__ void __launch_bounds__(kChainWarps * 32)
     const bool v0 = lane < K, v1 = lane + 32 < K;
     int sender = 0;
     for (int row = 0; row < a.tm1; ++row) {
-        const int64_t n = (int64_t)b * a.tm1 + row;
-        const float* tab = a.table + (n * K + sender) * K;
+        const int64_t n = n0 + row;
+        // loads that do not depend on the previous draw go first
+        const float un = a.u[n];
+        const int64_t gtok = a.greedy_tok[n];
+        const int64_t* cand = a.cand + n * K;
+        const int64_t cd0 = v0 ? cand[lane] : 0, cd1 = v1 ? cand[lane + 32] : 0;
+        cp_async_wait_all();
+        __syncwarp();  // this row's block is visible; every lane is done with the other buffer
+        if (row + 1 < a.tm1) prefetch(row + 1);
+        const float* tab = tb + (row & 1) * KK + sender * K;
         const float s0 = v0 ? tab[lane] * inv_t : -INFINITY;
         const float s1 = v1 ? tab[lane + 32] * inv_t : -INFINITY;
         const float mx = warp_max(fmaxf(s0, s1));
@@ -81,8 +122,8 @@ __global__ void __launch_bounds__(kChainWarps * 32)
         const float p0 = m0 / total, p1 = m1 / total;
         const float pmax = warp_max(fmaxf(v0 ? p0 : -INFINITY, v1 ? p1 : -INFINITY));
         if (a.confidence && !greedy && lane == 0) a.confidence[n] = pmax;
-        if (v0) P[lane] = p0;
-        if (v1) P[lane + 32] = p1;
+        P[lane] = v0 ? p0 : 0.0f;
+        P[lane + 32] = v1 ? p1 : 0.0f;
         __syncwarp();
         int r0 = 0, r1 = 0;
         for (int d = 0; d < K; ++d) {
@@ -90,38 +131,31 @@ __global__ void __launch_bounds__(kChainWarps * 32)
             r0 += (pd > p0) || (pd == p0 && d < lane);
             r1 += (pd > p1) || (pd == p1 && d < lane + 32);
         }
-        if (v0) ord[r0] = lane;
-        if (v1) ord[r1] = lane + 32;
+        // positions K..63 hold zeros; a lane's rank is < K (it never counts itself)
+        R[lane] = 0.0f;
+        R[lane + 32] = 0.0f;
         __syncwarp();
-        float b0 = 0.0f, b1 = 0.0f;  // mass ranked ahead, added in rank order
-        for (int r = 0; r < (v0 ? r0 : 0); ++r) b0 += P[ord[r] & (kMaxK - 1)];
-        for (int r = 0; r < (v1 ? r1 : 0); ++r) b1 += P[ord[r] & (kMaxK - 1)];
+        if (v0) R[r0 & (kMaxK - 1)] = p0;
+        if (v1) R[r1 & (kMaxK - 1)] = p1;
+        __syncwarp();
+        const float x0 = warp_scan(R[lane], lane);
+        const float x1 = warp_scan(R[lane + 32], lane) + __shfl_sync(0xffffffffu, x0, 31);
+        __syncwarp();
+        R[lane] = x0;
+        R[lane + 32] = x1;
+        __syncwarp();
+        const float b0 = r0 > 0 ? R[(r0 - 1) & (kMaxK - 1)] : 0.0f;  // mass ranked ahead
+        const float b1 = r1 > 0 ? R[(r1 - 1) & (kMaxK - 1)] : 0.0f;
         const float floor_p = min_p * pmax;
         const bool k0 = v0 && r0 < top_k && b0 <= top_p && p0 >= floor_p;
         const bool k1 = v1 && r1 < top_k && b1 <= top_p && p1 >= floor_p;
         const float w0 = k0 ? p0 : 0.0f, w1 = k1 ? p1 : 0.0f;
-        float wsum = 0.0f;  // kept mass in lane order
-        {
-            if (v0) Q[lane] = w0;
-            if (v1) Q[lane + 32] = w1;
-            __syncwarp();
-            for (int d = 0; d < K; ++d) wsum += Q[d];
-            __syncwarp();
-        }
+        const float wsum = warp_sum(w0 + w1);
         const float q0 = w0 / wsum, q1 = w1 / wsum;
-        if (v0) Q[lane] = q0;
-        if (v1) Q[lane + 32] = q1;
-        __syncwarp();
-        float c0 = 0.0f, c1 = 0.0f;  // running sums in lane order
-        for (int d = 0; d <= lane && d < K; ++d) c0 += Q[d];
-        if (v1) {
-            c1 = c0;
-            for (int d = lane + 1; d <= lane + 32; ++d) c1 += Q[d];
-        }
-        // cdf of the last lane (the total the draw is scaled by)
-        const int last_lane = (K - 1) & 31;
-        const float ctot = __shfl_sync(0xffffffffu, K > 32 ? c1 : c0, last_lane);
-        const float thr = a.u[n] * ctot;
+        const float c0 = warp_scan(v0 ? q0 : 0.0f, lane);
+        const float c1 = warp_scan(v1 ? q1 : 0.0f, lane) + __shfl_sync(0xffffffffu, c0, 31);
+        const float ctot = __shfl_sync(0xffffffffu, K > 32 ? c1 : c0, (K - 1) & 31);
+        const float thr = un * ctot;
         const unsigned under0 = __ballot_sync(0xffffffffu, v0 && c0 <= thr);
         const unsigned under1 = __ballot_sync(0xffffffffu, v1 && c1 <= thr);
         int choice = __popc(under0) + __popc(under1);
@@ -129,15 +163,14 @@ __global__ void __launch_bounds__(kChainWarps * 32)
         const unsigned kb1 = __ballot_sync(0xffffffffu, k1);
         const int last = kb1 ? 32 + 31 - __clz(kb1) : (kb0 ? 31 - __clz(kb0) : 0);
         choice = min(choice, last);
-        const int64_t* cand = a.cand + n * K;
-        const int64_t gtok = a.greedy_tok[n];
+        const int64_t picked = __shfl_sync(0xffffffffu, choice < 32 ? cd0 : cd1, choice & 31);
         float* qo = a.out_q + n * K;
-        if (v0) qo[lane] = greedy ? (cand[lane] == gtok ? 1.0f : 0.0f) : q0;
-        if (v1) qo[lane + 32] = greedy ? (cand[lane + 32] == gtok ? 1.0f : 0.0f) : q1;
-        if (lane == 0) a.out_tok[n] = greedy ? gtok : cand[choice];
+        if (v0) qo[lane] = greedy ? (cd0 == gtok ? 1.0f : 0.0f) : q0;
+        if (v1) qo[lane + 32] = greedy ? (cd1 == gtok ? 1.0f : 0.0f) : q1;
+        if (lane == 0) a.out_tok[n] = greedy ? gtok : picked;
         sender = choice;
-        __syncwarp();
     }
+    cp_async_wait_all();
 }
 
 // ---- greedy refinement table ---------------------------------------------------------------
@@ -280,23 +313,47 @@ __global__ void __launch_bounds__(kTabThreads)
 }
 
 // ---- greedy chain ---------------------------------------------------------------------------
-// One thread per request: j = idx[first row, lane 0], then per row the candidate at lane j and
-// the next row's lane idx[next row, j].  A lane outside [0, K) selects nothing (value 0), as
-// the reference's masked selection does.
-__global__ void chain_kernel(int bs, int tm1, int K, const int64_t* __restrict__ idx,
-                             const int64_t* __restrict__ cand, int64_t* out,
-                             const float* __restrict__ conf, float* conf_out) {
-    const int b = blockIdx.x * blockDim.x + threadIdx.x;
+// One warp per request: the request's (T-1) x K lane table is copied to shared memory, lane 0
+// walks it (j = idx[first row, lane 0], then idx[next row, j]), and the lanes gather the
+// candidates (and confidences) of the walked lanes in parallel.  A lane outside [0, K)
+// selects nothing (value 0), as the reference's masked selection does.
+constexpr int kWalkWarps = 4;
+
+size_t walk_smem_bytes(int tm1, int k) {
+    return (size_t)kWalkWarps * ((size_t)tm1 * k * sizeof(int64_t) + (size_t)tm1 * 2 * sizeof(int32_t));
+}
+
+__global__ void __launch_bounds__(kWalkWarps * 32)
+    chain_kernel(int bs, int tm1, int K, const int64_t* __restrict__ idx,
+                 const int64_t* __restrict__ cand, int64_t* out,
+                 const float* __restrict__ conf, float* conf_out) {
+    extern __shared__ __align__(16) unsigned char s_walk[];
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int b = blockIdx.x * kWalkWarps + warp;
     if (b >= bs) return;
+    const size_t per = (size_t)tm1 * K * sizeof(int64_t) + (size_t)tm1 * 2 * sizeof(int32_t);
+    int64_t* tab = reinterpret_cast<int64_t*>(s_walk + warp * per);
+    int32_t* js = reinterpret_cast<int32_t*>(tab + (size_t)tm1 * K);  // walked lane per row
+    int32_t* ps = js + tm1;                                           // previous lane per row
     const int64_t n0 = (int64_t)b * tm1;
-    int64_t j = idx[n0 * K];
-    int64_t prev = 0;
-    for (int r = 0; r < tm1; ++r) {
+    const int64_t* src = idx + n0 * K;
+    for (int i = lane; i < tm1 * K; i += 32) tab[i] = src[i];
+    __syncwarp();
+    if (lane == 0) {
+        int64_t j = tab[0], prev = 0;
+        for (int r = 0; r < tm1; ++r) {
+            const bool in = j >= 0 && j < K;
+            js[r] = in ? (int32_t)j : -1;
+            ps[r] = (prev >= 0 && prev < K) ? (int32_t)prev : -1;
+            prev = j;
+            j = (r + 1 < tm1 && in) ? tab[(size_t)(r + 1) * K + j] : 0;
+        }
+    }
+    __syncwarp();
+    for (int r = lane; r < tm1; r += 32) {
         const int64_t n = n0 + r;
-        if (conf) conf_out[n] = (prev >= 0 && prev < K) ? conf[n * K + prev] : 0.0f;
-        out[n] = (j >= 0 && j < K) ? cand[n * K + j] : 0;
-        prev = j;
-        j = (r + 1 < tm1 && j >= 0 && j < K) ? idx[(n + 1) * K + j] : 0;
+        out[n] = js[r] >= 0 ? cand[n * K + js[r]] : 0;
+        if (conf) conf_out[n] = ps[r] >= 0 ? conf[n * K + ps[r]] : 0.0f;
     }
 }
 
@@ -304,7 +361,12 @@ __global__ void chain_kernel(int bs, int tm1, int K, const int64_t* __restrict__
 
 int launch_sample_chain(const SampleChainArgs& a, cudaStream_t st) {
     const unsigned blocks = (unsigned)((a.bs + ser::kChainWarps - 1) / ser::kChainWarps);
-    ser::sample_chain_kernel<<<blocks, ser::kChainWarps * 32, 0, st>>>(a);
+    const size_t smem = ser::chain_smem_bytes(a.k);
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(ser::sample_chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
+        return kLaunchFailed;
+    ser::sample_chain_kernel<<<blocks, ser::kChainWarps * 32, smem, st>>>(a);
     return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
 }
 
@@ -322,11 +384,18 @@ int launch_serial_table(const TableArgs& a, cudaStream_t st) {
     return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
 }
 
+size_t serial_chain_smem(int tm1, int k) { return ser::walk_smem_bytes(tm1, k); }
+
 int launch_serial_chain(int bs, int tm1, int k, const int64_t* idx, const int64_t* cand,
                         int64_t* out, const float* conf, float* conf_out, cudaStream_t st) {
-    const int threads = 128;
-    ser::chain_kernel<<<(bs + threads - 1) / threads, threads, 0, st>>>(bs, tm1, k, idx, cand, out,
-                                                                      conf, conf_out);
+    const size_t smem = ser::walk_smem_bytes(tm1, k);
+    if (smem > 48 * 1024 &&
+        cudaFuncSetAttribute(ser::chain_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             (int)smem) != cudaSuccess)
+        return kLaunchFailed;
+    const unsigned blocks = (unsigned)((bs + ser::kWalkWarps - 1) / ser::kWalkWarps);
+    ser::chain_kernel<<<blocks, ser::kWalkWarps * 32, smem, st>>>(bs, tm1, k, idx, cand, out, conf,
+                                                                 conf_out);
     return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
 }
 

@@ -51,6 +51,14 @@ constexpr float kTwo23 = 8388608.0f;
 // counter [cat * 16 + phase], task count at phase 15; the chain kernel at [64 + phase]
 
 #ifdef DSV_PROFILE
+constexpr unsigned kTraceCap = 2600;   // task trace entries
+constexpr unsigned kTraceCtas = 800;   // per-CTA start / exit entries
+static_assert((260 + 3 * kTraceCap + 2 * kTraceCtas) * 8 <= kProfBytes, "trace fits the profiling area");
+__device__ __forceinline__ unsigned smid() {
+    unsigned r;
+    asm volatile("mov.u32 %0, %%smid;" : "=r"(r));
+    return r;
+}
 #define PROF_START() unsigned long long prof_t = globaltimer_ns()
 #define PROF_MARK(cat_, ph)                                                              \
     do {                                                                                 \
@@ -103,6 +111,19 @@ __device__ __forceinline__ uint32_t bf2_max(uint32_t a, uint32_t b) {
     __nv_bfloat162 r = __hmax2(*reinterpret_cast<const __nv_bfloat162*>(&a),
                                *reinterpret_cast<const __nv_bfloat162*>(&b));
     return *reinterpret_cast<uint32_t*>(&r);
+}
+
+// 0xFFFF in each 16-bit half of w whose sign bit is set, else 0 (prmt sign replication:
+// selector nibbles 0x9 / 0xB take bytes 1 / 3 with their top bit replicated)
+__device__ __forceinline__ uint32_t prmt_sign16(uint32_t w) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, 0, 0xBB99;" : "=r"(r) : "r"(w));
+    return r;
+}
+
+// one-count increment of the shared-memory u32 at byte address addr (no return value)
+__device__ __forceinline__ void red_shared_inc(uint32_t addr) {
+    asm volatile("red.shared.add.u32 [%0], 1;" ::"r"(addr) : "memory");
 }
 
 // y of one element, clamped at -64 (bulk passes; see file header)
@@ -210,6 +231,19 @@ __device__ int request_cat(const VerifyArgs& a, int b, float& c_out, int wink) {
     return kBinned;                           // pure top-k, large k: exact counts from the top
 }
 
+// The task table of a launch: per class g (binned, keep-all/window, greedy) the prefix sums
+// pre(g, b) of the rows of requests < b, and per request its class and cap.  It lives in
+// shared memory after the row kernel's fixed state, sized by the batch.
+struct Plan {
+    uint16_t* pre_;  // [3][B + 1]
+    uint8_t* req;    // [B]
+    int B;
+    __device__ __forceinline__ uint16_t& pre(int g, int b) const { return pre_[g * (B + 1) + b]; }
+};
+__host__ __device__ constexpr size_t plan_bytes(int B) {
+    return ((size_t)3 * (B + 1) * 2 + (size_t)B + 15) & ~(size_t)15;
+}
+
 // every CTA builds the same task table: binned rows first, then keep-all/window, then greedy
 template <typename Sm>
 __device__ void build_plan(const VerifyArgs& a, Sm* sh, int wink) {
@@ -218,7 +252,7 @@ __device__ void build_plan(const VerifyArgs& a, Sm* sh, int wink) {
         float c;
         const int cat = request_cat(a, b, c, wink);
         const int cap = clamp_cap(a.caps ? a.caps[b] : a.cap_all);
-        sh->req[b] = (uint8_t)(cat | (cap << 3));
+        sh->plan.req[b] = (uint8_t)(cat | (cap << 3));
     }
     __syncthreads();
     if (tid < 32) {
@@ -227,8 +261,8 @@ __device__ void build_plan(const VerifyArgs& a, Sm* sh, int wink) {
             const int b = b0 + tid;
             int n[3] = {0, 0, 0};
             if (b < a.B) {
-                const int cat = (int)(sh->req[b] & 7u);
-                const int cap = (int)(sh->req[b] >> 3);
+                const int cat = (int)(sh->plan.req[b] & 7u);
+                const int cap = (int)(sh->plan.req[b] >> 3);
                 const int rows = cap + ((cat != kGreedy && a.drf != nullptr) ? cap - 1 : 0);
                 const int g = cat == kBinned ? 0 : (cat == kGreedy ? 2 : 1);
                 n[g] = rows;
@@ -236,14 +270,14 @@ __device__ void build_plan(const VerifyArgs& a, Sm* sh, int wink) {
 #pragma unroll
             for (int g = 0; g < 3; ++g) {
                 const int inc = (int)warp_incl_u32((uint32_t)n[g]);
-                if (b < a.B) sh->pre[g][b + 1] = (uint16_t)(run[g] + inc);
+                if (b < a.B) sh->plan.pre(g, b + 1) = (uint16_t)(run[g] + inc);
                 run[g] += __shfl_sync(0xffffffffu, inc, 31);
             }
         }
         if (tid == 0) {
-            sh->pre[0][0] = 0;
-            sh->pre[1][0] = 0;
-            sh->pre[2][0] = 0;
+            sh->plan.pre(0, 0) = 0;
+            sh->plan.pre(1, 0) = 0;
+            sh->plan.pre(2, 0) = 0;
         }
     }
     __syncthreads();
@@ -251,28 +285,28 @@ __device__ void build_plan(const VerifyArgs& a, Sm* sh, int wink) {
 
 template <typename Sm>
 __device__ int total_tasks(const VerifyArgs& a, const Sm* sh) {
-    return sh->pre[0][a.B] + sh->pre[1][a.B] + sh->pre[2][a.B];
+    return sh->plan.pre(0, a.B) + sh->plan.pre(1, a.B) + sh->plan.pre(2, a.B);
 }
 
 template <typename Sm>
 __device__ TaskInfo decode_task(const VerifyArgs& a, const Sm* sh, int t) {
     int g = 0;
     int local = t;
-    while (g < 2 && local >= sh->pre[g][a.B]) {
-        local -= sh->pre[g][a.B];
+    while (g < 2 && local >= sh->plan.pre(g, a.B)) {
+        local -= sh->plan.pre(g, a.B);
         ++g;
     }
     // largest b with pre[g][b] <= local
     int lo = 0, hi = a.B - 1;
     while (lo < hi) {
         const int mid = (lo + hi + 1) >> 1;
-        if (sh->pre[g][mid] <= local) lo = mid; else hi = mid - 1;
+        if (sh->plan.pre(g, mid) <= local) lo = mid; else hi = mid - 1;
     }
     TaskInfo ti;
     ti.b = lo;
-    const int r = local - sh->pre[g][lo];
-    ti.cat = (int)(sh->req[lo] & 7u);
-    ti.cap = (int)(sh->req[lo] >> 3);
+    const int r = local - sh->plan.pre(g, lo);
+    ti.cat = (int)(sh->plan.req[lo] & 7u);
+    ti.cap = (int)(sh->plan.req[lo] >> 3);
     ti.kind = r < ti.cap ? 0 : 1;
     ti.s = ti.kind == 0 ? r : r - ti.cap;
     const long long base = ti.kind == 0 ? (a.tgt_row ? a.tgt_row[ti.b] : ti.b * a.row_step)
@@ -407,9 +441,20 @@ __device__ void key_range(int target, uint32_t kmin, uint32_t kmax, float m, flo
 // exchange); two CTAs per SM overlap a memory-bound pass with an ALU-bound one.  Rows are
 // handed out by a global counter, most expensive first.
 
-constexpr int kRT = 256;           // threads per CTA
-constexpr int kRW = kRT / 32;      // warps
-constexpr int kRWinK = kRT;        // top-k rows with k <= 256 select inside the window
+#ifndef DSV_ROWS_THREADS
+#define DSV_ROWS_THREADS 256
+#endif
+#ifndef DSV_ROWS_MIN_CTAS
+#define DSV_ROWS_MIN_CTAS 3
+#endif
+#ifndef DSV_RING_VECS
+#define DSV_RING_VECS (2 * DSV_ROWS_THREADS)
+#endif
+constexpr int kRT = DSV_ROWS_THREADS;  // threads per CTA
+constexpr int kRW = kRT / 32;          // warps
+constexpr int kRWinK = kRT < 256 ? kRT : 256;  // top-k rows with k <= this select in a window
+static_assert(kRT % 32 == 0 && kRWinK <= kRT, "row kernel launch shape");
+static_assert(kRT >= 256, "the group walks give every thread one group of 32 bins (256 groups)");
 constexpr int kRWinCap = 1024;     // window candidates per row
 constexpr int kRKeyCap = 2048;     // keys per chunk of an exact count walk (count_walk)
 constexpr int kHCap = 8192;        // per-key histogram bins (32 KB)
@@ -425,21 +470,36 @@ constexpr uint32_t kNInfRaw = 0x007Fu;        // key of -inf
 constexpr int kBandCap = 512;
 static_assert(kFPos == 4096u && kFNB - kFNLow + 1u == 4096u && 2 * kFPos == (uint32_t)kHCap,
               "fixed histogram geometry");
-constexpr int kRingS = 3;          // streaming ring: slots
-constexpr int kRingCW = 512;       // vectors (16 B) per slot: 8 KB
+#ifndef DSV_RING_SLOTS
+#define DSV_RING_SLOTS 3
+#endif
+constexpr int kRingS = DSV_RING_SLOTS;     // streaming ring: slots
+constexpr int kRingCW = DSV_RING_VECS;     // vectors (16 B) per slot (8 KB at 256 threads)
+static_assert(kRingCW % kRT == 0 && kRingCW / kRT <= 2, "ring slot: one or two vectors a thread");
+constexpr int kRedN = 8 * kRW > 32 ? 8 * kRW : 32;  // per-warp reduction slots (tie scan: per vector)
+#ifndef DSV_BIG_VECS
+#define DSV_BIG_VECS (3 * DSV_ROWS_THREADS)
+#endif
+constexpr int kBigCW = DSV_BIG_VECS;  // vectors per slot of the big ring
+constexpr int kBigS = (kHCap * 4 + kRingS * kRingCW * 16) / (kBigCW * 16);  // big-ring slots
+static_assert(kBigCW % kRT == 0 && kBigS >= 2, "big ring: whole vectors a thread, two slots");
+static_assert(kBigCW / kRT * kRW <= kRedN, "tie scan: one warp sum per vector of a thread");
 
 struct RSmem {
-    uint16_t pre[3][kMaxB + 1];
-    uint8_t req[kMaxB];
+    // first, so that histogram byte addresses stay below 32 KB (the packed bin arithmetic of
+    // the histogram pass adds the base to both 16-bit halves of a word)
+    alignas(16) uint32_t hist[kHCap];       // per-key counts / window candidates / count chunks
+    alignas(16) uint4 ring[kRingS][kRingCW];  // streaming ring filled by bulk copies
+    Plan plan;                     // task table (after this struct in shared memory)
     int task;
     int first_min;
     uint32_t nlist;
-    uint32_t red32[32];
-    unsigned long long red64[32];
+    uint32_t red32[kRedN];
+    unsigned long long red64[kRedN];
     int sel[16];
     unsigned long long self64[8];
-    uint32_t wc[32];
-    unsigned long long wm[32];
+    uint32_t wc[kRedN];
+    unsigned long long wm[kRedN];
     uint32_t nband;                // one-pass histogram: band elements listed
     uint32_t outside;              //                     a value outside the fixed range
     uint16_t band[kBandCap];       //                     the band's raw values
@@ -447,14 +507,19 @@ struct RSmem {
     unsigned long long gmass[kHCap / 32];  //                       masses
     uint32_t zcnt;                 // histogram band: elements
     unsigned long long zmass;      //                 exact mass
-    alignas(16) uint32_t hist[kHCap];       // per-key counts / window candidates / count chunks
-    alignas(16) uint4 ring[kRingS][kRingCW];  // streaming ring filled by bulk copies
     alignas(8) uint64_t ring_bar[kRingS];
     uint32_t ring_cnt;                      // chunks consumed so far (slot, phase)
+    // passes that need no histogram (max pass, tie cut) stream through the big ring: the
+    // histogram and the ring together, kBigS slots of kBigCW vectors, own barriers
+    alignas(8) uint64_t big_bar[kBigS];
+    uint32_t big_cnt;
 };
+static_assert(offsetof(RSmem, ring) == offsetof(RSmem, hist) + sizeof(uint32_t) * kHCap,
+              "the big ring spans the histogram and the ring");
 
-// three CTAs per SM: 3 x (this + 1 KB reserved) within the SM's 228 KB
-static_assert(sizeof(RSmem) <= 74 * 1024, "row kernel shared memory");
+// DSV_ROWS_MIN_CTAS CTAs per SM: each (this + 1 KB reserved) within the SM's 228 KB
+static_assert(DSV_ROWS_MIN_CTAS * (sizeof(RSmem) + plan_bytes(64) + 1024) <= 228 * 1024,
+              "row kernel shared memory (batches up to 64 at the intended occupancy)");
 static_assert(2 * kRWinCap * 4 <= kHCap * 4 && kRWinCap * 8 <= kRingS * kRingCW * 16,
               "window candidates fit the histogram, the ranked list the ring");
 
@@ -488,50 +553,70 @@ __device__ __forceinline__ uint4 row_vec(const RowGeo& g, int V, const uint4* sr
     return x;
 }
 
-// Stream the row through fn(vector, v) via the ring: thread 0 keeps kRingS chunks of kRingCW
+// The slots, barriers and chunk counter of the small ring (kBig = false: kRingS slots after
+// the histogram) or of the big ring (kBig = true: kBigS slots over the histogram and the ring;
+// only for passes that keep nothing in the histogram).
+template <bool kBig>
+struct Ring {
+    static constexpr int S = kBig ? kBigS : kRingS;
+    static constexpr int CW = kBig ? kBigCW : kRingCW;
+    uint4* buf;
+    uint64_t* bar;
+    uint32_t* cnt;
+    __device__ __forceinline__ explicit Ring(RSmem* sh)
+        : buf(kBig ? reinterpret_cast<uint4*>(sh->hist) : &sh->ring[0][0]),
+          bar(kBig ? sh->big_bar : sh->ring_bar),
+          cnt(kBig ? &sh->big_cnt : &sh->ring_cnt) {}
+    __device__ __forceinline__ uint4* slot(uint32_t i) const { return buf + (size_t)i * CW; }
+};
+
+// Stream the row through fn(vector, v) via a ring: thread 0 keeps S chunks of CW
 // vectors in flight with bulk copies (one mbarrier per slot, bounded waits); every thread
 // handles vectors tid and tid + kRT of each chunk.  All threads must call it.
-template <typename F>
+template <bool kBig = false, typename F>
 __device__ __forceinline__ void stream_row(RSmem* sh, const VerifyArgs& a, const RowGeo& g, int V,
                                            F&& fn) {
+    const Ring<kBig> R(sh);
+    constexpr int S = Ring<kBig>::S;
+    constexpr int CW = Ring<kBig>::CW;
     const int tid = threadIdx.x;
     const char* src = reinterpret_cast<const char*>(g.rowp - g.off);
-    const int nch = (g.nv + kRingCW - 1) / kRingCW;
-    const uint32_t base = sh->ring_cnt;  // uniform: read before any thread updates it
+    const int nch = (g.nv + CW - 1) / CW;
+    const uint32_t base = *R.cnt;  // uniform: read before any thread updates it
     __syncthreads();
     if (tid == 0) {
-        for (int c = 0; c < nch && c < kRingS; ++c) {
-            const uint32_t slot = (base + c) % kRingS;
-            const int nvec = min(kRingCW, g.nv - c * kRingCW);
+        for (int c = 0; c < nch && c < S; ++c) {
+            const uint32_t slot = (base + c) % S;
+            const int nvec = min(CW, g.nv - c * CW);
             fence_proxy_async_smem();
-            mbar_arrive_expect_tx(&sh->ring_bar[slot], (uint32_t)nvec * 16u);
-            bulk_g2s(sh->ring[slot], src + (size_t)c * kRingCW * 16, (uint32_t)nvec * 16u, &sh->ring_bar[slot]);
+            mbar_arrive_expect_tx(&R.bar[slot], (uint32_t)nvec * 16u);
+            bulk_g2s(R.slot(slot), src + (size_t)c * CW * 16, (uint32_t)nvec * 16u, &R.bar[slot]);
         }
     }
     for (int c = 0; c < nch; ++c) {
         const uint32_t k = base + c;
-        const uint32_t slot = k % kRingS;
-        if (!mbar_wait_bounded(&sh->ring_bar[slot], (k / kRingS) & 1u)) {
+        const uint32_t slot = k % S;
+        if (!mbar_wait_bounded(&R.bar[slot], (k / S) & 1u)) {
             if (tid == 0) atomicOr(&a.ws->err, 1u);
         }
-        const int v0 = c * kRingCW;
-        const int nvec = min(kRingCW, g.nv - v0);
+        const int v0 = c * CW;
+        const int nvec = min(CW, g.nv - v0);
 #pragma unroll
-        for (int u = 0; u < kRingCW / kRT; ++u) {
+        for (int u = 0; u < CW / kRT; ++u) {
             const int i = tid + u * kRT;
-            if (i < nvec) fn(row_vec(g, V, nullptr, v0 + i, sh->ring[slot][i]), v0 + i);
+            if (i < nvec) fn(row_vec(g, V, nullptr, v0 + i, R.slot(slot)[i]), v0 + i);
         }
         __syncthreads();  // the slot is consumed
-        if (tid == 0 && c + kRingS < nch) {
-            const int cn = c + kRingS;
-            const int nv2 = min(kRingCW, g.nv - cn * kRingCW);
+        if (tid == 0 && c + S < nch) {
+            const int cn = c + S;
+            const int nv2 = min(CW, g.nv - cn * CW);
             fence_proxy_async_smem();
-            mbar_arrive_expect_tx(&sh->ring_bar[slot], (uint32_t)nv2 * 16u);
-            bulk_g2s(sh->ring[slot], src + (size_t)cn * kRingCW * 16, (uint32_t)nv2 * 16u, &sh->ring_bar[slot]);
+            mbar_arrive_expect_tx(&R.bar[slot], (uint32_t)nv2 * 16u);
+            bulk_g2s(R.slot(slot), src + (size_t)cn * CW * 16, (uint32_t)nv2 * 16u, &R.bar[slot]);
         }
     }
     __syncthreads();
-    if (tid == 0) sh->ring_cnt = base + (uint32_t)nch;
+    if (tid == 0) *R.cnt = base + (uint32_t)nch;
     __syncthreads();
 }
 
@@ -653,25 +738,34 @@ __device__ int tie_scan(RSmem* sh, const VerifyArgs& a, const RowGeo& g, int V, 
     const uint32_t kb = key_bits(key);
     const uint32_t kb2 = kb | (kb << 16);
     const char* src = reinterpret_cast<const char*>(g.rowp - g.off);
-    const int nch = (g.nv + kRingCW - 1) / kRingCW;
-    const uint32_t base = sh->ring_cnt;
+    const Ring<true> R(sh);  // the histogram is no longer needed
+    constexpr int S = Ring<true>::S;
+    constexpr int CW = Ring<true>::CW;
+    const int nch = (g.nv + CW - 1) / CW;
+    const uint32_t base = *R.cnt;
     __syncthreads();
     if (tid == 0) {
         sh->sel[12] = -1;
-        for (int c = 0; c < nch && c < kRingS; ++c) {
-            const uint32_t slot = (base + c) % kRingS;
-            const int nvec = min(kRingCW, g.nv - c * kRingCW);
+        for (int c = 0; c < nch && c < S; ++c) {
+            const uint32_t slot = (base + c) % S;
+            const int nvec = min(CW, g.nv - c * CW);
             fence_proxy_async_smem();
-            mbar_arrive_expect_tx(&sh->ring_bar[slot], (uint32_t)nvec * 16u);
-            bulk_g2s(sh->ring[slot], src + (size_t)c * kRingCW * 16, (uint32_t)nvec * 16u, &sh->ring_bar[slot]);
+            mbar_arrive_expect_tx(&R.bar[slot], (uint32_t)nvec * 16u);
+            bulk_g2s(R.slot(slot), src + (size_t)c * CW * 16, (uint32_t)nvec * 16u, &R.bar[slot]);
         }
     }
     __syncthreads();
-    int issued = nch < kRingS ? nch : kRingS;
+    int issued = nch < S ? nch : S;
     unsigned long long run = 0;
     int found = -1;
+    // positions outside the row read as -inf (row_vec), so unless the key is -inf itself a
+    // vector's count is the number of equal halves: 16 mask bits each
+    const bool packed_count = kb != (kFill & 0xFFFFu);
     auto count_in = [&](uint4 x, int v) -> uint32_t {
         x = row_vec(g, V, nullptr, v, x);
+        if (packed_count)
+            return (uint32_t)(__popc(bf2_eq(x.x, kb2)) + __popc(bf2_eq(x.y, kb2)) +
+                              __popc(bf2_eq(x.z, kb2)) + __popc(bf2_eq(x.w, kb2))) >> 4;
         const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
         uint32_t c = 0;
 #pragma unroll
@@ -684,26 +778,26 @@ __device__ int tie_scan(RSmem* sh, const VerifyArgs& a, const RowGeo& g, int V, 
     };
     for (int c = 0; c < issued; ++c) {
         const uint32_t k = base + c;
-        const uint32_t slot = k % kRingS;
-        if (!mbar_wait_bounded(&sh->ring_bar[slot], (k / kRingS) & 1u)) {
+        const uint32_t slot = k % S;
+        if (!mbar_wait_bounded(&R.bar[slot], (k / S) & 1u)) {
             if (tid == 0) atomicOr(&a.ws->err, 1u);
         }
         if (found < 0) {
-            const int v0 = c * kRingCW;
-            const int nvec = min(kRingCW, g.nv - v0);
-            uint32_t cu[kRingCW / kRT];
+            const int v0 = c * CW;
+            const int nvec = min(CW, g.nv - v0);
+            uint32_t cu[CW / kRT];
 #pragma unroll
-            for (int u = 0; u < kRingCW / kRT; ++u) {
+            for (int u = 0; u < CW / kRT; ++u) {
                 const int i = tid + u * kRT;
-                cu[u] = i < nvec ? count_in(sh->ring[slot][i], v0 + i) : 0u;
+                cu[u] = i < nvec ? count_in(R.slot(slot)[i], v0 + i) : 0u;
                 const uint32_t ws_ = warp_sum_u32(cu[u]);
                 if (lane == 0) sh->red32[u * kRW + wid] = ws_;
             }
             __syncthreads();
-            uint32_t tot[kRingCW / kRT];
+            uint32_t tot[CW / kRT];
             uint32_t all = 0;
 #pragma unroll
-            for (int u = 0; u < kRingCW / kRT; ++u) {
+            for (int u = 0; u < CW / kRT; ++u) {
                 tot[u] = 0;
                 for (int w = 0; w < kRW; ++w) tot[u] += sh->red32[u * kRW + w];
                 all += tot[u];
@@ -712,7 +806,7 @@ __device__ int tie_scan(RSmem* sh, const VerifyArgs& a, const RowGeo& g, int V, 
                 // in this chunk: vectors are in index order u-major, then thread
                 uint32_t need = (uint32_t)(need_total - run);
 #pragma unroll
-                for (int u = 0; u < kRingCW / kRT; ++u) {
+                for (int u = 0; u < CW / kRT; ++u) {
                     if (need == 0u) break;
                     if (need > tot[u]) {
                         need -= tot[u];
@@ -725,7 +819,7 @@ __device__ int tie_scan(RSmem* sh, const VerifyArgs& a, const RowGeo& g, int V, 
                     if (cu[u] > 0 && lo < need && lo + cu[u] >= need) {
                         uint32_t k2 = need - lo;
                         const int v = v0 + tid + u * kRT;
-                        const uint4 x = row_vec(g, V, nullptr, v, sh->ring[slot][tid + u * kRT]);
+                        const uint4 x = row_vec(g, V, nullptr, v, R.slot(slot)[tid + u * kRT]);
                         const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
                         int e_found = -1;
 #pragma unroll
@@ -746,16 +840,16 @@ __device__ int tie_scan(RSmem* sh, const VerifyArgs& a, const RowGeo& g, int V, 
         const bool more = found < 0 && issued < nch;
         if (tid == 0 && more) {
             const int cn = issued;
-            const uint32_t slot2 = (base + cn) % kRingS;
-            const int nv2 = min(kRingCW, g.nv - cn * kRingCW);
+            const uint32_t slot2 = (base + cn) % S;
+            const int nv2 = min(CW, g.nv - cn * CW);
             fence_proxy_async_smem();
-            mbar_arrive_expect_tx(&sh->ring_bar[slot2], (uint32_t)nv2 * 16u);
-            bulk_g2s(sh->ring[slot2], src + (size_t)cn * kRingCW * 16, (uint32_t)nv2 * 16u, &sh->ring_bar[slot2]);
+            mbar_arrive_expect_tx(&R.bar[slot2], (uint32_t)nv2 * 16u);
+            bulk_g2s(R.slot(slot2), src + (size_t)cn * CW * 16, (uint32_t)nv2 * 16u, &R.bar[slot2]);
         }
         if (more) ++issued;
     }
     __syncthreads();
-    if (tid == 0) sh->ring_cnt = base + (uint32_t)issued;
+    if (tid == 0) *R.cnt = base + (uint32_t)issued;
     __syncthreads();
     return found;
 }
@@ -806,9 +900,6 @@ __device__ KeyStop count_walk(RSmem* sh, const VerifyArgs& a, const RowGeo& g, i
     return ks;
 }
 
-#ifndef DSV_ROWS_MIN_CTAS
-#define DSV_ROWS_MIN_CTAS 3
-#endif
 // One row task: its descriptor (and, for greedy rows, its packed first argmax).  All threads.
 __device__ void process_row(RSmem* sh, const VerifyArgs& a, const TaskInfo& ti) {
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
@@ -832,25 +923,51 @@ __device__ void process_row(RSmem* sh, const VerifyArgs& a, const TaskInfo& ti) 
         }
         __syncthreads();
         uint32_t vmax2 = 0xFF80FF80u;  // running bf16x2 maximum (-inf, -inf)
+        // Bins of a word whose two halves are both fine, packed: sgn = 0xFFFF in each negative
+        // half, y = bits (negative) or 0xFFFF - bits (positive), bin = y + (sgn & 0x1500) -
+        // 0xBA80, i.e. 0x457F - bits for positive v (descending key) and bits - 0xA580 for
+        // negative v (4096 + descending key of the negative part).  The histogram's word
+        // address / 4 is added to both halves and the result scaled by 4, so each half is the
+        // shared byte address of its bin: every half stays in [0, 0x4000) on the way (the
+        // histogram starts below 32 KB), so no carry or borrow crosses the halves.
+        const uint32_t hbase = smem_u32(sh->hist);
+        const uint32_t hq = hbase >> 2;
+        const uint32_t koff = ((hq << 16) | hq) - 0xBA80BA80u;
+        if (hbase + 4u * 0x2000u > 0x10000u && tid == 0) atomicOr(&a.ws->err, 32u);  // layout
         stream_row(sh, a, g, V, [&](const uint4& x, int) {
             const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
             vmax2 = bf2_max(vmax2, bf2_max(bf2_max(xs[0], xs[1]), bf2_max(xs[2], xs[3])));
-            uint32_t rare = 0;  // bit q: word q has an element outside the fine bins
+            // fine iff 2^-20 <= |v| < 2^12, i.e. 0x3580 <= |bits| <= 0x457F: bit 15 of
+            // |bits| + 0x4A80 says ">= 0x3580", of |bits| + 0x3A80 says ">= 0x4580"
+            uint32_t f[4];
 #pragma unroll
             for (int q = 0; q < 4; ++q) {
-                const uint32_t w = xs[q];
-                // fine iff 2^-20 <= |v| < 2^12, i.e. 0x3580 <= |bits| <= 0x457F: bit 15 of
-                // |bits| + 0x4A80 says ">= 0x3580", of |bits| + 0x3A80 says ">= 0x4580"
-                const uint32_t a2 = w & 0x7FFF7FFFu;
-                const uint32_t f2 = (a2 + 0x4A804A80u) & ~(a2 + 0x3A803A80u) & 0x80008000u;
-                // bin: positive v -> 0x457F - |bits| (descending key), negative v ->
-                // |bits| - 0x2580 (4096 + descending key of the negative part)
-                const uint32_t lo = w & 0xFFFFu, hi = w >> 16;
-                const uint32_t ilo = (lo & 0x8000u) ? (lo & 0x7FFFu) - 0x2580u : 0x457Fu - lo;
-                const uint32_t ihi = (hi & 0x8000u) ? (hi & 0x7FFFu) - 0x2580u : 0x457Fu - hi;
-                if (f2 & 0x00008000u) atomicAdd(&sh->hist[ilo], 1u);
-                if (f2 & 0x80000000u) atomicAdd(&sh->hist[ihi], 1u);
-                rare |= (f2 != 0x80008000u) ? (1u << q) : 0u;
+                const uint32_t a2 = xs[q] & 0x7FFF7FFFu;
+                f[q] = (a2 + 0x4A804A80u) & ~(a2 + 0x3A803A80u);
+            }
+            uint32_t rare = 0;  // bit q: word q has an element outside the fine bins
+            if ((f[0] & f[1] & f[2] & f[3] & 0x80008000u) == 0x80008000u) {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    const uint32_t w = xs[q];
+                    const uint32_t sgn = prmt_sign16(w);
+                    const uint32_t b2 = ((w ^ ~sgn) + (sgn & 0x15001500u) + koff) << 2;
+                    red_shared_inc(b2 & 0xFFFFu);
+                    red_shared_inc(b2 >> 16);
+                }
+            } else {
+#pragma unroll
+                for (int q = 0; q < 4; ++q) {
+                    if ((f[q] & 0x80008000u) == 0x80008000u) {
+                        const uint32_t w = xs[q];
+                        const uint32_t sgn = prmt_sign16(w);
+                        const uint32_t b2 = ((w ^ ~sgn) + (sgn & 0x15001500u) + koff) << 2;
+                        red_shared_inc(b2 & 0xFFFFu);
+                        red_shared_inc(b2 >> 16);
+                    } else {
+                        rare |= 1u << q;
+                    }
+                }
             }
             if (rare) {
 #pragma unroll 1
@@ -858,7 +975,10 @@ __device__ void process_row(RSmem* sh, const VerifyArgs& a, const TaskInfo& ti) 
                     if (!(rare & (1u << (h >> 1)))) continue;
                     const uint32_t u16 = (h & 1) ? (xs[h >> 1] >> 16) : (xs[h >> 1] & 0xFFFFu);
                     const uint32_t ab = u16 & 0x7FFFu;
-                    if (ab >= 0x3580u && ab <= 0x457Fu) continue;  // a fine element
+                    if (ab >= 0x3580u && ab <= 0x457Fu) {          // a fine element
+                        atomicAdd(&sh->hist[(u16 & 0x8000u) ? ab - 0x2580u : 0x457Fu - u16], 1u);
+                        continue;
+                    }
                     if (u16 == 0xFF80u) continue;                   // -inf (and the row's fill)
                     if (ab < 0x3580u) {                             // the band |v| < 2^-20
                         const uint32_t p = atomicAdd(&sh->nband, 1u);
@@ -887,7 +1007,7 @@ __device__ void process_row(RSmem* sh, const VerifyArgs& a, const TaskInfo& ti) 
         // ---- pass 1: max (greedy rows: and the first index of the max) ---------------
         tkey = 0;
         int tfirst = 0x7fffffff;
-        stream_row(sh, a, g, V, [&](const uint4& x, int v) {
+        stream_row<true>(sh, a, g, V, [&](const uint4& x, int v) {
             uint32_t mx = bf2_max(bf2_max(x.x, x.y), bf2_max(x.z, x.w));
             const uint32_t k0 = okey(mx & 0xFFFFu), k1 = okey(mx >> 16);
             const uint32_t vk = k0 > k1 ? k0 : k1;
@@ -1296,7 +1416,7 @@ __device__ __forceinline__ RowDesc load_desc_cg(const RowDesc* p) {
 // length for the chain kernel.  Greedy requests are decided there from the packed maxima.
 __device__ void row_done(RSmem* sh, const VerifyArgs& a, int b) {
     const int tid = threadIdx.x, lane = tid & 31;
-    const int cat = (int)(sh->req[b] & 7u), cap = (int)(sh->req[b] >> 3);
+    const int cat = (int)(sh->plan.req[b] & 7u), cap = (int)(sh->plan.req[b] >> 3);
     if (cat == kGreedy || a.cand == nullptr) return;
     const unsigned nrows = (unsigned)(cap + (a.drf != nullptr ? cap - 1 : 0));
     __syncthreads();
@@ -1351,9 +1471,17 @@ __global__ void __launch_bounds__(kRT, DSV_ROWS_MIN_CTAS) rows_kernel(VerifyArgs
     const int tid = threadIdx.x, lane = tid & 31;
     if (tid == 0) {
         for (int i = 0; i < kRingS; ++i) mbar_init(&sh->ring_bar[i], 1);
+        for (int i = 0; i < kBigS; ++i) mbar_init(&sh->big_bar[i], 1);
         fence_mbar_init();
         sh->ring_cnt = 0;
+        sh->big_cnt = 0;
+        uint16_t* pre = reinterpret_cast<uint16_t*>(smem_raw + sizeof(RSmem));
+        sh->plan = Plan{pre, reinterpret_cast<uint8_t*>(pre + 3 * (a.B + 1)), a.B};
     }
+#ifdef DSV_PROFILE
+    const unsigned long long trace_t0 = globaltimer_ns();
+#endif
+    __syncthreads();
     build_plan(a, sh, kRWinK);
     const int ntask = total_tasks(a, sh);
     if (blockIdx.x == 0 && tid < 32) {
@@ -1365,7 +1493,7 @@ __global__ void __launch_bounds__(kRT, DSV_ROWS_MIN_CTAS) rows_kernel(VerifyArgs
             const int b = b0 + lane;
             int g = -1;
             if (b < a.B) {
-                const int cat = (int)(sh->req[b] & 7u);
+                const int cat = (int)(sh->plan.req[b] & 7u);
                 g = cat == kGreedy ? 2 : (a.top_k[b] > kRWinK ? 0 : 1);
             }
 #pragma unroll
@@ -1377,7 +1505,7 @@ __global__ void __launch_bounds__(kRT, DSV_ROWS_MIN_CTAS) rows_kernel(VerifyArgs
             const int b = b0 + lane;
             int g = -1;
             if (b < a.B) {
-                const int cat = (int)(sh->req[b] & 7u);
+                const int cat = (int)(sh->plan.req[b] & 7u);
                 g = cat == kGreedy ? 2 : (a.top_k[b] > kRWinK ? 0 : 1);
             }
 #pragma unroll
@@ -1396,9 +1524,33 @@ __global__ void __launch_bounds__(kRT, DSV_ROWS_MIN_CTAS) rows_kernel(VerifyArgs
         const int t = sh->task;
         if (t >= ntask) break;
         const TaskInfo ti = decode_task(a, sh, t);
+#ifdef DSV_PROFILE
+        const unsigned long long trace_r0 = globaltimer_ns();
+#endif
         process_row(sh, a, ti);
         row_done(sh, a, ti.b);
+#ifdef DSV_PROFILE
+        // task trace: [256] entries used, [260 + 3 i] start, end, task | cat << 16 | sm << 24
+        if (tid == 0) {
+            const unsigned long long now = globaltimer_ns();
+            const unsigned long long i = atomicAdd(a.prof + 256, 1ull);
+            if (i < kTraceCap) {
+                unsigned long long* e = a.prof + 260 + 3 * i;
+                e[0] = trace_r0;
+                e[1] = now;
+                e[2] = (unsigned long long)t | ((unsigned long long)ti.cat << 16) |
+                       ((unsigned long long)smid() << 24) | ((unsigned long long)blockIdx.x << 40);
+            }
+        }
+#endif
     }
+#ifdef DSV_PROFILE
+    if (tid == 0 && blockIdx.x < kTraceCtas) {  // per CTA: start and exit
+        unsigned long long* e = a.prof + 260 + 3 * kTraceCap + 2 * blockIdx.x;
+        e[0] = trace_t0;
+        e[1] = globaltimer_ns();
+    }
+#endif
     // the last CTA out resets the row counter for the next launch
     __syncthreads();
     if (tid == 0) {
@@ -1413,25 +1565,30 @@ __global__ void __launch_bounds__(kRT, DSV_ROWS_MIN_CTAS) rows_kernel(VerifyArgs
 }
 
 int launch_rows_cta(VerifyArgs a, cudaStream_t stream) {
-    const size_t smem = sizeof(RSmem);
-    static int attr_done = 0;
-    static int cached_dev = -1, cached_blocks = 0;
-    if (!attr_done) {
-        if (cudaFuncSetAttribute(rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-            return kLaunchFailed;
-        attr_done = 1;
-    }
+    // fixed state + the batch's task table; the grid fills every SM at the occupancy this size
+    // allows (cached per device and size)
+    const size_t smem = sizeof(RSmem) + plan_bytes(a.B);
+    constexpr int kMaxDev = 64;
+    static int attr_done[kMaxDev] = {};
+    static size_t cached_smem[kMaxDev] = {};
+    static int cached_blocks[kMaxDev] = {};
     int dev = 0;
-    cudaGetDevice(&dev);
-    if (cached_dev != dev) {
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return kLaunchFailed;
+    if (!attr_done[dev]) {
+        if (cudaFuncSetAttribute(rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)(sizeof(RSmem) + plan_bytes(kMaxB))) != cudaSuccess)
+            return kLaunchFailed;
+        attr_done[dev] = 1;
+    }
+    if (cached_smem[dev] != smem) {
         int per_sm = 0, sms = 0;
         if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rows_kernel, kRT, smem) != cudaSuccess || per_sm < 1)
             return kLaunchFailed;
         if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return kLaunchFailed;
-        cached_dev = dev;
-        cached_blocks = per_sm * sms;
+        cached_smem[dev] = smem;
+        cached_blocks[dev] = per_sm * sms;
     }
-    rows_kernel<<<cached_blocks, kRT, smem, stream>>>(a);
+    rows_kernel<<<cached_blocks[dev], kRT, smem, stream>>>(a);
     return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
 }
 

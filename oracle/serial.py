@@ -5,8 +5,7 @@ confidences (paths inside the reference project, package ``sglang_dspine``):
 
   sample_chain   kernels/dspine.py:616-674 _serial_sample_chain (and its test oracle
                  tests/ref_utils.py:12-50 ref_sample_chain), in fp32 with the summation orders
-                 the CUDA kernel documents: rank-order sums for the mass ranked ahead, lane-order
-                 running sums for the kept mass and the CDF
+                 the CUDA kernel fixes (butterfly sums, Kogge-Stone prefix sums)
   table_scores   kernels/dspine.py:210-287 _serial_table: the score matrix s[n, j, c] in fp64
                  from the same bf16 inputs, with a bound on the fp32 accumulation error
   chain          kernels/dspine.py:290-324 _serial_chain
@@ -25,8 +24,41 @@ import numpy as np
 F32 = np.float32
 
 
+def _bfly_sum(v):
+    """Butterfly sum of up to 64 float32 values: lane l holds v[l] + v[l + 32], then
+    xor-shuffle steps 16, 8, 4, 2, 1 (every lane ends with the same value)."""
+    x = np.zeros(64, F32)
+    x[: len(v)] = v
+    s = (x[:32] + x[32:]).astype(F32)
+    lanes = np.arange(32)
+    for o in (16, 8, 4, 2, 1):
+        s = (s + s[lanes ^ o]).astype(F32)
+    return F32(s[0])
+
+
+def _scan32(v):
+    v = v.astype(F32).copy()
+    for o in (1, 2, 4, 8, 16):
+        v[o:] = (v[o:] + v[:-o]).astype(F32)
+    return v
+
+
+def _scan64(v):
+    """Inclusive prefix sums of up to 64 float32 values: Kogge-Stone scans (shifts 1..16) of
+    positions 0..31 and 32..63, the second half plus the total of the first."""
+    x = np.zeros(64, F32)
+    x[: len(v)] = v
+    lo = _scan32(x[:32])
+    hi = (_scan32(x[32:]) + lo[31]).astype(F32)
+    return np.concatenate((lo, hi))
+
+
 def sample_chain(table, inv_t, top_k, top_p, min_p, greedy, u, cand, greedy_tok, T):
-    """(tok int64 [n], q f32 [n, K], conf f32 [n] with NaN where a greedy row writes nothing)."""
+    """(tok int64 [n], q f32 [n, K], conf f32 [n] with NaN where a greedy row writes nothing).
+
+    fp32 throughout, with the summation orders the CUDA kernel fixes: butterfly sums for the
+    softmax denominator and the kept mass, Kogge-Stone prefix sums for the mass ranked ahead
+    (in rank order) and for the CDF (in lane order)."""
     table = np.asarray(table, F32)
     n, k, _ = table.shape
     tm1 = T - 1
@@ -42,7 +74,7 @@ def sample_chain(table, inv_t, top_k, top_p, min_p, greedy, u, cand, greedy_tok,
                 row = b * tm1 + i
                 s = (table[row, sender] * it).astype(F32)
                 m = np.exp((s - s.max()).astype(F32)).astype(F32)
-                total = F32(m.sum(dtype=F32))
+                total = _bfly_sum(m)
                 p = (m / total).astype(F32)
                 pmax = F32(p.max())
                 if not gr:
@@ -50,13 +82,12 @@ def sample_chain(table, inv_t, top_k, top_p, min_p, greedy, u, cand, greedy_tok,
                 order = sorted(range(k), key=lambda c: (-float(p[c]), c))
                 rank = np.empty(k, np.int64)
                 rank[order] = np.arange(k)
-                ahead = np.concatenate(([F32(0)], np.cumsum(p[order], dtype=F32)[:-1]))
+                ahead = np.concatenate(([F32(0)], _scan64(p[order])[: k - 1]))
                 before = ahead[rank]
                 keep = (rank < tk) & (before <= tp) & (p >= F32(mp * pmax))
                 w = np.where(keep, p, F32(0)).astype(F32)
-                wsum = np.cumsum(w, dtype=F32)[-1]
-                q = (w / wsum).astype(F32)
-                cdf = np.cumsum(q, dtype=F32)
+                q = (w / _bfly_sum(w)).astype(F32)
+                cdf = _scan64(q)[:k]
                 thr = F32(F32(u[row]) * cdf[-1])
                 choice = int((cdf <= thr).sum())
                 kept = np.nonzero(keep)[0]
