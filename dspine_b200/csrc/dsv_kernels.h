@@ -19,7 +19,8 @@ struct WsHeader {
     unsigned int exited;     // clusters that left the task loop
     unsigned int finalized;  // requests finalized in this launch
     unsigned int err;        // bit 0: bulk copy timed out; bit 1: bad row; bit 2: bad slot;
-                             // bit 3: a selection found no boundary; bit 4: tie cut not found
+                             // bit 3: a selection found no boundary; bit 4: tie cut not found;
+                             // bit 5: shared-memory layout check of the row kernel failed
 };
 
 // Descriptor of one processed logit row (streaming path): p_i = exp2c((l_i - m) c) * inv_s

@@ -220,12 +220,14 @@ struct TaskInfo {
 __device__ __forceinline__ int clamp_cap(int c) { return c < 1 ? 1 : (c > kT ? kT : c); }
 
 __device__ int request_cat(const VerifyArgs& a, int b, float& c_out, int wink) {
+    // all three loads issue before any branch (one memory round trip at kernel start)
     const float T = a.temperature[b];
     const int k = a.top_k[b];
+    const float p = a.top_p[b];
     const float c = log2e_over(T);
     c_out = c;
     if (is_greedy(T, k, c)) return kGreedy;
-    if (a.top_p[b] < 1.0f) return kBinned;    // nucleus (any k): per-key histogram walk
+    if (p < 1.0f) return kBinned;             // nucleus (any k): per-key histogram walk
     if (k >= a.V) return kKeepAll;
     if (k <= wink) return kWindow;            // pure top-k, small k: candidate window
     return kBinned;                           // pure top-k, large k: exact counts from the top
@@ -249,9 +251,9 @@ template <typename Sm>
 __device__ void build_plan(const VerifyArgs& a, Sm* sh, int wink) {
     const int tid = threadIdx.x;
     for (int b = tid; b < a.B; b += blockDim.x) {
+        const int cap = clamp_cap(a.caps ? a.caps[b] : a.cap_all);
         float c;
         const int cat = request_cat(a, b, c, wink);
-        const int cap = clamp_cap(a.caps ? a.caps[b] : a.cap_all);
         sh->plan.req[b] = (uint8_t)(cat | (cap << 3));
     }
     __syncthreads();
@@ -1993,44 +1995,43 @@ __global__ void __launch_bounds__(kCT, 4) chain3_kernel(VerifyArgs a) {
                     }
                     if (tid == 0) sh->bonus = -1;
                     __syncthreads();
-                    if (wid == ws_) {
-                        // element masses of the warp's 1024 elements go to shared memory (the
-                        // idle queue area), lane l's 32 elements at [32 l, 32 l + 32)
-                        unsigned long long* fm = reinterpret_cast<unsigned long long*>(&sh->queue[0][0]);
-                        const int t_ = ws_ * 32 + lane;
-                        uint4 xa[4], ya[4];
-#pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            const int v = tv0 + 4 * t_ + u;
-                            xa[u] = make_uint4(0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u);
-                            ya[u] = xa[u];
-                            if (v < tv1) load8(r, v, pure, xa[u], ya[u]);
-                        }
+                    {
+                        // the crossing warp's 128 vectors (1024 elements) by the whole CTA:
+                        // thread t takes elements [4 t, 4 t + 4) of the region (half of
+                        // vector t / 2), a block scan of the thread masses finds the thread,
+                        // and it walks its four elements
+                        const int v = tv0 + 128 * ws_ + (tid >> 1);
+                        uint4 xa = make_uint4(0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u);
+                        uint4 ya = xa;
+                        if (v < tv1) load8(r, v, pure, xa, ya);
+                        unsigned long long f4[4];
                         unsigned long long own = 0;
 #pragma unroll
-                        for (int u = 0; u < 4; ++u) {
-                            const int v = tv0 + 4 * t_ + u;
-#pragma unroll
-                            for (int h = 0; h < 8; ++h) {
-                                const int i = 8 * v + h - r.poff;
-                                unsigned long long f = 0;
-                                if (v < tv1 && i >= 0 && i < V && kept_in(r.dt, half16(xa[u], h), i)) {
-                                    uint32_t qb = half16(ya[u], h);
-                                    if (!pure && r.has_dq && !r.qvec)
-                                        qb = r.qrow ? (uint32_t)__ldg(r.qrow + i) : 0xFF80u;
-                                    f = resid_kept(r, pure, half16(xa[u], h), qb, i);
-                                }
-                                fm[lane * 32 + u * 8 + h] = f;
-                                own += f;
+                        for (int hh = 0; hh < 4; ++hh) {
+                            const int h = 4 * (tid & 1) + hh;
+                            const int i = 8 * v + h - r.poff;
+                            unsigned long long f = 0;
+                            if (v < tv1 && i >= 0 && i < V && kept_in(r.dt, half16(xa, h), i)) {
+                                uint32_t qb = half16(ya, h);
+                                if (!pure && r.has_dq && !r.qvec)
+                                    qb = r.qrow ? (uint32_t)__ldg(r.qrow + i) : 0xFF80u;
+                                f = resid_kept(r, pure, half16(xa, h), qb, i);
                             }
+                            f4[hh] = f;
+                            own += f;
                         }
                         const unsigned long long incl = warp_incl_u64(own);
-                        long long run = base + (long long)(incl - own);
+                        if (lane == 31) sh->wsum[wid] = incl;
+                        __syncthreads();
+                        unsigned long long wpre = 0;
+                        for (int w = 0; w < wid; ++w) wpre += sh->wsum[w];
+                        long long run = base + (long long)(wpre + incl - own);
                         if (run <= thr && run + (long long)own > thr) {
-                            for (int j = 0; j < 32; ++j) {
-                                run += (long long)fm[lane * 32 + j];
+#pragma unroll
+                            for (int hh = 0; hh < 4; ++hh) {
+                                run += (long long)f4[hh];
                                 if (run > thr) {
-                                    sh->bonus = 8 * (tv0 + 4 * t_) + j - r.poff;
+                                    sh->bonus = 8 * v + 4 * (tid & 1) + hh - r.poff;
                                     break;
                                 }
                             }
