@@ -466,6 +466,9 @@ int dsv_serial_table(int32_t batch, int32_t block_size, int32_t hidden, int32_t 
         !rms || !gate_b || !idx)
         return DSV_BAD_POINTER;
     if (!aligned(lm_head, 16) || lm_stride % 8) return DSV_BAD_ALIGNMENT;
+    if (!aligned(query, 4) || query_stride % 2 || !aligned(tg, 4) || !aligned(tsv, 4) ||
+        !aligned(gate_b, 4))
+        return DSV_BAD_ALIGNMENT;
     dsv::TableArgs a;
     a.n = (int)n;
     a.t = block_size;

@@ -234,23 +234,55 @@ __global__ void __launch_bounds__(kTabThreads)
         }
         return;
     }
-    // base[c]: one warp per candidate row, 8 bf16 per lane per step
-    for (int c = warp; c < K; c += kTabThreads / 32) {
-        const __nv_bfloat16* w = a.head_candidates ? a.lm_w + ((int64_t)n * K + c) * a.w_stride
-                                                   : a.lm_w + ids[c] * a.w_stride;
-        float acc = 0.0f;
-        for (int h = lane * 8; h < H; h += 256) {
-            const uint4 v = *reinterpret_cast<const uint4*>(w + h);
-            const __nv_bfloat162* p2 = reinterpret_cast<const __nv_bfloat162*>(&v);
+    // base[c]: each warp takes two candidate rows at a time; every lane keeps four 16-byte
+    // loads of each row in flight (the rows are gathered by id, so latency, not bandwidth,
+    // bounds a row), two partial sums per row
+    constexpr int kTW = kTabThreads / 32;
+    for (int c0 = warp; c0 < K; c0 += 2 * kTW) {
+        const int c1 = c0 + kTW;
+        const __nv_bfloat16* w0 = a.head_candidates ? a.lm_w + ((int64_t)n * K + c0) * a.w_stride
+                                                    : a.lm_w + ids[c0] * a.w_stride;
+        const __nv_bfloat16* w1 = c1 >= K ? w0
+                                  : (a.head_candidates ? a.lm_w + ((int64_t)n * K + c1) * a.w_stride
+                                                       : a.lm_w + ids[c1] * a.w_stride);
+        float acc0 = 0.0f, acc1 = 0.0f;
+        for (int hb = lane * 8; hb < H; hb += 4 * 256) {
+            uint4 x0[4], x1[4];
 #pragma unroll
-            for (int e = 0; e < 4; ++e) {
-                const float2 f = __bfloat1622float2(p2[e]);
-                acc = fmaf(f.x, u[h + 2 * e], acc);
-                acc = fmaf(f.y, u[h + 2 * e + 1], acc);
+            for (int j = 0; j < 4; ++j) {
+                const int h = hb + j * 256;
+                if (h < H) {
+                    x0[j] = *reinterpret_cast<const uint4*>(w0 + h);
+                    x1[j] = *reinterpret_cast<const uint4*>(w1 + h);
+                }
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int h = hb + j * 256;
+                if (h < H) {
+                    const float4 ua = *reinterpret_cast<const float4*>(u + h);
+                    const float4 ub = *reinterpret_cast<const float4*>(u + h + 4);
+                    const float uu[8] = {ua.x, ua.y, ua.z, ua.w, ub.x, ub.y, ub.z, ub.w};
+                    const __nv_bfloat162* p0 = reinterpret_cast<const __nv_bfloat162*>(&x0[j]);
+                    const __nv_bfloat162* p1 = reinterpret_cast<const __nv_bfloat162*>(&x1[j]);
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 f0 = __bfloat1622float2(p0[e]);
+                        const float2 f1 = __bfloat1622float2(p1[e]);
+                        acc0 = fmaf(f0.x, uu[2 * e], acc0);
+                        acc0 = fmaf(f0.y, uu[2 * e + 1], acc0);
+                        acc1 = fmaf(f1.x, uu[2 * e], acc1);
+                        acc1 = fmaf(f1.y, uu[2 * e + 1], acc1);
+                    }
+                }
             }
         }
-        acc = warp_sum(acc);
-        if (lane == 0) base[c] = acc;
+        acc0 = warp_sum(acc0);
+        acc1 = warp_sum(acc1);
+        if (lane == 0) {
+            base[c0] = acc0;
+            if (c1 < K) base[c1] = acc1;
+        }
     }
     const int pairs = K * K;
     float acc[kMaxPairs];
@@ -259,12 +291,21 @@ __global__ void __launch_bounds__(kTabThreads)
     const __nv_bfloat16* q = a.query + row * a.q_stride;
     for (int r0 = 0; r0 < RK; r0 += kRChunk) {
         __syncthreads();  // previous chunk consumed
-        for (int e = tid; e < K * kRChunk; e += kTabThreads) {
-            const int j = e / kRChunk, rr = e % kRChunk, col = r0 + rr;
+        // two columns per thread and step (4-byte loads), several steps in flight
+#pragma unroll 4
+        for (int e = tid; e < K * (kRChunk / 2); e += kTabThreads) {
+            const int j = e / (kRChunk / 2), rr = 2 * (e % (kRChunk / 2)), col = r0 + rr;
             const __nv_bfloat16* t = a.tsv + sid[j] * (int64_t)(2 * RK);
-            const float gate = (bf(q[col]) + bf(t[col])) + bf(a.gate_b[col]);
-            mch[j * kRPitch + rr] = sigmoidf_(gate) * bf(t[RK + col]);
-            gch[j * kRPitch + rr] = bf(a.tg[ids[j] * (int64_t)RK + col]);
+            const float2 q2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(q + col));
+            const float2 t2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(t + col));
+            const float2 b2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(a.gate_b + col));
+            const float2 v2 = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(t + RK + col));
+            const float2 g2 = __bfloat1622float2(
+                *reinterpret_cast<const __nv_bfloat162*>(a.tg + ids[j] * (int64_t)RK + col));
+            mch[j * kRPitch + rr] = sigmoidf_((q2.x + t2.x) + b2.x) * v2.x;
+            mch[j * kRPitch + rr + 1] = sigmoidf_((q2.y + t2.y) + b2.y) * v2.y;
+            gch[j * kRPitch + rr] = g2.x;
+            gch[j * kRPitch + rr + 1] = g2.y;
         }
         __syncthreads();
 #pragma unroll

@@ -1216,41 +1216,31 @@ __device__ void process_row(RSmem* sh, const VerifyArgs& a, const TaskInfo& ti) 
         }
         PROF_MARK(ti.cat, 2);
         // ---- S and the walk over groups of 32 bins: positive groups, the band, negative
-        // groups (rank order).  Each warp sums its groups (one bin per lane), thread g scans
-        // group g, and the warp of the stopping group finds the bin.
+        // groups (rank order).  Thread g sums group g (its 32 bins in a skewed order, so the
+        // lanes of a warp read distinct banks; one fix(exp2c) per nonzero bin), thread g
+        // scans group g, and the warp of the stopping group finds the bin.
         const uint32_t ngp = (npos + 31u) >> 5, ngn = (nneg + 31u) >> 5, ng = ngp + ngn;
-#pragma unroll 2
-        for (uint32_t gi = wid; gi < ng; gi += kRW) {
+        for (uint32_t gi = (uint32_t)tid; gi < ng; gi += kRT) {
             const bool neg = gi >= ngp;
-            const uint32_t j = neg ? gi - ngp : gi;
-            const uint32_t i = (j << 5) + lane;            // bin within its part
+            const uint32_t b0 = (neg ? gi - ngp : gi) << 5;   // first bin within its part
             const uint32_t lim = neg ? nneg : npos;
-            uint32_t cnt = 0;
-            unsigned long long ms = 0;
-            if (i < lim) cnt = sh->hist[(neg ? npos : 0u) + i];
-            if (!__any_sync(0xffffffffu, cnt != 0u)) {     // empty group
-                if (lane == 0) {
-                    sh->gcnt[gi] = 0u;
-                    sh->gmass[gi] = 0ull;
+            const uint32_t* hp = sh->hist + (neg ? npos : 0u);
+            const uint32_t top = neg ? negtop : topkey;
+            uint32_t gc = 0;
+            unsigned long long gm = 0;
+#pragma unroll 4
+            for (uint32_t jj = 0; jj < 32u; ++jj) {
+                const uint32_t i = b0 + ((jj + (uint32_t)tid) & 31u);
+                const uint32_t cnt = i < lim ? hp[i] : 0u;
+                if (cnt) {
+                    gc += cnt;
+                    const uint32_t key = top - i;
+                    if (key >= klo)
+                        gm += (unsigned long long)cnt * fix_of_y(y_clamped(bf(key_bits(key)), m, ti.c));
                 }
-                continue;
             }
-            {
-                const uint32_t key = (neg ? negtop : topkey) - i;
-                if (cnt && key >= klo)
-                    ms = (unsigned long long)cnt * fix_of_y(y_clamped(bf(key_bits(key)), m, ti.c));
-            }
-            // warp sums with single-instruction reductions: the mass (< 2^59) in three
-            // 21-bit parts, each summing below 2^26
-            const uint32_t gc = __reduce_add_sync(0xffffffffu, cnt);
-            const uint32_t s0 = __reduce_add_sync(0xffffffffu, (uint32_t)(ms & 0x1FFFFFu));
-            const uint32_t s1 = __reduce_add_sync(0xffffffffu, (uint32_t)((ms >> 21) & 0x1FFFFFu));
-            const uint32_t s2 = __reduce_add_sync(0xffffffffu, (uint32_t)(ms >> 42));
-            if (lane == 0) {
-                sh->gcnt[gi] = gc;
-                sh->gmass[gi] = (unsigned long long)s0 + ((unsigned long long)s1 << 21) +
-                                ((unsigned long long)s2 << 42);
-            }
+            sh->gcnt[gi] = gc;
+            sh->gmass[gi] = gm;
         }
         __syncthreads();
         const unsigned long long zc = sh->zcnt, zm = sh->zmass;
@@ -1519,9 +1509,13 @@ __global__ void __launch_bounds__(kRT, DSV_ROWS_MIN_CTAS) rows_kernel(VerifyArgs
         }
     }
 
+    // the first task of CTA i is task i; later ones come from the counter (offset by the grid)
+    bool first_task = true;
     for (;;) {
         __syncthreads();
-        if (tid == 0) sh->task = (int)atomicAdd(&a.ws->next, 1u);
+        if (tid == 0)
+            sh->task = first_task ? (int)blockIdx.x : (int)(gridDim.x + atomicAdd(&a.ws->next, 1u));
+        first_task = false;
         __syncthreads();
         const int t = sh->task;
         if (t >= ntask) break;

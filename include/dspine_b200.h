@@ -258,7 +258,8 @@ int dsv_serial_sample_chain(int32_t batch, int32_t block_size, int32_t k, const 
  * idx[n, j] = the first lane of max_c s[j, c]; confidence (optional, fp32 [n, K]) =
  * 1 / sum_c exp((s[j, c] - max) / max(rms, 1e-6)).  bf16 raw [batch*T, hidden] (row pitch
  * raw_stride), norm_w [hidden], lm_head (row pitch lm_stride, a multiple of 8, 16-byte aligned),
- * tg [vocab, rk], tsv [vocab, 2 rk], query (pitch query_stride), gate_b [rk]; rms fp32 [batch*T].
+ * tg [vocab, rk], tsv [vocab, 2 rk], query (pitch query_stride, even), gate_b [rk] (query, tg,
+ * tsv, gate_b 4-byte aligned); rms fp32 [batch*T].
  * hidden a multiple of 512 up to 16384, rk a multiple of 128, K a power of two in [2, 64].
  * A row whose candidate or sender id lies outside [0, vocab) writes idx -1 (confidence NaN). */
 int dsv_serial_table(int32_t batch, int32_t block_size, int32_t hidden, int32_t rk, int32_t k,
