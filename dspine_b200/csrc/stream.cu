@@ -733,7 +733,10 @@ __device__ KeyStop cta_walk_keys(RSmem* sh, const uint32_t* counts, uint32_t khi
 
 
 // index of occurrence number `need` (1-based) of the key in index order, streaming the row
-// through the ring; chunks already issued when it is found are drained, none is left in flight
+// through the ring; chunks already issued when it is found are drained, none is left in flight.
+// kRev streams the row from its end and `need` counts occurrences from the end (the caller
+// picks the nearer end: occurrence n of c in index order is occurrence c - n + 1 from the end).
+template <bool kRev>
 __device__ int tie_scan(RSmem* sh, const VerifyArgs& a, const RowGeo& g, int V, uint32_t key,
                         unsigned long long need_total) {
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
@@ -743,13 +746,17 @@ __device__ int tie_scan(RSmem* sh, const VerifyArgs& a, const RowGeo& g, int V, 
     const Ring<true> R(sh);  // the histogram is no longer needed
     constexpr int S = Ring<true>::S;
     constexpr int CW = Ring<true>::CW;
+    constexpr int U = CW / kRT;
     const int nch = (g.nv + CW - 1) / CW;
+    // the r-th chunk streamed is chunk position r (forward) or nch - 1 - r (from the end)
+    auto pos_of = [&](int r) { return kRev ? nch - 1 - r : r; };
     const uint32_t base = *R.cnt;
     __syncthreads();
     if (tid == 0) {
         sh->sel[12] = -1;
-        for (int c = 0; c < nch && c < S; ++c) {
-            const uint32_t slot = (base + c) % S;
+        for (int r = 0; r < nch && r < S; ++r) {
+            const uint32_t slot = (base + r) % S;
+            const int c = pos_of(r);
             const int nvec = min(CW, g.nv - c * CW);
             fence_proxy_async_smem();
             mbar_arrive_expect_tx(&R.bar[slot], (uint32_t)nvec * 16u);
@@ -778,46 +785,55 @@ __device__ int tie_scan(RSmem* sh, const VerifyArgs& a, const RowGeo& g, int V, 
         }
         return c;
     };
-    for (int c = 0; c < issued; ++c) {
-        const uint32_t k = base + c;
+    for (int r = 0; r < issued; ++r) {
+        const uint32_t k = base + r;
         const uint32_t slot = k % S;
         if (!mbar_wait_bounded(&R.bar[slot], (k / S) & 1u)) {
             if (tid == 0) atomicOr(&a.ws->err, 1u);
         }
         if (found < 0) {
-            const int v0 = c * CW;
+            const int v0 = pos_of(r) * CW;
             const int nvec = min(CW, g.nv - v0);
-            uint32_t cu[CW / kRT];
+            uint32_t cu[U];
 #pragma unroll
-            for (int u = 0; u < CW / kRT; ++u) {
+            for (int u = 0; u < U; ++u) {
                 const int i = tid + u * kRT;
                 cu[u] = i < nvec ? count_in(R.slot(slot)[i], v0 + i) : 0u;
                 const uint32_t ws_ = warp_sum_u32(cu[u]);
                 if (lane == 0) sh->red32[u * kRW + wid] = ws_;
             }
             __syncthreads();
-            uint32_t tot[CW / kRT];
+            uint32_t tot[U];
             uint32_t all = 0;
 #pragma unroll
-            for (int u = 0; u < CW / kRT; ++u) {
+            for (int u = 0; u < U; ++u) {
                 tot[u] = 0;
                 for (int w = 0; w < kRW; ++w) tot[u] += sh->red32[u * kRW + w];
                 all += tot[u];
             }
             if (run + all >= need_total) {
-                // in this chunk: vectors are in index order u-major, then thread
+                // in this chunk, vectors are in index order u-major, then thread, then half;
+                // from the end the same order is walked backwards
                 uint32_t need = (uint32_t)(need_total - run);
 #pragma unroll
-                for (int u = 0; u < CW / kRT; ++u) {
+                for (int uu = 0; uu < U; ++uu) {
+                    const int u = kRev ? U - 1 - uu : uu;
                     if (need == 0u) break;
                     if (need > tot[u]) {
                         need -= tot[u];
                         continue;
                     }
                     const uint32_t incl = warp_incl_u32(cu[u]);
-                    uint32_t wpre = 0;
-                    for (int w = 0; w < wid; ++w) wpre += sh->red32[u * kRW + w];
-                    const uint32_t lo = wpre + incl - cu[u];
+                    uint32_t lo;  // occurrences of this u ahead of the thread in walk order
+                    if (!kRev) {
+                        uint32_t wpre = 0;
+                        for (int w = 0; w < wid; ++w) wpre += sh->red32[u * kRW + w];
+                        lo = wpre + incl - cu[u];
+                    } else {
+                        uint32_t wsuf = 0;
+                        for (int w = wid + 1; w < kRW; ++w) wsuf += sh->red32[u * kRW + w];
+                        lo = wsuf + (sh->red32[u * kRW + wid] - incl);
+                    }
                     if (cu[u] > 0 && lo < need && lo + cu[u] >= need) {
                         uint32_t k2 = need - lo;
                         const int v = v0 + tid + u * kRT;
@@ -825,7 +841,8 @@ __device__ int tie_scan(RSmem* sh, const VerifyArgs& a, const RowGeo& g, int V, 
                         const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
                         int e_found = -1;
 #pragma unroll
-                        for (int h = 0; h < 8; ++h) {
+                        for (int hh = 0; hh < 8; ++hh) {
+                            const int h = kRev ? 7 - hh : hh;
                             const uint32_t eq = bf2_eq(xs[h >> 1], kb2) & ((h & 1) ? 0xFFFF0000u : 0x0000FFFFu);
                             const int e = 8 * v + h - g.off;
                             if (e_found < 0 && eq && e >= 0 && e < V && --k2 == 0u) e_found = e;
@@ -841,8 +858,8 @@ __device__ int tie_scan(RSmem* sh, const VerifyArgs& a, const RowGeo& g, int V, 
         found = sh->sel[12];
         const bool more = found < 0 && issued < nch;
         if (tid == 0 && more) {
-            const int cn = issued;
-            const uint32_t slot2 = (base + cn) % S;
+            const uint32_t slot2 = (base + issued) % S;
+            const int cn = pos_of(issued);
             const int nv2 = min(CW, g.nv - cn * CW);
             fence_proxy_async_smem();
             mbar_arrive_expect_tx(&R.bar[slot2], (uint32_t)nv2 * 16u);
@@ -1377,7 +1394,14 @@ __device__ void process_row(RSmem* sh, const VerifyArgs& a, const TaskInfo& ti) 
 
     // ---- tie cut: occurrence number ntie of the boundary key in index order ------------
     {
-        const int tie = tie_scan(sh, a, g, V, ks.key, ntie);
+        // from the nearer end: occurrence ntie of count in index order is occurrence
+        // count - ntie + 1 from the end.  Only for a normal nonzero key, where equal values are
+        // equal bits, so the scan's matches are exactly the key's counted elements.
+        const uint32_t kexp = (key_bits(ks.key) >> 7) & 0xFFu;
+        const bool normal_key = kexp != 0u && kexp != 0xFFu;
+        const int tie = (!normal_key || 2 * ntie <= (unsigned long long)ks.count + 1ull)
+                            ? tie_scan<false>(sh, a, g, V, ks.key, ntie)
+                            : tie_scan<true>(sh, a, g, V, ks.key, (unsigned long long)ks.count - ntie + 1ull);
         if (tid == 0) {
             if (tie < 0) atomicOr(&a.ws->err, 16u);
             put_desc(a, ti, m, ks.key, tie, skept, 0, 0u);
