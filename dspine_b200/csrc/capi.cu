@@ -167,7 +167,7 @@ int dsv_verify_logits(int32_t batch, int32_t vocab, int32_t dtype, const int64_t
     a.racc = reinterpret_cast<unsigned int*>(base + dsv::verify_racc_offset(batch));
     a.wmass = reinterpret_cast<unsigned long long*>(base + dsv::verify_wmass_offset(batch));
     if (dsv::stream_supported(a, dtype))
-        return counted(dsv::launch_stream(a, (cudaStream_t)stream), 2);
+        return counted(dsv::launch_stream(a, (cudaStream_t)stream), 1);
     return counted(dsv::launch_verify(a, dtype, (cudaStream_t)stream), 1);
 }
 

@@ -20,8 +20,13 @@ struct WsHeader {
     unsigned int finalized;  // requests finalized in this launch
     unsigned int err;        // bit 0: bulk copy timed out; bit 1: bad row; bit 2: bad slot;
                              // bit 3: a selection found no boundary; bit 4: tie cut not found;
-                             // bit 5: shared-memory layout check of the row kernel failed
+                             // bit 5: shared-memory layout check of the row kernel failed;
+                             // bit 6: a chain task's request was never published (time limit)
+    unsigned int next2;      // row kernel: greedy-row counter
+    unsigned int ready_tail; // row kernel: requests published to the ready list
+    unsigned int chain_next; // row kernel: chain tasks taken
 };
+static_assert(sizeof(WsHeader) <= 64, "workspace header");
 
 // Descriptor of one processed logit row (streaming path): p_i = exp2c((l_i - m) c) * inv_s
 // for kept elements (key > kstar, or key == kstar and index <= tie_cut), else 0; greedy rows
@@ -48,7 +53,8 @@ constexpr inline size_t verify_gmax_offset(int B) {
     return verify_desc_offset(B) + (size_t)B * 16 * 2 * sizeof(RowDesc);
 }
 // [u64 x B x 16]: greedy rows' packed (max key << 32 | ~first index), reset after use
-// [u32 x B]: streaming path: requests in chain-kernel dispatch order (costliest first)
+// [u32 x B]: streaming path: the ready list (request + 1 per sampled request whose rows are
+// done, in completion order; reset after use)
 constexpr inline size_t verify_order_offset(int B) {
     return verify_gmax_offset(B) + (size_t)B * 16 * sizeof(unsigned long long);
 }

@@ -493,6 +493,9 @@ struct RSmem {
     alignas(16) uint32_t hist[kHCap];       // per-key counts / window candidates / count chunks
     alignas(16) uint4 ring[kRingS][kRingCW];  // streaming ring filled by bulk copies
     Plan plan;                     // task table (after this struct in shared memory)
+    int q_nchain;                  // task sources: chain tasks of the launch
+    int q_sel_empty, q_gr_empty;   //               selection / greedy queues exhausted
+    int q_kind, q_b;               //               this task's kind and chain request
     int task;
     int first_min;
     uint32_t nlist;
@@ -1427,190 +1430,6 @@ __device__ __forceinline__ RowDesc load_desc_cg(const RowDesc* p) {
     return d;
 }
 
-// After a row of sampled request b: the CTA that completes the request's rows decides the
-// chain (warp 0, one lane per step: draft s+1 against target row s) and leaves the accepted
-// length for the chain kernel.  Greedy requests are decided there from the packed maxima.
-__device__ void row_done(RSmem* sh, const VerifyArgs& a, int b) {
-    const int tid = threadIdx.x, lane = tid & 31;
-    const int cat = (int)(sh->plan.req[b] & 7u), cap = (int)(sh->plan.req[b] >> 3);
-    if (cat == kGreedy || a.cand == nullptr) return;
-    const unsigned nrows = (unsigned)(cap + (a.drf != nullptr ? cap - 1 : 0));
-    __syncthreads();
-    if (tid == 0) {
-        __threadfence();
-        const unsigned old = atomicAdd(&a.racc[2 * b], 1u);
-        sh->first_min = old == nrows - 1u;
-    }
-    __syncthreads();
-    if (!sh->first_min || tid >= 32) return;
-    __threadfence();
-    const bool onehot_q = a.drf == nullptr;
-    const uint16_t* tgt = reinterpret_cast<const uint16_t*>(a.tgt);
-    const uint16_t* drf = reinterpret_cast<const uint16_t*>(a.drf);
-    bool acc = false;
-    const int s = lane;
-    if (s < cap - 1) {
-        const long long tok = a.cand[b * kT + s + 1];
-        const bool valid = tok >= 0 && tok < a.V;
-        float p = 0.0f, q = 0.0f;
-        if (valid) {
-            const RowDesc dt = load_desc_cg(&a.desc[(b * kT + s) * 2 + 0]);
-            const long long tr = a.tgt_row[b] + s;
-            if (tr >= 0 && tr < a.tgt_rows) {
-                const uint32_t pb = tgt[tr * a.stride + tok];
-                p = row_prob(dt, bf(pb), pb, (int)tok);
-            }
-            if (onehot_q) {
-                q = 1.0f;
-            } else {
-                const RowDesc dd = load_desc_cg(&a.desc[(b * kT + s) * 2 + 1]);
-                const long long dr = a.drf_row[b] + s;
-                if (dr >= 0 && dr < a.drf_rows) {
-                    const uint32_t qb = drf[dr * a.stride + tok];
-                    q = row_prob(dd, bf(qb), qb, (int)tok);
-                }
-            }
-        }
-        acc = q > 0.0f && q <= 1.0f && __fmul_rn(a.u[b * 15 + s], q) < p;
-    }
-    const uint32_t rej = __ballot_sync(0xffffffffu, !acc) &
-                         ((cap - 1 >= 32) ? 0xffffffffu : ((1u << (cap - 1)) - 1u));
-    if (lane == 0) {
-        a.racc[2 * b + 1] = (unsigned)(rej ? __ffs(rej) - 1 : cap - 1);
-        a.racc[2 * b] = 0u;  // for the next launch
-    }
-}
-
-__global__ void __launch_bounds__(kRT, DSV_ROWS_MIN_CTAS) rows_kernel(VerifyArgs a) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    RSmem* sh = reinterpret_cast<RSmem*>(smem_raw);
-    const int tid = threadIdx.x, lane = tid & 31;
-    if (tid == 0) {
-        for (int i = 0; i < kRingS; ++i) mbar_init(&sh->ring_bar[i], 1);
-        for (int i = 0; i < kBigS; ++i) mbar_init(&sh->big_bar[i], 1);
-        fence_mbar_init();
-        sh->ring_cnt = 0;
-        sh->big_cnt = 0;
-        uint16_t* pre = reinterpret_cast<uint16_t*>(smem_raw + sizeof(RSmem));
-        sh->plan = Plan{pre, reinterpret_cast<uint8_t*>(pre + 3 * (a.B + 1)), a.B};
-    }
-#ifdef DSV_PROFILE
-    const unsigned long long trace_t0 = globaltimer_ns();
-#endif
-    __syncthreads();
-    build_plan(a, sh, kRWinK);
-    const int ntask = total_tasks(a, sh);
-    if (blockIdx.x == 0 && tid < 32) {
-        // chain-kernel dispatch order: large-k sampled requests (big kept sets), then small-k
-        // sampled requests, then greedy ones (a counting sort, request order inside a class)
-        int base_[3] = {0, 0, 0};
-        int tot[3] = {0, 0, 0};
-        for (int b0 = 0; b0 < a.B; b0 += 32) {
-            const int b = b0 + lane;
-            int g = -1;
-            if (b < a.B) {
-                const int cat = (int)(sh->plan.req[b] & 7u);
-                g = cat == kGreedy ? 2 : (a.top_k[b] > kRWinK ? 0 : 1);
-            }
-#pragma unroll
-            for (int q = 0; q < 3; ++q) tot[q] += __popc(__ballot_sync(0xffffffffu, g == q));
-        }
-        base_[1] = tot[0];
-        base_[2] = tot[0] + tot[1];
-        for (int b0 = 0; b0 < a.B; b0 += 32) {
-            const int b = b0 + lane;
-            int g = -1;
-            if (b < a.B) {
-                const int cat = (int)(sh->plan.req[b] & 7u);
-                g = cat == kGreedy ? 2 : (a.top_k[b] > kRWinK ? 0 : 1);
-            }
-#pragma unroll
-            for (int q = 0; q < 3; ++q) {
-                const unsigned m = __ballot_sync(0xffffffffu, g == q);
-                if (g == q) a.order[base_[q] + __popc(m & ((1u << lane) - 1u))] = (unsigned)b;
-                base_[q] += __popc(m);
-            }
-        }
-    }
-
-    // the first task of CTA i is task i; later ones come from the counter (offset by the grid)
-    bool first_task = true;
-    for (;;) {
-        __syncthreads();
-        if (tid == 0)
-            sh->task = first_task ? (int)blockIdx.x : (int)(gridDim.x + atomicAdd(&a.ws->next, 1u));
-        first_task = false;
-        __syncthreads();
-        const int t = sh->task;
-        if (t >= ntask) break;
-        const TaskInfo ti = decode_task(a, sh, t);
-#ifdef DSV_PROFILE
-        const unsigned long long trace_r0 = globaltimer_ns();
-#endif
-        process_row(sh, a, ti);
-        row_done(sh, a, ti.b);
-#ifdef DSV_PROFILE
-        // task trace: [256] entries used, [260 + 3 i] start, end, task | cat << 16 | sm << 24
-        if (tid == 0) {
-            const unsigned long long now = globaltimer_ns();
-            const unsigned long long i = atomicAdd(a.prof + 256, 1ull);
-            if (i < kTraceCap) {
-                unsigned long long* e = a.prof + 260 + 3 * i;
-                e[0] = trace_r0;
-                e[1] = now;
-                e[2] = (unsigned long long)t | ((unsigned long long)ti.cat << 16) |
-                       ((unsigned long long)smid() << 24) | ((unsigned long long)blockIdx.x << 40);
-            }
-        }
-#endif
-    }
-#ifdef DSV_PROFILE
-    if (tid == 0 && blockIdx.x < kTraceCtas) {  // per CTA: start and exit
-        unsigned long long* e = a.prof + 260 + 3 * kTraceCap + 2 * blockIdx.x;
-        e[0] = trace_t0;
-        e[1] = globaltimer_ns();
-    }
-#endif
-    // the last CTA out resets the row counter for the next launch
-    __syncthreads();
-    if (tid == 0) {
-        __threadfence();
-        const unsigned old = atomicAdd(&a.ws->exited, 1u);
-        if (old == gridDim.x - 1) {
-            a.ws->next = 0;
-            a.ws->exited = 0;
-            __threadfence();
-        }
-    }
-}
-
-int launch_rows_cta(VerifyArgs a, cudaStream_t stream) {
-    // fixed state + the batch's task table; the grid fills every SM at the occupancy this size
-    // allows (cached per device and size)
-    const size_t smem = sizeof(RSmem) + plan_bytes(a.B);
-    constexpr int kMaxDev = 64;
-    static int attr_done[kMaxDev] = {};
-    static size_t cached_smem[kMaxDev] = {};
-    static int cached_blocks[kMaxDev] = {};
-    int dev = 0;
-    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return kLaunchFailed;
-    if (!attr_done[dev]) {
-        if (cudaFuncSetAttribute(rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)(sizeof(RSmem) + plan_bytes(kMaxB))) != cudaSuccess)
-            return kLaunchFailed;
-        attr_done[dev] = 1;
-    }
-    if (cached_smem[dev] != smem) {
-        int per_sm = 0, sms = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rows_kernel, kRT, smem) != cudaSuccess || per_sm < 1)
-            return kLaunchFailed;
-        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return kLaunchFailed;
-        cached_smem[dev] = smem;
-        cached_blocks[dev] = per_sm * sms;
-    }
-    rows_kernel<<<cached_blocks[dev], kRT, smem, stream>>>(a);
-    return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
-}
 
 __device__ __forceinline__ uint64_t fix_w(float w) {
     if (!(w > 0.0f)) return 0;
@@ -1831,272 +1650,521 @@ __device__ __forceinline__ unsigned long long block_sum_u64(unsigned long long v
     return t;
 }
 
-__global__ void __launch_bounds__(kCT, 4) chain3_kernel(VerifyArgs a) {
-    __shared__ Chain3Smem shm;
-    Chain3Smem* sh = &shm;
+// One chain task: slice `rank` of sampled request b (its accepted length was decided by the row
+// pass).  Each task sums the exact residual mass of its slice of the rejected position's rows
+// and records per-warp masses; the task that completes the request's slices finds the bonus
+// token and writes the request's outputs (returns true).
+__device__ bool chain_task(const VerifyArgs& a, Chain3Smem* sh, int b, int rank) {
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-    const int b = (int)a.order[blockIdx.x / kCP], rank = blockIdx.x % kCP;
     const int cap = clamp_cap(a.caps[b]);
-    const float T = a.temperature[b];
-    const int kq = a.top_k[b];
-    const float c = log2e_over(T);
-    const bool greedy = is_greedy(T, kq, c);
-    const bool onehot_q = greedy || a.drf == nullptr;
     const uint16_t* tgt = reinterpret_cast<const uint16_t*>(a.tgt);
     const uint16_t* drf = reinterpret_cast<const uint16_t*>(a.drf);
-    bool finished = false;  // this CTA wrote the request's outputs
-#ifdef DSV_PROFILE
-    unsigned long long cp3 = globaltimer_ns();
-    if (tid == 0) atomicMin(a.prof + 80, cp3);  // kernel start (host presets it to ~0)
-#define CP3(cond, ph)                                                                          \
-    do {                                                                                       \
-        if ((cond) && tid == 0) {                                                              \
-            const unsigned long long n_ = globaltimer_ns();                                   \
-            atomicAdd(a.prof + 64 + (ph), n_ - cp3);    \
-            cp3 = n_;                                                                          \
-        }                                                                                      \
-    } while (0)
-#else
-#define CP3(cond, ph) \
-    do {              \
-    } while (0)
-#endif
-
-    if (greedy) {
-        // one-hot p at each target row's first argmax (packed by the row kernel), one-hot q at
-        // the drafted token: rank 0 decides alone and resets the packed maxima
-        if (rank == 0 && tid < 32) {
-            const int s = lane;
-            bool accp = false;
-            long long am = 0;
-            if (s < cap) {
-                const unsigned long long g = a.gmax[b * kT + s];
-                am = g ? (long long)(0xFFFFFFFFull - (g & 0xFFFFFFFFull)) : 0ll;
-            }
-            if (s < cap - 1) {
-                const long long tok = a.cand[b * kT + s + 1];
-                const bool valid = tok >= 0 && tok < a.V;
-                const float p = (valid && tok == am) ? 1.0f : 0.0f;
-                const float q = valid ? 1.0f : 0.0f;
-                accp = q > 0.0f && q <= 1.0f && __fmul_rn(a.u[b * 15 + s], q) < p;
-            }
-            const uint32_t rej = __ballot_sync(0xffffffffu, !accp) & ((1u << (cap - 1)) - 1u);
-            const int acc = rej ? __ffs(rej) - 1 : cap - 1;
-            const long long ga = __shfl_sync(0xffffffffu, am, acc);
-            __syncwarp();
-            if (s < cap) a.gmax[b * kT + s] = 0ull;
-            if (lane == 0) {
-                // the residual against a one-hot q is the same one-hot or empty (then the
-                // fallback to p): the draw is the argmax unless u is outside [0, 1)
-                const long long thr = scale_floor(a.uf[b], 1ull << kFixBits);
-                const long long bo = thr == -2 ? (long long)a.V - 1 : (thr < 0 ? 0ll : ga);
-                write_request(a, b, acc, bo);
-            }
+    const bool onehot_q = a.drf == nullptr;
+    bool finished = false;
+    (void)lane;
+    // the accepted length, decided by the row kernel when the request's rows completed
+    if (tid == 0) sh->acc = (int)__ldcg(&a.racc[2 * b + 1]);
+    __syncthreads();
+    const int acc = sh->acc;
+    const bool pure0 = acc == cap - 1;
+    const int V = a.V;
+    BonusRow r;
+    r.dt = load_desc_cg(&a.desc[(b * kT + acc) * 2 + 0]);
+    const long long tr = a.tgt_row[b] + acc;
+    r.prow = (tr >= 0 && tr < a.tgt_rows) ? tgt + tr * a.stride : nullptr;
+    r.has_dq = false;
+    r.qrow = nullptr;
+    r.onehot = -1;
+    if (!pure0) {
+        if (onehot_q) {
+            r.onehot = a.cand[b * kT + acc + 1];
+        } else {
+            r.dd = load_desc_cg(&a.desc[(b * kT + acc) * 2 + 1]);
+            r.has_dq = true;
+            const long long dr = a.drf_row[b] + acc;
+            if (dr >= 0 && dr < a.drf_rows) r.qrow = drf + dr * a.stride;
         }
-        finished = rank == 0;
-    } else {
-        // the accepted length, decided by the row kernel when the request's rows completed
-        if (tid == 0) sh->acc = (int)a.racc[2 * b + 1];
+    }
+    r.poff = r.prow ? (int)((reinterpret_cast<uintptr_t>(r.prow) & 15u) >> 1) : 0;
+    r.nvp = r.prow ? (V + r.poff + 7) >> 3 : 0;
+    r.qvec = r.qrow && (int)((reinterpret_cast<uintptr_t>(r.qrow) & 15u) >> 1) == r.poff;
+    // this CTA's slice of vectors, in tiles of kCTileV; tile masses go to the request's
+    // task-result area (kCP x kCMaxTiles u64)
+    const int per = (r.nvp + kCP - 1) / kCP;
+    const int v0 = min(rank * per, r.nvp), v1 = min(v0 + per, r.nvp);
+    unsigned long long* tmass = reinterpret_cast<unsigned long long*>(a.res) + (size_t)b * kT * 2;
+    auto slice_tiles = [&](int q, bool pure_) -> unsigned long long {
+        const int u0 = min(q * per, r.nvp), u1 = min(u0 + per, r.nvp);
+        unsigned long long tot = 0;
+        if (tid == 0 && u0 >= u1) tmass[q * kCMaxTiles] = 0ull;  // an empty slice
+        for (int t = 0; u0 + t * kCTileV < u1 && t < kCMaxTiles; ++t) {
+            const int tv0 = u0 + t * kCTileV, tv1 = min(tv0 + kCTileV, u1);
+            const unsigned long long m =
+                block_sum_u64(tile_mass(r, V, tv0, tv1, pure_, sh->queue[wid]), sh->wsum);
+            if (tid == 0) tmass[q * kCMaxTiles + t] = m;
+            // per-warp masses (still in shared memory) for the crossing search
+            if (tid < kCTW) a.wmass[((size_t)b * kCP + q) * kCTW + tid] = sh->wsum[tid];
+            tot += m;
+        }
+        return tot;
+    };
+    const unsigned long long mine = slice_tiles(rank, pure0);
+    (void)v0;
+    (void)v1;
+    (void)mine;
+    if (tid == 0) {
+        __threadfence();
+        const unsigned old = atomicAdd(&a.done[b], 1u);
+        sh->last = old == (unsigned)(kCP - 1);
+    }
+    __syncthreads();
+    if (sh->last) {
+        __threadfence();
+        bool pure = pure0;
+        if (tid < kCP) sh->slice[tid] = __ldcg(&tmass[tid * kCMaxTiles]);  // one tile per slice
         __syncthreads();
-        CP3(true, 0);
-        const int acc = sh->acc;
-        const bool pure0 = acc == cap - 1;
-        const int V = a.V;
-        BonusRow r;
-        r.dt = a.desc[(b * kT + acc) * 2 + 0];
-        const long long tr = a.tgt_row[b] + acc;
-        r.prow = (tr >= 0 && tr < a.tgt_rows) ? tgt + tr * a.stride : nullptr;
-        r.has_dq = false;
-        r.qrow = nullptr;
-        r.onehot = -1;
-        if (!pure0) {
-            if (onehot_q) {
-                r.onehot = a.cand[b * kT + acc + 1];
-            } else {
-                r.dd = a.desc[(b * kT + acc) * 2 + 1];
-                r.has_dq = true;
-                const long long dr = a.drf_row[b] + acc;
-                if (dr >= 0 && dr < a.drf_rows) r.qrow = drf + dr * a.stride;
+        unsigned long long M = 0;
+#pragma unroll
+        for (int q = 0; q < kCP; ++q) M += sh->slice[q];
+        if (!pure && M == 0) {
+            // zero residual mass: draw from p (this CTA recomputes every slice)
+            pure = true;
+            M = 0;
+            for (int q = 0; q < kCP; ++q) {
+                const unsigned long long t = slice_tiles(q, true);
+                if (tid == 0) sh->slice[q] = t;
+                M += t;
             }
-        }
-        r.poff = r.prow ? (int)((reinterpret_cast<uintptr_t>(r.prow) & 15u) >> 1) : 0;
-        r.nvp = r.prow ? (V + r.poff + 7) >> 3 : 0;
-        r.qvec = r.qrow && (int)((reinterpret_cast<uintptr_t>(r.qrow) & 15u) >> 1) == r.poff;
-        // this CTA's slice of vectors, in tiles of kCTileV; tile masses go to the request's
-        // task-result area (kCP x kCMaxTiles u64)
-        const int per = (r.nvp + kCP - 1) / kCP;
-        const int v0 = min(rank * per, r.nvp), v1 = min(v0 + per, r.nvp);
-        unsigned long long* tmass = reinterpret_cast<unsigned long long*>(a.res) + (size_t)b * kT * 2;
-        auto slice_tiles = [&](int q, bool pure_) -> unsigned long long {
-            const int u0 = min(q * per, r.nvp), u1 = min(u0 + per, r.nvp);
-            unsigned long long tot = 0;
-            if (tid == 0 && u0 >= u1) tmass[q * kCMaxTiles] = 0ull;  // an empty slice
-            for (int t = 0; u0 + t * kCTileV < u1 && t < kCMaxTiles; ++t) {
-                const int tv0 = u0 + t * kCTileV, tv1 = min(tv0 + kCTileV, u1);
-                const unsigned long long m =
-                    block_sum_u64(tile_mass(r, V, tv0, tv1, pure_, sh->queue[wid]), sh->wsum);
-                if (tid == 0) tmass[q * kCMaxTiles + t] = m;
-                // per-warp masses (still in shared memory) for the crossing search
-                if (tid < kCTW) a.wmass[((size_t)b * kCP + q) * kCTW + tid] = sh->wsum[tid];
-                tot += m;
-            }
-            return tot;
-        };
-        const unsigned long long mine = slice_tiles(rank, pure0);
-        (void)v0;
-        (void)v1;
-        CP3(true, 1);
-        (void)mine;
-        if (tid == 0) {
-            __threadfence();
-            const unsigned old = atomicAdd(&a.done[b], 1u);
-            sh->last = old == (unsigned)(kCP - 1);
-        }
-        __syncthreads();
-        if (sh->last) {
-            __threadfence();
-            bool pure = pure0;
-            if (tid < kCP) sh->slice[tid] = __ldcg(&tmass[tid * kCMaxTiles]);  // one tile per slice
             __syncthreads();
-            unsigned long long M = 0;
-#pragma unroll
-            for (int q = 0; q < kCP; ++q) M += sh->slice[q];
-            if (!pure && M == 0) {
-                // zero residual mass: draw from p (this CTA recomputes every slice)
-                pure = true;
-                M = 0;
-                for (int q = 0; q < kCP; ++q) {
-                    const unsigned long long t = slice_tiles(q, true);
-                    if (tid == 0) sh->slice[q] = t;
-                    M += t;
+        }
+        const long long thr = scale_floor(a.uf[b], M);
+        long long bonus = (long long)V - 1;
+        if (thr == -1) {
+            bonus = 0;  // u < 0: the first running sum already exceeds it
+        } else if (thr != -2 && M != 0) {
+            // the crossing slice and tile from the totals, then the tile element by element
+            long long base = 0;
+            int qs = -1, tq = -1;
+            for (int q = 0; q < kCP && qs < 0; ++q) {
+                const long long t = (long long)sh->slice[q];
+                if (base + t > thr) {
+                    qs = q;
+                    tq = 0;  // one tile per slice (kCMaxTiles == 1)
+                } else {
+                    base += t;
                 }
-                __syncthreads();
             }
-            CP3(true, 2);
-            const long long thr = scale_floor(a.uf[b], M);
-            long long bonus = (long long)V - 1;
-            if (thr == -1) {
-                bonus = 0;  // u < 0: the first running sum already exceeds it
-            } else if (thr != -2 && M != 0) {
-                // the crossing slice and tile from the totals, then the tile element by element
-                long long base = 0;
-                int qs = -1, tq = -1;
-                for (int q = 0; q < kCP && qs < 0; ++q) {
-                    const long long t = (long long)sh->slice[q];
-                    if (base + t > thr) {
-                        qs = q;
-                        tq = 0;  // one tile per slice (kCMaxTiles == 1)
-                    } else {
-                        base += t;
+            if (qs >= 0 && tq >= 0) {
+                const int u0 = min(qs * per, r.nvp), u1 = min(u0 + per, r.nvp);
+                const int tv0 = u0 + tq * kCTileV, tv1 = min(tv0 + kCTileV, u1);
+                // the crossing warp from the slice's per-warp masses (warp w owns vectors
+                // tv0 + 128 w ..., so warp order is index order), then that warp alone:
+                // lane masses (4 consecutive vectors per lane), a warp scan, and the lane
+                // holding the crossing walks its 32 elements
+                const unsigned long long* wm = a.wmass + ((size_t)b * kCP + qs) * kCTW;
+                unsigned long long wv[kCTW];
+#pragma unroll
+                for (int w = 0; w < kCTW; ++w) wv[w] = __ldcg(&wm[w]);  // independent loads
+                int ws_ = kCTW - 1;
+#pragma unroll
+                for (int w = 0; w < kCTW; ++w) {
+                    const long long m_ = (long long)wv[w];
+                    if (base + m_ > thr) {
+                        ws_ = w;
+                        break;
                     }
+                    base += m_;
                 }
-                if (qs >= 0 && tq >= 0) {
-                    const int u0 = min(qs * per, r.nvp), u1 = min(u0 + per, r.nvp);
-                    const int tv0 = u0 + tq * kCTileV, tv1 = min(tv0 + kCTileV, u1);
-                    // the crossing warp from the slice's per-warp masses (warp w owns vectors
-                    // tv0 + 128 w ..., so warp order is index order), then that warp alone:
-                    // lane masses (4 consecutive vectors per lane), a warp scan, and the lane
-                    // holding the crossing walks its 32 elements
-                    const unsigned long long* wm = a.wmass + ((size_t)b * kCP + qs) * kCTW;
-                    unsigned long long wv[kCTW];
+                if (tid == 0) sh->bonus = -1;
+                __syncthreads();
+                {
+                    // the crossing warp's 128 vectors (1024 elements) by the whole CTA:
+                    // thread t takes elements [4 t, 4 t + 4) of the region (half of
+                    // vector t / 2), a block scan of the thread masses finds the thread,
+                    // and it walks its four elements
+                    const int v = tv0 + 128 * ws_ + (tid >> 1);
+                    uint4 xa = make_uint4(0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u);
+                    uint4 ya = xa;
+                    if (v < tv1) load8(r, v, pure, xa, ya);
+                    unsigned long long f4[4];
+                    unsigned long long own = 0;
 #pragma unroll
-                    for (int w = 0; w < kCTW; ++w) wv[w] = __ldcg(&wm[w]);  // independent loads
-                    int ws_ = kCTW - 1;
-#pragma unroll
-                    for (int w = 0; w < kCTW; ++w) {
-                        const long long m_ = (long long)wv[w];
-                        if (base + m_ > thr) {
-                            ws_ = w;
-                            break;
+                    for (int hh = 0; hh < 4; ++hh) {
+                        const int h = 4 * (tid & 1) + hh;
+                        const int i = 8 * v + h - r.poff;
+                        unsigned long long f = 0;
+                        if (v < tv1 && i >= 0 && i < V && kept_in(r.dt, half16(xa, h), i)) {
+                            uint32_t qb = half16(ya, h);
+                            if (!pure && r.has_dq && !r.qvec)
+                                qb = r.qrow ? (uint32_t)__ldg(r.qrow + i) : 0xFF80u;
+                            f = resid_kept(r, pure, half16(xa, h), qb, i);
                         }
-                        base += m_;
+                        f4[hh] = f;
+                        own += f;
                     }
-                    if (tid == 0) sh->bonus = -1;
+                    const unsigned long long incl = warp_incl_u64(own);
+                    if (lane == 31) sh->wsum[wid] = incl;
                     __syncthreads();
-                    {
-                        // the crossing warp's 128 vectors (1024 elements) by the whole CTA:
-                        // thread t takes elements [4 t, 4 t + 4) of the region (half of
-                        // vector t / 2), a block scan of the thread masses finds the thread,
-                        // and it walks its four elements
-                        const int v = tv0 + 128 * ws_ + (tid >> 1);
-                        uint4 xa = make_uint4(0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u);
-                        uint4 ya = xa;
-                        if (v < tv1) load8(r, v, pure, xa, ya);
-                        unsigned long long f4[4];
-                        unsigned long long own = 0;
+                    unsigned long long wpre = 0;
+                    for (int w = 0; w < wid; ++w) wpre += sh->wsum[w];
+                    long long run = base + (long long)(wpre + incl - own);
+                    if (run <= thr && run + (long long)own > thr) {
 #pragma unroll
                         for (int hh = 0; hh < 4; ++hh) {
-                            const int h = 4 * (tid & 1) + hh;
-                            const int i = 8 * v + h - r.poff;
-                            unsigned long long f = 0;
-                            if (v < tv1 && i >= 0 && i < V && kept_in(r.dt, half16(xa, h), i)) {
-                                uint32_t qb = half16(ya, h);
-                                if (!pure && r.has_dq && !r.qvec)
-                                    qb = r.qrow ? (uint32_t)__ldg(r.qrow + i) : 0xFF80u;
-                                f = resid_kept(r, pure, half16(xa, h), qb, i);
-                            }
-                            f4[hh] = f;
-                            own += f;
-                        }
-                        const unsigned long long incl = warp_incl_u64(own);
-                        if (lane == 31) sh->wsum[wid] = incl;
-                        __syncthreads();
-                        unsigned long long wpre = 0;
-                        for (int w = 0; w < wid; ++w) wpre += sh->wsum[w];
-                        long long run = base + (long long)(wpre + incl - own);
-                        if (run <= thr && run + (long long)own > thr) {
-#pragma unroll
-                            for (int hh = 0; hh < 4; ++hh) {
-                                run += (long long)f4[hh];
-                                if (run > thr) {
-                                    sh->bonus = 8 * v + 4 * (tid & 1) + hh - r.poff;
-                                    break;
-                                }
+                            run += (long long)f4[hh];
+                            if (run > thr) {
+                                sh->bonus = 8 * v + 4 * (tid & 1) + hh - r.poff;
+                                break;
                             }
                         }
                     }
-                    __syncthreads();
-                    if (sh->bonus >= 0) bonus = sh->bonus;
+                }
+                __syncthreads();
+                if (sh->bonus >= 0) bonus = sh->bonus;
+            }
+        }
+#ifdef DSV_PROFILE
+        if (tid == 0) atomicAdd(a.prof + 64 + 15, 1ull);
+        if (tid == 0 && b < 128) a.prof[128 + b] = globaltimer_ns();
+#endif
+        if (tid == 0) {
+            write_request(a, b, acc, bonus);
+            a.done[b] = 0u;
+        }
+        finished = true;
+    }
+    return finished;
+}
+
+// Greedy request b once all its rows are done (warp 0): one-hot p at each target row's first
+// argmax (packed by the row pass), one-hot q at the drafted token; writes the outputs and
+// resets the packed maxima.
+__device__ void greedy_decide(const VerifyArgs& a, int b, int cap) {
+    const int lane = threadIdx.x & 31;
+    const int s = lane;
+    bool accp = false;
+    long long am = 0;
+    if (s < cap) {
+        const unsigned long long g = __ldcg(&a.gmax[b * kT + s]);
+        am = g ? (long long)(0xFFFFFFFFull - (g & 0xFFFFFFFFull)) : 0ll;
+    }
+    if (s < cap - 1) {
+        const long long tok = a.cand[b * kT + s + 1];
+        const bool valid = tok >= 0 && tok < a.V;
+        const float p = (valid && tok == am) ? 1.0f : 0.0f;
+        const float q = valid ? 1.0f : 0.0f;
+        accp = q > 0.0f && q <= 1.0f && __fmul_rn(a.u[b * 15 + s], q) < p;
+    }
+    const uint32_t rej = __ballot_sync(0xffffffffu, !accp) & ((1u << (cap - 1)) - 1u);
+    const int acc = rej ? __ffs(rej) - 1 : cap - 1;
+    const long long ga = __shfl_sync(0xffffffffu, am, acc);
+    __syncwarp();
+    if (s < cap) a.gmax[b * kT + s] = 0ull;
+    if (lane == 0) {
+        // the residual against a one-hot q is the same one-hot or empty (then the
+        // fallback to p): the draw is the argmax unless u is outside [0, 1)
+        const long long thr = scale_floor(a.uf[b], 1ull << kFixBits);
+        const long long bo = thr == -2 ? (long long)a.V - 1 : (thr < 0 ? 0ll : ga);
+        write_request(a, b, acc, bo);
+    }
+}
+
+// After this CTA wrote the outputs of a request: the CTA that finishes the last request packs
+// tokens and KV slots (all threads of the CTA call it).
+__device__ void finalize_request(const VerifyArgs& a, Chain3Smem* sh) {
+    const int tid = threadIdx.x;
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        const unsigned old = atomicAdd(&a.ws->finalized, 1u);
+        sh->flag = old == (unsigned)(a.B - 1);
+    }
+    __syncthreads();
+    if (sh->flag) {
+        __threadfence();
+        if (a.tok_out != nullptr) compact_all_nt<kCT>(a, sh->red_a, sh->red_b);
+        __syncthreads();
+        if (tid == 0) a.ws->finalized = 0;
+    }
+    __syncthreads();
+}
+
+// After a row of request b: the CTA that completes the request's rows decides its chain
+// (warp 0, one lane per step: draft s+1 against target row s).  A greedy request is finished
+// right there (returns true: this CTA wrote its outputs); a sampled request leaves its
+// accepted length and joins the ready list, from which its chain tasks are taken.
+__device__ bool row_done(RSmem* sh, const VerifyArgs& a, int b) {
+    const int tid = threadIdx.x, lane = tid & 31;
+    if (a.cand == nullptr) return false;
+    const int cat = (int)(sh->plan.req[b] & 7u), cap = (int)(sh->plan.req[b] >> 3);
+    const bool greedy = cat == kGreedy;
+    const unsigned nrows = (unsigned)(cap + (!greedy && a.drf != nullptr ? cap - 1 : 0));
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        const unsigned old = atomicAdd(&a.racc[2 * b], 1u);
+        sh->first_min = old == nrows - 1u;
+    }
+    __syncthreads();
+    if (!sh->first_min) return false;
+    if (greedy) {
+        __threadfence();
+        if (tid < 32) {
+            greedy_decide(a, b, cap);
+            if (lane == 0) a.racc[2 * b] = 0u;  // for the next launch
+        }
+        return true;
+    }
+    if (tid >= 32) return false;
+    __threadfence();
+    const bool onehot_q = a.drf == nullptr;
+    const uint16_t* tgt = reinterpret_cast<const uint16_t*>(a.tgt);
+    const uint16_t* drf = reinterpret_cast<const uint16_t*>(a.drf);
+    bool acc = false;
+    const int s = lane;
+    if (s < cap - 1) {
+        const long long tok = a.cand[b * kT + s + 1];
+        const bool valid = tok >= 0 && tok < a.V;
+        float p = 0.0f, q = 0.0f;
+        if (valid) {
+            const RowDesc dt = load_desc_cg(&a.desc[(b * kT + s) * 2 + 0]);
+            const long long tr = a.tgt_row[b] + s;
+            if (tr >= 0 && tr < a.tgt_rows) {
+                const uint32_t pb = tgt[tr * a.stride + tok];
+                p = row_prob(dt, bf(pb), pb, (int)tok);
+            }
+            if (onehot_q) {
+                q = 1.0f;
+            } else {
+                const RowDesc dd = load_desc_cg(&a.desc[(b * kT + s) * 2 + 1]);
+                const long long dr = a.drf_row[b] + s;
+                if (dr >= 0 && dr < a.drf_rows) {
+                    const uint32_t qb = drf[dr * a.stride + tok];
+                    q = row_prob(dd, bf(qb), qb, (int)tok);
                 }
             }
-            CP3(true, 3);
-#ifdef DSV_PROFILE
-            if (tid == 0) atomicAdd(a.prof + 64 + 15, 1ull);
-            if (tid == 0 && b < 128) a.prof[128 + b] = globaltimer_ns();
-#endif
-            if (tid == 0) {
-                write_request(a, b, acc, bonus);
-                a.done[b] = 0u;
+        }
+        acc = q > 0.0f && q <= 1.0f && __fmul_rn(a.u[b * 15 + s], q) < p;
+    }
+    const uint32_t rej = __ballot_sync(0xffffffffu, !acc) &
+                         ((cap - 1 >= 32) ? 0xffffffffu : ((1u << (cap - 1)) - 1u));
+    if (lane == 0) {
+        a.racc[2 * b + 1] = (unsigned)(rej ? __ffs(rej) - 1 : cap - 1);
+        a.racc[2 * b] = 0u;  // for the next launch
+        __threadfence();
+        const unsigned pos = atomicAdd(&a.ws->ready_tail, 1u);
+        a.order[pos] = (unsigned)b + 1u;  // nonzero: published
+    }
+    return false;
+}
+
+// Request index of ready-list entry qi (thread 0; waits, bounded, for the entry to be
+// published), or -1 after the time limit (error bit 6).
+__device__ int wait_ready(const VerifyArgs& a, int qi) {
+    volatile unsigned* e = a.order + qi;
+    unsigned v = *e;
+    if (v == 0u) {
+        const uint64_t t0 = globaltimer_ns();
+        while ((v = *e) == 0u) {
+            if (globaltimer_ns() - t0 > 2000000000ull) {
+                atomicOr(&a.ws->err, 64u);
+                return -1;
             }
-            finished = true;
+            __nanosleep(256);
         }
     }
+    __threadfence();
+    return (int)v - 1;
+}
 
-    // ---- completion: the last request packs tokens and KV slots ---------------------------
-    if (finished) {
+__global__ void __launch_bounds__(kRT, DSV_ROWS_MIN_CTAS) rows_kernel(VerifyArgs a) {
+    extern __shared__ __align__(16) unsigned char smem_raw[];
+    RSmem* sh = reinterpret_cast<RSmem*>(smem_raw);
+    const int tid = threadIdx.x, lane = tid & 31;
+    if (tid == 0) {
+        for (int i = 0; i < kRingS; ++i) mbar_init(&sh->ring_bar[i], 1);
+        for (int i = 0; i < kBigS; ++i) mbar_init(&sh->big_bar[i], 1);
+        fence_mbar_init();
+        sh->ring_cnt = 0;
+        sh->big_cnt = 0;
+        uint16_t* pre = reinterpret_cast<uint16_t*>(smem_raw + sizeof(RSmem));
+        sh->plan = Plan{pre, reinterpret_cast<uint8_t*>(pre + 3 * (a.B + 1)), a.B};
+    }
+#ifdef DSV_PROFILE
+    const unsigned long long trace_t0 = globaltimer_ns();
+#endif
+    __syncthreads();
+    build_plan(a, sh, kRWinK);
+    // Task sources, in priority order: (1) rows with selection work (tasks [0, nsel): the
+    // ALU-heavy ones, first so they spread over every CTA), (2) greedy rows (tasks [nsel,
+    // ntask): memory-bound, they run beside the last selection rows), (3) chain tasks of
+    // requests whose rows are done (kCP slices per sampled request, from the ready list),
+    // (4) chain tasks whose request is not ready yet (the CTA waits: every selection row has
+    // been taken by then, so it will be).
+    const int nsel = (int)(sh->plan.pre(0, a.B) + sh->plan.pre(1, a.B));
+    const int ntask = total_tasks(a, sh);
+    if (tid < 32) {
+        int ns = 0;
+        for (int b0 = 0; b0 < a.B; b0 += 32) {
+            const int b = b0 + lane;
+            ns += __popc(__ballot_sync(0xffffffffu, b < a.B && (sh->plan.req[b] & 7u) != (unsigned)kGreedy));
+        }
+        if (lane == 0) {
+            sh->q_nchain = a.cand != nullptr ? ns * kCP : 0;
+            sh->q_sel_empty = 0;
+            sh->q_gr_empty = 0;
+        }
+    }
+    static_assert(sizeof(Chain3Smem) <= sizeof(uint32_t) * kHCap && alignof(Chain3Smem) <= 16,
+                  "chain tasks use the histogram area");
+    Chain3Smem* csh = reinterpret_cast<Chain3Smem*>(sh->hist);  // idle between tasks
+    bool first_task = true;
+    for (;;) {
         __syncthreads();
         if (tid == 0) {
-            __threadfence();
-            const unsigned old = atomicAdd(&a.ws->finalized, 1u);
-            sh->flag = old == (unsigned)(a.B - 1);
+            const int nchain = sh->q_nchain;
+            int kind = 0, t = -1;
+            if (first_task && (int)blockIdx.x < nsel) {
+                kind = 1;
+                t = (int)blockIdx.x;  // the first task of CTA i is selection row i
+            }
+            if (!kind && !sh->q_sel_empty) {
+                const int x = (int)(gridDim.x + atomicAdd(&a.ws->next, 1u));
+                if (x < nsel) {
+                    kind = 1;
+                    t = x;
+                } else {
+                    sh->q_sel_empty = 1;
+                }
+            }
+            if (!kind && !sh->q_gr_empty) {
+                const int x = (int)atomicAdd(&a.ws->next2, 1u);
+                if (nsel + x < ntask) {
+                    kind = 1;
+                    t = nsel + x;
+                } else {
+                    sh->q_gr_empty = 1;
+                }
+            }
+            if (!kind && nchain > 0) {
+                const unsigned ready = *(volatile unsigned*)&a.ws->ready_tail * (unsigned)kCP;
+                if (*(volatile unsigned*)&a.ws->chain_next < ready) {
+                    const int j = (int)atomicAdd(&a.ws->chain_next, 1u);
+                    if (j < nchain) {
+                        kind = 2;
+                        t = j;
+                    }
+                }
+            }
+            if (!kind && nchain > 0) {
+                const int j = (int)atomicAdd(&a.ws->chain_next, 1u);
+                if (j < nchain) {
+                    kind = 2;
+                    t = j;
+                }
+            }
+            if (kind == 2) {
+                const int b = wait_ready(a, t / kCP);
+                if (b < 0) kind = 3;  // gave up: the request stays unfinished (error bit 6)
+                sh->q_b = b;
+            }
+            sh->task = t;
+            sh->q_kind = kind;
         }
+        first_task = false;
         __syncthreads();
-        if (sh->flag) {
+        const int t = sh->task, kind = sh->q_kind;
+        if (kind == 0) break;
+        if (kind == 3) continue;
+#ifdef DSV_PROFILE
+        const unsigned long long trace_r0 = globaltimer_ns();
+        int trace_cat = 8;
+#endif
+        bool finished;
+        if (kind == 1) {
+            const TaskInfo ti = decode_task(a, sh, t);
+#ifdef DSV_PROFILE
+            trace_cat = ti.cat;
+#endif
+            process_row(sh, a, ti);
+            finished = row_done(sh, a, ti.b);
+        } else {
+            finished = chain_task(a, csh, sh->q_b, t % kCP);
+        }
+        if (finished) finalize_request(a, csh);
+#ifdef DSV_PROFILE
+        // task trace: [256] entries used, [260 + 3 i] start, end, task | cat << 16 | sm << 24
+        // (cat 8: a chain task)
+        if (tid == 0) {
+            const unsigned long long now = globaltimer_ns();
+            const unsigned long long i = atomicAdd(a.prof + 256, 1ull);
+            if (i < kTraceCap) {
+                unsigned long long* e = a.prof + 260 + 3 * i;
+                e[0] = trace_r0;
+                e[1] = now;
+                e[2] = (unsigned long long)t | ((unsigned long long)trace_cat << 16) |
+                       ((unsigned long long)smid() << 24) | ((unsigned long long)blockIdx.x << 40);
+            }
+        }
+#endif
+    }
+#ifdef DSV_PROFILE
+    if (tid == 0 && blockIdx.x < kTraceCtas) {  // per CTA: start and exit
+        unsigned long long* e = a.prof + 260 + 3 * kTraceCap + 2 * blockIdx.x;
+        e[0] = trace_t0;
+        e[1] = globaltimer_ns();
+    }
+#endif
+    // the last CTA out resets the counters and the ready list for the next launch
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        const unsigned old = atomicAdd(&a.ws->exited, 1u);
+        if (old == gridDim.x - 1) {
             __threadfence();
-            if (a.tok_out != nullptr) compact_all_nt<kCT>(a, sh->red_a, sh->red_b);
-            __syncthreads();
-            if (tid == 0) a.ws->finalized = 0;
+            const unsigned nready = a.ws->ready_tail;
+            for (unsigned i = 0; i < nready && i < (unsigned)a.B; ++i) a.order[i] = 0u;
+            a.ws->next = 0;
+            a.ws->next2 = 0;
+            a.ws->ready_tail = 0;
+            a.ws->chain_next = 0;
+            a.ws->exited = 0;
+            __threadfence();
         }
     }
+}
+
+int launch_rows_cta(VerifyArgs a, cudaStream_t stream) {
+    // fixed state + the batch's task table; the grid fills every SM at the occupancy this size
+    // allows (cached per device and size)
+    const size_t smem = sizeof(RSmem) + plan_bytes(a.B);
+    constexpr int kMaxDev = 64;
+    static int attr_done[kMaxDev] = {};
+    static size_t cached_smem[kMaxDev] = {};
+    static int cached_blocks[kMaxDev] = {};
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return kLaunchFailed;
+    if (!attr_done[dev]) {
+        if (cudaFuncSetAttribute(rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 (int)(sizeof(RSmem) + plan_bytes(kMaxB))) != cudaSuccess)
+            return kLaunchFailed;
+        attr_done[dev] = 1;
+    }
+    if (cached_smem[dev] != smem) {
+        int per_sm = 0, sms = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rows_kernel, kRT, smem) != cudaSuccess || per_sm < 1)
+            return kLaunchFailed;
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return kLaunchFailed;
+        cached_smem[dev] = smem;
+        cached_blocks[dev] = per_sm * sms;
+    }
+    rows_kernel<<<cached_blocks[dev], kRT, smem, stream>>>(a);
+    return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
 }
 
 // ---------------------------------------------------------------------------------------
 // launcher
 
-int launch_chain(VerifyArgs a, cudaStream_t stream) {
-    chain3_kernel<<<a.B * kCP, kCT, 0, stream>>>(a);
-    return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
-}
 
 // ---------------------------------------------------------------------------------------
 // dense target probabilities from the row descriptors (runtime/worker.py:440-508 output)
@@ -2144,9 +2212,7 @@ int launch_target_probs(VerifyArgs a, float* out, cudaStream_t stream) {
 }
 
 int launch_stream(VerifyArgs a, cudaStream_t stream) {
-    const int st_ = st::launch_rows_cta(a, stream);
-    if (st_ != kOk) return st_;
-    return st::launch_chain(a, stream);
+    return st::launch_rows_cta(a, stream);  // rows and chain tasks in one persistent launch
 }
 
 }  // namespace dsv
