@@ -26,7 +26,7 @@ inline int counted(int status, int kernels) {
 // module image: the driver places it when the library's kernels are loaded on a device, and it
 // starts zeroed.  Its address is looked up once per device and cached.
 constexpr int kNoAllocMaxBatch = 256;
-constexpr size_t kNoAllocBytes = dsv::verify_workspace_bytes(kNoAllocMaxBatch);
+constexpr size_t kNoAllocBytes = dsv::verify_base_bytes(kNoAllocMaxBatch);  // no split rows
 __device__ __align__(256) unsigned char g_noalloc_ws[kNoAllocBytes];
 
 constexpr int kMaxDevices = 64;
@@ -117,7 +117,8 @@ int dsv_verify_logits(int32_t batch, int32_t vocab, int32_t dtype, const int64_t
                     !compact->kept_slots || !compact->offsets || !compact->freed_slots ||
                     !compact->freed_offsets))
         return DSV_BAD_POINTER;
-    if (workspace_bytes < dsv::verify_workspace_bytes(batch)) return DSV_WORKSPACE_TOO_SMALL;
+    // the split-row region is optional: without it no row is split
+    if (workspace_bytes < dsv::verify_base_bytes(batch)) return DSV_WORKSPACE_TOO_SMALL;
     if (!aligned(workspace, 16)) return DSV_BAD_ALIGNMENT;
     const size_t esz = dtype == DSV_BF16 ? 2 : 4;
     if (!aligned(target_logits, esz) || (draft_logits && !aligned(draft_logits, esz)))
@@ -166,6 +167,11 @@ int dsv_verify_logits(int32_t batch, int32_t vocab, int32_t dtype, const int64_t
     a.order = reinterpret_cast<unsigned int*>(base + dsv::verify_order_offset(batch));
     a.racc = reinterpret_cast<unsigned int*>(base + dsv::verify_racc_offset(batch));
     a.wmass = reinterpret_cast<unsigned long long*>(base + dsv::verify_wmass_offset(batch));
+    if (workspace_bytes >= dsv::verify_workspace_bytes(batch)) {
+        a.split = reinterpret_cast<unsigned char*>(base + dsv::verify_split_offset(batch));
+        a.split_flag = reinterpret_cast<unsigned int*>(a.split + (size_t)dsv::kSplitCap * dsv::kSplitSlotBytes);
+        a.split_cap = dsv::kSplitCap;
+    }
     if (dsv::stream_supported(a, dtype))
         return counted(dsv::launch_stream(a, (cudaStream_t)stream), 1);
     return counted(dsv::launch_verify(a, dtype, (cudaStream_t)stream), 1);
@@ -397,7 +403,7 @@ int dsv_target_probs(int64_t rows, int32_t vocab, int32_t rows_per_request, cons
     const long long nreq = rows / rows_per_request;
     const int chunk = 1024;
     const int wsb = (int)(nreq < chunk ? nreq : chunk);
-    if (workspace_bytes < dsv::verify_workspace_bytes(wsb)) return DSV_WORKSPACE_TOO_SMALL;
+    if (workspace_bytes < dsv::verify_base_bytes(wsb)) return DSV_WORKSPACE_TOO_SMALL;
     char* base = reinterpret_cast<char*>(workspace);
     int launched = 0;
     for (long long r0 = 0; r0 < nreq; r0 += chunk) {
@@ -524,7 +530,7 @@ int dsv_verify_logits_noalloc(int32_t batch, int32_t vocab, int32_t dtype,
     if (batch == 0) return DSV_OK;
     char* ws = static_cast<char*>(noalloc_scratch());
     if (ws == nullptr) return DSV_LAUNCH_FAILED;
-    const size_t used = dsv::verify_workspace_bytes(batch);
+    const size_t used = dsv::verify_base_bytes(batch);  // scratch without split rows
     cudaStream_t st = (cudaStream_t)stream;
     // counters, the error word and the greedy maxima must start at zero; clearing the whole
     // used prefix also drops whatever an earlier call that failed on the device left behind

@@ -76,8 +76,18 @@ constexpr size_t kProfBytes = 2048;
 constexpr inline size_t verify_prof_offset(int B) {
     return verify_wmass_offset(B) + (size_t)B * 32 * 8 * 8;
 }
-constexpr inline size_t verify_workspace_bytes(int B) {
+// everything above: the workspace without split rows (the no-allocation entry point's scratch)
+constexpr inline size_t verify_base_bytes(int B) {
     return verify_prof_offset(B) + kProfBytes;
+}
+// Split rows (streaming path): nucleus rows beyond the first wave of the row kernel are
+// processed as two halves by two CTAs; the first half publishes its per-key histogram here.
+// [kSplitCap slots of kSplitSlotBytes][u32 flag x kSplitCap]
+constexpr int kSplitCap = 256;
+constexpr size_t kSplitSlotBytes = 8192 * 4 + 16 + 512 * 2 + 48;  // counts, meta, band, pad
+constexpr inline size_t verify_split_offset(int B) { return verify_base_bytes(B); }
+constexpr inline size_t verify_workspace_bytes(int B) {
+    return verify_split_offset(B) + (size_t)kSplitCap * (kSplitSlotBytes + 4);
 }
 
 struct VerifyArgs {
@@ -123,6 +133,9 @@ struct VerifyArgs {
     unsigned int* order;       // [B] streaming path: chain-kernel dispatch order
     unsigned int* racc;        // [B,2] streaming path: rows finished, accepted length
     unsigned long long* wmass; // [B,32,8] streaming path: residual mass per slice and warp
+    unsigned char* split;      // split-row slots (kSplitCap x kSplitSlotBytes) or null
+    unsigned int* split_flag;  // [kSplitCap]: 1 once the first half is published
+    int split_cap;             // rows that may be split in this launch (0: none)
     // standalone target probabilities (dsv_target_probs): caps == null means every request
     // has cap_all rows, tgt_row == null means request b starts at row b * row_step, cand ==
     // null skips the chain decision

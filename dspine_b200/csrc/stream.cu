@@ -215,6 +215,8 @@ struct TaskInfo {
     long long row;     // row index in its tensor (-1: invalid)
     float T, p, c;
     int k;
+    int half;          // -1: the whole row; 0 / 1: first / second half of a split row
+    int slot;          // split rows: the slot the first half publishes to
 };
 
 __device__ __forceinline__ int clamp_cap(int c) { return c < 1 ? 1 : (c > kT ? kT : c); }
@@ -320,6 +322,8 @@ __device__ TaskInfo decode_task(const VerifyArgs& a, const Sm* sh, int t) {
     ti.k = a.top_k[ti.b];
     ti.p = a.top_p[ti.b];
     ti.c = log2e_over(ti.T);
+    ti.half = -1;
+    ti.slot = -1;
     return ti;
 }
 
@@ -580,19 +584,22 @@ struct Ring {
 // handles vectors tid and tid + kRT of each chunk.  All threads must call it.
 template <bool kBig = false, typename F>
 __device__ __forceinline__ void stream_row(RSmem* sh, const VerifyArgs& a, const RowGeo& g, int V,
-                                           F&& fn) {
+                                           F&& fn, int vb = 0, int ve = -1) {
+    // vectors [vb, ve) of the row (default: all); fn sees row-global vector indices
     const Ring<kBig> R(sh);
     constexpr int S = Ring<kBig>::S;
     constexpr int CW = Ring<kBig>::CW;
     const int tid = threadIdx.x;
-    const char* src = reinterpret_cast<const char*>(g.rowp - g.off);
-    const int nch = (g.nv + CW - 1) / CW;
+    if (ve < 0) ve = g.nv;
+    const char* src = reinterpret_cast<const char*>(g.rowp - g.off) + (size_t)vb * 16;
+    const int nvr = ve - vb;
+    const int nch = (nvr + CW - 1) / CW;
     const uint32_t base = *R.cnt;  // uniform: read before any thread updates it
     __syncthreads();
     if (tid == 0) {
         for (int c = 0; c < nch && c < S; ++c) {
             const uint32_t slot = (base + c) % S;
-            const int nvec = min(CW, g.nv - c * CW);
+            const int nvec = min(CW, nvr - c * CW);
             fence_proxy_async_smem();
             mbar_arrive_expect_tx(&R.bar[slot], (uint32_t)nvec * 16u);
             bulk_g2s(R.slot(slot), src + (size_t)c * CW * 16, (uint32_t)nvec * 16u, &R.bar[slot]);
@@ -605,16 +612,16 @@ __device__ __forceinline__ void stream_row(RSmem* sh, const VerifyArgs& a, const
             if (tid == 0) atomicOr(&a.ws->err, 1u);
         }
         const int v0 = c * CW;
-        const int nvec = min(CW, g.nv - v0);
+        const int nvec = min(CW, nvr - v0);
 #pragma unroll
         for (int u = 0; u < CW / kRT; ++u) {
             const int i = tid + u * kRT;
-            if (i < nvec) fn(row_vec(g, V, nullptr, v0 + i, R.slot(slot)[i]), v0 + i);
+            if (i < nvec) fn(row_vec(g, V, nullptr, vb + v0 + i, R.slot(slot)[i]), vb + v0 + i);
         }
         __syncthreads();  // the slot is consumed
         if (tid == 0 && c + S < nch) {
             const int cn = c + S;
-            const int nv2 = min(CW, g.nv - cn * CW);
+            const int nv2 = min(CW, nvr - cn * CW);
             fence_proxy_async_smem();
             mbar_arrive_expect_tx(&R.bar[slot], (uint32_t)nv2 * 16u);
             bulk_g2s(R.slot(slot), src + (size_t)cn * CW * 16, (uint32_t)nv2 * 16u, &R.bar[slot]);
@@ -923,6 +930,62 @@ __device__ KeyStop count_walk(RSmem* sh, const VerifyArgs& a, const RowGeo& g, i
 }
 
 // One row task: its descriptor (and, for greedy rows, its packed first argmax).  All threads.
+// Split rows: the first half publishes its per-key counts, its maximum key, its band values
+// and its out-of-range flag to the row's slot, then a flag; the second half waits for the flag
+// (bounded; error bit 7) and adds them to its own.  Both halves are consecutive tasks, so the
+// wait is short; the first half never waits.
+__device__ void split_publish(RSmem* sh, const VerifyArgs& a, int slot, uint32_t mkey) {
+    const int tid = threadIdx.x;
+    uint32_t* cnt = reinterpret_cast<uint32_t*>(a.split + (size_t)slot * kSplitSlotBytes);
+    uint32_t* meta = cnt + kHCap;
+    uint16_t* band = reinterpret_cast<uint16_t*>(meta + 4);
+    for (int i = tid; i < kHCap; i += kRT) __stcg(cnt + i, sh->hist[i]);
+    const uint32_t nb = sh->nband;
+    for (uint32_t i = tid; i < nb && i < (uint32_t)kBandCap; i += kRT) band[i] = sh->band[i];
+    if (tid == 0) {
+        meta[0] = mkey;
+        meta[1] = nb;
+        meta[2] = sh->outside;
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) atomicExch(&a.split_flag[slot], 1u);
+}
+
+__device__ uint32_t split_merge(RSmem* sh, const VerifyArgs& a, int slot, uint32_t mkey) {
+    const int tid = threadIdx.x;
+    const uint32_t* cnt = reinterpret_cast<const uint32_t*>(a.split + (size_t)slot * kSplitSlotBytes);
+    const uint32_t* meta = cnt + kHCap;
+    const uint16_t* band = reinterpret_cast<const uint16_t*>(meta + 4);
+    if (tid == 0) {
+        volatile unsigned* f = a.split_flag + slot;
+        if (*f == 0u) {
+            const uint64_t t0 = globaltimer_ns();
+            while (*f == 0u) {
+                if (globaltimer_ns() - t0 > 2000000000ull) {
+                    atomicOr(&a.ws->err, 128u);
+                    break;
+                }
+                __nanosleep(128);
+            }
+        }
+        __threadfence();
+    }
+    __syncthreads();
+    for (int i = tid; i < kHCap; i += kRT) sh->hist[i] += __ldcg(cnt + i);
+    const uint32_t mk1 = __ldcg(meta + 0), nb1 = __ldcg(meta + 1), out1 = __ldcg(meta + 2);
+    const uint32_t nb0 = sh->nband;
+    for (uint32_t i = tid; i < nb1 && nb0 + i < (uint32_t)kBandCap; i += kRT) sh->band[nb0 + i] = band[i];
+    __syncthreads();
+    if (tid == 0) {
+        sh->nband = nb0 + nb1;
+        sh->outside |= out1;
+        a.split_flag[slot] = 0u;  // for the next launch
+    }
+    __syncthreads();
+    return mk1 > mkey ? mk1 : mkey;
+}
+
 __device__ void process_row(RSmem* sh, const VerifyArgs& a, const TaskInfo& ti) {
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
     const int V = a.V;
@@ -934,9 +997,14 @@ __device__ void process_row(RSmem* sh, const VerifyArgs& a, const TaskInfo& ti) 
     // Nucleus and keep-all rows start with the fixed-range histogram (one pass, no max
     // pass); the other rows, and rows with values outside that range, start with the max.
     const bool onepass = ti.cat == kKeepAll || (ti.cat == kBinned && ti.p < 1.0f);
+    if (ti.half == 0 && !onepass) return;  // only one-pass rows are split: the second half does all
+    const int half = onepass ? ti.half : -1;
     uint32_t tkey = 0, mkey = 0;
     bool fixed_hist = false;
     if (onepass) {
+        // a split row's halves: vectors [0, nv / 2) and [nv / 2, nv)
+        const int hb = half < 0 ? 0 : (half == 0 ? 0 : g.nv / 2);
+        const int he = half < 0 ? g.nv : (half == 0 ? g.nv / 2 : g.nv);
         __syncthreads();
         for (int i = tid; i < kHCap; i += kRT) sh->hist[i] = 0u;
         if (tid == 0) {
@@ -1010,7 +1078,7 @@ __device__ void process_row(RSmem* sh, const VerifyArgs& a, const TaskInfo& ti) 
                     }
                 }
             }
-        });
+        }, hb, he);
         {
             const uint32_t k0 = okey(vmax2 & 0xFFFFu), k1 = okey(vmax2 >> 16);
             tkey = k0 > k1 ? k0 : k1;
@@ -1021,6 +1089,11 @@ __device__ void process_row(RSmem* sh, const VerifyArgs& a, const TaskInfo& ti) 
         __syncthreads();
 #pragma unroll
         for (int i = 0; i < kRW; ++i) mkey = max(mkey, sh->red32[i]);
+        if (half == 0) {
+            split_publish(sh, a, ti.slot, mkey);
+            return;
+        }
+        if (half == 1) mkey = split_merge(sh, a, ti.slot, mkey);
         fixed_hist = sh->outside == 0u && sh->nband <= (uint32_t)kBandCap && mkey > kNInfRaw &&
                      mkey <= kFTop;
         __syncthreads();
@@ -2003,6 +2076,12 @@ __global__ void __launch_bounds__(kRT, DSV_ROWS_MIN_CTAS) rows_kernel(VerifyArgs
     // been taken by then, so it will be).
     const int nsel = (int)(sh->plan.pre(0, a.B) + sh->plan.pre(1, a.B));
     const int ntask = total_tasks(a, sh);
+    // Selection rows beyond the first wave (index >= grid) are split in two halves (up to the
+    // workspace's slot count): selection task t maps to row t below the grid, to row
+    // G + (t - G) / 2, half (t - G) % 2 for the next 2 * nsplit tasks, and to row t - nsplit after.
+    const int G = (int)gridDim.x;
+    const int nsplit = (a.split_cap > 0 && nsel > G) ? min(nsel - G, a.split_cap) : 0;
+    const int nseltask = nsel + nsplit;
     if (tid < 32) {
         int ns = 0;
         for (int b0 = 0; b0 < a.B; b0 += 32) {
@@ -2030,7 +2109,7 @@ __global__ void __launch_bounds__(kRT, DSV_ROWS_MIN_CTAS) rows_kernel(VerifyArgs
             }
             if (!kind && !sh->q_sel_empty) {
                 const int x = (int)(gridDim.x + atomicAdd(&a.ws->next, 1u));
-                if (x < nsel) {
+                if (x < nseltask) {
                     kind = 1;
                     t = x;
                 } else {
@@ -2041,7 +2120,7 @@ __global__ void __launch_bounds__(kRT, DSV_ROWS_MIN_CTAS) rows_kernel(VerifyArgs
                 const int x = (int)atomicAdd(&a.ws->next2, 1u);
                 if (nsel + x < ntask) {
                     kind = 1;
-                    t = nsel + x;
+                    t = nseltask + x;
                 } else {
                     sh->q_gr_empty = 1;
                 }
@@ -2082,12 +2161,23 @@ __global__ void __launch_bounds__(kRT, DSV_ROWS_MIN_CTAS) rows_kernel(VerifyArgs
 #endif
         bool finished;
         if (kind == 1) {
-            const TaskInfo ti = decode_task(a, sh, t);
+            int r = t, half = -1;
+            if (t >= nseltask) {
+                r = nsel + (t - nseltask);             // greedy rows
+            } else if (t >= G + 2 * nsplit) {
+                r = t - nsplit;
+            } else if (t >= G) {
+                r = G + (t - G) / 2;
+                half = (t - G) & 1;
+            }
+            TaskInfo ti = decode_task(a, sh, r);
+            ti.half = half;
+            ti.slot = half >= 0 ? (t - G) / 2 : -1;
 #ifdef DSV_PROFILE
             trace_cat = ti.cat;
 #endif
             process_row(sh, a, ti);
-            finished = row_done(sh, a, ti.b);
+            finished = half == 0 ? false : row_done(sh, a, ti.b);  // a first half is not a row
         } else {
             finished = chain_task(a, csh, sh->q_b, t % kCP);
         }

@@ -174,3 +174,36 @@ def test_invalid_arguments_raise_before_launch():
         verify.verify_logits(**{**kw, "top_k": kw["top_k"].long()})
     with pytest.raises(ValueError):
         verify.verify_logits(**{**kw, "draft_logits": kw["draft_logits"].float()})
+
+
+@pytest.mark.parametrize("case", ["plain", "ties", "outside", "band", "inf"])
+def test_split_rows_match_oracle(case):
+    """More selection rows than CTAs of the row kernel: the rows beyond the first wave are
+    split in two halves whose histograms meet through the workspace.  Every request sampled
+    with top_p < 1 and 16 positions, so 64 requests give 1984 one-pass rows; the cases put
+    ties, values outside the fixed histogram range (the halves fall back to the full-row path),
+    values in the listed band, and -inf into those rows."""
+    g = torch.Generator().manual_seed({"plain": 1, "ties": 2, "outside": 3, "band": 4, "inf": 5}[case])
+    B, V = 64, 4096
+    lens = torch.full((B,), 16, dtype=torch.int32)
+    temperature = 0.3 + torch.rand(B, generator=g)
+    top_k = torch.where(torch.rand(B, generator=g) < 0.5, torch.tensor(workloads.TOPK_OFF),
+                        torch.tensor(50)).to(torch.int32)
+    top_p = 0.6 + 0.39 * torch.rand(B, generator=g)
+    batch = workloads.build(lens, temperature, top_k, top_p, V=V, dtype=torch.float32, seed=5)
+    t, d = batch.target_logits, batch.draft_logits
+    if case == "ties":
+        t.copy_((t * 2).round() / 2)
+        d.copy_((d * 2).round() / 2)
+    elif case == "outside":
+        t[1::3, 7] = 5000.0  # above the fixed range in some rows, in one half or the other
+        t[2::3, 3000] = -6000.0
+    elif case == "band":
+        t[:, 100:140] = 1e-7  # |v| < 2^-20: listed element by element
+        d[:, 2100:2130] = -3e-8
+    elif case == "inf":
+        t[:, ::7] = -float("inf")
+    batch.target_logits = t.to(torch.bfloat16)
+    batch.draft_logits = d.to(torch.bfloat16)
+    batch = batch.to(DEV)
+    assert_same(run_kernel(batch), oracle_verify(batch), f"split rows {case}")
