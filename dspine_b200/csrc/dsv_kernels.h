@@ -67,9 +67,9 @@ constexpr inline size_t verify_wmass_offset(int B) {
     return verify_racc_offset(B) + (((size_t)B * 8 + 63) & ~(size_t)63);
 }
 // [2 KB]: phase timers of profiling builds (-DDSV_PROFILE); unused otherwise.  Profiling
-// builds add a 96 KB task trace after them.
+// builds add a 128 KB task trace after them.
 #ifdef DSV_PROFILE
-constexpr size_t kProfBytes = 2048 + 96 * 1024;
+constexpr size_t kProfBytes = 2048 + 128 * 1024;
 #else
 constexpr size_t kProfBytes = 2048;
 #endif

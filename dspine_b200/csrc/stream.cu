@@ -51,9 +51,9 @@ constexpr float kTwo23 = 8388608.0f;
 // counter [cat * 16 + phase], task count at phase 15; the chain kernel at [64 + phase]
 
 #ifdef DSV_PROFILE
-constexpr unsigned kTraceCap = 2600;   // task trace entries
+constexpr unsigned kTraceCap = 2600;   // task trace entries (5 words each)
 constexpr unsigned kTraceCtas = 800;   // per-CTA start / exit entries
-static_assert((260 + 3 * kTraceCap + 2 * kTraceCtas) * 8 <= kProfBytes, "trace fits the profiling area");
+static_assert((260 + 5 * kTraceCap + 2 * kTraceCtas) * 8 <= kProfBytes, "trace fits the profiling area");
 __device__ __forceinline__ unsigned smid() {
     unsigned r;
     asm volatile("mov.u32 %0, %%smid;" : "=r"(r));
@@ -66,6 +66,7 @@ __device__ __forceinline__ unsigned smid() {
             const unsigned long long prof_n = globaltimer_ns();                          \
             atomicAdd(a.prof + (cat_) * 16 + (ph), \
                       prof_n - prof_t);                                                  \
+            sh->prof_ph[ph] += (uint32_t)(prof_n - prof_t);                              \
             prof_t = prof_n;                                                             \
         }                                                                                \
     } while (0)
@@ -500,6 +501,9 @@ struct RSmem {
     int q_nchain;                  // task sources: chain tasks of the launch
     int q_sel_empty, q_gr_empty;   //               selection / greedy queues exhausted
     int q_kind, q_b;               //               this task's kind and chain request
+#ifdef DSV_PROFILE
+    uint32_t prof_ph[16];          // profiling builds: phase durations of the current task
+#endif
     int task;
     int first_min;
     uint32_t nlist;
@@ -2060,6 +2064,9 @@ __global__ void __launch_bounds__(kRT, DSV_ROWS_MIN_CTAS) rows_kernel(VerifyArgs
         fence_mbar_init();
         sh->ring_cnt = 0;
         sh->big_cnt = 0;
+#ifdef DSV_PROFILE
+        for (int q = 0; q < 16; ++q) sh->prof_ph[q] = 0u;
+#endif
         uint16_t* pre = reinterpret_cast<uint16_t*>(smem_raw + sizeof(RSmem));
         sh->plan = Plan{pre, reinterpret_cast<uint8_t*>(pre + 3 * (a.B + 1)), a.B};
     }
@@ -2183,24 +2190,27 @@ __global__ void __launch_bounds__(kRT, DSV_ROWS_MIN_CTAS) rows_kernel(VerifyArgs
         }
         if (finished) finalize_request(a, csh);
 #ifdef DSV_PROFILE
-        // task trace: [256] entries used, [260 + 3 i] start, end, task | cat << 16 | sm << 24
-        // (cat 8: a chain task)
+        // task trace: [256] entries used, [260 + 5 i] start, end, task | cat << 16 | sm << 24,
+        // phases 2 | 4 << 32, phases 6 | 8 << 32 (ns; cat 8: a chain task)
         if (tid == 0) {
             const unsigned long long now = globaltimer_ns();
             const unsigned long long i = atomicAdd(a.prof + 256, 1ull);
             if (i < kTraceCap) {
-                unsigned long long* e = a.prof + 260 + 3 * i;
+                unsigned long long* e = a.prof + 260 + 5 * i;
                 e[0] = trace_r0;
                 e[1] = now;
                 e[2] = (unsigned long long)t | ((unsigned long long)trace_cat << 16) |
                        ((unsigned long long)smid() << 24) | ((unsigned long long)blockIdx.x << 40);
+                e[3] = (unsigned long long)sh->prof_ph[2] | ((unsigned long long)sh->prof_ph[4] << 32);
+                e[4] = (unsigned long long)sh->prof_ph[6] | ((unsigned long long)(sh->prof_ph[7] + sh->prof_ph[8]) << 32);
             }
+            for (int q = 0; q < 16; ++q) sh->prof_ph[q] = 0u;
         }
 #endif
     }
 #ifdef DSV_PROFILE
     if (tid == 0 && blockIdx.x < kTraceCtas) {  // per CTA: start and exit
-        unsigned long long* e = a.prof + 260 + 3 * kTraceCap + 2 * blockIdx.x;
+        unsigned long long* e = a.prof + 260 + 5 * kTraceCap + 2 * blockIdx.x;
         e[0] = trace_t0;
         e[1] = globaltimer_ns();
     }
