@@ -384,7 +384,7 @@ def run_dspine(args):
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,
                          "traffic_kernels": traffic_kernels, "peak_source": peak_src,
-                         "kernel": "dsv::rows_kernel + dsv::chain3_kernel (one dsv_verify_logits call)",
+                         "kernel": "dsv::rows_kernel (the whole dsv_verify_logits call: rows and chain tasks)",
                          "algorithmic_bytes_per_launch": alg_bytes,
                          "kernel_ms": kernel_ms},
         }

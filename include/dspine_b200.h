@@ -43,15 +43,22 @@ const char* dsv_status_string(int status);
 uint64_t dsv_launch_count(void);
 
 /* ---- workspace ----------------------------------------------------------------------------
- * Scratch for dsv_verify_logits: task counters and per-row decisions.  Zero it once after
- * allocation (dsv_workspace_init); every launch leaves it zeroed again. */
+ * Scratch for dsv_verify_logits: task counters, per-row decisions, the ready list of requests
+ * and (last 8.5 MB) the slots through which the two halves of a split row meet.  Zero it once
+ * after allocation (dsv_workspace_init); every launch leaves it zeroed again.  A workspace
+ * without the split-row slots (the size for the batch minus that region) is accepted and then
+ * no row is split. */
 int dsv_verify_workspace_size(int32_t batch, size_t* bytes);
 int dsv_workspace_init(void* workspace, size_t bytes, dsv_stream_t stream);
 /* Copy the device error word of a workspace to *err and clear it (synchronizes `stream`).
  * bit 0: a shared-memory bulk copy did not complete within its time limit;
  * bit 1: a request addressed a row outside the logit tensors. */
 int dsv_workspace_error(void* workspace, uint32_t* err, dsv_stream_t stream);
-/* bit 2 of the error word: a compaction read a KV slot position outside `slots_len`. */
+/* bit 2 of the error word: a compaction read a KV slot position outside `slots_len`;
+ * bits 3-4: a selection or a tie cut found no boundary (inconsistent input); bit 6: a chain
+ * task waited past its time limit for its request; bit 7: the second half of a split row
+ * waited past its time limit for the first.  Bits 0 and 5-7 are internal failures: the
+ * outputs of that call are not valid. */
 
 /* ---- accept-compact outputs (optional argument of dsv_verify_logits) ----------------------
  * Restates SGLang's commit of accepted tokens and KV slots (wrapped by the reference at
