@@ -27,6 +27,8 @@
 #include <stddef.h>
 #include <stdint.h>
 
+#include <mutex>
+
 #include "dsv_common.cuh"
 #include "dsv_kernels.h"
 
@@ -1543,7 +1545,7 @@ constexpr int kCTW = kCT / 32;
 static_assert(kCP * 1 <= 2 * kT, "slice masses live in the request's task-result area (32 u64)");
 static_assert(kCP <= 32 && kCTW <= 8, "per-warp slice masses: [B][32][8] in the workspace");
 
-struct Chain3Smem {
+struct ChainSmem {
     uint2 queue[kCTW][256];        // per warp: kept elements of one vector per lane
     unsigned long long wsum[kCTW];
     uint32_t red_a[kCTW], red_b[kCTW];
@@ -1731,7 +1733,7 @@ __device__ __forceinline__ unsigned long long block_sum_u64(unsigned long long v
 // pass).  Each task sums the exact residual mass of its slice of the rejected position's rows
 // and records per-warp masses; the task that completes the request's slices finds the bonus
 // token and writes the request's outputs (returns true).
-__device__ bool chain_task(const VerifyArgs& a, Chain3Smem* sh, int b, int rank) {
+__device__ bool chain_task(const VerifyArgs& a, ChainSmem* sh, int b, int rank) {
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
     const int cap = clamp_cap(a.caps[b]);
     const uint16_t* tgt = reinterpret_cast<const uint16_t*>(a.tgt);
@@ -1948,7 +1950,7 @@ __device__ void greedy_decide(const VerifyArgs& a, int b, int cap) {
 
 // After this CTA wrote the outputs of a request: the CTA that finishes the last request packs
 // tokens and KV slots (all threads of the CTA call it).
-__device__ void finalize_request(const VerifyArgs& a, Chain3Smem* sh) {
+__device__ void finalize_request(const VerifyArgs& a, ChainSmem* sh) {
     const int tid = threadIdx.x;
     __syncthreads();
     if (tid == 0) {
@@ -2101,9 +2103,9 @@ __global__ void __launch_bounds__(kRT, DSV_ROWS_MIN_CTAS) rows_kernel(VerifyArgs
             sh->q_gr_empty = 0;
         }
     }
-    static_assert(sizeof(Chain3Smem) <= sizeof(uint32_t) * kHCap && alignof(Chain3Smem) <= 16,
+    static_assert(sizeof(ChainSmem) <= sizeof(uint32_t) * kHCap && alignof(ChainSmem) <= 16,
                   "chain tasks use the histogram area");
-    Chain3Smem* csh = reinterpret_cast<Chain3Smem*>(sh->hist);  // idle between tasks
+    ChainSmem* csh = reinterpret_cast<ChainSmem*>(sh->hist);  // idle between tasks
     bool first_task = true;
     for (;;) {
         __syncthreads();
@@ -2239,31 +2241,40 @@ int launch_rows_cta(VerifyArgs a, cudaStream_t stream) {
     // allows (cached per device and size)
     const size_t smem = sizeof(RSmem) + plan_bytes(a.B);
     constexpr int kMaxDev = 64;
-    static int attr_done[kMaxDev] = {};
-    static size_t cached_smem[kMaxDev] = {};
-    static int cached_blocks[kMaxDev] = {};
+    struct Cache {
+        bool attr;
+        size_t smem;
+        int blocks;
+    };
+    static Cache cache[kMaxDev] = {};
+    static std::mutex mu;
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return kLaunchFailed;
-    if (!attr_done[dev]) {
-        if (cudaFuncSetAttribute(rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 (int)(sizeof(RSmem) + plan_bytes(kMaxB))) != cudaSuccess)
-            return kLaunchFailed;
-        attr_done[dev] = 1;
+    int blocks = 0;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        Cache& c = cache[dev];
+        if (!c.attr) {
+            if (cudaFuncSetAttribute(rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)(sizeof(RSmem) + plan_bytes(kMaxB))) != cudaSuccess)
+                return kLaunchFailed;
+            c.attr = true;
+        }
+        if (c.smem != smem) {
+            int per_sm = 0, sms = 0;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rows_kernel, kRT, smem) != cudaSuccess ||
+                per_sm < 1)
+                return kLaunchFailed;
+            if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+                return kLaunchFailed;
+            c.smem = smem;
+            c.blocks = per_sm * sms;
+        }
+        blocks = c.blocks;
     }
-    if (cached_smem[dev] != smem) {
-        int per_sm = 0, sms = 0;
-        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, rows_kernel, kRT, smem) != cudaSuccess || per_sm < 1)
-            return kLaunchFailed;
-        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) return kLaunchFailed;
-        cached_smem[dev] = smem;
-        cached_blocks[dev] = per_sm * sms;
-    }
-    rows_kernel<<<cached_blocks[dev], kRT, smem, stream>>>(a);
+    rows_kernel<<<blocks, kRT, smem, stream>>>(a);
     return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
 }
-
-// ---------------------------------------------------------------------------------------
-// launcher
 
 
 // ---------------------------------------------------------------------------------------

@@ -1070,10 +1070,8 @@ int launch_verify_t(VerifyArgs a, cudaStream_t stream) {
     const size_t smem = verify_smem_bytes<T>(slice);
     if (smem > 227 * 1024) return kUnsupported;
     auto kern = verify_kernel<T, kC>;
-    static int configured_smem[2] = {0, 0};
     int dev = 0;
     cudaGetDevice(&dev);
-    (void)configured_smem;
     if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
         return kLaunchFailed;
     cudaLaunchConfig_t cfg = {};
@@ -1091,17 +1089,21 @@ int launch_verify_t(VerifyArgs a, cudaStream_t stream) {
     static int cached_dev[16] = {-1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1, -1};
     static size_t cached_smem[16];
     static int cached_n[16];
+    static std::mutex mu;
     const int slot = (dev & 7) * 2 + (sizeof(T) == 4 ? 1 : 0);
     int nclus = 0;
-    if (cached_dev[slot] == dev && cached_smem[slot] == smem) {
-        nclus = cached_n[slot];
-    } else {
-        cfg.gridDim = dim3(kC, 1, 1);
-        if (cudaOccupancyMaxActiveClusters(&nclus, kern, &cfg) != cudaSuccess || nclus <= 0)
-            return kLaunchFailed;
-        cached_dev[slot] = dev;
-        cached_smem[slot] = smem;
-        cached_n[slot] = nclus;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (cached_dev[slot] == dev && cached_smem[slot] == smem) {
+            nclus = cached_n[slot];
+        } else {
+            cfg.gridDim = dim3(kC, 1, 1);
+            if (cudaOccupancyMaxActiveClusters(&nclus, kern, &cfg) != cudaSuccess || nclus <= 0)
+                return kLaunchFailed;
+            cached_dev[slot] = dev;
+            cached_smem[slot] = smem;
+            cached_n[slot] = nclus;
+        }
     }
     const int tasks = a.B * kT;
     if (nclus > tasks) nclus = tasks;
