@@ -26,6 +26,8 @@
 
 #include <cooperative_groups.h>
 
+#include <mutex>
+
 #include "dsv_common.cuh"
 #include "dsv_kernels.h"
 
