@@ -207,3 +207,35 @@ def test_split_rows_match_oracle(case):
     batch.draft_logits = d.to(torch.bfloat16)
     batch = batch.to(DEV)
     assert_same(run_kernel(batch), oracle_verify(batch), f"split rows {case}")
+
+
+@pytest.mark.parametrize("B,V", [(1, 1031), (1024, 521), (1025, 521)])
+def test_batch_limits_match_oracle(B, V):
+    """One request; the largest batch of the one-launch bf16 path (1024: the task table and the
+    ready list at their largest); one more request (the clustered fallback path)."""
+    batch = random_batch(9000 + B, B, V, torch.bfloat16)
+    assert_same(run_kernel(batch), oracle_verify(batch), f"B={B} V={V}")
+
+
+def test_workspace_without_split_slots():
+    """A workspace that omits the split-row slots (the last kSplitCap x (slot + flag) bytes:
+    256 x 33860) is accepted and gives the same outputs; no row is split then."""
+    g = torch.Generator().manual_seed(8)
+    B, V = 64, 2048
+    lens = torch.full((B,), 16, dtype=torch.int32)
+    temperature = 0.3 + torch.rand(B, generator=g)
+    top_k = torch.full((B,), workloads.TOPK_OFF, dtype=torch.int32)
+    top_p = 0.6 + 0.39 * torch.rand(B, generator=g)
+    batch = workloads.build(lens, temperature, top_k, top_p, V=V, dtype=torch.bfloat16,
+                            seed=6).to(DEV)
+    full = verify.Workspace(B, DEV)
+    small = verify.Workspace(B, DEV)
+    small.nbytes -= 256 * 33860
+    kw = batch.kwargs()
+    got_full = verify.verify_logits(**kw, workspace=full)
+    got_small = verify.verify_logits(**kw, workspace=small)
+    torch.cuda.synchronize()
+    assert full.error_word() == 0 and small.error_word() == 0
+    for a_, b_ in zip(got_full, got_small):
+        assert torch.equal(a_, b_)
+    assert_same(got_full, oracle_verify(batch), "split slots")
