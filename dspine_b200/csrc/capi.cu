@@ -438,6 +438,19 @@ int dsv_target_probs(int64_t rows, int32_t vocab, int32_t rows_per_request, cons
     return counted(DSV_OK, launched);
 }
 
+int dsv_topk_ids(int64_t rows, int32_t vocab, int64_t row_stride, int32_t dtype,
+                 const void* logits, int32_t k, int64_t* out, dsv_stream_t stream) {
+    if (rows < 0 || vocab < 1 || vocab > dsv::topk_max_vocab() || row_stride < vocab) return DSV_BAD_SHAPE;
+    if (k < 1 || k > dsv::topk_max_k() || (k & (k - 1)) || (vocab + 63) / 64 < k) return DSV_BAD_SHAPE;
+    if (dtype < 0 || dtype > 2) return DSV_BAD_DTYPE;
+    if (rows == 0) return DSV_OK;
+    if (!logits || !out) return DSV_BAD_POINTER;
+    if (!aligned(logits, dtype == 1 ? 4 : 2)) return DSV_BAD_ALIGNMENT;
+    return counted(dsv::launch_topk_ids(logits, dtype, rows, vocab, row_stride, k, out,
+                                        (cudaStream_t)stream),
+                   1);
+}
+
 int dsv_serial_sample_chain(int32_t batch, int32_t block_size, int32_t k, const float* table,
                             const float* inv_temp, const int32_t* top_k, const float* top_p,
                             const float* min_p, const int32_t* greedy, const float* u,

@@ -278,6 +278,12 @@ int launch_serial_table(const TableArgs& a, cudaStream_t stream);
 int launch_serial_chain(int bs, int tm1, int k, const int64_t* idx, const int64_t* cand,
                         int64_t* out, const float* conf, float* conf_out, cudaStream_t stream);
 
+// ---- top-k ids of materialised logits (topk.cu) -------------------------------------------
+int topk_max_k();
+int topk_max_vocab();
+int launch_topk_ids(const void* logits, int dtype, long long rows, int V, long long stride, int k,
+                    int64_t* out, cudaStream_t stream);
+
 // ---- per-request steps (small.cu) -----------------------------------------------------------
 struct GreedyArgs {
     int B;

@@ -1,9 +1,9 @@
 """Draft-side serial chains at the reference's ``sglang_dspine.kernels.dspine`` interface.
 
-`serial_sample_chain`, `serial_table` and `serial_chain` keep the reference's signatures,
-argument checks (ValueError before anything is launched) and caller-owned, in-place outputs
-(kernels/dspine.py:357-502, 677-772); each is one launch of the library's C ABI
-(dsv_serial_sample_chain, dsv_serial_table, dsv_serial_chain).  `build_serial_tables` is the
+`serial_sample_chain`, `serial_table`, `serial_chain` and `topk_ids` keep the reference's
+signatures, argument checks (ValueError before anything is launched) and caller-owned, in-place
+outputs (kernels/dspine.py:165-207, 357-502, 677-772); each is one launch of the library's C ABI
+(dsv_serial_sample_chain, dsv_serial_table, dsv_serial_chain, dsv_topk_ids).  `build_serial_tables` is the
 offline table build (kernels/dspine.py:327-351): two plain bf16 library GEMMs per vocabulary
 chunk, run once per weight load, not per step.
 """
@@ -23,6 +23,39 @@ def _cuda(*tensors):
     for t in tensors:
         if t is not None and t.device.type != "cuda":
             raise ValueError("dspine_b200 runs the serial chains on CUDA tensors only")
+
+
+_TOPK_CHUNK = 64
+_TOPK_DTYPES = {torch.bfloat16: 0, torch.float32: 1, torch.float16: 2}
+
+
+def topk_ids(logits: torch.Tensor, k: int, out: torch.Tensor = None) -> torch.Tensor:
+    """logits [N, V] (contiguous rows) -> int64 [N, k] ids of the k largest values, ascending
+    by id (kernels/dspine.py:165-207).  The reference's two stages (maxima of 64-wide chunks,
+    then the top-k of the k chunks with the largest maxima) give the row's top-k by (value
+    descending, id ascending); one launch of dsv_topk_ids, one CTA per row."""
+    if logits.dim() != 2 or logits.stride(1) != 1:
+        raise ValueError("topk_ids expects a row-contiguous [N, V] tensor")
+    if k & k - 1 or not 1 <= k <= 64:
+        raise ValueError(f"topk_ids needs a power-of-two k in [1, 64], got {k}")
+    n, v = logits.shape
+    nch = -(-v // _TOPK_CHUNK)
+    if nch < k:
+        raise ValueError(f"topk_ids needs at least k={k} chunks of {_TOPK_CHUNK}, vocab={v}")
+    if logits.dtype not in _TOPK_DTYPES:
+        raise ValueError(f"topk_ids supports bf16, fp16 and fp32 logits, got {logits.dtype}")
+    if out is None:
+        out = torch.empty((n, k), dtype=torch.int64, device=logits.device)
+    elif tuple(out.shape) != (n, k) or out.dtype != torch.int64 or not out.is_contiguous():
+        raise ValueError("topk_ids: out must be a contiguous int64 [N, k] tensor")
+    if n == 0:
+        return out
+    _cuda(logits, out)
+    stride = logits.stride(0) if n > 1 else v
+    with torch.cuda.device(logits.device):
+        _lib.call("dsv_topk_ids", n, v, stride, _TOPK_DTYPES[logits.dtype], logits.data_ptr(), k,
+                  out.data_ptr(), _stream(logits))
+    return out
 
 
 def build_serial_tables(lm_head_w, norm_w, write_w, pv_w, codebook, chunk: int = 8192):

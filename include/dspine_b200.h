@@ -284,6 +284,16 @@ int dsv_serial_chain(int32_t batch, int32_t block_size, int32_t k, const int64_t
                      const int64_t* candidates, int64_t* out, const float* confidence,
                      float* confidence_out, dsv_stream_t stream);
 
+/* ---- top-k ids of materialised logits ------------------------------------------------------
+ * Replaces kernels/dspine.py:165-207 topk_ids (with _chunk_max :111-121 and _select_topk
+ * :124-162): out[r, :] = the ids of the k largest values of row r of logits (dtype 0 bf16,
+ * 1 fp32, 2 fp16; row pitch row_stride elements), ascending by id; ties at the k-th place go to
+ * the lower id (the reference's two-stage selection over 64-wide chunks gives exactly this).
+ * k a power of two in [1, 64]; ceil(vocab / 64) >= k (as the reference); vocab <= 262144.
+ * -0 equals +0; NaN ranks below every number. */
+int dsv_topk_ids(int64_t rows, int32_t vocab, int64_t row_stride, int32_t dtype,
+                 const void* logits, int32_t k, int64_t* out, dsv_stream_t stream);
+
 /* ---- the same verification without a caller workspace ------------------------------------
  * No counterpart in the reference: for callers that cannot allocate device memory (or hand out
  * scratch) at verification time.  Same arguments, outputs and results as dsv_verify_logits,
