@@ -6,21 +6,28 @@
 // elements of a row always lie in those chunks, so the result is the row's top-k by
 // (value desc, id asc); this kernel computes it in the same two stages, one CTA per row:
 //
-//   1. chunk maxima: one warp per chunk (lane l reads elements l and l + 32, coalesced), kept
-//      as 64-bit keys (ordered value bits << 32 | ~chunk) in shared memory;
-//   2. the k-th largest chunk key by a bit search (one block-wide count per bit), so the
-//      selected chunks are those with keys at or above it;
-//   3. candidates: the elements of the selected chunks whose value reaches the k-th chunk
-//      maximum (every top-k element does), as keys (ordered value bits << 32 | ~id);
-//   4. the k-th largest candidate key by the same bit search; the k candidates at or above it
-//      are the answer, written in ascending id order.
+//   1. chunk maxima (all warps): 16-byte vector loads (8 bf16 / fp16 or 4 fp32 values per
+//      thread, 8 vectors in flight per thread), a packed NaN-ignoring max per vector, the 8 or
+//      16 threads of a chunk combine theirs by shuffles; kept as 64-bit keys (ordered value
+//      bits << 32 | ~chunk) in shared memory;
+//   2. the k chunks with the largest keys (warp 0): thread t's maximum over chunks t, t + 256,
+//      ... gives 256 keys whose k-th largest, L, has at least k chunk keys at or above it; warp
+//      0 compacts those few keys and finds the k-th largest among them by a bit search (one
+//      warp-wide count per bit, no block barrier);
+//   3. candidates (all warps, one selected chunk per warp at a time): the elements of the
+//      selected chunks whose value reaches the k-th chunk maximum (every top-k element does),
+//      as keys (ordered value bits << 32 | ~id);
+//   4. the k largest candidates (warp 0, the same bit search), written in ascending id order.
 //
 // Values compare as fp32 (bf16 / fp16 widen exactly); -0 equals +0; NaN ranks below every
-// number.  One pass over each row (HBM-bound), the selection works in shared memory.
+// number.  One pass over each row (HBM-bound); the selection works in shared memory.
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+
+#include <cstring>
+#include <mutex>
 
 #include "dsv_common.cuh"
 #include "dsv_kernels.h"
@@ -34,14 +41,15 @@ constexpr int kChunk = 64;
 constexpr int kMaxChunks = 4096;           // vocabularies up to 262144
 constexpr int kMaxK = 64;
 constexpr int kCandCap = kMaxK * kChunk;   // every element of the selected chunks
+constexpr int kChunkBits = 12;             // chunk index < 2^12
+constexpr int kIdBits = 18;                // element id < 2^18
 
 struct Smem {
     unsigned long long ck[kMaxChunks];     // chunk keys
-    unsigned long long cand[kCandCap];     // candidate keys
-    unsigned int wsum[2][kWarps];
+    unsigned long long cand[kCandCap];     // compacted chunk keys, then candidate keys
+    unsigned long long tmax[kThreads];     // thread t: max of chunk keys t, t + 256, ...
+    int selc[kMaxK];                       // the selected chunks, then the selected ids
     unsigned int ncand;
-    unsigned int nsel;
-    long long sel[kMaxK];
 };
 
 __device__ __forceinline__ uint32_t ordered(float v) {
@@ -56,31 +64,129 @@ template <> __device__ __forceinline__ float as_float<float>(float x) { return x
 template <> __device__ __forceinline__ float as_float<__nv_bfloat16>(__nv_bfloat16 x) { return __bfloat162float(x); }
 template <> __device__ __forceinline__ float as_float<__half>(__half x) { return __half2float(x); }
 
-// The k-th largest of the n distinct 64-bit keys keys[0, n) (k <= n): a bit search from the top
-// bit, one block-wide count per bit.  All threads call it; every thread gets the result.
-__device__ unsigned long long kth_largest(const unsigned long long* keys, int n, int k, Smem* sh) {
-    const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
+// The largest value of a 16-byte vector, NaN only if every lane is NaN (NaN-ignoring max:
+// __hmax2 / __hmax / fmaxf return the other operand when one is NaN).
+template <typename T> __device__ __forceinline__ float vec_max(const uint4& v);
+template <> __device__ __forceinline__ float vec_max<float>(const uint4& v) {
+    return fmaxf(fmaxf(__uint_as_float(v.x), __uint_as_float(v.y)),
+                 fmaxf(__uint_as_float(v.z), __uint_as_float(v.w)));
+}
+template <> __device__ __forceinline__ float vec_max<__nv_bfloat16>(const uint4& v) {
+    __nv_bfloat162 a, b, c, d;
+    memcpy(&a, &v.x, 4); memcpy(&b, &v.y, 4); memcpy(&c, &v.z, 4); memcpy(&d, &v.w, 4);
+    const __nv_bfloat162 m = __hmax2(__hmax2(a, b), __hmax2(c, d));
+    return __bfloat162float(__hmax(m.x, m.y));
+}
+template <> __device__ __forceinline__ float vec_max<__half>(const uint4& v) {
+    __half2 a, b, c, d;
+    memcpy(&a, &v.x, 4); memcpy(&b, &v.y, 4); memcpy(&c, &v.z, 4); memcpy(&d, &v.w, 4);
+    const __half2 m = __hmax2(__hmax2(a, b), __hmax2(c, d));
+    return __half2float(__hmax(m.x, m.y));
+}
+
+template <typename T> __device__ __forceinline__ T nan_value();
+template <> __device__ __forceinline__ float nan_value<float>() { return __uint_as_float(0x7FC00000u); }
+template <> __device__ __forceinline__ __nv_bfloat16 nan_value<__nv_bfloat16>() { return __ushort_as_bfloat16(0x7FC0u); }
+template <> __device__ __forceinline__ __half nan_value<__half>() { return __ushort_as_half(0x7E00u); }
+
+// The k-th largest of the n distinct 64-bit keys keys[0, n) (k <= n), by one warp: a bit
+// search from the top bit, one warp-wide count per bit.  The low word of every key is ~index
+// with index < 2^lowbits, so its bits 31..lowbits are set in every key and need no count.  Keys
+// of value 0 (empty slots) never count.  Every lane gets the result.
+__device__ __forceinline__ unsigned long long kth_largest_warp(const unsigned long long* keys, int n,
+                                                               int k, int lowbits) {
+    const int lane = threadIdx.x & 31;
+    constexpr int kReg = 8;                 // up to 256 keys are held in registers
+    unsigned long long held[kReg];
+    const bool in_regs = n <= 32 * kReg;
+    if (in_regs) {
+#pragma unroll
+        for (int q = 0; q < kReg; ++q) held[q] = lane + 32 * q < n ? keys[lane + 32 * q] : 0ull;
+    }
     unsigned long long prefix = 0ull;
     for (int bit = 63; bit >= 0; --bit) {
+        if (bit == 31) {
+            prefix |= 0xFFFFFFFFull & (0xFFFFFFFFull << lowbits);
+            bit = lowbits;
+            continue;
+        }
         const unsigned long long trial = prefix | (1ull << bit);
         unsigned int c = 0;
-        for (int i = tid; i < n; i += kThreads) c += keys[i] >= trial;
-        c = __reduce_add_sync(0xffffffffu, c);
-        const int buf = bit & 1;            // alternate buffers: one barrier per bit
-        if (lane == 0) sh->wsum[buf][wid] = c;
-        __syncthreads();
-        unsigned int total = 0;
+        if (in_regs) {
 #pragma unroll
-        for (int w = 0; w < kWarps; ++w) total += sh->wsum[buf][w];
-        if (total >= (unsigned int)k) prefix = trial;
+            for (int q = 0; q < kReg; ++q) c += held[q] >= trial;
+        } else {
+            for (int i = lane; i < n; i += 32) c += keys[i] >= trial;
+        }
+        if (__reduce_add_sync(0xffffffffu, c) >= (unsigned int)k) prefix = trial;
     }
     return prefix;
 }
 
+// Warp-wide stream compaction: appends keys[i] (i < n) with keys[i] >= lo to dst in index
+// order; returns the count (every lane).
+__device__ __forceinline__ int compact_at_least(const unsigned long long* keys, int n,
+                                                unsigned long long lo, unsigned long long* dst) {
+    const int lane = threadIdx.x & 31;
+    int m = 0;
+    for (int base = 0; base < n; base += 32) {
+        const int i = base + lane;
+        const unsigned long long key = i < n ? keys[i] : 0ull;
+        const bool take = i < n && key >= lo;
+        const unsigned int b = __ballot_sync(0xffffffffu, take);
+        if (take) dst[m + __popc(b & ((1u << lane) - 1u))] = key;
+        m += __popc(b);
+    }
+    return m;
+}
+
+// Chunk maxima of one row into sh->ck[0, nch): thread t of the CTA handles 16-byte vectors
+// t, t + 256, ... (kUnroll loads issued before any is used); the kTpc consecutive threads whose
+// vectors form one chunk combine their maxima by xor-shuffles.  vec_ok: the row start and pitch
+// are 16-byte aligned, so full vectors load as one uint4; the last, partial vector (and every
+// vector of an unaligned row) loads element by element within the row, NaN beyond it.
 template <typename T>
-__global__ void __launch_bounds__(kThreads) topk_ids_kernel(const T* __restrict__ x, long long rows,
+__device__ __forceinline__ void chunk_maxima(const T* __restrict__ row, int V, bool vec_ok, Smem* sh) {
+    constexpr int kE = 16 / sizeof(T);          // values per vector
+    constexpr int kTpc = kChunk / kE;           // threads per chunk (8 or 16)
+    constexpr int kUnroll = 8;
+    const int tid = threadIdx.x;
+    const int nvec = (V + kE - 1) / kE;
+    const int nfull = V / kE;
+    for (int j0 = 0; j0 < nvec; j0 += kThreads * kUnroll) {
+        uint4 v[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            const int j = j0 + u * kThreads + tid;
+            if (vec_ok && j < nfull) {
+                v[u] = __ldg(reinterpret_cast<const uint4*>(row) + j);
+            } else {
+                T e[kE];
+#pragma unroll
+                for (int q = 0; q < kE; ++q) {
+                    const int i = j * kE + q;
+                    e[q] = i < V ? row[i] : nan_value<T>();
+                }
+                memcpy(&v[u], e, 16);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+            const int j = j0 + u * kThreads + tid;
+            uint32_t m = ordered(vec_max<T>(v[u]));
+#pragma unroll
+            for (int o = 1; o < kTpc; o <<= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
+            const int c = j / kTpc;
+            if ((tid & (kTpc - 1)) == 0 && j < nvec)
+                sh->ck[c] = ((unsigned long long)m << 32) | (0xFFFFFFFFu - (uint32_t)c);
+        }
+    }
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kThreads, 3) topk_ids_kernel(const T* __restrict__ x, long long rows,
                                                             int V, long long stride, int k,
-                                                            int64_t* __restrict__ out) {
+                                                            bool vec_ok, int64_t* __restrict__ out) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     Smem* sh = reinterpret_cast<Smem*>(smem_raw);
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
@@ -88,26 +194,40 @@ __global__ void __launch_bounds__(kThreads) topk_ids_kernel(const T* __restrict_
     for (long long r = blockIdx.x; r < rows; r += gridDim.x) {
         const T* row = x + r * stride;
         // 1. chunk maxima
-#pragma unroll 4
-        for (int c = wid; c < nch; c += kWarps) {
-            const int i0 = c * kChunk + lane, i1 = i0 + 32;
-            uint32_t m = 0u;
-            if (i0 < V) m = ordered(as_float<T>(row[i0]));
-            if (i1 < V) m = max(m, ordered(as_float<T>(row[i1])));
-            m = __reduce_max_sync(0xffffffffu, m);
-            if (lane == 0) sh->ck[c] = ((unsigned long long)m << 32) | (0xFFFFFFFFu - (uint32_t)c);
-        }
-        if (tid == 0) {
-            sh->ncand = 0u;
-            sh->nsel = 0u;
+        chunk_maxima<T>(row, V, vec_ok, sh);
+        __syncthreads();
+        {
+            unsigned long long t = 0ull;
+            for (int c = tid; c < nch; c += kThreads) t = max(t, sh->ck[c]);
+            sh->tmax[tid] = t;
         }
         __syncthreads();
-        // 2. the k chunks with the largest maxima (ties to the lower chunk)
-        const unsigned long long kc = kth_largest(sh->ck, nch, k, sh);
-        const uint32_t vmin = (uint32_t)(kc >> 32);   // the k-th largest chunk maximum
-        // 3. candidates: elements of the selected chunks that reach it
-        for (int c = wid; c < nch; c += kWarps) {
-            if (sh->ck[c] < kc) continue;             // warp-uniform
+        // 2. the k chunks with the largest keys (ties to the lower chunk)
+        if (wid == 0) {
+            // at least k threads hold a key >= lo, so at least k chunk keys are >= lo
+            const unsigned long long lo = kth_largest_warp(sh->tmax, kThreads, k, kChunkBits);
+            const int m = compact_at_least(sh->ck, nch, lo, sh->cand);
+            __syncwarp();
+            const unsigned long long kc = kth_largest_warp(sh->cand, m, k, kChunkBits);
+            int s = 0;
+            for (int base = 0; base < m; base += 32) {
+                const int i = base + lane;
+                const bool take = i < m && sh->cand[i] >= kc;
+                const unsigned int b = __ballot_sync(0xffffffffu, take);
+                if (take) sh->selc[s + __popc(b & ((1u << lane) - 1u))] =
+                    (int)(0xFFFFFFFFu - (uint32_t)(sh->cand[i] & 0xFFFFFFFFull));
+                s += __popc(b);
+            }
+            if (lane == 0) {
+                sh->ncand = 0u;
+                sh->tmax[0] = kc;                  // the k-th chunk key, for step 3
+            }
+        }
+        __syncthreads();
+        // 3. candidates: elements of the selected chunks that reach the k-th chunk maximum
+        const uint32_t vmin = (uint32_t)(sh->tmax[0] >> 32);
+        for (int s = wid; s < k; s += kWarps) {
+            const int c = sh->selc[s];
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
                 const int i = c * kChunk + lane + 32 * h;
@@ -125,21 +245,25 @@ __global__ void __launch_bounds__(kThreads) topk_ids_kernel(const T* __restrict_
         }
         __syncthreads();
         // 4. the k largest candidates, written by ascending id
-        const int n = (int)sh->ncand;
-        const unsigned long long kk = kth_largest(sh->cand, n, k, sh);
-        for (int i = tid; i < n; i += kThreads) {
-            const unsigned long long key = sh->cand[i];
-            if (key >= kk) {
-                const unsigned int p = atomicAdd(&sh->nsel, 1u);
-                if (p < (unsigned int)kMaxK) sh->sel[p] = (long long)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull));
+        if (wid == 0) {
+            const int n = (int)sh->ncand;
+            const unsigned long long kk = kth_largest_warp(sh->cand, n, k, kIdBits);
+            int s = 0;
+            for (int base = 0; base < n; base += 32) {
+                const int i = base + lane;
+                const bool take = i < n && sh->cand[i] >= kk;
+                const unsigned int b = __ballot_sync(0xffffffffu, take);
+                if (take) sh->selc[s + __popc(b & ((1u << lane) - 1u))] =
+                    (int)(0xFFFFFFFFu - (uint32_t)(sh->cand[i] & 0xFFFFFFFFull));
+                s += __popc(b);
             }
-        }
-        __syncthreads();
-        if (tid < k) {
-            const long long id = sh->sel[tid];
-            int rank = 0;
-            for (int j = 0; j < k; ++j) rank += sh->sel[j] < id;
-            out[r * k + rank] = id;
+            __syncwarp();
+            for (int q = lane; q < k; q += 32) {
+                const int id = sh->selc[q];
+                int rank = 0;
+                for (int j = 0; j < k; ++j) rank += sh->selc[j] < id;
+                out[r * k + rank] = id;
+            }
         }
         __syncthreads();  // shared state is reused by the next row
     }
@@ -150,40 +274,58 @@ __global__ void __launch_bounds__(kThreads) topk_ids_kernel(const T* __restrict_
 int topk_max_k() { return tk::kMaxK; }
 int topk_max_vocab() { return tk::kMaxChunks * tk::kChunk; }
 
+namespace {
+
+template <typename T>
+int launch_typed(const void* logits, long long rows, int V, long long stride, int k, bool vec_ok,
+                 int64_t* out, cudaStream_t st) {
+    // Per device: the dynamic shared memory opt-in and the resident CTAs (set up once).
+    constexpr int kMaxDev = 64;
+    struct Cache {
+        bool ready;
+        int blocks;
+    };
+    static Cache cache[kMaxDev] = {};
+    static std::mutex mu;
+    const size_t smem = sizeof(tk::Smem);
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return kLaunchFailed;
+    int blocks = 0;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        Cache& c = cache[dev];
+        if (!c.ready) {
+            int per_sm = 0, sms = 0;
+            if (cudaFuncSetAttribute(tk::topk_ids_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     (int)smem) != cudaSuccess ||
+                cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tk::topk_ids_kernel<T>, tk::kThreads,
+                                                              smem) != cudaSuccess ||
+                cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+                per_sm < 1)
+                return kLaunchFailed;
+            c.blocks = per_sm * sms;
+            c.ready = true;
+        }
+        blocks = c.blocks;
+    }
+    const unsigned grid = (unsigned)(rows < blocks ? rows : blocks);
+    tk::topk_ids_kernel<T><<<grid, tk::kThreads, smem, st>>>(static_cast<const T*>(logits), rows, V,
+                                                             stride, k, vec_ok, out);
+    return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
+}
+
+}  // namespace
+
 int launch_topk_ids(const void* logits, int dtype, long long rows, int V, long long stride, int k,
                     int64_t* out, cudaStream_t st) {
-    const size_t smem = sizeof(tk::Smem);
-    int dev = 0, sms = 148;
-    if (cudaGetDevice(&dev) != cudaSuccess) return kLaunchFailed;
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const long long cap = (long long)sms * 3;
-    const unsigned grid = (unsigned)(rows < cap ? rows : cap);
+    const size_t esz = dtype == 1 ? 4 : 2;
+    const bool vec_ok = (reinterpret_cast<uintptr_t>(logits) % 16 == 0) && ((stride * esz) % 16 == 0);
     switch (dtype) {
-        case 0:
-            if (cudaFuncSetAttribute(tk::topk_ids_kernel<__nv_bfloat16>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-                return kLaunchFailed;
-            tk::topk_ids_kernel<__nv_bfloat16><<<grid, tk::kThreads, smem, st>>>(
-                static_cast<const __nv_bfloat16*>(logits), rows, V, stride, k, out);
-            break;
-        case 1:
-            if (cudaFuncSetAttribute(tk::topk_ids_kernel<float>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-                return kLaunchFailed;
-            tk::topk_ids_kernel<float><<<grid, tk::kThreads, smem, st>>>(
-                static_cast<const float*>(logits), rows, V, stride, k, out);
-            break;
-        case 2:
-            if (cudaFuncSetAttribute(tk::topk_ids_kernel<__half>,
-                                     cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
-                return kLaunchFailed;
-            tk::topk_ids_kernel<__half><<<grid, tk::kThreads, smem, st>>>(
-                static_cast<const __half*>(logits), rows, V, stride, k, out);
-            break;
-        default:
-            return kBadDtype;
+        case 0: return launch_typed<__nv_bfloat16>(logits, rows, V, stride, k, vec_ok, out, st);
+        case 1: return launch_typed<float>(logits, rows, V, stride, k, vec_ok, out, st);
+        case 2: return launch_typed<__half>(logits, rows, V, stride, k, vec_ok, out, st);
+        default: return kBadDtype;
     }
-    return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
 }
 
 }  // namespace dsv

@@ -52,9 +52,13 @@ def topk_ids(logits: torch.Tensor, k: int, out: torch.Tensor = None) -> torch.Te
         return out
     _cuda(logits, out)
     stride = logits.stride(0) if n > 1 else v
-    with torch.cuda.device(logits.device):
+    if torch.cuda.current_device() == logits.device.index:
         _lib.call("dsv_topk_ids", n, v, stride, _TOPK_DTYPES[logits.dtype], logits.data_ptr(), k,
                   out.data_ptr(), _stream(logits))
+    else:
+        with torch.cuda.device(logits.device):
+            _lib.call("dsv_topk_ids", n, v, stride, _TOPK_DTYPES[logits.dtype], logits.data_ptr(),
+                      k, out.data_ptr(), _stream(logits))
     return out
 
 
