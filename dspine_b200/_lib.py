@@ -87,6 +87,13 @@ _SIGNATURES = {
     "dsv_accept_compact": [c_int32, c_void_p, c_void_p, c_void_p, ctypes.POINTER(CompactOut),
                            c_void_p, c_void_p],
     "dsv_topk_ids": [c_int64, c_int32, c_int64, c_int32, c_void_p, c_int32, c_void_p, c_void_p],
+    "dsv_topk_ranked": [c_int64, c_int32, c_int64, c_int32, c_void_p, c_int32, c_void_p, c_void_p],
+    "dsv_fp8_quantize_rows": [c_int64, c_int32, c_int64, c_int32, c_void_p, c_void_p, c_int64,
+                              c_void_p, c_void_p],
+    "dsv_fp8_coarse_scores": [c_int32, c_int32, c_int32, c_void_p, c_int64, c_void_p, c_void_p,
+                              c_int64, c_void_p, c_void_p, c_int64, c_void_p, c_void_p],
+    "dsv_rescore_select16": [c_int32, c_int32, c_int32, c_int32, c_void_p, c_int64, c_void_p,
+                             c_void_p, c_int64, c_int32, c_void_p, c_int32, c_void_p, c_void_p],
     "dsv_serial_sample_chain": [c_int32, c_int32, c_int32] + [c_void_p] * 13,
     "dsv_serial_table": [c_int32, c_int32, c_int32, c_int32, c_int32, c_int64, c_void_p, c_int64,
                          c_void_p, c_void_p, c_void_p, c_void_p, c_int64, c_int32, c_void_p,

@@ -451,6 +451,85 @@ int dsv_topk_ids(int64_t rows, int32_t vocab, int64_t row_stride, int32_t dtype,
                    1);
 }
 
+int dsv_topk_ranked(int64_t rows, int32_t vocab, int64_t row_stride, int32_t dtype,
+                    const void* logits, int32_t k, int64_t* out, dsv_stream_t stream) {
+    if (rows < 0 || vocab < 1 || vocab > dsv::topk_max_vocab() || row_stride < vocab) return DSV_BAD_SHAPE;
+    if (k < 1 || k > dsv::topk_ranked_max_k() || k > vocab) return DSV_BAD_SHAPE;
+    if (dtype < 0 || dtype > 2) return DSV_BAD_DTYPE;
+    if (rows == 0) return DSV_OK;
+    if (!logits || !out) return DSV_BAD_POINTER;
+    if (!aligned(logits, dtype == 1 ? 4 : 2)) return DSV_BAD_ALIGNMENT;
+    return counted(dsv::launch_topk_ranked(logits, dtype, rows, vocab, row_stride, k, out,
+                                           (cudaStream_t)stream),
+                   1);
+}
+
+int dsv_fp8_quantize_rows(int64_t rows, int32_t cols, int64_t row_stride, int32_t dtype,
+                          const void* x, void* q, int64_t q_stride, float* scale,
+                          dsv_stream_t stream) {
+    if (rows < 0 || cols < 1 || row_stride < cols || q_stride < cols) return DSV_BAD_SHAPE;
+    if (dtype < 0 || dtype > 1) return DSV_BAD_DTYPE;
+    if (rows == 0) return DSV_OK;
+    if (!x || !q || !scale) return DSV_BAD_POINTER;
+    if (!aligned(x, dtype == 1 ? 4 : 2) || !aligned(scale, 4)) return DSV_BAD_ALIGNMENT;
+    return counted(dsv::launch_fp8_quantize(x, dtype, rows, cols, row_stride, static_cast<uint8_t*>(q),
+                                            q_stride, scale, (cudaStream_t)stream),
+                   1);
+}
+
+int dsv_fp8_coarse_scores(int32_t rows, int32_t vocab, int32_t hidden, const void* xq,
+                          int64_t x_stride, const float* x_scale, const void* wq, int64_t w_stride,
+                          const float* w_scale, void* out, int64_t out_stride, uint32_t* err,
+                          dsv_stream_t stream) {
+    if (rows < 0 || vocab < 1 || hidden < 128 || hidden % 128) return DSV_BAD_SHAPE;
+    if (x_stride < hidden || w_stride < hidden || out_stride < vocab) return DSV_BAD_SHAPE;
+    if (rows == 0) return DSV_OK;
+    if (!xq || !x_scale || !wq || !w_scale || !out || !err) return DSV_BAD_POINTER;
+    // TMA: 16-byte aligned bases and row pitches
+    if (!aligned(xq, 16) || !aligned(wq, 16) || (x_stride % 16) || (w_stride % 16)) return DSV_BAD_ALIGNMENT;
+    if (!aligned(out, 2) || !aligned(x_scale, 4) || !aligned(w_scale, 4) || !aligned(err, 4))
+        return DSV_BAD_ALIGNMENT;
+    dsv::Coarse8Args a = {};
+    a.M = rows;
+    a.N = vocab;
+    a.K = hidden;
+    a.xq = xq;
+    a.x_stride = x_stride;
+    a.sx = x_scale;
+    a.wq = wq;
+    a.w_stride = w_stride;
+    a.sw = w_scale;
+    a.out = out;
+    a.out_stride = out_stride;
+    a.err = err;
+    return counted(dsv::launch_coarse8(a, (cudaStream_t)stream), 1);
+}
+
+int dsv_rescore_select16(int32_t rows, int32_t cands, int32_t hidden, int32_t vocab,
+                         const void* weight, int64_t w_stride, const int64_t* ids,
+                         const void* hidden_rows, int64_t h_stride, int32_t hidden_dtype,
+                         void* scores, int32_t scores_f32, int64_t* out16, dsv_stream_t stream) {
+    if (rows < 0 || cands < 1 || cands > dsv::fp8_max_candidates() || vocab < 1) return DSV_BAD_SHAPE;
+    if (out16 && cands < 16) return DSV_BAD_SHAPE;
+    if (weight) {
+        if (hidden < 8 || hidden % 8 || hidden > dsv::fp8_max_hidden()) return DSV_BAD_SHAPE;
+        if (w_stride < hidden || h_stride < hidden) return DSV_BAD_SHAPE;
+        if (hidden_dtype < 0 || hidden_dtype > 1) return DSV_BAD_DTYPE;
+    } else {
+        hidden = 0;  // selection only
+        if (!out16) return DSV_BAD_POINTER;
+    }
+    if (rows == 0) return DSV_OK;
+    if (!ids || !scores || (weight && !hidden_rows)) return DSV_BAD_POINTER;
+    if ((weight && (!aligned(weight, 16) || (w_stride % 8) || !aligned(hidden_rows, hidden_dtype ? 4 : 2))) ||
+        !aligned(ids, 8) || !aligned(scores, scores_f32 ? 4 : 2) || (out16 && !aligned(out16, 8)))
+        return DSV_BAD_ALIGNMENT;
+    return counted(dsv::launch_rescore16(rows, cands, hidden, vocab, weight, w_stride, ids, hidden_rows,
+                                         hidden_dtype, h_stride, scores, scores_f32, out16,
+                                         (cudaStream_t)stream),
+                   1);
+}
+
 int dsv_serial_sample_chain(int32_t batch, int32_t block_size, int32_t k, const float* table,
                             const float* inv_temp, const int32_t* top_k, const float* top_p,
                             const float* min_p, const int32_t* greedy, const float* u,

@@ -278,11 +278,36 @@ int launch_serial_table(const TableArgs& a, cudaStream_t stream);
 int launch_serial_chain(int bs, int tm1, int k, const int64_t* idx, const int64_t* cand,
                         int64_t* out, const float* conf, float* conf_out, cudaStream_t stream);
 
+// ---- FP8 coarse retrieval (lmhead.cu, fp8.cu) ---------------------------------------------
+struct Coarse8Args {
+    int M, N, K;               // rows, weight rows (vocabulary), hidden (multiple of 128)
+    const void* xq;            // [M, K] e4m3, rows x_stride bytes apart
+    long long x_stride;
+    const float* sx;           // [M]
+    const void* wq;            // [N, K] e4m3, rows w_stride bytes apart
+    long long w_stride;
+    const float* sw;           // [N]
+    void* out;                 // [M, N] bf16 scores, rows out_stride elements apart
+    long long out_stride;
+    unsigned int* err;         // error word (bit 0: a pipeline wait timed out)
+};
+int launch_coarse8(const Coarse8Args& a, cudaStream_t stream);
+int launch_fp8_quantize(const void* x, int dtype, long long rows, int cols, long long stride,
+                        uint8_t* q, long long q_stride, float* scale, cudaStream_t stream);
+int launch_rescore16(int M, int C, int H, int V, const void* w, long long w_stride, const int64_t* ids,
+                     const void* hidden, int hidden_dtype, long long h_stride, void* scores,
+                     int scores_f32, int64_t* out16, cudaStream_t stream);
+int fp8_max_candidates();
+int fp8_max_hidden();
+
 // ---- top-k ids of materialised logits (topk.cu) -------------------------------------------
 int topk_max_k();
 int topk_max_vocab();
 int launch_topk_ids(const void* logits, int dtype, long long rows, int V, long long stride, int k,
                     int64_t* out, cudaStream_t stream);
+int topk_ranked_max_k();
+int launch_topk_ranked(const void* logits, int dtype, long long rows, int V, long long stride, int k,
+                       int64_t* out, cudaStream_t stream);
 
 // ---- per-request steps (small.cu) -----------------------------------------------------------
 struct GreedyArgs {

@@ -28,6 +28,7 @@
 #include <cudaTypedefs.h>
 #include <stdint.h>
 
+#include <cstring>
 #include <mutex>
 
 #include "dsv_common.cuh"
@@ -376,6 +377,208 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// ---- FP8 coarse scores (layers/fp8/coarse.py:84-93) ----------------------------------------
+//
+// scores[r, c] = bf16((sum_h xq[r, h] * wq[c, h]) * sx[r] * sw[c]) with e4m3 operands, the fp32
+// accumulation of tcgen05.mma kind::f8f6f4 and one bf16 rounding: the row-scaled FP8 GEMM the
+// reference runs through torch._scaled_mm (use_fast_accum=False, out_dtype bf16).  Same
+// pipeline as lmhead_kernel: a K stage is 128 e4m3 values = one 128-byte swizzle row, so the
+// stage bytes, the swizzle atoms and the 32-byte descriptor step per MMA (K = 32) are unchanged.
+
+// instruction descriptor, kind::f8f6f4: D f32, A and B e4m3 (format 0), both K-major,
+// M = 128, N = 256
+constexpr uint32_t kIdescF8 = (1u << 4)               // D format f32
+                            | (0u << 7)               // A format e4m3
+                            | (0u << 10)              // B format e4m3
+                            | ((uint32_t)(kBN >> 3) << 17)
+                            | ((uint32_t)(kBM >> 4) << 24);
+constexpr int kBK8 = 128;                  // e4m3 values per stage row (128 bytes)
+
+__device__ __forceinline__ void mma_e4m3(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                         uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "setp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(kIdescF8), "r"(accumulate)
+        : "memory");
+}
+
+struct CoarseArgs {
+    int M, N, K;
+    int mt, nsplit, ntiles;
+    const float* sx;         // [M] row scales of the quantized rows
+    const float* sw;         // [N] row scales of the quantized weight
+    __nv_bfloat16* out;      // [M, N] scores, rows out_stride elements apart
+    long long out_stride;
+    unsigned int* err;       // bit 0 set when a wait timed out
+};
+
+__global__ void __launch_bounds__(kThreads, 1)
+    coarse8_kernel(const __grid_constant__ CUtensorMap tma_x, const __grid_constant__ CUtensorMap tma_w,
+                   CoarseArgs a) {
+    extern __shared__ uint8_t smem_raw[];
+    const uint32_t raw_addr = smem_u32(smem_raw);
+    uint8_t* base = smem_raw + ((1024u - (raw_addr & 1023u)) & 1023u);
+    uint8_t* sa = base;                                  // [kStages][kABytes]
+    uint8_t* sb = base + kStages * kABytes;              // [kStages][kBBytes]
+    Bars* bars = reinterpret_cast<Bars*>(base + kStages * kStageBytes);
+    volatile int* abort = &bars->abort;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int m_tile = blockIdx.x % a.mt;
+    const int j = blockIdx.x / a.mt;
+    const int my_tiles = (j < a.ntiles) ? (a.ntiles - 1 - j) / a.nsplit + 1 : 0;
+    const int nk = a.K / kBK8;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&bars->full[s], 1);
+            mbar_init(&bars->empty[s], 1);
+        }
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&bars->tfull[i], 1);
+            mbar_init(&bars->tempty[i], 4);
+        }
+        mbar_init(&bars->drain, 1);
+        bars->abort = 0;
+        fence_mbar_init();
+    }
+    if (warp == 1) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(
+                         smem_u32(&bars->tmem_base)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem = bars->tmem_base;
+
+    if (warp == 0) {
+        // ---------------- TMA producer ----------------
+        uint32_t g = 0;
+        bool ok = true;
+        for (int t = 0; t < my_tiles && ok; ++t) {
+            const int n_tile = j + t * a.nsplit;
+            for (int kb = 0; kb < nk; ++kb, ++g) {
+                const uint32_t s = g % kStages, ph = (g / kStages) & 1u;
+                if (lane == 0) {
+                    ok = wait_or_abort(&bars->empty[s], ph ^ 1u, abort);
+                    if (ok) {
+                        mbar_arrive_expect_tx(&bars->full[s], (uint32_t)kStageBytes);
+                        tma_load_2d(sa + s * kABytes, &tma_x, kb * kBK8, m_tile * kBM, &bars->full[s]);
+                        tma_load_2d(sb + s * kBBytes, &tma_w, kb * kBK8, n_tile * kBN, &bars->full[s]);
+                    }
+                }
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) break;
+            }
+        }
+        if (lane == 0) {
+            for (uint32_t s = 0; s < kStages && s < g; ++s) {
+                const uint32_t last = g - 1 - ((g - 1 - s) % kStages);
+                if (!mbar_wait_bounded(&bars->full[s], (last / kStages) & 1u)) *abort = 1;
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        // ---------------- MMA issuer ----------------
+        uint32_t g = 0;
+        bool ok = true;
+        for (int t = 0; t < my_tiles && ok; ++t) {
+            const uint32_t acc = t & 1, use = (uint32_t)t >> 1;
+            if (lane == 0) {
+                ok = wait_or_abort(&bars->tempty[acc], (use & 1u) ^ 1u, abort);
+                tc_fence_after();
+            }
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            const uint32_t d_tmem = tmem + acc * kBN;
+            for (int kb = 0; kb < nk; ++kb, ++g) {
+                const uint32_t s = g % kStages, ph = (g / kStages) & 1u;
+                if (lane == 0) {
+                    ok = wait_or_abort(&bars->full[s], ph, abort);
+                    if (ok) {
+                        tc_fence_after();
+                        const uint32_t a0 = smem_u32(sa + s * kABytes);
+                        const uint32_t b0 = smem_u32(sb + s * kBBytes);
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk)   // K = 32 e4m3 = 32 bytes per MMA
+                            mma_e4m3(d_tmem, umma_desc_sw128(a0 + kk * 32),
+                                     umma_desc_sw128(b0 + kk * 32), (kb | kk) != 0);
+                        mma_commit(&bars->empty[s]);
+                    }
+                }
+                ok = __shfl_sync(0xffffffffu, ok, 0);
+                if (!ok) break;
+            }
+            if (ok && lane == 0) mma_commit(&bars->tfull[acc]);
+        }
+        if (lane == 0) {
+            mma_commit(&bars->drain);
+            if (!mbar_wait_bounded(&bars->drain, 0)) *abort = 1;
+        }
+        __syncwarp();
+    } else {
+        // ---------------- epilogue: one row per thread, scaled and rounded to bf16 -------------
+        const int q = warp & 3;
+        const int row = m_tile * kBM + q * 32 + lane;
+        const float sxr = row < a.M ? a.sx[row] : 0.f;
+        __nv_bfloat16* orow = a.out + (long long)(row < a.M ? row : 0) * a.out_stride;
+        const bool vec = ((reinterpret_cast<uintptr_t>(a.out) | (uintptr_t)(a.out_stride * 2)) & 15u) == 0;
+        bool ok = true;
+        for (int t = 0; t < my_tiles; ++t) {
+            const uint32_t acc = t & 1, use = (uint32_t)t >> 1;
+            const int col0 = (j + t * a.nsplit) * kBN;
+            if (lane == 0) ok = wait_or_abort(&bars->tfull[acc], use & 1u, abort);
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            tc_fence_after();
+            const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + acc * kBN;
+#pragma unroll 1
+            for (int c = 0; c < kBN / 32; ++c) {
+                float v[32];
+                __syncwarp();
+                tmem_ld32(taddr + c * 32, v);
+                const int cb = col0 + c * 32;
+                if (row >= a.M || cb >= a.N) continue;
+                if (vec && cb + 32 <= a.N) {
+                    uint32_t pk[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const float lo = v[2 * i] * sxr * __ldg(a.sw + cb + 2 * i);
+                        const float hi = v[2 * i + 1] * sxr * __ldg(a.sw + cb + 2 * i + 1);
+                        const __nv_bfloat162 b2 = __floats2bfloat162_rn(lo, hi);
+                        memcpy(&pk[i], &b2, 4);
+                    }
+                    uint4* dst = reinterpret_cast<uint4*>(orow + cb);
+#pragma unroll
+                    for (int i = 0; i < 4; ++i)
+                        dst[i] = make_uint4(pk[4 * i], pk[4 * i + 1], pk[4 * i + 2], pk[4 * i + 3]);
+                } else {
+#pragma unroll
+                    for (int i = 0; i < 32; ++i)
+                        if (cb + i < a.N) orow[cb + i] = __float2bfloat16_rn(v[i] * sxr * __ldg(a.sw + cb + i));
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&bars->tempty[acc]);
+        }
+        if (!ok) atomicOr(a.err, 1u);
+    }
+
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem),
+                     "r"(kTmemCols)
+                     : "memory");
+    }
+}
+
 // ---- merge of sorted partial lists ---------------------------------------------------------
 
 __device__ __forceinline__ bool ahead(float va, int64_t ia, float vb, int64_t ib) {
@@ -509,6 +712,20 @@ bool make_map(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int
               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// 2-D e4m3 tensor [rows, cols] (bytes), box [box_rows, 128] with 128-byte swizzle
+bool make_map_u8(CUtensorMap* map, const void* ptr, int64_t rows, int64_t cols, int64_t stride,
+                 int box_rows) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)stride};
+    const cuuint32_t box[2] = {(cuuint32_t)kBK8, (cuuint32_t)box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(ptr), dims, strides, box,
+              estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 int sm_count() {
     int dev = 0, n = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return 0;
@@ -591,6 +808,38 @@ int launch_lmhead(const LmHeadArgs& h, cudaStream_t st) {
         h.M, a.nsplit, h.k, a.part_val, tk, (int64_t)a.nsplit * tk, a.part_id, tk,
         (int64_t)a.nsplit * tk, a.part_lse, 1, a.nsplit, h.id_offset, h.pad_id, h.sort_ids,
         h.out_ids, h.out_val, h.out_lse);
+    return cudaGetLastError() == cudaSuccess ? 0 : kLaunchFailed;
+}
+
+int launch_coarse8(const Coarse8Args& h, cudaStream_t st) {
+    using namespace lm;
+    CoarseArgs a = {};
+    a.M = h.M;
+    a.N = h.N;
+    a.K = h.K;
+    geometry(h.M, h.N, &a.mt, &a.nsplit, &a.ntiles);
+    a.sx = h.sx;
+    a.sw = h.sw;
+    a.out = static_cast<__nv_bfloat16*>(h.out);
+    a.out_stride = h.out_stride;
+    a.err = h.err;
+    CUtensorMap mx, mw;
+    if (!make_map_u8(&mx, h.xq, h.M, h.K, h.x_stride, kBM)) return kLaunchFailed;
+    if (!make_map_u8(&mw, h.wq, h.N, h.K, h.w_stride, kBN)) return kLaunchFailed;
+    static int attr_set[64] = {};
+    static std::mutex mu;
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return kLaunchFailed;
+    {
+        std::lock_guard<std::mutex> lock(mu);
+        if (!attr_set[dev]) {
+            if (cudaFuncSetAttribute(coarse8_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                     kSmemBytes) != cudaSuccess)
+                return kLaunchFailed;
+            attr_set[dev] = 1;
+        }
+    }
+    coarse8_kernel<<<a.mt * a.nsplit, kThreads, kSmemBytes, st>>>(mx, mw, a);
     return cudaGetLastError() == cudaSuccess ? 0 : kLaunchFailed;
 }
 

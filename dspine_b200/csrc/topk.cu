@@ -39,18 +39,24 @@ constexpr int kThreads = 256;
 constexpr int kWarps = kThreads / 32;
 constexpr int kChunk = 64;
 constexpr int kMaxChunks = 4096;           // vocabularies up to 262144
-constexpr int kMaxK = 64;
-constexpr int kCandCap = kMaxK * kChunk;   // every element of the selected chunks
+constexpr int kMaxK = 128;                 // 64 for topk_ids, 128 for the ranked form
 constexpr int kChunkBits = 12;             // chunk index < 2^12
 constexpr int kIdBits = 18;                // element id < 2^18
 
 struct Smem {
     unsigned long long ck[kMaxChunks];     // chunk keys
-    unsigned long long cand[kCandCap];     // compacted chunk keys, then candidate keys
     unsigned long long tmax[kThreads];     // thread t: max of chunk keys t, t + 256, ...
+    unsigned long long selk[kMaxK];        // the selected candidate keys
     int selc[kMaxK];                       // the selected chunks, then the selected ids
     unsigned int ncand;
+    unsigned int pad[3];
+    unsigned long long cand[1];            // [k * 64]: compacted chunk keys, then candidate keys
 };
+
+// dynamic shared memory for top-k with k <= kk
+constexpr size_t smem_bytes(int kk) {
+    return sizeof(Smem) - sizeof(unsigned long long) + (size_t)kk * kChunk * sizeof(unsigned long long);
+}
 
 __device__ __forceinline__ uint32_t ordered(float v) {
     if (v != v) return 0u;                 // NaN: below -inf
@@ -124,9 +130,10 @@ __device__ __forceinline__ unsigned long long kth_largest_warp(const unsigned lo
 }
 
 // Warp-wide stream compaction: appends keys[i] (i < n) with keys[i] >= lo to dst in index
-// order; returns the count (every lane).
+// order, writing only the first cap of them; returns the full count (every lane).
 __device__ __forceinline__ int compact_at_least(const unsigned long long* keys, int n,
-                                                unsigned long long lo, unsigned long long* dst) {
+                                                unsigned long long lo, unsigned long long* dst,
+                                                int cap) {
     const int lane = threadIdx.x & 31;
     int m = 0;
     for (int base = 0; base < n; base += 32) {
@@ -134,7 +141,8 @@ __device__ __forceinline__ int compact_at_least(const unsigned long long* keys, 
         const unsigned long long key = i < n ? keys[i] : 0ull;
         const bool take = i < n && key >= lo;
         const unsigned int b = __ballot_sync(0xffffffffu, take);
-        if (take) dst[m + __popc(b & ((1u << lane) - 1u))] = key;
+        const int pos = m + __popc(b & ((1u << lane) - 1u));
+        if (take && pos < cap) dst[pos] = key;
         m += __popc(b);
     }
     return m;
@@ -186,7 +194,8 @@ __device__ __forceinline__ void chunk_maxima(const T* __restrict__ row, int V, b
 template <typename T>
 __global__ void __launch_bounds__(kThreads, 3) topk_ids_kernel(const T* __restrict__ x, long long rows,
                                                             int V, long long stride, int k,
-                                                            bool vec_ok, int64_t* __restrict__ out) {
+                                                            bool vec_ok, bool ranked,
+                                                            int64_t* __restrict__ out) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     Smem* sh = reinterpret_cast<Smem*>(smem_raw);
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
@@ -202,20 +211,33 @@ __global__ void __launch_bounds__(kThreads, 3) topk_ids_kernel(const T* __restri
             sh->tmax[tid] = t;
         }
         __syncthreads();
-        // 2. the k chunks with the largest keys (ties to the lower chunk)
-        if (wid == 0) {
-            // at least k threads hold a key >= lo, so at least k chunk keys are >= lo
+        // 2. the k chunks with the largest keys (ties to the lower chunk); a row of at most k
+        //    chunks (the ranked form only) keeps all of them and every element is a candidate
+        const int nsel = nch < k ? nch : k;
+        if (nch <= k) {
+            for (int c = tid; c < nch; c += kThreads) sh->selc[c] = c;
+            if (tid == 0) {
+                sh->ncand = 0u;
+                sh->tmax[0] = 0ull;
+            }
+        } else if (wid == 0) {
+            // at least k threads hold a key >= lo, so at least k chunk keys are >= lo; the
+            // search runs over those (all chunk keys when they overflow the candidate buffer)
             const unsigned long long lo = kth_largest_warp(sh->tmax, kThreads, k, kChunkBits);
-            const int m = compact_at_least(sh->ck, nch, lo, sh->cand);
+            const int cap = k * kChunk;
+            const int m = compact_at_least(sh->ck, nch, lo, sh->cand, cap);
             __syncwarp();
-            const unsigned long long kc = kth_largest_warp(sh->cand, m, k, kChunkBits);
+            const unsigned long long* pool = m <= cap ? sh->cand : sh->ck;
+            const int np = m <= cap ? m : nch;
+            const unsigned long long kc = kth_largest_warp(pool, np, k, kChunkBits);
             int s = 0;
-            for (int base = 0; base < m; base += 32) {
+            for (int base = 0; base < np; base += 32) {
                 const int i = base + lane;
-                const bool take = i < m && sh->cand[i] >= kc;
+                const unsigned long long key = i < np ? pool[i] : 0ull;
+                const bool take = i < np && key >= kc;
                 const unsigned int b = __ballot_sync(0xffffffffu, take);
                 if (take) sh->selc[s + __popc(b & ((1u << lane) - 1u))] =
-                    (int)(0xFFFFFFFFu - (uint32_t)(sh->cand[i] & 0xFFFFFFFFull));
+                    (int)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull));
                 s += __popc(b);
             }
             if (lane == 0) {
@@ -226,7 +248,7 @@ __global__ void __launch_bounds__(kThreads, 3) topk_ids_kernel(const T* __restri
         __syncthreads();
         // 3. candidates: elements of the selected chunks that reach the k-th chunk maximum
         const uint32_t vmin = (uint32_t)(sh->tmax[0] >> 32);
-        for (int s = wid; s < k; s += kWarps) {
+        for (int s = wid; s < nsel; s += kWarps) {
             const int c = sh->selc[s];
 #pragma unroll
             for (int h = 0; h < 2; ++h) {
@@ -244,25 +266,28 @@ __global__ void __launch_bounds__(kThreads, 3) topk_ids_kernel(const T* __restri
             }
         }
         __syncthreads();
-        // 4. the k largest candidates, written by ascending id
+        // 4. the k largest candidates, written by ascending id (ranked: by descending key,
+        //    i.e. value desc, id asc)
         if (wid == 0) {
             const int n = (int)sh->ncand;
             const unsigned long long kk = kth_largest_warp(sh->cand, n, k, kIdBits);
             int s = 0;
             for (int base = 0; base < n; base += 32) {
                 const int i = base + lane;
-                const bool take = i < n && sh->cand[i] >= kk;
+                const unsigned long long key = i < n ? sh->cand[i] : 0ull;
+                const bool take = i < n && key >= kk;
                 const unsigned int b = __ballot_sync(0xffffffffu, take);
-                if (take) sh->selc[s + __popc(b & ((1u << lane) - 1u))] =
-                    (int)(0xFFFFFFFFu - (uint32_t)(sh->cand[i] & 0xFFFFFFFFull));
+                if (take) sh->selk[s + __popc(b & ((1u << lane) - 1u))] = key;
                 s += __popc(b);
             }
             __syncwarp();
             for (int q = lane; q < k; q += 32) {
-                const int id = sh->selc[q];
+                const unsigned long long key = sh->selk[q];
+                const uint32_t low = (uint32_t)(key & 0xFFFFFFFFull);   // ~id
                 int rank = 0;
-                for (int j = 0; j < k; ++j) rank += sh->selc[j] < id;
-                out[r * k + rank] = id;
+                for (int j = 0; j < k; ++j)
+                    rank += ranked ? sh->selk[j] > key : (uint32_t)(sh->selk[j] & 0xFFFFFFFFull) > low;
+                out[r * k + rank] = (int64_t)(0xFFFFFFFFu - (uint32_t)(key & 0xFFFFFFFFull));
             }
         }
         __syncthreads();  // shared state is reused by the next row
@@ -271,33 +296,36 @@ __global__ void __launch_bounds__(kThreads, 3) topk_ids_kernel(const T* __restri
 
 }  // namespace tk
 
-int topk_max_k() { return tk::kMaxK; }
+int topk_max_k() { return 64; }
+int topk_ranked_max_k() { return tk::kMaxK; }
 int topk_max_vocab() { return tk::kMaxChunks * tk::kChunk; }
 
 namespace {
 
 template <typename T>
 int launch_typed(const void* logits, long long rows, int V, long long stride, int k, bool vec_ok,
-                 int64_t* out, cudaStream_t st) {
-    // Per device: the dynamic shared memory opt-in and the resident CTAs (set up once).
+                 bool ranked, int64_t* out, cudaStream_t st) {
+    // Per device and buffer class (k <= 64, k <= 128): the dynamic shared memory opt-in and the
+    // resident CTAs (set up once).
     constexpr int kMaxDev = 64;
     struct Cache {
         bool ready;
         int blocks;
     };
-    static Cache cache[kMaxDev] = {};
+    static Cache cache[kMaxDev][2] = {};
     static std::mutex mu;
-    const size_t smem = sizeof(tk::Smem);
+    const int cls = k <= 64 ? 0 : 1;
+    const size_t smem = tk::smem_bytes(cls == 0 ? 64 : 128);
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return kLaunchFailed;
     int blocks = 0;
     {
         std::lock_guard<std::mutex> lock(mu);
-        Cache& c = cache[dev];
+        Cache& c = cache[dev][cls];
         if (!c.ready) {
             int per_sm = 0, sms = 0;
             if (cudaFuncSetAttribute(tk::topk_ids_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)smem) != cudaSuccess ||
+                                     (int)tk::smem_bytes(128)) != cudaSuccess ||
                 cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tk::topk_ids_kernel<T>, tk::kThreads,
                                                               smem) != cudaSuccess ||
                 cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
@@ -310,22 +338,32 @@ int launch_typed(const void* logits, long long rows, int V, long long stride, in
     }
     const unsigned grid = (unsigned)(rows < blocks ? rows : blocks);
     tk::topk_ids_kernel<T><<<grid, tk::kThreads, smem, st>>>(static_cast<const T*>(logits), rows, V,
-                                                             stride, k, vec_ok, out);
+                                                             stride, k, vec_ok, ranked, out);
     return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
+}
+
+int launch_any(const void* logits, int dtype, long long rows, int V, long long stride, int k,
+               bool ranked, int64_t* out, cudaStream_t st) {
+    const size_t esz = dtype == 1 ? 4 : 2;
+    const bool vec_ok = (reinterpret_cast<uintptr_t>(logits) % 16 == 0) && ((stride * esz) % 16 == 0);
+    switch (dtype) {
+        case 0: return launch_typed<__nv_bfloat16>(logits, rows, V, stride, k, vec_ok, ranked, out, st);
+        case 1: return launch_typed<float>(logits, rows, V, stride, k, vec_ok, ranked, out, st);
+        case 2: return launch_typed<__half>(logits, rows, V, stride, k, vec_ok, ranked, out, st);
+        default: return kBadDtype;
+    }
 }
 
 }  // namespace
 
 int launch_topk_ids(const void* logits, int dtype, long long rows, int V, long long stride, int k,
                     int64_t* out, cudaStream_t st) {
-    const size_t esz = dtype == 1 ? 4 : 2;
-    const bool vec_ok = (reinterpret_cast<uintptr_t>(logits) % 16 == 0) && ((stride * esz) % 16 == 0);
-    switch (dtype) {
-        case 0: return launch_typed<__nv_bfloat16>(logits, rows, V, stride, k, vec_ok, out, st);
-        case 1: return launch_typed<float>(logits, rows, V, stride, k, vec_ok, out, st);
-        case 2: return launch_typed<__half>(logits, rows, V, stride, k, vec_ok, out, st);
-        default: return kBadDtype;
-    }
+    return launch_any(logits, dtype, rows, V, stride, k, false, out, st);
+}
+
+int launch_topk_ranked(const void* logits, int dtype, long long rows, int V, long long stride, int k,
+                       int64_t* out, cudaStream_t st) {
+    return launch_any(logits, dtype, rows, V, stride, k, true, out, st);
 }
 
 }  // namespace dsv

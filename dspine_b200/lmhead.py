@@ -173,6 +173,18 @@ class TPHead:
         ids = self.group.all_gather(local_ids, dim=-1)
         return merge_topk(values, ids, k)
 
+    def rescore(self, ids, hidden):
+        """The original BF16 head dot of global candidate ids (sampling/tp_head.py:91-103): the
+        owner rank computes it (dsv_rescore_select16), the others contribute 0, one
+        all-reduce sums the exchange."""
+        from .layers.fp8 import gather
+
+        owner = (ids >= self.start) & (ids < self.end)
+        local_ids = (ids - self.start).clamp(0, self.weight.shape[0] - 1).contiguous()
+        scores = gather.rescore(torch, self.weight, local_ids, hidden)
+        scores.masked_fill_(~owner, 0)
+        return self.group.all_reduce(scores)
+
     def topk_lse(self, hidden, k, *, sort_ids=False):
         """Global top-k ids/values and logsumexp of ``hidden @ W_full.T`` with ONE all-gather:
         the local fused head (padding rows beyond num_local excluded, ids shifted by start)
@@ -202,13 +214,18 @@ class TPHead:
 
 
 class TorchGroup:
-    """`all_gather(tensor, dim)` / `world_size` over a torch.distributed process group."""
+    """`all_gather(tensor, dim)` / `all_reduce(tensor)` / `world_size` over a torch.distributed
+    process group."""
 
     def __init__(self, group=None):
         import torch.distributed as dist
         self._dist = dist
         self.group = group
         self.world_size = dist.get_world_size(group)
+
+    def all_reduce(self, tensor):
+        self._dist.all_reduce(tensor, group=self.group)
+        return tensor
 
     def all_gather(self, tensor, dim=0):
         tensor = tensor.contiguous()

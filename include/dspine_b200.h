@@ -294,6 +294,45 @@ int dsv_serial_chain(int32_t batch, int32_t block_size, int32_t k, const int64_t
 int dsv_topk_ids(int64_t rows, int32_t vocab, int64_t row_stride, int32_t dtype,
                  const void* logits, int32_t k, int64_t* out, dsv_stream_t stream);
 
+/* The row's top-k (value desc, id asc) for any k in [1, min(128, vocab)], the ids written in
+ * that rank order: the ids of stable_local_topk's portable path (layers/fp8/coarse.py:19-35: a
+ * stable descending argsort, the first k).  Same kernel as dsv_topk_ids. */
+int dsv_topk_ranked(int64_t rows, int32_t vocab, int64_t row_stride, int32_t dtype,
+                    const void* logits, int32_t k, int64_t* out, dsv_stream_t stream);
+
+/* ---- FP8 coarse retrieval + BF16 rescore (layers/fp8/coarse.py, layers/fp8/gather.py) -------
+ * dsv_fp8_quantize_rows replaces _scale + _quantize (coarse.py:41-55): per row
+ * scale[r] = max|x[r, :]| / 448 (1 for an all-zero row), q[r, c] = e4m3(clamp(x / scale, -448,
+ * 448)) with IEEE division and round-to-nearest-even (dtype 0 bf16, 1 fp32; q rows q_stride
+ * bytes apart).  FullVFP8Coarse.__init__ (coarse.py:58-73) quantizes the head with it once;
+ * retrieve_and_rescore quantizes the hidden rows with it every step. */
+int dsv_fp8_quantize_rows(int64_t rows, int32_t cols, int64_t row_stride, int32_t dtype,
+                          const void* x, void* q, int64_t q_stride, float* scale,
+                          dsv_stream_t stream);
+
+/* Replaces torch.ops.aten._scaled_mm(xq, wq.T, x_scale, w_scale, out_dtype=bf16,
+ * use_fast_accum=False) of retrieve_and_rescore (coarse.py:78-93):
+ * out[r, c] = bf16(sum_h xq[r, h] * wq[c, h] * x_scale[r] * w_scale[c]), fp32 accumulation on
+ * the tensor cores (tcgen05 kind::f8f6f4).  hidden a multiple of 128; xq, wq 16-byte aligned
+ * with row pitches (bytes) multiples of 16.  *err (device, caller-zeroed) gets bit 0 when a
+ * pipeline wait timed out. */
+int dsv_fp8_coarse_scores(int32_t rows, int32_t vocab, int32_t hidden, const void* xq,
+                          int64_t x_stride, const float* x_scale, const void* wq, int64_t w_stride,
+                          const float* w_scale, void* out, int64_t out_stride, uint32_t* err,
+                          dsv_stream_t stream);
+
+/* Replaces rescore + select16 (gather.py:53-79 with gather_dot :7-34 and global_top16 :37-50):
+ * scores[r, c] = sum_h weight[ids[r, c], h] * hidden_rows[r, h] in fp32, stored as bf16
+ * (scores_f32 = 0, the hidden dtype of the reference) or fp32; ids outside [0, vocab) score
+ * -inf.  With out16 non-null, out16[r, :] = the 16 tokens of the 16 selection rounds of
+ * global_top16 (largest stored score, lowest token among equals), ascending.  A null weight
+ * runs the selection alone on the given scores (select16; out16 required).  weight bf16,
+ * 16-byte aligned, pitch a multiple of 8; hidden a multiple of 8, at most 16384; cands <= 128. */
+int dsv_rescore_select16(int32_t rows, int32_t cands, int32_t hidden, int32_t vocab,
+                         const void* weight, int64_t w_stride, const int64_t* ids,
+                         const void* hidden_rows, int64_t h_stride, int32_t hidden_dtype,
+                         void* scores, int32_t scores_f32, int64_t* out16, dsv_stream_t stream);
+
 /* ---- the same verification without a caller workspace ------------------------------------
  * No counterpart in the reference: for callers that cannot allocate device memory (or hand out
  * scratch) at verification time.  Same arguments, outputs and results as dsv_verify_logits,

@@ -1,0 +1,56 @@
+"""The FP8 retrieval oracle pinned on the CPU: its e4m3 encoder against torch's
+float8_e4m3fn conversion, its row quantization against the reference's _scale/_quantize
+formulas (layers/fp8/coarse.py:41-55) run by torch on the CPU, and its selection rules against
+known answers (coarse.py:19-35 lower-index ties; gather.py:37-50 selection rounds)."""
+
+import numpy as np
+import torch
+
+import oracle.fp8 as OF
+
+
+def test_e4m3_encoder_matches_torch():
+    rng = np.random.default_rng(0)
+    vals = np.concatenate([
+        rng.standard_normal(20000) * 50,
+        rng.standard_normal(5000) * 0.01,          # subnormal range
+        np.ldexp(1.0, np.arange(-12, 9)),           # powers of two
+        (np.arange(1, 256) / 8.0),                  # midpoints / exact values
+        [0.0, -0.0, 448.0, -448.0, 2.0 ** -9, 2.0 ** -10, 3 * 2.0 ** -10, 2.0 ** -6 - 2.0 ** -10],
+    ]).astype(np.float32)
+    vals = np.clip(vals, -448, 448).astype(np.float32)
+    # every midpoint between neighbouring codes (ties to even)
+    finite = OF.e4m3_decode(np.arange(0, 0x7F, dtype=np.uint8))
+    mids = ((finite[1:] + finite[:-1]) / 2).astype(np.float32)
+    vals = np.concatenate([vals, mids, -mids])
+    ref = torch.from_numpy(vals).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    np.testing.assert_array_equal(OF.e4m3_encode(vals), ref)
+
+
+def test_decode_encode_round_trip():
+    codes = np.array([c for c in range(256) if c & 0x7F != 0x7F], np.uint8)
+    np.testing.assert_array_equal(OF.e4m3_encode(OF.e4m3_decode(codes).astype(np.float32)), codes)
+
+
+def test_quantize_rows_matches_reference_formula():
+    rng = np.random.default_rng(1)
+    x = (rng.standard_normal((6, 700)) * rng.uniform(0.01, 30, size=(6, 1))).astype(np.float32)
+    x[2] = 0.0                                     # all-zero row: scale 1
+    x[3, 5] = 1e-30                                # tiny row maximum
+    x[3, 6:] = 0.0
+    xt = torch.from_numpy(x).bfloat16().float()    # bf16 inputs, as the hidden rows
+    maximum = xt.abs().amax(dim=1, keepdim=True)
+    scale = torch.where(maximum > 0, maximum / 448.0, torch.ones_like(maximum)).float()
+    q_ref = (xt / scale).clamp(-448.0, 448.0).to(torch.float8_e4m3fn).view(torch.uint8).numpy()
+    q, s = OF.quantize_rows(xt.numpy())
+    np.testing.assert_array_equal(s, scale[:, 0].numpy())
+    np.testing.assert_array_equal(q, q_ref)
+
+
+def test_lexical_topk_and_select16_known_answers():
+    scores = np.array([[1.0, 3.0, 3.0, 2.0, 3.0] + [0.0] * 15], np.float32)
+    np.testing.assert_array_equal(OF.lexical_topk(scores, 4), [[1, 2, 4, 3]])
+    ids = np.arange(100, 120)[None, :]
+    got = OF.select16(scores, ids)
+    expected = sorted([101, 102, 104, 103, 100] + [105 + i for i in range(11)])
+    np.testing.assert_array_equal(got, [expected])
