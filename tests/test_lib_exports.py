@@ -79,3 +79,51 @@ def test_topk_ids_validation(lib):
     assert lib.dsv_topk_ids(2, 262145, 262145, 0, None, 4, None, None) == 1   # vocab too large
     assert lib.dsv_topk_ids(2, 4000, 4000, 0, None, 64, None, None) == 1      # fewer chunks than k
     assert lib.dsv_topk_ids(0, 4096, 4096, 0, None, 4, None, None) == 0       # no rows: no-op
+
+
+def test_fp8_entry_validation(lib):
+    """The FP8 retrieval entries refuse bad shapes, dtypes, pointers and alignments before any
+    launch; the host modules raise ValueError as the reference's argument checks do."""
+    import torch
+
+    from dspine_b200.layers.fp8 import coarse as C
+    from dspine_b200.layers.fp8 import gather as G
+
+    # dsv_topk_ranked: any k in [1, min(128, vocab)]
+    assert lib.dsv_topk_ranked(2, 100, 100, 0, None, 100, None, None) == 3    # shape ok, null pointers
+    assert lib.dsv_topk_ranked(2, 100, 100, 0, None, 101, None, None) == 1    # k > vocab
+    assert lib.dsv_topk_ranked(2, 4096, 4096, 0, None, 129, None, None) == 1  # k > 128
+    assert lib.dsv_topk_ranked(2, 4096, 4096, 3, None, 16, None, None) == 2   # dtype
+    # dsv_fp8_quantize_rows
+    assert lib.dsv_fp8_quantize_rows(2, 64, 64, 0, None, None, 64, None, None) == 3
+    assert lib.dsv_fp8_quantize_rows(2, 64, 32, 0, None, None, 64, None, None) == 1
+    assert lib.dsv_fp8_quantize_rows(2, 64, 64, 2, None, None, 64, None, None) == 2
+    assert lib.dsv_fp8_quantize_rows(0, 64, 64, 0, None, None, 64, None, None) == 0
+    # dsv_fp8_coarse_scores: hidden a multiple of 128, 16-byte TMA alignment
+    cs = lib.dsv_fp8_coarse_scores
+    assert cs(4, 512, 100, None, 100, None, None, 100, None, None, 512, None, None) == 1
+    assert cs(4, 512, 512, None, 512, None, None, 512, None, None, 512, None, None) == 3
+    assert cs(4, 512, 512, 16, 520, 16, 16, 512, 16, 16, 512, 16, None) == 4  # pitch not 16-byte multiple
+    assert cs(0, 512, 512, None, 512, None, None, 512, None, None, 512, None, None) == 0
+    # dsv_rescore_select16
+    rs = lib.dsv_rescore_select16
+    assert rs(4, 129, 512, 1000, None, 512, None, None, 512, 0, None, 0, None, None) == 1  # > 128 candidates
+    assert rs(4, 8, 512, 1000, 16, 512, 16, 16, 512, 0, 16, 0, 16, None) == 1            # top-16 of 8
+    assert rs(4, 128, 500, 1000, 16, 512, 16, 16, 512, 0, 16, 0, None, None) == 1         # hidden % 8
+    assert rs(4, 128, 512, 1000, 16, 512, 16, 16, 512, 2, 16, 0, None, None) == 2         # hidden dtype
+    assert rs(4, 128, 0, 1, None, 0, 16, None, 0, 0, 16, 0, None, None) == 3              # selection needs out16
+    # host modules
+    with pytest.raises(ValueError, match="multiple of 128"):
+        C.FullVFP8Coarse(torch, torch.zeros(64, 100, dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match="bf16 head"):
+        C.FullVFP8Coarse(torch, torch.zeros(64, 128))
+    with pytest.raises(ValueError, match="1 <= k"):
+        C.stable_local_topk(torch.zeros(2, 100), 101)
+    with pytest.raises(ValueError, match="1..128 candidates"):
+        G.rescore(torch, torch.zeros(10, 64, dtype=torch.bfloat16), torch.zeros(2, 129, dtype=torch.int64),
+                  torch.zeros(2, 64, dtype=torch.bfloat16))
+    with pytest.raises(ValueError, match="at least 16"):
+        G.select16(torch, torch.zeros(2, 8), torch.zeros(2, 8, dtype=torch.int64))
+    with pytest.raises(ValueError, match="multiple of 128"):
+        C.coarse_scores(torch.zeros(2, 100, dtype=torch.uint8), torch.ones(2),
+                        torch.zeros(8, 100, dtype=torch.uint8), torch.ones(8))
