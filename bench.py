@@ -51,8 +51,13 @@ WORKLOADS = {
     "config3": "vocab-parallel TP head, TP = --gpus: hidden bf16 [512, 5120] (32 requests x 16), "
                "W [151936, 5120] ~ N(0, 0.02^2) sharded contiguously; per rank fused top-20 + "
                "logsumexp, one all-gather, replicated merge and greedy accept on every rank",
+    "fp8": "FP8 coarse retrieval + BF16 rescore + top-16 (layers/fp8/coarse.py), the optimized "
+           "V=248320 / H=5120 head: hidden bf16 [960, 5120] (64 requests x 15) ~ N(0,1), "
+           "W bf16 [248320, 5120] ~ N(0, 0.02^2) quantized to e4m3 once; per step quantize, "
+           "FP8 GEMM, top-128, rescore, top-16",
 }
 HEAD_SHAPES = {"config2": (1024, 4096, 8, 64), "config3": (512, 5120, 20, 32)}  # rows, H, k, B
+FP8_SHAPE = (960, 5120, 248320)  # rows, H, vocab
 VOCAB = 151936
 HEAD_METRIC = {"config2": "fused LM head + top-8 + logsumexp: hidden rows/s (1024 x 4096 x 151936)",
                "config3": "vocab-parallel TP head top-20 + logsumexp + accept: draft rows/s "
@@ -626,6 +631,102 @@ def run_head(args):
         print(json.dumps(line), flush=True)
 
 
+def run_fp8(args):
+    """FP8 coarse retrieval (one GPU; under torchrun every rank runs an independent replica)."""
+    import torch
+    from dspine_b200 import _lib
+    from dspine_b200.layers.fp8 import coarse as C
+    rank, local_rank, world = dist_env()
+    if not torch.cuda.is_available():
+        raise SystemExit("bench.py needs a CUDA device (there is no CPU fallback)")
+    dev = torch.device("cuda", local_rank)
+    torch.cuda.set_device(dev)
+    rows, H, V = FP8_SHAPE
+    lib = _lib.load()
+    g = torch.Generator(device=dev).manual_seed(7)
+    hidden = torch.randn(rows, H, generator=g, device=dev).to(torch.bfloat16)
+    w = (torch.randn(V, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+    local = C.FullVFP8Coarse(torch, w)
+    wq, sw = local.weight8.view(torch.uint8), local.weight_scale.reshape(-1)
+
+    def step():
+        return local.retrieve_and_rescore(hidden)[0]
+
+    def timed(fn, n):
+        for _ in range(max(args.warmup, 3)):
+            fn()
+        torch.cuda.synchronize(dev)
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(n):
+            fn()
+        b.record()
+        torch.cuda.synchronize(dev)
+        return a.elapsed_time(b) / n
+
+    # K steps back to back (the 1.27 GB e4m3 head is larger than L2: it streams every step)
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize(dev)
+    launches0 = lib.dsv_launch_count()
+    sampler = ClockSampler(dev)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with sampler:
+        t0.record()
+        for _ in range(args.steps):
+            step()
+        t1.record()
+        torch.cuda.synchronize(dev)
+    launches = lib.dsv_launch_count() - launches0
+    ms_per_step = t0.elapsed_time(t1) / args.steps
+    # the dominant kernel alone, and the reference's library call for the same GEMM
+    xq, sx = C.quantize_rows(hidden)
+    gemm_ms = timed(lambda: C.coarse_scores(xq, sx, wq, sw), args.steps)
+    flops = 2.0 * rows * V * H
+    ref_ms = None
+    try:
+        sxt, swt = sx.reshape(-1, 1).contiguous(), local.weight_scale
+        ref_ms = timed(lambda: torch.ops.aten._scaled_mm.default(
+            xq.view(torch.float8_e4m3fn), local.weight8_t, sxt, swt, bias=None, scale_result=None,
+            out_dtype=torch.bfloat16, use_fast_accum=False), args.steps)
+    except Exception as exc:  # the library call is a yardstick only
+        log(f"torch._scaled_mm unavailable: {exc!r}")
+    # end to end: hidden rows from pinned host memory, the 16 tokens of every row read back
+    host_x = hidden.cpu().pin_memory()
+    host_ids = torch.empty(rows, 16, dtype=torch.int64).pin_memory()
+
+    def e2e_step():
+        hidden.copy_(host_x, non_blocking=True)
+        host_ids.copy_(step(), non_blocking=True)
+        torch.cuda.current_stream(dev).synchronize()
+    e2e_ms = timed(e2e_step, max(3, min(args.steps, 20)))
+    if local.error_word():
+        raise SystemExit(f"device error word {local.error_word():#x}")
+    if rank != 0:
+        return
+    achieved = flops / (gemm_ms * 1e-3) / 1e12
+    peak = flops / (ref_ms * 1e-3) / 1e12 if ref_ms else None
+    print(json.dumps({
+        "metric": "FP8 coarse retrieval + rescore + top-16: hidden rows/s (960 x 5120 x 248320)",
+        "value": rows / (ms_per_step * 1e-3), "unit": "rows/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "e4m3 GEMM (fp32 accumulate) + bf16 rescore", "data": "synthetic",
+        "config": {"workload": f"fp8: {WORKLOADS['fp8']}", "rows": rows, "hidden": H, "vocab": V,
+                   "candidates": 128, "parallelism": "dp1 (replicas)",
+                   "l2": "inputs larger than L2 (e4m3 head streamed every step)"},
+        "clocks": sampler.summary(),
+        "e2e": {"value": rows / (e2e_ms * 1e-3), "unit": "rows/s",
+                "h2d_bytes_per_step": host_x.numel() * 2, "d2h_bytes_per_step": host_ids.numel() * 8},
+        "gpu_launches": launches,
+        "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
+                     "frac": achieved / peak if peak else None, "traffic": None,
+                     "peak_source": "torch._scaled_mm (cuBLASLt FP8, same shapes) timed in this run",
+                     "kernel": "dsv::lm::coarse8_kernel", "flops_per_launch": flops,
+                     "kernel_ms": gemm_ms},
+    }), flush=True)
+
+
 def run_head_reference(args):
     rank, _, world = dist_env()
     if rank != 0:
@@ -654,7 +755,13 @@ def run_head_reference(args):
 
 def main():
     args = parse_args()
-    if args.config in HEAD_SHAPES:
+    if args.config == "fp8":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the reference's FP8 head runs "
+                              "torch._scaled_mm and FlashInfer on the GPU; no CPU path"}), flush=True)
+        else:
+            run_fp8(args)
+    elif args.config in HEAD_SHAPES:
         run_head_reference(args) if args.impl == "reference" else run_head(args)
     elif args.impl == "reference":
         run_reference(args)
