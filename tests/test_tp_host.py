@@ -108,3 +108,51 @@ def test_sync_accept_broadcasts_in_place_two_ranks():
     for p in procs:
         p.join(timeout=60)
     assert res == {0: "ok", 1: "ok"}, res
+
+
+def _rescore_worker(rank, world, port, q):
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        dist.init_process_group("gloo", rank=rank, world_size=world)
+        from dspine_b200.layers.fp8 import gather
+        from dspine_b200.lmhead import TPHead, TorchGroup
+
+        # the per-rank dot is a GPU kernel; on CPU ranks it is the reference's CPU formula
+        # (sampling/tp_head.py:100-101), which leaves the exchange logic under test
+        def cpu_rescore(torch_mod, weight, ids, hidden, *, fp32_output=False):
+            return (weight[ids].float() * hidden[:, None].float()).sum(-1).to(hidden.dtype)
+        gather.rescore = cpu_rescore
+        V, H = 1000, 16
+        g = torch.Generator().manual_seed(0)
+        full = torch.randn(V, H, generator=g).to(torch.bfloat16)
+        hidden = torch.randn(3, H, generator=g).to(torch.bfloat16)
+        ids = torch.randint(0, V, (3, 128), generator=g)
+        ids[0, :4] = V                                # padding ids score 0 on every rank
+        start, end = V * rank // world, V * (rank + 1) // world
+        shard = torch.cat([full[start:end], torch.zeros(5, H, dtype=torch.bfloat16)])
+        head = TPHead(shard, start, end, V, TorchGroup())
+        got = head.rescore(ids, hidden)
+        safe = ids.clamp(0, V - 1)
+        expected = (full[safe].float() * hidden[:, None].float()).sum(-1).to(hidden.dtype)
+        expected[0, :4] = 0
+        assert torch.equal(got, expected)
+        dist.destroy_process_group()
+        q.put((rank, "ok"))
+    except Exception as e:  # report to the parent instead of hanging it
+        q.put((rank, repr(e)))
+
+
+def test_tp_rescore_exchange_two_ranks():
+    """TPHead.rescore (sampling/tp_head.py:91-103): the owner rank's dot, zeros elsewhere, one
+    all-reduce: every rank ends with the full-vocabulary scores."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_rescore_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = dict(q.get(timeout=120) for _ in procs)
+    for p in procs:
+        p.join(timeout=60)
+    assert res == {0: "ok", 1: "ok"}, res
