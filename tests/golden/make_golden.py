@@ -22,6 +22,8 @@ Fixture groups (reference function -> file):
   serial    kernels/dspine.py:210-351,616-772 serial_table / serial_chain /
             build_serial_tables / serial_sample_chain, and tests/ref_utils.py:12-76
             ref_sample_chain / ref_refine_table                             serial.npz
+  fp8       layers/fp8/coarse.py FullVFP8Coarse (weight quantization), _scale/_quantize,
+            stable_local_topk; layers/fp8/gather.py rescore / select16      fp8.npz
 """
 
 import os
@@ -481,6 +483,56 @@ def gen_serial(torch, ref_dir):
     return out
 
 
+def gen_fp8(torch):
+    """layers/fp8/coarse.py FullVFP8Coarse.__init__ (weight quantization), _scale/_quantize
+    (hidden rows), stable_local_topk (portable argsort path), and layers/fp8/gather.py rescore
+    and select16 (Triton kernels under the interpreter).  torch's CPU _scaled_mm refuses
+    per-row scales, so the coarse GEMM itself has no CPU fixture."""
+    from sglang_dspine.layers.fp8 import coarse, gather
+
+    out = {}
+    g = torch.Generator().manual_seed(13)
+    # the reference test's exact two-column head (tests/test_topk_compat_cuda.py:103-109)
+    w2 = torch.zeros(512, 512, dtype=torch.bfloat16)
+    w2[:, 0] = torch.arange(512).remainder(47).bfloat16() / 32
+    w2[:, 1] = torch.arange(512).remainder(31).bfloat16() / 64
+    # a random head with an all-zero row and a tiny row
+    wr = (torch.randn(300, 256, generator=g) * 0.05).bfloat16()
+    wr[7] = 0
+    wr[8] = 0
+    wr[8, 3] = 1e-30
+    for name, w in (("two", w2), ("rand", wr)):
+        local = coarse.FullVFP8Coarse(torch, w)
+        out[f"{name}_w"] = _np(w.float())
+        out[f"{name}_wq"] = _np(local.weight8.view(torch.uint8))
+        out[f"{name}_ws"] = _np(local.weight_scale[0])
+    hidden = (torch.randn(6, 256, generator=g) * torch.tensor([[0.01], [1], [30], [0], [2], [5]])).bfloat16()
+    scale = coarse._scale(torch, hidden)
+    out["hidden"] = _np(hidden.float())
+    out["hidden_q"] = _np(coarse._quantize(torch, hidden, scale).view(torch.uint8))
+    out["hidden_s"] = _np(scale[:, 0])
+    # stable top-k of tied bf16 scores
+    scores = ((torch.randn(5, 3000, generator=g) * 3).round() / 2).bfloat16()
+    scores[1] = 1.0
+    scores[2, ::5] = float("-inf")
+    out["topk_scores"] = _np(scores.float())
+    for k in (1, 16, 128):
+        out[f"topk_ids_{k}"] = _np(coarse.stable_local_topk(scores, k, None)[1])
+    # rescore + select16 on the random head
+    ids = torch.stack([torch.randperm(300, generator=g)[:128] for _ in range(6)])
+    rescored = gather.rescore(torch, wr, ids, hidden)
+    out["rescore_ids"] = _np(ids)
+    out["rescore_scores"] = _np(rescored.float())
+    out["rescore_top16"] = _np(gather.select16(torch, rescored, ids))
+    # select16 on heavily tied scores
+    tied = ((torch.randn(4, 128, generator=g)).round() / 2).bfloat16()
+    tied_ids = torch.stack([torch.randperm(1000, generator=g)[:128] for _ in range(4)])
+    out["tied_scores"] = _np(tied.float())
+    out["tied_ids"] = _np(tied_ids)
+    out["tied_top16"] = _np(gather.select16(torch, tied, tied_ids))
+    return out
+
+
 def main(ref_dir):
     os.environ.setdefault("TRITON_INTERPRET", "1")
     os.environ.setdefault("PYTHONDONTWRITEBYTECODE", "1")
@@ -500,6 +552,7 @@ def main(ref_dir):
         "merge": lambda: gen_merge(torch),
         "greedy": lambda: gen_greedy(torch),
         "serial": lambda: gen_serial(torch, ref_dir),
+        "fp8": lambda: gen_fp8(torch),
     }
     only = set(sys.argv[2:])
     for name, fn in groups.items():

@@ -54,3 +54,34 @@ def test_lexical_topk_and_select16_known_answers():
     got = OF.select16(scores, ids)
     expected = sorted([101, 102, 104, 103, 100] + [105 + i for i in range(11)])
     np.testing.assert_array_equal(got, [expected])
+
+
+GOLDEN = np.load(__import__("pathlib").Path(__file__).resolve().parent / "golden" / "fp8.npz")
+
+
+def test_quantization_matches_reference_fixtures():
+    """FullVFP8Coarse.__init__ and _scale/_quantize of the reference (tests/golden/fp8.npz)."""
+    for name in ("two", "rand"):
+        q, s = OF.quantize_rows(GOLDEN[f"{name}_w"])
+        np.testing.assert_array_equal(q, GOLDEN[f"{name}_wq"])
+        np.testing.assert_array_equal(s, GOLDEN[f"{name}_ws"])
+    q, s = OF.quantize_rows(GOLDEN["hidden"])
+    np.testing.assert_array_equal(q, GOLDEN["hidden_q"])
+    np.testing.assert_array_equal(s, GOLDEN["hidden_s"])
+
+
+def test_lexical_topk_matches_reference_stable_topk():
+    for k in (1, 16, 128):
+        np.testing.assert_array_equal(OF.lexical_topk(GOLDEN["topk_scores"], k), GOLDEN[f"topk_ids_{k}"])
+
+
+def test_rescore_and_select16_match_reference_kernels():
+    """gather.rescore (fp32 sums stored bf16) within one bf16 ulp plus the fp32 accumulation
+    bound (the fixture ran under the Triton interpreter, whose fp32 -> bf16 store truncates
+    where the GPU rounds to nearest); select16 exact on the reference's own stored scores."""
+    exact, bound = OF.rescore_exact(GOLDEN["rand_w"], GOLDEN["rescore_ids"], GOLDEN["hidden"])
+    ref = GOLDEN["rescore_scores"]
+    assert (np.abs(ref - exact) <= 2.0 ** -7 * np.abs(exact) + 2.0 ** -12 * bound).all()
+    np.testing.assert_array_equal(OF.select16(ref, GOLDEN["rescore_ids"]), GOLDEN["rescore_top16"])
+    np.testing.assert_array_equal(OF.select16(GOLDEN["tied_scores"], GOLDEN["tied_ids"]),
+                                  GOLDEN["tied_top16"])

@@ -170,3 +170,46 @@ def test_retrieve_and_rescore_random_and_single_shard_tp():
     np.testing.assert_array_equal(t16.cpu().numpy(), top16.cpu().numpy())
     np.testing.assert_array_equal(_bf16_np(tscores), got)
     assert local.error_word() == 0 and tp.error_word() == 0
+
+
+GOLDEN = np.load(__import__("pathlib").Path(__file__).resolve().parent / "golden" / "fp8.npz")
+
+
+def test_reference_fixtures():
+    """tests/golden/fp8.npz (the reference's own FullVFP8Coarse quantization, _scale/_quantize,
+    stable_local_topk, gather.rescore and gather.select16): quantization, the stable top-k and
+    the selection exact; rescored scores within one bf16 ulp of the reference's (its fixture
+    was stored by the Triton interpreter, which truncates to bf16) and within half an ulp plus
+    the fp32 accumulation bound of the exact dot."""
+    for name in ("two", "rand"):
+        w = torch.from_numpy(GOLDEN[f"{name}_w"]).bfloat16().to(DEV)
+        local = C.FullVFP8Coarse(torch, w) if w.shape[1] % 128 == 0 else None
+        q, s = C.quantize_rows(w)
+        torch.cuda.synchronize()
+        np.testing.assert_array_equal(q.cpu().numpy(), GOLDEN[f"{name}_wq"])
+        np.testing.assert_array_equal(s.cpu().numpy(), GOLDEN[f"{name}_ws"])
+        if local is not None:
+            np.testing.assert_array_equal(local.weight8.view(torch.uint8).cpu().numpy(), GOLDEN[f"{name}_wq"])
+    hidden = torch.from_numpy(GOLDEN["hidden"]).bfloat16().to(DEV)
+    q, s = C.quantize_rows(hidden)
+    scores = torch.from_numpy(GOLDEN["topk_scores"]).bfloat16().to(DEV)
+    tops = {k: C.stable_local_topk(scores, k)[1] for k in (1, 16, 128)}
+    w = torch.from_numpy(GOLDEN["rand_w"]).bfloat16().to(DEV)
+    ids = torch.from_numpy(GOLDEN["rescore_ids"]).to(DEV)
+    got, top16 = G.rescore_select16(torch, w, ids, hidden)
+    ref_scores = torch.from_numpy(GOLDEN["rescore_scores"]).bfloat16().to(DEV)
+    sel_ref = G.select16(torch, ref_scores, ids)
+    tied = torch.from_numpy(GOLDEN["tied_scores"]).bfloat16().to(DEV)
+    sel_tied = G.select16(torch, tied, torch.from_numpy(GOLDEN["tied_ids"]).to(DEV))
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(q.cpu().numpy(), GOLDEN["hidden_q"])
+    np.testing.assert_array_equal(s.cpu().numpy(), GOLDEN["hidden_s"])
+    for k, t in tops.items():
+        np.testing.assert_array_equal(t.cpu().numpy(), GOLDEN[f"topk_ids_{k}"])
+    exact, bound = OF.rescore_exact(GOLDEN["rand_w"], GOLDEN["rescore_ids"], GOLDEN["hidden"])
+    g = _bf16_np(got)
+    assert (np.abs(g - exact) <= 2.0 ** -8 * np.abs(exact) + 2.0 ** -12 * bound).all()
+    assert (np.abs(g - GOLDEN["rescore_scores"]) <= 2.0 ** -7 * np.abs(exact) + 2.0 ** -11 * bound).all()
+    np.testing.assert_array_equal(top16.cpu().numpy(), OF.select16(g, GOLDEN["rescore_ids"]))
+    np.testing.assert_array_equal(sel_ref.cpu().numpy(), GOLDEN["rescore_top16"])
+    np.testing.assert_array_equal(sel_tied.cpu().numpy(), GOLDEN["tied_top16"])
