@@ -213,3 +213,34 @@ def test_reference_fixtures():
     np.testing.assert_array_equal(top16.cpu().numpy(), OF.select16(g, GOLDEN["rescore_ids"]))
     np.testing.assert_array_equal(sel_ref.cpu().numpy(), GOLDEN["rescore_top16"])
     np.testing.assert_array_equal(sel_tied.cpu().numpy(), GOLDEN["tied_top16"])
+
+
+def test_retrieve_and_rescore_replays_in_a_cuda_graph():
+    """tests/test_topk_compat_cuda.py:121-132: the step captured once in a CUDA graph and
+    replayed on new hidden rows gives the eager results."""
+    w = torch.zeros(512, 512, dtype=torch.bfloat16)
+    w[:, 0] = torch.arange(512).remainder(47).bfloat16() / 32
+    w[:, 1] = torch.arange(512).remainder(31).bfloat16() / 64
+    local = C.FullVFP8Coarse(torch, w.to(DEV))
+    hidden = torch.zeros(4, 512, device=DEV, dtype=torch.bfloat16)
+    hidden[:, :2] = torch.tensor([[1, 2], [2, -1], [-1, 1], [0, 0]], device=DEV)
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(3):
+            local.retrieve_and_rescore(hidden)
+    torch.cuda.current_stream().wait_stream(side)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    try:
+        with torch.cuda.graph(graph):
+            replayed = local.retrieve_and_rescore(hidden)
+        for _ in range(2):
+            hidden.neg_()
+            graph.replay()
+            eager = local.retrieve_and_rescore(hidden)
+            torch.cuda.synchronize()
+            for a, b in zip(replayed, eager):
+                assert torch.equal(a, b)
+    finally:
+        graph.reset()
