@@ -631,6 +631,51 @@ def run_head(args):
         print(json.dumps(line), flush=True)
 
 
+def fp8_cpu_time(n_rows, cores, vocab=None):
+    """torch CPU port of retrieve_and_rescore (layers/fp8/coarse.py:41-113, gather.py) on
+    n_rows hidden rows over the whole vocabulary: e4m3 quantization with per-row scales, the
+    coarse product in fp32 over dequantized codes (vocabulary chunks), stable top-128, the
+    BF16 rescore and the 16 selection rounds.  Returns once() -> seconds of one step."""
+    import torch
+    torch.set_num_threads(cores)
+    _, H, V = FP8_SHAPE
+    V = vocab or V
+    chunk = 16384
+    g = torch.Generator().manual_seed(17)
+
+    def quantize(t):
+        amax = t.float().abs().amax(dim=1, keepdim=True)
+        sc = torch.where(amax > 0, amax / 448.0, torch.ones_like(amax))
+        return (t.float() / sc).clamp(-448.0, 448.0).to(torch.float8_e4m3fn), sc[:, 0]
+
+    w = torch.empty(V, H, dtype=torch.bfloat16)
+    w8 = torch.empty(V, H, dtype=torch.float8_e4m3fn)
+    sw = torch.empty(V)
+    for s0 in range(0, V, chunk):
+        blk = (torch.randn(min(chunk, V - s0), H, generator=g) * 0.02).bfloat16()
+        w[s0:s0 + blk.shape[0]] = blk
+        w8[s0:s0 + blk.shape[0]], sw[s0:s0 + blk.shape[0]] = quantize(blk)
+    x = torch.randn(n_rows, H, generator=g).bfloat16()
+
+    def once():
+        t0 = time.perf_counter()
+        xq, sx = quantize(x)
+        xf = xq.float()
+        coarse = torch.empty(n_rows, V, dtype=torch.bfloat16)
+        for s0 in range(0, V, chunk):
+            s1 = min(V, s0 + chunk)
+            coarse[:, s0:s1] = ((xf @ w8[s0:s1].float().T) * sx[:, None] * sw[None, s0:s1]).bfloat16()
+        ids = torch.argsort(coarse.float(), dim=1, descending=True, stable=True)[:, :128]
+        scores = (w[ids].float() * x.float()[:, None]).sum(-1).bfloat16()
+        # 16 best by (stored score desc, token asc), ascending tokens
+        by_id = torch.argsort(ids, dim=1)
+        sv, si = scores.gather(1, by_id), ids.gather(1, by_id)
+        best = torch.argsort(sv.float(), dim=1, descending=True, stable=True)[:, :16]
+        si.gather(1, best).sort(dim=1)
+        return time.perf_counter() - t0
+    return once
+
+
 def run_fp8(args):
     """FP8 coarse retrieval (one GPU; under torchrun every rank runs an independent replica)."""
     import torch
@@ -706,7 +751,17 @@ def run_fp8(args):
         return
     achieved = flops / (gemm_ms * 1e-3) / 1e12
     peak = flops / (ref_ms * 1e-3) / 1e12 if ref_ms else None
-    print(json.dumps({
+    cpu = None
+    if world == 1 and not args.no_cpu_baseline:
+        cores = host_cores()
+        n_cpu = 2
+        once = fp8_cpu_time(n_cpu, cores)
+        once()
+        t = min(once() for _ in range(2))
+        cpu = {"value": n_cpu / t, "unit": "rows/s", "cores": cores, "kind": "port",
+               "sample": f"{n_cpu} rows x full vocabulary: torch CPU port (e4m3 quantization, "
+                         f"fp32 coarse product, stable top-128, bf16 rescore, top-16), {cores} threads"}
+    line = {
         "metric": "FP8 coarse retrieval + rescore + top-16: hidden rows/s (960 x 5120 x 248320)",
         "value": rows / (ms_per_step * 1e-3), "unit": "rows/s", "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_per_step,
@@ -724,6 +779,37 @@ def run_fp8(args):
                      "peak_source": "torch._scaled_mm (cuBLASLt FP8, same shapes) timed in this run",
                      "kernel": "dsv::lm::coarse8_kernel", "flops_per_launch": flops,
                      "kernel_ms": gemm_ms},
+    }
+    if cpu is not None:
+        line["cpu_baseline"] = cpu
+    print(json.dumps(line), flush=True)
+
+
+def run_fp8_reference(args):
+    """The CPU port of retrieve_and_rescore on every host core (rank 0 only)."""
+    rank, _, _ = dist_env()
+    if rank != 0:
+        return
+    cores = host_cores()
+    n_rows = 2
+    once = fp8_cpu_time(n_rows, cores)
+    for _ in range(min(args.warmup, 1)):
+        once()
+    times = [once() for _ in range(min(args.steps, 3))]
+    step_s = sum(times) / len(times)
+    value = n_rows / step_s
+    print(json.dumps({
+        "impl": "reference",
+        "metric": "FP8 coarse retrieval + rescore + top-16: hidden rows/s (960 x 5120 x 248320)",
+        "value": value, "unit": "rows/s", "n_gpus": args.gpus, "steps": len(times),
+        "warmup": args.warmup, "ms_per_step": step_s * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "e4m3 codes, fp32 product, bf16 rescore",
+        "data": "synthetic",
+        "config": {"workload": f"fp8: {WORKLOADS['fp8']}", "sample_rows": n_rows,
+                   "parallelism": "host cores"},
+        "cpu_baseline": {"value": value, "unit": "rows/s", "cores": cores, "kind": "port",
+                         "sample": f"{n_rows} rows x full vocabulary per step: torch CPU port"},
+        "e2e": {"value": value, "unit": "rows/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }), flush=True)
 
 
@@ -756,11 +842,7 @@ def run_head_reference(args):
 def main():
     args = parse_args()
     if args.config == "fp8":
-        if args.impl == "reference":
-            print(json.dumps({"impl": "reference", "unavailable": "the reference's FP8 head runs "
-                              "torch._scaled_mm and FlashInfer on the GPU; no CPU path"}), flush=True)
-        else:
-            run_fp8(args)
+        run_fp8_reference(args) if args.impl == "reference" else run_fp8(args)
     elif args.config in HEAD_SHAPES:
         run_head_reference(args) if args.impl == "reference" else run_head(args)
     elif args.impl == "reference":
