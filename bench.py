@@ -751,6 +751,11 @@ def run_fp8(args):
         return
     achieved = flops / (gemm_ms * 1e-3) / 1e12
     peak = flops / (ref_ms * 1e-3) / 1e12 if ref_ms else None
+    traffic = None   # DRAM bytes of one full launch, scaled from a smaller ncu capture
+    prof = ROOT / "profiles" / "fp8_retrieval_v248320_h5120.md"
+    if prof.exists():
+        m = re.search(r"full_launch_dram_bytes_coarse8_kernel:\s*([0-9]+)", prof.read_text())
+        traffic = float(m.group(1)) if m else None
     cpu = None
     if world == 1 and not args.no_cpu_baseline:
         cores = host_cores()
@@ -775,7 +780,8 @@ def run_fp8(args):
                 "h2d_bytes_per_step": host_x.numel() * 2, "d2h_bytes_per_step": host_ids.numel() * 8},
         "gpu_launches": launches,
         "roofline": {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s",
-                     "frac": achieved / peak if peak else None, "traffic": None,
+                     "frac": achieved / peak if peak else None, "traffic": traffic,
+                     "traffic_source": "ncu capture at V=32768 scaled by vocabulary rows",
                      "peak_source": "torch._scaled_mm (cuBLASLt FP8, same shapes) timed in this run",
                      "kernel": "dsv::lm::coarse8_kernel", "flops_per_launch": flops,
                      "kernel_ms": gemm_ms},
