@@ -18,6 +18,7 @@ from __future__ import annotations
 
 from dataclasses import dataclass, field
 
+import numpy as np
 import torch
 
 T = 16
@@ -178,6 +179,56 @@ def config1(seed=1, device="cpu", V=VOCAB, B=64) -> Batch:
     lens, temperature, top_k, top_p = config1_params(B, seed)
     return build(lens, temperature, top_k, top_p, V=V, dtype=torch.bfloat16, seed=seed + 100,
                  device=device)
+
+
+def subset(batch: Batch, requests) -> Batch:
+    """The requests `requests` of `batch` (in that order) as a batch of their own: their
+    target and draft rows repacked, every per-request tensor indexed.  The rows are the very
+    rows of the parent batch, so results on a subset equal the parent's for those requests."""
+    idx = torch.as_tensor(list(requests), dtype=torch.int64)
+    lens = batch.verify_lens.cpu()[idx]
+    nd = (lens.long() - 1).clamp_min(0)
+
+    def rows_of(src, starts, counts):
+        parts = [src[int(s):int(s) + int(n)] for s, n in zip(starts, counts)]
+        return torch.cat(parts) if parts else src[:0]
+
+    tgt = rows_of(batch.target_logits.cpu(), batch.target_rows.cpu()[idx], lens)
+    tgt_rows = torch.zeros(idx.numel(), dtype=torch.int64)
+    tgt_rows[1:] = lens.long().cumsum(0)[:-1]
+    draft = draft_rows = None
+    if batch.draft_logits is not None:
+        draft = rows_of(batch.draft_logits.cpu(), batch.draft_rows.cpu()[idx], nd)
+        if draft.shape[0] == 0:
+            draft = batch.draft_logits.cpu()[:1]
+        draft_rows = torch.zeros(idx.numel(), dtype=torch.int64)
+        draft_rows[1:] = nd.cumsum(0)[:-1]
+    slots = slot_rows = None
+    if batch.slots is not None:
+        slots = rows_of(batch.slots.cpu(), batch.slot_rows.cpu()[idx], lens)
+        slot_rows = tgt_rows.clone()
+
+    def pick(t):
+        return t.cpu()[idx].contiguous()
+    sub = Batch(batch.V, pick(batch.candidates), tgt, tgt_rows, draft, draft_rows,
+                pick(batch.temperature), pick(batch.top_k), pick(batch.top_p), lens.contiguous(),
+                pick(batch.uniforms), pick(batch.uniform_final), pick(batch.prefix_lens), slots,
+                slot_rows, meta=dict(batch.meta, subset=idx.tolist()))
+    return sub.to(batch.candidates.device)
+
+
+def config1_subset(n=16, seed=1, device="cpu") -> Batch:
+    """The first n requests of the config 1 batch (the benchmark's own rows)."""
+    return subset(config1(seed=seed), range(n)).to(device)
+
+
+def fingerprint(batch: Batch) -> np.ndarray:
+    """float64 sums of the target logits, draft logits and uniforms plus the candidate sum: a
+    check that a regenerated batch is the one a fixture was made from."""
+    def s(t):
+        return 0.0 if t is None else float(t.double().sum())
+    return np.array([s(batch.target_logits), s(batch.draft_logits), s(batch.uniforms),
+                     s(batch.uniform_final), float(batch.candidates.sum())], dtype=np.float64)
 
 
 def config4(seed=4, device="cpu", V=VOCAB, B=256) -> Batch:

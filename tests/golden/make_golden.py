@@ -24,6 +24,8 @@ Fixture groups (reference function -> file):
             ref_sample_chain / ref_refine_table                             serial.npz
   fp8       layers/fp8/coarse.py FullVFP8Coarse (weight quantization), _scale/_quantize,
             stable_local_topk; layers/fp8/gather.py rescore / select16      fp8.npz
+  fullv     configs 0, 1 and 4 at V = 151936: ref_target_row rows +
+            sampling/rejection.py:101-153 sample_capped_chain_from_probs     fullv.npz
 """
 
 import os
@@ -533,6 +535,78 @@ def gen_fp8(torch):
     return out
 
 
+def _fullv_case(torch, batch, ref_target_row, chain):
+    """Reference outputs of one benchmark batch at the full vocabulary: target rows through
+    ref_target_row (float64, then float32) or a one-hot at the lowest-index argmax for greedy
+    requests (runtime/worker.py:461-469), q rows the same filter on the draft logits (one-hot
+    at the drafted token for greedy requests), then the reference's
+    sample_capped_chain_from_probs under the Triton interpreter."""
+    B, V = batch.B, batch.V
+    lens = batch.verify_lens.tolist()
+    P = torch.zeros(B, 16, V)
+    Q = torch.zeros(B, 15, V)
+    for b in range(B):
+        T, k, tp = float(batch.temperature[b]), int(batch.top_k[b]), float(batch.top_p[b])
+        greedy = k <= 1 or not T > 0
+        for s in range(lens[b]):
+            row = batch.target_logits[int(batch.target_rows[b]) + s]
+            if greedy:
+                P[b, s, int(row.argmax())] = 1.0
+            else:
+                P[b, s] = ref_target_row(row.float(), T, k, tp, 0.0, "flashinfer").float()
+        for s in range(lens[b] - 1):
+            if greedy:
+                Q[b, s, int(batch.candidates[b, s + 1])] = 1.0
+            else:
+                row = batch.draft_logits[int(batch.draft_rows[b]) + s]
+                Q[b, s] = ref_target_row(row.float(), T, k, tp, 0.0, "flashinfer").float()
+    outs = _buffers(torch, B)
+    chain(candidates=batch.candidates, target_probs=P.contiguous(), draft_probs=Q.contiguous(),
+          verify_lens=batch.verify_lens, uniforms=batch.uniforms,
+          uniform_final=batch.uniform_final, prefix_lens=batch.prefix_lens, outputs=outs)
+    # distance of each bonus draw from the nearest CDF step, relative to the draw's mass
+    # (float64 over the float32 rows the reference kernel consumed)
+    margin = np.zeros(B)
+    for b in range(B):
+        a = int(outs[0][b])
+        p = P[b, a].double()
+        if a == lens[b] - 1:
+            w = p
+        else:
+            w = (p - Q[b, a].double().clamp(0, 1)).clamp_min(0)
+            if float(w.sum()) <= 0:
+                w = p
+        cdf = torch.cumsum(w, 0)
+        thr = float(batch.uniform_final[b]) * float(cdf[-1])
+        j = int(outs[2][b])
+        lo = float(cdf[j - 1]) if j > 0 else 0.0
+        margin[b] = min(abs(thr - lo), abs(float(cdf[j]) - thr)) / float(cdf[-1])
+    return outs, margin
+
+
+def gen_fullv(torch):
+    """Benchmark configurations at V = 151936 pinned to the reference itself: configs 0, 1
+    and 4 whole (dspine_b200.workloads), outputs of the reference's
+    sample_capped_chain_from_probs over ref_target_row probabilities.  Only the outputs, a
+    fingerprint of the regenerated inputs and the draw margins are stored; the tests
+    regenerate the inputs from the same seeds."""
+    from ref_utils import ref_target_row
+    from sglang_dspine.sampling.rejection import sample_capped_chain_from_probs
+
+    sys.path.insert(0, str(HERE.parents[1]))
+    from dspine_b200 import workloads
+
+    out = {}
+    for name, batch in (("config0", workloads.config0()), ("config1", workloads.config1()),
+                        ("config4", workloads.config4())):
+        outs, margin = _fullv_case(torch, batch, ref_target_row, sample_capped_chain_from_probs)
+        out[f"{name}_fingerprint"] = workloads.fingerprint(batch)
+        out[f"{name}_margin"] = margin
+        for key, val in zip(("accept", "commit", "bonus", "output", "new_seq"), outs):
+            out[f"{name}_{key}"] = _np(val)
+    return out
+
+
 def main(ref_dir):
     os.environ.setdefault("TRITON_INTERPRET", "1")
     os.environ.setdefault("PYTHONDONTWRITEBYTECODE", "1")
@@ -542,6 +616,7 @@ def main(ref_dir):
     import torch
 
     torch.manual_seed(0)
+    sys.path.insert(0, str(Path(ref_dir) / "tests"))
     groups = {
         "chain": lambda: gen_chain(torch),
         "sparse": lambda: gen_sparse(torch),
@@ -553,6 +628,7 @@ def main(ref_dir):
         "greedy": lambda: gen_greedy(torch),
         "serial": lambda: gen_serial(torch, ref_dir),
         "fp8": lambda: gen_fp8(torch),
+        "fullv": lambda: gen_fullv(torch),
     }
     only = set(sys.argv[2:])
     for name, fn in groups.items():
