@@ -222,13 +222,17 @@ def config1_subset(n=16, seed=1, device="cpu") -> Batch:
     return subset(config1(seed=seed), range(n)).to(device)
 
 
-def fingerprint(batch: Batch) -> np.ndarray:
-    """float64 sums of the target logits, draft logits and uniforms plus the candidate sum: a
-    check that a regenerated batch is the one a fixture was made from."""
-    def s(t):
-        return 0.0 if t is None else float(t.double().sum())
-    return np.array([s(batch.target_logits), s(batch.draft_logits), s(batch.uniforms),
-                     s(batch.uniform_final), float(batch.candidates.sum())], dtype=np.float64)
+def fingerprint(batch: Batch) -> str:
+    """SHA-256 of the raw bytes of the logits, candidates and uniforms: a check that a
+    regenerated batch is bit for bit the one a fixture was made from."""
+    import hashlib
+
+    h = hashlib.sha256()
+    for t in (batch.target_logits, batch.draft_logits, batch.candidates, batch.uniforms,
+              batch.uniform_final):
+        if t is not None:
+            h.update(t.detach().cpu().contiguous().view(torch.uint8).numpy().tobytes())
+    return h.hexdigest()
 
 
 def config4(seed=4, device="cpu", V=VOCAB, B=256) -> Batch:
