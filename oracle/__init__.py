@@ -68,6 +68,21 @@ def lib():
     L.or_process_row.restype = None
     L.or_process_row.argtypes = [F32P, c.c_int32, c.c_float, c.c_int32, c.c_float,
                                  c.POINTER(RowDesc)]
+    L.or_process_row_ex.restype = None
+    L.or_process_row_ex.argtypes = [F32P, c.c_int32, c.c_float, c.c_int32, c.c_float, c.c_float,
+                                    c.c_int32, c.POINTER(RowDesc)]
+    L.or_minp_floor.restype = c.c_uint32
+    L.or_minp_floor.argtypes = [c.c_float, c.c_float, c.c_float]
+    L.or_target_probs_ex.restype = None
+    L.or_target_probs_ex.argtypes = [F32P, c.c_int64, c.c_int32, c.c_int32, F32P, I32P, F32P,
+                                     c.c_void_p, c.c_int32, F32P, c.c_int32]
+    L.or_verify_logits_ex.restype = None
+    L.or_verify_logits_ex.argtypes = [c.c_int32, c.c_int32, I64P, F32P, I64P, c.c_void_p, I64P,
+                                      c.c_int64, F32P, I32P, F32P, c.c_void_p, c.c_int32, I32P,
+                                      F32P, F32P, I32P, I32P, I32P, I64P, I64P, I32P, c.c_int32]
+    L.or_sparse_target.restype = None
+    L.or_sparse_target.argtypes = [F32P, c.c_int64, c.c_int32, F32P, I32P, F32P, c.c_int32,
+                                   I32P, F32P, I32P, I32P, F32P, c.c_int32]
     L.or_target_probs.restype = None
     L.or_target_probs.argtypes = [F32P, c.c_int64, c.c_int32, c.c_int32, F32P, I32P, F32P,
                                   F32P, c.c_int32]
@@ -153,23 +168,61 @@ def scale_floor(u: float, m: int) -> int:
 # ---- target distribution (runtime/worker.py:440-508) -----------------------------------
 
 
-def process_row(logits, temperature, top_k, top_p) -> RowDesc:
+# filter modes of runtime/worker.py:473-508 (dsv_oracle.h OR_JOINT / OR_SEQ / OR_TORCH)
+JOINT, SEQUENTIAL, TORCH = 0, 1, 2
+
+
+def filter_mode(sampling_backend: str, need_min_p: bool) -> int:
+    """The filter mode of a batch: the pytorch backend, or flashinfer with the batch's min-p
+    flag deciding between the sequential and the joint filter (runtime/worker.py:473-508)."""
+    if sampling_backend == "pytorch":
+        return TORCH
+    if sampling_backend == "flashinfer":
+        return SEQUENTIAL if need_min_p else JOINT
+    raise ValueError(f"unsupported sampling backend {sampling_backend!r}")
+
+
+def process_row(logits, temperature, top_k, top_p, min_p=0.0, mode=JOINT) -> RowDesc:
     l = _f32(logits).reshape(-1)
     d = RowDesc()
-    lib().or_process_row(l, l.size, float(temperature), int(top_k), float(top_p), ctypes.byref(d))
+    lib().or_process_row_ex(l, l.size, float(temperature), int(top_k), float(top_p),
+                            float(min_p), int(mode), ctypes.byref(d))
     return d
 
 
-def target_probs(logits, temperature, top_k, top_p, rows_per_request=1, nthreads=None):
-    """Dense p [rows, V] of build_dspine_target_probs (flashinfer backend, min-p off).
-    temperature/top_k/top_p are per request; request of row r = r // rows_per_request."""
+def minp_floor(m, c, min_p) -> int:
+    return int(lib().or_minp_floor(float(m), float(c), float(min_p)))
+
+
+def target_probs(logits, temperature, top_k, top_p, rows_per_request=1, nthreads=None,
+                 min_p=None, mode=JOINT):
+    """Dense p [rows, V] of build_dspine_target_probs; temperature/top_k/top_p (and min_p)
+    are per request; request of row r = r // rows_per_request; mode = filter mode."""
     l = _f32(logits)
     rows, V = l.shape
     out = np.empty_like(l)
-    lib().or_target_probs(l, rows, V, int(rows_per_request), _f32(temperature).reshape(-1),
-                          _i32(top_k).reshape(-1), _f32(top_p).reshape(-1), out,
-                          _nthreads(nthreads))
+    mp = None if min_p is None else _f32(min_p).reshape(-1)
+    lib().or_target_probs_ex(l, rows, V, int(rows_per_request), _f32(temperature).reshape(-1),
+                             _i32(top_k).reshape(-1), _f32(top_p).reshape(-1), _ptr(mp),
+                             int(mode), out, _nthreads(nthreads))
     return out
+
+
+def sparse_target(logits, temperature, top_k, top_p, capacity=32, nthreads=None):
+    """build_sparse_target (sampling/sparse/target.py:95-178) per row: returns (ids i32
+    [rows, capacity], values f32, lengths i32, overflow i32, dense f32 [rows, V] with the
+    overflow rows written and the others zero).  temperature/top_k/top_p are per row."""
+    l = _f32(logits)
+    rows, V = l.shape
+    ids = np.empty((rows, capacity), np.int32)
+    vals = np.empty((rows, capacity), np.float32)
+    lens = np.empty(rows, np.int32)
+    ovf = np.empty(rows, np.int32)
+    dense = np.zeros_like(l)
+    lib().or_sparse_target(l, rows, V, _f32(temperature).reshape(-1), _i32(top_k).reshape(-1),
+                           _f32(top_p).reshape(-1), int(capacity), ids, vals, lens, ovf, dense,
+                           _nthreads(nthreads))
+    return ids, vals, lens, ovf, dense
 
 
 # ---- rejection (sampling/rejection.py:12-153) ------------------------------------------
@@ -196,7 +249,7 @@ def chain_from_probs(candidates, target_probs, draft_probs, verify_lens, uniform
 
 def verify_logits(candidates, target_logits, target_rows, draft_logits, draft_rows,
                   temperature, top_k, top_p, verify_lens, uniforms, uniform_final,
-                  prefix_lens, nthreads=None):
+                  prefix_lens, nthreads=None, min_p=None, mode=JOINT):
     """Fused logits -> target p, draft q -> chain + residual bonus.  target_logits/draft_logits
     are [rows, V] (any float dtype, computed in fp32); target_rows[b] / draft_rows[b] give the
     first row of request b.  draft_logits=None: q is one-hot at the drafted token."""
@@ -209,10 +262,11 @@ def verify_logits(candidates, target_logits, target_rows, draft_logits, draft_ro
         raise ValueError("draft vocab differs")
     out = _outputs(B)
     drows = _i64(draft_rows if draft_rows is not None else np.zeros(B))
-    lib().or_verify_logits(B, V, cand, tl, _i64(target_rows), _ptr(dl), drows, V,
-                           _f32(temperature), _i32(top_k), _f32(top_p), _i32(verify_lens),
-                           _f32(uniforms), _f32(uniform_final), _i32(prefix_lens), *out,
-                           _nthreads(nthreads))
+    mp = None if min_p is None else _f32(min_p).reshape(-1)
+    lib().or_verify_logits_ex(B, V, cand, tl, _i64(target_rows), _ptr(dl), drows, V,
+                              _f32(temperature), _i32(top_k), _f32(top_p), _ptr(mp), int(mode),
+                              _i32(verify_lens), _f32(uniforms), _f32(uniform_final),
+                              _i32(prefix_lens), *out, _nthreads(nthreads))
     return out
 
 

@@ -97,8 +97,50 @@ static int row_is_greedy(float T, int32_t top_k, float* c_out) {
     return (top_k <= 1) || !(T > 0.0f) || !(c < INFINITY);
 }
 
-void or_process_row(const float* l, int32_t V, float T, int32_t top_k, float top_p,
-                    or_row_desc* d) {
+/* min-p key floor (runtime/worker.py:485-491 "p >= min_p * max p"; tests/ref_utils.py:95-105):
+ * the max element has e = exp2(0) = 1, so the test is e >= min_p.  exp2 is monotone only up to
+ * one-ulp ripples, so the floor is defined as the result of a bisection over the 32-bit ordered
+ * keys between -inf (e = 0) and the max (e = 1): the smallest key hi with e(val(hi)) >= min_p
+ * that the bisection reaches.  Every element whose key is >= the floor passes.  min_p > 1
+ * passes nothing (the caller keeps at least one element). */
+uint32_t or_minp_floor(float m, float c, float min_p) {
+    uint32_t lo = or_key_f32(-INFINITY), hi = or_key_f32(m);
+    if (!(min_p <= 1.0f)) return hi + 1u;
+    while (hi - lo > 1u) {
+        uint32_t mid = lo + (hi - lo) / 2u;
+        uint32_t u = (mid & 0x80000000u) ? (mid & 0x7FFFFFFFu) : ~mid;
+        float e = or_exp2((from_bits(u) - m) * c);
+        if (e >= min_p) hi = mid; else lo = mid;
+    }
+    return hi;
+}
+
+int64_t or_scale_floor_exact(float u, uint64_t m, int* exact) {
+    int64_t f = or_scale_floor(u, m);
+    *exact = 0;
+    if (f >= 0) {
+        uint32_t b = bits_of(u);
+        uint32_t e = (b >> 23) & 0xFFu;
+        uint64_t mant = (b & 0x7FFFFFu) | (e ? 0x800000u : 0u);
+        int shift = e ? (150 - (int)e) : 149;
+        unsigned __int128 prod = (unsigned __int128)mant * m;
+        *exact = shift >= 128 ? prod == 0 : ((prod & ((((unsigned __int128)1) << shift) - 1)) == 0);
+    }
+    return f;
+}
+
+/* The kept set of one row (runtime/worker.py:440-508 build_dspine_target_probs +
+ * filter_target_probs; tests/ref_utils.py:79-108 ref_target_row), as a prefix of the rank order
+ * (key desc, index asc) of length n:
+ *   OR_JOINT  (flashinfer, min-p off for the batch): n = min(top_k, n_p), n_p = ranks whose
+ *             mass ranked ahead is <= floor(top_p * S), S the whole row's mass;
+ *   OR_SEQ    (flashinfer, min-p on for the batch; worker.py:485-491): top-k, then top-p
+ *             against the top-k's own mass S_k (floor(top_p * S_k)), then the min-p floor;
+ *   OR_TORCH  (pytorch backend, worker.py:52-67 _torch_backend_filtered_probs): the joint
+ *             top-k / top-p set, then the min-p floor.
+ * min_p <= 0 switches the floor off.  At least one element is kept. */
+void or_process_row_ex(const float* l, int32_t V, float T, int32_t top_k, float top_p,
+                       float min_p, int32_t mode, or_row_desc* d) {
     memset(d, 0, sizeof(*d));
     int32_t g = 0;
     float m = l[0];
@@ -130,26 +172,40 @@ void or_process_row(const float* l, int32_t V, float T, int32_t top_k, float top
         ck[i] = ~comp;
     }
     radix_sort_u64(ck, tmp, V);
+#define RANK_IDX(r) ((int32_t)(0xFFFFFFFFu - (uint32_t)(~ck[r] & 0xFFFFFFFFu)))
+#define RANK_KEY(r) ((uint32_t)(~ck[r] >> 32))
     int32_t n = (top_k >= V) ? V : top_k;
     if (top_p < 1.0f) {
-        int64_t thr = or_scale_floor(top_p, S);
+        uint64_t base = S;
+        if (mode == OR_SEQ && n >= 1 && n < V) {
+            base = 0;
+            for (int32_t r = 0; r < n; ++r) base += F[RANK_IDX(r)];
+        }
+        int64_t thr = or_scale_floor(top_p, base);
         uint64_t A = 0;
         int32_t np = 0;
         for (int32_t r = 0; r < V; ++r) {
-            int32_t idx = (int32_t)(0xFFFFFFFFu - (uint32_t)(~ck[r] & 0xFFFFFFFFu));
             if ((int64_t)A <= thr) np = r + 1; else break;
-            A += F[idx];
+            A += F[RANK_IDX(r)];
         }
         if (np < n) n = np;
+    }
+    if (mode != OR_JOINT && min_p > 0.0f) {
+        uint32_t kf = or_minp_floor(m, c, min_p);
+        int32_t nm = 0;
+        while (nm < V && RANK_KEY(nm) >= kf) ++nm;
+        if (nm < n) n = nm;
     }
     if (n < 1) n = 1;
     uint64_t SK = 0;
     int32_t last = 0;
     for (int32_t r = 0; r < n; ++r) {
-        int32_t idx = (int32_t)(0xFFFFFFFFu - (uint32_t)(~ck[r] & 0xFFFFFFFFu));
+        int32_t idx = RANK_IDX(r);
         SK += F[idx];
         last = idx;
     }
+#undef RANK_IDX
+#undef RANK_KEY
     d->kstar = or_key_f32(l[last]);
     d->tie_cut = last;
     d->n_kept = n;
@@ -166,6 +222,11 @@ void or_process_row(const float* l, int32_t V, float T, int32_t top_k, float top
     free(tmp);
 }
 
+void or_process_row(const float* l, int32_t V, float T, int32_t top_k, float top_p,
+                    or_row_desc* d) {
+    or_process_row_ex(l, V, T, top_k, top_p, 0.0f, OR_JOINT, d);
+}
+
 float or_row_prob(const float* l, const or_row_desc* d, int32_t i) {
     if (d->greedy) return i == d->argmax ? 1.0f : 0.0f;
     uint32_t k = or_key_f32(l[i]);
@@ -175,9 +236,9 @@ float or_row_prob(const float* l, const or_row_desc* d, int32_t i) {
     return e * d->inv_s;
 }
 
-void or_target_probs(const float* logits, int64_t rows, int32_t V, int32_t rpr,
-                     const float* temperature, const int32_t* top_k, const float* top_p,
-                     float* out, int32_t nthreads) {
+void or_target_probs_ex(const float* logits, int64_t rows, int32_t V, int32_t rpr,
+                        const float* temperature, const int32_t* top_k, const float* top_p,
+                        const float* min_p, int32_t mode, float* out, int32_t nthreads) {
 #ifdef _OPENMP
     if (nthreads > 0) omp_set_num_threads(nthreads);
 #pragma omp parallel for schedule(dynamic, 1)
@@ -186,8 +247,124 @@ void or_target_probs(const float* logits, int64_t rows, int32_t V, int32_t rpr,
         int64_t b = r / rpr;
         const float* l = logits + r * (int64_t)V;
         or_row_desc d;
-        or_process_row(l, V, temperature[b], top_k[b], top_p[b], &d);
+        or_process_row_ex(l, V, temperature[b], top_k[b], top_p[b], min_p ? min_p[b] : 0.0f,
+                          mode, &d);
         for (int32_t i = 0; i < V; ++i) out[r * (int64_t)V + i] = or_row_prob(l, &d, i);
+    }
+}
+
+void or_target_probs(const float* logits, int64_t rows, int32_t V, int32_t rpr,
+                     const float* temperature, const int32_t* top_k, const float* top_p,
+                     float* out, int32_t nthreads) {
+    or_target_probs_ex(logits, rows, V, rpr, temperature, top_k, top_p, NULL, OR_JOINT, out,
+                       nthreads);
+}
+
+/* ---- small-support joint target (build_sparse_target) ---------------------------------- */
+
+/* build_sparse_target (sampling/sparse/target.py:95-178; its CPU branch :156-178 is the
+ * definition, _pack_joint :23-53 and _overflow_dense :56-76 the CUDA branch), one row at a
+ * time over rows of logits:
+ *   threshold = the k-th largest p (k = top_k, ties kept: every p >= threshold passes);
+ *   nucleus   = the mass of strictly larger p is < top_p (or top_p >= 1);
+ *   kept      = p > 0 and both tests.  count > capacity: overflow, and the dense row holds
+ *               p >= threshold renormalised (no nucleus test is needed there: a (capacity+1)-th
+ *               kept element ties the k-th, so every p >= threshold is in the nucleus);
+ *               otherwise the kept ids ascending with p / (kept mass).
+ * Canonical arithmetic: p ~ e_i = exp2((l_i - m) c); "strictly larger p" = larger key; masses
+ * are exact fixed-point sums; "mass < top_p" is H < top_p * S exactly.  A row with temperature
+ * <= 0 is one-hot at its first argmax (the reference gates greedy batches away).
+ * Outputs per row r: ids [r, capacity] i32 (-1 padded), values f32 (0 padded), lengths
+ * (min(count, capacity)), overflow (0/1); dense[r, :] is written for overflow rows only. */
+void or_sparse_target(const float* logits, int64_t rows, int32_t V, const float* temperature,
+                      const int32_t* top_k, const float* top_p, int32_t capacity, int32_t* ids,
+                      float* values, int32_t* lengths, int32_t* overflow, float* dense,
+                      int32_t nthreads) {
+#ifdef _OPENMP
+    if (nthreads > 0) omp_set_num_threads(nthreads);
+#pragma omp parallel for schedule(dynamic, 1)
+#endif
+    for (int64_t r = 0; r < rows; ++r) {
+        const float* l = logits + r * (int64_t)V;
+        int32_t* rid = ids + r * (int64_t)capacity;
+        float* rval = values + r * (int64_t)capacity;
+        for (int32_t j = 0; j < capacity; ++j) { rid[j] = -1; rval[j] = 0.0f; }
+        int32_t g = 0;
+        float m = l[0];
+        for (int32_t i = 1; i < V; ++i)
+            if (l[i] > m) { m = l[i]; g = i; }
+        float c = from_bits(LOG2E_BITS) / temperature[r];
+        if (!(temperature[r] > 0.0f) || !(c < INFINITY)) {
+            rid[0] = g;
+            rval[0] = 1.0f;
+            lengths[r] = 1;
+            overflow[r] = 0;
+            continue;
+        }
+        uint64_t* F = (uint64_t*)malloc((size_t)V * sizeof(uint64_t));
+        float* e = (float*)malloc((size_t)V * sizeof(float));
+        uint64_t* ck = (uint64_t*)malloc((size_t)V * sizeof(uint64_t));
+        uint64_t* tmp = (uint64_t*)malloc((size_t)V * sizeof(uint64_t));
+        uint64_t S = 0;
+        for (int32_t i = 0; i < V; ++i) {
+            e[i] = or_exp2((l[i] - m) * c);
+            F[i] = or_fix(e[i]);
+            S += F[i];
+            uint64_t comp = ((uint64_t)or_key_f32(l[i]) << 32) | (uint64_t)(0xFFFFFFFFu - (uint32_t)i);
+            ck[i] = ~comp;
+        }
+        radix_sort_u64(ck, tmp, V);
+        int32_t k = top_k[r] < 1 ? 1 : (top_k[r] > V ? V : top_k[r]);
+        uint32_t thr_key = (uint32_t)(~ck[k - 1] >> 32);
+        int exact = 0;
+        int64_t pf = or_scale_floor_exact(top_p[r], S, &exact);
+        /* H < top_p * S  <=>  H <= floor - (exact ? 1 : 0);  pf == -2: top_p >= 1 (or NaN) */
+        int use_p = !(top_p[r] >= 1.0f);
+        int64_t hmax = pf >= 0 ? pf - (exact ? 1 : 0) : -1;
+        uint64_t H = 0, Sk = 0, Sthr = 0;
+        int32_t count = 0;
+        uint32_t prev_key = 0xFFFFFFFFu;
+        uint64_t run = 0; /* mass of keys strictly above the current key */
+        for (int32_t rk = 0; rk < V; ++rk) {
+            uint32_t key = (uint32_t)(~ck[rk] >> 32);
+            int32_t idx = (int32_t)(0xFFFFFFFFu - (uint32_t)(~ck[rk] & 0xFFFFFFFFu));
+            if (key < thr_key) break;
+            if (key != prev_key) { H = run; prev_key = key; }
+            run += F[idx];
+            Sthr += F[idx];
+            int nucleus = !use_p || (pf != -2 && (int64_t)H <= hmax);
+            if (e[idx] > 0.0f && nucleus) { ++count; Sk += F[idx]; }
+        }
+        overflow[r] = count > capacity;
+        lengths[r] = count < capacity ? count : capacity;
+        if (count > capacity) {
+            float inv = Sthr ? 1.0f / ((float)(int64_t)Sthr * 9.094947017729282e-13f) : 0.0f;
+            float* d = dense + r * (int64_t)V;
+            for (int32_t i = 0; i < V; ++i)
+                d[i] = or_key_f32(l[i]) >= thr_key ? e[i] * inv : 0.0f;
+        } else if (count > 0) {
+            float inv = Sk ? 1.0f / ((float)(int64_t)Sk * 9.094947017729282e-13f) : 0.0f;
+            /* kept ids ascending: every kept element has key >= thr_key, and its key's mass
+             * ranked above passes the nucleus test */
+            int32_t n = 0;
+            for (int32_t i = 0; i < V && n < count; ++i) {
+                uint32_t key = or_key_f32(l[i]);
+                if (key < thr_key || !(e[i] > 0.0f)) continue;
+                uint64_t Hk = 0;
+                if (use_p) {
+                    for (int32_t j = 0; j < V; ++j)
+                        if (or_key_f32(l[j]) > key) Hk += F[j];
+                    if (!(pf != -2 && (int64_t)Hk <= hmax)) continue;
+                }
+                rid[n] = i;
+                rval[n] = e[i] * inv;
+                ++n;
+            }
+        }
+        free(F);
+        free(e);
+        free(ck);
+        free(tmp);
     }
 }
 
@@ -299,12 +476,13 @@ static float logit_w(const void* vctx, int32_t i) {
     return fmaxf(p - qq, 0.0f);
 }
 
-void or_verify_logits(int32_t B, int32_t V, const int64_t* cand, const float* target,
-                      const int64_t* tgt_row, const float* draft, const int64_t* drf_row,
-                      int64_t stride, const float* temperature, const int32_t* top_k,
-                      const float* top_p, const int32_t* caps, const float* U, const float* UF,
-                      const int32_t* prefix, int32_t* accept, int32_t* commit, int64_t* bonus,
-                      int64_t* output, int32_t* new_seq, int32_t nthreads) {
+void or_verify_logits_ex(int32_t B, int32_t V, const int64_t* cand, const float* target,
+                         const int64_t* tgt_row, const float* draft, const int64_t* drf_row,
+                         int64_t stride, const float* temperature, const int32_t* top_k,
+                         const float* top_p, const float* min_p, int32_t mode,
+                         const int32_t* caps, const float* U, const float* UF,
+                         const int32_t* prefix, int32_t* accept, int32_t* commit,
+                         int64_t* bonus, int64_t* output, int32_t* new_seq, int32_t nthreads) {
     /* phase 1: every row descriptor a request may consult */
     or_row_desc* dt = (or_row_desc*)calloc((size_t)B * 16, sizeof(or_row_desc));
     or_row_desc* dq = (or_row_desc*)calloc((size_t)B * 16, sizeof(or_row_desc));
@@ -320,12 +498,12 @@ void or_verify_logits(int32_t B, int32_t V, const int64_t* cand, const float* ta
         int greedy = row_is_greedy(temperature[b], top_k[b], &c);
         if (kind == 0) {
             if (s >= cap) continue;
-            or_process_row(target + (tgt_row[b] + s) * stride, V, temperature[b], top_k[b],
-                           top_p[b], &dt[b * 16 + s]);
+            or_process_row_ex(target + (tgt_row[b] + s) * stride, V, temperature[b], top_k[b],
+                              top_p[b], min_p ? min_p[b] : 0.0f, mode, &dt[b * 16 + s]);
         } else {
             if (s >= cap - 1 || greedy || draft == NULL) continue;
-            or_process_row(draft + (drf_row[b] + s) * stride, V, temperature[b], top_k[b],
-                           top_p[b], &dq[b * 16 + s]);
+            or_process_row_ex(draft + (drf_row[b] + s) * stride, V, temperature[b], top_k[b],
+                              top_p[b], min_p ? min_p[b] : 0.0f, mode, &dq[b * 16 + s]);
         }
     }
     /* phase 2: chain + bonus per request */
@@ -374,6 +552,17 @@ void or_verify_logits(int32_t B, int32_t V, const int64_t* cand, const float* ta
     }
     free(dt);
     free(dq);
+}
+
+void or_verify_logits(int32_t B, int32_t V, const int64_t* cand, const float* target,
+                      const int64_t* tgt_row, const float* draft, const int64_t* drf_row,
+                      int64_t stride, const float* temperature, const int32_t* top_k,
+                      const float* top_p, const int32_t* caps, const float* U, const float* UF,
+                      const int32_t* prefix, int32_t* accept, int32_t* commit, int64_t* bonus,
+                      int64_t* output, int32_t* new_seq, int32_t nthreads) {
+    or_verify_logits_ex(B, V, cand, target, tgt_row, draft, drf_row, stride, temperature, top_k,
+                        top_p, NULL, OR_JOINT, caps, U, UF, prefix, accept, commit, bonus, output,
+                        new_seq, nthreads);
 }
 
 /* ---- sparse q (accept_sparse) ---------------------------------------------------------- */

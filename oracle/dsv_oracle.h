@@ -55,6 +55,20 @@ typedef struct {
 
 void or_process_row(const float* logits, int32_t V, float temperature, int32_t top_k,
                     float top_p, or_row_desc* out);
+
+/* Filter modes of runtime/worker.py:473-508 filter_target_probs (see or_process_row_ex). */
+#define OR_JOINT 0  /* flashinfer backend, no min-p in the batch: joint top-k / top-p      */
+#define OR_SEQ 1    /* flashinfer backend, min-p in the batch: top-k -> top-p -> min-p     */
+#define OR_TORCH 2  /* pytorch backend: joint top-k / top-p, then min-p                    */
+
+/* or_process_row with min-p and a filter mode (min_p <= 0: no min-p floor) */
+void or_process_row_ex(const float* logits, int32_t V, float temperature, int32_t top_k,
+                       float top_p, float min_p, int32_t mode, or_row_desc* out);
+/* the min-p key floor of a row with max m and c = log2(e) / T: elements whose 32-bit ordered
+ * key is >= the floor pass "p >= min_p * max p" */
+uint32_t or_minp_floor(float m, float c, float min_p);
+/* floor(u * m) as or_scale_floor, and *exact = 1 when u * m is an integer */
+int64_t or_scale_floor_exact(float u, uint64_t m, int* exact);
 /* p_i of a processed row (0 outside the kept set) */
 float or_row_prob(const float* logits, const or_row_desc* d, int32_t i);
 
@@ -63,6 +77,21 @@ float or_row_prob(const float* logits, const or_row_desc* d, int32_t i);
 void or_target_probs(const float* logits, int64_t rows, int32_t V, int32_t rows_per_request,
                      const float* temperature, const int32_t* top_k, const float* top_p,
                      float* out, int32_t nthreads);
+
+/* or_target_probs with per-request min_p (NULL: none) and a filter mode */
+void or_target_probs_ex(const float* logits, int64_t rows, int32_t V, int32_t rows_per_request,
+                        const float* temperature, const int32_t* top_k, const float* top_p,
+                        const float* min_p, int32_t mode, float* out, int32_t nthreads);
+
+/* build_sparse_target (sampling/sparse/target.py:95-178): per row the kept set of the
+ * small-support joint target (threshold = k-th largest p, ties kept; nucleus = the mass of
+ * strictly larger p below top_p), packed ids ascending / values (capacity wide), lengths,
+ * overflow, and for overflow rows the dense row p >= threshold renormalised.  temperature,
+ * top_k, top_p per row. */
+void or_sparse_target(const float* logits, int64_t rows, int32_t V, const float* temperature,
+                      const int32_t* top_k, const float* top_p, int32_t capacity, int32_t* ids,
+                      float* values, int32_t* lengths, int32_t* overflow, float* dense,
+                      int32_t nthreads);
 
 /* sample_capped_chain_from_probs (sampling/rejection.py:12-153) with the exact residual
  * CDF.  candidates [B,16] i64, target [B,16,V] f32, draft [B,15,V] f32, caps [B] i32,
@@ -85,6 +114,15 @@ void or_verify_logits(int32_t B, int32_t V, const int64_t* candidates, const flo
                       const float* uniform_final, const int32_t* prefix, int32_t* accept,
                       int32_t* commit, int64_t* bonus, int64_t* output, int32_t* new_seq,
                       int32_t nthreads);
+
+/* or_verify_logits with per-request min_p (NULL: none) and a filter mode */
+void or_verify_logits_ex(int32_t B, int32_t V, const int64_t* candidates, const float* target,
+                         const int64_t* tgt_row, const float* draft, const int64_t* drf_row,
+                         int64_t stride, const float* temperature, const int32_t* top_k,
+                         const float* top_p, const float* min_p, int32_t mode,
+                         const int32_t* caps, const float* uniforms, const float* uniform_final,
+                         const int32_t* prefix, int32_t* accept, int32_t* commit,
+                         int64_t* bonus, int64_t* output, int32_t* new_seq, int32_t nthreads);
 
 /* accept_sparse (sampling/sparse/accept.py:207-543): sparse q (K=16), dense p (optionally
  * RAW with a denominator) or packed p with dense overflow rows, optional row offsets.

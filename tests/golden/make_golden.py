@@ -24,6 +24,8 @@ Fixture groups (reference function -> file):
             ref_sample_chain / ref_refine_table                             serial.npz
   fp8       layers/fp8/coarse.py FullVFP8Coarse (weight quantization), _scale/_quantize,
             stable_local_topk; layers/fp8/gather.py rescore / select16      fp8.npz
+  target_minp  tests/ref_utils.py:79-108 ref_target_row with min-p, both backends  target_minp.npz
+  sparse_target  sampling/sparse/target.py:95-178 build_sparse_target (CPU branch)  sparse_target.npz
   fullv     configs 0, 1 and 4 at V = 151936: ref_target_row rows +
             sampling/rejection.py:101-153 sample_capped_chain_from_probs     fullv.npz
 """
@@ -535,6 +537,82 @@ def gen_fp8(torch):
     return out
 
 
+def gen_target_minp(torch):
+    """ref_target_row (tests/ref_utils.py:79-108, float64) with min-p on, for the flashinfer
+    backend (sequential top-k -> top-p -> min-p) and the pytorch backend (joint top-k / top-p
+    and min-p), and with min-p off for the pytorch backend."""
+    from ref_utils import ref_target_row
+
+    out = {}
+    ci = 0
+    g = torch.Generator().manual_seed(11)
+    params = [(0.7, 20, 0.9, 0.05), (1.0, 1 << 30, 0.95, 0.01), (1.3, 50, 1.0, 0.1),
+              (0.5, 30, 0.8, 0.0), (1.0, 8, 0.6, 0.02), (2.0, 1 << 30, 1.0, 0.3),
+              (0.9, 100, 0.7, 0.001), (1.1, 5, 0.99, 0.5)]
+    for (T, k, tp, mp) in params:
+        for backend in ("flashinfer", "pytorch"):
+            for rep in range(2):
+                V = [317, 2048][rep]
+                l = torch.randn(V, generator=g) * 3
+                if rep == 1:
+                    l = l.bfloat16().float()  # quantised: ties everywhere
+                ref = ref_target_row(l, T, k, tp, mp, backend)
+                out[f"c{ci}_logits"] = _np(l.float())
+                out[f"c{ci}_params"] = np.array([T, k, tp, mp], dtype=np.float64)
+                out[f"c{ci}_backend"] = np.array(backend)
+                out[f"c{ci}_p"] = _np(ref)
+                ci += 1
+    out["n"] = np.array(ci)
+    return out
+
+
+def gen_sparse_target(torch):
+    """build_sparse_target's CPU branch (sampling/sparse/target.py:156-178) on CPU logits:
+    random rows, bf16-quantised rows (ties at the k-th p), all-equal rows (overflow), a
+    cutting top-p and every top-k in [1, 32]; compact rows mapped by row_to_request."""
+    import types as _t
+
+    from sglang_dspine.sampling.sparse.target import build_sparse_target
+
+    out = {}
+    ci = 0
+    g = torch.Generator().manual_seed(23)
+    for V, rows in ((257, 24), (4099, 16), (1000, 40)):
+        for kind in ("random", "quantised", "ties"):
+            bs = 8
+            temps = 0.3 + 1.2 * torch.rand(bs, generator=g)
+            ks = torch.randint(1, 33, (bs,), generator=g, dtype=torch.int32)
+            tps = torch.where(torch.rand(bs, generator=g) < 0.5, torch.ones(bs),
+                              0.5 + 0.5 * torch.rand(bs, generator=g))
+            l = torch.randn(rows, V, generator=g) * 2.5
+            if kind == "quantised":
+                l = (l * 2).round() / 2  # many equal values, ties at the k-th p
+            elif kind == "ties":
+                l = (l > 1.5).float() * 3.0  # a plateau of equal tops: overflow rows
+                l[::5] = 0.0                   # all-equal rows
+            r2r = torch.randint(0, bs, (rows,), generator=g)
+            info = _t.SimpleNamespace(temperatures=temps[:, None], top_ks=ks, top_ps=tps,
+                                      min_ps=torch.zeros(bs), max_top_k=int(ks.max()),
+                                      need_min_p_sampling=False, is_any_greedy=False)
+            res = build_sparse_target(l, info, row_to_request=r2r, capacity=32,
+                                      sampling_backend="flashinfer")
+            ids, vals, lens, ovf = res.packed
+            out[f"c{ci}_logits"] = _np(l.float())
+            out[f"c{ci}_temp"] = _np(temps[r2r].float())
+            out[f"c{ci}_topk"] = _np(ks[r2r])
+            out[f"c{ci}_topp"] = _np(tps[r2r].float())
+            out[f"c{ci}_ids"] = _np(ids)
+            out[f"c{ci}_vals"] = _np(vals)
+            out[f"c{ci}_lens"] = _np(lens)
+            out[f"c{ci}_ovf"] = _np(ovf)
+            ovf_rows = np.flatnonzero(_np(ovf))
+            out[f"c{ci}_ovf_rows"] = ovf_rows
+            out[f"c{ci}_dense"] = _np(res.dense_p[torch.as_tensor(ovf_rows, dtype=torch.long)])
+            ci += 1
+    out["n"] = np.array(ci)
+    return out
+
+
 def _fullv_case(torch, batch, ref_target_row, chain):
     """Reference outputs of one benchmark batch at the full vocabulary: target rows through
     ref_target_row (float64, then float32) or a one-hot at the lowest-index argmax for greedy
@@ -629,6 +707,8 @@ def main(ref_dir):
         "serial": lambda: gen_serial(torch, ref_dir),
         "fp8": lambda: gen_fp8(torch),
         "fullv": lambda: gen_fullv(torch),
+        "target_minp": lambda: gen_target_minp(torch),
+        "sparse_target": lambda: gen_sparse_target(torch),
     }
     only = set(sys.argv[2:])
     for name, fn in groups.items():

@@ -233,3 +233,45 @@ def test_serial_table_oracle_pins_reference_kernel():
         out, cout = OS.chain(ref["idx"], case["cand"], case["T"], ref["conf"])
         np.testing.assert_array_equal(out, ref["chain"])
         np.testing.assert_array_equal(cout, ref["chain_conf"])
+
+
+def test_target_probs_min_p_and_pytorch_backend_match_reference_rows():
+    """ref_target_row with min-p on (flashinfer: sequential top-k -> top-p -> min-p; pytorch:
+    joint top-k / top-p and min-p) and the pytorch backend with min-p off: exact support,
+    values within rtol 1e-5 (target_minp.npz)."""
+    d = load("target_minp")
+    for ci in cases(d):
+        T, k, tp, mp = d[f"c{ci}_params"]
+        backend = str(d[f"c{ci}_backend"])
+        mode = O.filter_mode(backend, mp > 0)
+        got = O.target_probs(d[f"c{ci}_logits"][None], [T], [int(k)], [tp], min_p=[mp],
+                             mode=mode)[0]
+        ref = d[f"c{ci}_p"]
+        np.testing.assert_array_equal(got > 0, ref > 0,
+                                      err_msg=f"support differs case {ci} ({backend}, {mp})")
+        np.testing.assert_allclose(got, ref, rtol=1e-5, atol=1e-7, err_msg=f"case {ci}")
+
+
+def test_sparse_target_matches_reference_cpu_branch():
+    """build_sparse_target's CPU branch (sampling/sparse/target.py:156-178): lengths, overflow
+    flags and the packed ids of packed rows exact, their values and the dense overflow rows
+    within rtol 1e-5, on
+    random, bf16-like quantised (ties at the k-th p) and plateau / all-equal rows."""
+    d = load("sparse_target")
+    n_ovf = 0
+    for ci in cases(d):
+        ids, vals, lens, ovf, dense = O.sparse_target(
+            d[f"c{ci}_logits"], d[f"c{ci}_temp"], d[f"c{ci}_topk"], d[f"c{ci}_topp"], 32)
+        np.testing.assert_array_equal(ovf, d[f"c{ci}_ovf"], err_msg=f"overflow case {ci}")
+        np.testing.assert_array_equal(lens, d[f"c{ci}_lens"], err_msg=f"lengths case {ci}")
+        # packed entries of overflow rows are unused (accept_sparse reads the dense row), and
+        # the reference fills them from whichever tied ids torch.topk returned
+        keep = d[f"c{ci}_ovf"] == 0
+        np.testing.assert_array_equal(ids[keep], d[f"c{ci}_ids"][keep], err_msg=f"ids case {ci}")
+        np.testing.assert_allclose(vals[keep], d[f"c{ci}_vals"][keep], rtol=1e-5, atol=1e-7,
+                                   err_msg=f"values case {ci}")
+        rows = d[f"c{ci}_ovf_rows"]
+        n_ovf += len(rows)
+        np.testing.assert_allclose(dense[rows], d[f"c{ci}_dense"], rtol=1e-5, atol=1e-7,
+                                   err_msg=f"dense overflow rows case {ci}")
+    assert n_ovf > 0
