@@ -81,6 +81,8 @@ def parse_args():
     p.add_argument("--config", choices=tuple(WORKLOADS), default="config1")
     p.add_argument("--no-cpu-baseline", action="store_true",
                    help="skip the CPU baseline leg (it is reported by default at N=1)")
+    p.add_argument("--no-tp-head", action="store_true",
+                   help="at N > 1, skip the config-3 TP head timed beside the replicas")
     return p.parse_args()
 
 
@@ -119,9 +121,12 @@ def profiled_traffic(config: str):
 
 
 def make_batch(config: str, rank: int, device):
+    """The config's batch.  Every replica verifies the same seeded batch, so that the time of
+    N replicas measures the machine (HBM, clocks, launch) rather than the cost spread between
+    differently seeded batches."""
     from dspine_b200 import workloads
     fn = getattr(workloads, config)
-    seed = {"config0": 0, "config1": 1, "config4": 4}[config] + 1000 * rank
+    seed = {"config0": 0, "config1": 1, "config4": 4}[config]
     return fn(seed=seed, device=device)
 
 
@@ -364,6 +369,10 @@ def run_dspine(args):
     if ws.error_word() != 0:
         raise SystemExit("device error word set during the timed region")
 
+    tp_head = None
+    if dist is not None and args.config == "config1" and not args.no_tp_head:
+        tp_head = tp_head_report(dev, dist, rank, world, args.steps, args.warmup)
+
     line = None
     if rank == 0:
         alg_bytes = batch.algorithmic_bytes()
@@ -393,6 +402,8 @@ def run_dspine(args):
                          "algorithmic_bytes_per_launch": alg_bytes,
                          "kernel_ms": kernel_ms},
         }
+        if tp_head is not None:
+            line["tp_head"] = tp_head
     if dist is not None:
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()
@@ -455,6 +466,103 @@ def head_cpu_time(config, n_rows, cores):
         torch.logsumexp(logits.float(), dim=1)
         return time.perf_counter() - t0
     return once
+
+
+def tp_head_report(dev, dist, rank, world, steps, warmup):
+    """Config 3's vocab-parallel head at TP = world, timed in the same run as the verification
+    replicas: per step the shard's fused head (top-20 + logsumexp), ONE all-gather of the packed
+    candidate block, the replicated merge and the greedy accept, captured in a CUDA graph and
+    replayed back to back (max over ranks).  Beside it: the unsharded head on one GPU (TP = 1),
+    the all-gather of the same block alone, and whether every rank's merged ids and accept
+    outputs equal each other's and the TP = 1 result."""
+    import torch
+    from dspine_b200 import accept, lmhead
+    rows, H, k, B = HEAD_SHAPES["config3"]
+    hidden, shard, start, end = head_inputs("config3", rank, world, dev)
+    _, full, _, _ = head_inputs("config3", 0, 1, dev)
+    group = lmhead.TorchGroup()
+    head = lmhead.TPHead(shard, start, end, VOCAB, group)
+    g = torch.Generator(device="cpu").manual_seed(9)
+    cand = torch.randint(0, VOCAB, (B, 16), generator=g).to(dev)
+    caps = torch.randint(1, 17, (B,), generator=g, dtype=torch.int32).to(dev)
+    outs = accept.new_outputs(B, dev)
+    outs1 = accept.new_outputs(B, dev)
+    full_out = (torch.empty(rows, k, dtype=torch.int64, device=dev),
+                torch.empty(rows, k, dtype=torch.float32, device=dev),
+                torch.empty(rows, dtype=torch.float32, device=dev))
+    res = {}
+
+    def step_tp():
+        ids, _, _ = head.topk_lse(hidden, k)
+        accept.accept_greedy(cand, ids[:, 0].view(B, 16), caps, outputs=outs)
+        res["ids"] = ids
+
+    def step_one():
+        lmhead.lmhead_topk(hidden, full, k, out=full_out)
+        accept.accept_greedy(cand, full_out[0][:, 0].view(B, 16), caps, outputs=outs1)
+
+    words = rows * k * 3 + rows
+    words += words & 1
+    block = torch.zeros(words, dtype=torch.int32, device=dev)
+    gathered = torch.empty(world * words, dtype=torch.int32, device=dev)
+
+    def step_ag():
+        dist.all_gather_into_tensor(gathered, block)
+
+    def barrier():
+        dist.barrier(device_ids=[dev.index])
+        torch.cuda.synchronize(dev)
+
+    def timed(fn, graph_it):
+        for _ in range(max(warmup, 3)):
+            fn()
+        barrier()
+        run = fn
+        graph = None
+        if graph_it:
+            side = torch.cuda.Stream(device=dev)
+            side.wait_stream(torch.cuda.current_stream(dev))
+            with torch.cuda.stream(side):
+                fn()
+            torch.cuda.current_stream(dev).wait_stream(side)
+            barrier()
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph):
+                fn()
+            barrier()
+            run = graph.replay
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        for _ in range(steps):
+            run()
+        e1.record()
+        barrier()
+        t = torch.tensor([e0.elapsed_time(e1) / steps], dtype=torch.float64, device=dev)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        del graph
+        return float(t[0])
+
+    tp_ms = timed(step_tp, True)
+    ag_ms = timed(step_ag, True)
+    one_ms = timed(step_one, False)
+    step_tp()
+    step_one()
+    torch.cuda.synchronize(dev)
+    same_as_tp1 = torch.equal(res["ids"], full_out[0]) and all(
+        torch.equal(a, b) for a, b in zip(outs, outs1))
+    digest = torch.cat([res["ids"].view(-1), *(o.view(-1).to(torch.int64) for o in outs)])
+    everyone = torch.empty((world, digest.numel()), dtype=torch.int64, device=dev)
+    dist.all_gather_into_tensor(everyone.view(-1), digest)
+    across = bool((everyone == everyone[0:1]).all())
+    flags = torch.tensor([0.0 if same_as_tp1 else 1.0], dtype=torch.float64, device=dev)
+    dist.all_reduce(flags, op=dist.ReduceOp.MAX)
+    return {"tp": world, "workload": "config3: 512 draft rows x H 5120 x V 151936, top-20 + "
+                                     "logsumexp + greedy accept of 32 requests",
+            "ms_per_step": tp_ms, "tp1_ms_per_step": one_ms, "speedup_vs_tp1": one_ms / tp_ms,
+            "allgather_us": ag_ms * 1e3, "allgather_share": ag_ms / tp_ms,
+            "allgather_bytes_per_rank": words * 4,
+            "identical_across_ranks": across, "identical_to_tp1": bool(flags[0] == 0.0),
+            "rows_per_s": rows / (tp_ms * 1e-3)}
 
 
 def run_head(args):

@@ -63,6 +63,14 @@ _SIGNATURES = {
                           c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
                           c_void_p, c_void_p, ctypes.POINTER(CompactOut), c_void_p, c_size_t,
                           c_void_p],
+    "dsv_verify_logits_ex": [c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_int64,
+                             c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
+                             c_void_p, c_int32, c_void_p, c_void_p, c_void_p, c_void_p,
+                             c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,
+                             ctypes.POINTER(CompactOut), c_void_p, c_size_t, c_void_p],
+    "dsv_target_probs_ex": [c_int64, c_int32, c_int32, c_int32, c_void_p, c_int64, c_void_p,
+                            c_void_p, c_void_p, c_void_p, c_int32, c_void_p, c_void_p, c_size_t,
+                            c_void_p],
     "dsv_lmhead_workspace_size": [c_int32, c_int32, c_int32, ctypes.POINTER(c_size_t)],
     "dsv_lmhead_topk": [c_int32, c_int32, c_int32, c_int32, c_void_p, c_int64, c_void_p, c_int64,
                         c_int64, c_int64, c_int32, c_void_p, c_void_p, c_void_p, c_void_p,
@@ -75,6 +83,9 @@ _SIGNATURES = {
     "dsv_target_probs": [c_int64, c_int32, c_int32, c_void_p, c_int64, c_void_p, c_void_p,
                          c_void_p, c_void_p, c_void_p, c_size_t, c_void_p],
     "dsv_accept_sparse": [c_int32, c_int32, c_int32] + [c_void_p] * 19 + [c_void_p],
+    "dsv_sparse_target": [c_int64, c_int32, c_int32, c_void_p, c_int64, c_void_p, c_int32,
+                          c_void_p, c_void_p, c_void_p, c_int32, c_void_p, c_void_p, c_void_p,
+                          c_void_p, c_void_p, c_void_p],
     "dsv_compress_probs": [c_int64, c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_void_p,
                            c_void_p, c_void_p],
     "dsv_adjust_logits": [c_void_p, c_int32, c_int64, c_int32, c_int64, c_void_p, c_int32,

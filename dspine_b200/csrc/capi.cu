@@ -94,16 +94,18 @@ int dsv_workspace_error(void* ws, uint32_t* err, dsv_stream_t stream) {
     return DSV_OK;
 }
 
-int dsv_verify_logits(int32_t batch, int32_t vocab, int32_t dtype, const int64_t* candidates,
-                      const void* target_logits, const int64_t* target_row, int64_t target_rows,
-                      const void* draft_logits, const int64_t* draft_row, int64_t draft_rows,
-                      int64_t row_stride, const float* temperature, const int32_t* top_k,
-                      const float* top_p, const int32_t* verify_lens, const float* uniforms,
-                      const float* uniform_final, const int32_t* prefix_lens, int32_t* accept,
-                      int32_t* commit, int64_t* bonus, int64_t* output, int32_t* new_seq,
-                      const dsv_compact_out* compact, void* workspace, size_t workspace_bytes,
-                      dsv_stream_t stream) {
+int dsv_verify_logits_ex(int32_t batch, int32_t vocab, int32_t dtype, const int64_t* candidates,
+                         const void* target_logits, const int64_t* target_row,
+                         int64_t target_rows, const void* draft_logits, const int64_t* draft_row,
+                         int64_t draft_rows, int64_t row_stride, const float* temperature,
+                         const int32_t* top_k, const float* top_p, const float* min_p,
+                         int32_t filter_mode, const int32_t* verify_lens, const float* uniforms,
+                         const float* uniform_final, const int32_t* prefix_lens, int32_t* accept,
+                         int32_t* commit, int64_t* bonus, int64_t* output, int32_t* new_seq,
+                         const dsv_compact_out* compact, void* workspace,
+                         size_t workspace_bytes, dsv_stream_t stream) {
     if (batch < 0 || vocab < 1 || row_stride < vocab || target_rows < 0) return DSV_BAD_SHAPE;
+    if (filter_mode < DSV_FILTER_JOINT || filter_mode > DSV_FILTER_TORCH) return DSV_UNSUPPORTED;
     if (dtype != DSV_BF16 && dtype != DSV_F32) return DSV_BAD_DTYPE;
     if (batch == 0) return DSV_OK;
     if (target_rows < 1 || (draft_logits && draft_rows < 1)) return DSV_BAD_SHAPE;
@@ -138,6 +140,8 @@ int dsv_verify_logits(int32_t batch, int32_t vocab, int32_t dtype, const int64_t
     a.temperature = temperature;
     a.top_k = top_k;
     a.top_p = top_p;
+    a.min_p = min_p;
+    a.mode = filter_mode;
     a.caps = verify_lens;
     a.u = uniforms;
     a.uf = uniform_final;
@@ -175,6 +179,22 @@ int dsv_verify_logits(int32_t batch, int32_t vocab, int32_t dtype, const int64_t
     if (dsv::stream_supported(a, dtype))
         return counted(dsv::launch_stream(a, (cudaStream_t)stream), 1);
     return counted(dsv::launch_verify(a, dtype, (cudaStream_t)stream), 1);
+}
+
+int dsv_verify_logits(int32_t batch, int32_t vocab, int32_t dtype, const int64_t* candidates,
+                      const void* target_logits, const int64_t* target_row, int64_t target_rows,
+                      const void* draft_logits, const int64_t* draft_row, int64_t draft_rows,
+                      int64_t row_stride, const float* temperature, const int32_t* top_k,
+                      const float* top_p, const int32_t* verify_lens, const float* uniforms,
+                      const float* uniform_final, const int32_t* prefix_lens, int32_t* accept,
+                      int32_t* commit, int64_t* bonus, int64_t* output, int32_t* new_seq,
+                      const dsv_compact_out* compact, void* workspace, size_t workspace_bytes,
+                      dsv_stream_t stream) {
+    return dsv_verify_logits_ex(batch, vocab, dtype, candidates, target_logits, target_row,
+                                target_rows, draft_logits, draft_row, draft_rows, row_stride,
+                                temperature, top_k, top_p, nullptr, DSV_FILTER_JOINT, verify_lens,
+                                uniforms, uniform_final, prefix_lens, accept, commit, bonus,
+                                output, new_seq, compact, workspace, workspace_bytes, stream);
 }
 
 int dsv_lmhead_workspace_size(int32_t rows, int32_t vocab, int32_t k, size_t* bytes) {
@@ -318,6 +338,25 @@ int dsv_compress_probs(int64_t rows, int32_t vocab, int32_t capacity, const floa
                    1);
 }
 
+int dsv_sparse_target(int64_t rows, int32_t vocab, int32_t dtype, const void* logits,
+                      int64_t row_stride, const int64_t* row_request, int32_t rows_per_request,
+                      const float* temperature, const int32_t* top_k, const float* top_p,
+                      int32_t capacity, int32_t* ids, float* values, int32_t* lengths,
+                      int32_t* overflow, float* dense, dsv_stream_t stream) {
+    if (rows < 0 || vocab < 1 || row_stride < vocab || capacity < 1 || capacity > 64)
+        return DSV_BAD_SHAPE;
+    if (!row_request && rows_per_request < 1) return DSV_BAD_SHAPE;
+    if (dtype != DSV_BF16 && dtype != DSV_F32) return DSV_BAD_DTYPE;
+    if (rows == 0) return DSV_OK;
+    if (!logits || !temperature || !top_k || !top_p || !ids || !values || !lengths || !overflow ||
+        !dense)
+        return DSV_BAD_POINTER;
+    dsv::SparseTargetArgs a = {rows, vocab, capacity, logits, row_stride, row_request,
+                               rows_per_request, temperature, top_k, top_p, ids, values,
+                               lengths, overflow, dense};
+    return counted(dsv::launch_sparse_target(a, dtype, (cudaStream_t)stream), 1);
+}
+
 int dsv_adjust_logits(void* logits, int32_t dtype, int64_t rows, int32_t vocab, int64_t row_stride,
                       const int64_t* row_to_request, int32_t rows_per_request,
                       const float* additive, const float* scaling, const uint32_t* vocab_mask,
@@ -390,21 +429,44 @@ int dsv_accept_compact(int32_t batch, const int32_t* commit, const int32_t* veri
                    1);
 }
 
-int dsv_target_probs(int64_t rows, int32_t vocab, int32_t rows_per_request, const void* logits,
-                     int64_t row_stride, const float* temperature, const int32_t* top_k,
-                     const float* top_p, float* probs, void* workspace, size_t workspace_bytes,
-                     dsv_stream_t stream) {
-    if (rows < 0 || vocab < 1 || vocab > 262000 || rows_per_request < 1 || rows_per_request > 16 ||
-        row_stride < vocab || rows % rows_per_request != 0)
+int dsv_target_probs_ex(int64_t rows, int32_t vocab, int32_t dtype, int32_t rows_per_request,
+                        const void* logits, int64_t row_stride, const float* temperature,
+                        const int32_t* top_k, const float* top_p, const float* min_p,
+                        int32_t filter_mode, float* probs, void* workspace,
+                        size_t workspace_bytes, dsv_stream_t stream) {
+    if (rows < 0 || vocab < 1 || rows_per_request < 1 || row_stride < vocab ||
+        rows % rows_per_request != 0)
         return DSV_BAD_SHAPE;
+    if (dtype != DSV_BF16 && dtype != DSV_F32) return DSV_BAD_DTYPE;
+    if (filter_mode < DSV_FILTER_JOINT || filter_mode > DSV_FILTER_TORCH) return DSV_UNSUPPORTED;
+    const bool rows_path = dtype == DSV_BF16 && vocab <= 262000 && rows_per_request <= 16;
     if (rows == 0) return DSV_OK;
     if (!logits || !temperature || !top_k || !top_p || !probs || !workspace) return DSV_BAD_POINTER;
-    if (!aligned(logits, 2) || !aligned(workspace, 16)) return DSV_BAD_ALIGNMENT;
+    if (!aligned(logits, dtype == DSV_BF16 ? 2 : 4) || !aligned(workspace, 16))
+        return DSV_BAD_ALIGNMENT;
     const long long nreq = rows / rows_per_request;
+    char* base = reinterpret_cast<char*>(workspace);
+    if (!rows_path) {
+        // one cluster per row (verify.cu): only the task counters of the workspace are used
+        if (workspace_bytes < 64) return DSV_WORKSPACE_TOO_SMALL;
+        dsv::VerifyArgs a = {};
+        a.B = (int)(nreq < 0x7fffffff ? nreq : 0x7fffffff);
+        a.V = vocab;
+        a.tgt = logits;
+        a.tgt_rows = rows;
+        a.row_step = rows_per_request;
+        a.stride = row_stride;
+        a.temperature = temperature;
+        a.top_k = top_k;
+        a.top_p = top_p;
+        a.min_p = min_p;
+        a.mode = filter_mode;
+        a.ws = reinterpret_cast<dsv::WsHeader*>(base);
+        return counted(dsv::launch_probs_cluster(a, dtype, probs, (cudaStream_t)stream), 1);
+    }
     const int chunk = 1024;
     const int wsb = (int)(nreq < chunk ? nreq : chunk);
     if (workspace_bytes < dsv::verify_base_bytes(wsb)) return DSV_WORKSPACE_TOO_SMALL;
-    char* base = reinterpret_cast<char*>(workspace);
     int launched = 0;
     for (long long r0 = 0; r0 < nreq; r0 += chunk) {
         const int B = (int)((nreq - r0) < chunk ? (nreq - r0) : chunk);
@@ -419,6 +481,8 @@ int dsv_target_probs(int64_t rows, int32_t vocab, int32_t rows_per_request, cons
         a.temperature = temperature + r0;
         a.top_k = top_k + r0;
         a.top_p = top_p + r0;
+        a.min_p = min_p ? min_p + r0 : nullptr;
+        a.mode = filter_mode;
         a.caps = nullptr;
         a.cap_all = rows_per_request;
         a.ws = reinterpret_cast<dsv::WsHeader*>(base);
@@ -436,6 +500,16 @@ int dsv_target_probs(int64_t rows, int32_t vocab, int32_t rows_per_request, cons
         launched += 2;
     }
     return counted(DSV_OK, launched);
+}
+
+int dsv_target_probs(int64_t rows, int32_t vocab, int32_t rows_per_request, const void* logits,
+                     int64_t row_stride, const float* temperature, const int32_t* top_k,
+                     const float* top_p, float* probs, void* workspace, size_t workspace_bytes,
+                     dsv_stream_t stream) {
+    if (vocab > 262000 || rows_per_request > 16) return DSV_BAD_SHAPE;
+    return dsv_target_probs_ex(rows, vocab, DSV_BF16, rows_per_request, logits, row_stride,
+                               temperature, top_k, top_p, nullptr, DSV_FILTER_JOINT, probs,
+                               workspace, workspace_bytes, stream);
 }
 
 int dsv_topk_ids(int64_t rows, int32_t vocab, int64_t row_stride, int32_t dtype,

@@ -87,6 +87,41 @@ __device__ __forceinline__ bool is_greedy(float T, int top_k, float c) {
     return (top_k <= 1) || !(T > 0.0f) || !(c < __int_as_float(0x7f800000));
 }
 
+// ---- filter modes of the target distribution (runtime/worker.py:473-508) ------------------
+//   kModeJoint  flashinfer backend, no min-p in the batch: joint top-k / top-p on unfiltered p
+//   kModeSeq    flashinfer backend, min-p in the batch: top-k, then top-p against the top-k's
+//               own mass, then the min-p floor
+//   kModeTorch  pytorch backend: joint top-k / top-p, then the min-p floor
+enum FilterMode : int { kModeJoint = 0, kModeSeq = 1, kModeTorch = 2 };
+
+// The min-p floor of a row with maximum m and c = log2(e) / T: "p >= min_p * max p" is
+// e = exp2c((v - m) c) >= min_p (the maximum has e = 1).  exp2c is monotone only up to one-ulp
+// ripples, so the floor is the result of a bisection over the 32-bit ordered keys between -inf
+// (e = 0) and m (e = 1): elements whose 32-bit key is >= the returned key pass.  min_p > 1
+// passes nothing.  Identical to the oracle's or_minp_floor.
+__device__ __forceinline__ uint32_t minp_floor32(float m, float c, float min_p) {
+    uint32_t lo = 0x007FFFFFu;  // key of -inf
+    const uint32_t mb = __float_as_uint(m);
+    uint32_t hi = (mb == 0x80000000u) ? 0x80000000u : ((mb & 0x80000000u) ? ~mb : (mb | 0x80000000u));
+    if (!(min_p <= 1.0f)) return hi + 1u;
+    while (hi - lo > 1u) {
+        const uint32_t mid = lo + (hi - lo) / 2u;
+        const uint32_t u = (mid & 0x80000000u) ? (mid & 0x7FFFFFFFu) : ~mid;
+        const float e = exp2c(__fmul_rn(__fsub_rn(__uint_as_float(u), m), c));
+        if (e >= min_p) hi = mid; else lo = mid;
+    }
+    return hi;
+}
+
+// the smallest bf16 ordered key whose element's 32-bit key is >= k32 (a bf16 value's 32-bit
+// key is key16 << 16, with the low half all ones for negative values)
+__device__ __forceinline__ uint32_t key16_floor(uint32_t k32) {
+    uint32_t k16 = k32 >> 16;
+    const uint32_t full = (k16 << 16) | ((k16 & 0x8000u) ? 0u : 0xFFFFu);
+    if (full < k32) ++k16;
+    return k16;
+}
+
 // 1 / (S * 2^-40) for an exact fixed-point sum S (0 -> 0)
 __device__ __forceinline__ float inv_from_fix(uint64_t S) {
     if (S == 0) return 0.0f;

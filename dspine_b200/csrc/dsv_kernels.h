@@ -22,6 +22,9 @@ struct WsHeader {
                              // bit 3: a selection found no boundary; bit 4: tie cut not found;
                              // bit 5: shared-memory layout check of the row kernel failed;
                              // bit 6: a chain task's request was never published (time limit)
+                             // bit 7: the second half of a split row gave up waiting for the
+                             //        first (time limit); bits 0, 5-7 leave counters / flags
+                             //        possibly set: the workspace must be zeroed again
     unsigned int next2;      // row kernel: greedy-row counter
     unsigned int ready_tail; // row kernel: requests published to the ready list
     unsigned int chain_next; // row kernel: chain tasks taken
@@ -32,6 +35,10 @@ static_assert(sizeof(WsHeader) <= 64, "workspace header");
 // for kept elements (key > kstar, or key == kstar and index <= tie_cut), else 0; greedy rows
 // are one-hot at argmax.
 constexpr uint32_t kDescGreedy = 1u;
+// verification rows whose kept set ends inside the ties of the boundary key: the cut (the
+// index of occurrence `pad` of kstar in index order) is found only where a draw or a drafted
+// token needs it; until then tie_cut holds kTiePending and flags >> 8 the key's count
+constexpr int32_t kTiePending = (int32_t)0x80000000;
 struct RowDesc {
     float m;
     float c;
@@ -105,6 +112,8 @@ struct VerifyArgs {
     const float* temperature;  // [B]
     const int32_t* top_k;      // [B]
     const float* top_p;        // [B]
+    const float* min_p;        // [B] or null (no min-p floor)
+    int mode;                  // FilterMode (dsv_common.cuh)
     const int32_t* caps;       // [B] verify lengths
     const float* u;            // [B,15]
     const float* uf;           // [B]
@@ -143,6 +152,27 @@ struct VerifyArgs {
     long long row_step;
 };
 
+// build_sparse_target (sparse_target.cu): per row the packed kept set of the small-support joint
+// target, or the dense renormalised row when it overflows the capacity
+struct SparseTargetArgs {
+    long long rows;
+    int V;
+    int capacity;                  // packed width (<= 64); top-k values are clamped to it
+    const void* logits;            // rows of `stride` elements
+    long long stride;
+    const int64_t* row_request;    // [rows] request of each row, or null: row / rows_per_request
+    int rows_per_request;
+    const float* temperature;      // per request
+    const int32_t* top_k;
+    const float* top_p;
+    int32_t* ids;                  // [rows, capacity]
+    float* values;                 // [rows, capacity]
+    int32_t* lengths;              // [rows]
+    int32_t* overflow;             // [rows]
+    float* dense;                  // [rows, V]: overflow rows only
+};
+int launch_sparse_target(const SparseTargetArgs& a, int dtype, cudaStream_t stream);
+
 // launchers (return a dsv::Status)
 int launch_verify(const VerifyArgs& a, int dtype, cudaStream_t stream);
 // streaming path (bf16 rows, B <= 1024, V <= 262144): rows kernel + chain kernel
@@ -150,6 +180,9 @@ bool stream_supported(const VerifyArgs& a, int dtype);
 int launch_stream(VerifyArgs a, cudaStream_t stream);
 // descriptors of every target row (rows kernel only) and the dense probabilities they define
 int launch_target_probs(VerifyArgs a, float* out, cudaStream_t stream);
+// the same probabilities from the cluster kernel of verify.cu (fp32 logits, or any vocabulary):
+// rows tgt_rows, request of row t = t / row_step
+int launch_probs_cluster(const VerifyArgs& a, int dtype, float* out, cudaStream_t stream);
 
 // ---- LM head fused with top-k (lmhead.cu) ---------------------------------------------------
 struct LmHeadArgs {

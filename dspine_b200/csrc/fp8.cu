@@ -46,20 +46,33 @@ __global__ void __launch_bounds__(kThreads) quantize_kernel(const T* __restrict_
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
     for (long long r = blockIdx.x; r < rows; r += gridDim.x) {
         const T* xr = x + r * stride;
+        // the row maximum of |x| propagates NaN, as torch's amax: a NaN row gets scale 1
+        // (NaN > 0 is false) and its NaN entries stay NaN through the clamp
         float m = 0.f;
-        for (int i = tid; i < cols; i += kThreads) m = fmaxf(m, fabsf(to_f32<T>(xr[i])));
+        bool nan = false;
+        for (int i = tid; i < cols; i += kThreads) {
+            const float a = fabsf(to_f32<T>(xr[i]));
+            nan |= a != a;
+            m = fmaxf(m, a);
+        }
 #pragma unroll
         for (int o = 16; o > 0; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
-        if (lane == 0) wmax[wid] = m;
+        nan = __any_sync(0xffffffffu, nan);
+        if (lane == 0) wmax[wid] = nan ? __int_as_float(0x7fc00000) : m;
         __syncthreads();
         float amax = wmax[0];
+        bool any_nan = amax != amax;
 #pragma unroll
-        for (int w = 1; w < kWarps; ++w) amax = fmaxf(amax, wmax[w]);
-        const float s = amax > 0.f ? __fdiv_rn(amax, 448.0f) : 1.0f;
+        for (int w = 1; w < kWarps; ++w) {
+            any_nan |= wmax[w] != wmax[w];
+            amax = fmaxf(amax, wmax[w]);
+        }
+        const float s = (!any_nan && amax > 0.f) ? __fdiv_rn(amax, 448.0f) : 1.0f;
         if (tid == 0) scale[r] = s;
         uint8_t* qr = q + r * q_stride;
         for (int i = tid; i < cols; i += kThreads) {
-            const float v = fminf(fmaxf(__fdiv_rn(to_f32<T>(xr[i]), s), -448.0f), 448.0f);
+            const float t = __fdiv_rn(to_f32<T>(xr[i]), s);
+            const float v = (t != t) ? t : fminf(fmaxf(t, -448.0f), 448.0f);
             qr[i] = (uint8_t)__nv_cvt_float_to_fp8(v, __NV_SATFINITE, __NV_E4M3);
         }
         __syncthreads();  // wmax is reused by the next row

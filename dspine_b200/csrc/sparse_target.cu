@@ -1,0 +1,396 @@
+// sparse_target.cu -- the small-support joint target of build_sparse_target (sm_100a).
+//
+// Replaces sampling/sparse/target.py:95-178 (build_sparse_target; its CPU branch :156-178 is the
+// definition, _pack_joint :23-53 and _overflow_dense :56-76 the CUDA branch).  Per logit row,
+// with e_i = exp2c((l_i - m) c) and S the exact fixed-point mass of the whole row:
+//   threshold key = the k-th largest key (k = top_k <= capacity), every tie of it passes;
+//   nucleus       = the exact mass H of strictly larger keys satisfies H < top_p * S (or
+//                   top_p >= 1);
+//   kept          = e_i > 0, key_i >= threshold key, nucleus(key_i).
+// count <= capacity: the kept ids ascending, values e_i / S_kept, length count.  count >
+// capacity (overflow): the dense row p_i = e_i / S_thr for key_i >= threshold key (S_thr their
+// mass), 0 elsewhere; packed entries -1 / 0, length = capacity.  Dense rows of packed rows are
+// not written (accept_sparse reads only overflow rows).
+//
+// One CTA of 256 threads per row, two streaming passes from HBM:
+//   pass A  the row's maximum and every thread's maximum;
+//   pass B  the exact mass S and the candidate window: elements whose key is at least tau, the
+//           largest key that at least k thread maxima reach (so the window holds the k largest
+//           elements and every tie of the k-th);
+// then the threshold, the nucleus and the kept set from the window (a few dozen elements), and
+// for overflow rows one write pass.  A window of more than kWinCap elements (a plateau of equal
+// values) switches to a bit search of the threshold with counting passes.
+//
+// Rows are read with 16-byte loads when the row start allows it (scalar head and tail
+// otherwise); bf16 and fp32 logits share the code through Elem<T>.
+
+#include "dsv_common.cuh"
+#include "dsv_kernels.h"
+
+namespace dsv {
+namespace spt {
+
+constexpr int kNT = 256;
+constexpr int kNW = kNT / 32;
+constexpr int kWinCap = 1024;  // window candidates per row
+constexpr int kMaxCap = 64;    // largest capacity (and top-k)
+
+struct Smem {
+    uint32_t wkey[kWinCap];
+    int32_t widx[kWinCap];
+    uint32_t nwin;
+    uint32_t ngt, neq;
+    uint32_t gt_key[kMaxCap];
+    int32_t gt_idx[kMaxCap];
+    int32_t eq_idx[kMaxCap + 1];
+    int32_t out_idx[kMaxCap];
+    uint32_t red32[kNW];
+    unsigned long long red64[kNW];
+    uint32_t thr_key;
+    int32_t count;
+    int32_t overflow;
+    float inv;
+};
+
+__device__ __forceinline__ uint32_t block_max_u32(uint32_t v, Smem* sh) {
+    v = __reduce_max_sync(0xffffffffu, v);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) sh->red32[threadIdx.x >> 5] = v;
+    __syncthreads();
+    uint32_t r = 0;
+#pragma unroll
+    for (int i = 0; i < kNW; ++i) r = max(r, sh->red32[i]);
+    return r;
+}
+
+__device__ __forceinline__ uint32_t block_sum_u32(uint32_t v, Smem* sh) {
+    v = __reduce_add_sync(0xffffffffu, v);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) sh->red32[threadIdx.x >> 5] = v;
+    __syncthreads();
+    uint32_t r = 0;
+#pragma unroll
+    for (int i = 0; i < kNW; ++i) r += sh->red32[i];
+    return r;
+}
+
+__device__ __forceinline__ unsigned long long block_sum_u64(unsigned long long v, Smem* sh) {
+    v = warp_sum_u64(v);
+    __syncthreads();
+    if ((threadIdx.x & 31) == 0) sh->red64[threadIdx.x >> 5] = v;
+    __syncthreads();
+    unsigned long long r = 0;
+#pragma unroll
+    for (int i = 0; i < kNW; ++i) r += sh->red64[i];
+    return r;
+}
+
+// fn(i, raw bits) for every element of the row, each element by exactly one thread; 16-byte
+// loads (four in flight per thread) between a scalar head and tail
+template <typename T, typename F>
+__device__ __forceinline__ void for_row(const T* row, int V, F&& fn) {
+    using E = Elem<T>;
+    const int tid = threadIdx.x;
+    const uintptr_t addr = reinterpret_cast<uintptr_t>(row);
+    int head = (int)(((16u - (addr & 15u)) & 15u) / sizeof(T));
+    if ((addr & (sizeof(T) - 1)) != 0) head = V;  // not even element-aligned: all scalar
+    if (head > V) head = V;
+    const int nvec = (V - head) / E::kEV;
+    const int tail0 = head + nvec * E::kEV;
+    for (int i = tid; i < head; i += kNT) fn(i, E::raw(row, i));
+    const uint4* vp = reinterpret_cast<const uint4*>(row + head);
+    int v = tid;
+    for (; v + 3 * kNT < nvec; v += 4 * kNT) {
+        uint4 x[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) x[u] = __ldg(vp + v + u * kNT);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            uint32_t e[E::kEV];
+            E::unpack(x[u], e);
+#pragma unroll
+            for (int j = 0; j < E::kEV; ++j) fn(head + (v + u * kNT) * E::kEV + j, e[j]);
+        }
+    }
+    for (; v < nvec; v += kNT) {
+        uint32_t e[E::kEV];
+        E::unpack(__ldg(vp + v), e);
+#pragma unroll
+        for (int j = 0; j < E::kEV; ++j) fn(head + v * E::kEV + j, e[j]);
+    }
+    for (int i = tail0 + tid; i < V; i += kNT) fn(i, E::raw(row, i));
+}
+
+// floor(u * m) and whether u * m is an integer (u in [0, 1))
+__device__ __forceinline__ long long scale_floor_exact(float u, unsigned long long m, bool& exact) {
+    const long long f = scale_floor(u, m);
+    exact = false;
+    if (f >= 0) {
+        const uint32_t b = __float_as_uint(u);
+        const uint32_t e = (b >> 23) & 0xFFu;
+        const unsigned long long mant = (b & 0x7FFFFFu) | (e ? 0x800000u : 0u);
+        const int shift = e ? (150 - (int)e) : 149;
+        const unsigned long long lo = mant * m, hi = __umul64hi(mant, m);
+        if (shift >= 128) exact = (lo | hi) == 0ull;
+        else if (shift >= 64) exact = lo == 0ull && (hi & ((1ull << (shift - 64)) - 1ull)) == 0ull;
+        else exact = (lo & ((1ull << shift) - 1ull)) == 0ull;
+    }
+    return f;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kNT) sparse_target_kernel(SparseTargetArgs a) {
+    using E = Elem<T>;
+    __shared__ Smem sh_;
+    Smem* sh = &sh_;
+    const int tid = threadIdx.x;
+    for (long long r = blockIdx.x; r < a.rows; r += gridDim.x) {
+        const T* row = reinterpret_cast<const T*>(a.logits) + r * a.stride;
+        const long long req = a.row_request ? a.row_request[r] : r / a.rows_per_request;
+        const float Tm = a.temperature[req];
+        const int topk = a.top_k[req];
+        const float topp = a.top_p[req];
+        const int V = a.V;
+        const int cap = a.capacity;
+        int32_t* oid = a.ids + r * cap;
+        float* oval = a.values + r * cap;
+        const int kk = topk < 1 ? 1 : (topk > V ? V : (topk > cap ? cap : topk));
+        const float c = log2e_over(Tm);
+
+        // ---- pass A: maxima (key order; the first index of the row maximum) -----------------
+        uint32_t tkey = 0;
+        int tfirst = 0x7fffffff;
+        for_row<T>(row, V, [&](int i, uint32_t u) {
+            const uint32_t k = E::key(u);
+            if (k > tkey || (k == tkey && i < tfirst)) { tkey = k; tfirst = i; }
+        });
+        const uint32_t mkey = block_max_u32(tkey, sh);
+        const float m = E::key_to_float(mkey);
+        if (!(Tm > 0.0f) || !(c < __int_as_float(0x7f800000))) {
+            // no temperature: one-hot at the first maximum (the reference gates such rows away)
+            if (tid == 0) sh->count = 0x7fffffff;
+            __syncthreads();
+            if (tkey == mkey) atomicMin(&sh->count, tfirst);
+            __syncthreads();
+            for (int j = tid; j < cap; j += kNT) {
+                oid[j] = j == 0 ? sh->count : -1;
+                oval[j] = j == 0 ? 1.0f : 0.0f;
+            }
+            if (tid == 0) {
+                a.lengths[r] = 1;
+                a.overflow[r] = 0;
+            }
+            __syncthreads();
+            continue;
+        }
+        // tau: the largest key that at least kk thread maxima reach
+        uint32_t tau = 0;
+        for (int bit = E::kKeyBits - 1; bit >= 0; --bit) {
+            const uint32_t cand = tau | (1u << bit);
+            if (__syncthreads_count(tkey >= cand) >= kk) tau = cand;
+        }
+        if (tid == 0) sh->nwin = 0;
+        __syncthreads();
+
+        // ---- pass B: exact mass S and the window of keys >= tau ----------------------------
+        unsigned long long sacc = 0;
+        for_row<T>(row, V, [&](int i, uint32_t u) {
+            const uint32_t k = E::key(u);
+            const float y = __fmul_rn(__fsub_rn(E::to_float(u), m), c);
+            if (y >= -41.5f) sacc += fix01(exp2c(y));
+            if (k >= tau) {
+                const uint32_t pos = atomicAdd(&sh->nwin, 1u);
+                if (pos < (uint32_t)kWinCap) {
+                    sh->wkey[pos] = k;
+                    sh->widx[pos] = i;
+                }
+            }
+        });
+        const unsigned long long S = block_sum_u64(sacc, sh);
+        const uint32_t nwin = sh->nwin;
+
+        // ---- the threshold key and the lists above / at it ------------------------------------
+        uint32_t thr_key;
+        if (nwin <= (uint32_t)kWinCap) {
+            // the kk-th largest key of the window (which holds every element >= tau)
+            if (tid == 0) sh->thr_key = 0;
+            __syncthreads();
+            for (uint32_t i = tid; i < nwin; i += kNT) {
+                const uint32_t ki = sh->wkey[i];
+                uint32_t gt = 0, ge = 0;
+                for (uint32_t j = 0; j < nwin; ++j) {
+                    const uint32_t kj = sh->wkey[j];
+                    gt += kj > ki;
+                    ge += kj >= ki;
+                }
+                if (gt < (uint32_t)kk && ge >= (uint32_t)kk) sh->thr_key = ki;  // same value
+            }
+            __syncthreads();
+            thr_key = sh->thr_key;
+            if (tid == 0) {
+                sh->ngt = 0;
+                sh->neq = 0;
+            }
+            __syncthreads();
+            for (uint32_t i = tid; i < nwin; i += kNT) {
+                const uint32_t ki = sh->wkey[i];
+                if (ki > thr_key) {
+                    const uint32_t p = atomicAdd(&sh->ngt, 1u);
+                    if (p < (uint32_t)kMaxCap) {
+                        sh->gt_key[p] = ki;
+                        sh->gt_idx[p] = sh->widx[i];
+                    }
+                } else if (ki == thr_key) {
+                    const uint32_t p = atomicAdd(&sh->neq, 1u);
+                    if (p <= (uint32_t)kMaxCap) sh->eq_idx[p] = sh->widx[i];
+                }
+            }
+            __syncthreads();
+        } else {
+            // a plateau: the threshold by a bit search over counting passes
+            thr_key = 0;
+            for (int bit = E::kKeyBits - 1; bit >= 0; --bit) {
+                const uint32_t cand = thr_key | (1u << bit);
+                uint32_t cnt = 0;
+                for_row<T>(row, V, [&](int, uint32_t u) { cnt += E::key(u) >= cand; });
+                if (block_sum_u32(cnt, sh) >= (uint32_t)kk) thr_key = cand;
+            }
+            if (tid == 0) {
+                sh->ngt = 0;
+                sh->neq = 0;
+            }
+            __syncthreads();
+            for_row<T>(row, V, [&](int i, uint32_t u) {
+                const uint32_t k = E::key(u);
+                if (k > thr_key) {
+                    const uint32_t p = atomicAdd(&sh->ngt, 1u);
+                    if (p < (uint32_t)kMaxCap) {
+                        sh->gt_key[p] = k;
+                        sh->gt_idx[p] = i;
+                    }
+                } else if (k == thr_key) {
+                    const uint32_t p = atomicAdd(&sh->neq, 1u);
+                    if (p <= (uint32_t)kMaxCap) sh->eq_idx[p] = i;
+                }
+            });
+            __syncthreads();
+        }
+
+        // ---- nucleus, counts and the kept ids (thread 0; a few dozen elements) -------------
+        if (tid == 0) {
+            const int ngt = (int)min(sh->ngt, (uint32_t)kMaxCap);  // < kk <= kMaxCap
+            const uint32_t neq = sh->neq;
+            // gt elements by key descending, index ascending (insertion sort)
+            for (int i = 1; i < ngt; ++i) {
+                const uint32_t k = sh->gt_key[i];
+                const int x = sh->gt_idx[i];
+                int j = i - 1;
+                while (j >= 0 && (sh->gt_key[j] < k || (sh->gt_key[j] == k && sh->gt_idx[j] > x))) {
+                    sh->gt_key[j + 1] = sh->gt_key[j];
+                    sh->gt_idx[j + 1] = sh->gt_idx[j];
+                    --j;
+                }
+                sh->gt_key[j + 1] = k;
+                sh->gt_idx[j + 1] = x;
+            }
+            bool exact = false;
+            const long long pf = scale_floor_exact(topp, S, exact);
+            const bool use_p = !(topp >= 1.0f);
+            const long long hmax = pf >= 0 ? pf - (exact ? 1 : 0) : -1;
+            unsigned long long run = 0, H = 0, skept = 0;
+            int kept_gt = 0;
+            bool pass = true;
+            uint32_t prev = 0xFFFFFFFFu;
+            for (int i = 0; i < ngt && pass; ++i) {
+                const uint32_t k = sh->gt_key[i];
+                const float e = exp2c(__fmul_rn(__fsub_rn(E::key_to_float(k), m), c));
+                const unsigned long long F = fixv(e);
+                if (k != prev) {
+                    H = run;
+                    prev = k;
+                }
+                pass = e > 0.0f && (!use_p || (pf != -2 && (long long)H <= hmax));
+                if (pass) {
+                    ++kept_gt;
+                    skept += F;
+                }
+                run += F;
+            }
+            const float et = exp2c(__fmul_rn(__fsub_rn(E::key_to_float(thr_key), m), c));
+            const unsigned long long Ft = fixv(et);
+            const bool thr_pass = pass && et > 0.0f && (!use_p || (pf != -2 && (long long)run <= hmax));
+            const long long count = kept_gt + (thr_pass ? (long long)neq : 0ll);
+            if (thr_pass) skept += (unsigned long long)neq * Ft;
+            const bool ovf = count > cap;
+            sh->thr_key = thr_key;
+            sh->overflow = ovf ? 1 : 0;
+            sh->count = ovf ? cap : (int)count;
+            sh->inv = inv_from_fix(skept);
+            a.lengths[r] = ovf ? cap : (int)count;
+            a.overflow[r] = ovf ? 1 : 0;
+            if (!ovf) {
+                int n = 0;
+                for (int i = 0; i < kept_gt; ++i) sh->out_idx[n++] = sh->gt_idx[i];
+                if (thr_pass)
+                    for (uint32_t i = 0; i < neq; ++i) sh->out_idx[n++] = sh->eq_idx[i];
+                for (int i = 1; i < n; ++i) {  // ascending ids
+                    const int x = sh->out_idx[i];
+                    int j = i - 1;
+                    while (j >= 0 && sh->out_idx[j] > x) {
+                        sh->out_idx[j + 1] = sh->out_idx[j];
+                        --j;
+                    }
+                    sh->out_idx[j + 1] = x;
+                }
+            }
+        }
+        __syncthreads();
+        const int count = sh->count;
+        const float inv = sh->inv;
+        if (!sh->overflow) {
+            for (int j = tid; j < cap; j += kNT) {
+                if (j < count) {
+                    const int i = sh->out_idx[j];
+                    const float e = exp2c(__fmul_rn(__fsub_rn(E::to_float(E::raw(row, i)), m), c));
+                    oid[j] = i;
+                    oval[j] = __fmul_rn(e, inv);
+                } else {
+                    oid[j] = -1;
+                    oval[j] = 0.0f;
+                }
+            }
+        } else {
+            for (int j = tid; j < cap; j += kNT) {
+                oid[j] = -1;
+                oval[j] = 0.0f;
+            }
+            // the dense row: every element at or above the threshold, renormalised
+            float* d = a.dense + r * (long long)V;
+            const uint32_t tk = sh->thr_key;
+            for_row<T>(row, V, [&](int i, uint32_t u) {
+                float p = 0.0f;
+                if (E::key(u) >= tk)
+                    p = __fmul_rn(exp2c(__fmul_rn(__fsub_rn(E::to_float(u), m), c)), inv);
+                d[i] = p;
+            });
+        }
+        __syncthreads();
+    }
+}
+
+}  // namespace spt
+
+int launch_sparse_target(const SparseTargetArgs& a, int dtype, cudaStream_t stream) {
+    if (a.rows <= 0) return kOk;
+    if (a.capacity < 1 || a.capacity > spt::kMaxCap) return kBadShape;
+    const long long grid = a.rows < 65535 ? a.rows : 65535;
+    if (dtype == 0)
+        spt::sparse_target_kernel<__nv_bfloat16><<<(unsigned)grid, spt::kNT, 0, stream>>>(a);
+    else if (dtype == 1)
+        spt::sparse_target_kernel<float><<<(unsigned)grid, spt::kNT, 0, stream>>>(a);
+    else
+        return kBadDtype;
+    return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
+}
+
+}  // namespace dsv

@@ -217,6 +217,7 @@ struct TaskInfo {
     int b, s, kind, cat, cap;
     long long row;     // row index in its tensor (-1: invalid)
     float T, p, c;
+    float mp;          // min-p of the request (0: no floor; always 0 in the joint mode)
     int k;
     int half;          // -1: the whole row; 0 / 1: first / second half of a split row
     int slot;          // split rows: the slot the first half publishes to
@@ -229,11 +230,12 @@ __device__ int request_cat(const VerifyArgs& a, int b, float& c_out, int wink) {
     const float T = a.temperature[b];
     const int k = a.top_k[b];
     const float p = a.top_p[b];
+    const float mp = (a.mode != kModeJoint && a.min_p) ? a.min_p[b] : 0.0f;
     const float c = log2e_over(T);
     c_out = c;
     if (is_greedy(T, k, c)) return kGreedy;
     if (p < 1.0f) return kBinned;             // nucleus (any k): per-key histogram walk
-    if (k >= a.V) return kKeepAll;
+    if (k >= a.V) return mp > 0.0f ? kBinned : kKeepAll;  // min-p alone: counts from the top
     if (k <= wink) return kWindow;            // pure top-k, small k: candidate window
     return kBinned;                           // pure top-k, large k: exact counts from the top
 }
@@ -324,6 +326,7 @@ __device__ TaskInfo decode_task(const VerifyArgs& a, const Sm* sh, int t) {
     ti.T = a.temperature[ti.b];
     ti.k = a.top_k[ti.b];
     ti.p = a.top_p[ti.b];
+    ti.mp = (a.mode != kModeJoint && a.min_p) ? a.min_p[ti.b] : 0.0f;
     ti.c = log2e_over(ti.T);
     ti.half = -1;
     ti.slot = -1;
@@ -550,6 +553,14 @@ __device__ __forceinline__ RowGeo row_geo(const VerifyArgs& a, const TaskInfo& t
     g.off = (int)((reinterpret_cast<uintptr_t>(g.rowp) & 15u) >> 1);
     g.nv = ti.row < 0 ? 0 : (a.V + g.off + 7) >> 3;
     return g;
+}
+
+// geometry of row `row` of the target (kind 0) or draft (kind 1) logits
+__device__ __forceinline__ RowGeo row_geo_at(const VerifyArgs& a, int kind, long long row) {
+    TaskInfo ti;
+    ti.kind = kind;
+    ti.row = row;
+    return row_geo(a, ti);
 }
 
 // vector v of the row with the halves outside [0, V) set to -inf
@@ -935,6 +946,21 @@ __device__ KeyStop count_walk(RSmem* sh, const VerifyArgs& a, const RowGeo& g, i
     return ks;
 }
 
+// Elements of the row whose key is >= kf (the min-p floor): one pass through the small ring
+// (the histogram stays intact), packed bf16x2 compares.  All threads must call it.
+__device__ long long count_ge_key(RSmem* sh, const VerifyArgs& a, const RowGeo& g, int V,
+                                  uint32_t kf) {
+    const uint32_t fb = key_bits(kf);
+    const uint32_t fb2 = fb | (fb << 16);
+    uint32_t cnt = 0;
+    stream_row(sh, a, g, V, [&](const uint4& x, int) {
+        // halves outside the row read as -inf, below every floor
+        cnt += (uint32_t)(__popc(bf2_ge(x.x, fb2)) + __popc(bf2_ge(x.y, fb2)) +
+                          __popc(bf2_ge(x.z, fb2)) + __popc(bf2_ge(x.w, fb2))) >> 4;
+    });
+    return (long long)rcta_sum_u64(cnt, sh);
+}
+
 // One row task: its descriptor (and, for greedy rows, its packed first argmax).  All threads.
 // Split rows: the first half publishes its per-key counts, its maximum key, its band values
 // and its out-of-range flag to the row's slot, then a flag; the second half waits for the flag
@@ -1002,7 +1028,10 @@ __device__ void process_row(RSmem* sh, const VerifyArgs& a, const TaskInfo& ti) 
 
     // Nucleus and keep-all rows start with the fixed-range histogram (one pass, no max
     // pass); the other rows, and rows with values outside that range, start with the max.
-    const bool onepass = ti.cat == kKeepAll || (ti.cat == kBinned && ti.p < 1.0f);
+    // sequential-mode nucleus rows with a top-k need the top-k's mass before the histogram
+    // walk (counts from the top, which reuse the histogram's storage): they take the max pass
+    const bool seq_k = a.mode == kModeSeq && ti.k < V && ti.p < 1.0f;
+    const bool onepass = ti.cat == kKeepAll || (ti.cat == kBinned && ti.p < 1.0f && !seq_k);
     if (ti.half == 0 && !onepass) return;  // only one-pass rows are split: the second half does all
     const int half = onepass ? ti.half : -1;
     uint32_t tkey = 0, mkey = 0;
@@ -1153,7 +1182,17 @@ __device__ void process_row(RSmem* sh, const VerifyArgs& a, const TaskInfo& ti) 
         }
     }
     const float m = bf(key_bits(mkey));
-    const long long kk = ti.k < V ? (long long)ti.k : (long long)V;
+    const long long k_top = ti.k < V ? (long long)ti.k : (long long)V;
+    long long kk = k_top;
+    if (ti.mp > 0.0f) {
+        // min-p: the kept set is also a prefix of the elements at or above the floor key
+        if (tid == 0) sh->sel[13] = (int)key16_floor(minp_floor32(m, ti.c, ti.mp));
+        __syncthreads();
+        const uint32_t kf = (uint32_t)sh->sel[13];
+        const long long cm = kf > 0xFFFFu ? 0ll : count_ge_key(sh, a, g, V, kf);
+        if (cm < kk) kk = cm;
+        if (kk < 1) kk = 1;
+    }
     const int cat = ti.cat;
     const bool nucleus = ti.p < 1.0f;
     const uint32_t kninf = okey(0xFF80u);  // key of -inf
@@ -1161,6 +1200,17 @@ __device__ void process_row(RSmem* sh, const VerifyArgs& a, const TaskInfo& ti) 
     ks.found = 0;
     unsigned long long S = 0;
     long long thr = 0x7fffffffffffffffll;
+    // sequential mode: top-p is taken against the mass of the top-k elements (k before the
+    // min-p floor), found by counting from the top
+    unsigned long long s_top = 0;
+    bool have_s_top = false;
+    if (seq_k) {
+        const KeyStop k1 = count_walk(sh, a, g, V, mkey, kninf, m, ti.c, 0ull, 0ull, k_top, thr);
+        if (k1.found) {
+            s_top = k1.mass + (unsigned long long)(k_top - (long long)k1.cnt) * k1.F;
+            have_s_top = true;
+        }
+    }
 
     if (cat == kWindow) {
         // ---- pure top-k, k <= 256: candidates >= tau, ranked exactly -------------------
@@ -1380,7 +1430,7 @@ __device__ void process_row(RSmem* sh, const VerifyArgs& a, const TaskInfo& ti) 
             PROF_END(ti.cat, 3);
             return;
         }
-        thr = scale_floor(ti.p, S);
+        thr = scale_floor(ti.p, have_s_top ? s_top : S);
         PROF_MARK(ti.cat, 4);
         if (gme < ng && ct > 0 && ((long long)(cb + ct) >= kk || (long long)(mb + mt) > thr))
             atomicMin(&sh->sel[6], tid);
@@ -1474,6 +1524,16 @@ __device__ void process_row(RSmem* sh, const VerifyArgs& a, const TaskInfo& ti) 
         return;
     }
 
+    if (a.cand != nullptr) {
+        // verification: the cut inside the boundary key's ties is needed only where a drafted
+        // token or a bonus draw meets that key, and is resolved there (row_done)
+        if (tid == 0) {
+            put_desc(a, ti, m, ks.key, kTiePending, skept, 0, (uint32_t)ks.count << 8);
+            a.desc[(ti.b * kT + ti.s) * 2 + ti.kind].pad = (uint32_t)ntie;
+        }
+        PROF_END(ti.cat, 7);
+        return;
+    }
     // ---- tie cut: occurrence number ntie of the boundary key in index order ------------
     {
         // from the nearer end: occurrence ntie of count in index order is occurrence
@@ -1994,41 +2054,117 @@ __device__ bool row_done(RSmem* sh, const VerifyArgs& a, int b) {
         }
         return true;
     }
-    if (tid >= 32) return false;
     __threadfence();
     const bool onehot_q = a.drf == nullptr;
     const uint16_t* tgt = reinterpret_cast<const uint16_t*>(a.tgt);
     const uint16_t* drf = reinterpret_cast<const uint16_t*>(a.drf);
-    bool acc = false;
-    const int s = lane;
-    if (s < cap - 1) {
-        const long long tok = a.cand[b * kT + s + 1];
-        const bool valid = tok >= 0 && tok < a.V;
+    // per position s (lane s of warp 0): the drafted token's p and q; a token whose key is the
+    // boundary key of a row with a pending tie cut needs that key's occurrences before it
+    // (counted by the whole CTA below): pend[s][r] = 1 + the number needed, or 0
+    float* pq = reinterpret_cast<float*>(sh->hist);              // [32][2] p, q
+    uint32_t* pend = reinterpret_cast<uint32_t*>(sh->hist + 64);  // [32][2]
+    uint32_t* cnt = reinterpret_cast<uint32_t*>(sh->hist + 128);  // [32][2] occurrences found
+    if (tid < 32) {
+        const int s = lane;
         float p = 0.0f, q = 0.0f;
-        if (valid) {
-            const RowDesc dt = load_desc_cg(&a.desc[(b * kT + s) * 2 + 0]);
-            const long long tr = a.tgt_row[b] + s;
-            if (tr >= 0 && tr < a.tgt_rows) {
-                const uint32_t pb = tgt[tr * a.stride + tok];
-                p = row_prob(dt, bf(pb), pb, (int)tok);
-            }
-            if (onehot_q) {
-                q = 1.0f;
-            } else {
-                const RowDesc dd = load_desc_cg(&a.desc[(b * kT + s) * 2 + 1]);
-                const long long dr = a.drf_row[b] + s;
-                if (dr >= 0 && dr < a.drf_rows) {
-                    const uint32_t qb = drf[dr * a.stride + tok];
-                    q = row_prob(dd, bf(qb), qb, (int)tok);
+        uint32_t pt = 0u, pd = 0u;
+        if (s < cap - 1) {
+            const long long tok = a.cand[b * kT + s + 1];
+            const bool valid = tok >= 0 && tok < a.V;
+            if (valid) {
+                const RowDesc dt = load_desc_cg(&a.desc[(b * kT + s) * 2 + 0]);
+                const long long tr = a.tgt_row[b] + s;
+                if (tr >= 0 && tr < a.tgt_rows) {
+                    const uint32_t pb = tgt[tr * a.stride + tok];
+                    if (dt.tie_cut == kTiePending && okey(pb) == dt.kstar) {
+                        pt = 1u + dt.pad;
+                        p = __fmul_rn(exp2c(__fmul_rn(__fadd_rn(bf(pb), -dt.m), dt.c)), dt.inv_s);
+                    } else {
+                        p = row_prob(dt, bf(pb), pb, (int)tok);
+                    }
+                }
+                if (onehot_q) {
+                    q = 1.0f;
+                } else {
+                    const RowDesc dd = load_desc_cg(&a.desc[(b * kT + s) * 2 + 1]);
+                    const long long dr = a.drf_row[b] + s;
+                    if (dr >= 0 && dr < a.drf_rows) {
+                        const uint32_t qb = drf[dr * a.stride + tok];
+                        if (dd.tie_cut == kTiePending && okey(qb) == dd.kstar) {
+                            pd = 1u + dd.pad;
+                            q = __fmul_rn(exp2c(__fmul_rn(__fadd_rn(bf(qb), -dd.m), dd.c)), dd.inv_s);
+                        } else {
+                            q = row_prob(dd, bf(qb), qb, (int)tok);
+                        }
+                    }
                 }
             }
         }
-        acc = q > 0.0f && q <= 1.0f && __fmul_rn(a.u[b * 15 + s], q) < p;
+        pq[2 * s] = p;
+        pq[2 * s + 1] = q;
+        pend[2 * s] = pt;
+        pend[2 * s + 1] = pd;
+        cnt[2 * s] = 0u;
+        cnt[2 * s + 1] = 0u;
+        const uint32_t any = __ballot_sync(0xffffffffu, (pt | pd) != 0u);
+        if (lane == 0) sh->sel[14] = (int)any;
     }
-    const uint32_t rej = __ballot_sync(0xffffffffu, !acc) &
-                         ((cap - 1 >= 32) ? 0xffffffffu : ((1u << (cap - 1)) - 1u));
-    if (lane == 0) {
-        a.racc[2 * b + 1] = (unsigned)(rej ? __ffs(rej) - 1 : cap - 1);
+    __syncthreads();
+    const uint32_t any_pending = (uint32_t)sh->sel[14];
+    if (any_pending) {
+        // occurrences of the boundary key before the drafted token, counted by the CTA
+        for (int e = 0; e < 2 * (cap - 1); ++e) {
+            const int s = e >> 1, r = e & 1;
+            if (!(any_pending & (1u << s)) || pend[e] == 0u) continue;
+            const long long tok = a.cand[b * kT + s + 1];
+            const long long row = r == 0 ? a.tgt_row[b] + s : a.drf_row[b] + s;
+            const uint16_t* rp = (r == 0 ? tgt : drf) + row * a.stride;
+            const uint32_t ks = load_desc_cg(&a.desc[(b * kT + s) * 2 + r]).kstar;
+            uint32_t c = 0;
+            for (long long i = tid; i < tok; i += kRT) c += okey(rp[i]) == ks;
+            const uint32_t tot = (uint32_t)rcta_sum_u64(c, sh);
+            if (tid == 0) cnt[e] = tot;
+        }
+        __syncthreads();
+    }
+    if (tid < 32) {
+        const int s = lane;
+        bool acc = false;
+        if (s < cap - 1) {
+            float p = pq[2 * s], q = pq[2 * s + 1];
+            // kept iff fewer than ntie occurrences precede it (ntie = pend - 1)
+            if (pend[2 * s] && !(cnt[2 * s] < pend[2 * s] - 1u)) p = 0.0f;
+            if (pend[2 * s + 1] && !(cnt[2 * s + 1] < pend[2 * s + 1] - 1u)) q = 0.0f;
+            acc = q > 0.0f && q <= 1.0f && __fmul_rn(a.u[b * 15 + s], q) < p;
+        }
+        const uint32_t rej = __ballot_sync(0xffffffffu, !acc) &
+                             ((cap - 1 >= 32) ? 0xffffffffu : ((1u << (cap - 1)) - 1u));
+        if (lane == 0) sh->sel[15] = rej ? __ffs(rej) - 1 : cap - 1;
+    }
+    __syncthreads();
+    const int acc_len = sh->sel[15];
+    // the rows of the bonus draw: their pending tie cuts are resolved before the chain tasks
+    // read them (the target row, and the draft row unless the whole block was accepted)
+    for (int r = 0; r < 2; ++r) {
+        if (r == 1 && (onehot_q || acc_len == cap - 1)) break;
+        RowDesc* dp = &a.desc[(b * kT + acc_len) * 2 + r];
+        const RowDesc d = load_desc_cg(dp);
+        if (d.tie_cut != kTiePending) continue;
+        const long long row = r == 0 ? a.tgt_row[b] + acc_len : a.drf_row[b] + acc_len;
+        const RowGeo g = row_geo_at(a, r, row);
+        const unsigned long long count = d.flags >> 8, ntie = d.pad;
+        const uint32_t kexp = (key_bits(d.kstar) >> 7) & 0xFFu;
+        const bool normal_key = kexp != 0u && kexp != 0xFFu;
+        const int tie = (!normal_key || 2 * ntie <= count + 1ull)
+                            ? tie_scan<false>(sh, a, g, a.V, d.kstar, ntie)
+                            : tie_scan<true>(sh, a, g, a.V, d.kstar, count - ntie + 1ull);
+        if (tid == 0) {
+            if (tie < 0) atomicOr(&a.ws->err, 16u);
+            __stcg(&dp->tie_cut, tie);
+        }
+    }
+    if (tid == 0) {
+        a.racc[2 * b + 1] = (unsigned)acc_len;
         a.racc[2 * b] = 0u;  // for the next launch
         __threadfence();
         const unsigned pos = atomicAdd(&a.ws->ready_tail, 1u);

@@ -58,6 +58,8 @@ struct RowState {
     int k_on, p_on;
     int k;
     float top_p;
+    float mp;           // min-p (0: no floor)
+    int thr_preset;     // thr was set before the walk (sequential mode: from the top-k mass)
     float c;            // log2(e) / T
     float m;            // max logit
     int argmax;
@@ -382,10 +384,12 @@ __device__ void level_scan(Shared* sh, cg::cluster_group& cluster, int pi, bool 
         long long thr = rs.thr;
         if (first) {
             const unsigned long long tot = warp_sum_u64(lm);
-            thr = 0x7fffffffffffffffll;
-            if (rs.p_on) {
-                thr = scale_floor(rs.top_p, tot);
-                if (thr < 0) thr = 0;  // top_p <= 0: only the first element survives
+            if (!rs.thr_preset) {
+                thr = 0x7fffffffffffffffll;
+                if (rs.p_on) {
+                    thr = scale_floor(rs.top_p, tot);
+                    if (thr < 0) thr = 0;  // top_p <= 0: only the first element survives
+                }
             }
             if (lane == 0) { rs.s_total = tot; rs.thr = thr; }
         }
@@ -465,6 +469,105 @@ __device__ void radix_levels(Ctx<T>& cx, cg::cluster_group& cluster, int nrows) 
         level_scan<kC>(sh, cluster, pi, first, mask);
         first = false;
     }
+}
+
+// min-p: count the elements at or above each row's floor (minp_floor32 of its maximum) over
+// the cluster and cap the row's top-k at that count (the kept set stays a prefix of the rank
+// order).  All CTAs of the cluster call it.
+template <typename T, int kC>
+__device__ void minp_pass(Ctx<T>& cx, cg::cluster_group& cluster, int nrows) {
+    using E = Elem<T>;
+    Shared* sh = cx.sh;
+    Pub& pb = sh->pub[cx.bar_i & 1];
+    for (int r = 0; r < nrows; ++r) {
+        const RowState& rs = sh->rs[r];
+        uint32_t cnt = 0;
+        if (!rs.done && rs.mp > 0.0f) {
+            const uint32_t f32 = minp_floor32(rs.m, rs.c, rs.mp);
+            const uint32_t kf = E::kKeyBits == 16 ? key16_floor(f32) : f32;
+            const bool none = E::kKeyBits == 16 && kf > 0xFFFFu;
+            const uint4* vb = reinterpret_cast<const uint4*>(cx.buf[r]);
+            for (int v = threadIdx.x; v < cx.nvec && !none; v += kNT) {
+                uint32_t u[E::kEV];
+                E::unpack(vb[v], u);
+#pragma unroll
+                for (int j = 0; j < E::kEV; ++j) {
+                    const int li = v * E::kEV + j;
+                    if (li < cx.n && E::key(u[j]) >= kf) ++cnt;
+                }
+            }
+        }
+        cnt = block_sum_u32(sh, cnt);
+        if (threadIdx.x == 0) pb.tie_cnt[r] = cnt;
+    }
+    cluster.sync();
+    const int pi = cx.bar_i & 1;
+    cx.bar_i++;
+    if (threadIdx.x < nrows) {
+        RowState& rs = sh->rs[threadIdx.x];
+        if (!rs.done && rs.mp > 0.0f) {
+            uint32_t total = 0;
+#pragma unroll
+            for (int q = 0; q < kC; ++q)
+                total += cluster.map_shared_rank(&sh->pub[pi], q)->tie_cnt[threadIdx.x];
+            long long k = rs.k_on ? (long long)rs.k : (long long)cx.a->V;
+            if ((long long)total < k) k = (long long)total;
+            if (k < 1) k = 1;
+            if (k < (long long)cx.a->V) {
+                rs.k = (int)k;
+                rs.k_on = 1;
+            }
+        }
+    }
+    __syncthreads();
+}
+
+// sequential mode (flashinfer with min-p in the batch): top-p is taken against the mass of the
+// row's top-k elements.  A walk with the top-k alone gives that mass; the rows are then reset
+// for the final walk with the threshold preset.
+__device__ void seq_prepare(Shared* sh, int nrows, int key_bits, bool first_stage) {
+    if (threadIdx.x < nrows) {
+        RowState& rs = sh->rs[threadIdx.x];
+        if (first_stage) {
+            rs.p_on = 0;
+        } else {
+            long long thr = scale_floor(rs.top_p, rs.s_kept);
+            if (thr < 0) thr = 0;
+            rs.thr = thr;
+            rs.thr_preset = 1;
+            rs.p_on = 1;
+            rs.done = 0;
+            rs.keep_all = 0;
+            rs.prefix = 0;
+            rs.shift = key_bits - 8;
+            rs.cnt_above = 0;
+            rs.mass_above = 0;
+            rs.kstar = 0;
+            rs.tstar = 0;
+            rs.partial = 0;
+            rs.s_kept = 0;
+            rs.inv_s = 0.0f;
+        }
+    }
+    __syncthreads();
+}
+
+// The kept set of the task's rows: the sequential mode's top-k mass first, the min-p cap, then
+// the radix walk.  Both rows of a task belong to one request, so they share the mode.
+template <typename T, int kC>
+__device__ void select_rows(Ctx<T>& cx, cg::cluster_group& cluster, int nrows) {
+    Shared* sh = cx.sh;
+    const RowState& r0 = sh->rs[0];
+    const bool seq = cx.a->mode == kModeSeq && !r0.done && r0.k_on && r0.p_on;
+    const bool minp = r0.mp > 0.0f && !r0.done;
+    __syncthreads();  // every thread has read the row state before seq_prepare changes it
+    if (seq) {
+        seq_prepare(sh, nrows, Elem<T>::kKeyBits, true);
+        radix_levels<T, kC>(cx, cluster, nrows);
+        seq_prepare(sh, nrows, Elem<T>::kKeyBits, false);
+    }
+    if (minp) minp_pass<T, kC>(cx, cluster, nrows);
+    radix_levels<T, kC>(cx, cluster, nrows);
 }
 
 // Ties straddle the boundary of a row: count them per CTA, locate the drafted token among
@@ -941,6 +1044,8 @@ __global__ void __launch_bounds__(kNT) verify_kernel(VerifyArgs a) {
                     rs.k_on = !greedy && topk < a.V;
                     rs.top_p = a.top_p[b];
                     rs.p_on = !greedy && (rs.top_p < 1.0f);
+                    rs.mp = (!greedy && a.mode != kModeJoint && a.min_p) ? a.min_p[b] : 0.0f;
+                    rs.thr_preset = 0;
                     rs.c = c;
                     rs.done = greedy;
                     rs.keep_all = 0;
@@ -990,7 +1095,7 @@ __global__ void __launch_bounds__(kNT) verify_kernel(VerifyArgs a) {
                     res->bonus = bonus;
                 }
             } else {
-                radix_levels<T, kC>(cx, cluster, nrows);
+                select_rows<T, kC>(cx, cluster, nrows);
                 const bool anyp = sh->rs[0].partial || (nrows > 1 && sh->rs[1].partial);
                 if (anyp) tie_pass<T, kC>(cx, cluster, nrows);
                 decide<T>(cx, nrows);
@@ -1047,6 +1152,116 @@ __global__ void __launch_bounds__(kNT) verify_kernel(VerifyArgs a) {
         }
     }
     // no CTA may leave while a peer can still read its shared memory
+    cluster.sync();
+}
+
+// ---------------------------------------------------------------------------------------
+// Dense target probabilities of logit rows (dsv_target_probs for fp32 logits): the same
+// cluster-per-row selection as verify_kernel (slices staged in shared memory, radix walk,
+// tie cut), then every CTA writes its slice of p.  Row t belongs to request t / row_step.
+
+template <typename T, int kC>
+__global__ void __launch_bounds__(kNT) probs_kernel(VerifyArgs a, float* out) {
+    using E = Elem<T>;
+    cg::cluster_group cluster = cg::this_cluster();
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    const int tid = threadIdx.x;
+    const size_t slice_bytes = ((size_t)a.slice * sizeof(T) + 127) & ~(size_t)127;
+    Ctx<T> cx;
+    cx.a = &a;
+    cx.buf[0] = reinterpret_cast<T*>(smem_raw);
+    cx.buf[1] = reinterpret_cast<T*>(smem_raw + slice_bytes);
+    cx.sh = reinterpret_cast<Shared*>(smem_raw + 2 * slice_bytes);
+    cx.rank = (int)cluster.block_rank();
+    cx.lo = cx.rank * a.slice;
+    cx.n = max(0, min(a.slice, a.V - cx.lo));
+    cx.nvec = (cx.n + E::kEV - 1) / E::kEV;
+    cx.bar_i = 0;
+    cx.phase = 0;
+    Shared* sh = cx.sh;
+    if (tid == 0) {
+        mbar_init(&sh->bar, 1);
+        fence_mbar_init();
+        if (cx.rank == 0) sh->task_slot[0] = (int)atomicAdd(&a.ws->next, 1u);
+    }
+    cluster.sync();
+    cx.bar_i++;
+    const long long total = a.tgt_rows;
+    long long t = *cluster.map_shared_rank(&sh->task_slot[0], 0);
+    int iter = 0;
+    while (t < total) {
+        __syncthreads();
+        if (cx.rank == 0 && tid == 0)
+            sh->task_slot[(iter + 1) & 1] = (int)atomicAdd(&a.ws->next, 1u);
+        const int b = (int)(t / a.row_step);
+        const float Tb = a.temperature[b];
+        const int topk = a.top_k[b];
+        const float c = log2e_over(Tb);
+        const bool greedy = is_greedy(Tb, topk, c);
+        if (tid == 0) {
+            Task& tk = sh->tk;
+            tk.cand = -1;
+            tk.onehot_q = 1;
+            tk.pure = 1;
+            RowState& rs = sh->rs[0];
+            rs.greedy = greedy;
+            rs.k = topk;
+            rs.k_on = !greedy && topk < a.V;
+            rs.top_p = a.top_p[b];
+            rs.p_on = !greedy && (rs.top_p < 1.0f);
+            rs.mp = (!greedy && a.mode != kModeJoint && a.min_p) ? a.min_p[b] : 0.0f;
+            rs.thr_preset = 0;
+            rs.c = c;
+            rs.done = greedy;
+            rs.keep_all = 0;
+            rs.prefix = 0;
+            rs.shift = E::kKeyBits - 8;
+            rs.cnt_above = 0;
+            rs.mass_above = 0;
+            rs.thr = 0;
+            rs.kstar = 0;
+            rs.tstar = 0;
+            rs.partial = 0;
+            rs.s_total = 0;
+            rs.s_kept = 0;
+            rs.inv_s = 0.0f;
+            rs.tie_prefix = 0;
+            rs.tie_local = 0;
+            rs.local_cut = -1;
+            rs.cand_kept = 0;
+            rs.row = t;
+        }
+        __syncthreads();
+        load_slices<T>(cx, 1);
+        pass_max<T, kC>(cx, cluster, 1);
+        if (!greedy) {
+            select_rows<T, kC>(cx, cluster, 1);
+            if (sh->rs[0].partial) {
+                tie_pass<T, kC>(cx, cluster, 1);
+                local_cuts<T>(cx, 1);
+            }
+        }
+        // this CTA's slice of the row's probabilities
+        const RowState& rs = sh->rs[0];
+        float* orow = out + t * (long long)a.V + cx.lo;
+        for (int i = tid; i < cx.n; i += kNT) {
+            const uint32_t u = E::raw(cx.buf[0], i);
+            orow[i] = row_prob<T>(rs, u, cx.lo + i);
+        }
+        t = *cluster.map_shared_rank(&sh->task_slot[(iter + 1) & 1], 0);
+        ++iter;
+        cluster.sync();  // the next task's state is written only after every CTA is done here
+        cx.bar_i++;
+    }
+    if (cx.rank == 0 && tid == 0) {
+        __threadfence();
+        const unsigned old = atomicAdd(&a.ws->exited, 1u);
+        if (old == (unsigned)(a.num_clusters - 1)) {
+            a.ws->next = 0;
+            a.ws->exited = 0;
+            __threadfence();
+        }
+    }
     cluster.sync();
 }
 
@@ -1116,7 +1331,47 @@ int launch_verify_t(VerifyArgs a, cudaStream_t stream) {
     return kOk;
 }
 
+template <typename T, int kC>
+int launch_probs_t(VerifyArgs a, float* out, cudaStream_t stream) {
+    const int EV = Elem<T>::kEV;
+    int slice = (a.V + kC - 1) / kC;
+    slice = ((slice + EV - 1) / EV) * EV;
+    a.slice = slice;
+    const size_t smem = verify_smem_bytes<T>(slice);
+    if (smem > 227 * 1024) return kUnsupported;
+    auto kern = probs_kernel<T, kC>;
+    if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem) != cudaSuccess)
+        return kLaunchFailed;
+    cudaLaunchConfig_t cfg = {};
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kC;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.blockDim = dim3(kNT, 1, 1);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    cfg.gridDim = dim3(kC, 1, 1);
+    int nclus = 0;
+    if (cudaOccupancyMaxActiveClusters(&nclus, kern, &cfg) != cudaSuccess || nclus <= 0)
+        return kLaunchFailed;
+    if ((long long)nclus > a.tgt_rows) nclus = (int)a.tgt_rows;
+    if (nclus < 1) nclus = 1;
+    a.num_clusters = nclus;
+    cfg.gridDim = dim3(nclus * kC, 1, 1);
+    if (cudaLaunchKernelEx(&cfg, kern, a, out) != cudaSuccess) return kLaunchFailed;
+    return kOk;
+}
+
 }  // namespace
+
+int launch_probs_cluster(const VerifyArgs& a, int dtype, float* out, cudaStream_t stream) {
+    if (dtype == 0) return launch_probs_t<__nv_bfloat16, 8>(a, out, stream);
+    if (dtype == 1) return launch_probs_t<float, 8>(a, out, stream);
+    return kBadDtype;
+}
 
 int launch_verify(const VerifyArgs& a, int dtype, cudaStream_t stream) {
     if (dtype == 0) return launch_verify_t<__nv_bfloat16, 8>(a, stream);

@@ -64,21 +64,28 @@ def topk_ids(logits: torch.Tensor, k: int, out: torch.Tensor = None) -> torch.Te
 
 def build_serial_tables(lm_head_w, norm_w, write_w, pv_w, codebook, chunk: int = 8192):
     """(TG [V, R] bf16, TSV [V, 2R] bf16) with TG[v] = bf16(LmHead[v] * norm_w) @ W_last and
-    TSV[v] = [G_p; A] @ bf16(sqrt(C) * Codebook[v]) (kernels/dspine.py:327-351)."""
+    TSV[v] = [G_p; A] @ bf16(sqrt(C) * Codebook[v]) (kernels/dspine.py:327-351): the per-token
+    tables the serial refinement gathers by id.  Offline (once per weight load): the normed
+    head rows and the scaled codebook rows are rounded to bf16 block by block and multiplied
+    by the two fixed factors with library GEMMs written straight into the tables."""
     (v, h) = lm_head_w.shape
     r = write_w.shape[1]
     c = codebook.shape[1]
     if (codebook.shape[0] != v or tuple(write_w.shape) != (h, r) or tuple(pv_w.shape) != (2 * r, c)
             or norm_w.shape != (h,)):
         raise ValueError("build_serial_tables: shape contract violated")
-    tg = torch.empty((v, r), device=lm_head_w.device, dtype=torch.bfloat16)
-    tsv = torch.empty((v, 2 * r), device=lm_head_w.device, dtype=torch.bfloat16)
-    nwf, wb, scale = norm_w.float(), write_w.to(torch.bfloat16), float(c) ** 0.5
-    for s in range(0, v, chunk):
-        e = min(s + chunk, v)
-        tg[s:e] = torch.matmul((lm_head_w[s:e].float() * nwf).to(torch.bfloat16), wb)
-        tsv[s:e] = torch.nn.functional.linear((scale * codebook[s:e].float()).to(torch.bfloat16),
-                                              pv_w)
+    device = lm_head_w.device
+    tg = torch.empty((v, r), device=device, dtype=torch.bfloat16)
+    tsv = torch.empty((v, 2 * r), device=device, dtype=torch.bfloat16)
+    w_last = write_w.to(torch.bfloat16)   # [H, R]
+    gate_value = pv_w.t()                 # [C, 2R]: x @ pv_w.T
+    norm = norm_w.float()
+    scale = float(c) ** 0.5
+    step = max(1, int(chunk))
+    for lo in range(0, v, step):
+        hi = min(lo + step, v)
+        torch.mm((lm_head_w[lo:hi].float() * norm).to(torch.bfloat16), w_last, out=tg[lo:hi])
+        torch.mm((codebook[lo:hi].float() * scale).to(torch.bfloat16), gate_value, out=tsv[lo:hi])
     return (tg, tsv)
 
 

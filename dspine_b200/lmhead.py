@@ -125,19 +125,47 @@ def merge_shards(values, ids, lse, k, *, pad_id, sort_ids=False, out=None):
     return out
 
 
-def merge_topk(values, ids, k):
-    """sampling/tp_head.py:9-14: global top-k, lower ids winning ties (torch, any device)."""
-    order = torch.argsort(ids, dim=-1, stable=True)
-    values, ids = values.gather(-1, order), ids.gather(-1, order)
-    order = torch.argsort(values, dim=-1, descending=True, stable=True)[..., :k]
+def _ordered_keys(values):
+    """int32 keys ordered as torch's sort orders the values: NaN above every number, -0 equal
+    to +0 (values of any float dtype, compared exactly in float32)."""
+    v = values.float() + 0.0                     # -0 + 0 = +0
+    bits = v.view(torch.int32)
+    keys = torch.where(bits < 0, bits ^ 0x7FFFFFFF, bits)
+    return torch.where(torch.isnan(v), torch.full_like(keys, 0x7FFFFFFF), keys)
+
+
+def merge_topk(values, ids, k, *, max_pairs: int = 1 << 24):
+    """The global top-k of candidate rows, lower token ids winning value ties
+    (sampling/tp_head.py:9-14), on any device: candidate j of a row outranks candidate i when
+    its value is larger, or equal with a smaller id, or equal in both and earlier in the row;
+    the first min(k, width) candidates in that order are returned (values, ids).  The ranks come
+    from pairwise comparisons, rows taken in blocks of at most ``max_pairs`` comparisons."""
+    width = values.shape[-1]
+    lead = values.shape[:-1]
+    keys = _ordered_keys(values.reshape(-1, width))
+    flat_ids = ids.reshape(-1, width)
+    n = keys.shape[0]
+    kk = min(int(k), width)
+    order = torch.empty((n, kk + 1), dtype=torch.int64, device=values.device)
+    position = torch.arange(width, device=values.device)
+    earlier = position[None, :] < position[:, None]          # [i, j]: j before i
+    step = max(1, max_pairs // max(1, width * width))
+    for lo in range(0, n, step):
+        hi = min(lo + step, n)
+        ki, kj = keys[lo:hi, :, None], keys[lo:hi, None, :]
+        ii, ij = flat_ids[lo:hi, :, None], flat_ids[lo:hi, None, :]
+        beats = (kj > ki) | ((kj == ki) & ((ij < ii) | ((ij == ii) & earlier)))
+        rank = beats.sum(-1).clamp_(max=kk)                   # [rows, width], distinct below kk
+        order[lo:hi].scatter_(1, rank, position.expand(hi - lo, width))
+    order = order[:, :kk].reshape(*lead, kk)
     return values.gather(-1, order), ids.gather(-1, order)
 
 
 class TPHead:
     """Vocabulary-sharded head (sampling/tp_head.py:17-103): each rank keeps its weight shard;
-    only candidates cross ranks.  ``tp_group`` provides ``world_size`` and
-    ``all_gather(tensor, dim)`` (SGLang's GroupCoordinator; `TorchGroup` adapts a
-    torch.distributed process group)."""
+    only candidates cross ranks.  ``tp_group`` provides ``world_size``,
+    ``all_gather(tensor, dim)`` and ``all_reduce(tensor)`` (SGLang's GroupCoordinator;
+    `TorchGroup` adapts a torch.distributed process group)."""
 
     def __init__(self, weight, start, end, global_vocab_size, tp_group):
         self.weight = weight
@@ -145,33 +173,64 @@ class TPHead:
         self.global_vocab_size = int(global_vocab_size)
         self.group = tp_group
         self.world_size = int(tp_group.world_size)
-        if (weight.ndim != 2 or weight.dtype != torch.bfloat16 or weight.stride(1) != 1
-                or not 0 <= self.start <= self.end <= self.global_vocab_size
-                or self.end - self.start > weight.shape[0] or weight.shape[0] == 0):
+        valid_shard = (weight.ndim == 2 and weight.dtype == torch.bfloat16
+                       and weight.stride(1) == 1 and weight.shape[0] > 0
+                       and 0 <= self.start <= self.end <= self.global_vocab_size
+                       and self.end - self.start <= weight.shape[0])
+        if not valid_shard:
             raise ValueError("Invalid DSpine vocabulary head shard")
-        geometry = torch.tensor([[self.start, self.end, weight.shape[0]]], device=weight.device,
-                                dtype=torch.int64)
-        geometry = self.group.all_gather(geometry, dim=0).cpu().tolist()
-        cursor = 0
-        for begin, finish, allocated in geometry:
-            if begin != cursor or finish < begin or finish - begin > allocated:
-                raise ValueError("DSpine head shards must partition the original vocabulary")
-            cursor = finish
-        if cursor != self.global_vocab_size:
+        mine = torch.tensor([[self.start, self.end, weight.shape[0]]], device=weight.device,
+                            dtype=torch.int64)
+        table = self.group.all_gather(mine, dim=0).cpu()      # [world, 3], rank order
+        begins, ends, allocated = table[:, 0], table[:, 1], table[:, 2]
+        follows = torch.cat([begins.new_zeros(1), ends[:-1]])  # each shard starts where the last ended
+        if not (torch.equal(begins, follows) and bool((ends >= begins).all())
+                and bool((ends - begins <= allocated).all())):
+            raise ValueError("DSpine head shards must partition the original vocabulary")
+        if int(ends[-1]) != self.global_vocab_size:
             raise ValueError("DSpine head shards do not cover the original vocabulary")
-        self.geometry = tuple(tuple(row) for row in geometry)
+        self.geometry = tuple(tuple(int(x) for x in row) for row in table.tolist())
+        self.max_rows = int(allocated.max())
 
     @property
     def num_local(self):
         return self.end - self.start
 
     def global_topk(self, local_values, local_ids, k):
-        """Merge equally padded local candidate blocks (two all-gathers, as the reference)."""
+        """Merge equally padded local candidate blocks: the values (as their float32 bits, exact
+        for bf16 / fp16 / fp32) and the ids cross ranks in ONE all-gather of an int64 block,
+        then `merge_topk` on the rank-ordered concatenation (sampling/tp_head.py:76-82)."""
         if local_values.shape != local_ids.shape:
             raise ValueError("DSpine local candidate values and IDs must match")
-        values = self.group.all_gather(local_values, dim=-1)
-        ids = self.group.all_gather(local_ids, dim=-1)
-        return merge_topk(values, ids, k)
+        bits = local_values.float().view(torch.int32).to(torch.int64)
+        block = torch.stack((bits, local_ids.to(torch.int64)))
+        gathered = self.group.all_gather(block, dim=-1)
+        values = gathered[0].to(torch.int32).view(torch.float32).to(local_values.dtype)
+        return merge_topk(values, gathered[1].to(local_ids.dtype), k)
+
+    def gather_vocab_rows(self, local):
+        """The full-vocabulary table from every rank's rows (sampling/tp_head.py:58-71): shards
+        padded to the largest allocation, all-gathered, each rank's real rows placed at its
+        vocabulary range."""
+        if local.shape[0] != self.num_local:
+            raise ValueError("DSpine local vocabulary table has the wrong row count")
+        padded = local.new_zeros((self.max_rows, *local.shape[1:]))
+        padded[: self.num_local] = local
+        blocks = self.group.all_gather(padded, dim=0).view(self.world_size, self.max_rows,
+                                                           *local.shape[1:])
+        full = local.new_empty((self.global_vocab_size, *local.shape[1:]))
+        for rank, (begin, end, _) in enumerate(self.geometry):
+            full[begin:end] = blocks[rank, : end - begin]
+        return full
+
+    def selected_rows(self, ids):
+        """The bf16 head rows of global ids (sampling/tp_head.py:84-89): the owner rank
+        contributes each row, the others zeros, and one all-reduce sums them."""
+        local = ids - self.start
+        owner = (local >= 0) & (ids < self.end)
+        rows = self.weight[local.clamp(0, self.weight.shape[0] - 1)]
+        rows = rows * owner[..., None].to(rows.dtype)
+        return self.group.all_reduce(rows.contiguous())
 
     def rescore(self, ids, hidden):
         """The original BF16 head dot of global candidate ids (sampling/tp_head.py:91-103): the
@@ -228,11 +287,18 @@ class TorchGroup:
         return tensor
 
     def all_gather(self, tensor, dim=0):
+        """Rank blocks concatenated along ``dim`` (one output allocation; for dim != 0 the
+        rank-major result is moved into place with one copy)."""
         tensor = tensor.contiguous()
-        out = torch.empty((self.world_size * tensor.shape[0], *tensor.shape[1:]),
-                          dtype=tensor.dtype, device=tensor.device)
-        self._dist.all_gather_into_tensor(out, tensor, group=self.group)
-        if dim == 0 or tensor.dim() == 1:
+        out = torch.empty((self.world_size, *tensor.shape), dtype=tensor.dtype,
+                          device=tensor.device)
+        self._dist.all_gather_into_tensor(out.view(-1), tensor.view(-1), group=self.group)
+        if tensor.dim() == 0:
             return out
-        parts = out.view(self.world_size, *tensor.shape)
-        return torch.cat(list(parts.unbind(0)), dim=dim)
+        d = dim % tensor.dim()
+        if d == 0:
+            return out.view(self.world_size * tensor.shape[0], *tensor.shape[1:])
+        moved = out.movedim(0, d)                              # [..., world, n_d, ...]
+        shape = list(tensor.shape)
+        shape[d] *= self.world_size
+        return moved.reshape(shape)

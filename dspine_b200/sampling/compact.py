@@ -1,41 +1,99 @@
 """Request-wise logit adjustments (sampling/compact.py of the reference) on the GPU.
 
-`adjust_logits(logits, info, row_to_request)` keeps the reference's signature and order of
-transforms; the additive penalties, scaling penalties, grammar bitmask (xgrammar layout:
-int32 words, bit set = allowed) and logit bias run as one dsv_adjust_logits pass.  Prepared
-penalizers of SGLang's orchestrator are applied in their own order through the same kernel.
+`adjust_logits(logits, info, row_to_request)` keeps the reference's signature and its order of
+transforms (compact.py:14-79): the batch's additive penalties, its scaling penalties, each
+prepared penalizer of SGLang's orchestrator in the orchestrator's order, the grammar mask, the
+logit bias.  The work is a short list of in-place dsv_adjust_logits passes: the additive and
+scaling penalties share one pass, every penalizer is one pass (their order matters, so they
+are not merged), and the grammar mask shares the bias pass.  Each step rounds to the logit
+dtype exactly as the torch op it replaces.
+
+Grammar masks: an int32 token bitmask (xgrammar's layout, bit set = allowed) or a bool mask
+(True = disallowed, the outlines layout) is applied inside the pass; a grammar with any other
+mask layout is applied by its own ``apply_vocab_mask``, as the reference always does.
+
+`around_verify_logits_adjustments` is the plugin's AROUND hook for SGLang's verify-logits
+adjustments (compact.py:82-116).
 """
 
 import torch
 
 from .. import _lib
 
+_DTYPES = {torch.bfloat16: 0, torch.float32: 1}
+
 
 def can_keep_compact(info):
-    return (info is not None and not getattr(info, "has_custom_logit_processor", False)
-            and getattr(info, "sampling_mask_batch_indices", None) is None)
+    """Packed verification rows stay packed unless a custom logit processor or a sampling
+    mask needs SGLang's full-batch layout (compact.py:4-10)."""
+    if info is None or getattr(info, "has_custom_logit_processor", False):
+        return False
+    return getattr(info, "sampling_mask_batch_indices", None) is None
 
 
-def _launch(logits, mapping, rpr, additive=None, scaling=None, mask=None, bias=None):
-    rows2d = logits.reshape(-1, logits.shape[-1])
-    if rows2d.stride(-1) != 1:
-        raise ValueError("logit rows must be contiguous")
-    V = rows2d.shape[-1]
-    dtype = {torch.bfloat16: 0, torch.float32: 1}.get(rows2d.dtype)
-    if dtype is None:
-        raise ValueError("logits must be bf16 or fp32")
+class _Pass:
+    """One dsv_adjust_logits pass over the rows (any of its four inputs may be absent)."""
 
-    def f32(t):
-        return None if t is None else t.to(device=logits.device, dtype=torch.float32).contiguous()
-    m = None
-    words = 0
-    if mask is not None:
-        m = mask.to(device=logits.device, dtype=torch.int32).contiguous()
-        words = m.shape[-1]
-    add, sc, bi = f32(additive), f32(scaling), f32(bias)
-    _lib.call("dsv_adjust_logits", rows2d.data_ptr(), dtype, rows2d.shape[0], V, rows2d.stride(0),
-              _lib.ptr(mapping), int(rpr), _lib.ptr(add), _lib.ptr(sc), _lib.ptr(m), words,
-              _lib.ptr(bi), torch.cuda.current_stream(logits.device).cuda_stream)
+    def __init__(self, logits, row_to_request):
+        rows = logits.reshape(-1, logits.shape[-1])
+        if rows.stride(-1) != 1:
+            raise ValueError("logit rows must be contiguous")
+        if rows.dtype not in _DTYPES:
+            raise ValueError("logits must be bf16 or fp32")
+        self.rows = rows
+        self.device = logits.device
+        if row_to_request is not None:
+            self.mapping = row_to_request.to(device=self.device, dtype=torch.int64).contiguous()
+            self.per_request = 1
+        else:  # full blocks [B, T, V]: request of row r is r // T
+            self.mapping = None
+            self.per_request = logits.shape[1] if logits.dim() == 3 else 1
+
+    def _f32(self, t):
+        return None if t is None else t.to(device=self.device, dtype=torch.float32).contiguous()
+
+    def __call__(self, additive=None, scaling=None, bitmask=None, bias=None):
+        add, sc, bi = self._f32(additive), self._f32(scaling), self._f32(bias)
+        words = 0
+        if bitmask is not None:
+            bitmask = bitmask.to(device=self.device, dtype=torch.int32).contiguous()
+            words = bitmask.shape[-1]
+        rows = self.rows
+        with torch.cuda.device(self.device):
+            _lib.call("dsv_adjust_logits", rows.data_ptr(), _DTYPES[rows.dtype], rows.shape[0],
+                      rows.shape[1], rows.stride(0), _lib.ptr(self.mapping), self.per_request,
+                      _lib.ptr(add), _lib.ptr(sc), _lib.ptr(bitmask), words, _lib.ptr(bi),
+                      torch.cuda.current_stream(self.device).cuda_stream)
+
+
+def _bool_mask_as_bitmask(mask, vocab):
+    """A bool [B, V] mask (True = disallowed) as int32 allow-words (bit set = allowed)."""
+    allowed = ~mask.to(torch.bool)
+    words = (vocab + 31) // 32
+    padded = torch.zeros((allowed.shape[0], words * 32), dtype=torch.int64, device=mask.device)
+    padded[:, :vocab] = allowed[:, :vocab].to(torch.int64)
+    weights = torch.bitwise_left_shift(torch.ones(32, dtype=torch.int64, device=mask.device),
+                                       torch.arange(32, device=mask.device))
+    packed = (padded.view(allowed.shape[0], words, 32) * weights).sum(-1)
+    return packed.to(torch.int64).where(packed < 2**31, packed - 2**32).to(torch.int32)
+
+
+def _penalizer_stages(info, vocab, device):
+    """(kind, tensor) for each prepared penalizer, in the orchestrator's order: a
+    multiplicative penalizer scales, any other adds the bias its apply() writes into a zeroed
+    [B, V] buffer (the orchestrator's own convention)."""
+    orchestrator = getattr(info, "penalizer_orchestrator", None)
+    if orchestrator is None or not orchestrator.is_required:
+        return
+    for penalizer in orchestrator.penalizers.values():
+        if not penalizer.is_prepared():
+            continue
+        if penalizer.is_multiplicative:
+            yield "scale", penalizer.get_scaling_penalties()
+        else:
+            buffer = torch.zeros((len(info), vocab), device=device, dtype=torch.float32)
+            penalizer.apply(buffer)
+            yield "add", buffer
 
 
 def adjust_logits(logits, info, row_to_request):
@@ -45,34 +103,61 @@ def adjust_logits(logits, info, row_to_request):
         return
     if logits.device.type != "cuda":
         raise ValueError("dspine_b200 adjusts logits on CUDA tensors only")
-    if row_to_request is not None:
-        mapping = row_to_request.to(device=logits.device, dtype=torch.int64).contiguous()
-        rpr = 1
-    else:
-        mapping = None
-        rpr = logits.shape[1] if logits.dim() == 3 else 1
-    linear = getattr(info, "acc_additive_penalties", None)
-    if linear is None:
-        linear = getattr(info, "acc_linear_penalties", None)
+    launch = _Pass(logits, row_to_request)
+    vocab = logits.shape[-1]
+    additive = getattr(info, "acc_additive_penalties", None)
+    if additive is None:  # older DFlash callers name the same buffer "linear"
+        additive = getattr(info, "acc_linear_penalties", None)
     scaling = getattr(info, "acc_scaling_penalties", None)
-    # the native buffers first (one pass), then the orchestrator's penalizers in order, then
-    # the grammar mask and the bias (one pass) -- the reference's order
-    if linear is not None or scaling is not None:
-        _launch(logits, mapping, rpr, additive=linear, scaling=scaling)
-    penalizer = getattr(info, "penalizer_orchestrator", None)
-    if penalizer is not None and penalizer.is_required:
-        for penalty in penalizer.penalizers.values():
-            if not penalty.is_prepared():
-                continue
-            if penalty.is_multiplicative:
-                _launch(logits, mapping, rpr, scaling=penalty.get_scaling_penalties())
-            else:
-                bias = torch.zeros((len(info), logits.shape[-1]), device=logits.device,
-                                   dtype=torch.float32)
-                penalty.apply(bias)
-                _launch(logits, mapping, rpr, additive=bias)
+    if additive is not None or scaling is not None:
+        launch(additive=additive, scaling=scaling)
+    for kind, tensor in _penalizer_stages(info, vocab, logits.device):
+        launch(**({"scaling": tensor} if kind == "scale" else {"additive": tensor}))
     grammar = getattr(info, "grammar_mask", None)
-    mask = None if grammar is None else grammar.vocab_mask
     bias = getattr(info, "logit_bias", None)
-    if mask is not None or bias is not None:
-        _launch(logits, mapping, rpr, mask=mask, bias=bias)
+    bitmask = None
+    if grammar is not None:
+        mask = grammar.vocab_mask
+        if mask.dtype == torch.int32:
+            bitmask = mask
+        elif mask.dtype == torch.bool:
+            bitmask = _bool_mask_as_bitmask(mask.to(logits.device), vocab)
+        else:
+            # an unknown layout: the grammar applies its own mask, rows mapped as the reference
+            mask = mask.to(device=logits.device)
+            rows_mask = (mask.index_select(0, launch.mapping) if launch.mapping is not None
+                         else mask.repeat_interleave(launch.per_request, dim=0))
+            grammar.grammar.apply_vocab_mask(logits=logits.reshape(-1, vocab), vocab_mask=rows_mask)
+    if bitmask is not None or bias is not None:
+        launch(bitmask=bitmask, bias=bias)
+
+
+def around_verify_logits_adjustments(original, *, next_token_logits, sampling_info,
+                                     draft_token_num):
+    """The AROUND hook of SGLang's apply_dflash_verify_logits_adjustments (compact.py:82-116):
+    packed rounds adjust their packed rows through the controller's row mapping; full rounds
+    adjust [bs, draft_token_num, V] blocks; without a DSpine worker the original runs."""
+    from ..runtime import worker as module
+    from ..verification.caps import active_controller
+
+    controller = active_controller()
+    if controller is None and module._active_worker is None:
+        return original(next_token_logits=next_token_logits, sampling_info=sampling_info,
+                        draft_token_num=draft_token_num)
+    if controller is not None and getattr(controller, "compact_round", False):
+        if next_token_logits is not controller.compact_logits:
+            raise RuntimeError("Packed verification logits do not belong to this round")
+        return adjust_logits(next_token_logits, sampling_info, controller.row_to_request)
+    if sampling_info is None:
+        return
+    if next_token_logits.ndim != 2 or draft_token_num <= 0:
+        raise ValueError("Verification needs 2D logits and a positive draft width")
+    bs = len(sampling_info)
+    if next_token_logits.shape[0] != bs * draft_token_num:
+        raise ValueError("Verification logits do not match the request/block layout")
+    if getattr(sampling_info, "has_custom_logit_processor", False):
+        from sglang.srt.layers.sampler import apply_custom_logit_processor  # SGLang's own
+
+        apply_custom_logit_processor(next_token_logits, sampling_info,
+                                     num_tokens_in_batch=draft_token_num)
+    return adjust_logits(next_token_logits.view(bs, draft_token_num, -1), sampling_info, None)

@@ -45,3 +45,45 @@ def sample_capped_chain_from_probs(*, candidates, target_probs, draft_probs, ver
               uniform_final.data_ptr(), prefix_lens.data_ptr(), *(o.data_ptr() for o in outputs),
               torch.cuda.current_stream(candidates.device).cuda_stream)
     return outputs
+
+
+def accept_sampled_prefix(controller, *, candidates, next_token_logits, sampling_info,
+                          prefix_lens, bs, verify_lens, row_offsets=None, row_to_request=None):
+    """Verify one shortened target call against this round's sampled chain q
+    (sampling/rejection.py:156-239): the worker's TargetDistribution when it has one, else the
+    dense target of the full 16-row envelope with the sparse q through dsv_accept_sparse (the
+    reference scatters q into a dense buffer for sample_capped_chain_from_probs; a sparse q
+    gives the same chain without that buffer)."""
+    from ..runtime.worker import build_dspine_target_probs
+    from .random import verification_uniforms
+    from .sparse.accept import accept_sparse
+    from .target import _sampling_backend
+
+    worker = controller.worker
+    if getattr(worker, "target_distribution", None) is not None:
+        result = worker.target_distribution.sample_prefix(
+            candidates=candidates, next_token_logits=next_token_logits,
+            sampling_info=sampling_info, prefix_lens=prefix_lens, bs=bs,
+            verify_lens=verify_lens, row_offsets=row_offsets, row_to_request=row_to_request)
+        if result is not None:
+            controller.sampled_executions += 1
+            return result
+    sampler = worker._dspine_sampler
+    if not sampler.round_sampled or sampler.round_bs != bs:
+        raise RuntimeError("Sampled caps require the current sampled proposal and q")
+    width = int(worker.block_size)
+    if width != 16 or candidates.shape != (bs, width):
+        raise ValueError("Sampled caps require full16 proposal storage")
+    if next_token_logits.shape[0] != bs * width:
+        raise ValueError("Target output must retain the full16 mapped row envelope")
+    target_probs = build_dspine_target_probs(
+        next_token_logits=next_token_logits, sampling_info=sampling_info, block_size=width,
+        bs=bs, sampling_backend=_sampling_backend(worker))
+    outputs = worker._next_accept_bonus_buffers(bs)
+    uniforms, final = verification_uniforms(bs, width, candidates.device, sampler.random)
+    accept_sparse(torch, candidates=candidates, dense_p=target_probs.reshape(bs * width, -1),
+                  packed=None, q_ids=sampler.candidate_out[:bs], q_values=sampler.q_out[:bs],
+                  verify_lens=verify_lens, uniforms=uniforms, uniform_final=final,
+                  prefix_lens=prefix_lens, outputs=outputs)
+    controller.sampled_executions += 1
+    return outputs

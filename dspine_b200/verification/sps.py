@@ -54,3 +54,65 @@ def sps_plan(raw, probabilities, depth, budget, boundaries=None):
 def allocate_verify_lens(raw, probabilities, depth, budget, boundaries=None):
     """Keep the highest-survival prefixes, including one root per request."""
     return sps_plan(raw, probabilities, depth, budget, boundaries)[0]
+
+
+class RaggedVerifyLayout:
+    """The device half of SGLang's RaggedVerifyLayout that the ragged verify path reads:
+    per-request verify lengths, their exclusive scan (qo_indptr_device [B+1]) and the token
+    budget.  When SGLang is importable, `device_plan` returns SGLang's own layout instead."""
+
+    def __init__(self, verify_lens, qo_indptr_device, graph_num_tokens, total_verify_tokens):
+        self.verify_lens = verify_lens
+        self.qo_indptr_device = qo_indptr_device
+        self.graph_num_tokens = int(graph_num_tokens)
+        self.total_verify_tokens = int(total_verify_tokens)
+
+    @classmethod
+    def _assemble_device(cls, *, verify_lens, graph_num_tokens, total_verify_tokens,
+                         qo_indptr=None):
+        if qo_indptr is None:
+            qo_indptr = torch.zeros(verify_lens.numel() + 1, device=verify_lens.device,
+                                    dtype=torch.int64)
+            qo_indptr[1:] = verify_lens.to(torch.int64).cumsum(0)
+        return cls(verify_lens, qo_indptr, graph_num_tokens, total_verify_tokens)
+
+
+def _layout_class():
+    try:
+        from sglang.srt.speculative.ragged_verify import RaggedVerifyLayout as sglang_layout
+    except ImportError:
+        return None
+    return sglang_layout
+
+
+def device_plan(raw, probabilities, depth, budget, cfg, graph_tokens=None, boundaries=None, *,
+                tp=None):
+    """(layout, index) of one SPS round (verification/sps.py:61-99): the verify lengths of
+    allocate_verify_lens, their layout and index[qo[b] + t] = b * 16 + t, from one
+    dsv_sps_plan launch.  Under TP the lengths are synchronised from the leader and the index
+    is rebuilt on the device from the synchronised lengths (no host read)."""
+    if cfg.min_verify_len != 1 or cfg.survival_eps != 0.0:
+        raise ValueError("DSpine SPS requires one root per request and no survival cutoff")
+    bs, gamma = raw.shape
+    full = gamma + 1
+    if graph_tokens is None:
+        graph_tokens = budget
+    if graph_tokens != budget:
+        raise ValueError("SPS graph tier must equal the verified token budget")
+    lens, qo, index = sps_plan(raw, probabilities, depth, budget, boundaries)
+    if tp is not None:
+        tp.sync_tensor(lens)
+        qo = torch.zeros_like(qo)
+        qo[1:] = lens.to(torch.int64).cumsum(0)
+        token = torch.arange(budget, device=raw.device)
+        row = torch.searchsorted(qo[1:], token, right=True)
+        index = row * full + token - qo[row]
+    sglang_layout = _layout_class()
+    if sglang_layout is not None:
+        layout = sglang_layout._assemble_device(verify_lens=lens, graph_num_tokens=graph_tokens,
+                                                total_verify_tokens=budget)
+    else:
+        layout = RaggedVerifyLayout._assemble_device(verify_lens=lens,
+                                                     graph_num_tokens=graph_tokens,
+                                                     total_verify_tokens=budget, qo_indptr=qo)
+    return layout, index

@@ -32,13 +32,33 @@ class Workspace:
         self.batch = int(batch)
         self.nbytes = int(size.value)
         self.buf = torch.empty(self.nbytes, dtype=torch.uint8, device=device)
-        _lib.call("dsv_workspace_init", self.buf.data_ptr(), self.nbytes, _stream(device))
+        self.layout_batch = None  # the batch size whose layout the zeroed state follows
+        self.zero()
+
+    def zero(self):
+        """Zero the whole workspace on the current stream (dsv_workspace_init)."""
+        _lib.call("dsv_workspace_init", self.buf.data_ptr(), self.nbytes, _stream(self.buf.device))
+
+    def prepare(self, batch: int):
+        """A launch leaves the counters of its own batch's layout zeroed; another batch size
+        lays them out elsewhere, so the workspace is zeroed again when the size changes."""
+        if self.layout_batch is not None and self.layout_batch != int(batch):
+            self.zero()
+        self.layout_batch = int(batch)
+
+    # error bits after which the counters and flags of the workspace may not be zero: a bulk
+    # copy that timed out (bit 0), a layout check (5), a chain task or a split half that gave up
+    # waiting (6, 7); the workspace is zeroed again before it is reused
+    RESET_BITS = 0x1 | 0x20 | 0x40 | 0x80
 
     def error_word(self) -> int:
-        """Device error bits (synchronizes the current stream); cleared after reading."""
+        """Device error bits (synchronizes the current stream); cleared after reading.  After an
+        internal failure (RESET_BITS) the whole workspace is zeroed again."""
         err = ctypes.c_uint32()
         _lib.call("dsv_workspace_error", self.buf.data_ptr(), ctypes.byref(err),
                   _stream(self.buf.device))
+        if err.value & self.RESET_BITS:
+            self.zero()
         return int(err.value)
 
 
@@ -46,13 +66,15 @@ _workspaces: dict = {}
 
 
 def workspace_for(batch: int, device) -> Workspace:
+    """The device's workspace, grown to the largest batch asked for (a workspace sized for a
+    larger batch serves any smaller one); one per device."""
     device = torch.device(device)
-    key = (device.index, int(batch))
-    ws = _workspaces.get(key)
-    if ws is None:
-        # grow to the largest batch seen on this device
-        ws = Workspace(batch, device)
-        _workspaces[key] = ws
+    if device.index is None:
+        device = torch.device(device.type, torch.cuda.current_device())
+    ws = _workspaces.get(device.index)
+    if ws is None or ws.batch < int(batch):
+        ws = Workspace(max(int(batch), 1), device)
+        _workspaces[device.index] = ws
     return ws
 
 
@@ -93,6 +115,19 @@ def new_outputs(batch: int, device):
 def _check(cond, msg):
     if not cond:
         raise ValueError(msg)
+
+
+JOINT, SEQUENTIAL, TORCH = 0, 1, 2   # filter modes (dsv_filter_mode)
+
+
+def filter_mode(sampling_backend: str = "flashinfer", need_min_p: bool = False) -> int:
+    """The filter mode of a batch (runtime/worker.py:473-508): the pytorch backend's joint
+    filter plus min-p, or the flashinfer backend, sequential when the batch has min-p."""
+    if sampling_backend == "pytorch":
+        return TORCH
+    if sampling_backend == "flashinfer":
+        return SEQUENTIAL if need_min_p else JOINT
+    raise ValueError(f"DSPINE sampled verify: unsupported sampling backend {sampling_backend!r}")
 
 
 def _prepare(candidates, target_logits, target_rows, temperature, top_k, top_p, verify_lens,
@@ -166,7 +201,7 @@ def _prepare(candidates, target_logits, target_rows, temperature, top_k, top_p, 
 def verify_logits(*, candidates, target_logits, target_rows, temperature, top_k, top_p,
                   verify_lens, uniforms, uniform_final, prefix_lens, draft_logits=None,
                   draft_rows=None, outputs=None, slots=None, slot_rows=None, compact=None,
-                  workspace: Workspace | None = None):
+                  workspace: Workspace | None = None, min_p=None, mode: int = JOINT):
     """Verify a ragged batch of 16-token draft blocks directly from logits.
 
     candidates [B,16] int64 (anchor + 15 drafts); target_logits [R,V] bf16/fp32 rows;
@@ -175,7 +210,9 @@ def verify_logits(*, candidates, target_logits, target_rows, temperature, top_k,
     temperature [B] f32, top_k [B] i32 (>= V: off, <= 1: greedy), top_p [B] f32;
     verify_lens [B] i32 in [1,16]; uniforms [B,15] f32; uniform_final [B] f32;
     prefix_lens [B] i32.  Optional ``slots`` [*] i32 with ``slot_rows`` [B] i64 and a
-    ``compact`` CompactOutputs receive the packed accepted tokens and KV slots.
+    ``compact`` CompactOutputs receive the packed accepted tokens and KV slots.  ``min_p``
+    [B] f32 with ``mode`` (JOINT, SEQUENTIAL or TORCH, see `filter_mode`) selects the other
+    filter branches of runtime/worker.py:473-508.
     Returns (accept, commit, bonus, output, new_seq)."""
     B, dev, outputs, args, _keep = _prepare(
         candidates, target_logits, target_rows, temperature, top_k, top_p, verify_lens,
@@ -184,8 +221,16 @@ def verify_logits(*, candidates, target_logits, target_rows, temperature, top_k,
     if workspace is None:
         workspace = workspace_for(B, dev)
     _check(workspace.batch >= B, "workspace is too small for this batch")
-    _lib.call("dsv_verify_logits", *args, workspace.buf.data_ptr(), workspace.nbytes,
-              _stream(dev))
+    _check(mode in (JOINT, SEQUENTIAL, TORCH), "unknown filter mode")
+    workspace.prepare(B)
+    if min_p is not None:
+        _check(min_p.dtype == torch.float32 and tuple(min_p.shape) == (B,) and
+               min_p.is_contiguous() and min_p.device == dev, "min_p must be a contiguous f32 [B]")
+    # dsv_verify_logits_ex takes min_p and the mode after top_p (the 14th argument)
+    ex_args = args[:14] + (_lib.ptr(min_p), int(mode)) + args[14:]
+    with torch.cuda.device(dev):
+        _lib.call("dsv_verify_logits_ex", *ex_args, workspace.buf.data_ptr(), workspace.nbytes,
+                  _stream(dev))
     return outputs
 
 
@@ -210,5 +255,7 @@ def verify_logits_noalloc(*, candidates, target_logits, target_rows, temperature
     if device_error is not None:
         _check(device_error.device == dev and device_error.numel() >= 1 and
                device_error.element_size() == 4, "device_error must be a 4-byte CUDA tensor")
-    _lib.call("dsv_verify_logits_noalloc", *args, _lib.ptr(device_error), _stream(dev))
+    # the scratch address is looked up for the current device: make it the tensors' device
+    with torch.cuda.device(dev):
+        _lib.call("dsv_verify_logits_noalloc", *args, _lib.ptr(device_error), _stream(dev))
     return outputs

@@ -35,6 +35,17 @@ typedef enum {
 
 typedef enum { DSV_BF16 = 0, DSV_F32 = 1 } dsv_dtype;
 
+/* Filter modes of the target distribution (runtime/worker.py:473-508 filter_target_probs):
+ * JOINT  flashinfer backend, no min-p in the batch: rank < top_k and mass ranked ahead <= top_p,
+ *        both on the unfiltered p;
+ * SEQ    flashinfer backend with min-p in the batch (need_min_p_sampling): top-k, then top-p
+ *        against the top-k's own mass, then p >= min_p * max p;
+ * TORCH  pytorch backend (runtime/worker.py:52-67): the joint top-k / top-p set and
+ *        p >= min_p * max p.
+ * The min-p test is e >= min_p with e = exp2c((l - m) c); the floor is found by bisection over
+ * the 32-bit ordered keys (so the kept set stays a prefix of the rank order). */
+typedef enum { DSV_FILTER_JOINT = 0, DSV_FILTER_SEQ = 1, DSV_FILTER_TORCH = 2 } dsv_filter_mode;
+
 /* Library version string and a readable name for a status code. */
 const char* dsv_version(void);
 const char* dsv_status_string(int status);
@@ -45,7 +56,10 @@ uint64_t dsv_launch_count(void);
 /* ---- workspace ----------------------------------------------------------------------------
  * Scratch for dsv_verify_logits: task counters, per-row decisions, the ready list of requests
  * and (last 8.5 MB) the slots through which the two halves of a split row meet.  Zero it once
- * after allocation (dsv_workspace_init); every launch leaves it zeroed again.  A workspace
+ * after allocation (dsv_workspace_init); every launch that ends without an internal failure
+ * (error bits 0, 5-7 below) leaves it zeroed again for the next launch with the same batch
+ * size.  Its regions are laid out by the batch size, so a workspace sized for the largest
+ * batch serves smaller ones, but must be zeroed again when the batch size changes.  A workspace
  * without the split-row slots (the size for the batch minus that region) is accepted and then
  * no row is split. */
 int dsv_verify_workspace_size(int32_t batch, size_t* bytes);
@@ -58,7 +72,9 @@ int dsv_workspace_error(void* workspace, uint32_t* err, dsv_stream_t stream);
  * bits 3-4: a selection or a tie cut found no boundary (inconsistent input); bit 6: a chain
  * task waited past its time limit for its request; bit 7: the second half of a split row
  * waited past its time limit for the first.  Bits 0 and 5-7 are internal failures: the
- * outputs of that call are not valid. */
+ * outputs of that call are not valid, and the workspace's counters and split-row flags may be
+ * left set (a late first half can raise its flag after the second gave up), so zero the
+ * workspace again (dsv_workspace_init) before its next use. */
 
 /* ---- accept-compact outputs (optional argument of dsv_verify_logits) ----------------------
  * Restates SGLang's commit of accepted tokens and KV slots (wrapped by the reference at
@@ -98,6 +114,21 @@ int dsv_verify_logits(int32_t batch, int32_t vocab, int32_t dtype, const int64_t
                       int32_t* commit, int64_t* bonus, int64_t* output, int32_t* new_seq,
                       const dsv_compact_out* compact, void* workspace, size_t workspace_bytes,
                       dsv_stream_t stream);
+
+/* The same verification with min-p and a filter mode (dsv_filter_mode): min_p [B] (NULL, or
+ * 0 for a request, means no min-p floor; ignored in the JOINT mode).  Replaces the other
+ * branches of runtime/worker.py:473-508 filter_target_probs (min-p on: :485-491; the pytorch
+ * backend: :52-67, :480-484).  dsv_verify_logits is this call with min_p NULL and JOINT. */
+int dsv_verify_logits_ex(int32_t batch, int32_t vocab, int32_t dtype, const int64_t* candidates,
+                         const void* target_logits, const int64_t* target_row,
+                         int64_t target_rows, const void* draft_logits, const int64_t* draft_row,
+                         int64_t draft_rows, int64_t row_stride, const float* temperature,
+                         const int32_t* top_k, const float* top_p, const float* min_p,
+                         int32_t filter_mode, const int32_t* verify_lens, const float* uniforms,
+                         const float* uniform_final, const int32_t* prefix_lens, int32_t* accept,
+                         int32_t* commit, int64_t* bonus, int64_t* output, int32_t* new_seq,
+                         const dsv_compact_out* compact, void* workspace,
+                         size_t workspace_bytes, dsv_stream_t stream);
 
 /* ---- draft LM head fused with top-k and logsumexp --------------------------------------------
  * Replaces the materialised `torch.matmul(rows, W.T)` of runtime/worker.py:283-285 followed by
@@ -142,6 +173,18 @@ int dsv_target_probs(int64_t rows, int32_t vocab, int32_t rows_per_request, cons
                      const float* top_p, float* probs, void* workspace, size_t workspace_bytes,
                      dsv_stream_t stream);
 
+/* dsv_target_probs for bf16 or fp32 logits (dtype), with min-p and a filter mode (see
+ * dsv_verify_logits_ex): min_p per request or NULL.  bf16 rows with vocab <= 262000 and
+ * rows_per_request <= 16 take the streaming row kernel and need a dsv_verify_logits workspace
+ * for min(requests, 1024) requests; other rows (fp32, larger vocabularies, any
+ * rows_per_request) take one 8-CTA cluster per row and use only the first 64 bytes of a zeroed
+ * workspace (vocab up to about 220000 for fp32). */
+int dsv_target_probs_ex(int64_t rows, int32_t vocab, int32_t dtype, int32_t rows_per_request,
+                        const void* logits, int64_t row_stride, const float* temperature,
+                        const int32_t* top_k, const float* top_p, const float* min_p,
+                        int32_t filter_mode, float* probs, void* workspace,
+                        size_t workspace_bytes, dsv_stream_t stream);
+
 /* ---- capped chain rejection from dense probabilities ---------------------------------------
  * Replaces sampling/rejection.py:101-153 sample_capped_chain_from_probs (_sample_capped_chain,
  * :12-98): target_probs [B,16,V] and draft_probs [B,15,V] fp32, contiguous.  Draft s+1 is
@@ -182,6 +225,24 @@ int dsv_accept_sparse(int32_t batch, int32_t vocab, int32_t width, const int64_t
 int dsv_compress_probs(int64_t rows, int32_t vocab, int32_t capacity, const float* probs,
                        int32_t* ids, float* values, int32_t* lengths, int32_t* overflow,
                        dsv_stream_t stream);
+
+/* ---- small-support joint target ---------------------------------------------------------
+ * Replaces sampling/sparse/target.py:95-178 build_sparse_target (its CPU branch :156-178 is the
+ * definition; _pack_joint :23-53 and _overflow_dense :56-76 the reference's CUDA branch).  Row r
+ * of logits [rows, vocab] (dtype 0 bf16, 1 fp32; row_stride elements apart) belongs to request
+ * row_request[r] (or r / rows_per_request when row_request is NULL), with temperature, top_k
+ * (clamped to [1, capacity]) and top_p of that request.  With p = softmax(l / T): kept = p > 0,
+ * p >= the k-th largest p (every tie kept), and the mass of strictly larger p below top_p (or
+ * top_p >= 1).  count <= capacity: ids [r, :] the kept ids ascending (-1 padded), values their
+ * p renormalised over the kept set (0 padded), lengths[r] = count, overflow[r] = 0.  count >
+ * capacity: overflow[r] = 1, lengths[r] = capacity, packed entries -1 / 0, and dense [r, :] =
+ * p where p >= the k-th largest p, renormalised, else 0.  Dense rows of packed rows are not
+ * written.  Canonical arithmetic (exp2c, exact 2^-40 fixed-point masses); capacity <= 64. */
+int dsv_sparse_target(int64_t rows, int32_t vocab, int32_t dtype, const void* logits,
+                      int64_t row_stride, const int64_t* row_request, int32_t rows_per_request,
+                      const float* temperature, const int32_t* top_k, const float* top_p,
+                      int32_t capacity, int32_t* ids, float* values, int32_t* lengths,
+                      int32_t* overflow, float* dense, dsv_stream_t stream);
 
 /* ---- logit adjustments ---------------------------------------------------------------------
  * Replaces sampling/compact.py:14-79 adjust_logits (the native transforms of SGLang's

@@ -26,6 +26,7 @@ Fixture groups (reference function -> file):
             stable_local_topk; layers/fp8/gather.py rescore / select16      fp8.npz
   target_minp  tests/ref_utils.py:79-108 ref_target_row with min-p, both backends  target_minp.npz
   sparse_target  sampling/sparse/target.py:95-178 build_sparse_target (CPU branch)  sparse_target.npz
+  adjust    sampling/compact.py:14-79 adjust_logits (pure torch, CPU tensors)       adjust.npz
   fullv     configs 0, 1 and 4 at V = 151936: ref_target_row rows +
             sampling/rejection.py:101-153 sample_capped_chain_from_probs     fullv.npz
 """
@@ -613,6 +614,84 @@ def gen_sparse_target(torch):
     return out
 
 
+class _Info:
+    """SamplingBatchInfo stand-in for adjust_logits: the fields it reads and len()."""
+
+    def __init__(self, bs, **fields):
+        self._bs = bs
+        self.__dict__.update(fields)
+
+    def __len__(self):
+        return self._bs
+
+
+def _xgrammar_apply(logits, vocab_mask):
+    """xgrammar's token-bitmask semantics (SGLang's XGrammarGrammar.apply_vocab_mask): bit i of
+    row r's int32 words clear means token i is disallowed (-inf)."""
+    import torch
+
+    V = logits.shape[-1]
+    shifts = torch.arange(32, dtype=torch.int32)
+    bits = ((vocab_mask[:, :, None] >> shifts) & 1).reshape(vocab_mask.shape[0], -1)[:, :V]
+    logits.masked_fill_(bits == 0, float("-inf"))
+
+
+def gen_adjust(torch):
+    """sampling/compact.py:14-79 adjust_logits on CPU tensors (pure torch in the reference):
+    additive and scaling penalties, two penalizers of an orchestrator (multiplicative, then
+    additive), a grammar bitmask applied through the grammar's own apply_vocab_mask (xgrammar
+    semantics) and a logit bias; full [B, T, V] blocks and packed rows with row_to_request;
+    bf16 and fp32 logits."""
+    import types as _t
+
+    from sglang_dspine.sampling.compact import adjust_logits
+
+    out = {}
+    ci = 0
+    g = torch.Generator().manual_seed(31)
+    B, T, V = 4, 16, 517
+    words = (V + 31) // 32
+    for dtype in (torch.float32, torch.bfloat16):
+        for packed in (False, True):
+            add = torch.randn(B, V, generator=g)
+            scl = 1.0 + torch.rand(B, V, generator=g)
+            bias = torch.randn(B, V, generator=g) * 0.5
+            mask = torch.randint(-2**31, 2**31 - 1, (B, words), generator=g,
+                                 dtype=torch.int64).to(torch.int32)
+            pen_scale = 1.0 + 0.5 * torch.rand(B, V, generator=g)
+            pen_add = torch.randn(B, V, generator=g) * 0.25
+            mult = _t.SimpleNamespace(is_prepared=lambda: True, is_multiplicative=True,
+                                      get_scaling_penalties=lambda s=pen_scale: s)
+            addp = _t.SimpleNamespace(is_prepared=lambda: True, is_multiplicative=False,
+                                      apply=lambda b, a=pen_add: b.add_(a))
+            idle = _t.SimpleNamespace(is_prepared=lambda: False, is_multiplicative=False)
+            info = _Info(B, acc_additive_penalties=add, acc_scaling_penalties=scl,
+                         penalizer_orchestrator=_t.SimpleNamespace(
+                             is_required=True, penalizers={"m": mult, "i": idle, "a": addp}),
+                         grammar_mask=_t.SimpleNamespace(
+                             vocab_mask=mask, grammar=_t.SimpleNamespace(apply_vocab_mask=_xgrammar_apply)),
+                         logit_bias=bias)
+            if packed:
+                rows = 37
+                r2r = torch.randint(0, B, (rows,), generator=g)
+                x = (torch.randn(rows, V, generator=g) * 3).to(dtype)
+            else:
+                r2r = None
+                x = (torch.randn(B, T, V, generator=g) * 3).to(dtype)
+            y = x.clone()
+            adjust_logits(y, info, r2r)
+            for name, val in (("add", add), ("scl", scl), ("bias", bias), ("mask", mask),
+                              ("pen_scale", pen_scale), ("pen_add", pen_add)):
+                out[f"c{ci}_{name}"] = _np(val)
+            out[f"c{ci}_r2r"] = _np(r2r) if r2r is not None else np.zeros(0, np.int64)
+            out[f"c{ci}_x"] = _np(x.float())
+            out[f"c{ci}_y"] = _np(y.float())
+            out[f"c{ci}_bf16"] = np.array(dtype == torch.bfloat16)
+            ci += 1
+    out["n"] = np.array(ci)
+    return out
+
+
 def _fullv_case(torch, batch, ref_target_row, chain):
     """Reference outputs of one benchmark batch at the full vocabulary: target rows through
     ref_target_row (float64, then float32) or a one-hot at the lowest-index argmax for greedy
@@ -709,6 +788,7 @@ def main(ref_dir):
         "fullv": lambda: gen_fullv(torch),
         "target_minp": lambda: gen_target_minp(torch),
         "sparse_target": lambda: gen_sparse_target(torch),
+        "adjust": lambda: gen_adjust(torch),
     }
     only = set(sys.argv[2:])
     for name, fn in groups.items():

@@ -1,9 +1,14 @@
-"""Parity of the fused logit adjustments (dsv_adjust_logits) with the reference's torch ops
-(sampling/compact.py:14-79: add_, torch.where(l < 0, l * s, l / s), masked -inf, add_) on
-the same tensors, bf16 and fp32, packed (row_to_request) and full-block layouts: bitwise."""
+"""Parity of the logit adjustments (dsv_adjust_logits behind sampling/compact.py adjust_logits)
+with the reference's own adjust_logits (sampling/compact.py:14-79, pure torch), run on CPU
+tensors by tests/golden/make_golden.py (adjust.npz): additive and scaling penalties, an
+orchestrator with a multiplicative, an idle and an additive penalizer, a grammar bitmask
+applied through the grammar's own apply_vocab_mask (xgrammar semantics) and a logit bias; full
+[B, T, V] blocks and packed rows with row_to_request; bf16 and fp32 logits.  Bitwise."""
 
+from pathlib import Path
 from types import SimpleNamespace
 
+import numpy as np
 import pytest
 import torch
 
@@ -12,45 +17,73 @@ from dspine_b200.sampling.compact import adjust_logits
 pytestmark = pytest.mark.gpu
 
 DEV = "cuda"
+FIX = np.load(Path(__file__).resolve().parent / "golden" / "adjust.npz")
 
 
-def reference(logits, info, row_to_request):
-    def mapped(v):
-        v = v.to(logits.device)
-        return v.index_select(0, row_to_request) if row_to_request is not None else v[:, None, :]
-    logits.add_(mapped(info.acc_additive_penalties))
-    s = mapped(info.acc_scaling_penalties)
-    logits.copy_(torch.where(logits < 0, logits * s, logits / s))
-    words = info.grammar_mask.vocab_mask
-    V = logits.shape[-1]
-    bits = ((words[:, :, None] >> torch.arange(32, device=words.device)) & 1).reshape(words.shape[0], -1)[:, :V].bool()
-    allowed = bits.index_select(0, row_to_request) if row_to_request is not None else bits[:, None, :]
-    logits.masked_fill_(~allowed, float("-inf"))
-    logits.add_(mapped(info.logit_bias))
+class Info(SimpleNamespace):
+    def __len__(self):
+        return self.acc_additive_penalties.shape[0]
 
 
-@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
-@pytest.mark.parametrize("packed", [False, True])
-def test_adjust_logits_matches_torch(dtype, packed):
-    g = torch.Generator(device=DEV).manual_seed(7)
-    B, T, V = 6, 16, 4099
-    words = (V + 31) // 32
-    info = SimpleNamespace(
-        acc_additive_penalties=torch.randn(B, V, generator=g, device=DEV),
-        acc_scaling_penalties=1.0 + torch.rand(B, V, generator=g, device=DEV),
-        grammar_mask=SimpleNamespace(vocab_mask=torch.randint(-2**31, 2**31 - 1, (B, words), generator=g,
-                                                              device=DEV, dtype=torch.int64).to(torch.int32)),
-        logit_bias=torch.randn(B, V, generator=g, device=DEV) * 0.5)
-    if packed:
-        rows = 37
-        r2r = torch.randint(0, B, (rows,), generator=g, device=DEV)
-        x = (torch.randn(rows, V, generator=g, device=DEV) * 3).to(dtype)
-    else:
-        r2r = None
-        x = (torch.randn(B, T, V, generator=g, device=DEV) * 3).to(dtype)
-    want = x.clone()
-    reference(want, info, r2r)
-    adjust_logits(x, info, r2r)
+def case_info(ci, grammar_mask):
+    def t(name):
+        return torch.from_numpy(FIX[f"c{ci}_{name}"]).to(DEV)
+    pen_scale, pen_add = t("pen_scale"), t("pen_add")
+    mult = SimpleNamespace(is_prepared=lambda: True, is_multiplicative=True,
+                           get_scaling_penalties=lambda: pen_scale)
+    addp = SimpleNamespace(is_prepared=lambda: True, is_multiplicative=False,
+                           apply=lambda b: b.add_(pen_add))
+    idle = SimpleNamespace(is_prepared=lambda: False, is_multiplicative=False)
+    return Info(acc_additive_penalties=t("add"), acc_scaling_penalties=t("scl"),
+                penalizer_orchestrator=SimpleNamespace(is_required=True,
+                                                       penalizers={"m": mult, "i": idle, "a": addp}),
+                grammar_mask=grammar_mask(t("mask")), logit_bias=t("bias"))
+
+
+def run_case(ci, grammar_mask):
+    dtype = torch.bfloat16 if bool(FIX[f"c{ci}_bf16"]) else torch.float32
+    x = torch.from_numpy(FIX[f"c{ci}_x"]).to(dtype).to(DEV)
+    r2r = FIX[f"c{ci}_r2r"]
+    r2r = torch.from_numpy(r2r).to(DEV) if r2r.size else None
+    adjust_logits(x, case_info(ci, grammar_mask), r2r)
     torch.cuda.synchronize()
-    assert torch.equal(x.view(torch.int16 if dtype == torch.bfloat16 else torch.int32),
-                       want.view(torch.int16 if dtype == torch.bfloat16 else torch.int32))
+    want = torch.from_numpy(FIX[f"c{ci}_y"]).to(dtype)
+    return x.cpu(), want
+
+
+@pytest.mark.parametrize("ci", range(int(FIX["n"])))
+def test_adjust_logits_matches_reference(ci):
+    got, want = run_case(ci, lambda m: SimpleNamespace(vocab_mask=m))
+    assert torch.equal(got.float().view(torch.int32), want.float().view(torch.int32))
+
+
+@pytest.mark.parametrize("ci", range(int(FIX["n"])))
+def test_bool_grammar_mask_matches_the_bitmask(ci):
+    """A bool mask (True = disallowed) packs to the same allow-bits inside the pass."""
+    def as_bool(words):
+        V = FIX[f"c{ci}_x"].shape[-1]
+        shifts = torch.arange(32, device=DEV, dtype=torch.int32)
+        bits = ((words[:, :, None] >> shifts) & 1).reshape(words.shape[0], -1)[:, :V]
+        return SimpleNamespace(vocab_mask=bits == 0)
+    got, want = run_case(ci, as_bool)
+    assert torch.equal(got.float().view(torch.int32), want.float().view(torch.int32))
+
+
+def test_other_mask_layouts_use_the_grammars_own_apply():
+    """A mask of another layout goes to grammar.apply_vocab_mask with rows mapped as the
+    reference maps them (repeat_interleave over full blocks)."""
+    seen = {}
+
+    def apply(logits, vocab_mask):
+        seen["rows"] = vocab_mask.shape[0]
+        logits[vocab_mask > 0.5] = float("-inf")
+
+    B, T, V = 2, 16, 97
+    x = torch.zeros(B, T, V, device=DEV)
+    mask = torch.zeros(B, V, device=DEV, dtype=torch.float16)
+    mask[1, 5] = 1
+    info = SimpleNamespace(grammar_mask=SimpleNamespace(vocab_mask=mask,
+                                                        grammar=SimpleNamespace(apply_vocab_mask=apply)))
+    adjust_logits(x, info, None)
+    assert seen["rows"] == B * T
+    assert torch.isinf(x[1, :, 5]).all() and not torch.isinf(x[0]).any()

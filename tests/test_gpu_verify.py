@@ -239,3 +239,58 @@ def test_workspace_without_split_slots():
     for a_, b_ in zip(got_full, got_small):
         assert torch.equal(a_, b_)
     assert_same(got_full, oracle_verify(batch), "split slots")
+
+
+def _with_min_p(batch, seed, off_fraction=0.3):
+    g = torch.Generator().manual_seed(seed)
+    B = batch.B
+    mp = torch.rand(B, generator=g) * 0.2
+    mp[torch.rand(B, generator=g) < off_fraction] = 0.0
+    mp[0] = 0.05
+    return mp
+
+
+@pytest.mark.parametrize("mode", [verify.SEQUENTIAL, verify.TORCH, verify.JOINT])
+@pytest.mark.parametrize("dtype,V,quantize", [(torch.bfloat16, 4099, False),
+                                              (torch.float32, 2053, False),
+                                              (torch.bfloat16, 2053, True),
+                                              (torch.bfloat16, 151936, False)])
+def test_min_p_and_filter_modes_match_oracle(mode, dtype, V, quantize):
+    """min-p (the floor key of "p >= min_p * max p") and the three filter modes of
+    runtime/worker.py:473-508: the flashinfer backend with min-p in the batch (top-k, then top-p
+    against the top-k's mass, then min-p; rows with min_p 0 included), the pytorch backend
+    (joint top-k / top-p and min-p), and the joint mode, which ignores min-p."""
+    for seed in range(2 if V < 100000 else 1):
+        batch = random_batch(500 + seed * 13 + V + mode, 10, V, dtype, quantize=quantize)
+        mp = _with_min_p(batch, seed + V)
+        got = verify.verify_logits(**batch.kwargs(), min_p=mp.to(DEV), mode=mode)
+        torch.cuda.synchronize()
+        assert verify.workspace_for(batch.B, DEV).error_word() == 0
+        want = O.verify_logits(*(t.detach().cpu().numpy() for t in (
+            batch.candidates, batch.target_logits.float(), batch.target_rows,
+            batch.draft_logits.float(), batch.draft_rows, batch.temperature, batch.top_k,
+            batch.top_p, batch.verify_lens, batch.uniforms, batch.uniform_final,
+            batch.prefix_lens)), min_p=mp.numpy(), mode=mode)
+        assert_same(got, want, f"mode={mode} V={V} seed={seed}")
+
+
+def test_min_p_changes_the_kept_set():
+    """A min-p floor that cuts inside a top-k: the probability of a token below the floor is
+    zero, so a draft of it is rejected (q > 0, p = 0) under min-p and accepted without."""
+    V = 257
+    logits = torch.full((2, V), -10.0)
+    logits[:, 5] = 2.0
+    logits[:, 9] = 0.0     # p / p_max = e^-2 = 0.135: kept at min_p 0.1, cut at 0.2
+    logits[:, 11] = 1.0
+    batch = workloads.build([2], [1.0], [3], [1.0], V=V, dtype=torch.float32, seed=1)
+    batch.target_logits = logits[:2].clone()
+    batch.draft_logits = logits[:1].clone()
+    batch.candidates[0, 1] = 9
+    batch.uniforms.zero_()
+    batch = batch.to(DEV)
+    res = {}
+    for mp in (0.1, 0.2):
+        got = verify.verify_logits(**batch.kwargs(), min_p=torch.tensor([mp], device=DEV),
+                                   mode=verify.TORCH)
+        res[mp] = int(got[0][0])
+    assert res[0.1] == 1 and res[0.2] == 0
