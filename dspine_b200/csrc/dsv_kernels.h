@@ -35,10 +35,6 @@ static_assert(sizeof(WsHeader) <= 64, "workspace header");
 // for kept elements (key > kstar, or key == kstar and index <= tie_cut), else 0; greedy rows
 // are one-hot at argmax.
 constexpr uint32_t kDescGreedy = 1u;
-// verification rows whose kept set ends inside the ties of the boundary key: the cut (the
-// index of occurrence `pad` of kstar in index order) is found only where a draw or a drafted
-// token needs it; until then tie_cut holds kTiePending and flags >> 8 the key's count
-constexpr int32_t kTiePending = (int32_t)0x80000000;
 struct RowDesc {
     float m;
     float c;

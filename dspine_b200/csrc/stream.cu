@@ -555,14 +555,6 @@ __device__ __forceinline__ RowGeo row_geo(const VerifyArgs& a, const TaskInfo& t
     return g;
 }
 
-// geometry of row `row` of the target (kind 0) or draft (kind 1) logits
-__device__ __forceinline__ RowGeo row_geo_at(const VerifyArgs& a, int kind, long long row) {
-    TaskInfo ti;
-    ti.kind = kind;
-    ti.row = row;
-    return row_geo(a, ti);
-}
-
 // vector v of the row with the halves outside [0, V) set to -inf
 __device__ __forceinline__ uint4 row_vec(const RowGeo& g, int V, const uint4* src, int v, uint4 x) {
     if (v == 0 || v == g.nv - 1) {
@@ -1059,7 +1051,7 @@ __device__ void process_row(RSmem* sh, const VerifyArgs& a, const TaskInfo& ti) 
         const uint32_t hq = hbase >> 2;
         const uint32_t koff = ((hq << 16) | hq) - 0xBA80BA80u;
         if (hbase + 4u * 0x2000u > 0x10000u && tid == 0) atomicOr(&a.ws->err, 32u);  // layout
-        stream_row(sh, a, g, V, [&](const uint4& x, int) {
+        auto hist_fn = [&](const uint4& x, int) {
             const uint32_t xs[4] = {x.x, x.y, x.z, x.w};
             vmax2 = bf2_max(vmax2, bf2_max(bf2_max(xs[0], xs[1]), bf2_max(xs[2], xs[3])));
             // fine iff 2^-20 <= |v| < 2^12, i.e. 0x3580 <= |bits| <= 0x457F: bit 15 of
@@ -1113,7 +1105,8 @@ __device__ void process_row(RSmem* sh, const VerifyArgs& a, const TaskInfo& ti) 
                     }
                 }
             }
-        }, hb, he);
+        };
+        stream_row(sh, a, g, V, hist_fn, hb, he);
         {
             const uint32_t k0 = okey(vmax2 & 0xFFFFu), k1 = okey(vmax2 >> 16);
             tkey = k0 > k1 ? k0 : k1;
@@ -1137,7 +1130,7 @@ __device__ void process_row(RSmem* sh, const VerifyArgs& a, const TaskInfo& ti) 
         // ---- pass 1: max (greedy rows: and the first index of the max) ---------------
         tkey = 0;
         int tfirst = 0x7fffffff;
-        stream_row<true>(sh, a, g, V, [&](const uint4& x, int v) {
+        auto max_fn = [&](const uint4& x, int v) {
             uint32_t mx = bf2_max(bf2_max(x.x, x.y), bf2_max(x.z, x.w));
             const uint32_t k0 = okey(mx & 0xFFFFu), k1 = okey(mx >> 16);
             const uint32_t vk = k0 > k1 ? k0 : k1;
@@ -1158,7 +1151,8 @@ __device__ void process_row(RSmem* sh, const VerifyArgs& a, const TaskInfo& ti) 
                     tfirst = f;
                 }
             }
-        });
+        };
+        stream_row<true>(sh, a, g, V, max_fn);
         PROF_MARK(ti.cat, 0);
         const uint32_t wk = __reduce_max_sync(0xffffffffu, tkey);
         if (lane == 0) sh->red32[wid] = wk;
@@ -1377,16 +1371,22 @@ __device__ void process_row(RSmem* sh, const VerifyArgs& a, const TaskInfo& ti) 
             const uint32_t top = neg ? negtop : topkey;
             uint32_t gc = 0;
             unsigned long long gm = 0;
+            // branchless, two bins per packed exp: keys below klo (and empty bins) give
+            // fix = 0 or count 0, so every bin can be evaluated
+            const float2 nm2 = make_float2(-m, -m), c2 = make_float2(ti.c, ti.c);
 #pragma unroll 4
-            for (uint32_t jj = 0; jj < 32u; ++jj) {
-                const uint32_t i = b0 + ((jj + (uint32_t)tid) & 31u);
-                const uint32_t cnt = i < lim ? hp[i] : 0u;
-                if (cnt) {
-                    gc += cnt;
-                    const uint32_t key = top - i;
-                    if (key >= klo)
-                        gm += (unsigned long long)cnt * fix_of_y(y_clamped(bf(key_bits(key)), m, ti.c));
-                }
+            for (uint32_t jp = 0; jp < 16u; ++jp) {
+                const uint32_t i0 = b0 + ((2u * jp + 2u * (uint32_t)tid) & 31u);
+                // (scalar loads: the negative part's base, hist + npos, may be odd)
+                const uint2 cc = make_uint2(i0 < lim ? hp[i0] : 0u, i0 + 1u < lim ? hp[i0 + 1u] : 0u);
+                const uint32_t w = key_bits(top - i0) | (key_bits(top - i0 - 1u) << 16);
+                const Pair pr = exp_pair(w, nm2, c2);
+                const unsigned long long F0 =
+                    (unsigned long long)((long long)(pr.h0 - 0x4B000000u) * 8388608 + (int32_t)(pr.l0 - 0x4B400000u));
+                const unsigned long long F1 =
+                    (unsigned long long)((long long)(pr.h1 - 0x4B000000u) * 8388608 + (int32_t)(pr.l1 - 0x4B400000u));
+                gc += cc.x + cc.y;
+                gm += (unsigned long long)cc.x * F0 + (unsigned long long)cc.y * F1;
             }
             sh->gcnt[gi] = gc;
             sh->gmass[gi] = gm;
@@ -1524,16 +1524,6 @@ __device__ void process_row(RSmem* sh, const VerifyArgs& a, const TaskInfo& ti) 
         return;
     }
 
-    if (a.cand != nullptr) {
-        // verification: the cut inside the boundary key's ties is needed only where a drafted
-        // token or a bonus draw meets that key, and is resolved there (row_done)
-        if (tid == 0) {
-            put_desc(a, ti, m, ks.key, kTiePending, skept, 0, (uint32_t)ks.count << 8);
-            a.desc[(ti.b * kT + ti.s) * 2 + ti.kind].pad = (uint32_t)ntie;
-        }
-        PROF_END(ti.cat, 7);
-        return;
-    }
     // ---- tie cut: occurrence number ntie of the boundary key in index order ------------
     {
         // from the nearer end: occurrence ntie of count in index order is occurrence
@@ -2054,117 +2044,41 @@ __device__ bool row_done(RSmem* sh, const VerifyArgs& a, int b) {
         }
         return true;
     }
+    if (tid >= 32) return false;
     __threadfence();
     const bool onehot_q = a.drf == nullptr;
     const uint16_t* tgt = reinterpret_cast<const uint16_t*>(a.tgt);
     const uint16_t* drf = reinterpret_cast<const uint16_t*>(a.drf);
-    // per position s (lane s of warp 0): the drafted token's p and q; a token whose key is the
-    // boundary key of a row with a pending tie cut needs that key's occurrences before it
-    // (counted by the whole CTA below): pend[s][r] = 1 + the number needed, or 0
-    float* pq = reinterpret_cast<float*>(sh->hist);              // [32][2] p, q
-    uint32_t* pend = reinterpret_cast<uint32_t*>(sh->hist + 64);  // [32][2]
-    uint32_t* cnt = reinterpret_cast<uint32_t*>(sh->hist + 128);  // [32][2] occurrences found
-    if (tid < 32) {
-        const int s = lane;
+    bool acc = false;
+    const int s = lane;
+    if (s < cap - 1) {
+        const long long tok = a.cand[b * kT + s + 1];
+        const bool valid = tok >= 0 && tok < a.V;
         float p = 0.0f, q = 0.0f;
-        uint32_t pt = 0u, pd = 0u;
-        if (s < cap - 1) {
-            const long long tok = a.cand[b * kT + s + 1];
-            const bool valid = tok >= 0 && tok < a.V;
-            if (valid) {
-                const RowDesc dt = load_desc_cg(&a.desc[(b * kT + s) * 2 + 0]);
-                const long long tr = a.tgt_row[b] + s;
-                if (tr >= 0 && tr < a.tgt_rows) {
-                    const uint32_t pb = tgt[tr * a.stride + tok];
-                    if (dt.tie_cut == kTiePending && okey(pb) == dt.kstar) {
-                        pt = 1u + dt.pad;
-                        p = __fmul_rn(exp2c(__fmul_rn(__fadd_rn(bf(pb), -dt.m), dt.c)), dt.inv_s);
-                    } else {
-                        p = row_prob(dt, bf(pb), pb, (int)tok);
-                    }
-                }
-                if (onehot_q) {
-                    q = 1.0f;
-                } else {
-                    const RowDesc dd = load_desc_cg(&a.desc[(b * kT + s) * 2 + 1]);
-                    const long long dr = a.drf_row[b] + s;
-                    if (dr >= 0 && dr < a.drf_rows) {
-                        const uint32_t qb = drf[dr * a.stride + tok];
-                        if (dd.tie_cut == kTiePending && okey(qb) == dd.kstar) {
-                            pd = 1u + dd.pad;
-                            q = __fmul_rn(exp2c(__fmul_rn(__fadd_rn(bf(qb), -dd.m), dd.c)), dd.inv_s);
-                        } else {
-                            q = row_prob(dd, bf(qb), qb, (int)tok);
-                        }
-                    }
+        if (valid) {
+            const RowDesc dt = load_desc_cg(&a.desc[(b * kT + s) * 2 + 0]);
+            const long long tr = a.tgt_row[b] + s;
+            if (tr >= 0 && tr < a.tgt_rows) {
+                const uint32_t pb = tgt[tr * a.stride + tok];
+                p = row_prob(dt, bf(pb), pb, (int)tok);
+            }
+            if (onehot_q) {
+                q = 1.0f;
+            } else {
+                const RowDesc dd = load_desc_cg(&a.desc[(b * kT + s) * 2 + 1]);
+                const long long dr = a.drf_row[b] + s;
+                if (dr >= 0 && dr < a.drf_rows) {
+                    const uint32_t qb = drf[dr * a.stride + tok];
+                    q = row_prob(dd, bf(qb), qb, (int)tok);
                 }
             }
         }
-        pq[2 * s] = p;
-        pq[2 * s + 1] = q;
-        pend[2 * s] = pt;
-        pend[2 * s + 1] = pd;
-        cnt[2 * s] = 0u;
-        cnt[2 * s + 1] = 0u;
-        const uint32_t any = __ballot_sync(0xffffffffu, (pt | pd) != 0u);
-        if (lane == 0) sh->sel[14] = (int)any;
+        acc = q > 0.0f && q <= 1.0f && __fmul_rn(a.u[b * 15 + s], q) < p;
     }
-    __syncthreads();
-    const uint32_t any_pending = (uint32_t)sh->sel[14];
-    if (any_pending) {
-        // occurrences of the boundary key before the drafted token, counted by the CTA
-        for (int e = 0; e < 2 * (cap - 1); ++e) {
-            const int s = e >> 1, r = e & 1;
-            if (!(any_pending & (1u << s)) || pend[e] == 0u) continue;
-            const long long tok = a.cand[b * kT + s + 1];
-            const long long row = r == 0 ? a.tgt_row[b] + s : a.drf_row[b] + s;
-            const uint16_t* rp = (r == 0 ? tgt : drf) + row * a.stride;
-            const uint32_t ks = load_desc_cg(&a.desc[(b * kT + s) * 2 + r]).kstar;
-            uint32_t c = 0;
-            for (long long i = tid; i < tok; i += kRT) c += okey(rp[i]) == ks;
-            const uint32_t tot = (uint32_t)rcta_sum_u64(c, sh);
-            if (tid == 0) cnt[e] = tot;
-        }
-        __syncthreads();
-    }
-    if (tid < 32) {
-        const int s = lane;
-        bool acc = false;
-        if (s < cap - 1) {
-            float p = pq[2 * s], q = pq[2 * s + 1];
-            // kept iff fewer than ntie occurrences precede it (ntie = pend - 1)
-            if (pend[2 * s] && !(cnt[2 * s] < pend[2 * s] - 1u)) p = 0.0f;
-            if (pend[2 * s + 1] && !(cnt[2 * s + 1] < pend[2 * s + 1] - 1u)) q = 0.0f;
-            acc = q > 0.0f && q <= 1.0f && __fmul_rn(a.u[b * 15 + s], q) < p;
-        }
-        const uint32_t rej = __ballot_sync(0xffffffffu, !acc) &
-                             ((cap - 1 >= 32) ? 0xffffffffu : ((1u << (cap - 1)) - 1u));
-        if (lane == 0) sh->sel[15] = rej ? __ffs(rej) - 1 : cap - 1;
-    }
-    __syncthreads();
-    const int acc_len = sh->sel[15];
-    // the rows of the bonus draw: their pending tie cuts are resolved before the chain tasks
-    // read them (the target row, and the draft row unless the whole block was accepted)
-    for (int r = 0; r < 2; ++r) {
-        if (r == 1 && (onehot_q || acc_len == cap - 1)) break;
-        RowDesc* dp = &a.desc[(b * kT + acc_len) * 2 + r];
-        const RowDesc d = load_desc_cg(dp);
-        if (d.tie_cut != kTiePending) continue;
-        const long long row = r == 0 ? a.tgt_row[b] + acc_len : a.drf_row[b] + acc_len;
-        const RowGeo g = row_geo_at(a, r, row);
-        const unsigned long long count = d.flags >> 8, ntie = d.pad;
-        const uint32_t kexp = (key_bits(d.kstar) >> 7) & 0xFFu;
-        const bool normal_key = kexp != 0u && kexp != 0xFFu;
-        const int tie = (!normal_key || 2 * ntie <= count + 1ull)
-                            ? tie_scan<false>(sh, a, g, a.V, d.kstar, ntie)
-                            : tie_scan<true>(sh, a, g, a.V, d.kstar, count - ntie + 1ull);
-        if (tid == 0) {
-            if (tie < 0) atomicOr(&a.ws->err, 16u);
-            __stcg(&dp->tie_cut, tie);
-        }
-    }
-    if (tid == 0) {
-        a.racc[2 * b + 1] = (unsigned)acc_len;
+    const uint32_t rej = __ballot_sync(0xffffffffu, !acc) &
+                         ((cap - 1 >= 32) ? 0xffffffffu : ((1u << (cap - 1)) - 1u));
+    if (lane == 0) {
+        a.racc[2 * b + 1] = (unsigned)(rej ? __ffs(rej) - 1 : cap - 1);
         a.racc[2 * b] = 0u;  // for the next launch
         __threadfence();
         const unsigned pos = atomicAdd(&a.ws->ready_tail, 1u);
