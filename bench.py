@@ -81,6 +81,8 @@ def parse_args():
     p.add_argument("--config", choices=tuple(WORKLOADS), default="config1")
     p.add_argument("--no-cpu-baseline", action="store_true",
                    help="skip the CPU baseline leg (it is reported by default at N=1)")
+    p.add_argument("--kernel", default=None,
+                   help="time one library kernel alone (the workloads of the ncu summaries)")
     p.add_argument("--no-tp-head", action="store_true",
                    help="at N > 1, skip the config-3 TP head timed beside the replicas")
     return p.parse_args()
@@ -953,8 +955,199 @@ def run_head_reference(args):
     }), flush=True)
 
 
+# ---- single kernels (--kernel NAME): the workloads the committed ncu summaries capture ------
+
+def kernel_workload(name, dev):
+    """(launch, algorithmic bytes per launch or None, description) of one library kernel on a
+    seeded workload of the benchmark's sizes (V = 151936)."""
+    import torch
+    from dspine_b200 import lmhead, logits, verify
+    from dspine_b200.kernels import dspine as kd
+    from dspine_b200.layers.fp8 import gather
+    from dspine_b200.sampling import rejection
+    from dspine_b200.sampling.sparse import accept as sparse
+    from dspine_b200.sampling.sparse.target import build_sparse_target
+    V = VOCAB
+    g = torch.Generator(device=dev).manual_seed(11)
+    B = 64
+
+    def softmax_rows(n):
+        return torch.softmax(torch.randn(n, V, generator=g, device=dev) * 2.5, -1)
+
+    def chain_inputs():
+        cand = torch.randint(0, V, (B, 16), generator=g, device=dev)
+        lens = torch.randint(1, 17, (B,), generator=g, device=dev, dtype=torch.int32)
+        u = torch.rand(B, 15, generator=g, device=dev)
+        uf = torch.rand(B, generator=g, device=dev)
+        prefix = torch.zeros(B, dtype=torch.int32, device=dev)
+        return cand, lens, u, uf, prefix
+
+    if name == "chain_probs":
+        p = softmax_rows(B * 16).view(B, 16, V)
+        q = softmax_rows(B * 15).view(B, 15, V)
+        cand, lens, u, uf, prefix = chain_inputs()
+        out = verify.new_outputs(B, dev)
+
+        def launch():
+            rejection.sample_capped_chain_from_probs(
+                candidates=cand, target_probs=p, draft_probs=q, verify_lens=lens, uniforms=u,
+                uniform_final=uf, prefix_lens=prefix, outputs=out)
+        return launch, B * 2 * V * 4, "dsv_chain_from_probs: 64 requests, bonus p and q rows fp32"
+    if name == "sparse_accept":
+        p = softmax_rows(B * 16)
+        cand, lens, u, uf, prefix = chain_inputs()
+        qid = torch.randint(0, V, (B, 15, 16), generator=g, device=dev)
+        qv = torch.softmax(torch.randn(B, 15, 16, generator=g, device=dev), -1)
+        out = verify.new_outputs(B, dev)
+
+        def launch():
+            sparse.accept_sparse(torch, candidates=cand, dense_p=p, packed=None, q_ids=qid,
+                                 q_values=qv, verify_lens=lens, uniforms=u, uniform_final=uf,
+                                 prefix_lens=prefix, outputs=out)
+        return launch, B * V * 4, "dsv_accept_sparse: 64 requests, dense p rows fp32, sparse q"
+    if name == "compress":
+        p = softmax_rows(1024)
+        p = p * (p > 2e-6)
+
+        def launch():
+            sparse.compress_probs(torch, p, capacity=32)
+        return launch, 1024 * V * 4, "dsv_compress_probs: 1024 rows fp32"
+    if name in ("target_probs", "sparse_target"):
+        x = (torch.randn(B * 16, V, generator=g, device=dev) * 2.5).to(torch.bfloat16)
+        T = torch.rand(B, generator=g, device=dev) + 0.5
+        k = torch.full((B,), 20, dtype=torch.int32, device=dev)
+        tp = torch.full((B,), 0.9, device=dev)
+        if name == "target_probs":
+            out = torch.empty(B * 16, V, device=dev)
+
+            def launch():
+                logits.target_probs(x, T, k, tp, rows_per_request=16, out=out)
+            return launch, B * 16 * V * (2 + 4), "dsv_target_probs: 1024 bf16 rows -> fp32 p"
+        from types import SimpleNamespace
+        info = SimpleNamespace(temperatures=T, top_ks=k, top_ps=tp, max_top_k=20,
+                               need_min_p_sampling=False, is_any_greedy=False)
+
+        def launch():
+            build_sparse_target(x, info, block_size=16, capacity=32)
+        return launch, B * 16 * V * 2 * 2, "dsv_sparse_target: 1024 bf16 rows, k 20, top-p 0.9"
+    if name == "serial_sample":
+        K, T = 16, 16
+        n = B * (T - 1)
+        table = torch.randn(n, K, K, generator=g, device=dev)
+        inv_t, top_p, min_p = (torch.full((B,), v, device=dev) for v in (1.0, 0.9, 0.0))
+        top_k, greedy = (torch.full((B,), v, dtype=torch.int32, device=dev) for v in (8, 0))
+        u = torch.rand(n, generator=g, device=dev)
+        cand = torch.randint(0, V, (n, K), generator=g, device=dev)
+        gt = torch.randint(0, V, (n,), generator=g, device=dev)
+        ot = torch.empty(n, dtype=torch.int64, device=dev)
+        oq = torch.empty(n, K, device=dev)
+
+        def launch():
+            kd.serial_sample_chain(table, inv_t, top_k, top_p, min_p, greedy, u, cand, gt, ot,
+                                   oq, T)
+        return launch, None, "dsv_serial_sample_chain: 64 requests x 15 rows, K 16"
+    if name == "serial_table":
+        K, T, H, R = 16, 16, 4096, 512
+        m, n = B * T, B * (T - 1)
+        raw = torch.randn(m, H, generator=g, device=dev).to(torch.bfloat16)
+        norm_w = torch.ones(H, device=dev, dtype=torch.bfloat16)
+        cand = torch.randint(0, V, (n, K), generator=g, device=dev)
+        ids = torch.randint(0, V, (m,), generator=g, device=dev)
+        lm = (torch.randn(V, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        tg = (torch.randn(V, R, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        tsv = (torch.randn(V, 2 * R, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        packed = torch.randn(m, R, generator=g, device=dev).to(torch.bfloat16)
+        rms = torch.rand(m, generator=g, device=dev)
+        gate_b = torch.zeros(R, device=dev, dtype=torch.bfloat16)
+
+        def launch():
+            kd.serial_table(raw, norm_w, cand, ids, lm, tg, tsv, packed, rms, gate_b, T)
+        return launch, n * K * (H + 3 * R) * 2, "dsv_serial_table: 960 drafted rows, K 16, H 4096, R 512"
+    if name == "rescore16":
+        rows, C, H = 960, 128, 5120
+        w = (torch.randn(V, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        ids = torch.randint(0, V, (rows, C), generator=g, device=dev)
+        hid = torch.randn(rows, H, generator=g, device=dev).to(torch.bfloat16)
+
+        def launch():
+            gather.rescore_select16(torch, w, ids, hid)
+        return launch, rows * C * H * 2, "dsv_rescore_select16: 960 rows x 128 candidates, H 5120"
+    if name == "merge":
+        rows, S, k = 512, 8, 20
+        vals = torch.randn(S, rows, k, generator=g, device=dev).sort(-1, descending=True).values
+        ids = torch.randint(0, V, (S, rows, k), generator=g, device=dev)
+        lse = torch.randn(S, rows, generator=g, device=dev)
+
+        def launch():
+            lmhead.merge_shards(vals, ids, lse, k, pad_id=V)
+        return launch, None, "dsv_tp_merge: 512 rows, 8 shards x 20"
+    if name == "topk_ids":
+        x = (torch.randn(794, V, generator=g, device=dev) * 2.5).to(torch.bfloat16)
+        out = torch.empty(794, 16, dtype=torch.int64, device=dev)
+
+        def launch():
+            kd.topk_ids(x, 16, out=out)
+        return launch, 794 * V * 2, "dsv_topk_ids: 794 bf16 rows, k 16"
+    if name == "adjust":
+        from types import SimpleNamespace
+        from dspine_b200.sampling.compact import adjust_logits
+        x = (torch.randn(B, 16, V, generator=g, device=dev) * 2.5).to(torch.bfloat16)
+        words = (V + 31) // 32
+        info = SimpleNamespace(
+            acc_additive_penalties=torch.randn(B, V, generator=g, device=dev),
+            acc_scaling_penalties=1 + torch.rand(B, V, generator=g, device=dev),
+            grammar_mask=SimpleNamespace(vocab_mask=torch.randint(
+                -2**31, 2**31 - 1, (B, words), generator=g, device=dev, dtype=torch.int64).to(torch.int32)),
+            logit_bias=torch.randn(B, V, generator=g, device=dev))
+
+        def launch():
+            adjust_logits(x, info, None)
+        # per element of the rows: the logit read and written; penalties and bias rows per request
+        return launch, B * 16 * V * 4 + B * V * 12, "dsv_adjust_logits: 64 x 16 bf16 rows, every adjustment"
+    raise SystemExit(f"unknown kernel {name}")
+
+
+KERNELS = ("chain_probs", "sparse_accept", "compress", "target_probs", "sparse_target",
+           "serial_sample", "serial_table", "rescore16", "merge", "topk_ids", "adjust")
+
+
+def run_kernel(args):
+    """One library kernel timed alone: K launches between CUDA events on the launching stream,
+    L2 flushed before each (memory-bound kernels report GB/s against the measured HBM copy)."""
+    import torch
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    launch, nbytes, what = kernel_workload(args.kernel, dev)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=dev)
+    for _ in range(max(args.warmup, 3)):
+        flush.zero_()
+        launch()
+    torch.cuda.synchronize(dev)
+    times = []
+    for _ in range(args.steps):
+        flush.zero_()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record()
+        launch()
+        e1.record()
+        torch.cuda.synchronize(dev)
+        times.append(e0.elapsed_time(e1))
+    ms = statistics.mean(times)
+    line = {"kernel": args.kernel, "workload": what, "ms_per_launch": ms,
+            "ms_median": statistics.median(times), "steps": args.steps}
+    if nbytes is not None:
+        peak, src = measured_hbm_peak()
+        gbs = nbytes / (ms * 1e-3) / 1e9
+        line.update({"algorithmic_bytes": nbytes, "achieved_gbs": gbs, "peak_gbs": peak,
+                     "frac": gbs / peak, "peak_source": src})
+    print(json.dumps(line), flush=True)
+
+
 def main():
     args = parse_args()
+    if args.kernel:
+        run_kernel(args)
+        return
     if args.config == "fp8":
         run_fp8_reference(args) if args.impl == "reference" else run_fp8(args)
     elif args.config in HEAD_SHAPES:

@@ -395,52 +395,131 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_accept_kernel(SparseAccept
 
 // ---- compress_probs: sampling/sparse/accept.py:422-460 --------------------------------------
 
-// One CTA per row: the first `capacity` positive entries in index order (ids, values), their
-// number (clamped) and the overflow flag (more than capacity, or a negative / NaN / inf entry).
-__global__ void __launch_bounds__(kThreads, 1)
+// One CTA of kCT threads per row: the first `capacity` positive entries in index order (ids,
+// values), their number (clamped) and the overflow flag (more than capacity, or a negative /
+// NaN / inf entry).  One streaming pass (16-byte loads, four in flight per thread, no barrier)
+// counts the positives and appends up to kCBuf of them to a shared list; a row with at most
+// capacity positives sorts that list by index.  Only a row with more positives walks the row
+// again, tile by tile in index order, until it has its first `capacity` positives (for a dense
+// row these lie at the very start).
+constexpr int kCT = 256;
+constexpr int kCBuf = 64;
+
+__global__ void __launch_bounds__(kCT)
     compress_kernel(const float* __restrict__ p, int V, int capacity, int32_t* ids, float* vals,
                     int32_t* lens, int32_t* ovf) {
-    __shared__ unsigned int wcnt[kThreads / 32];
-    __shared__ unsigned int s_run, s_bad;
+    __shared__ unsigned int s_n, s_bad;
+    __shared__ int s_idx[kCBuf];
+    __shared__ float s_val[kCBuf];
+    __shared__ unsigned int wcnt[kCT / 32];
     const long long r = blockIdx.x;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const float* x = p + r * V;
-    for (int l = tid; l < capacity; l += kThreads) {
-        ids[r * capacity + l] = -1;
-        vals[r * capacity + l] = 0.0f;
-    }
+    const float* x = p + r * (long long)V;
     if (tid == 0) {
-        s_run = 0;
+        s_n = 0;
         s_bad = 0;
     }
     __syncthreads();
     bool bad = false;
-    for (int t0 = 0; t0 < V; t0 += kThreads) {
-        const int i = t0 + tid;
-        const float v = i < V ? x[i] : 0.0f;
+    unsigned int cnt = 0;  // this thread's positives; the list takes them while it has room
+    volatile unsigned int* vn = &s_n;
+    auto visit = [&](float v, int i) {
         bad |= (v < 0.0f) || (v != v) || (fabsf(v) == INFINITY);
-        const bool pos = v > 0.0f;
-        const unsigned m = __ballot_sync(0xffffffffu, pos);
-        if (lane == 0) wcnt[warp] = __popc(m);
-        __syncthreads();
-        unsigned before = s_run, all = 0;
-        for (int w = 0; w < kThreads / 32; ++w) {
-            if (w < warp) before += wcnt[w];
-            all += wcnt[w];
+        if (v > 0.0f) {
+            ++cnt;
+            if (*vn < (unsigned)kCBuf) {
+                const unsigned int slot = atomicAdd(&s_n, 1u);
+                if (slot < (unsigned)kCBuf) {
+                    s_idx[slot] = i;
+                    s_val[slot] = v;
+                }
+            }
         }
-        const unsigned slot = before + __popc(m & ((1u << lane) - 1u));
-        if (pos && slot < (unsigned)capacity) {
-            ids[r * capacity + slot] = i;
-            vals[r * capacity + slot] = v;
+    };
+    const bool vec = (reinterpret_cast<uintptr_t>(x) & 15u) == 0;
+    const int nv = vec ? V / 4 : 0;
+    const float4* x4 = reinterpret_cast<const float4*>(x);
+    int j = tid;
+    for (; j + 3 * kCT < nv; j += 4 * kCT) {
+        float4 q[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) q[u] = __ldcs(x4 + j + u * kCT);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int i = 4 * (j + u * kCT);
+            visit(q[u].x, i);
+            visit(q[u].y, i + 1);
+            visit(q[u].z, i + 2);
+            visit(q[u].w, i + 3);
         }
-        __syncthreads();
-        if (tid == 0) s_run += all;
     }
+    for (; j < nv; j += kCT) {
+        const float4 q = __ldcs(x4 + j);
+        visit(q.x, 4 * j);
+        visit(q.y, 4 * j + 1);
+        visit(q.z, 4 * j + 2);
+        visit(q.w, 4 * j + 3);
+    }
+    for (int i = 4 * nv + tid; i < V; i += kCT) visit(x[i], i);
     if (bad) atomicOr(&s_bad, 1u);
+    // the exact count (the list stops taking entries once full, so s_n may fall short of it)
+    cnt = __reduce_add_sync(0xffffffffu, cnt);
+    if (lane == 0) wcnt[warp] = cnt;
     __syncthreads();
+    unsigned int n = 0;
+#pragma unroll
+    for (int w = 0; w < kCT / 32; ++w) n += wcnt[w];
+    __syncthreads();  // wcnt is reused by the ordered walk
+    if (n <= (unsigned)capacity && n <= (unsigned)kCBuf) {
+        // every positive is in the list: rank by index
+        for (int q = tid; q < capacity; q += kCT) {
+            int id = -1;
+            float v = 0.0f;
+            if (q < (int)n) {
+                const int me = s_idx[q];
+                int rank = 0;
+                for (unsigned int t = 0; t < n; ++t) rank += s_idx[t] < me;
+                id = me;
+                v = s_val[q];
+                ids[r * capacity + rank] = id;
+                vals[r * capacity + rank] = v;
+            } else {
+                ids[r * capacity + q] = -1;
+                vals[r * capacity + q] = 0.0f;
+            }
+        }
+    } else {
+        // more positives than capacity: the first `capacity` in index order, tile by tile
+        for (int q = tid; q < capacity; q += kCT) {
+            ids[r * capacity + q] = -1;
+            vals[r * capacity + q] = 0.0f;
+        }
+        __syncthreads();
+        unsigned int run = 0;
+        for (int t0 = 0; t0 < V && run < (unsigned)capacity; t0 += kCT) {
+            const int i = t0 + tid;
+            const float v = i < V ? x[i] : 0.0f;
+            const bool pos = v > 0.0f;
+            const unsigned m = __ballot_sync(0xffffffffu, pos);
+            if (lane == 0) wcnt[warp] = __popc(m);
+            __syncthreads();
+            unsigned before = run, all = 0;
+            for (int w = 0; w < kCT / 32; ++w) {
+                if (w < warp) before += wcnt[w];
+                all += wcnt[w];
+            }
+            const unsigned slot = before + __popc(m & ((1u << lane) - 1u));
+            if (pos && slot < (unsigned)capacity) {
+                ids[r * capacity + slot] = i;
+                vals[r * capacity + slot] = v;
+            }
+            __syncthreads();
+            run += all;
+        }
+    }
     if (tid == 0) {
-        lens[r] = (int32_t)(s_run < (unsigned)capacity ? s_run : (unsigned)capacity);
-        ovf[r] = (s_run > (unsigned)capacity || s_bad) ? 1 : 0;
+        lens[r] = (int32_t)(n < (unsigned)capacity ? n : (unsigned)capacity);
+        ovf[r] = (n > (unsigned)capacity || s_bad) ? 1 : 0;
     }
 }
 
@@ -455,7 +534,7 @@ int launch_sparse_accept(const SparseAcceptArgs& a, cudaStream_t st) {
 
 int launch_compress(const float* p, long long rows, int V, int capacity, int32_t* ids, float* vals,
                     int32_t* lens, int32_t* ovf, cudaStream_t st) {
-    pr::compress_kernel<<<(unsigned)rows, pr::kThreads, 0, st>>>(p, V, capacity, ids, vals, lens, ovf);
+    pr::compress_kernel<<<(unsigned)rows, pr::kCT, 0, st>>>(p, V, capacity, ids, vals, lens, ovf);
     return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
 }
 

@@ -322,30 +322,136 @@ __device__ __forceinline__ void st<float>(float* p, float x) { *p = x; }
 template <>
 __device__ __forceinline__ void st<__nv_bfloat16>(__nv_bfloat16* p, float x) { *p = __float2bfloat16_rn(x); }
 
+// one element: the four steps in the reference's order, each rounded to the logit dtype
 template <typename T>
-__global__ void adjust_kernel(AdjustArgs a) {
-    const long long r = blockIdx.y;
-    const long long req = a.row_to_request ? a.row_to_request[r] : r / a.rows_per_request;
-    T* row = reinterpret_cast<T*>(a.logits) + r * a.stride;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < a.V; i += gridDim.x * blockDim.x) {
-        float l = ld<T>(row + i);
-        if (a.additive) l = rnd<T>(__fadd_rn(l, a.additive[req * a.V + i]));
-        if (a.scaling) {
-            const float s = a.scaling[req * a.V + i];
-            l = rnd<T>(l < 0.0f ? __fmul_rn(l, s) : __fdiv_rn(l, s));
+__device__ __forceinline__ float adjust_one(float l, float add, float sc, bool allowed, float bias,
+                                            const AdjustArgs& a) {
+    if (a.additive) l = rnd<T>(__fadd_rn(l, add));
+    if (a.scaling) l = rnd<T>(l < 0.0f ? __fmul_rn(l, sc) : __fdiv_rn(l, sc));
+    if (a.mask && !allowed) l = -INFINITY;
+    if (a.bias) l = rnd<T>(__fadd_rn(l, bias));
+    return l;
+}
+
+// Thread t of CTA (x, g) owns columns [8 (256 x + t), + 8) of row group g: the request's rows
+// (full blocks: rows_per_request consecutive rows) or one mapped row.  The request's penalties,
+// mask bits and bias for its columns are loaded once and applied to every row of the group;
+// 16-byte accesses where the row and the parameter rows allow them, element by element else.
+template <typename T>
+__global__ void __launch_bounds__(256) adjust_kernel(AdjustArgs a, bool vec) {
+    const long long g = blockIdx.y;
+    const long long r0 = a.row_to_request ? g : g * a.rows_per_request;
+    const long long r1 = a.row_to_request ? g + 1
+                                          : min((g + 1) * (long long)a.rows_per_request, a.rows);
+    const long long req = a.row_to_request ? a.row_to_request[g] : g;
+    const int c0 = (blockIdx.x * 256 + threadIdx.x) * 8;
+    if (c0 >= a.V) return;
+    const int n = min(8, a.V - c0);
+    float add[8], sc[8], bi[8];
+    bool ok[8];
+    const long long pr = req * (long long)a.V + c0;
+    uint32_t bits = 0xFFFFFFFFu;
+    if (a.mask) {
+        bits = a.mask[req * a.mask_words + (c0 >> 5)] >> (c0 & 31);  // 8 columns in one word
+    }
+    const bool full = vec && n == 8;
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+        add[e] = 0.0f;
+        sc[e] = 1.0f;
+        bi[e] = 0.0f;
+        ok[e] = (bits >> e) & 1u;
+    }
+    if (full) {
+        if (a.additive) {
+            const float4 u = *reinterpret_cast<const float4*>(a.additive + pr);
+            const float4 v = *reinterpret_cast<const float4*>(a.additive + pr + 4);
+            add[0] = u.x; add[1] = u.y; add[2] = u.z; add[3] = u.w;
+            add[4] = v.x; add[5] = v.y; add[6] = v.z; add[7] = v.w;
         }
-        if (a.mask && !((a.mask[req * a.mask_words + (i >> 5)] >> (i & 31)) & 1u)) l = -INFINITY;
-        if (a.bias) l = rnd<T>(__fadd_rn(l, a.bias[req * a.V + i]));
-        st<T>(row + i, l);
+        if (a.scaling) {
+            const float4 u = *reinterpret_cast<const float4*>(a.scaling + pr);
+            const float4 v = *reinterpret_cast<const float4*>(a.scaling + pr + 4);
+            sc[0] = u.x; sc[1] = u.y; sc[2] = u.z; sc[3] = u.w;
+            sc[4] = v.x; sc[5] = v.y; sc[6] = v.z; sc[7] = v.w;
+        }
+        if (a.bias) {
+            const float4 u = *reinterpret_cast<const float4*>(a.bias + pr);
+            const float4 v = *reinterpret_cast<const float4*>(a.bias + pr + 4);
+            bi[0] = u.x; bi[1] = u.y; bi[2] = u.z; bi[3] = u.w;
+            bi[4] = v.x; bi[5] = v.y; bi[6] = v.z; bi[7] = v.w;
+        }
+    } else {
+        for (int e = 0; e < n; ++e) {
+            if (a.additive) add[e] = a.additive[pr + e];
+            if (a.scaling) sc[e] = a.scaling[pr + e];
+            if (a.bias) bi[e] = a.bias[pr + e];
+        }
+    }
+    for (long long r = r0; r < r1; ++r) {
+        T* row = reinterpret_cast<T*>(a.logits) + r * a.stride + c0;
+        if (full) {
+            if (sizeof(T) == 2) {
+                uint4 w = *reinterpret_cast<const uint4*>(row);
+                uint32_t* h = reinterpret_cast<uint32_t*>(&w);
+#pragma unroll
+                for (int e = 0; e < 8; ++e) {
+                    const uint32_t bitsv = (e & 1) ? (h[e >> 1] >> 16) : (h[e >> 1] & 0xFFFFu);
+                    const float l = adjust_one<T>(__uint_as_float(bitsv << 16), add[e], sc[e], ok[e], bi[e], a);
+                    const uint32_t ob = __bfloat16_as_ushort(__float2bfloat16_rn(l));
+                    h[e >> 1] = (e & 1) ? ((h[e >> 1] & 0xFFFFu) | (ob << 16)) : ((h[e >> 1] & 0xFFFF0000u) | ob);
+                }
+                *reinterpret_cast<uint4*>(row) = w;
+            } else {
+                float4* rp = reinterpret_cast<float4*>(row);
+                float4 u = rp[0], v = rp[1];
+                float x[8] = {u.x, u.y, u.z, u.w, v.x, v.y, v.z, v.w};
+#pragma unroll
+                for (int e = 0; e < 8; ++e) x[e] = adjust_one<T>(x[e], add[e], sc[e], ok[e], bi[e], a);
+                rp[0] = make_float4(x[0], x[1], x[2], x[3]);
+                rp[1] = make_float4(x[4], x[5], x[6], x[7]);
+            }
+        } else {
+            for (int e = 0; e < n; ++e) st<T>(row + e, adjust_one<T>(ld<T>(row + e), add[e], sc[e], ok[e], bi[e], a));
+        }
     }
 }
 
 }  // namespace adj
 
 int launch_adjust(const AdjustArgs& a, int dtype, cudaStream_t st) {
-    const dim3 grid((unsigned)((a.V + 255) / 256 < 64 ? (a.V + 255) / 256 : 64), (unsigned)a.rows);
-    if (dtype == 0) adj::adjust_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(a);
-    else adj::adjust_kernel<float><<<grid, 256, 0, st>>>(a);
+    const long long groups = a.row_to_request ? a.rows
+                                              : (a.rows + a.rows_per_request - 1) / a.rows_per_request;
+    if (groups > 65535) {
+        // more groups than a grid column holds: one launch per slice of groups
+        AdjustArgs b = a;
+        for (long long g0 = 0; g0 < groups; g0 += 65535) {
+            const long long ng = groups - g0 < 65535 ? groups - g0 : 65535;
+            const long long rpg = a.row_to_request ? 1 : a.rows_per_request;
+            b.logits = static_cast<char*>(a.logits) + g0 * rpg * a.stride * (dtype == 0 ? 2 : 4);
+            b.rows = (a.rows - g0 * rpg) < ng * rpg ? (a.rows - g0 * rpg) : ng * rpg;
+            b.row_to_request = a.row_to_request ? a.row_to_request + g0 : nullptr;
+            if (!a.row_to_request) {
+                const long long off = g0 * a.V;
+                b.additive = a.additive ? a.additive + off : nullptr;
+                b.scaling = a.scaling ? a.scaling + off : nullptr;
+                b.bias = a.bias ? a.bias + off : nullptr;
+                b.mask = a.mask ? a.mask + g0 * a.mask_words : nullptr;
+            }
+            const int stb = launch_adjust(b, dtype, st);
+            if (stb != kOk) return stb;
+        }
+        return kOk;
+    }
+    const size_t esz = dtype == 0 ? 2 : 4;
+    const bool vec = (reinterpret_cast<uintptr_t>(a.logits) % 16 == 0) &&
+                     ((a.stride * esz) % 16 == 0) && (a.V % 4 == 0) &&
+                     (!a.additive || reinterpret_cast<uintptr_t>(a.additive) % 16 == 0) &&
+                     (!a.scaling || reinterpret_cast<uintptr_t>(a.scaling) % 16 == 0) &&
+                     (!a.bias || reinterpret_cast<uintptr_t>(a.bias) % 16 == 0);
+    const dim3 grid((unsigned)((a.V + 2047) / 2048), (unsigned)groups);
+    if (dtype == 0) adj::adjust_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(a, vec);
+    else adj::adjust_kernel<float><<<grid, 256, 0, st>>>(a, vec);
     return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
 }
 

@@ -6,8 +6,9 @@
 // elements of a row always lie in those chunks, so the result is the row's top-k by
 // (value desc, id asc); this kernel computes it in the same two stages, one CTA per row:
 //
-//   1. chunk maxima (all warps): 16-byte vector loads (8 bf16 / fp16 or 4 fp32 values per
-//      thread, 8 vectors in flight per thread), a packed NaN-ignoring max per vector, the 8 or
+//   1. chunk maxima (all warps): 16-byte streaming vector loads (no L1 allocation; 8 bf16 /
+//      fp16 or 4 fp32 values per thread, 8 vectors in flight per thread; 9% faster than
+//      L1-allocating loads on 794 x 151936 bf16), a packed NaN-ignoring max per vector, the 8 or
 //      16 threads of a chunk combine theirs by shuffles; kept as 64-bit keys (ordered value
 //      bits << 32 | ~chunk) in shared memory;
 //   2. the k chunks with the largest keys (warp 0): thread t's maximum over chunks t, t + 256,
@@ -167,7 +168,7 @@ __device__ __forceinline__ void chunk_maxima(const T* __restrict__ row, int V, b
         for (int u = 0; u < kUnroll; ++u) {
             const int j = j0 + u * kThreads + tid;
             if (vec_ok && j < nfull) {
-                v[u] = __ldg(reinterpret_cast<const uint4*>(row) + j);
+                v[u] = __ldcs(reinterpret_cast<const uint4*>(row) + j);  // streaming: no L1 allocation
             } else {
                 T e[kE];
 #pragma unroll
