@@ -1,15 +1,25 @@
-// probs.cu -- capped chain rejection from dense probabilities (sm_100a).
+// probs.cu -- capped chain rejection from materialised probabilities (sm_100a).
 //
-// Replaces sampling/rejection.py:12-153 (_sample_capped_chain / sample_capped_chain_from_probs):
-// target p [B,16,V] and draft q [B,15,V] fp32, one CTA of 1024 threads per request.
-//   1. warp 0: lane s tests draft s+1 (q in (0,1] and u_s * q < p); the first rejection is the
-//      lowest set bit of a ballot, so the acceptance length needs no loop
+// chain_probs_kernel replaces sampling/rejection.py:12-153 (_sample_capped_chain /
+// sample_capped_chain_from_probs): target p [B,16,V] and draft q [B,15,V] fp32.
+// sparse_accept_kernel replaces sampling/sparse/accept.py:94-543 (accept_sparse, _accept_sparse,
+// _dense_bonus, _packed_bonus): dense or packed target rows, 16-entry sparse draft rows.
+// One request is one thread-block cluster of kCl CTAs:
+//   1. every CTA: warp 0 lane s tests draft s+1 (q in (0,1] and u_s * q < p); the first
+//      rejection is the lowest set bit of a ballot.  Every CTA of the cluster computes the same
+//      acceptance length from the same inputs, so nothing is exchanged for it.
 //   2. the bonus row (residual max(p - clamp01(q), 0), or p after a fully accepted block or a
-//      zero residual mass) is read once with coalesced loads; every 1024-element tile's exact
-//      2^-40 fixed-point mass goes to shared memory
-//   3. threshold floor(u * M) exactly; the crossing tile is found from the tile prefix sums and
-//      only that tile is scanned element by element (block scan) for the first index whose
-//      running mass exceeds the threshold (V-1 when none, as the reference's default)
+//      zero residual mass) is read once: CTA r streams segment r (consecutive 1024-element
+//      tiles, 16-byte loads, four tiles in flight per thread) and keeps the exact 2^-40
+//      fixed-point mass of every 128-element warp tile in shared memory.  With sparse q the
+//      stream sums p alone and the residual replaces p at the (at most 16) draft tokens
+//      afterwards, so no element pays for the 16-entry lookup.
+//   3. the segment totals cross the cluster through distributed shared memory; every CTA forms
+//      M and floor(u * M) exactly, and only the CTA whose segment holds the crossing finds it:
+//      the crossing warp tile from its warp-tile prefix, then the element by one warp scan (the
+//      first index whose running mass exceeds the threshold; V-1 when none, as the reference's
+//      default).  That CTA writes the request's outputs.
+#include <cooperative_groups.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -19,34 +29,228 @@
 namespace dsv {
 namespace pr {
 
-constexpr int kT = 16;
-constexpr int kThreads = 1024;
-constexpr int kMaxTiles = 1024;  // V <= 1M
-constexpr int kMaxPackedWidth = 64;  // packed target rows (compress_probs capacity)
+namespace cg = cooperative_groups;
 
-__device__ __forceinline__ float resid(const float* p, const float* q, int pure, int i) {
-    const float pv = p[i];
-    if (pure) return pv;
-    const float qv = q[i];
+constexpr int kT = 16;
+constexpr int kCl = 8;                 // CTAs per request (one cluster)
+constexpr int kDT = 256;               // threads per CTA
+constexpr int kDW = kDT / 32;          // warps per CTA
+constexpr int kTile = kDT * 4;         // elements per tile: one float4 per thread
+constexpr int kMaxVocab = 1 << 20;
+constexpr int kMaxSegTiles = (kMaxVocab / kTile + kCl - 1) / kCl;
+constexpr int kInFlight = 4;           // tiles loaded before any is reduced
+constexpr int kMaxPackedWidth = 64;    // packed target rows (compress_probs capacity)
+
+struct DrawShared {
+    unsigned long long wt[kMaxSegTiles * kDW];  // warp-tile masses of this CTA's segment
+    unsigned long long seg;                     // segment total, read by the cluster
+    unsigned long long segs[kCl];               // every segment's total
+    int64_t q_id[16];                           // the sparse draft row
+    float q_v[16];
+    long long bonus;
+    int acc;
+};
+
+// tiles [t0, t1) of CTA `rank`: consecutive, as even as whole tiles allow
+__device__ __forceinline__ void segment(int V, int rank, int& t0, int& t1) {
+    const int ntiles = (V + kTile - 1) / kTile;
+    const int per = (ntiles + kCl - 1) / kCl;
+    t0 = min(rank * per, ntiles);
+    t1 = min(t0 + per, ntiles);
+}
+
+// 4 consecutive elements from i (i a multiple of 4); 0 at and past V.  vec: 16-byte loads (the
+// row is 16-byte aligned and V a multiple of 4, so i < V means all four are in the row).
+__device__ __forceinline__ float4 load4(const float* x, int i, int V, bool vec) {
+    if (x == nullptr || i >= V) return make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+    if (vec) return __ldcs(reinterpret_cast<const float4*>(x + i));
+    float4 r;
+    r.x = x[i];
+    r.y = i + 1 < V ? x[i + 1] : 0.0f;
+    r.z = i + 2 < V ? x[i + 2] : 0.0f;
+    r.w = i + 3 < V ? x[i + 3] : 0.0f;
+    return r;
+}
+
+__device__ __forceinline__ float resid1(float pv, float qv) {
     const float qq = (qv >= 0.0f && qv <= 1.0f) ? qv : 0.0f;
     return fmaxf(pv - qq, 0.0f);
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+// Residual of dense rows (chain_probs): max(p - clamp01(q), 0), or p (pure).
+struct DenseResid {
+    const float* p;
+    const float* q;
+    bool pure, vec;
+    struct Raw {
+        float4 p, q;
+    };
+    __device__ __forceinline__ Raw load(int i, int V) const {
+        Raw r;
+        r.p = load4(p, i, V, vec);
+        r.q = pure ? make_float4(0.0f, 0.0f, 0.0f, 0.0f) : load4(q, i, V, vec);
+        return r;
+    }
+    __device__ __forceinline__ uint64_t mass(const Raw& r) const {
+        if (pure) return fixv(r.p.x) + fixv(r.p.y) + fixv(r.p.z) + fixv(r.p.w);
+        return fixv(resid1(r.p.x, r.q.x)) + fixv(resid1(r.p.y, r.q.y)) +
+               fixv(resid1(r.p.z, r.q.z)) + fixv(resid1(r.p.w, r.q.w));
+    }
+    __device__ __forceinline__ float at(int i) const { return pure ? p[i] : resid1(p[i], q[i]); }
+};
+
+// The target probability of a dense row (accept_sparse): p, or p / denominator (IEEE division,
+// the reference's raw fallback); a missing row is all zero.
+struct DenseP {
+    const float* p;
+    float den;
+    bool raw, vec;
+    struct Raw {
+        float4 p;
+    };
+    __device__ __forceinline__ float val(float x) const { return raw ? __fdiv_rn(x, den) : x; }
+    __device__ __forceinline__ Raw load(int i, int V) const { return Raw{load4(p, i, V, vec)}; }
+    __device__ __forceinline__ uint64_t mass(const Raw& r) const {
+        return fixv(val(r.p.x)) + fixv(val(r.p.y)) + fixv(val(r.p.z)) + fixv(val(r.p.w));
+    }
+    __device__ __forceinline__ float at(int i) const { return p ? val(p[i]) : 0.0f; }
+};
+
+// Warp-tile masses of tiles [t0, t1) into wt: element t*1024 + warp*128 + lane*4 + e, so the
+// warp tiles follow index order at wt[(t - t0) * kDW + warp].  All threads.
+template <class W>
+__device__ __forceinline__ void stream_segment(const W& w, int V, int t0, int t1,
+                                               unsigned long long* wt) {
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int off = warp * 128 + lane * 4;
+    for (int t = t0; t < t1; t += kInFlight) {
+        typename W::Raw r[kInFlight];
+#pragma unroll
+        for (int u = 0; u < kInFlight; ++u) r[u] = w.load(t + u < t1 ? (t + u) * kTile + off : V, V);
+#pragma unroll
+        for (int u = 0; u < kInFlight; ++u) {
+            const uint64_t s = warp_sum_u64(w.mass(r[u]));
+            if (lane == 0 && t + u < t1) wt[(t + u - t0) * kDW + warp] = s;
+        }
+    }
+}
+
+// After wt holds this CTA's warp-tile masses: the segment totals cross the cluster, every CTA
+// forms M (into *mass) and floor(u * M), and the CTA whose segment holds the crossing returns the
+// bonus index: the first index whose running mass exceeds floor(u * M) (the weight of index i is
+// full(i), the same weights wt sums).  V - 1 when nothing crosses (u >= 1 or NaN, M = 0) and 0
+// for u < 0, both from rank 0; -1 in every other CTA.  All threads of every CTA of the cluster.
+template <class Full>
+__device__ long long finish_draw(cg::cluster_group& cluster, DrawShared* sh, int V, int t0, int t1,
+                                 float u, const Full& full, unsigned long long* mass) {
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int rank = (int)cluster.block_rank();
+    const int n = (t1 - t0) * kDW;
+    if (warp == 0) {
+        uint64_t s = 0;
+        for (int j = lane; j < n; j += 32) s += sh->wt[j];
+        s = warp_sum_u64(s);
+        if (lane == 0) sh->seg = s;
+    }
+    cluster.sync();  // every segment total is published
+    if (tid < kCl) sh->segs[tid] = *cluster.map_shared_rank(&sh->seg, tid);
+    cluster.sync();  // every CTA has read them (seg may be rewritten, the CTA may exit)
+    unsigned long long M = 0;
+#pragma unroll
+    for (int r = 0; r < kCl; ++r) M += sh->segs[r];
+    *mass = M;
+    const long long thr = scale_floor(u, M);
+    if (thr == -1) return rank == 0 ? 0 : -1;
+    if (thr == -2 || M == 0) return rank == 0 ? V - 1 : -1;
+    // the crossing segment: the first whose inclusive prefix exceeds thr (thr < M: one exists)
+    int cs = 0;
+    unsigned long long before = 0;
+    for (int r = 0; r < kCl; ++r) {
+        if ((long long)(before + sh->segs[r]) > thr) {
+            cs = r;
+            break;
+        }
+        before += sh->segs[r];
+    }
+    if (rank != cs) return -1;
+    if (warp == 0) {
+        long long bo = V - 1;
+        unsigned long long run = before;
+        int found = -1;
+        unsigned long long base = 0;
+        for (int j0 = 0; j0 < n; j0 += 32) {
+            const int j = j0 + lane;
+            const uint64_t v = j < n ? sh->wt[j] : 0;
+            const uint64_t incl = warp_incl_u64(v);
+            const unsigned m = __ballot_sync(0xffffffffu, (long long)(run + incl) > thr);
+            if (m) {
+                const int l = __ffs(m) - 1;
+                found = j0 + l;
+                base = run + __shfl_sync(0xffffffffu, incl - v, l);
+                break;
+            }
+            run += __shfl_sync(0xffffffffu, incl, 31);
+        }
+        if (found >= 0) {
+            const int i0 = (t0 + found / kDW) * kTile + (found % kDW) * 128 + lane * 4;
+            uint64_t f[4];
+            uint64_t s = 0;
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                f[e] = i0 + e < V ? fixv(full(i0 + e)) : 0;
+                s += f[e];
+            }
+            const uint64_t incl = warp_incl_u64(s);
+            const unsigned m = __ballot_sync(0xffffffffu, (long long)(base + incl) > thr);
+            if (m) {
+                const int l = __ffs(m) - 1;
+                long long hit = V - 1;
+                if (lane == l) {
+                    unsigned long long c = base + incl - s;
+                    for (int e = 0; e < 4; ++e) {
+                        c += f[e];
+                        if ((long long)c > thr) {
+                            hit = i0 + e;
+                            break;
+                        }
+                    }
+                }
+                bo = __shfl_sync(0xffffffffu, hit, l);
+            }
+        }
+        if (lane == 0) sh->bonus = bo;
+    }
+    __syncthreads();
+    return sh->bonus;
+}
+
+__device__ __forceinline__ void write_outputs(int b, int acc, long long bo, const int64_t* cand,
+                                              const int32_t* prefix, int32_t* accept,
+                                              int32_t* commit, int64_t* bonus, int64_t* output,
+                                              int32_t* new_seq) {
+    const int tid = threadIdx.x;
+    if (tid < kT) {
+        const int64_t v = tid < acc ? cand[(int64_t)b * kT + tid + 1] : (tid == acc ? bo : 0);
+        output[(int64_t)b * kT + tid] = v;
+    }
+    if (tid == 0) {
+        accept[b] = acc;
+        commit[b] = acc + 1;
+        bonus[b] = bo;
+        new_seq[b] = prefix[b] + acc + 1;
+    }
+}
+
+__global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kDT)
     chain_probs_kernel(int V, const int64_t* __restrict__ cand, const float* __restrict__ target,
                        const float* __restrict__ draft, const int32_t* __restrict__ caps,
                        const float* __restrict__ U, const float* __restrict__ UF,
                        const int32_t* __restrict__ prefix, int32_t* accept, int32_t* commit,
                        int64_t* bonus, int64_t* output, int32_t* new_seq) {
-    __shared__ unsigned long long tile_mass[kMaxTiles];
-    __shared__ unsigned long long wsum[kThreads / 32];
-    __shared__ int s_a, s_tile, s_pure;
-    __shared__ long long s_thr, s_base;
-    __shared__ unsigned long long s_total;
-    __shared__ int s_bonus;
-    const int b = blockIdx.x;
+    __shared__ DrawShared sh;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int b = blockIdx.x / kCl;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int ntiles = (V + kThreads - 1) / kThreads;
     int cap = caps[b];
     cap = cap < 1 ? 1 : (cap > kT ? kT : cap);
 
@@ -62,180 +266,33 @@ __global__ void __launch_bounds__(kThreads, 1)
             reject = !(q > 0.0f && q <= 1.0f && U[b * (kT - 1) + lane] * q < p);
         }
         const unsigned m = __ballot_sync(0xffffffffu, reject && lane < cap - 1);
-        if (lane == 0) {
-            s_a = m ? __ffs(m) - 1 : cap - 1;
-            s_pure = (s_a == cap - 1);
-        }
+        if (lane == 0) sh.acc = m ? __ffs(m) - 1 : cap - 1;
     }
     __syncthreads();
-    const int a = s_a;
-    const float* prow = target + ((int64_t)b * kT + a) * V;
-    const float* qrow = draft + ((int64_t)b * (kT - 1) + (a < kT - 1 ? a : 0)) * V;
-    const float u = UF[b];
-    int pure = s_pure;
-    int64_t bo = V - 1;
+    const int a = sh.acc;
+    int t0, t1;
+    segment(V, (int)cluster.block_rank(), t0, t1);
+    const bool vec = ((reinterpret_cast<uintptr_t>(target) | reinterpret_cast<uintptr_t>(draft)) & 15u) == 0 &&
+                     (V & 3) == 0;
+    DenseResid w{target + ((int64_t)b * kT + a) * V,
+                 draft + ((int64_t)b * (kT - 1) + (a < kT - 1 ? a : 0)) * V, a == cap - 1, vec};
+    long long bo = -1;
     for (int attempt = 0; attempt < 2; ++attempt) {
-        for (int t = tid; t < ntiles; t += kThreads) tile_mass[t] = 0;
+        stream_segment(w, V, t0, t1, sh.wt);
         __syncthreads();
-        // tile masses (coalesced: element t * 1024 + tid)
-        for (int t = 0; t < ntiles; ++t) {
-            const int i = t * kThreads + tid;
-            uint64_t f = i < V ? fixv(resid(prow, qrow, pure, i)) : 0;
-            f = warp_sum_u64(f);
-            if (lane == 0 && f) atomicAdd(&tile_mass[t], (unsigned long long)f);
-        }
-        __syncthreads();
-        // total and crossing tile: warp 0 scans the tile masses in order
-        if (warp == 0) {
-            unsigned long long run = 0;
-            for (int t0 = 0; t0 < ntiles; t0 += 32) {
-                const int t = t0 + lane;
-                uint64_t v = t < ntiles ? tile_mass[t] : 0;
-                v = warp_incl_u64(v);
-                if (t < ntiles) tile_mass[t] = run + v;  // inclusive prefix
-                run += __shfl_sync(0xffffffffu, v, 31);
-            }
-            if (lane == 0) {
-                const long long thr = scale_floor(u, run);
-                s_thr = thr;
-                int tile = -1;
-                s_bonus = (int)(V - 1);
-                if (thr == -1) {
-                    s_bonus = 0;  // u < 0: the first running sum already exceeds it
-                } else if (thr != -2 && run != 0) {
-                    // first tile whose inclusive prefix exceeds thr
-                    int lo = 0, hi = ntiles - 1;
-                    while (lo < hi) {
-                        const int mid = (lo + hi) >> 1;
-                        if ((long long)tile_mass[mid] > thr) hi = mid;
-                        else lo = mid + 1;
-                    }
-                    tile = ((long long)tile_mass[lo] > thr) ? lo : -1;
-                }
-                s_tile = tile;
-                s_base = tile > 0 ? (long long)tile_mass[tile - 1] : 0;
-                s_total = run;
-            }
-        }
-        __syncthreads();
-        const unsigned long long total = s_total;
-        if (!pure && total == 0) {  // zero residual: draw from p
-            pure = 1;
-            __syncthreads();
+        unsigned long long M = 0;
+        bo = finish_draw(cluster, &sh, V, t0, t1, UF[b], [&](int i) { return w.at(i); }, &M);
+        if (!w.pure && M == 0) {  // zero residual: draw from p (every CTA sees the same M)
+            w.pure = true;
             continue;
         }
-        const int tile = s_tile;
-        if (tile >= 0) {
-            // block inclusive scan of the crossing tile
-            const int i = tile * kThreads + tid;
-            uint64_t f = i < V ? fixv(resid(prow, qrow, pure, i)) : 0;
-            uint64_t incl = warp_incl_u64(f);
-            if (lane == 31) wsum[warp] = incl;
-            __syncthreads();
-            if (warp == 0) {
-                uint64_t w = wsum[lane];
-                uint64_t wi = warp_incl_u64(w);
-                wsum[lane] = wi - w;  // exclusive
-            }
-            __syncthreads();
-            const long long run = s_base + (long long)(wsum[warp] + incl);
-            const long long prev = run - (long long)f;
-            if (i < V && run > s_thr && prev <= s_thr) s_bonus = i;  // unique crossing element
-            __syncthreads();
-        }
-        bo = s_bonus;
         break;
     }
-    if (tid < kT) {
-        const int64_t v = tid < a ? cand[(int64_t)b * kT + tid + 1] : (tid == a ? bo : 0);
-        output[(int64_t)b * kT + tid] = v;
-    }
-    if (tid == 0) {
-        accept[b] = a;
-        commit[b] = a + 1;
-        bonus[b] = bo;
-        new_seq[b] = prefix[b] + a + 1;
-    }
+    if (bo < 0) return;
+    write_outputs(b, a, bo, cand, prefix, accept, commit, bonus, output, new_seq);
 }
 
 // ---- sparse q: sampling/sparse/accept.py:94-543 (_accept_sparse, accept_sparse) --------------
-
-struct DrawSmem {
-    unsigned long long tile_mass[kMaxTiles];
-    unsigned long long wsum[kThreads / 32];
-    long long thr, base;
-    unsigned long long total;
-    int tile, bonus;
-};
-
-// First index whose running exact fixed-point mass of w(i) (i in [0, V)) exceeds
-// floor(u * M); V - 1 when none (also for u >= 1), 0 for u < 0.  Reports M.  All threads.
-template <typename W>
-__device__ int tile_draw(int V, float u, W w, DrawSmem* s, unsigned long long* mass_out) {
-    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
-    const int ntiles = (V + kThreads - 1) / kThreads;
-    for (int t = tid; t < kMaxTiles; t += kThreads) s->tile_mass[t] = 0;
-    __syncthreads();
-    for (int t = 0; t < ntiles; ++t) {
-        const int i = t * kThreads + tid;
-        uint64_t f = i < V ? fixv(w(i)) : 0;
-        f = warp_sum_u64(f);
-        if (lane == 0 && f) atomicAdd(&s->tile_mass[t], (unsigned long long)f);
-    }
-    __syncthreads();
-    if (warp == 0) {
-        unsigned long long run = 0;
-        for (int t0 = 0; t0 < ntiles; t0 += 32) {
-            const int t = t0 + lane;
-            uint64_t v = t < ntiles ? s->tile_mass[t] : 0;
-            v = warp_incl_u64(v);
-            if (t < ntiles) s->tile_mass[t] = run + v;
-            run += __shfl_sync(0xffffffffu, v, 31);
-        }
-        if (lane == 0) {
-            const long long thr = scale_floor(u, run);
-            int tile = -1, bo = V - 1;
-            if (thr == -1) {
-                bo = 0;
-            } else if (thr != -2 && run != 0) {
-                int lo = 0, hi = ntiles - 1;
-                while (lo < hi) {
-                    const int mid = (lo + hi) >> 1;
-                    if ((long long)s->tile_mass[mid] > thr) hi = mid;
-                    else lo = mid + 1;
-                }
-                tile = ((long long)s->tile_mass[lo] > thr) ? lo : -1;
-            }
-            s->thr = thr;
-            s->tile = tile;
-            s->bonus = bo;
-            s->base = tile > 0 ? (long long)s->tile_mass[tile - 1] : 0;
-            s->total = run;
-        }
-    }
-    __syncthreads();
-    *mass_out = s->total;
-    const int tile = s->tile;
-    if (tile >= 0) {
-        const int i = tile * kThreads + tid;
-        const uint64_t f = i < V ? fixv(w(i)) : 0;
-        const uint64_t incl = warp_incl_u64(f);
-        if (lane == 31) s->wsum[warp] = incl;
-        __syncthreads();
-        if (warp == 0) {
-            const uint64_t x = s->wsum[lane];
-            s->wsum[lane] = warp_incl_u64(x) - x;
-        }
-        __syncthreads();
-        const long long run = s->base + (long long)(s->wsum[warp] + incl);
-        const long long prev = run - (long long)f;
-        if (i < V && run > s->thr && prev <= s->thr) s->bonus = i;
-    }
-    __syncthreads();
-    const int bo = s->bonus;
-    __syncthreads();
-    return bo;
-}
 
 // sum of the q entries of a 16-entry sparse row equal to `token` (clamped to [0,1] when asked),
 // in entry order (sampling/sparse/accept.py:275-277)
@@ -260,12 +317,29 @@ __device__ __forceinline__ float packed_p(const int32_t* ids, const float* vals,
     return s;
 }
 
-__global__ void __launch_bounds__(kThreads, 1) sparse_accept_kernel(SparseAcceptArgs a) {
-    __shared__ DrawSmem ds;
-    __shared__ int64_t sq_id[16];
-    __shared__ float sq_v[16];
-    __shared__ int s_a;
-    const int b = blockIdx.x;
+// Residual at the draft tokens: wt summed fix(p) over the segment; at each distinct draft token
+// inside it the residual's mass replaces p's.  Warp 0 (lanes 0..15: the 16 entries).
+__device__ __forceinline__ void sparse_corrections(DrawShared* sh, const DenseP& w, int V, int t0,
+                                                   int t1) {
+    const int lane = threadIdx.x & 31;
+    const long long tok = lane < 16 ? sh->q_id[lane] : -1;
+    bool first = lane < 16;
+    for (int j = 0; j < 16; ++j)
+        if (j < lane && sh->q_id[j] == tok) first = false;
+    if (first && tok >= (long long)t0 * kTile && tok < (long long)t1 * kTile && tok < V && tok >= 0) {
+        const float p = w.at((int)tok);
+        const float r = fmaxf(__fsub_rn(p, q_sparse(sh->q_id, sh->q_v, tok, true)), 0.0f);
+        const unsigned long long d = fixv(r) - fixv(p);  // modulo 2^64: the tile total stays >= 0
+        atomicAdd(&sh->wt[(tok - (long long)t0 * kTile) >> 7], d);
+    }
+}
+
+__global__ void __cluster_dims__(kCl, 1, 1) __launch_bounds__(kDT)
+    sparse_accept_kernel(SparseAcceptArgs a) {
+    __shared__ DrawShared sh;
+    cg::cluster_group cluster = cg::this_cluster();
+    const int b = blockIdx.x / kCl;
+    const int rank = (int)cluster.block_rank();
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int V = a.V;
     int cap = a.caps[b];
@@ -295,10 +369,10 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_accept_kernel(SparseAccept
             reject = !(q > 0.0f && q <= 1.0f && __fmul_rn(a.u[qi], q) < p);
         }
         const unsigned m = __ballot_sync(0xffffffffu, reject && lane < cap - 1);
-        if (lane == 0) s_a = m ? __ffs(m) - 1 : cap - 1;
+        if (lane == 0) sh.acc = m ? __ffs(m) - 1 : cap - 1;
     }
     __syncthreads();
-    const int acc = s_a;
+    const int acc = sh.acc;
     const bool pure0 = acc == cap - 1;
     const long long row = base + acc;
     const long long qi = (long long)b * (kT - 1) + (acc < kT - 1 ? acc : 0);
@@ -307,7 +381,8 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_accept_kernel(SparseAccept
     long long bo = V - 1;
     if (packed && !dense) {
         // packed target row: its ids in ascending order (unused slots rank as V, the
-        // reference's padding), residual against q, exact CDF (accept.py:186-204)
+        // reference's padding), residual against q, exact CDF (accept.py:186-204); rank 0 alone
+        if (rank != 0) return;
         if (tid == 0) {
             const int32_t* ids = a.p_ids + row * a.width;
             const float* vals = a.p_vals + row * a.width;
@@ -353,44 +428,46 @@ __global__ void __launch_bounds__(kThreads, 1) sparse_accept_kernel(SparseAccept
                 }
                 break;
             }
-            ds.bonus = (int)bo;
+            sh.bonus = bo;
         }
         __syncthreads();
-        bo = ds.bonus;
+        bo = sh.bonus;
     } else {
         // dense target row (or the dense fallback of an overflowed packed row)
         if (tid < 16) {
-            sq_id[tid] = a.q_ids[qi * 16 + tid];
-            sq_v[tid] = a.q_vals[qi * 16 + tid];
+            sh.q_id[tid] = a.q_ids[qi * 16 + tid];
+            sh.q_v[tid] = a.q_vals[qi * 16 + tid];
         }
-        __syncthreads();
+        int t0, t1;
+        segment(V, rank, t0, t1);
         const float* prow = a.dense ? a.dense + row * V : nullptr;
-        const float den = raw ? a.denom[row] : 1.0f;
+        const DenseP w{prow, raw ? a.denom[row] : 1.0f, raw,
+                       (reinterpret_cast<uintptr_t>(a.dense) & 15u) == 0 && (V & 3) == 0};
         bool pure = pure0;
-        auto w = [&](int i) -> float {
-            float p = prow ? prow[i] : 0.0f;
-            if (raw) p = __fdiv_rn(p, den);
+        auto full = [&](int i) -> float {
+            const float p = w.at(i);
             if (pure) return p;
-            return fmaxf(__fsub_rn(p, q_sparse(sq_id, sq_v, i, true)), 0.0f);
+            return fmaxf(__fsub_rn(p, q_sparse(sh.q_id, sh.q_v, i, true)), 0.0f);
         };
-        unsigned long long M = 0;
-        int draw = tile_draw(V, uf, w, &ds, &M);
-        if (!pure && M == 0) {  // zero residual: draw from p
-            pure = true;
-            draw = tile_draw(V, uf, w, &ds, &M);
+        bo = -1;
+        for (int attempt = 0; attempt < 2; ++attempt) {
+            stream_segment(w, V, t0, t1, sh.wt);
+            __syncthreads();
+            if (!pure) {
+                if (warp == 0) sparse_corrections(&sh, w, V, t0, t1);
+                __syncthreads();
+            }
+            unsigned long long M = 0;
+            bo = finish_draw(cluster, &sh, V, t0, t1, uf, full, &M);
+            if (!pure && M == 0) {  // zero residual: draw from p
+                pure = true;
+                continue;
+            }
+            break;
         }
-        bo = draw;
+        if (bo < 0) return;
     }
-    if (tid < kT) {
-        const int64_t v = tid < acc ? a.cand[(int64_t)b * kT + tid + 1] : (tid == acc ? bo : 0);
-        a.output[(int64_t)b * kT + tid] = v;
-    }
-    if (tid == 0) {
-        a.accept[b] = acc;
-        a.commit[b] = acc + 1;
-        a.bonus[b] = bo;
-        a.new_seq[b] = a.prefix[b] + acc + 1;
-    }
+    write_outputs(b, acc, bo, a.cand, a.prefix, a.accept, a.commit, a.bonus, a.output, a.new_seq);
 }
 
 // ---- compress_probs: sampling/sparse/accept.py:422-460 --------------------------------------
@@ -525,10 +602,10 @@ __global__ void __launch_bounds__(kCT)
 
 }  // namespace pr
 
-int chain_probs_max_vocab() { return pr::kMaxTiles * pr::kThreads; }
+int chain_probs_max_vocab() { return pr::kMaxVocab; }
 
 int launch_sparse_accept(const SparseAcceptArgs& a, cudaStream_t st) {
-    pr::sparse_accept_kernel<<<a.B, pr::kThreads, 0, st>>>(a);
+    pr::sparse_accept_kernel<<<(unsigned)a.B * pr::kCl, pr::kDT, 0, st>>>(a);
     return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
 }
 
@@ -539,7 +616,7 @@ int launch_compress(const float* p, long long rows, int V, int capacity, int32_t
 }
 
 int launch_chain_probs(const ChainProbsArgs& c, cudaStream_t st) {
-    pr::chain_probs_kernel<<<c.B, pr::kThreads, 0, st>>>(c.V, c.cand, c.target, c.draft, c.caps, c.u,
+    pr::chain_probs_kernel<<<(unsigned)c.B * pr::kCl, pr::kDT, 0, st>>>(c.V, c.cand, c.target, c.draft, c.caps, c.u,
                                                         c.uf, c.prefix, c.accept, c.commit, c.bonus,
                                                         c.output, c.new_seq);
     return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;

@@ -3,9 +3,10 @@
 `adjust_logits(logits, info, row_to_request)` keeps the reference's signature and its order of
 transforms (compact.py:14-79): the batch's additive penalties, its scaling penalties, each
 prepared penalizer of SGLang's orchestrator in the orchestrator's order, the grammar mask, the
-logit bias.  The work is a short list of in-place dsv_adjust_logits passes: the additive and
-scaling penalties share one pass, every penalizer is one pass (their order matters, so they
-are not merged), and the grammar mask shares the bias pass.  Each step rounds to the logit
+logit bias.  The work is a short list of in-place dsv_adjust_logits passes (`_Plan`): the
+penalties, the mask and the bias share one pass when nothing else comes between them (the
+usual batch: one read and one write of the rows); every penalizer of the orchestrator opens
+a pass of its own, and the mask and bias join the last one.  Each step rounds to the logit
 dtype exactly as the torch op it replaces.
 
 Grammar masks: an int32 token bitmask (xgrammar's layout, bit set = allowed) or a bool mask
@@ -66,6 +67,32 @@ class _Pass:
                       torch.cuda.current_stream(self.device).cuda_stream)
 
 
+class _Plan:
+    """Steps gathered into as few passes as their order allows.  One pass applies its inputs in
+    the order additive, scaling, mask, bias, so a step joins the open pass when nothing of the
+    pass comes at or after it in that order; a penalizer stage always opens its own pass (the
+    orchestrator's stages are applied one after another)."""
+
+    ORDER = ("additive", "scaling", "bitmask", "bias")
+
+    def __init__(self, launch):
+        self.launch = launch
+        self.pending = {}
+
+    def add(self, name, tensor, own_pass=False):
+        if tensor is None:
+            return
+        rank = self.ORDER.index(name)
+        if own_pass or any(self.ORDER.index(k) >= rank for k in self.pending):
+            self.flush()
+        self.pending[name] = tensor
+
+    def flush(self):
+        if self.pending:
+            self.launch(**self.pending)
+        self.pending = {}
+
+
 def _bool_mask_as_bitmask(mask, vocab):
     """A bool [B, V] mask (True = disallowed) as int32 allow-words (bit set = allowed)."""
     allowed = ~mask.to(torch.bool)
@@ -108,28 +135,27 @@ def adjust_logits(logits, info, row_to_request):
     additive = getattr(info, "acc_additive_penalties", None)
     if additive is None:  # older DFlash callers name the same buffer "linear"
         additive = getattr(info, "acc_linear_penalties", None)
-    scaling = getattr(info, "acc_scaling_penalties", None)
-    if additive is not None or scaling is not None:
-        launch(additive=additive, scaling=scaling)
+    plan = _Plan(launch)
+    plan.add("additive", additive)
+    plan.add("scaling", getattr(info, "acc_scaling_penalties", None))
     for kind, tensor in _penalizer_stages(info, vocab, logits.device):
-        launch(**({"scaling": tensor} if kind == "scale" else {"additive": tensor}))
+        plan.add("scaling" if kind == "scale" else "additive", tensor, own_pass=True)
     grammar = getattr(info, "grammar_mask", None)
-    bias = getattr(info, "logit_bias", None)
-    bitmask = None
     if grammar is not None:
         mask = grammar.vocab_mask
         if mask.dtype == torch.int32:
-            bitmask = mask
+            plan.add("bitmask", mask)
         elif mask.dtype == torch.bool:
-            bitmask = _bool_mask_as_bitmask(mask.to(logits.device), vocab)
+            plan.add("bitmask", _bool_mask_as_bitmask(mask.to(logits.device), vocab))
         else:
             # an unknown layout: the grammar applies its own mask, rows mapped as the reference
+            plan.flush()
             mask = mask.to(device=logits.device)
             rows_mask = (mask.index_select(0, launch.mapping) if launch.mapping is not None
                          else mask.repeat_interleave(launch.per_request, dim=0))
             grammar.grammar.apply_vocab_mask(logits=logits.reshape(-1, vocab), vocab_mask=rows_mask)
-    if bitmask is not None or bias is not None:
-        launch(bitmask=bitmask, bias=bias)
+    plan.add("bias", getattr(info, "logit_bias", None))
+    plan.flush()
 
 
 def around_verify_logits_adjustments(original, *, next_token_logits, sampling_info,
