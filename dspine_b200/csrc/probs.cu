@@ -10,7 +10,7 @@
 //      acceptance length from the same inputs, so nothing is exchanged for it.
 //   2. the bonus row (residual max(p - clamp01(q), 0), or p after a fully accepted block or a
 //      zero residual mass) is read once: CTA r streams segment r (consecutive 1024-element
-//      tiles, 16-byte loads, four tiles in flight per thread) and keeps the exact 2^-40
+//      tiles, 16-byte loads, four or eight in flight per thread) and keeps the exact 2^-40
 //      fixed-point mass of every 128-element warp tile in shared memory.  With sparse q the
 //      stream sums p alone and the residual replaces p at the (at most 16) draft tokens
 //      afterwards, so no element pays for the 16-entry lookup.
@@ -38,7 +38,6 @@ constexpr int kDW = kDT / 32;          // warps per CTA
 constexpr int kTile = kDT * 4;         // elements per tile: one float4 per thread
 constexpr int kMaxVocab = 1 << 20;
 constexpr int kMaxSegTiles = (kMaxVocab / kTile + kCl - 1) / kCl;
-constexpr int kInFlight = 4;           // tiles loaded before any is reduced
 constexpr int kMaxPackedWidth = 64;    // packed target rows (compress_probs capacity)
 
 struct DrawShared {
@@ -82,6 +81,7 @@ struct DenseResid {
     const float* p;
     const float* q;
     bool pure, vec;
+    static constexpr int kInFlight = 4;  // two rows: eight loads
     struct Raw {
         float4 p, q;
     };
@@ -105,6 +105,7 @@ struct DenseP {
     const float* p;
     float den;
     bool raw, vec;
+    static constexpr int kInFlight = 4;  // eight was slower (33 vs 29 us on 64 requests)
     struct Raw {
         float4 p;
     };
@@ -117,12 +118,14 @@ struct DenseP {
 };
 
 // Warp-tile masses of tiles [t0, t1) into wt: element t*1024 + warp*128 + lane*4 + e, so the
-// warp tiles follow index order at wt[(t - t0) * kDW + warp].  All threads.
+// warp tiles follow index order at wt[(t - t0) * kDW + warp].  W::kInFlight tiles are loaded
+// before any is reduced.  All threads.
 template <class W>
 __device__ __forceinline__ void stream_segment(const W& w, int V, int t0, int t1,
                                                unsigned long long* wt) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int off = warp * 128 + lane * 4;
+    constexpr int kInFlight = W::kInFlight;
     for (int t = t0; t < t1; t += kInFlight) {
         typename W::Raw r[kInFlight];
 #pragma unroll

@@ -2332,8 +2332,12 @@ int launch_rows_cta(VerifyArgs a, cudaStream_t stream) {
 
 constexpr int kPW = 256;  // threads per CTA of the writer
 constexpr int kPWChunk = 8192;  // elements per CTA
+static_assert(kPWChunk % (8 * kPW) == 0, "whole 8-element vectors per thread");
 
-__global__ void __launch_bounds__(kPW) probs_write_kernel(VerifyArgs a, float* out) {
+// CTA (x, r) writes elements [8192 x, 8192 (x + 1)) of row r.  vec: the logit row and the output
+// row are 16-byte aligned and V is a multiple of 8, so each thread loads its four 8-element
+// vectors (16 bytes each, all four in flight) before writing any of their 32 probabilities.
+__global__ void __launch_bounds__(kPW) probs_write_kernel(VerifyArgs a, float* out, bool vec) {
     const long long r = blockIdx.y;                 // row within the launch's requests
     const int b = (int)(r / a.cap_all), s = (int)(r % a.cap_all);
     const RowDesc d = a.desc[(b * kT + s) * 2 + 0];
@@ -2342,9 +2346,33 @@ __global__ void __launch_bounds__(kPW) probs_write_kernel(VerifyArgs a, float* o
     float* o = out + r * (long long)a.V;
     const int i0 = blockIdx.x * kPWChunk;
     const int i1 = min(i0 + kPWChunk, a.V);
-    for (int i = i0 + threadIdx.x; i < i1; i += kPW) {
-        const uint32_t u = lr[i];
-        o[i] = row_prob(d, bf(u), u, i);
+    if (vec) {
+        constexpr int kVec = kPWChunk / (8 * kPW);
+        uint4 x[kVec];
+#pragma unroll
+        for (int j = 0; j < kVec; ++j) {
+            const int i = i0 + (threadIdx.x + j * kPW) * 8;
+            if (i < i1) x[j] = __ldcs(reinterpret_cast<const uint4*>(lr + i));
+        }
+#pragma unroll
+        for (int j = 0; j < kVec; ++j) {
+            const int i = i0 + (threadIdx.x + j * kPW) * 8;
+            if (i >= i1) continue;
+            float pv[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) {
+                const uint32_t u = half16(x[j], e);
+                pv[e] = row_prob(d, bf(u), u, i + e);
+            }
+            float4* o4 = reinterpret_cast<float4*>(o + i);
+            o4[0] = make_float4(pv[0], pv[1], pv[2], pv[3]);
+            o4[1] = make_float4(pv[4], pv[5], pv[6], pv[7]);
+        }
+    } else {
+        for (int i = i0 + threadIdx.x; i < i1; i += kPW) {
+            const uint32_t u = lr[i];
+            o[i] = row_prob(d, bf(u), u, i);
+        }
     }
     // greedy rows packed their first argmax for the chain step; clear it for the next launch
     if (blockIdx.x == 0 && threadIdx.x == 0 && (d.flags & kDescGreedy)) a.gmax[b * kT + s] = 0ull;
@@ -2354,7 +2382,9 @@ int launch_target_probs(VerifyArgs a, float* out, cudaStream_t stream) {
     const int st_ = launch_rows_cta(a, stream);
     if (st_ != kOk) return st_;
     const dim3 grid((unsigned)((a.V + kPWChunk - 1) / kPWChunk), (unsigned)(a.B * a.cap_all));
-    probs_write_kernel<<<grid, kPW, 0, stream>>>(a, out);
+    const bool vec = (a.V % 8 == 0) && (a.stride % 8 == 0) &&
+                     ((reinterpret_cast<uintptr_t>(a.tgt) | reinterpret_cast<uintptr_t>(out)) & 15u) == 0;
+    probs_write_kernel<<<grid, kPW, 0, stream>>>(a, out, vec);
     return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
 }
 

@@ -36,7 +36,7 @@
 namespace dsv {
 namespace tk {
 
-constexpr int kThreads = 256;
+constexpr int kThreads = 128;              // six CTAs per SM: one row each, all rows in one wave
 constexpr int kWarps = kThreads / 32;
 constexpr int kChunk = 64;
 constexpr int kMaxChunks = 4096;           // vocabularies up to 262144
@@ -44,19 +44,21 @@ constexpr int kMaxK = 128;                 // 64 for topk_ids, 128 for the ranke
 constexpr int kChunkBits = 12;             // chunk index < 2^12
 constexpr int kIdBits = 18;                // element id < 2^18
 
+// Dynamic shared memory: this head, then ck[nch] (chunk keys), then cand[k * 64] (compacted
+// chunk keys, then candidate keys), both sized by the launch's row length and k.
 struct Smem {
-    unsigned long long ck[kMaxChunks];     // chunk keys
-    unsigned long long tmax[kThreads];     // thread t: max of chunk keys t, t + 256, ...
+    unsigned long long tmax[kThreads];     // thread t: max of chunk keys t, t + kThreads, ...
     unsigned long long selk[kMaxK];        // the selected candidate keys
     int selc[kMaxK];                       // the selected chunks, then the selected ids
     unsigned int ncand;
     unsigned int pad[3];
-    unsigned long long cand[1];            // [k * 64]: compacted chunk keys, then candidate keys
 };
+static_assert(sizeof(Smem) % 16 == 0, "ck starts 16-byte aligned");
 
-// dynamic shared memory for top-k with k <= kk
-constexpr size_t smem_bytes(int kk) {
-    return sizeof(Smem) - sizeof(unsigned long long) + (size_t)kk * kChunk * sizeof(unsigned long long);
+__host__ __device__ constexpr int chunks_of(int V) { return (V + kChunk - 1) / kChunk; }
+
+constexpr size_t smem_bytes(int V, int k) {
+    return sizeof(Smem) + ((size_t)chunks_of(V) + (size_t)k * kChunk) * sizeof(unsigned long long);
 }
 
 __device__ __forceinline__ uint32_t ordered(float v) {
@@ -149,13 +151,14 @@ __device__ __forceinline__ int compact_at_least(const unsigned long long* keys, 
     return m;
 }
 
-// Chunk maxima of one row into sh->ck[0, nch): thread t of the CTA handles 16-byte vectors
-// t, t + 256, ... (kUnroll loads issued before any is used); the kTpc consecutive threads whose
+// Chunk maxima of one row into ck[0, nch): thread t of the CTA handles 16-byte vectors
+// t, t + kThreads, ... (kUnroll loads issued before any is used); the kTpc consecutive threads whose
 // vectors form one chunk combine their maxima by xor-shuffles.  vec_ok: the row start and pitch
 // are 16-byte aligned, so full vectors load as one uint4; the last, partial vector (and every
 // vector of an unaligned row) loads element by element within the row, NaN beyond it.
 template <typename T>
-__device__ __forceinline__ void chunk_maxima(const T* __restrict__ row, int V, bool vec_ok, Smem* sh) {
+__device__ __forceinline__ void chunk_maxima(const T* __restrict__ row, int V, bool vec_ok,
+                                             unsigned long long* ck) {
     constexpr int kE = 16 / sizeof(T);          // values per vector
     constexpr int kTpc = kChunk / kE;           // threads per chunk (8 or 16)
     constexpr int kUnroll = 8;
@@ -187,28 +190,30 @@ __device__ __forceinline__ void chunk_maxima(const T* __restrict__ row, int V, b
             for (int o = 1; o < kTpc; o <<= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
             const int c = j / kTpc;
             if ((tid & (kTpc - 1)) == 0 && j < nvec)
-                sh->ck[c] = ((unsigned long long)m << 32) | (0xFFFFFFFFu - (uint32_t)c);
+                ck[c] = ((unsigned long long)m << 32) | (0xFFFFFFFFu - (uint32_t)c);
         }
     }
 }
 
 template <typename T>
-__global__ void __launch_bounds__(kThreads, 3) topk_ids_kernel(const T* __restrict__ x, long long rows,
+__global__ void __launch_bounds__(kThreads, 6) topk_ids_kernel(const T* __restrict__ x, long long rows,
                                                             int V, long long stride, int k,
                                                             bool vec_ok, bool ranked,
                                                             int64_t* __restrict__ out) {
     extern __shared__ __align__(16) unsigned char smem_raw[];
     Smem* sh = reinterpret_cast<Smem*>(smem_raw);
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
-    const int nch = (V + kChunk - 1) / kChunk;
+    const int nch = chunks_of(V);
+    unsigned long long* ck = reinterpret_cast<unsigned long long*>(smem_raw + sizeof(Smem));
+    unsigned long long* cand = ck + nch;
     for (long long r = blockIdx.x; r < rows; r += gridDim.x) {
         const T* row = x + r * stride;
         // 1. chunk maxima
-        chunk_maxima<T>(row, V, vec_ok, sh);
+        chunk_maxima<T>(row, V, vec_ok, ck);
         __syncthreads();
         {
             unsigned long long t = 0ull;
-            for (int c = tid; c < nch; c += kThreads) t = max(t, sh->ck[c]);
+            for (int c = tid; c < nch; c += kThreads) t = max(t, ck[c]);
             sh->tmax[tid] = t;
         }
         __syncthreads();
@@ -226,9 +231,9 @@ __global__ void __launch_bounds__(kThreads, 3) topk_ids_kernel(const T* __restri
             // search runs over those (all chunk keys when they overflow the candidate buffer)
             const unsigned long long lo = kth_largest_warp(sh->tmax, kThreads, k, kChunkBits);
             const int cap = k * kChunk;
-            const int m = compact_at_least(sh->ck, nch, lo, sh->cand, cap);
+            const int m = compact_at_least(ck, nch, lo, cand, cap);
             __syncwarp();
-            const unsigned long long* pool = m <= cap ? sh->cand : sh->ck;
+            const unsigned long long* pool = m <= cap ? cand : ck;
             const int np = m <= cap ? m : nch;
             const unsigned long long kc = kth_largest_warp(pool, np, k, kChunkBits);
             int s = 0;
@@ -262,7 +267,7 @@ __global__ void __launch_bounds__(kThreads, 3) topk_ids_kernel(const T* __restri
                 base = __shfl_sync(0xffffffffu, base, 0);
                 if (take) {
                     const unsigned int pos = base + __popc(m & ((1u << lane) - 1u));
-                    sh->cand[pos] = ((unsigned long long)key << 32) | (0xFFFFFFFFu - (uint32_t)i);
+                    cand[pos] = ((unsigned long long)key << 32) | (0xFFFFFFFFu - (uint32_t)i);
                 }
             }
         }
@@ -271,11 +276,11 @@ __global__ void __launch_bounds__(kThreads, 3) topk_ids_kernel(const T* __restri
         //    i.e. value desc, id asc)
         if (wid == 0) {
             const int n = (int)sh->ncand;
-            const unsigned long long kk = kth_largest_warp(sh->cand, n, k, kIdBits);
+            const unsigned long long kk = kth_largest_warp(cand, n, k, kIdBits);
             int s = 0;
             for (int base = 0; base < n; base += 32) {
                 const int i = base + lane;
-                const unsigned long long key = i < n ? sh->cand[i] : 0ull;
+                const unsigned long long key = i < n ? cand[i] : 0ull;
                 const bool take = i < n && key >= kk;
                 const unsigned int b = __ballot_sync(0xffffffffu, take);
                 if (take) sh->selk[s + __popc(b & ((1u << lane) - 1u))] = key;
@@ -306,34 +311,39 @@ namespace {
 template <typename T>
 int launch_typed(const void* logits, long long rows, int V, long long stride, int k, bool vec_ok,
                  bool ranked, int64_t* out, cudaStream_t st) {
-    // Per device and buffer class (k <= 64, k <= 128): the dynamic shared memory opt-in and the
-    // resident CTAs (set up once).
+    // Per device: the dynamic shared memory opt-in (once, for the largest row and k) and the
+    // resident CTAs for the last shared-memory size launched (re-queried when it changes).
     constexpr int kMaxDev = 64;
     struct Cache {
         bool ready;
+        size_t smem;
         int blocks;
     };
-    static Cache cache[kMaxDev][2] = {};
+    static Cache cache[kMaxDev] = {};
     static std::mutex mu;
-    const int cls = k <= 64 ? 0 : 1;
-    const size_t smem = tk::smem_bytes(cls == 0 ? 64 : 128);
+    const size_t smem = tk::smem_bytes(V, k);
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return kLaunchFailed;
     int blocks = 0;
     {
         std::lock_guard<std::mutex> lock(mu);
-        Cache& c = cache[dev][cls];
+        Cache& c = cache[dev];
         if (!c.ready) {
-            int per_sm = 0, sms = 0;
             if (cudaFuncSetAttribute(tk::topk_ids_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                     (int)tk::smem_bytes(128)) != cudaSuccess ||
-                cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tk::topk_ids_kernel<T>, tk::kThreads,
+                                     (int)tk::smem_bytes(tk::kMaxChunks * tk::kChunk, tk::kMaxK)) != cudaSuccess)
+                return kLaunchFailed;
+            c.ready = true;
+            c.smem = 0;
+        }
+        if (c.smem != smem) {
+            int per_sm = 0, sms = 0;
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tk::topk_ids_kernel<T>, tk::kThreads,
                                                               smem) != cudaSuccess ||
                 cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
                 per_sm < 1)
                 return kLaunchFailed;
+            c.smem = smem;
             c.blocks = per_sm * sms;
-            c.ready = true;
         }
         blocks = c.blocks;
     }

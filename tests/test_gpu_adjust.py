@@ -87,3 +87,46 @@ def test_other_mask_layouts_use_the_grammars_own_apply():
     adjust_logits(x, info, None)
     assert seen["rows"] == B * T
     assert torch.isinf(x[1, :, 5]).all() and not torch.isinf(x[0]).any()
+
+
+@pytest.mark.parametrize("ci", range(int(FIX["n"])))
+def test_around_hook_adjusts_full_and_packed_rounds(ci):
+    """The plugin's AROUND hook (sampling/compact.py:82-116): without a DSpine worker the
+    original runs untouched; with one, a full round adjusts the [bs * T, V] logits as
+    [bs, T, V] blocks and a packed round adjusts the controller's packed rows through its row
+    mapping; both equal the reference's own adjust_logits."""
+    from dspine_b200.runtime import worker as W
+    from dspine_b200.sampling.compact import around_verify_logits_adjustments
+
+    dtype = torch.bfloat16 if bool(FIX[f"c{ci}_bf16"]) else torch.float32
+    x = torch.from_numpy(FIX[f"c{ci}_x"]).to(dtype).to(DEV)
+    r2r = FIX[f"c{ci}_r2r"]
+    info = case_info(ci, lambda m: SimpleNamespace(vocab_mask=m))
+    want = torch.from_numpy(FIX[f"c{ci}_y"]).to(dtype)
+    calls = []
+
+    def original(**kw):
+        calls.append(kw)
+
+    rows = x.reshape(-1, x.shape[-1])
+    T = x.shape[1] if x.dim() == 3 else 16
+    previous = W._active_worker
+    try:
+        W.set_active_worker(None)
+        around_verify_logits_adjustments(original, next_token_logits=rows, sampling_info=info,
+                                         draft_token_num=T)
+        assert len(calls) == 1 and calls[0]["next_token_logits"] is rows
+        if r2r.size:
+            ctl = SimpleNamespace(compact_round=True, compact_logits=rows,
+                                  row_to_request=torch.from_numpy(r2r).to(DEV))
+            W.set_active_worker(SimpleNamespace(verify_caps=ctl))
+        else:
+            W.set_active_worker(SimpleNamespace(verify_caps=None))
+        around_verify_logits_adjustments(original, next_token_logits=rows, sampling_info=info,
+                                         draft_token_num=T)
+    finally:
+        W.set_active_worker(previous)
+    torch.cuda.synchronize()
+    assert len(calls) == 1
+    got = rows.view_as(x).cpu()
+    assert torch.equal(got.float().view(torch.int32), want.float().view(torch.int32))
