@@ -10,7 +10,7 @@
 //      acceptance length from the same inputs, so nothing is exchanged for it.
 //   2. the bonus row (residual max(p - clamp01(q), 0), or p after a fully accepted block or a
 //      zero residual mass) is read once: CTA r streams segment r (consecutive 1024-element
-//      tiles, 16-byte loads, four or eight in flight per thread) and keeps the exact 2^-40
+//      tiles, 16-byte loads, four tiles in flight per thread) and keeps the exact 2^-40
 //      fixed-point mass of every 128-element warp tile in shared memory.  With sparse q the
 //      stream sums p alone and the residual replaces p at the (at most 16) draft tokens
 //      afterwards, so no element pays for the 16-entry lookup.

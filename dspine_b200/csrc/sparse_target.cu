@@ -16,7 +16,8 @@
 //   pass A  the row's maximum and every thread's maximum;
 //   pass B  the exact mass S and the candidate window: elements whose key is at least tau, the
 //           largest key that at least k thread maxima reach (so the window holds the k largest
-//           elements and every tie of the k-th);
+//           elements and every tie of the k-th); bf16 rows take both exps of a word in one
+//           packed fp32x2 evaluation (exp_pair);
 // then the threshold, the nucleus and the kept set from the window (a few dozen elements), and
 // for overflow rows one write pass.  A window of more than kWinCap elements (a plateau of equal
 // values) switches to a bit search of the threshold with counting passes.
@@ -121,6 +122,66 @@ __device__ __forceinline__ void for_row(const T* row, int V, F&& fn) {
     for (int i = tail0 + tid; i < V; i += kNT) fn(i, E::raw(row, i));
 }
 
+// Pass B over a bf16 row: the thread's share of S = sum fix(exp2c((l - m) c)) and win(i, key) for
+// every element.  Whole words of the 16-byte vectors (four in flight per thread) take both exps
+// in one packed-pair evaluation (exp_pair, bit-identical to fix01(exp2c(y)) for y <= 0); the
+// fix values are summed as their (h, lo) halves and combined once.  Scalar head and tail.
+template <typename W>
+__device__ __forceinline__ unsigned long long mass_bf16(const uint16_t* row, int V, float m, float c,
+                                                        W&& win) {
+    using E = Elem<__nv_bfloat16>;
+    const int tid = threadIdx.x;
+    const uintptr_t addr = reinterpret_cast<uintptr_t>(row);
+    int head = (int)(((16u - (addr & 15u)) & 15u) / 2u);
+    if ((addr & 1u) != 0) head = V;  // not even element-aligned: all scalar
+    if (head > V) head = V;
+    const int nvec = (V - head) / E::kEV;
+    const int tail0 = head + nvec * E::kEV;
+    unsigned long long sacc = 0;
+    auto scalar = [&](int i) {
+        const uint32_t u = row[i];
+        const float y = __fmul_rn(__fsub_rn(E::to_float(u), m), c);
+        if (y >= -41.5f) sacc += fix01(exp2c(y));
+        win(i, E::key(u));
+    };
+    for (int i = tid; i < head; i += kNT) scalar(i);
+    const float2 nm2 = make_float2(-m, -m), c2 = make_float2(c, c);
+    uint32_t hs = 0;   // sum of rne(x) over the thread's words: <= V / kNT * 2^17 elements' worth
+    long long ls = 0;  // sum of the signed low parts
+    auto word = [&](uint32_t w, int i) {
+        const Pair pr = exp_pair(w, nm2, c2);
+        hs += (pr.h0 - 0x4B000000u) + (pr.h1 - 0x4B000000u);
+        ls += (long long)((int32_t)(pr.l0 - 0x4B400000u) + (int32_t)(pr.l1 - 0x4B400000u));
+        win(i, E::key(w & 0xFFFFu));
+        win(i + 1, E::key(w >> 16));
+    };
+    const uint4* vp = reinterpret_cast<const uint4*>(row + head);
+    int v = tid;
+    for (; v + 3 * kNT < nvec; v += 4 * kNT) {
+        uint4 x[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) x[u] = __ldg(vp + v + u * kNT);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int i = head + (v + u * kNT) * E::kEV;
+            word(x[u].x, i);
+            word(x[u].y, i + 2);
+            word(x[u].z, i + 4);
+            word(x[u].w, i + 6);
+        }
+    }
+    for (; v < nvec; v += kNT) {
+        const uint4 x = __ldg(vp + v);
+        const int i = head + v * E::kEV;
+        word(x.x, i);
+        word(x.y, i + 2);
+        word(x.z, i + 4);
+        word(x.w, i + 6);
+    }
+    for (int i = tail0 + tid; i < V; i += kNT) scalar(i);
+    return sacc + (unsigned long long)hs * 8388608ull + (unsigned long long)ls;
+}
+
 // floor(u * m) and whether u * m is an integer (u in [0, 1))
 __device__ __forceinline__ long long scale_floor_exact(float u, unsigned long long m, bool& exact) {
     const long long f = scale_floor(u, m);
@@ -193,11 +254,7 @@ __global__ void __launch_bounds__(kNT) sparse_target_kernel(SparseTargetArgs a) 
         __syncthreads();
 
         // ---- pass B: exact mass S and the window of keys >= tau ----------------------------
-        unsigned long long sacc = 0;
-        for_row<T>(row, V, [&](int i, uint32_t u) {
-            const uint32_t k = E::key(u);
-            const float y = __fmul_rn(__fsub_rn(E::to_float(u), m), c);
-            if (y >= -41.5f) sacc += fix01(exp2c(y));
+        auto window = [&](int i, uint32_t k) {
             if (k >= tau) {
                 const uint32_t pos = atomicAdd(&sh->nwin, 1u);
                 if (pos < (uint32_t)kWinCap) {
@@ -205,7 +262,17 @@ __global__ void __launch_bounds__(kNT) sparse_target_kernel(SparseTargetArgs a) 
                     sh->widx[pos] = i;
                 }
             }
-        });
+        };
+        unsigned long long sacc = 0;
+        if constexpr (sizeof(T) == 2) {
+            sacc = mass_bf16(reinterpret_cast<const uint16_t*>(row), V, m, c, window);
+        } else {
+            for_row<T>(row, V, [&](int i, uint32_t u) {
+                const float y = __fmul_rn(__fsub_rn(E::to_float(u), m), c);
+                if (y >= -41.5f) sacc += fix01(exp2c(y));
+                window(i, E::key(u));
+            });
+        }
         const unsigned long long S = block_sum_u64(sacc, sh);
         const uint32_t nwin = sh->nwin;
 
@@ -383,6 +450,8 @@ __global__ void __launch_bounds__(kNT) sparse_target_kernel(SparseTargetArgs a) 
 int launch_sparse_target(const SparseTargetArgs& a, int dtype, cudaStream_t stream) {
     if (a.rows <= 0) return kOk;
     if (a.capacity < 1 || a.capacity > spt::kMaxCap) return kBadShape;
+    // one CTA per row: a persistent grid of 2 or 3 CTAs per SM (its rows' second pass then
+    // finds them in L2) measured 0.390 / 0.328 ms against 0.271 on 1024 rows
     const long long grid = a.rows < 65535 ? a.rows : 65535;
     if (dtype == 0)
         spt::sparse_target_kernel<__nv_bfloat16><<<(unsigned)grid, spt::kNT, 0, stream>>>(a);

@@ -163,43 +163,6 @@ __device__ __forceinline__ uint64_t fix_of_y(float yc) {
     return (uint64_t)((int64_t)hi * 8388608 + lv);
 }
 
-// packed pair: yc (clamped y) and the raw float bits of h = 2^23 + rne(x), lo = 1.5*2^23 +
-// rne((x - rne(x)) * 2^23) for both halves of a bf16x2 word (x = exp2(yc) * 2^17)
-struct Pair {
-    float2 yc;
-    uint32_t h0, h1, l0, l1;
-};
-
-__device__ __forceinline__ Pair exp_pair(uint32_t w, float2 nm, float2 c2) {
-    const float2 l = make_float2(__uint_as_float(w << 16), __uint_as_float(w & 0xFFFF0000u));
-    float2 y = __fmul2_rn(__fadd2_rn(l, nm), c2);
-    y.x = fmaxf(y.x, -64.0f);
-    y.y = fmaxf(y.y, -64.0f);
-    const float M17 = 12582912.0f + 17.0f;
-    const float2 t = __fadd2_rn(y, make_float2(M17, M17));
-    const float2 tm = __fadd2_rn(t, make_float2(-M17, -M17));
-    const float2 f = __ffma2_rn(tm, make_float2(-1.0f, -1.0f), y);
-    float2 p = make_float2(__uint_as_float(0x3920fddcu), __uint_as_float(0x3920fddcu));
-    p = __ffma2_rn(p, f, make_float2(__uint_as_float(0x3aaf9f2bu), __uint_as_float(0x3aaf9f2bu)));
-    p = __ffma2_rn(p, f, make_float2(__uint_as_float(0x3c1d96a6u), __uint_as_float(0x3c1d96a6u)));
-    p = __ffma2_rn(p, f, make_float2(__uint_as_float(0x3d635774u), __uint_as_float(0x3d635774u)));
-    p = __ffma2_rn(p, f, make_float2(__uint_as_float(0x3e75fdeeu), __uint_as_float(0x3e75fdeeu)));
-    p = __ffma2_rn(p, f, make_float2(__uint_as_float(0x3f317218u), __uint_as_float(0x3f317218u)));
-    p = __ffma2_rn(p, f, make_float2(1.0f, 1.0f));
-    const float2 x = make_float2(__uint_as_float(__float_as_uint(p.x) + (__float_as_uint(t.x) << 23)),
-                                 __uint_as_float(__float_as_uint(p.y) + (__float_as_uint(t.y) << 23)));
-    const float2 h = __fadd2_rn(x, make_float2(kTwo23, kTwo23));
-    const float2 hm = __fadd2_rn(h, make_float2(-kTwo23, -kTwo23));
-    const float2 r = __ffma2_rn(hm, make_float2(-1.0f, -1.0f), x);
-    const float2 lo = __ffma2_rn(r, make_float2(kTwo23, kTwo23), make_float2(12582912.0f, 12582912.0f));
-    Pair o;
-    o.yc = y;
-    o.h0 = __float_as_uint(h.x);
-    o.h1 = __float_as_uint(h.y);
-    o.l0 = __float_as_uint(lo.x);
-    o.l1 = __float_as_uint(lo.y);
-    return o;
-}
 
 // exact probability of element value l under a row descriptor (oracle or_row_prob)
 __device__ __forceinline__ float row_prob(const RowDesc& d, float l, uint32_t u16, int i) {
