@@ -5,10 +5,16 @@ per-request verify lengths from the round's layout (``layout.verify_lens``).  Gr
 take the target's top-1 of the full 16-row envelope (the controller's prepare step pads the
 packed rows back to it) and dsv_accept_greedy with those lengths (ragged.py:51-76 `_accept`);
 sampled rounds go to `accept_sampled_prefix`, with the compact row mapping when the round
-verified packed rows.  The controller's SGLang half (packing and replaying the ragged target
-forward) is outside this package; a controller sets ``ragged_round``, ``batch_size``,
-``tokens`` / ``executed_tokens``, ``layout``, ``compact_round``, ``row_offsets`` and
-``row_to_request``.
+verified packed rows.  The controller's SGLang half (attention backends and CUDA-graph
+runners of the ragged target forward) is outside this package; a controller sets
+``ragged_round``, ``batch_size``, ``tokens`` / ``executed_tokens``, ``layout``,
+``compact_round``, ``row_offsets`` and ``row_to_request``.
+
+The data steps around that forward are here: `compact_window` (ragged.py:192-200: the verify
+input's draft tokens, positions and KV slots gathered to the SPS window, the layout attached,
+the originals kept for `restore_window`) and `expand_rows` (ragged.py:257-266: packed target
+rows scattered back into the full [bs * 16, V] envelope over neutral padding rows, and the
+packed row -> request mapping of compact rounds).
 """
 
 from __future__ import annotations
@@ -16,7 +22,42 @@ from __future__ import annotations
 import torch
 
 from .. import accept as _accept
+from ..sampling.padding import logits_padding
 from .caps import VerifyCaps, target_top1
+
+
+def compact_window(verify_input, batch, window_index, layout):
+    """Gather the verify input to the SPS window (flat request * full + position indices) and
+    attach the ragged layout; returns what `restore_window` needs."""
+    saved = (verify_input, verify_input.draft_token, verify_input.positions,
+             getattr(verify_input, "ragged_verify_layout", None),
+             getattr(verify_input, "kv_loc_cols", None), batch, batch.out_cache_loc)
+    verify_input.draft_token = verify_input.draft_token.index_select(0, window_index)
+    verify_input.positions = verify_input.positions.index_select(0, window_index)
+    verify_input.ragged_verify_layout = layout
+    verify_input.kv_loc_cols = window_index
+    batch.out_cache_loc = batch.out_cache_loc.index_select(0, window_index)
+    return saved
+
+
+def restore_window(saved):
+    (verify_input, verify_input.draft_token, verify_input.positions,
+     verify_input.ragged_verify_layout, verify_input.kv_loc_cols, batch,
+     batch.out_cache_loc) = saved
+
+
+def expand_rows(controller, packed, window_index, bs, full=16, logits=True):
+    """Packed rows of the window back at their (request, position) rows of the full envelope;
+    the other rows neutral (logits: one-point padding rows, other tensors: zeros)."""
+    shape = (bs * full, packed.shape[-1])
+    rows = logits_padding(controller, packed, shape) if logits else packed.new_zeros(shape)
+    rows.index_copy_(0, window_index, packed)
+    return rows
+
+
+def window_requests(window_index, full=16):
+    """The request of every packed row (compact rounds' row -> request mapping)."""
+    return window_index.div(full, rounding_mode="floor")
 
 
 class RaggedVerifyCaps(VerifyCaps):
