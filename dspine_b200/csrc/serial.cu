@@ -198,7 +198,11 @@ size_t table_smem_bytes(int h, int k) {
     return (size_t)h * 4 + (size_t)2 * k * kRPitch * 4 + (size_t)k * 4 + (size_t)2 * k * 8 + 16;
 }
 
-__global__ void __launch_bounds__(kTabThreads)
+// kP: (candidate, candidate) pairs per thread, ceil(K^2 / kTabThreads) rounded up to a power
+// of two (the refinement sums stay in registers; a small K keeps the register count, and so
+// the resident CTAs per SM, of a small K)
+template <int kP>
+__global__ void __launch_bounds__(kTabThreads, kP <= 2 ? 3 : 2)
     table_kernel(TableArgs a) {
     extern __shared__ __align__(16) unsigned char smem[];
     const int K = a.k, H = a.h, RK = a.rk;
@@ -285,9 +289,9 @@ __global__ void __launch_bounds__(kTabThreads)
         }
     }
     const int pairs = K * K;
-    float acc[kMaxPairs];
+    float acc[kP];
 #pragma unroll
-    for (int i = 0; i < kMaxPairs; ++i) acc[i] = 0.0f;
+    for (int i = 0; i < kP; ++i) acc[i] = 0.0f;
     const __nv_bfloat16* q = a.query + row * a.q_stride;
     for (int r0 = 0; r0 < RK; r0 += kRChunk) {
         __syncthreads();  // previous chunk consumed
@@ -309,7 +313,7 @@ __global__ void __launch_bounds__(kTabThreads)
         }
         __syncthreads();
 #pragma unroll
-        for (int i = 0; i < kMaxPairs; ++i) {
+        for (int i = 0; i < kP; ++i) {
             const int pidx = tid + i * kTabThreads;
             if (pidx < pairs) {
                 const int j = pidx / K, c = pidx % K;
@@ -326,7 +330,7 @@ __global__ void __launch_bounds__(kTabThreads)
     float* sv = mch;
     const float rms = a.rms[row];
 #pragma unroll
-    for (int i = 0; i < kMaxPairs; ++i) {
+    for (int i = 0; i < kP; ++i) {
         const int pidx = tid + i * kTabThreads;
         if (pidx < pairs) {
             const int j = pidx / K, c = pidx % K;
@@ -415,14 +419,27 @@ int serial_max_k() { return ser::kMaxK; }
 
 size_t serial_table_smem(int h, int k) { return ser::table_smem_bytes(h, k); }
 
-int launch_serial_table(const TableArgs& a, cudaStream_t st) {
-    const size_t smem = ser::table_smem_bytes(a.h, a.k);
+namespace {
+template <int kP>
+int launch_table_p(const TableArgs& a, size_t smem, cudaStream_t st) {
     if (smem > 48 * 1024 &&
-        cudaFuncSetAttribute(ser::table_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        cudaFuncSetAttribute(ser::table_kernel<kP>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                              (int)smem) != cudaSuccess)
         return kLaunchFailed;
-    ser::table_kernel<<<(unsigned)a.n, ser::kTabThreads, smem, st>>>(a);
+    ser::table_kernel<kP><<<(unsigned)a.n, ser::kTabThreads, smem, st>>>(a);
     return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
+}
+}  // namespace
+
+int launch_serial_table(const TableArgs& a, cudaStream_t st) {
+    const size_t smem = ser::table_smem_bytes(a.h, a.k);
+    const int pairs = a.k * a.k;
+    static_assert(ser::kMaxPairs == 16, "pair classes 1, 2, 4, 8, 16");
+    if (pairs <= ser::kTabThreads) return launch_table_p<1>(a, smem, st);
+    if (pairs <= 2 * ser::kTabThreads) return launch_table_p<2>(a, smem, st);
+    if (pairs <= 4 * ser::kTabThreads) return launch_table_p<4>(a, smem, st);
+    if (pairs <= 8 * ser::kTabThreads) return launch_table_p<8>(a, smem, st);
+    return launch_table_p<16>(a, smem, st);
 }
 
 size_t serial_chain_smem(int tm1, int k) { return ser::walk_smem_bytes(tm1, k); }
