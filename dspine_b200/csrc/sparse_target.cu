@@ -86,6 +86,57 @@ __device__ __forceinline__ unsigned long long block_sum_u64(unsigned long long v
     return r;
 }
 
+// Packed keys of a bf16x2 word: both halves' ordered keys (negative: ~bits, else bits | 0x8000),
+// except that -0 gives 0x7FFF where the canonical key of zero is 0x8000 (the callers allow for
+// it).  Two instructions.
+__device__ __forceinline__ uint32_t keys2(uint32_t w) {
+    uint32_t sgn;
+    asm("prmt.b32 %0, %1, 0, 0xBB99;" : "=r"(sgn) : "r"(w));  // 0xFFFF in each negative half
+    return w ^ (sgn | 0x80008000u);
+}
+
+__device__ __forceinline__ uint32_t max_u16x2(uint32_t a, uint32_t b) {
+    uint32_t d;
+    asm("max.u16x2 %0, %1, %2;" : "=r"(d) : "r"(a), "r"(b));
+    return d;
+}
+
+// Pass A over a bf16 row: the thread's largest canonical key (packed max of the words' keys,
+// three instructions per word; scalar head and tail).
+__device__ __forceinline__ uint32_t max_key_bf16(const uint16_t* row, int V) {
+    using E = Elem<__nv_bfloat16>;
+    const int tid = threadIdx.x;
+    const uintptr_t addr = reinterpret_cast<uintptr_t>(row);
+    int head = (int)(((16u - (addr & 15u)) & 15u) / 2u);
+    if ((addr & 1u) != 0) head = V;
+    if (head > V) head = V;
+    const int nvec = (V - head) / E::kEV;
+    const int tail0 = head + nvec * E::kEV;
+    uint32_t acc = 0u, tk = 0u;
+    for (int i = tid; i < head; i += kNT) tk = max(tk, E::key(row[i]));
+    const uint4* vp = reinterpret_cast<const uint4*>(row + head);
+    int v = tid;
+    for (; v + 3 * kNT < nvec; v += 4 * kNT) {
+        uint4 x[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) x[u] = __ldg(vp + v + u * kNT);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            acc = max_u16x2(acc, max_u16x2(max_u16x2(keys2(x[u].x), keys2(x[u].y)),
+                                           max_u16x2(keys2(x[u].z), keys2(x[u].w))));
+        }
+    }
+    for (; v < nvec; v += kNT) {
+        const uint4 x = __ldg(vp + v);
+        acc = max_u16x2(acc, max_u16x2(max_u16x2(keys2(x.x), keys2(x.y)),
+                                       max_u16x2(keys2(x.z), keys2(x.w))));
+    }
+    for (int i = tail0 + tid; i < V; i += kNT) tk = max(tk, E::key(row[i]));
+    uint32_t pk = max(acc & 0xFFFFu, acc >> 16);
+    if (pk == 0x7FFFu) pk = 0x8000u;  // -0 is zero
+    return max(tk, pk);
+}
+
 // fn(i, raw bits) for every element of the row, each element by exactly one thread; 16-byte
 // loads (four in flight per thread) between a scalar head and tail
 template <typename T, typename F>
@@ -128,7 +179,7 @@ __device__ __forceinline__ void for_row(const T* row, int V, F&& fn) {
 // fix values are summed as their (h, lo) halves and combined once.  Scalar head and tail.
 template <typename W>
 __device__ __forceinline__ unsigned long long mass_bf16(const uint16_t* row, int V, float m, float c,
-                                                        W&& win) {
+                                                        uint32_t tau, W&& win) {
     using E = Elem<__nv_bfloat16>;
     const int tid = threadIdx.x;
     const uintptr_t addr = reinterpret_cast<uintptr_t>(row);
@@ -148,12 +199,19 @@ __device__ __forceinline__ unsigned long long mass_bf16(const uint16_t* row, int
     const float2 nm2 = make_float2(-m, -m), c2 = make_float2(c, c);
     uint32_t hs = 0;   // sum of rne(x) over the thread's words: <= V / kNT * 2^17 elements' worth
     long long ls = 0;  // sum of the signed low parts
+    // window pre-test on packed keys: a half reaching tau - 1 (a -0 key is one below zero's)
+    // goes to the exact test; tau < 2 sends every element there
+    const uint32_t lo = tau >= 2u ? tau - 2u : 0u;
+    const uint32_t lo2 = lo | (lo << 16);
+    const bool all = tau < 2u;
     auto word = [&](uint32_t w, int i) {
         const Pair pr = exp_pair(w, nm2, c2);
         hs += (pr.h0 - 0x4B000000u) + (pr.h1 - 0x4B000000u);
         ls += (long long)((int32_t)(pr.l0 - 0x4B400000u) + (int32_t)(pr.l1 - 0x4B400000u));
-        win(i, E::key(w & 0xFFFFu));
-        win(i + 1, E::key(w >> 16));
+        if (all || max_u16x2(keys2(w), lo2) != lo2) {
+            win(i, E::key(w & 0xFFFFu));
+            win(i + 1, E::key(w >> 16));
+        }
     };
     const uint4* vp = reinterpret_cast<const uint4*>(row + head);
     int v = tid;
@@ -220,18 +278,22 @@ __global__ void __launch_bounds__(kNT) sparse_target_kernel(SparseTargetArgs a) 
 
         // ---- pass A: maxima (key order; the first index of the row maximum) -----------------
         uint32_t tkey = 0;
-        int tfirst = 0x7fffffff;
-        for_row<T>(row, V, [&](int i, uint32_t u) {
-            const uint32_t k = E::key(u);
-            if (k > tkey || (k == tkey && i < tfirst)) { tkey = k; tfirst = i; }
-        });
+        if constexpr (sizeof(T) == 2) {
+            tkey = max_key_bf16(reinterpret_cast<const uint16_t*>(row), V);
+        } else {
+            for_row<T>(row, V, [&](int, uint32_t u) { tkey = max(tkey, E::key(u)); });
+        }
         const uint32_t mkey = block_max_u32(tkey, sh);
         const float m = E::key_to_float(mkey);
         if (!(Tm > 0.0f) || !(c < __int_as_float(0x7f800000))) {
             // no temperature: one-hot at the first maximum (the reference gates such rows away)
             if (tid == 0) sh->count = 0x7fffffff;
             __syncthreads();
-            if (tkey == mkey) atomicMin(&sh->count, tfirst);
+            int tfirst = 0x7fffffff;
+            for_row<T>(row, V, [&](int i, uint32_t u) {
+                if (i < tfirst && E::key(u) == mkey) tfirst = i;
+            });
+            if (tfirst != 0x7fffffff) atomicMin(&sh->count, tfirst);
             __syncthreads();
             for (int j = tid; j < cap; j += kNT) {
                 oid[j] = j == 0 ? sh->count : -1;
@@ -265,7 +327,7 @@ __global__ void __launch_bounds__(kNT) sparse_target_kernel(SparseTargetArgs a) 
         };
         unsigned long long sacc = 0;
         if constexpr (sizeof(T) == 2) {
-            sacc = mass_bf16(reinterpret_cast<const uint16_t*>(row), V, m, c, window);
+            sacc = mass_bf16(reinterpret_cast<const uint16_t*>(row), V, m, c, tau, window);
         } else {
             for_row<T>(row, V, [&](int i, uint32_t u) {
                 const float y = __fmul_rn(__fsub_rn(E::to_float(u), m), c);
