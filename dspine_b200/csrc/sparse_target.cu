@@ -35,6 +35,8 @@ constexpr int kNT = 256;
 constexpr int kNW = kNT / 32;
 constexpr int kWinCap = 1024;  // window candidates per row
 constexpr int kMaxCap = 64;    // largest capacity (and top-k)
+constexpr int kLd = 4;  // 16-byte loads in flight per thread in the row passes (8: 0.230 ms
+                        // against 0.208 on 1024 rows: register pressure)
 
 struct Smem {
     uint32_t wkey[kWinCap];
@@ -116,12 +118,12 @@ __device__ __forceinline__ uint32_t max_key_bf16(const uint16_t* row, int V) {
     for (int i = tid; i < head; i += kNT) tk = max(tk, E::key(row[i]));
     const uint4* vp = reinterpret_cast<const uint4*>(row + head);
     int v = tid;
-    for (; v + 3 * kNT < nvec; v += 4 * kNT) {
-        uint4 x[4];
+    for (; v + (kLd - 1) * kNT < nvec; v += kLd * kNT) {
+        uint4 x[kLd];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) x[u] = __ldg(vp + v + u * kNT);
+        for (int u = 0; u < kLd; ++u) x[u] = __ldg(vp + v + u * kNT);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < kLd; ++u) {
             acc = max_u16x2(acc, max_u16x2(max_u16x2(keys2(x[u].x), keys2(x[u].y)),
                                            max_u16x2(keys2(x[u].z), keys2(x[u].w))));
         }
@@ -152,12 +154,12 @@ __device__ __forceinline__ void for_row(const T* row, int V, F&& fn) {
     for (int i = tid; i < head; i += kNT) fn(i, E::raw(row, i));
     const uint4* vp = reinterpret_cast<const uint4*>(row + head);
     int v = tid;
-    for (; v + 3 * kNT < nvec; v += 4 * kNT) {
-        uint4 x[4];
+    for (; v + (kLd - 1) * kNT < nvec; v += kLd * kNT) {
+        uint4 x[kLd];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) x[u] = __ldg(vp + v + u * kNT);
+        for (int u = 0; u < kLd; ++u) x[u] = __ldg(vp + v + u * kNT);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < kLd; ++u) {
             uint32_t e[E::kEV];
             E::unpack(x[u], e);
 #pragma unroll
@@ -215,12 +217,12 @@ __device__ __forceinline__ unsigned long long mass_bf16(const uint16_t* row, int
     };
     const uint4* vp = reinterpret_cast<const uint4*>(row + head);
     int v = tid;
-    for (; v + 3 * kNT < nvec; v += 4 * kNT) {
-        uint4 x[4];
+    for (; v + (kLd - 1) * kNT < nvec; v += kLd * kNT) {
+        uint4 x[kLd];
 #pragma unroll
-        for (int u = 0; u < 4; ++u) x[u] = __ldg(vp + v + u * kNT);
+        for (int u = 0; u < kLd; ++u) x[u] = __ldg(vp + v + u * kNT);
 #pragma unroll
-        for (int u = 0; u < 4; ++u) {
+        for (int u = 0; u < kLd; ++u) {
             const int i = head + (v + u * kNT) * E::kEV;
             word(x[u].x, i);
             word(x[u].y, i + 2);
