@@ -130,3 +130,30 @@ def test_around_hook_adjusts_full_and_packed_rounds(ci):
     assert len(calls) == 1
     got = rows.view_as(x).cpu()
     assert torch.equal(got.float().view(torch.int32), want.float().view(torch.int32))
+
+
+def test_scaling_matches_the_ieee_quotient_for_every_bf16_logit():
+    """The scaling step's l / s (l >= 0) takes a reciprocal product away from bf16 rounding
+    midpoints; across every finite bf16 logit of both signs and penalties from tiny to huge, the
+    result must equal the reference's rule (compact.py:32-34: fp32 l / s or l * s, then bf16)."""
+    pos = torch.arange(0, 0x7F80, dtype=torch.int32)                 # +0 .. largest finite
+    bits = torch.cat([pos, pos | 0x8000]).to(torch.int16)            # and every negative
+    V = bits.numel()
+    g = torch.Generator().manual_seed(5)
+    B = 12
+    logits = bits.view(torch.bfloat16).repeat(B, 1).view(B, 1, V).contiguous()
+    scales = torch.empty(B, V)
+    for b in range(B - 4):  # random penalties over [0.25, 8)
+        scales[b] = torch.exp2(torch.rand(V, generator=g) * 5 - 2)
+    scales[B - 4] = 3.0
+    scales[B - 3] = 1.0
+    scales[B - 2] = 1e-30  # outside the reciprocal's range: the division itself
+    scales[B - 1] = 7e29
+    want = torch.where(logits.float() < 0, logits.float() * scales[:, None, :],
+                       logits.float() / scales[:, None, :]).to(torch.bfloat16)
+    x = logits.to(DEV)
+    adjust_logits(x, SimpleNamespace(acc_scaling_penalties=scales.to(DEV)), None)
+    got = x.cpu()
+    same = got.view(torch.int16) == want.view(torch.int16)
+    both_nan = torch.isnan(got.float()) & torch.isnan(want.float())
+    assert bool((same | both_nan).all())
