@@ -11,13 +11,14 @@
 //      L1-allocating loads on 794 x 151936 bf16), a packed NaN-ignoring max per vector, the 8 or
 //      16 threads of a chunk combine theirs by shuffles; kept as 64-bit keys (ordered value
 //      bits << 32 | ~chunk) in shared memory;
-//   2. the k chunks with the largest keys (warp 0): thread t's maximum over chunks t, t + 256,
-//      ... gives 256 keys whose k-th largest, L, has at least k chunk keys at or above it; warp
-//      0 compacts those few keys and finds the k-th largest among them by a bit search (one
-//      warp-wide count per bit, no block barrier);
-//   3. candidates (all warps, one selected chunk per warp at a time): the elements of the
-//      selected chunks whose value reaches the k-th chunk maximum (every top-k element does),
-//      as keys (ordered value bits << 32 | ~id);
+//   2. the k chunks with the largest keys: thread t's maximum over chunks t, t + 128, ...
+//      gives 128 keys whose k-th largest, L (warp 0, bit search), has at least k chunk keys at
+//      or above it; every warp compacts those few keys, and warp 0 finds the k-th largest among
+//      them by a bit search (one warp-wide count per bit; for bf16 the 16 widening bits of the
+//      value are not searched);
+//   3. candidates (all threads, every load of the row's selected chunks issued together): the
+//      elements of the selected chunks whose value reaches the k-th chunk maximum (every top-k
+//      element does), as keys (ordered value bits << 32 | ~id);
 //   4. the k largest candidates (warp 0, the same bit search), written in ascending id order.
 //
 // Values compare as fp32 (bf16 / fp16 widen exactly); -0 equals +0; NaN ranks below every
@@ -29,6 +30,7 @@
 
 #include <cstring>
 #include <mutex>
+#include <type_traits>
 
 #include "dsv_common.cuh"
 #include "dsv_kernels.h"
@@ -37,7 +39,6 @@ namespace dsv {
 namespace tk {
 
 constexpr int kThreads = 128;              // six CTAs per SM: one row each, all rows in one wave
-constexpr int kWarps = kThreads / 32;
 constexpr int kChunk = 64;
 constexpr int kMaxChunks = 4096;           // vocabularies up to 262144
 constexpr int kMaxK = 128;                 // 64 for topk_ids, 128 for the ranked form
@@ -102,8 +103,11 @@ template <> __device__ __forceinline__ __half nan_value<__half>() { return __ush
 // search from the top bit, one warp-wide count per bit.  The low word of every key is ~index
 // with index < 2^lowbits, so its bits 31..lowbits are set in every key and need no count.  Keys
 // of value 0 (empty slots) never count.  Every lane gets the result.
+// bf16: every key's high word is the ordered value of a bf16 number widened to fp32, whose low
+// 16 bits are 0 (non-negative values) or all ones (negative values; NaN's key is 0), so once bits
+// 63..48 are known those 16 bits follow and are not searched.
 __device__ __forceinline__ unsigned long long kth_largest_warp(const unsigned long long* keys, int n,
-                                                               int k, int lowbits) {
+                                                               int k, int lowbits, bool bf16 = false) {
     const int lane = threadIdx.x & 31;
     constexpr int kReg = 8;                 // up to 256 keys are held in registers
     unsigned long long held[kReg];
@@ -114,6 +118,11 @@ __device__ __forceinline__ unsigned long long kth_largest_warp(const unsigned lo
     }
     unsigned long long prefix = 0ull;
     for (int bit = 63; bit >= 0; --bit) {
+        if (bf16 && bit == 47) {
+            if ((prefix >> 48) != 0ull && (prefix >> 63) == 0ull) prefix |= 0xFFFFull << 32;
+            bit = 32;
+            continue;
+        }
         if (bit == 31) {
             prefix |= 0xFFFFFFFFull & (0xFFFFFFFFull << lowbits);
             bit = lowbits;
@@ -130,25 +139,6 @@ __device__ __forceinline__ unsigned long long kth_largest_warp(const unsigned lo
         if (__reduce_add_sync(0xffffffffu, c) >= (unsigned int)k) prefix = trial;
     }
     return prefix;
-}
-
-// Warp-wide stream compaction: appends keys[i] (i < n) with keys[i] >= lo to dst in index
-// order, writing only the first cap of them; returns the full count (every lane).
-__device__ __forceinline__ int compact_at_least(const unsigned long long* keys, int n,
-                                                unsigned long long lo, unsigned long long* dst,
-                                                int cap) {
-    const int lane = threadIdx.x & 31;
-    int m = 0;
-    for (int base = 0; base < n; base += 32) {
-        const int i = base + lane;
-        const unsigned long long key = i < n ? keys[i] : 0ull;
-        const bool take = i < n && key >= lo;
-        const unsigned int b = __ballot_sync(0xffffffffu, take);
-        const int pos = m + __popc(b & ((1u << lane) - 1u));
-        if (take && pos < cap) dst[pos] = key;
-        m += __popc(b);
-    }
-    return m;
 }
 
 // Chunk maxima of one row into ck[0, nch): thread t of the CTA handles 16-byte vectors
@@ -204,6 +194,7 @@ __global__ void __launch_bounds__(kThreads, 6) topk_ids_kernel(const T* __restri
     Smem* sh = reinterpret_cast<Smem*>(smem_raw);
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
     const int nch = chunks_of(V);
+    constexpr bool kBf16 = sizeof(T) == 2 && !std::is_same<T, __half>::value;
     unsigned long long* ck = reinterpret_cast<unsigned long long*>(smem_raw + sizeof(Smem));
     unsigned long long* cand = ck + nch;
     for (long long r = blockIdx.x; r < rows; r += gridDim.x) {
@@ -226,16 +217,38 @@ __global__ void __launch_bounds__(kThreads, 6) topk_ids_kernel(const T* __restri
                 sh->ncand = 0u;
                 sh->tmax[0] = 0ull;
             }
-        } else if (wid == 0) {
+        } else {
             // at least k threads hold a key >= lo, so at least k chunk keys are >= lo; the
-            // search runs over those (all chunk keys when they overflow the candidate buffer)
-            const unsigned long long lo = kth_largest_warp(sh->tmax, kThreads, k, kChunkBits);
+            // search runs over those (all chunk keys when they overflow the candidate buffer),
+            // compacted by every warp (order is not kept: only the set matters)
+            if (wid == 0) {
+                const unsigned long long lo = kth_largest_warp(sh->tmax, kThreads, k, kChunkBits, kBf16);
+                if (lane == 0) {
+                    sh->selk[0] = lo;
+                    sh->ncand = 0u;
+                }
+            }
+            __syncthreads();
+            const unsigned long long lo = sh->selk[0];
             const int cap = k * kChunk;
-            const int m = compact_at_least(ck, nch, lo, cand, cap);
-            __syncwarp();
-            const unsigned long long* pool = m <= cap ? cand : ck;
-            const int np = m <= cap ? m : nch;
-            const unsigned long long kc = kth_largest_warp(pool, np, k, kChunkBits);
+            for (int base = wid * 32; base < nch; base += kThreads) {
+                const int i = base + lane;
+                const unsigned long long key = i < nch ? ck[i] : 0ull;
+                const bool take = i < nch && key >= lo;
+                const unsigned int b = __ballot_sync(0xffffffffu, take);
+                unsigned int at = 0;
+                if (lane == 0 && b) at = atomicAdd(&sh->ncand, (unsigned int)__popc(b));
+                at = __shfl_sync(0xffffffffu, at, 0);
+                const unsigned int pos = at + __popc(b & ((1u << lane) - 1u));
+                if (take && pos < (unsigned int)cap) cand[pos] = key;
+            }
+            __syncthreads();
+        }
+        if (nch > k && wid == 0) {
+            const int m = (int)sh->ncand;
+            const unsigned long long* pool = m <= k * kChunk ? cand : ck;
+            const int np = m <= k * kChunk ? m : nch;
+            const unsigned long long kc = kth_largest_warp(pool, np, k, kChunkBits, kBf16);
             int s = 0;
             for (int base = 0; base < np; base += 32) {
                 const int i = base + lane;
@@ -252,14 +265,24 @@ __global__ void __launch_bounds__(kThreads, 6) topk_ids_kernel(const T* __restri
             }
         }
         __syncthreads();
-        // 3. candidates: elements of the selected chunks that reach the k-th chunk maximum
+        // 3. candidates: elements of the selected chunks that reach the k-th chunk maximum.
+        //    Element e of the nsel chunks (chunk s = e / 64) goes to thread e % kThreads, kCU of
+        //    them per thread whose loads issue together (a row's candidates in one round trip).
         const uint32_t vmin = (uint32_t)(sh->tmax[0] >> 32);
-        for (int s = wid; s < nsel; s += kWarps) {
-            const int c = sh->selc[s];
+        constexpr int kCU = 8;
+        for (int e0 = 0; e0 < nsel * kChunk; e0 += kThreads * kCU) {
+            T raw[kCU];
 #pragma unroll
-            for (int h = 0; h < 2; ++h) {
-                const int i = c * kChunk + lane + 32 * h;
-                const uint32_t key = i < V ? ordered(as_float<T>(row[i])) : 0u;
+            for (int u = 0; u < kCU; ++u) {
+                const int e = e0 + u * kThreads + tid;
+                const int i = e < nsel * kChunk ? sh->selc[e / kChunk] * kChunk + (e % kChunk) : V;
+                if (i < V) raw[u] = row[i];
+            }
+#pragma unroll
+            for (int u = 0; u < kCU; ++u) {
+                const int e = e0 + u * kThreads + tid;
+                const int i = e < nsel * kChunk ? sh->selc[e / kChunk] * kChunk + (e % kChunk) : V;
+                const uint32_t key = i < V ? ordered(as_float<T>(raw[u])) : 0u;
                 const bool take = i < V && key >= vmin;
                 const unsigned int m = __ballot_sync(0xffffffffu, take);
                 unsigned int base = 0;
@@ -276,7 +299,7 @@ __global__ void __launch_bounds__(kThreads, 6) topk_ids_kernel(const T* __restri
         //    i.e. value desc, id asc)
         if (wid == 0) {
             const int n = (int)sh->ncand;
-            const unsigned long long kk = kth_largest_warp(cand, n, k, kIdBits);
+            const unsigned long long kk = kth_largest_warp(cand, n, k, kIdBits, kBf16);
             int s = 0;
             for (int base = 0; base < n; base += 32) {
                 const int i = base + lane;
