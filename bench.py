@@ -15,7 +15,7 @@ The only collectives are the barrier around the timed region and the max/sum of 
 
 ``--impl reference`` times the reference algorithm on the host cores instead: the CPU
 restatement under oracle/ (the reference itself is Python/Triton and cannot run on the GPU box)
-on a bounded sample of the same workload, with every host thread.
+on the same config's whole batch, with every host thread.
 """
 
 from __future__ import annotations
@@ -38,7 +38,6 @@ UNIT = "tokens/s"
 L2_FLUSH_BYTES = 256 << 20  # > 126 MB L2
 FALLBACK_HBM_GBS = 6650.0
 FALLBACK_BF16_TFLOPS = 1590.0
-REF_SAMPLE_REQUESTS = 16
 
 WORKLOADS = {
     "config1": "ragged continuous batch: 64 requests, verify length U{1..16}, V=151936, bf16 "
@@ -234,14 +233,14 @@ def run_reference(args):
     cores = host_cores()
     torch.set_num_threads(cores)
     batch = make_batch(args.config, 0, "cpu")
-    n = min(REF_SAMPLE_REQUESTS, batch.B)
+    n = batch.B  # the whole batch of this arm's config: every request, every row
     once, tokens = cpu_port_time(batch, n, nthreads=cores)
     for _ in range(args.warmup):
         once()
     times = [once() for _ in range(args.steps)]
     step_s = sum(times) / len(times)
     value = tokens / step_s
-    sample = (f"requests 0-{n - 1} of {args.config} ({tokens} verified tokens) per step, "
+    sample = (f"all {n} requests of {args.config} ({tokens} verified tokens) per step, "
               f"oracle port with {cores} OpenMP threads")
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT,
@@ -249,7 +248,7 @@ def run_reference(args):
         "ms_per_step": step_s * 1e3, "higher_is_better": True, "scaling": "weak",
         "vs_baseline": None, "dtype": "f32+i64", "data": "synthetic",
         "config": {"workload": f"{args.config}: {WORKLOADS[args.config]}",
-                   "sample_requests": n, "parallelism": "host cores"},
+                   "requests": n, "same_config": True, "parallelism": "host cores"},
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "port",
                          "sample": sample},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -1105,11 +1104,32 @@ def kernel_workload(name, dev):
             adjust_logits(x, info, None)
         # per element of the rows: the logit read and written; penalties and bias rows per request
         return launch, B * 16 * V * 4 + B * V * 12, "dsv_adjust_logits: 64 x 16 bf16 rows, every adjustment"
+    if name in ("coarse8", "fp8_step"):
+        from dspine_b200.layers.fp8 import coarse as C
+        rows, H, Vf = FP8_SHAPE
+        if name == "coarse8":
+            Vf = 32768  # the capture size: a 32768-row slice of the head (168 MB e4m3 > L2)
+        hidden = torch.randn(rows, H, generator=g, device=dev).to(torch.bfloat16)
+        w = (torch.randn(Vf, H, generator=g, device=dev) * 0.02).to(torch.bfloat16)
+        head = C.FullVFP8Coarse(torch, w)
+        del w
+        if name == "fp8_step":
+            def launch():
+                head.retrieve_and_rescore(hidden)
+            return launch, None, "FullVFP8Coarse.retrieve_and_rescore: 960 x 5120 hidden, V 248320"
+        xq, xs = C.quantize_rows(hidden)
+        wq, ws = head.weight8.view(torch.uint8), head.weight_scale.reshape(-1)
+
+        def launch():
+            C.coarse_scores(xq, xs, wq, ws)
+        # a tensor-core GEMM (2 x 960 x 32768 x 5120 = 322 GFLOP): no HBM roofline line
+        return launch, None, "dsv_fp8_coarse_scores: 960 x 5120 x 32768 e4m3"
     raise SystemExit(f"unknown kernel {name}")
 
 
 KERNELS = ("chain_probs", "sparse_accept", "compress", "target_probs", "sparse_target",
-           "serial_sample", "serial_table", "rescore16", "merge", "topk_ids", "adjust")
+           "serial_sample", "serial_table", "rescore16", "merge", "topk_ids", "adjust",
+           "coarse8", "fp8_step")
 
 
 def run_kernel(args):
