@@ -38,7 +38,11 @@
 namespace dsv {
 namespace tk {
 
-constexpr int kThreads = 128;              // six CTAs per SM: one row each, all rows in one wave
+// Threads per CTA: 128 when the row's shared memory allows six CTAs per SM (one row each, a
+// batch of rows in one wave), 256 for large k or long rows (at most two or three per SM).
+constexpr int kThreadsSmall = 128;
+constexpr int kThreadsLarge = 256;
+constexpr size_t kSmallSmemMax = 40 * 1024;
 constexpr int kChunk = 64;
 constexpr int kMaxChunks = 4096;           // vocabularies up to 262144
 constexpr int kMaxK = 128;                 // 64 for topk_ids, 128 for the ranked form
@@ -48,7 +52,7 @@ constexpr int kIdBits = 18;                // element id < 2^18
 // Dynamic shared memory: this head, then ck[nch] (chunk keys), then cand[k * 64] (compacted
 // chunk keys, then candidate keys), both sized by the launch's row length and k.
 struct Smem {
-    unsigned long long tmax[kThreads];     // thread t: max of chunk keys t, t + kThreads, ...
+    unsigned long long tmax[kThreadsLarge];  // thread t: max of chunk keys t, t + NT, ...
     unsigned long long selk[kMaxK];        // the selected candidate keys
     int selc[kMaxK];                       // the selected chunks, then the selected ids
     unsigned int ncand;
@@ -142,11 +146,11 @@ __device__ __forceinline__ unsigned long long kth_largest_warp(const unsigned lo
 }
 
 // Chunk maxima of one row into ck[0, nch): thread t of the CTA handles 16-byte vectors
-// t, t + kThreads, ... (kUnroll loads issued before any is used); the kTpc consecutive threads whose
+// t, t + NT, ... (kUnroll loads issued before any is used); the kTpc consecutive threads whose
 // vectors form one chunk combine their maxima by xor-shuffles.  vec_ok: the row start and pitch
 // are 16-byte aligned, so full vectors load as one uint4; the last, partial vector (and every
 // vector of an unaligned row) loads element by element within the row, NaN beyond it.
-template <typename T>
+template <typename T, int NT>
 __device__ __forceinline__ void chunk_maxima(const T* __restrict__ row, int V, bool vec_ok,
                                              unsigned long long* ck) {
     constexpr int kE = 16 / sizeof(T);          // values per vector
@@ -155,11 +159,11 @@ __device__ __forceinline__ void chunk_maxima(const T* __restrict__ row, int V, b
     const int tid = threadIdx.x;
     const int nvec = (V + kE - 1) / kE;
     const int nfull = V / kE;
-    for (int j0 = 0; j0 < nvec; j0 += kThreads * kUnroll) {
+    for (int j0 = 0; j0 < nvec; j0 += NT * kUnroll) {
         uint4 v[kUnroll];
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
-            const int j = j0 + u * kThreads + tid;
+            const int j = j0 + u * NT + tid;
             if (vec_ok && j < nfull) {
                 v[u] = __ldcs(reinterpret_cast<const uint4*>(row) + j);  // streaming: no L1 allocation
             } else {
@@ -174,7 +178,7 @@ __device__ __forceinline__ void chunk_maxima(const T* __restrict__ row, int V, b
         }
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
-            const int j = j0 + u * kThreads + tid;
+            const int j = j0 + u * NT + tid;
             uint32_t m = ordered(vec_max<T>(v[u]));
 #pragma unroll
             for (int o = 1; o < kTpc; o <<= 1) m = max(m, __shfl_xor_sync(0xffffffffu, m, o));
@@ -185,8 +189,8 @@ __device__ __forceinline__ void chunk_maxima(const T* __restrict__ row, int V, b
     }
 }
 
-template <typename T>
-__global__ void __launch_bounds__(kThreads, 6) topk_ids_kernel(const T* __restrict__ x, long long rows,
+template <typename T, int NT>
+__global__ void __launch_bounds__(NT, NT == kThreadsSmall ? 6 : 3) topk_ids_kernel(const T* __restrict__ x, long long rows,
                                                             int V, long long stride, int k,
                                                             bool vec_ok, bool ranked,
                                                             int64_t* __restrict__ out) {
@@ -200,11 +204,11 @@ __global__ void __launch_bounds__(kThreads, 6) topk_ids_kernel(const T* __restri
     for (long long r = blockIdx.x; r < rows; r += gridDim.x) {
         const T* row = x + r * stride;
         // 1. chunk maxima
-        chunk_maxima<T>(row, V, vec_ok, ck);
+        chunk_maxima<T, NT>(row, V, vec_ok, ck);
         __syncthreads();
         {
             unsigned long long t = 0ull;
-            for (int c = tid; c < nch; c += kThreads) t = max(t, ck[c]);
+            for (int c = tid; c < nch; c += NT) t = max(t, ck[c]);
             sh->tmax[tid] = t;
         }
         __syncthreads();
@@ -212,7 +216,7 @@ __global__ void __launch_bounds__(kThreads, 6) topk_ids_kernel(const T* __restri
         //    chunks (the ranked form only) keeps all of them and every element is a candidate
         const int nsel = nch < k ? nch : k;
         if (nch <= k) {
-            for (int c = tid; c < nch; c += kThreads) sh->selc[c] = c;
+            for (int c = tid; c < nch; c += NT) sh->selc[c] = c;
             if (tid == 0) {
                 sh->ncand = 0u;
                 sh->tmax[0] = 0ull;
@@ -222,7 +226,7 @@ __global__ void __launch_bounds__(kThreads, 6) topk_ids_kernel(const T* __restri
             // search runs over those (all chunk keys when they overflow the candidate buffer),
             // compacted by every warp (order is not kept: only the set matters)
             if (wid == 0) {
-                const unsigned long long lo = kth_largest_warp(sh->tmax, kThreads, k, kChunkBits, kBf16);
+                const unsigned long long lo = kth_largest_warp(sh->tmax, NT, k, kChunkBits, kBf16);
                 if (lane == 0) {
                     sh->selk[0] = lo;
                     sh->ncand = 0u;
@@ -231,7 +235,7 @@ __global__ void __launch_bounds__(kThreads, 6) topk_ids_kernel(const T* __restri
             __syncthreads();
             const unsigned long long lo = sh->selk[0];
             const int cap = k * kChunk;
-            for (int base = wid * 32; base < nch; base += kThreads) {
+            for (int base = wid * 32; base < nch; base += NT) {
                 const int i = base + lane;
                 const unsigned long long key = i < nch ? ck[i] : 0ull;
                 const bool take = i < nch && key >= lo;
@@ -266,21 +270,21 @@ __global__ void __launch_bounds__(kThreads, 6) topk_ids_kernel(const T* __restri
         }
         __syncthreads();
         // 3. candidates: elements of the selected chunks that reach the k-th chunk maximum.
-        //    Element e of the nsel chunks (chunk s = e / 64) goes to thread e % kThreads, kCU of
+        //    Element e of the nsel chunks (chunk s = e / 64) goes to thread e % NT, kCU of
         //    them per thread whose loads issue together (a row's candidates in one round trip).
         const uint32_t vmin = (uint32_t)(sh->tmax[0] >> 32);
         constexpr int kCU = 8;
-        for (int e0 = 0; e0 < nsel * kChunk; e0 += kThreads * kCU) {
+        for (int e0 = 0; e0 < nsel * kChunk; e0 += NT * kCU) {
             T raw[kCU];
 #pragma unroll
             for (int u = 0; u < kCU; ++u) {
-                const int e = e0 + u * kThreads + tid;
+                const int e = e0 + u * NT + tid;
                 const int i = e < nsel * kChunk ? sh->selc[e / kChunk] * kChunk + (e % kChunk) : V;
                 if (i < V) raw[u] = row[i];
             }
 #pragma unroll
             for (int u = 0; u < kCU; ++u) {
-                const int e = e0 + u * kThreads + tid;
+                const int e = e0 + u * NT + tid;
                 const int i = e < nsel * kChunk ? sh->selc[e / kChunk] * kChunk + (e % kChunk) : V;
                 const uint32_t key = i < V ? ordered(as_float<T>(raw[u])) : 0u;
                 const bool take = i < V && key >= vmin;
@@ -331,9 +335,9 @@ int topk_max_vocab() { return tk::kMaxChunks * tk::kChunk; }
 
 namespace {
 
-template <typename T>
-int launch_typed(const void* logits, long long rows, int V, long long stride, int k, bool vec_ok,
-                 bool ranked, int64_t* out, cudaStream_t st) {
+template <typename T, int NT>
+int launch_nt(const void* logits, long long rows, int V, long long stride, int k, bool vec_ok,
+              bool ranked, int64_t* out, size_t smem, cudaStream_t st) {
     // Per device: the dynamic shared memory opt-in (once, for the largest row and k) and the
     // resident CTAs for the last shared-memory size launched (re-queried when it changes).
     constexpr int kMaxDev = 64;
@@ -344,7 +348,6 @@ int launch_typed(const void* logits, long long rows, int V, long long stride, in
     };
     static Cache cache[kMaxDev] = {};
     static std::mutex mu;
-    const size_t smem = tk::smem_bytes(V, k);
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return kLaunchFailed;
     int blocks = 0;
@@ -352,7 +355,7 @@ int launch_typed(const void* logits, long long rows, int V, long long stride, in
         std::lock_guard<std::mutex> lock(mu);
         Cache& c = cache[dev];
         if (!c.ready) {
-            if (cudaFuncSetAttribute(tk::topk_ids_kernel<T>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            if (cudaFuncSetAttribute(tk::topk_ids_kernel<T, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                      (int)tk::smem_bytes(tk::kMaxChunks * tk::kChunk, tk::kMaxK)) != cudaSuccess)
                 return kLaunchFailed;
             c.ready = true;
@@ -360,7 +363,7 @@ int launch_typed(const void* logits, long long rows, int V, long long stride, in
         }
         if (c.smem != smem) {
             int per_sm = 0, sms = 0;
-            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tk::topk_ids_kernel<T>, tk::kThreads,
+            if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, tk::topk_ids_kernel<T, NT>, NT,
                                                               smem) != cudaSuccess ||
                 cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
                 per_sm < 1)
@@ -371,9 +374,21 @@ int launch_typed(const void* logits, long long rows, int V, long long stride, in
         blocks = c.blocks;
     }
     const unsigned grid = (unsigned)(rows < blocks ? rows : blocks);
-    tk::topk_ids_kernel<T><<<grid, tk::kThreads, smem, st>>>(static_cast<const T*>(logits), rows, V,
-                                                             stride, k, vec_ok, ranked, out);
+    tk::topk_ids_kernel<T, NT><<<grid, NT, smem, st>>>(static_cast<const T*>(logits), rows, V,
+                                                        stride, k, vec_ok, ranked, out);
     return cudaGetLastError() == cudaSuccess ? kOk : kLaunchFailed;
+}
+
+template <typename T>
+int launch_typed(const void* logits, long long rows, int V, long long stride, int k, bool vec_ok,
+                 bool ranked, int64_t* out, cudaStream_t st) {
+    const size_t smem = tk::smem_bytes(V, k);
+    // 128-thread CTAs where six fit an SM (794 x 151936, k = 16: 0.070 ms against 0.100 with
+    // 256); 256 threads where shared memory allows only two or three (ranked top-128 of
+    // 960 x 248320: 255 us against 387 with 128)
+    return smem <= tk::kSmallSmemMax
+               ? launch_nt<T, tk::kThreadsSmall>(logits, rows, V, stride, k, vec_ok, ranked, out, smem, st)
+               : launch_nt<T, tk::kThreadsLarge>(logits, rows, V, stride, k, vec_ok, ranked, out, smem, st);
 }
 
 int launch_any(const void* logits, int dtype, long long rows, int V, long long stride, int k,
