@@ -84,6 +84,8 @@ def parse_args():
                    help="time one library kernel alone (the workloads of the ncu summaries)")
     p.add_argument("--no-tp-head", action="store_true",
                    help="at N > 1, skip the config-3 TP head timed beside the replicas")
+    p.add_argument("--no-other-configs", action="store_true",
+                   help="at N = 1, skip configs 0, 4, 2 and the FP8 head measured after config 1")
     return p.parse_args()
 
 
@@ -411,7 +413,8 @@ def run_dspine(args):
     if rank == 0:
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(batch)
-        print(json.dumps(line), flush=True)
+        return line
+    return None
 
 
 def cpu_baseline(batch):
@@ -737,7 +740,8 @@ def run_head(args):
                                     "kind": "port",
                                     "sample": f"{n_rows} rows x full vocab: torch CPU matmul + "
                                               f"topk + logsumexp, {cores} threads"}
-        print(json.dumps(line), flush=True)
+        return line
+    return None
 
 
 def fp8_cpu_time(n_rows, cores, vocab=None):
@@ -897,7 +901,7 @@ def run_fp8(args):
     }
     if cpu is not None:
         line["cpu_baseline"] = cpu
-    print(json.dumps(line), flush=True)
+    return line
 
 
 def run_fp8_reference(args):
@@ -1164,19 +1168,56 @@ def run_kernel(args):
     print(json.dumps(line), flush=True)
 
 
+def other_configs(args):
+    """The plan's other configurations measured in the same run (one GPU): configs 0 and 4 of
+    the verification, the fused LM head (config 2) and the FP8 head, each with its own metric
+    (20 timed steps, 3 warm-up steps, no CPU leg)."""
+    import copy
+    out = {}
+    for name in ("config0", "config4", "config2", "fp8"):
+        a = copy.copy(args)
+        a.config, a.steps, a.warmup = name, 20, 3
+        a.no_cpu_baseline = a.no_tp_head = True
+        try:
+            if name == "fp8":
+                line = run_fp8(a)
+            elif name in HEAD_SHAPES:
+                line = run_head(a)
+            else:
+                line = run_dspine(a)
+        except Exception as e:  # one failed extra must not lose the headline line
+            out[name] = {"error": repr(e)[:200]}
+            continue
+        roof = line.get("roofline") or {}
+        metric = line["metric"] if name in HEAD_SHAPES or name == "fp8" else \
+            f"verified draft tokens/s, {name} ({line['config']['requests_per_gpu']} requests, V={VOCAB})"
+        out[name] = {"metric": metric, "value": line["value"], "unit": line["unit"],
+                     "ms_per_step": line["ms_per_step"], "e2e": line["e2e"]["value"],
+                     "roofline": {k: roof.get(k) for k in ("bound", "achieved", "peak", "unit",
+                                                           "frac")},
+                     "clocks": line.get("clocks"), "workload": line["config"]["workload"]}
+    return out
+
+
 def main():
     args = parse_args()
     if args.kernel:
         run_kernel(args)
         return
+    line = None
     if args.config == "fp8":
-        run_fp8_reference(args) if args.impl == "reference" else run_fp8(args)
+        run_fp8_reference(args) if args.impl == "reference" else (line := run_fp8(args))
     elif args.config in HEAD_SHAPES:
-        run_head_reference(args) if args.impl == "reference" else run_head(args)
+        run_head_reference(args) if args.impl == "reference" else (line := run_head(args))
     elif args.impl == "reference":
         run_reference(args)
     else:
-        run_dspine(args)
+        line = run_dspine(args)
+        if (line is not None and args.config == "config1" and dist_env()[2] == 1
+                and not args.no_other_configs):
+            line["other_configs"] = other_configs(args)
+    if line is not None:
+        print(json.dumps(line), flush=True)
 
 
 if __name__ == "__main__":
