@@ -314,6 +314,7 @@ def run_dspine(args):
     starts = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     ends = [torch.cuda.Event(enable_timing=True) for _ in range(args.steps)]
     launches0 = lib.dsv_launch_count()
+    read0 = ws.bytes_read()
     sampler = ClockSampler(dev)
     barrier()
     with sampler:
@@ -324,6 +325,7 @@ def run_dspine(args):
             ends[i].record()
         barrier()
     launches = lib.dsv_launch_count() - launches0
+    bytes_read = (ws.bytes_read() - read0) / args.steps  # per launch (bf16 streaming path)
     step_ms = [s.elapsed_time(e) for s, e in zip(starts, ends)]
     total_ms = sum(step_ms)
     tokens = batch.verified_tokens()
@@ -379,8 +381,12 @@ def run_dspine(args):
     line = None
     if rank == 0:
         alg_bytes = batch.algorithmic_bytes()
+        # the bf16 path drops rows that cannot change an outcome: the roofline is taken on the
+        # bytes it read (counted by the kernel); the fp32 cluster path reads every row
+        read_bytes = bytes_read if bytes_read > 0 else float(alg_bytes)
+        deciding = batch.deciding_bytes(out[0])
         kernel_ms = statistics.mean(step_ms)
-        achieved = alg_bytes / (kernel_ms * 1e-3) / 1e9
+        achieved = read_bytes / (kernel_ms * 1e-3) / 1e9
         peak, peak_src = measured_hbm_peak()
         traffic, traffic_kernels = profiled_traffic(args.config)
         line = {
@@ -402,7 +408,12 @@ def run_dspine(args):
                          "frac": achieved / peak, "traffic": traffic,
                          "traffic_kernels": traffic_kernels, "peak_source": peak_src,
                          "kernel": "dsv::rows_kernel (the whole dsv_verify_logits call: rows and chain tasks)",
+                         "bytes_read_per_launch": read_bytes,
                          "algorithmic_bytes_per_launch": alg_bytes,
+                         "deciding_bytes_per_launch": deciding,
+                         "bytes_basis": "rows read (rows that cannot change an outcome are "
+                                        "dropped; all rows of the batch: algorithmic_bytes, "
+                                        "rows the outcome depends on: deciding_bytes)",
                          "kernel_ms": kernel_ms},
         }
         if tp_head is not None:

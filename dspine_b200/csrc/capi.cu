@@ -94,6 +94,18 @@ int dsv_workspace_error(void* ws, uint32_t* err, dsv_stream_t stream) {
     return DSV_OK;
 }
 
+int dsv_workspace_bytes_read(const void* ws, uint64_t* bytes, dsv_stream_t stream) {
+    if (ws == nullptr || bytes == nullptr) return DSV_BAD_POINTER;
+    const dsv::WsHeader* h = reinterpret_cast<const dsv::WsHeader*>(ws);
+    unsigned long long v = 0;
+    if (cudaMemcpyAsync(&v, &h->bytes_read, sizeof(v), cudaMemcpyDeviceToHost, (cudaStream_t)stream) !=
+        cudaSuccess)
+        return DSV_LAUNCH_FAILED;
+    if (cudaStreamSynchronize((cudaStream_t)stream) != cudaSuccess) return DSV_LAUNCH_FAILED;
+    *bytes = v;
+    return DSV_OK;
+}
+
 int dsv_verify_logits_ex(int32_t batch, int32_t vocab, int32_t dtype, const int64_t* candidates,
                          const void* target_logits, const int64_t* target_row,
                          int64_t target_rows, const void* draft_logits, const int64_t* draft_row,

@@ -28,6 +28,11 @@ struct WsHeader {
     unsigned int next2;      // row kernel: greedy-row counter
     unsigned int ready_tail; // row kernel: requests published to the ready list
     unsigned int chain_next; // row kernel: chain tasks taken
+    unsigned int pad_;
+    unsigned long long bytes_read;  // row kernel: logit bytes read from memory by the rows'
+                                    // first passes, summed over launches (never reset by a
+                                    // launch; verification drops rows that cannot change an
+                                    // outcome, so this is what was read)
 };
 static_assert(sizeof(WsHeader) <= 64, "workspace header");
 
@@ -61,7 +66,8 @@ constexpr inline size_t verify_gmax_offset(int B) {
 constexpr inline size_t verify_order_offset(int B) {
     return verify_gmax_offset(B) + (size_t)B * 16 * sizeof(unsigned long long);
 }
-// [u32 x 2 x B]: streaming path: rows finished per request (reset after use), accepted length
+// [u32 x 2 x B]: streaming path: per request its rows done and its chain steps decided (reset
+// by the last CTA of each launch)
 constexpr inline size_t verify_racc_offset(int B) {
     return verify_order_offset(B) + (((size_t)B * 4 + 63) & ~(size_t)63);
 }

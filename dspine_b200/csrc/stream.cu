@@ -1,22 +1,31 @@
 // stream.cu -- streaming verification of bf16 logit rows (sm_100a).
 //
-// Two kernels replace the reference's build_dspine_target_probs + chain rejection
+// One persistent kernel replaces the reference's build_dspine_target_probs + chain rejection
 // (runtime/worker.py:440-508, sampling/rejection.py:12-153) for bf16 logits:
 //
 //   rows_kernel   one CTA per logit row (a target row, or the draft row of a sampled request);
-//                 rows are handed out by a global counter, most expensive first.  The CTA
-//                 streams its row through a shared-memory ring filled by cp.async.bulk copies
-//                 and computes the row's descriptor: max, exact 2^-40 fixed-point softmax sum,
-//                 and the kept set of the joint top-k / top-p filter as (boundary key, tie cut).
-//                   pass 1  bf16x2 max (greedy rows: and the first index of the max) -- HBM
-//                   pass 2  exp + fixed-point split with packed f32x2 FMA, and either the
-//                           candidate window (top-k <= 256) or 24 y-bins with exact masses in
-//                           thread-private shared accumulators                       -- L2
-//                   then, binned rows only: per-key counts of the boundary bin (sub-bins first
-//                   when it spans many keys) and the tie cut in index order
-//   chain_kernel  one 8-CTA cluster per request: the capped chain from the descriptors (one
-//                 logit load per step), the residual (p - q)+ draw over target row a and draft
-//                 row a, the five outputs and, for the last request, the accept-compact.
+//                 rows are handed out by a global counter in verify-position order (every
+//                 request's position 0, then position 1, ...; the rows of the first positions
+//                 as two halves on two CTAs).  The CTA streams its row through a shared-memory
+//                 ring filled by cp.async.bulk copies and computes the row's descriptor: max,
+//                 exact 2^-40 fixed-point softmax sum, and the kept set of the joint top-k /
+//                 top-p filter as (boundary key, tie cut).  The CTA that completes a position
+//                 decides that chain step; a chain stops at its first rejected step, so rows
+//                 after a known rejection (or of a request whose outcome is known) are dropped
+//                 when dequeued or abandoned during their first pass: they cannot change any
+//                 output.  Outputs are those of processing every row, bit for bit.
+//                   nucleus and keep-all rows: one pass from HBM counts every bf16 key of the
+//                           row in a per-key histogram (2^-20 <= |v| < 2^12; the rare values
+//                           outside it fall back to the passes below), then S and the kept-set
+//                           walk come from the counts (one packed exp per key, not per element)
+//                           and the tie cut in index order re-reads the row from L2
+//                   other rows: bf16x2 max pass from HBM (greedy rows: and the first index of
+//                           the max; they finish here), then the candidate window (top-k <= 256)
+//                           or exact count walks from the top, from L2
+//   chain tasks   (in the same persistent kernel) kCP CTAs per sampled request once its
+//                 outcome is known: the residual (p - q)+ draw over target row a and draft row a
+//                 of the stopping position a, the five outputs and, for the last request, the
+//                 accept-compact.
 //
 // Arithmetic is the canonical one of dsv_common.cuh (exp2c, fix, scale_floor), so the result
 // equals the CPU oracle bit for bit.  Bulk passes clamp y at -64 before the exponent trick:
@@ -203,53 +212,101 @@ __device__ int request_cat(const VerifyArgs& a, int b, float& c_out, int wink) {
     return kBinned;                           // pure top-k, large k: exact counts from the top
 }
 
-// The task table of a launch: per class g (binned, keep-all/window, greedy) the prefix sums
-// pre(g, b) of the rows of requests < b, and per request its class and cap.  It lives in
-// shared memory after the row kernel's fixed state, sized by the batch.
+// The task table of a launch, identical in every CTA.  Row tasks are ordered by verify
+// position first: the position-0 rows of every request, then position 1, and so on, so that
+// the rows that decide the chains (a chain stops at its first rejected step) come first and
+// the later rows of a request can be dropped once its outcome is known.  Within a position:
+// binned target rows, binned draft rows, keep-all/window target rows, their draft rows,
+// greedy target rows.  Each class lists its requests by decreasing cap (a stable counting
+// sort), so the requests with a row at position s are a prefix of the class list: n(g, s) of
+// them (cap > s), and n(g, s + 1) of them have a draft row there.
 struct Plan {
-    uint16_t* pre_;  // [3][B + 1]
-    uint8_t* req;    // [B]
+    uint32_t* key;   // [48]: per (class, cap) counts, then scatter bases (build only)
+    uint16_t* perm;  // [B]: class 0 requests, class 1, class 2, each by decreasing cap
+    uint16_t* n;     // [3][17]: requests of class g with cap > s
+    uint16_t* pos;   // [17]: first row task of position s; pos[16] = row tasks
+    uint16_t* gs;    // [4]: start of class g in perm
+    uint8_t* req;    // [B]: cat | cap << 3
     int B;
-    __device__ __forceinline__ uint16_t& pre(int g, int b) const { return pre_[g * (B + 1) + b]; }
+    __device__ __forceinline__ int cnt(int g, int s) const { return n[g * 17 + s]; }
 };
+constexpr int kPlanFixed = 48 * 4 + (3 * 17 + 17 + 4) * 2;  // bytes besides the [B] arrays
 __host__ __device__ constexpr size_t plan_bytes(int B) {
-    return ((size_t)3 * (B + 1) * 2 + (size_t)B + 15) & ~(size_t)15;
+    return ((size_t)kPlanFixed + (size_t)B * 2 + (size_t)B + 15) & ~(size_t)15;
+}
+__device__ __forceinline__ Plan plan_at(unsigned char* base, int B) {
+    Plan p;
+    p.key = reinterpret_cast<uint32_t*>(base);
+    p.n = reinterpret_cast<uint16_t*>(base + 48 * 4);
+    p.pos = p.n + 3 * 17;
+    p.gs = p.pos + 17;
+    p.perm = p.gs + 4;
+    p.req = reinterpret_cast<uint8_t*>(p.perm + B);
+    p.B = B;
+    return p;
 }
 
-// every CTA builds the same task table: binned rows first, then keep-all/window, then greedy
 template <typename Sm>
 __device__ void build_plan(const VerifyArgs& a, Sm* sh, int wink) {
-    const int tid = threadIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31;
+    const Plan& P = sh->plan;
+    for (int i = tid; i < 48; i += blockDim.x) P.key[i] = 0u;
+    __syncthreads();
     for (int b = tid; b < a.B; b += blockDim.x) {
         const int cap = clamp_cap(a.caps ? a.caps[b] : a.cap_all);
         float c;
         const int cat = request_cat(a, b, c, wink);
-        sh->plan.req[b] = (uint8_t)(cat | (cap << 3));
+        P.req[b] = (uint8_t)(cat | (cap << 3));
+        const int g = cat == kBinned ? 0 : (cat == kGreedy ? 2 : 1);
+        atomicAdd(&P.key[g * 16 + cap - 1], 1u);
     }
     __syncthreads();
     if (tid < 32) {
-        int run[3] = {0, 0, 0};
-        for (int b0 = 0; b0 < a.B; b0 += 32) {
-            const int b = b0 + tid;
-            int n[3] = {0, 0, 0};
-            if (b < a.B) {
-                const int cat = (int)(sh->plan.req[b] & 7u);
-                const int cap = (int)(sh->plan.req[b] >> 3);
-                const int rows = cap + ((cat != kGreedy && a.drf != nullptr) ? cap - 1 : 0);
-                const int g = cat == kBinned ? 0 : (cat == kGreedy ? 2 : 1);
-                n[g] = rows;
-            }
-#pragma unroll
-            for (int g = 0; g < 3; ++g) {
-                const int inc = (int)warp_incl_u32((uint32_t)n[g]);
-                if (b < a.B) sh->plan.pre(g, b + 1) = (uint16_t)(run[g] + inc);
-                run[g] += __shfl_sync(0xffffffffu, inc, 31);
+        if (lane < 3) {
+            // n(g, s) = requests of class g with cap >= s + 1
+            uint32_t acc = 0;
+            P.n[lane * 17 + 16] = 0;
+            for (int s = 15; s >= 0; --s) {
+                acc += P.key[lane * 16 + s];
+                P.n[lane * 17 + s] = (uint16_t)acc;
             }
         }
-        if (tid == 0) {
-            sh->plan.pre(0, 0) = 0;
-            sh->plan.pre(1, 0) = 0;
-            sh->plan.pre(2, 0) = 0;
+        __syncwarp();
+        if (lane == 0) {
+            P.gs[0] = 0;
+            P.gs[1] = P.n[0];
+            P.gs[2] = (uint16_t)(P.n[0] + P.n[17]);
+            P.gs[3] = (uint16_t)a.B;
+            const int dr = a.drf != nullptr ? 1 : 0;
+            uint32_t t = 0;
+            for (int s = 0; s < 16; ++s) {
+                P.pos[s] = (uint16_t)t;
+                t += P.cnt(0, s) + dr * P.cnt(0, s + 1) + P.cnt(1, s) + dr * P.cnt(1, s + 1) + P.cnt(2, s);
+            }
+            P.pos[16] = (uint16_t)t;
+        }
+        __syncwarp();
+        if (lane < 3) {
+            // first slot of each (class, cap) in perm: caps above it come first
+            for (int cp = 1; cp <= 16; ++cp) P.key[lane * 16 + cp - 1] = P.gs[lane] + P.n[lane * 17 + cp];
+        }
+        __syncwarp();
+        for (int b0 = 0; b0 < a.B; b0 += 32) {
+            const int b = b0 + lane;
+            int k = 64 + lane;  // no class: a key of its own
+            if (b < a.B) {
+                const int cat = (int)(P.req[b] & 7u), cap = (int)(P.req[b] >> 3);
+                k = (cat == kBinned ? 0 : (cat == kGreedy ? 2 : 1)) * 16 + cap - 1;
+            }
+            const unsigned peers = __match_any_sync(0xffffffffu, k);
+            const int rank = __popc(peers & ((1u << lane) - 1u));
+            const uint32_t base = b < a.B ? P.key[k] : 0u;
+            __syncwarp();
+            if (b < a.B) {
+                P.perm[base + rank] = (uint16_t)b;
+                if (rank == 0) P.key[k] = base + (uint32_t)__popc(peers);
+            }
+            __syncwarp();
         }
     }
     __syncthreads();
@@ -257,30 +314,30 @@ __device__ void build_plan(const VerifyArgs& a, Sm* sh, int wink) {
 
 template <typename Sm>
 __device__ int total_tasks(const VerifyArgs& a, const Sm* sh) {
-    return sh->plan.pre(0, a.B) + sh->plan.pre(1, a.B) + sh->plan.pre(2, a.B);
+    (void)a;
+    return sh->plan.pos[16];
 }
 
 template <typename Sm>
 __device__ TaskInfo decode_task(const VerifyArgs& a, const Sm* sh, int t) {
-    int g = 0;
-    int local = t;
-    while (g < 2 && local >= sh->plan.pre(g, a.B)) {
-        local -= sh->plan.pre(g, a.B);
-        ++g;
+    const Plan& P = sh->plan;
+    int s = 0;
+    while (s < 15 && (int)P.pos[s + 1] <= t) ++s;
+    int j = t - (int)P.pos[s];
+    const int dr = a.drf != nullptr ? 1 : 0;
+    const int seg[5] = {P.cnt(0, s), dr * P.cnt(0, s + 1), P.cnt(1, s), dr * P.cnt(1, s + 1), P.cnt(2, s)};
+    int q = 0;
+    while (q < 4 && j >= seg[q]) {
+        j -= seg[q];
+        ++q;
     }
-    // largest b with pre[g][b] <= local
-    int lo = 0, hi = a.B - 1;
-    while (lo < hi) {
-        const int mid = (lo + hi + 1) >> 1;
-        if (sh->plan.pre(g, mid) <= local) lo = mid; else hi = mid - 1;
-    }
+    const int g = q >> 1;
     TaskInfo ti;
-    ti.b = lo;
-    const int r = local - sh->plan.pre(g, lo);
-    ti.cat = (int)(sh->plan.req[lo] & 7u);
-    ti.cap = (int)(sh->plan.req[lo] >> 3);
-    ti.kind = r < ti.cap ? 0 : 1;
-    ti.s = ti.kind == 0 ? r : r - ti.cap;
+    ti.b = P.perm[P.gs[g] + j];
+    ti.kind = q & 1;
+    ti.s = s;
+    ti.cat = (int)(P.req[ti.b] & 7u);
+    ti.cap = (int)(P.req[ti.b] >> 3);
     const long long base = ti.kind == 0 ? (a.tgt_row ? a.tgt_row[ti.b] : ti.b * a.row_step)
                                         : a.drf_row[ti.b];
     const long long lim = ti.kind == 0 ? a.tgt_rows : a.drf_rows;
@@ -425,6 +482,10 @@ __device__ void key_range(int target, uint32_t kmin, uint32_t kmax, float m, flo
 #ifndef DSV_RING_VECS
 #define DSV_RING_VECS (2 * DSV_ROWS_THREADS)
 #endif
+#ifndef DSV_SPLIT_POS
+#define DSV_SPLIT_POS 2  // verification splits the rows of the first DSV_SPLIT_POS positions
+#endif
+constexpr int kSplitPos = DSV_SPLIT_POS;
 constexpr int kRT = DSV_ROWS_THREADS;  // threads per CTA
 constexpr int kRW = kRT / 32;          // warps
 constexpr int kRWinK = kRT < 256 ? kRT : 256;  // top-k rows with k <= this select in a window
@@ -467,13 +528,20 @@ struct RSmem {
     alignas(16) uint4 ring[kRingS][kRingCW];  // streaming ring filled by bulk copies
     Plan plan;                     // task table (after this struct in shared memory)
     int q_nchain;                  // task sources: chain tasks of the launch
-    int q_sel_empty, q_gr_empty;   //               selection / greedy queues exhausted
+    int q_sel_empty;               //               row queue exhausted
     int q_kind, q_b;               //               this task's kind and chain request
 #ifdef DSV_PROFILE
     uint32_t prof_ph[16];          // profiling builds: phase durations of the current task
 #endif
     int task;
     int first_min;
+    int fin_claim;                 // row_finish: 1 + accepted length of a claimed request
+    int exit_last;                 // this CTA is the last out of the launch
+    int watch_b, watch_s;          // the row's request and position while its first pass may
+                                   // be abandoned (watch_s < 0: not watched)
+    int abort_row;                 // the first pass was abandoned: the row cannot change an outcome
+    int stream_end;                // chunks of the current stream that were issued
+    uint32_t hbm_vecs;             // 16-byte vectors the row's first pass read from memory
     uint32_t nlist;
     uint32_t red32[kRedN];
     unsigned long long red64[kRedN];
@@ -503,6 +571,39 @@ static_assert(DSV_ROWS_MIN_CTAS * (sizeof(RSmem) + plan_bytes(64) + 1024) <= 228
               "row kernel shared memory (batches up to 64 at the intended occupancy)");
 static_assert(2 * kRWinCap * 4 <= kHCap * 4 && kRWinCap * 8 <= kRingS * kRingCW * 16,
               "window candidates fit the histogram, the ranked list the ring");
+
+// Per-request progress of a verification launch, two words of the workspace (zeroed by the
+// last CTA out of each launch):
+//   racc[2 b]      rows done: bit s = target row s, bit 16 + s = draft row s
+//   racc[2 b + 1]  chain steps: bit s (s < 15) = step s accepted, bit 16 + s = step s rejected,
+//                  bit 15 = the last target row (cap - 1) is done, bit 31 = outcome claimed
+constexpr uint32_t kStepLast = 1u << 15;
+constexpr uint32_t kClaimed = 1u << 31;
+
+// accepted length of a request from its step word, or -1 while it is not known: the first
+// rejected step r once steps 0..r-1 are all accepted, or cap - 1 once every step is accepted
+// and the last target row is done
+__device__ __forceinline__ int outcome_of(uint32_t w, int cap) {
+    const uint32_t rej = (w >> 16) & 0x7FFFu, ok = w & 0x7FFFu;
+    if (rej) {
+        const int r = __ffs(rej) - 1;
+        const uint32_t m = (1u << r) - 1u;
+        return (ok & m) == m ? r : -1;
+    }
+    const uint32_t m = (1u << (cap - 1)) - 1u;
+    return ((ok & m) == m && (w & kStepLast)) ? cap - 1 : -1;
+}
+
+// Whether row (b, s) can still change the outcome: not once the outcome is claimed, nor when
+// a step before s is known to be rejected (the chain stops there; rows after it are never
+// read).  Both only become true over time, so a row found unneeded stays unneeded.
+__device__ __forceinline__ bool row_needed(const VerifyArgs& a, int b, int s) {
+    if (a.cand == nullptr) return true;
+    const uint32_t w = *(volatile const uint32_t*)&a.racc[2 * b + 1];
+    if (w & kClaimed) return false;
+    const uint32_t rej = (w >> 16) & 0x7FFFu;
+    return rej == 0u || s <= __ffs(rej) - 1;
+}
 
 struct RowGeo {
     const uint16_t* rowp;
@@ -555,9 +656,12 @@ struct Ring {
 // vectors in flight with bulk copies (one mbarrier per slot, bounded waits); every thread
 // handles vectors tid and tid + kRT of each chunk.  All threads must call it.
 template <bool kBig = false, typename F>
-__device__ __forceinline__ void stream_row(RSmem* sh, const VerifyArgs& a, const RowGeo& g, int V,
-                                           F&& fn, int vb = 0, int ve = -1) {
-    // vectors [vb, ve) of the row (default: all); fn sees row-global vector indices
+__device__ __forceinline__ int stream_row(RSmem* sh, const VerifyArgs& a, const RowGeo& g, int V,
+                                          F&& fn, int vb = 0, int ve = -1) {
+    // vectors [vb, ve) of the row (default: all); fn sees row-global vector indices.  While
+    // the row is watched (watch_s >= 0), thread 0 checks every 8 chunks whether it can still
+    // change an outcome; if not, no further chunk is issued, the ones in flight are drained
+    // unprocessed and abort_row is set.  Returns the vectors read.
     const Ring<kBig> R(sh);
     constexpr int S = Ring<kBig>::S;
     constexpr int CW = Ring<kBig>::CW;
@@ -567,6 +671,7 @@ __device__ __forceinline__ void stream_row(RSmem* sh, const VerifyArgs& a, const
     const int nvr = ve - vb;
     const int nch = (nvr + CW - 1) / CW;
     const uint32_t base = *R.cnt;  // uniform: read before any thread updates it
+    if (tid == 0) sh->stream_end = nch;
     __syncthreads();
     if (tid == 0) {
         for (int c = 0; c < nch && c < S; ++c) {
@@ -585,23 +690,38 @@ __device__ __forceinline__ void stream_row(RSmem* sh, const VerifyArgs& a, const
         }
         const int v0 = c * CW;
         const int nvec = min(CW, nvr - v0);
+        if (!sh->abort_row) {
 #pragma unroll
-        for (int u = 0; u < CW / kRT; ++u) {
-            const int i = tid + u * kRT;
-            if (i < nvec) fn(row_vec(g, V, nullptr, vb + v0 + i, R.slot(slot)[i]), vb + v0 + i);
+            for (int u = 0; u < CW / kRT; ++u) {
+                const int i = tid + u * kRT;
+                if (i < nvec) fn(row_vec(g, V, nullptr, vb + v0 + i, R.slot(slot)[i]), vb + v0 + i);
+            }
         }
         __syncthreads();  // the slot is consumed
-        if (tid == 0 && c + S < nch) {
-            const int cn = c + S;
-            const int nv2 = min(CW, nvr - cn * CW);
-            fence_proxy_async_smem();
-            mbar_arrive_expect_tx(&R.bar[slot], (uint32_t)nv2 * 16u);
-            bulk_g2s(R.slot(slot), src + (size_t)cn * CW * 16, (uint32_t)nv2 * 16u, &R.bar[slot]);
+        // every thread sees the same stream_end here: thread 0 changes it only after this
+        // barrier, and to a value the next iteration cannot reach
+        if (c + 1 >= sh->stream_end) break;
+        if (tid == 0) {
+            if (sh->watch_s >= 0 && !sh->abort_row && (c & 7) == 7 &&
+                !row_needed(a, sh->watch_b, sh->watch_s)) {
+                sh->abort_row = 1;
+                sh->stream_end = min(nch, c + S);  // chunks c + 1 .. c + S - 1 are in flight
+            }
+            if (!sh->abort_row && c + S < nch) {
+                const int cn = c + S;
+                const int nv2 = min(CW, nvr - cn * CW);
+                fence_proxy_async_smem();
+                mbar_arrive_expect_tx(&R.bar[slot], (uint32_t)nv2 * 16u);
+                bulk_g2s(R.slot(slot), src + (size_t)cn * CW * 16, (uint32_t)nv2 * 16u, &R.bar[slot]);
+            }
         }
     }
     __syncthreads();
-    if (tid == 0) *R.cnt = base + (uint32_t)nch;
+    const int issued = sh->stream_end;
     __syncthreads();
+    if (tid == 0) *R.cnt = base + (uint32_t)issued;
+    __syncthreads();
+    return min(nvr, issued * CW);
 }
 
 __device__ __forceinline__ unsigned long long rcta_sum_u64(unsigned long long v, RSmem* sh) {
@@ -973,7 +1093,14 @@ __device__ uint32_t split_merge(RSmem* sh, const VerifyArgs& a, int slot, uint32
     return mk1 > mkey ? mk1 : mkey;
 }
 
-__device__ void process_row(RSmem* sh, const VerifyArgs& a, const TaskInfo& ti) {
+// Nucleus and keep-all rows start with the fixed-range histogram (one pass, no max pass) and
+// are the ones split in halves; sequential-mode nucleus rows with a top-k take the max pass
+__device__ __forceinline__ bool row_onepass(const VerifyArgs& a, const TaskInfo& ti) {
+    const bool seq_k = a.mode == kModeSeq && ti.k < a.V && ti.p < 1.0f;
+    return ti.cat == kKeepAll || (ti.cat == kBinned && ti.p < 1.0f && !seq_k);
+}
+
+__device__ void process_row_body(RSmem* sh, const VerifyArgs& a, const TaskInfo& ti) {
     const int tid = threadIdx.x, lane = tid & 31, wid = tid >> 5;
     const int V = a.V;
     PROF_START();
@@ -986,7 +1113,7 @@ __device__ void process_row(RSmem* sh, const VerifyArgs& a, const TaskInfo& ti) 
     // sequential-mode nucleus rows with a top-k need the top-k's mass before the histogram
     // walk (counts from the top, which reuse the histogram's storage): they take the max pass
     const bool seq_k = a.mode == kModeSeq && ti.k < V && ti.p < 1.0f;
-    const bool onepass = ti.cat == kKeepAll || (ti.cat == kBinned && ti.p < 1.0f && !seq_k);
+    const bool onepass = row_onepass(a, ti);
     if (ti.half == 0 && !onepass) return;  // only one-pass rows are split: the second half does all
     const int half = onepass ? ti.half : -1;
     uint32_t tkey = 0, mkey = 0;
@@ -1069,7 +1196,12 @@ __device__ void process_row(RSmem* sh, const VerifyArgs& a, const TaskInfo& ti) 
                 }
             }
         };
-        stream_row(sh, a, g, V, hist_fn, hb, he);
+        const int nread = stream_row(sh, a, g, V, hist_fn, hb, he);
+        if (tid == 0) {
+            sh->hbm_vecs = (uint32_t)nread;
+            sh->watch_s = -1;  // later passes run from L2 and are short: not abandoned
+        }
+        if (sh->abort_row) return;  // the row can no longer change an outcome
         {
             const uint32_t k0 = okey(vmax2 & 0xFFFFu), k1 = okey(vmax2 >> 16);
             tkey = k0 > k1 ? k0 : k1;
@@ -1115,7 +1247,12 @@ __device__ void process_row(RSmem* sh, const VerifyArgs& a, const TaskInfo& ti) 
                 }
             }
         };
-        stream_row<true>(sh, a, g, V, max_fn);
+        const int nread = stream_row<true>(sh, a, g, V, max_fn);
+        if (tid == 0) {
+            if (!onepass) sh->hbm_vecs = (uint32_t)nread;
+            sh->watch_s = -1;
+        }
+        if (sh->abort_row) return;
         PROF_MARK(ti.cat, 0);
         const uint32_t wk = __reduce_max_sync(0xffffffffu, tkey);
         if (lane == 0) sh->red32[wid] = wk;
@@ -1129,8 +1266,9 @@ __device__ void process_row(RSmem* sh, const VerifyArgs& a, const TaskInfo& ti) 
             __syncthreads();
             if (tid == 0) {
                 const int f = sh->first_min;
-                if (f != 0x7fffffff)
-                    a.gmax[ti.b * kT + ti.s] = ((unsigned long long)mkey << 32) | (0xFFFFFFFFull - (unsigned)f);
+                // always written (0: no finite maximum), so no value of an earlier launch is read
+                a.gmax[ti.b * kT + ti.s] =
+                    f == 0x7fffffff ? 0ull : (((unsigned long long)mkey << 32) | (0xFFFFFFFFull - (unsigned)f));
                 put_desc(a, ti, bf(key_bits(mkey)), mkey, f, 1ull << kFixBits, f == 0x7fffffff ? 0 : f,
                          kDescGreedy);
             }
@@ -1505,6 +1643,14 @@ __device__ void process_row(RSmem* sh, const VerifyArgs& a, const TaskInfo& ti) 
     PROF_END(ti.cat, 8);
 }
 
+// One row task (all threads); returns the bytes its first pass read from memory (the later
+// passes re-read the row from L2).  abort_row is set if the row was abandoned.
+__device__ unsigned long long process_row(RSmem* sh, const VerifyArgs& a, const TaskInfo& ti) {
+    process_row_body(sh, a, ti);
+    __syncthreads();
+    return (unsigned long long)sh->hbm_vecs * 16ull;
+}
+
 // a row descriptor written by another CTA of this launch (L2, not a stale L1 line)
 __device__ __forceinline__ RowDesc load_desc_cg(const RowDesc* p) {
     static_assert(sizeof(RowDesc) == 32, "row descriptor: two 16-byte words");
@@ -1561,7 +1707,7 @@ static_assert(kCP <= 32 && kCTW <= 8, "per-warp slice masses: [B][32][8] in the 
 struct ChainSmem {
     uint2 queue[kCTW][256];        // per warp: kept elements of one vector per lane
     unsigned long long wsum[kCTW];
-    uint32_t red_a[kCTW], red_b[kCTW];
+    uint32_t red_a[kRW > kCTW ? kRW : kCTW], red_b[kRW > kCTW ? kRW : kCTW];  // per warp of the CTA
     unsigned long long slice[kCP];
     long long thr, base;
     int acc, bonus, flag, last, cross;
@@ -1687,6 +1833,7 @@ __device__ unsigned long long tile_mass(const BonusRow& r, int V, int tv0, int t
                                         uint2* queue) {
     const int tid = threadIdx.x, lane = tid & 31;
     unsigned long long mine = 0;
+    if (tid >= kCT) return 0ull;  // a tile is kCT threads' work (whole warps return here)
     // the thread's 4 vectors (p and q) are loaded before any is used
     uint4 xa[4], ya[4];
 #pragma unroll
@@ -1733,7 +1880,7 @@ __device__ __forceinline__ unsigned long long block_sum_u64(unsigned long long v
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     v = warp_sum_u64(v);
     __syncthreads();
-    if (lane == 0) wsum[wid] = v;
+    if (lane == 0 && wid < kCTW) wsum[wid] = v;  // warps beyond kCTW hold no tile work
     __syncthreads();
     unsigned long long t = 0;
 #pragma unroll
@@ -1755,7 +1902,7 @@ __device__ bool chain_task(const VerifyArgs& a, ChainSmem* sh, int b, int rank) 
     bool finished = false;
     (void)lane;
     // the accepted length, decided by the row kernel when the request's rows completed
-    if (tid == 0) sh->acc = (int)__ldcg(&a.racc[2 * b + 1]);
+    if (tid == 0) sh->acc = outcome_of(__ldcg(&a.racc[2 * b + 1]), cap);  // claimed: known
     __syncthreads();
     const int acc = sh->acc;
     const bool pure0 = acc == cap - 1;
@@ -1792,7 +1939,7 @@ __device__ bool chain_task(const VerifyArgs& a, ChainSmem* sh, int b, int rank) 
         for (int t = 0; u0 + t * kCTileV < u1 && t < kCMaxTiles; ++t) {
             const int tv0 = u0 + t * kCTileV, tv1 = min(tv0 + kCTileV, u1);
             const unsigned long long m =
-                block_sum_u64(tile_mass(r, V, tv0, tv1, pure_, sh->queue[wid]), sh->wsum);
+                block_sum_u64(tile_mass(r, V, tv0, tv1, pure_, sh->queue[wid < kCTW ? wid : 0]), sh->wsum);
             if (tid == 0) tmass[q * kCMaxTiles + t] = m;
             // per-warp masses (still in shared memory) for the crossing search
             if (tid < kCTW) a.wmass[((size_t)b * kCP + q) * kCTW + tid] = sh->wsum[tid];
@@ -1874,10 +2021,12 @@ __device__ bool chain_task(const VerifyArgs& a, ChainSmem* sh, int b, int rank) 
                     // thread t takes elements [4 t, 4 t + 4) of the region (half of
                     // vector t / 2), a block scan of the thread masses finds the thread,
                     // and it walks its four elements
+                    // (threads beyond kCT take no element: the region is kCT threads' work)
+                    const bool mine_t = tid < kCT;
                     const int v = tv0 + 128 * ws_ + (tid >> 1);
                     uint4 xa = make_uint4(0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u, 0xFF80FF80u);
                     uint4 ya = xa;
-                    if (v < tv1) load8(r, v, pure, xa, ya);
+                    if (mine_t && v < tv1) load8(r, v, pure, xa, ya);
                     unsigned long long f4[4];
                     unsigned long long own = 0;
 #pragma unroll
@@ -1885,7 +2034,7 @@ __device__ bool chain_task(const VerifyArgs& a, ChainSmem* sh, int b, int rank) 
                         const int h = 4 * (tid & 1) + hh;
                         const int i = 8 * v + h - r.poff;
                         unsigned long long f = 0;
-                        if (v < tv1 && i >= 0 && i < V && kept_in(r.dt, half16(xa, h), i)) {
+                        if (mine_t && v < tv1 && i >= 0 && i < V && kept_in(r.dt, half16(xa, h), i)) {
                             uint32_t qb = half16(ya, h);
                             if (!pure && r.has_dq && !r.qvec)
                                 qb = r.qrow ? (uint32_t)__ldg(r.qrow + i) : 0xFF80u;
@@ -1895,12 +2044,12 @@ __device__ bool chain_task(const VerifyArgs& a, ChainSmem* sh, int b, int rank) 
                         own += f;
                     }
                     const unsigned long long incl = warp_incl_u64(own);
-                    if (lane == 31) sh->wsum[wid] = incl;
+                    if (lane == 31 && mine_t) sh->wsum[wid] = incl;
                     __syncthreads();
                     unsigned long long wpre = 0;
-                    for (int w = 0; w < wid; ++w) wpre += sh->wsum[w];
+                    for (int w = 0; w < wid && mine_t; ++w) wpre += sh->wsum[w];
                     long long run = base + (long long)(wpre + incl - own);
-                    if (run <= thr && run + (long long)own > thr) {
+                    if (mine_t && run <= thr && run + (long long)own > thr) {
 #pragma unroll
                         for (int hh = 0; hh < 4; ++hh) {
                             run += (long long)f4[hh];
@@ -1928,37 +2077,39 @@ __device__ bool chain_task(const VerifyArgs& a, ChainSmem* sh, int b, int rank) 
     return finished;
 }
 
-// Greedy request b once all its rows are done (warp 0): one-hot p at each target row's first
-// argmax (packed by the row pass), one-hot q at the drafted token; writes the outputs and
-// resets the packed maxima.
-__device__ void greedy_decide(const VerifyArgs& a, int b, int cap) {
-    const int lane = threadIdx.x & 31;
-    const int s = lane;
-    bool accp = false;
-    long long am = 0;
-    if (s < cap) {
+// Step s of request b (s < cap - 1): draft token s + 1 against target row s, both rows done
+// (sampling/rejection.py:66-98: u * q < p with q in (0, 1]).  Greedy requests: one-hot p at
+// the row's first argmax (packed by the row pass), one-hot q at the drafted token.
+__device__ bool step_accepted(const VerifyArgs& a, int b, int s, bool greedy) {
+    const long long tok = a.cand[b * kT + s + 1];
+    const bool valid = tok >= 0 && tok < a.V;
+    float p = 0.0f, q = 0.0f;
+    if (greedy) {
         const unsigned long long g = __ldcg(&a.gmax[b * kT + s]);
-        am = g ? (long long)(0xFFFFFFFFull - (g & 0xFFFFFFFFull)) : 0ll;
+        const long long am = g ? (long long)(0xFFFFFFFFull - (g & 0xFFFFFFFFull)) : 0ll;
+        p = (valid && tok == am) ? 1.0f : 0.0f;
+        q = valid ? 1.0f : 0.0f;
+    } else if (valid) {
+        const uint16_t* tgt = reinterpret_cast<const uint16_t*>(a.tgt);
+        const uint16_t* drf = reinterpret_cast<const uint16_t*>(a.drf);
+        const RowDesc dt = load_desc_cg(&a.desc[(b * kT + s) * 2 + 0]);
+        const long long tr = a.tgt_row[b] + s;
+        if (tr >= 0 && tr < a.tgt_rows) {
+            const uint32_t pb = tgt[tr * a.stride + tok];
+            p = row_prob(dt, bf(pb), pb, (int)tok);
+        }
+        if (a.drf == nullptr) {
+            q = 1.0f;
+        } else {
+            const RowDesc dd = load_desc_cg(&a.desc[(b * kT + s) * 2 + 1]);
+            const long long dr = a.drf_row[b] + s;
+            if (dr >= 0 && dr < a.drf_rows) {
+                const uint32_t qb = drf[dr * a.stride + tok];
+                q = row_prob(dd, bf(qb), qb, (int)tok);
+            }
+        }
     }
-    if (s < cap - 1) {
-        const long long tok = a.cand[b * kT + s + 1];
-        const bool valid = tok >= 0 && tok < a.V;
-        const float p = (valid && tok == am) ? 1.0f : 0.0f;
-        const float q = valid ? 1.0f : 0.0f;
-        accp = q > 0.0f && q <= 1.0f && __fmul_rn(a.u[b * 15 + s], q) < p;
-    }
-    const uint32_t rej = __ballot_sync(0xffffffffu, !accp) & ((1u << (cap - 1)) - 1u);
-    const int acc = rej ? __ffs(rej) - 1 : cap - 1;
-    const long long ga = __shfl_sync(0xffffffffu, am, acc);
-    __syncwarp();
-    if (s < cap) a.gmax[b * kT + s] = 0ull;
-    if (lane == 0) {
-        // the residual against a one-hot q is the same one-hot or empty (then the
-        // fallback to p): the draw is the argmax unless u is outside [0, 1)
-        const long long thr = scale_floor(a.uf[b], 1ull << kFixBits);
-        const long long bo = thr == -2 ? (long long)a.V - 1 : (thr < 0 ? 0ll : ga);
-        write_request(a, b, acc, bo);
-    }
+    return q > 0.0f && q <= 1.0f && __fmul_rn(a.u[b * (kT - 1) + s], q) < p;
 }
 
 // After this CTA wrote the outputs of a request: the CTA that finishes the last request packs
@@ -1974,79 +2125,58 @@ __device__ void finalize_request(const VerifyArgs& a, ChainSmem* sh) {
     __syncthreads();
     if (sh->flag) {
         __threadfence();
-        if (a.tok_out != nullptr) compact_all_nt<kCT>(a, sh->red_a, sh->red_b);
+        if (a.tok_out != nullptr) compact_all_nt<kRT>(a, sh->red_a, sh->red_b);
         __syncthreads();
         if (tid == 0) a.ws->finalized = 0;
     }
     __syncthreads();
 }
 
-// After a row of request b: the CTA that completes the request's rows decides its chain
-// (warp 0, one lane per step: draft s+1 against target row s).  A greedy request is finished
-// right there (returns true: this CTA wrote its outputs); a sampled request leaves its
-// accepted length and joins the ready list, from which its chain tasks are taken.
-__device__ bool row_done(RSmem* sh, const VerifyArgs& a, int b) {
-    const int tid = threadIdx.x, lane = tid & 31;
+// After a whole row of request b (verification only; all threads): marks the row done.  The
+// CTA whose row completes verify position s (its target row and, where the chain has one,
+// its draft row) decides step s, or for s = cap - 1 records the last target row.  The CTA
+// whose decision makes the outcome known claims the request: a greedy request is finished
+// right there (returns true: this CTA wrote its outputs); a sampled one joins the ready list,
+// from which its chain tasks (the bonus draw) are taken.
+__device__ bool row_finish(RSmem* sh, const VerifyArgs& a, const TaskInfo& ti) {
+    const int tid = threadIdx.x;
     if (a.cand == nullptr) return false;
-    const int cat = (int)(sh->plan.req[b] & 7u), cap = (int)(sh->plan.req[b] >> 3);
-    const bool greedy = cat == kGreedy;
-    const unsigned nrows = (unsigned)(cap + (!greedy && a.drf != nullptr ? cap - 1 : 0));
+    const int b = ti.b, s = ti.s, cap = ti.cap;
+    const bool greedy = ti.cat == kGreedy;
+    const bool has_d = !greedy && a.drf != nullptr && s < cap - 1;
     __syncthreads();
     if (tid == 0) {
-        __threadfence();
-        const unsigned old = atomicAdd(&a.racc[2 * b], 1u);
-        sh->first_min = old == nrows - 1u;
+        __threadfence();  // this row's descriptor and packed argmax before its mark
+        const uint32_t bit = ti.kind == 0 ? (1u << s) : (1u << (16 + s));
+        const uint32_t need = (1u << s) | (has_d ? (1u << (16 + s)) : 0u);
+        const uint32_t old = atomicOr(&a.racc[2 * b], bit);
+        int claim = 0;
+        if (((old | bit) & need) == need && (old & need) != need) {
+            __threadfence();
+            const uint32_t dbit = s < cap - 1 ? (step_accepted(a, b, s, greedy) ? 1u << s : 1u << (16 + s))
+                                              : kStepLast;
+            const uint32_t w = atomicOr(&a.racc[2 * b + 1], dbit) | dbit;
+            const int acc = outcome_of(w, cap);
+            if (acc >= 0 && !(atomicOr(&a.racc[2 * b + 1], kClaimed) & kClaimed)) claim = acc + 1;
+        }
+        sh->fin_claim = claim;
     }
     __syncthreads();
-    if (!sh->first_min) return false;
+    const int claim = sh->fin_claim;
+    if (!claim || tid != 0) return claim != 0 && greedy;
+    const int acc = claim - 1;
     if (greedy) {
-        __threadfence();
-        if (tid < 32) {
-            greedy_decide(a, b, cap);
-            if (lane == 0) a.racc[2 * b] = 0u;  // for the next launch
-        }
+        // the residual against a one-hot q is the same one-hot or empty (then the fallback to
+        // p): the draw is the argmax of row acc unless u is outside [0, 1)
+        const unsigned long long g = __ldcg(&a.gmax[b * kT + acc]);
+        const long long ga = g ? (long long)(0xFFFFFFFFull - (g & 0xFFFFFFFFull)) : 0ll;
+        const long long thr = scale_floor(a.uf[b], 1ull << kFixBits);
+        write_request(a, b, acc, thr == -2 ? (long long)a.V - 1 : (thr < 0 ? 0ll : ga));
         return true;
     }
-    if (tid >= 32) return false;
     __threadfence();
-    const bool onehot_q = a.drf == nullptr;
-    const uint16_t* tgt = reinterpret_cast<const uint16_t*>(a.tgt);
-    const uint16_t* drf = reinterpret_cast<const uint16_t*>(a.drf);
-    bool acc = false;
-    const int s = lane;
-    if (s < cap - 1) {
-        const long long tok = a.cand[b * kT + s + 1];
-        const bool valid = tok >= 0 && tok < a.V;
-        float p = 0.0f, q = 0.0f;
-        if (valid) {
-            const RowDesc dt = load_desc_cg(&a.desc[(b * kT + s) * 2 + 0]);
-            const long long tr = a.tgt_row[b] + s;
-            if (tr >= 0 && tr < a.tgt_rows) {
-                const uint32_t pb = tgt[tr * a.stride + tok];
-                p = row_prob(dt, bf(pb), pb, (int)tok);
-            }
-            if (onehot_q) {
-                q = 1.0f;
-            } else {
-                const RowDesc dd = load_desc_cg(&a.desc[(b * kT + s) * 2 + 1]);
-                const long long dr = a.drf_row[b] + s;
-                if (dr >= 0 && dr < a.drf_rows) {
-                    const uint32_t qb = drf[dr * a.stride + tok];
-                    q = row_prob(dd, bf(qb), qb, (int)tok);
-                }
-            }
-        }
-        acc = q > 0.0f && q <= 1.0f && __fmul_rn(a.u[b * 15 + s], q) < p;
-    }
-    const uint32_t rej = __ballot_sync(0xffffffffu, !acc) &
-                         ((cap - 1 >= 32) ? 0xffffffffu : ((1u << (cap - 1)) - 1u));
-    if (lane == 0) {
-        a.racc[2 * b + 1] = (unsigned)(rej ? __ffs(rej) - 1 : cap - 1);
-        a.racc[2 * b] = 0u;  // for the next launch
-        __threadfence();
-        const unsigned pos = atomicAdd(&a.ws->ready_tail, 1u);
-        a.order[pos] = (unsigned)b + 1u;  // nonzero: published
-    }
+    const unsigned pos = atomicAdd(&a.ws->ready_tail, 1u);
+    a.order[pos] = (unsigned)b + 1u;  // nonzero: published
     return false;
 }
 
@@ -2082,28 +2212,49 @@ __global__ void __launch_bounds__(kRT, DSV_ROWS_MIN_CTAS) rows_kernel(VerifyArgs
 #ifdef DSV_PROFILE
         for (int q = 0; q < 16; ++q) sh->prof_ph[q] = 0u;
 #endif
-        uint16_t* pre = reinterpret_cast<uint16_t*>(smem_raw + sizeof(RSmem));
-        sh->plan = Plan{pre, reinterpret_cast<uint8_t*>(pre + 3 * (a.B + 1)), a.B};
+        sh->plan = plan_at(smem_raw + sizeof(RSmem), a.B);
     }
 #ifdef DSV_PROFILE
     const unsigned long long trace_t0 = globaltimer_ns();
 #endif
     __syncthreads();
     build_plan(a, sh, kRWinK);
-    // Task sources, in priority order: (1) rows with selection work (tasks [0, nsel): the
-    // ALU-heavy ones, first so they spread over every CTA), (2) greedy rows (tasks [nsel,
-    // ntask): memory-bound, they run beside the last selection rows), (3) chain tasks of
-    // requests whose rows are done (kCP slices per sampled request, from the ready list),
-    // (4) chain tasks whose request is not ready yet (the CTA waits: every selection row has
-    // been taken by then, so it will be).
-    const int nsel = (int)(sh->plan.pre(0, a.B) + sh->plan.pre(1, a.B));
-    const int ntask = total_tasks(a, sh);
-    // Selection rows beyond the first wave (index >= grid) are split in two halves (up to the
-    // workspace's slot count): selection task t maps to row t below the grid, to row
-    // G + (t - G) / 2, half (t - G) % 2 for the next 2 * nsplit tasks, and to row t - nsplit after.
+    // Task sources.  Row tasks come in plan order (positions first, see Plan).  Some rows are
+    // split in two halves, up to the workspace's slot count: in verification, the rows of the
+    // first kSplitPos positions (the rows most likely to decide a chain: two CTAs halve the
+    // latency of their histogram pass), as tasks 2 r and 2 r + 1 of row r < nfront; for target
+    // probabilities, the rows beyond the first wave (index >= grid), whose halves shorten the
+    // tail: row task x maps to row x below the grid, to row G + (x - G) / 2, half (x - G) % 2
+    // for the next 2 * nsplit tasks, and to row x - nsplit after.  After its first row a CTA
+    // takes, in order: (1) a chain task of a request whose outcome is known (kCP bonus slices
+    // per sampled request, from the ready list), (2) the next row task that can still change
+    // an outcome (rows after a known rejection, or of a request already claimed, are dropped
+    // at dequeue or abandoned during their first pass), (3) a chain task whose request is not
+    // ready yet (every row has been taken by then, so it will be; the wait is bounded).
+    const int nrows = total_tasks(a, sh);
     const int G = (int)gridDim.x;
-    const int nsplit = (a.split_cap > 0 && nsel > G) ? min(nsel - G, a.split_cap) : 0;
-    const int nseltask = nsel + nsplit;
+    const bool verifying = a.cand != nullptr;
+    const int nfront = (verifying && kSplitPos > 0 && a.split_cap > 0)
+                           ? min((int)sh->plan.pos[kSplitPos], a.split_cap) : 0;
+    const int nsplit = (!verifying && a.split_cap > 0 && nrows > G) ? min(nrows - G, a.split_cap) : 0;
+    const int nrt = nrows + nfront + nsplit;
+    auto row_of = [&](int x, int& half) {
+        half = -1;
+        if (nfront > 0) {
+            if (x < 2 * nfront) {
+                half = x & 1;
+                return x >> 1;
+            }
+            return x - nfront;
+        }
+        if (x >= G + 2 * nsplit) return x - nsplit;
+        if (x >= G) {
+            half = (x - G) & 1;
+            return G + (x - G) / 2;
+        }
+        return x;
+    };
+    auto slot_of = [&](int x) { return nfront > 0 ? x >> 1 : (x - G) / 2; };
     if (tid < 32) {
         int ns = 0;
         for (int b0 = 0; b0 < a.B; b0 += 32) {
@@ -2113,7 +2264,6 @@ __global__ void __launch_bounds__(kRT, DSV_ROWS_MIN_CTAS) rows_kernel(VerifyArgs
         if (lane == 0) {
             sh->q_nchain = a.cand != nullptr ? ns * kCP : 0;
             sh->q_sel_empty = 0;
-            sh->q_gr_empty = 0;
         }
     }
     static_assert(sizeof(ChainSmem) <= sizeof(uint32_t) * kHCap && alignof(ChainSmem) <= 16,
@@ -2125,31 +2275,47 @@ __global__ void __launch_bounds__(kRT, DSV_ROWS_MIN_CTAS) rows_kernel(VerifyArgs
         if (tid == 0) {
             const int nchain = sh->q_nchain;
             int kind = 0, t = -1;
-            if (first_task && (int)blockIdx.x < nsel) {
-                kind = 1;
-                t = (int)blockIdx.x;  // the first task of CTA i is selection row i
-            }
-            if (!kind && !sh->q_sel_empty) {
-                const int x = (int)(gridDim.x + atomicAdd(&a.ws->next, 1u));
-                if (x < nseltask) {
+            auto try_chain = [&]() {
+                // a chain task of a published request, claimed only below the published count
+                for (int tries = 0; tries < 4; ++tries) {
+                    const unsigned ready = *(volatile unsigned*)&a.ws->ready_tail * (unsigned)kCP;
+                    const unsigned cn = *(volatile unsigned*)&a.ws->chain_next;
+                    if (cn >= ready || cn >= (unsigned)nchain) return false;
+                    if (atomicCAS(&a.ws->chain_next, cn, cn + 1u) == cn) {
+                        kind = 2;
+                        t = (int)cn;
+                        return true;
+                    }
+                }
+                return false;
+            };
+            for (;;) {
+                if (nchain > 0 && try_chain()) break;
+                if (sh->q_sel_empty) break;
+                int x;
+                if (first_task && (int)blockIdx.x < nrt) {
+                    x = (int)blockIdx.x;  // the first task of CTA i is row task i
+                    first_task = false;
+                } else {
+                    x = (int)(gridDim.x + atomicAdd(&a.ws->next, 1u));
+                }
+                if (x >= nrt) {
+                    sh->q_sel_empty = 1;
+                    break;
+                }
+                // the first half of a split row is always taken: its second half may have been
+                // dequeued (and found needed) before this check, and it waits for the first
+                int half;
+                const TaskInfo ti = decode_task(a, sh, row_of(x, half));
+                if (half == 0 || row_needed(a, ti.b, ti.s)) {
                     kind = 1;
                     t = x;
-                } else {
-                    sh->q_sel_empty = 1;
+                    break;
                 }
             }
-            if (!kind && !sh->q_gr_empty) {
-                const int x = (int)atomicAdd(&a.ws->next2, 1u);
-                if (nsel + x < ntask) {
-                    kind = 1;
-                    t = nseltask + x;
-                } else {
-                    sh->q_gr_empty = 1;
-                }
-            }
-            if (!kind && nchain > 0) {
-                const unsigned ready = *(volatile unsigned*)&a.ws->ready_tail * (unsigned)kCP;
-                if (*(volatile unsigned*)&a.ws->chain_next < ready) {
+            if (!kind) {
+                // every row taken: a chain task whose request is not published yet
+                if (nchain > 0) {
                     const int j = (int)atomicAdd(&a.ws->chain_next, 1u);
                     if (j < nchain) {
                         kind = 2;
@@ -2157,22 +2323,23 @@ __global__ void __launch_bounds__(kRT, DSV_ROWS_MIN_CTAS) rows_kernel(VerifyArgs
                     }
                 }
             }
-            if (!kind && nchain > 0) {
-                const int j = (int)atomicAdd(&a.ws->chain_next, 1u);
-                if (j < nchain) {
-                    kind = 2;
-                    t = j;
-                }
-            }
             if (kind == 2) {
                 const int b = wait_ready(a, t / kCP);
                 if (b < 0) kind = 3;  // gave up: the request stays unfinished (error bit 6)
                 sh->q_b = b;
             }
+            if (kind == 1) {
+                int half;
+                const TaskInfo ti = decode_task(a, sh, row_of(t, half));
+                const bool watch = a.cand != nullptr && half < 0;
+                sh->watch_b = watch ? ti.b : -1;
+                sh->watch_s = watch ? ti.s : -1;
+            }
+            sh->abort_row = 0;
+            sh->hbm_vecs = 0u;
             sh->task = t;
             sh->q_kind = kind;
         }
-        first_task = false;
         __syncthreads();
         const int t = sh->task, kind = sh->q_kind;
         if (kind == 0) break;
@@ -2183,23 +2350,18 @@ __global__ void __launch_bounds__(kRT, DSV_ROWS_MIN_CTAS) rows_kernel(VerifyArgs
 #endif
         bool finished;
         if (kind == 1) {
-            int r = t, half = -1;
-            if (t >= nseltask) {
-                r = nsel + (t - nseltask);             // greedy rows
-            } else if (t >= G + 2 * nsplit) {
-                r = t - nsplit;
-            } else if (t >= G) {
-                r = G + (t - G) / 2;
-                half = (t - G) & 1;
-            }
+            int half;
+            const int r = row_of(t, half);
             TaskInfo ti = decode_task(a, sh, r);
             ti.half = half;
-            ti.slot = half >= 0 ? (t - G) / 2 : -1;
+            ti.slot = half >= 0 ? slot_of(t) : -1;
 #ifdef DSV_PROFILE
             trace_cat = ti.cat;
 #endif
-            process_row(sh, a, ti);
-            finished = half == 0 ? false : row_done(sh, a, ti.b);  // a first half is not a row
+            const unsigned long long nbytes = process_row(sh, a, ti);
+            if (tid == 0 && nbytes) atomicAdd(&a.ws->bytes_read, nbytes);
+            // an abandoned row is not done (nothing waits for it); a first half is not a row
+            finished = (sh->abort_row || half == 0) ? false : row_finish(sh, a, ti);
         } else {
             finished = chain_task(a, csh, sh->q_b, t % kCP);
         }
@@ -2230,22 +2392,30 @@ __global__ void __launch_bounds__(kRT, DSV_ROWS_MIN_CTAS) rows_kernel(VerifyArgs
         e[1] = globaltimer_ns();
     }
 #endif
-    // the last CTA out resets the counters and the ready list for the next launch
+    // the last CTA out resets the counters, the ready list, the per-request progress words and
+    // the split flags for the next launch
     __syncthreads();
     if (tid == 0) {
         __threadfence();
-        const unsigned old = atomicAdd(&a.ws->exited, 1u);
-        if (old == gridDim.x - 1) {
-            __threadfence();
-            const unsigned nready = a.ws->ready_tail;
-            for (unsigned i = 0; i < nready && i < (unsigned)a.B; ++i) a.order[i] = 0u;
+        sh->exit_last = atomicAdd(&a.ws->exited, 1u) == gridDim.x - 1;
+    }
+    __syncthreads();
+    if (sh->exit_last) {
+        __threadfence();
+        const unsigned nready = *(volatile unsigned*)&a.ws->ready_tail;
+        for (unsigned i = tid; i < nready && i < (unsigned)a.B; i += kRT) a.order[i] = 0u;
+        if (a.cand != nullptr)
+            for (int i = tid; i < 2 * a.B; i += kRT) a.racc[i] = 0u;
+        for (int i = tid; i < nsplit + nfront; i += kRT) a.split_flag[i] = 0u;
+        __syncthreads();
+        if (tid == 0) {
             a.ws->next = 0;
             a.ws->next2 = 0;
             a.ws->ready_tail = 0;
             a.ws->chain_next = 0;
             a.ws->exited = 0;
-            __threadfence();
         }
+        __threadfence();
     }
 }
 

@@ -37,7 +37,13 @@ namespace dsv {
 
 namespace {
 
-constexpr int kNT = 256;            // threads per CTA
+#ifndef DSV_VERIFY_THREADS
+#define DSV_VERIFY_THREADS 1024
+#endif
+// threads per CTA: one CTA per SM (two staged fp32 slices fill its shared memory), so the
+// per-element exp and fixed-point work of the passes needs all the SM's warps (config 0,
+// fp32: 0.145 ms per call at 1024 threads against 0.157 at 512 and 0.226 at 256)
+constexpr int kNT = DSV_VERIFY_THREADS;
 constexpr int kNW = kNT / 32;
 constexpr int kBins = 256;
 

@@ -51,6 +51,16 @@ class Workspace:
     # waiting (6, 7); the workspace is zeroed again before it is reused
     RESET_BITS = 0x1 | 0x20 | 0x40 | 0x80
 
+    def bytes_read(self) -> int:
+        """Logit bytes the streaming row kernel has read from memory through this workspace,
+        summed over its launches since the workspace was last zeroed.  Verification drops rows
+        that cannot change an outcome, so this is what was read, not every row of the batch.
+        Synchronizes the current stream."""
+        n = ctypes.c_uint64()
+        _lib.call("dsv_workspace_bytes_read", self.buf.data_ptr(), ctypes.byref(n),
+                  _stream(self.buf.device))
+        return int(n.value)
+
     def error_word(self) -> int:
         """Device error bits (synchronizes the current stream); cleared after reading.  After an
         internal failure (RESET_BITS) the whole workspace is zeroed again."""

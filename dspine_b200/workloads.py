@@ -77,6 +77,19 @@ class Batch:
             rows += int(((lens - 1).clamp_min(0) * (~greedy)).sum())
         return rows * self.V * esz
 
+    def deciding_bytes(self, accept) -> int:
+        """Bytes of the rows the outcome depends on, given the accepted lengths: target rows
+        0..accept and, for sampled requests with draft logits, draft rows 0..min(accept,
+        len - 2) (a chain stops at its first rejected step; later rows are never consulted)."""
+        esz = self.target_logits.element_size()
+        lens = self.verify_lens.cpu().long()
+        acc = torch.as_tensor(accept).cpu().long()
+        greedy = _greedy_mask(self.temperature.cpu(), self.top_k.cpu())
+        rows = int((acc + 1).sum())
+        if self.draft_logits is not None:
+            rows += int(((torch.minimum(acc + 1, lens - 1)).clamp_min(0) * (~greedy)).sum())
+        return rows * self.V * esz
+
     def verified_tokens(self) -> int:
         return int(self.verify_lens.sum())
 

@@ -58,7 +58,7 @@ uint64_t dsv_launch_count(void);
  * and (last 8.5 MB) the slots through which the two halves of a split row meet.  Zero it once
  * after allocation (dsv_workspace_init); every launch that ends without an internal failure
  * (error bits 0, 5-7 below) leaves it zeroed again for the next launch with the same batch
- * size.  Its regions are laid out by the batch size, so a workspace sized for the largest
+ * size, except for a counter of the logit bytes read (dsv_workspace_bytes_read).  Its regions are laid out by the batch size, so a workspace sized for the largest
  * batch serves smaller ones, but must be zeroed again when the batch size changes.  A workspace
  * without the split-row slots (the size for the batch minus that region) is accepted and then
  * no row is split. */
@@ -68,6 +68,13 @@ int dsv_workspace_init(void* workspace, size_t bytes, dsv_stream_t stream);
  * bit 0: a shared-memory bulk copy did not complete within its time limit;
  * bit 1: a request addressed a row outside the logit tensors. */
 int dsv_workspace_error(void* workspace, uint32_t* err, dsv_stream_t stream);
+/* Logit bytes that bf16 verifications and target-probability calls through this workspace
+ * have read from memory since it was last zeroed (synchronizes `stream`).  Verification takes
+ * the rows in verify-position order across the batch and drops the rows after a step already
+ * known to be rejected (the chain stops there) and the rows of a request whose outcome is
+ * already known, when it reaches them or while it reads them: those rows cannot change any
+ * output.  No counterpart in the reference (a diagnostic). */
+int dsv_workspace_bytes_read(const void* workspace, uint64_t* bytes, dsv_stream_t stream);
 /* bit 2 of the error word: a compaction read a KV slot position outside `slots_len`;
  * bits 3-4: a selection or a tie cut found no boundary (inconsistent input); bit 6: a chain
  * task waited past its time limit for its request; bit 7: the second half of a split row

@@ -209,6 +209,52 @@ def test_split_rows_match_oracle(case):
     assert_same(run_kernel(batch), oracle_verify(batch), f"split rows {case}")
 
 
+@pytest.mark.parametrize("case", ["accept", "reject", "mixed"])
+def test_dropped_rows_do_not_change_outputs(case):
+    """A chain stops at its first rejected step, so the row kernel drops (at dequeue, or during
+    a row's first pass) the rows after a known rejection and the rows of a request whose outcome
+    is known.  Drafts equal to the target accept every step (no row can be dropped), drafts
+    opposite to it reject at once (most rows are dropped); outputs equal the oracle's, which
+    processes every row, and the bytes read show what was dropped."""
+    g = torch.Generator().manual_seed(77)
+    B, V = 64, 4099
+    lens = torch.full((B,), 16, dtype=torch.int32)
+    lens[::5] = torch.randint(1, 16, (len(lens[::5]),), generator=g, dtype=torch.int32)
+    temperature = 0.4 + torch.rand(B, generator=g)
+    temperature[::7] = 0.0
+    top_k = torch.where(torch.rand(B, generator=g) < 0.5, torch.tensor(workloads.TOPK_OFF),
+                        torch.tensor(20)).to(torch.int32)
+    top_p = 0.7 + 0.3 * torch.rand(B, generator=g)
+    batch = workloads.build(lens, temperature, top_k, top_p, V=V, dtype=torch.float32, seed=9)
+    batch.target_logits = batch.target_logits.to(torch.bfloat16)
+    batch.draft_logits = batch.draft_logits.to(torch.bfloat16)
+    if case == "accept":
+        # draft row (b, s) is target row (b, s), so q = p; drafted tokens are each row's first
+        # argmax (kept by every filter; what greedy requests accept)
+        batch.draft_logits = batch.target_logits.clone()
+        batch.draft_rows = batch.target_rows.clone()
+        am = batch.target_logits.float().argmax(dim=1)
+        rows = batch.target_rows.long()
+        for b in range(B):
+            n = int(lens[b])
+            batch.candidates[b, 1:n] = am[rows[b]:rows[b] + n - 1]
+    elif case == "reject":
+        batch.draft_logits = -batch.draft_logits
+    batch = batch.to(DEV)
+    ws = verify.workspace_for(batch.B, DEV)
+    before = ws.bytes_read()
+    got = run_kernel(batch)
+    read = ws.bytes_read() - before
+    expected = oracle_verify(batch)
+    assert_same(got, expected, f"dropped rows {case}")
+    all_rows = batch.algorithmic_bytes()
+    if case == "accept":
+        assert (expected[0] == batch.verify_lens.cpu().numpy() - 1).all()
+        assert read >= all_rows  # every row read (16-byte vectors round each row up)
+    elif case == "reject":
+        assert read < all_rows // 2
+
+
 @pytest.mark.parametrize("B,V", [(1, 1031), (1024, 521), (1025, 521)])
 def test_batch_limits_match_oracle(B, V):
     """One request; the largest batch of the one-launch bf16 path (1024: the task table and the
