@@ -84,6 +84,9 @@ def parse_args():
                    help="time one library kernel alone (the workloads of the ncu summaries)")
     p.add_argument("--no-tp-head", action="store_true",
                    help="at N > 1, skip the config-3 TP head timed beside the replicas")
+    p.add_argument("--requests", type=int, default=None,
+                   help="config1 with this many requests instead of 64 (small ncu cases; not a "
+                        "benchmark line)")
     p.add_argument("--no-other-configs", action="store_true",
                    help="at N = 1, skip configs 0, 4, 2 and the FP8 head measured after config 1")
     return p.parse_args()
@@ -123,13 +126,18 @@ def profiled_traffic(config: str):
     return (total if kernels else None), kernels
 
 
-def make_batch(config: str, rank: int, device):
+def make_batch(config: str, rank: int, device, requests=None):
     """The config's batch.  Every replica verifies the same seeded batch, so that the time of
     N replicas measures the machine (HBM, clocks, launch) rather than the cost spread between
-    differently seeded batches."""
+    differently seeded batches.  `requests` (config 1 only) draws a smaller batch with the same
+    distributions: the small case of an ncu capture."""
     from dspine_b200 import workloads
     fn = getattr(workloads, config)
     seed = {"config0": 0, "config1": 1, "config4": 4}[config]
+    if requests:
+        if config != "config1":
+            raise SystemExit("--requests applies to config1 only")
+        return fn(seed=seed, device=device, B=requests)
     return fn(seed=seed, device=device)
 
 
@@ -275,7 +283,7 @@ def run_dspine(args):
     from dspine_b200 import _lib, verify
 
     lib = _lib.load()
-    batch = make_batch(args.config, rank, dev)
+    batch = make_batch(args.config, rank, dev, args.requests)
     kw = batch.kwargs()
     B = batch.B
     out = verify.new_outputs(B, dev)
