@@ -539,6 +539,7 @@ struct RSmem {
     int exit_last;                 // this CTA is the last out of the launch
     int watch_b, watch_s;          // the row's request and position while its first pass may
                                    // be abandoned (watch_s < 0: not watched)
+    int late_b, late_s;            // the same for the tie cut (late_s < 0: not watched)
     int abort_row;                 // the first pass was abandoned: the row cannot change an outcome
     int stream_end;                // chunks of the current stream that were issued
     uint32_t hbm_vecs;             // 16-byte vectors the row's first pass read from memory
@@ -838,6 +839,7 @@ __device__ KeyStop cta_walk_keys(RSmem* sh, const uint32_t* counts, uint32_t khi
 // through the ring; chunks already issued when it is found are drained, none is left in flight.
 // kRev streams the row from its end and `need` counts occurrences from the end (the caller
 // picks the nearer end: occurrence n of c in index order is occurrence c - n + 1 from the end).
+// Returns the index, -1 if not found, or -2 if the watched row was abandoned.
 template <bool kRev>
 __device__ int tie_scan(RSmem* sh, const VerifyArgs& a, const RowGeo& g, int V, uint32_t key,
                         unsigned long long need_total) {
@@ -893,7 +895,7 @@ __device__ int tie_scan(RSmem* sh, const VerifyArgs& a, const RowGeo& g, int V, 
         if (!mbar_wait_bounded(&R.bar[slot], (k / S) & 1u)) {
             if (tid == 0) atomicOr(&a.ws->err, 1u);
         }
-        if (found < 0) {
+        if (found == -1) {
             const int v0 = pos_of(r) * CW;
             const int nvec = min(CW, g.nv - v0);
             uint32_t cu[U];
@@ -956,9 +958,15 @@ __device__ int tie_scan(RSmem* sh, const VerifyArgs& a, const RowGeo& g, int V, 
             }
             run += all;
         }
+        // a watched row that can no longer change an outcome is abandoned (checked every 8
+        // chunks): -2 stops the issue of further chunks; a cut found in this same chunk may
+        // win the race for sel[12], and then the row simply completes
+        if (tid == 0 && (r & 7) == 7 && sh->late_s >= 0 && !row_needed(a, sh->late_b, sh->late_s) &&
+            sh->sel[12] == -1)
+            sh->sel[12] = -2;
         __syncthreads();  // the slot is consumed; sel[12] is visible
         found = sh->sel[12];
-        const bool more = found < 0 && issued < nch;
+        const bool more = found == -1 && issued < nch;
         if (tid == 0 && more) {
             const uint32_t slot2 = (base + issued) % S;
             const int cn = pos_of(issued);
@@ -1632,9 +1640,18 @@ __device__ void process_row_body(RSmem* sh, const VerifyArgs& a, const TaskInfo&
         // equal bits, so the scan's matches are exactly the key's counted elements.
         const uint32_t kexp = (key_bits(ks.key) >> 7) & 0xFFu;
         const bool normal_key = kexp != 0u && kexp != 0xFFu;
+        // a row that can no longer change an outcome stops here (no descriptor: nothing reads it)
+        if (tid == 0 && sh->late_s >= 0 && !row_needed(a, sh->late_b, sh->late_s)) sh->abort_row = 1;
+        __syncthreads();
+        if (sh->abort_row) return;
         const int tie = (!normal_key || 2 * ntie <= (unsigned long long)ks.count + 1ull)
                             ? tie_scan<false>(sh, a, g, V, ks.key, ntie)
                             : tie_scan<true>(sh, a, g, V, ks.key, (unsigned long long)ks.count - ntie + 1ull);
+        if (tie == -2) {
+            if (tid == 0) sh->abort_row = 1;
+            __syncthreads();
+            return;
+        }
         if (tid == 0) {
             if (tie < 0) atomicOr(&a.ws->err, 16u);
             put_desc(a, ti, m, ks.key, tie, skept, 0, 0u);
@@ -2334,6 +2351,8 @@ __global__ void __launch_bounds__(kRT, DSV_ROWS_MIN_CTAS) rows_kernel(VerifyArgs
                 const bool watch = a.cand != nullptr && half < 0;
                 sh->watch_b = watch ? ti.b : -1;
                 sh->watch_s = watch ? ti.s : -1;
+                sh->late_b = sh->watch_b;
+                sh->late_s = sh->watch_s;
             }
             sh->abort_row = 0;
             sh->hbm_vecs = 0u;
