@@ -389,8 +389,8 @@ def run_dspine(args):
     line = None
     if rank == 0:
         alg_bytes = batch.algorithmic_bytes()
-        # the bf16 path drops rows that cannot change an outcome: the roofline is taken on the
-        # bytes it read (counted by the kernel); the fp32 cluster path reads every row
+        # verification drops rows that cannot change an outcome: the roofline is taken on the
+        # bytes it read (counted by the kernels)
         read_bytes = bytes_read if bytes_read > 0 else float(alg_bytes)
         deciding = batch.deciding_bytes(out[0])
         kernel_ms = statistics.mean(step_ms)

@@ -114,6 +114,7 @@ struct Shared {
     int flag_final;
     int flag_compact;
     int cut_found;
+    int skip;          // rank 0: the task (or its bonus) cannot change the request's outcome
     unsigned long long seg[1];  // segment sums; sized at launch
 };
 
@@ -975,6 +976,20 @@ __device__ void finalize_request(const VerifyArgs& a, int b, int cap) {
 }  // namespace
 
 // ---------------------------------------------------------------------------------------
+// Early exit: a chain stops at its first rejected step, so a task past a known rejection of
+// its request cannot change any output.  racc[2 b] holds 16 - r for the earliest rejected step
+// r found so far (0: none; reset by the request's finalisation).  The decision to drop is
+// rank 0's, shared through DSMEM after a cluster barrier, so every CTA of the cluster takes
+// the same branches.
+template <int kC>
+__device__ bool cluster_past_rejection(const VerifyArgs& a, Shared* sh, cg::cluster_group& cluster,
+                                       int& bar_i, int b, int s) {
+    if (cluster.block_rank() == 0 && threadIdx.x == 0)
+        sh->skip = a.cand != nullptr && 16 - s < (int)*(volatile unsigned*)&a.racc[2 * b];
+    cluster.sync();
+    bar_i++;
+    return *cluster.map_shared_rank(&sh->skip, 0) != 0;
+}
 
 template <typename T, int kC>
 __global__ void __launch_bounds__(kNT) verify_kernel(VerifyArgs a) {
@@ -1074,10 +1089,16 @@ __global__ void __launch_bounds__(kNT) verify_kernel(VerifyArgs a) {
                 }
             }
             __syncthreads();
-            load_slices<T>(cx, nrows);
-            pass_max<T, kC>(cx, cluster, nrows);
-
-            if (greedy) {
+            const bool drop = cluster_past_rejection<kC>(a, sh, cluster, cx.bar_i, b, s);
+            if (!drop) {
+                load_slices<T>(cx, nrows);
+                if (tid == 0 && cx.n > 0)  // the workspace's count of logit bytes read
+                    atomicAdd(&a.ws->bytes_read, (unsigned long long)cx.n * sizeof(T) * (unsigned)nrows);
+                pass_max<T, kC>(cx, cluster, nrows);
+            }
+            if (drop) {
+                // nothing to compute: only the completion signal below
+            } else if (greedy) {
                 // one-hot p at the argmax, one-hot q at the drafted token: closed form
                 if (cx.rank == 0 && tid == 0) {
                     const Task& tk = sh->tk;
@@ -1093,6 +1114,7 @@ __global__ void __launch_bounds__(kNT) verify_kernel(VerifyArgs a) {
                     res->d = d;
                     res->p = 0.0f;
                     res->q = 0.0f;
+                    if (!d && s < cap - 1) atomicMax(&a.racc[2 * b], (unsigned)(16 - s));
                     int bonus = -1;
                     if (!d || s == cap - 1) {
                         const long long thr = scale_floor(tk.uf, 1ull << kFixBits);
@@ -1111,8 +1133,11 @@ __global__ void __launch_bounds__(kNT) verify_kernel(VerifyArgs a) {
                     res->p = sh->tk.p;
                     res->q = sh->tk.q;
                     res->bonus = -1;
+                    if (!sh->tk.d && s < cap - 1) atomicMax(&a.racc[2 * b], (unsigned)(16 - s));
                 }
-                if (sh->tk.need_bonus) bonus_draw<T, kC>(cx, cluster, nrows);
+                // the bonus of a rejected step counts only if no earlier step is rejected
+                if (sh->tk.need_bonus && !cluster_past_rejection<kC>(a, sh, cluster, cx.bar_i, b, s))
+                    bonus_draw<T, kC>(cx, cluster, nrows);
             }
 
             // completion signal; the last task of the request finalizes it
@@ -1127,6 +1152,7 @@ __global__ void __launch_bounds__(kNT) verify_kernel(VerifyArgs a) {
                         __threadfence();
                         finalize_request(a, b, cap);
                         a.done[b] = 0;
+                        a.racc[2 * b] = 0u;  // the earliest rejection, for the next launch
                         __threadfence();
                         const unsigned fo = atomicAdd(&a.ws->finalized, 1u);
                         sh->flag_compact = (fo == (unsigned)(a.B - 1));

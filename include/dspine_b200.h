@@ -68,12 +68,12 @@ int dsv_workspace_init(void* workspace, size_t bytes, dsv_stream_t stream);
  * bit 0: a shared-memory bulk copy did not complete within its time limit;
  * bit 1: a request addressed a row outside the logit tensors. */
 int dsv_workspace_error(void* workspace, uint32_t* err, dsv_stream_t stream);
-/* Logit bytes that bf16 verifications and target-probability calls through this workspace
+/* Logit bytes that verifications and bf16 target-probability calls through this workspace
  * have read from memory since it was last zeroed (synchronizes `stream`).  Verification takes
  * the rows in verify-position order across the batch and drops the rows after a step already
- * known to be rejected (the chain stops there) and the rows of a request whose outcome is
- * already known, when it reaches them or while it reads them: those rows cannot change any
- * output.  No counterpart in the reference (a diagnostic). */
+ * known to be rejected (the chain stops there) and, for bf16 logits, the rows of a request
+ * whose outcome is already known, when it reaches them or while it reads them: those rows
+ * cannot change any output.  No counterpart in the reference (a diagnostic). */
 int dsv_workspace_bytes_read(const void* workspace, uint64_t* bytes, dsv_stream_t stream);
 /* bit 2 of the error word: a compaction read a KV slot position outside `slots_len`;
  * bits 3-4: a selection or a tie cut found no boundary (inconsistent input); bit 6: a chain

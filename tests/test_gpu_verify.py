@@ -209,13 +209,15 @@ def test_split_rows_match_oracle(case):
     assert_same(run_kernel(batch), oracle_verify(batch), f"split rows {case}")
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 @pytest.mark.parametrize("case", ["accept", "reject", "mixed"])
-def test_dropped_rows_do_not_change_outputs(case):
+def test_dropped_rows_do_not_change_outputs(case, dtype):
     """A chain stops at its first rejected step, so the row kernel drops (at dequeue, or during
     a row's first pass) the rows after a known rejection and the rows of a request whose outcome
     is known.  Drafts equal to the target accept every step (no row can be dropped), drafts
     opposite to it reject at once (most rows are dropped); outputs equal the oracle's, which
-    processes every row, and the bytes read show what was dropped."""
+    processes every row, and the bytes read show what was dropped.  fp32 logits take the
+    cluster kernel, which drops whole (request, position) tasks past a known rejection."""
     g = torch.Generator().manual_seed(77)
     B, V = 64, 4099
     lens = torch.full((B,), 16, dtype=torch.int32)
@@ -226,8 +228,8 @@ def test_dropped_rows_do_not_change_outputs(case):
                         torch.tensor(20)).to(torch.int32)
     top_p = 0.7 + 0.3 * torch.rand(B, generator=g)
     batch = workloads.build(lens, temperature, top_k, top_p, V=V, dtype=torch.float32, seed=9)
-    batch.target_logits = batch.target_logits.to(torch.bfloat16)
-    batch.draft_logits = batch.draft_logits.to(torch.bfloat16)
+    batch.target_logits = batch.target_logits.to(dtype)
+    batch.draft_logits = batch.draft_logits.to(dtype)
     if case == "accept":
         # draft row (b, s) is target row (b, s), so q = p; drafted tokens are each row's first
         # argmax (kept by every filter; what greedy requests accept)
@@ -246,7 +248,7 @@ def test_dropped_rows_do_not_change_outputs(case):
     got = run_kernel(batch)
     read = ws.bytes_read() - before
     expected = oracle_verify(batch)
-    assert_same(got, expected, f"dropped rows {case}")
+    assert_same(got, expected, f"dropped rows {case} {dtype}")
     all_rows = batch.algorithmic_bytes()
     if case == "accept":
         assert (expected[0] == batch.verify_lens.cpu().numpy() - 1).all()
