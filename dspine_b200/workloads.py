@@ -255,7 +255,11 @@ def config4(seed=4, device="cpu", V=VOCAB, B=256) -> Batch:
     lens = torch.randint(1, T + 1, (B,), generator=g, dtype=torch.int32)
     buckets = [1, 2, 4, 8, 16, 32, 64, 128, 256]
     widths = {bs: int(w) for bs, w in zip(buckets, torch.randint(4, 17, (len(buckets),), generator=g))}
-    width = widths[min(bk for bk in buckets if bk >= B)] if B <= 256 else 16
+    # the verify width of the batch's bucket from an SPS policy holding that table (the
+    # reference's DSpineSpsPolicy.width, verification/policy.py)
+    from dspine_b200.verification.policy import SpsPolicy
+    policy = SpsPolicy(verify_widths=widths)
+    width = policy.width(min(bk for bk in buckets if bk >= B)) if B <= 256 else 16
     temperature = torch.where(torch.arange(B) % 2 == 0, torch.zeros(B), torch.ones(B))
     top_k = torch.where(temperature == 0, torch.ones(B, dtype=torch.int32),
                         torch.full((B,), TOPK_OFF, dtype=torch.int32))
