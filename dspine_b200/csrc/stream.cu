@@ -22,7 +22,7 @@
 //                   other rows: bf16x2 max pass from HBM (greedy rows: and the first index of
 //                           the max; they finish here), then the candidate window (top-k <= 256)
 //                           or exact count walks from the top, from L2
-//   chain tasks   (in the same persistent kernel) kCP CTAs per sampled request once its
+//   chain tasks   (in the same persistent kernel) up to kCP CTAs per sampled request once its
 //                 outcome is known: the residual (p - q)+ draw over target row a and draft row a
 //                 of the stopping position a, the five outputs and, for the last request, the
 //                 accept-compact.
@@ -483,7 +483,7 @@ __device__ void key_range(int target, uint32_t kmin, uint32_t kmax, float m, flo
 #define DSV_RING_VECS (2 * DSV_ROWS_THREADS)
 #endif
 #ifndef DSV_SPLIT_POS
-#define DSV_SPLIT_POS 2  // verification splits the rows of the first DSV_SPLIT_POS positions
+#define DSV_SPLIT_POS 3  // verification splits the rows of the first DSV_SPLIT_POS positions
 #endif
 constexpr int kSplitPos = DSV_SPLIT_POS;
 constexpr int kRT = DSV_ROWS_THREADS;  // threads per CTA
@@ -1706,7 +1706,7 @@ __device__ void write_request(const VerifyArgs& a, int b, int acc, long long bon
 }
 
 // ---------------------------------------------------------------------------------------
-// chain + bonus + outputs: kCP CTAs per request, no cluster
+// chain + bonus + outputs: up to kCP CTAs per request (chain_slices), no cluster
 //
 // Every CTA of a request decides the chain (warp 0, one lane per step), then takes one slice
 // of the bonus row: the slice's exact residual mass goes to the request's task-result area in
@@ -1809,6 +1809,16 @@ constexpr int kCTileV = 4 * kCT;           // vectors per tile: 4 consecutive pe
 constexpr int kCMaxTiles = 1;              // tiles per slice (kCP x kCMaxTiles <= 32): V <= kMaxV
 static_assert(kCMaxTiles == 1, "the crossing search takes the slice as its tile");
 constexpr int kMaxV = 8 * (kCP * kCMaxTiles * kCTileV - kCP) - 16;  // vectors of every slice fit
+
+// Slices (chain tasks) per sampled request for rows of V elements: as few as keep every slice
+// within one tile (a row at any alignment spans at most (V + 14) / 8 vectors), at most kCP.
+// Fewer, fuller slices: the per-task costs (descriptor loads, block sums, the dequeue) are paid
+// fewer times (V = 151936: 19 slices instead of 32).
+__device__ __forceinline__ int chain_slices(int V) {
+    const int nvp = (V + 14) >> 3;
+    const int n = (nvp + kCTileV - 1) / kCTileV;
+    return n < 1 ? 1 : (n > kCP ? kCP : n);
+}
 
 __device__ __forceinline__ bool kept_in(const RowDesc& d, uint32_t u16, int i) {
     const uint32_t k = okey(u16);
@@ -1946,7 +1956,8 @@ __device__ bool chain_task(const VerifyArgs& a, ChainSmem* sh, int b, int rank) 
     r.qvec = r.qrow && (int)((reinterpret_cast<uintptr_t>(r.qrow) & 15u) >> 1) == r.poff;
     // this CTA's slice of vectors, in tiles of kCTileV; tile masses go to the request's
     // task-result area (kCP x kCMaxTiles u64)
-    const int per = (r.nvp + kCP - 1) / kCP;
+    const int ncp = chain_slices(V);
+    const int per = (r.nvp + ncp - 1) / ncp;
     const int v0 = min(rank * per, r.nvp), v1 = min(v0 + per, r.nvp);
     unsigned long long* tmass = reinterpret_cast<unsigned long long*>(a.res) + (size_t)b * kT * 2;
     auto slice_tiles = [&](int q, bool pure_) -> unsigned long long {
@@ -1971,22 +1982,22 @@ __device__ bool chain_task(const VerifyArgs& a, ChainSmem* sh, int b, int rank) 
     if (tid == 0) {
         __threadfence();
         const unsigned old = atomicAdd(&a.done[b], 1u);
-        sh->last = old == (unsigned)(kCP - 1);
+        sh->last = old == (unsigned)(ncp - 1);
     }
     __syncthreads();
     if (sh->last) {
         __threadfence();
         bool pure = pure0;
-        if (tid < kCP) sh->slice[tid] = __ldcg(&tmass[tid * kCMaxTiles]);  // one tile per slice
+        if (tid < ncp) sh->slice[tid] = __ldcg(&tmass[tid * kCMaxTiles]);  // one tile per slice
         __syncthreads();
         unsigned long long M = 0;
 #pragma unroll
-        for (int q = 0; q < kCP; ++q) M += sh->slice[q];
+        for (int q = 0; q < ncp; ++q) M += sh->slice[q];
         if (!pure && M == 0) {
             // zero residual mass: draw from p (this CTA recomputes every slice)
             pure = true;
             M = 0;
-            for (int q = 0; q < kCP; ++q) {
+            for (int q = 0; q < ncp; ++q) {
                 const unsigned long long t = slice_tiles(q, true);
                 if (tid == 0) sh->slice[q] = t;
                 M += t;
@@ -2001,7 +2012,7 @@ __device__ bool chain_task(const VerifyArgs& a, ChainSmem* sh, int b, int rank) 
             // the crossing slice and tile from the totals, then the tile element by element
             long long base = 0;
             int qs = -1, tq = -1;
-            for (int q = 0; q < kCP && qs < 0; ++q) {
+            for (int q = 0; q < ncp && qs < 0; ++q) {
                 const long long t = (long long)sh->slice[q];
                 if (base + t > thr) {
                     qs = q;
@@ -2239,16 +2250,18 @@ __global__ void __launch_bounds__(kRT, DSV_ROWS_MIN_CTAS) rows_kernel(VerifyArgs
     // Task sources.  Row tasks come in plan order (positions first, see Plan).  Some rows are
     // split in two halves, up to the workspace's slot count: in verification, the rows of the
     // first kSplitPos positions (the rows most likely to decide a chain: two CTAs halve the
-    // latency of their histogram pass), as tasks 2 r and 2 r + 1 of row r < nfront; for target
+    // latency of their histogram pass; positions 0-2 measured 1.5% faster than 0-1 on config
+    // 1), as tasks 2 r and 2 r + 1 of row r < nfront; for target
     // probabilities, the rows beyond the first wave (index >= grid), whose halves shorten the
     // tail: row task x maps to row x below the grid, to row G + (x - G) / 2, half (x - G) % 2
     // for the next 2 * nsplit tasks, and to row x - nsplit after.  After its first row a CTA
-    // takes, in order: (1) a chain task of a request whose outcome is known (kCP bonus slices
+    // takes, in order: (1) a chain task of a request whose outcome is known (ncp bonus slices
     // per sampled request, from the ready list), (2) the next row task that can still change
     // an outcome (rows after a known rejection, or of a request already claimed, are dropped
     // at dequeue or abandoned during their first pass), (3) a chain task whose request is not
     // ready yet (every row has been taken by then, so it will be; the wait is bounded).
     const int nrows = total_tasks(a, sh);
+    const int ncp = chain_slices(a.V);  // chain tasks per sampled request
     const int G = (int)gridDim.x;
     const bool verifying = a.cand != nullptr;
     const int nfront = (verifying && kSplitPos > 0 && a.split_cap > 0)
@@ -2279,7 +2292,7 @@ __global__ void __launch_bounds__(kRT, DSV_ROWS_MIN_CTAS) rows_kernel(VerifyArgs
             ns += __popc(__ballot_sync(0xffffffffu, b < a.B && (sh->plan.req[b] & 7u) != (unsigned)kGreedy));
         }
         if (lane == 0) {
-            sh->q_nchain = a.cand != nullptr ? ns * kCP : 0;
+            sh->q_nchain = a.cand != nullptr ? ns * ncp : 0;
             sh->q_sel_empty = 0;
         }
     }
@@ -2295,7 +2308,7 @@ __global__ void __launch_bounds__(kRT, DSV_ROWS_MIN_CTAS) rows_kernel(VerifyArgs
             auto try_chain = [&]() {
                 // a chain task of a published request, claimed only below the published count
                 for (int tries = 0; tries < 4; ++tries) {
-                    const unsigned ready = *(volatile unsigned*)&a.ws->ready_tail * (unsigned)kCP;
+                    const unsigned ready = *(volatile unsigned*)&a.ws->ready_tail * (unsigned)ncp;
                     const unsigned cn = *(volatile unsigned*)&a.ws->chain_next;
                     if (cn >= ready || cn >= (unsigned)nchain) return false;
                     if (atomicCAS(&a.ws->chain_next, cn, cn + 1u) == cn) {
@@ -2341,7 +2354,7 @@ __global__ void __launch_bounds__(kRT, DSV_ROWS_MIN_CTAS) rows_kernel(VerifyArgs
                 }
             }
             if (kind == 2) {
-                const int b = wait_ready(a, t / kCP);
+                const int b = wait_ready(a, t / ncp);
                 if (b < 0) kind = 3;  // gave up: the request stays unfinished (error bit 6)
                 sh->q_b = b;
             }
@@ -2382,7 +2395,7 @@ __global__ void __launch_bounds__(kRT, DSV_ROWS_MIN_CTAS) rows_kernel(VerifyArgs
             // an abandoned row is not done (nothing waits for it); a first half is not a row
             finished = (sh->abort_row || half == 0) ? false : row_finish(sh, a, ti);
         } else {
-            finished = chain_task(a, csh, sh->q_b, t % kCP);
+            finished = chain_task(a, csh, sh->q_b, t % ncp);
         }
         if (finished) finalize_request(a, csh);
 #ifdef DSV_PROFILE
