@@ -418,6 +418,7 @@ def run_dspine(args):
                          "kernel": "dsv::rows_kernel (the whole dsv_verify_logits call: rows and chain tasks)",
                          "bytes_read_per_launch": read_bytes,
                          "algorithmic_bytes_per_launch": alg_bytes,
+                         "frac_on_algorithmic_bytes": alg_bytes / (kernel_ms * 1e-3) / 1e9 / peak,
                          "deciding_bytes_per_launch": deciding,
                          "bytes_basis": "rows read (rows that cannot change an outcome are "
                                         "dropped; all rows of the batch: algorithmic_bytes, "
