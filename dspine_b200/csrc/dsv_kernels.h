@@ -92,7 +92,10 @@ constexpr inline size_t verify_base_bytes(int B) {
 // Split rows (streaming path): nucleus rows beyond the first wave of the row kernel are
 // processed as two halves by two CTAs; the first half publishes its per-key histogram here.
 // [kSplitCap slots of kSplitSlotBytes][u32 flag x kSplitCap]
-constexpr int kSplitCap = 256;
+#ifndef DSV_SPLIT_CAP
+#define DSV_SPLIT_CAP 256
+#endif
+constexpr int kSplitCap = DSV_SPLIT_CAP;
 constexpr size_t kSplitSlotBytes = 8192 * 4 + 16 + 512 * 2 + 48;  // counts, meta, band, pad
 constexpr inline size_t verify_split_offset(int B) { return verify_base_bytes(B); }
 constexpr inline size_t verify_workspace_bytes(int B) {
