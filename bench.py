@@ -348,24 +348,28 @@ def run_dspine(args):
     ms_per_step = total_ms / args.steps
     value = all_tokens / (ms_per_step * 1e-3)
 
-    # ---- end to end: pinned host inputs -> device, verify, outputs -> host, every step ----
+    # ---- end to end: the public call on pinned host inputs (verify.verify_logits_host: it
+    # copies to the device the logit rows the outcome can depend on, in widening windows of
+    # verify positions, verifies, compacts and reads the outputs back), every step ----
     inputs = {**kw, "slots": batch.slots, "slot_rows": batch.slot_rows}
-    dev_in = {k: v for k, v in inputs.items() if v is not None}
-    host_in = {k: v.cpu().pin_memory() for k, v in dev_in.items()}
-    host_out = [o.cpu().pin_memory() for o in out]
-    h2d = sum(v.numel() * v.element_size() for v in host_in.values())
-    d2h = sum(o.numel() * o.element_size() for o in host_out)
+    host_in = {k: v.cpu().pin_memory() for k, v in inputs.items() if v is not None}
     e2e_steps = max(3, min(args.steps, 20))
+    h2d_total = d2h_total = 0
+    windows = ()
 
     def e2e_step():
-        for k, v in host_in.items():
-            dev_in[k].copy_(v, non_blocking=True)
-        verify.verify_logits(**dev_in, outputs=out, compact=comp, workspace=ws)
-        for h, o in zip(host_out, out):
-            h.copy_(o, non_blocking=True)
-        torch.cuda.current_stream(dev).synchronize()
+        nonlocal h2d_total, d2h_total, windows
+        host_out, _, info = verify.verify_logits_host(**host_in, device=dev)
+        h2d_total += info.h2d_bytes
+        d2h_total += info.d2h_bytes
+        windows = info.windows
+        return host_out
 
-    e2e_step()
+    check = e2e_step()
+    for got, want in zip(check, out):
+        if not torch.equal(got, want.cpu()):
+            raise SystemExit("host-input verification differs from the device-input call")
+    h2d_total = d2h_total = 0
     barrier()
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     e0.record()
@@ -374,6 +378,8 @@ def run_dspine(args):
     e1.record()
     barrier()
     e2e_ms = e0.elapsed_time(e1) / e2e_steps
+    h2d = h2d_total / e2e_steps
+    d2h = d2h_total / e2e_steps
     if dist is not None:
         t = torch.tensor([e2e_ms], dtype=torch.float64, device=dev)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -410,7 +416,11 @@ def run_dspine(args):
                        "l2": "flushed before every timed step (256 MiB memset, untimed)"},
             "clocks": sampler.summary(),
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h},
+                    "d2h_bytes_per_step": d2h,
+                    "call": "verify.verify_logits_host (pinned host inputs; logit rows copied in "
+                            "widening windows of verify positions, outputs read back)",
+                    "windows": list(windows),
+                    "all_input_bytes": sum(v.numel() * v.element_size() for v in host_in.values())},
             "gpu_launches": all_launches,
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                          "frac": achieved / peak, "traffic": traffic,

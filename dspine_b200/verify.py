@@ -269,3 +269,150 @@ def verify_logits_noalloc(*, candidates, target_logits, target_rows, temperature
     with torch.cuda.device(dev):
         _lib.call("dsv_verify_logits_noalloc", *args, _lib.ptr(device_error), _stream(dev))
     return outputs
+
+
+# ---- verification from host-resident logits -------------------------------------------------
+
+_staging: dict = {}
+
+
+def _device_rows(host: torch.Tensor, device, slot: str) -> torch.Tensor:
+    """A device buffer shaped like the host logits (reused across calls; never zeroed: only
+    the rows a call copies are read)."""
+    key = (slot, torch.device(device), tuple(host.shape), host.dtype)
+    buf = _staging.get(key)
+    if buf is None:
+        buf = torch.empty(host.shape, dtype=host.dtype, device=device)
+        _staging[key] = buf
+    return buf
+
+
+@dataclass
+class HostVerifyInfo:
+    """What a verify_logits_host call moved: logit bytes copied to the device, bytes read back,
+    and the windows (verify positions per request) of its rounds."""
+    h2d_bytes: int
+    d2h_bytes: int
+    windows: tuple
+
+
+def window_rounds(lens, first_window, run_round):
+    """The widening windows of verify_logits_host.  ``run_round(pending, lo, W)`` verifies the
+    requests ``pending`` with their lengths capped at W (the rows of positions [lo, W) are new
+    to this round) and returns their accepted lengths, in order, and a callable that keeps the
+    results of the requests it is given (positions in ``pending``).  A request is final once
+    its capped chain stops before the cap (accepted length < W - 1) or its length is at most
+    W: the capped run then takes the same steps, rows and uniforms as the full one.  Returns
+    the windows used."""
+    pending = list(range(len(lens)))
+    lo, W, windows = 0, int(first_window), []
+    while pending:
+        windows.append(W)
+        acc, keep = run_round(pending, lo, W)
+        done = [int(a) < W - 1 or int(lens[b]) <= W for b, a in zip(pending, acc)]
+        if any(done):
+            keep([i for i, f in enumerate(done) if f])
+        pending = [b for b, f in zip(pending, done) if not f]
+        lo, W = W, 2 * W
+    return tuple(windows)
+
+
+def verify_logits_host(*, candidates, target_logits, target_rows, temperature, top_k, top_p,
+                       verify_lens, uniforms, uniform_final, prefix_lens, device,
+                       draft_logits=None, draft_rows=None, slots=None, slot_rows=None,
+                       min_p=None, mode: int = JOINT, first_window: int = 2):
+    """verify_logits for inputs in host memory (CPU tensors; pinned ones copy asynchronously),
+    copying to the device only the logit rows the outcome can depend on.
+
+    A chain stops at its first rejected step, so rounds widen a window of verify positions:
+    round 1 copies the rows of positions [0, W) of every request (W = first_window) and
+    verifies with each request's length capped at W.  A request whose chain is rejected at a
+    step s < W - 1, or whose length is at most W, has its final outcome (the capped run takes
+    the same steps, rows and uniforms); the others are verified again with the window doubled,
+    after the rows of the new positions are copied.  The outputs equal verify_logits on the
+    whole batch bit for bit; compaction (``slots`` / ``slot_rows``) runs once at the end with
+    the true lengths.  Returns host tensors (accept, commit, bonus, output, new_seq), the host
+    CompactOutputs (or None) and a HostVerifyInfo."""
+    dev = torch.device(device)
+    _check(dev.type == "cuda", "verify_logits_host needs a CUDA device")
+    host = [candidates, target_logits, target_rows, temperature, top_k, top_p, verify_lens,
+            uniforms, uniform_final, prefix_lens]
+    _check(all(t.device.type == "cpu" for t in host) and
+           (draft_logits is None or (draft_logits.device.type == "cpu" and
+                                     draft_rows is not None and draft_rows.device.type == "cpu")),
+           "verify_logits_host takes CPU tensors")
+    _check(first_window >= 2, "the first window must hold at least two positions")
+    B = candidates.shape[0]
+    lens = verify_lens.numpy().astype("int64").clip(1, T)
+    trow = target_rows.numpy()
+    greedy = ((top_k <= 1) | ~(temperature > 0)).numpy()
+    with_draft = draft_logits is not None
+    drow = draft_rows.numpy() if with_draft else None
+
+    def up(t):
+        return None if t is None else t.to(dev, non_blocking=True)
+
+    small = dict(candidates=up(candidates), target_rows=up(target_rows),
+                 temperature=up(temperature), top_k=up(top_k), top_p=up(top_p),
+                 verify_lens=up(verify_lens), uniforms=up(uniforms),
+                 uniform_final=up(uniform_final), prefix_lens=up(prefix_lens))
+    if with_draft:
+        small["draft_rows"] = up(draft_rows)
+    mp = up(min_p)
+    t_dev = _device_rows(target_logits, dev, "target")
+    d_dev = _device_rows(draft_logits, dev, "draft") if with_draft else None
+    row_bytes = target_logits.shape[1] * target_logits.element_size()
+    h2d = sum(t.numel() * t.element_size() for t in small.values())
+    d2h = 0
+    out = new_outputs(B, dev)
+    moved = [h2d, 0]
+
+    def run_round(pending, lo, W):
+        for b in pending:  # the rows of positions [lo, W) (clipped to the request's length)
+            hi = min(W, int(lens[b]))
+            if hi > lo:
+                r0 = int(trow[b])
+                t_dev[r0 + lo:r0 + hi].copy_(target_logits[r0 + lo:r0 + hi], non_blocking=True)
+                moved[0] += (hi - lo) * row_bytes
+            dhi = min(W, int(lens[b]) - 1)
+            if with_draft and not greedy[b] and dhi > lo:
+                r0 = int(drow[b])
+                d_dev[r0 + lo:r0 + dhi].copy_(draft_logits[r0 + lo:r0 + dhi], non_blocking=True)
+                moved[0] += (dhi - lo) * row_bytes
+        idx_h = torch.tensor(pending, dtype=torch.int64)
+        idx = idx_h.to(dev, non_blocking=True)
+        moved[0] += idx_h.numel() * 8
+        sub = {k: v.index_select(0, idx) for k, v in small.items()}
+        sub["verify_lens"] = sub["verify_lens"].clamp(max=W)
+        res = verify_logits(**sub, target_logits=t_dev, draft_logits=d_dev,
+                            min_p=None if mp is None else mp.index_select(0, idx), mode=mode)
+        acc = res[0].cpu()
+        moved[1] += acc.numel() * 4
+
+        def keep(positions):
+            sel = torch.tensor(positions, dtype=torch.int64).to(dev, non_blocking=True)
+            di = idx.index_select(0, sel)
+            for full, part in zip(out, res):
+                full.index_copy_(0, di, part.index_select(0, sel))
+
+        return acc.tolist(), keep
+
+    windows = window_rounds(lens, first_window, run_round)
+    h2d, d2h = moved
+    compact = None
+    if slots is not None:
+        from .accept import accept_compact  # the compaction with the true lengths
+        compact = accept_compact(out[1], small["verify_lens"], out[3], up(slots), up(slot_rows))
+    host_out = tuple(o.to("cpu", non_blocking=True) for o in out)
+    d2h += sum(o.numel() * o.element_size() for o in host_out)
+    host_compact = None
+    if compact is not None:
+        host_compact = CompactOutputs(*(t.to("cpu", non_blocking=True) for t in (
+            compact.tokens, compact.kept_slots, compact.offsets, compact.freed_slots,
+            compact.freed_offsets)))
+        d2h += sum(t.numel() * t.element_size() for t in (
+            compact.tokens, compact.kept_slots, compact.offsets, compact.freed_slots,
+            compact.freed_offsets))
+        h2d += slots.numel() * slots.element_size() + slot_rows.numel() * 8
+    torch.cuda.current_stream(dev).synchronize()
+    return host_out, host_compact, HostVerifyInfo(h2d, d2h, windows)

@@ -257,6 +257,54 @@ def test_dropped_rows_do_not_change_outputs(case, dtype):
         assert read < all_rows // 2
 
 
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+@pytest.mark.parametrize("case", ["random", "accept", "config1"])
+def test_host_inputs_copy_only_what_the_outcome_needs(case, dtype):
+    """verify_logits_host on CPU (pinned) inputs: rows copied in widening windows of verify
+    positions, each window verified with lengths capped at it; outputs and compaction equal the
+    device call on the whole batch (and the oracle), and fewer logit bytes cross to the device
+    unless every step is accepted."""
+    if case == "config1":
+        if dtype == torch.float32:
+            pytest.skip("config 1 is bf16")
+        batch = workloads.config1()
+    else:
+        batch = random_batch(4242, 48, 4099, dtype).to("cpu")
+        if case == "accept":
+            batch.draft_logits = batch.target_logits.clone()
+            batch.draft_rows = batch.target_rows.clone()
+            am = batch.target_logits.float().argmax(dim=1)
+            for b in range(batch.B):
+                n = int(batch.verify_lens[b])
+                r0 = int(batch.target_rows[b])
+                batch.candidates[b, 1:n] = am[r0:r0 + n - 1]
+    kw = {k: v.pin_memory() for k, v in batch.kwargs().items() if v is not None}
+    slots, slot_rows = batch.slots.pin_memory(), batch.slot_rows.pin_memory()
+    got, comp, info = verify.verify_logits_host(**kw, slots=slots, slot_rows=slot_rows,
+                                                device=DEV)
+    dev_batch = batch.to(DEV)
+    want_comp = verify.CompactOutputs.allocate(batch.B, DEV)
+    want = verify.verify_logits(**dev_batch.kwargs(), slots=dev_batch.slots,
+                                slot_rows=dev_batch.slot_rows, compact=want_comp)
+    torch.cuda.synchronize()
+    assert verify.workspace_for(batch.B, DEV).error_word() == 0
+    for g, w in zip(got, want):
+        assert torch.equal(g, w.cpu())
+    n_tok = int(want[1].sum())
+    assert torch.equal(comp.offsets, want_comp.offsets.cpu())
+    assert torch.equal(comp.tokens[:n_tok], want_comp.tokens[:n_tok].cpu())
+    assert torch.equal(comp.kept_slots[:n_tok], want_comp.kept_slots[:n_tok].cpu())
+    n_free = int(want_comp.freed_offsets[-1])
+    assert torch.equal(comp.freed_slots[:n_free], want_comp.freed_slots[:n_free].cpu())
+    if case != "accept":
+        assert_same(got, oracle_verify(batch), f"host inputs {case}")
+    logit_bytes = batch.target_logits.numel() * batch.target_logits.element_size() + (
+        batch.draft_logits.numel() * batch.draft_logits.element_size())
+    if case == "config1":
+        assert info.h2d_bytes < logit_bytes // 2
+    assert info.windows[0] == 2
+
+
 @pytest.mark.parametrize("B,V", [(1, 1031), (1024, 521), (1025, 521)])
 def test_batch_limits_match_oracle(B, V):
     """One request; the largest batch of the one-launch bf16 path (1024: the task table and the
