@@ -59,6 +59,8 @@ _SIGNATURES = {
     "dsv_workspace_init": [c_void_p, c_size_t, c_void_p],
     "dsv_workspace_error": [c_void_p, ctypes.POINTER(ctypes.c_uint32), c_void_p],
     "dsv_workspace_bytes_read": [c_void_p, ctypes.POINTER(ctypes.c_uint64), c_void_p],
+    "dsv_copy_row_ranges": [c_void_p, c_void_p, ctypes.c_size_t, ctypes.c_int32, c_void_p, c_void_p,
+                            c_void_p],
     "dsv_verify_logits": [c_int32, c_int32, c_int32, c_void_p, c_void_p, c_void_p, c_int64,
                           c_void_p, c_void_p, c_int64, c_int64, c_void_p, c_void_p, c_void_p,
                           c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p,

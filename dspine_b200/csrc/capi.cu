@@ -94,6 +94,38 @@ int dsv_workspace_error(void* ws, uint32_t* err, dsv_stream_t stream) {
     return DSV_OK;
 }
 
+int dsv_copy_row_ranges(void* dst, const void* src, size_t row_bytes, int32_t n,
+                        const int64_t* first_row, const int64_t* n_rows, dsv_stream_t stream) {
+    if (n < 0) return DSV_BAD_SHAPE;
+    if (n == 0) return DSV_OK;
+    if (dst == nullptr || src == nullptr || first_row == nullptr || n_rows == nullptr)
+        return DSV_BAD_POINTER;
+    char* d = static_cast<char*>(dst);
+    const char* s = static_cast<const char*>(src);
+    int64_t r0 = -1, nr = 0;  // the range being merged
+    for (int32_t i = 0; i <= n; ++i) {
+        if (i < n) {
+            if (first_row[i] < 0 || n_rows[i] < 0) return DSV_BAD_SHAPE;
+            if (n_rows[i] == 0) continue;
+            if (r0 >= 0 && r0 + nr == first_row[i]) {
+                nr += n_rows[i];
+                continue;
+            }
+        }
+        if (r0 >= 0 && nr > 0) {
+            const size_t off = (size_t)r0 * row_bytes;
+            if (cudaMemcpyAsync(d + off, s + off, (size_t)nr * row_bytes, cudaMemcpyHostToDevice,
+                                (cudaStream_t)stream) != cudaSuccess)
+                return DSV_LAUNCH_FAILED;
+        }
+        if (i < n) {
+            r0 = first_row[i];
+            nr = n_rows[i];
+        }
+    }
+    return DSV_OK;
+}
+
 int dsv_workspace_bytes_read(const void* ws, uint64_t* bytes, dsv_stream_t stream) {
     if (ws == nullptr || bytes == nullptr) return DSV_BAD_POINTER;
     const dsv::WsHeader* h = reinterpret_cast<const dsv::WsHeader*>(ws);

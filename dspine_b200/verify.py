@@ -12,6 +12,7 @@ from __future__ import annotations
 import ctypes
 from dataclasses import dataclass
 
+import numpy as np
 import torch
 
 from . import _lib
@@ -342,6 +343,10 @@ def verify_logits_host(*, candidates, target_logits, target_rows, temperature, t
                                      draft_rows is not None and draft_rows.device.type == "cpu")),
            "verify_logits_host takes CPU tensors")
     _check(first_window >= 2, "the first window must hold at least two positions")
+    _check(target_logits.is_contiguous() and (draft_logits is None or draft_logits.is_contiguous()),
+           "host logits must be contiguous")
+    _check(draft_logits is None or draft_logits.shape[1] == target_logits.shape[1],
+           "draft vocab differs")
     B = candidates.shape[0]
     lens = verify_lens.numpy().astype("int64").clip(1, T)
     trow = target_rows.numpy()
@@ -367,18 +372,23 @@ def verify_logits_host(*, candidates, target_logits, target_rows, temperature, t
     out = new_outputs(B, dev)
     moved = [h2d, 0]
 
+    stream = _stream(dev)
+
+    def copy_ranges(dst, src, first, count):
+        first = np.ascontiguousarray(first, dtype=np.int64)
+        count = np.ascontiguousarray(count, dtype=np.int64)
+        _lib.call("dsv_copy_row_ranges", dst.data_ptr(), src.data_ptr(), row_bytes, len(first),
+                  first.ctypes.data, count.ctypes.data, stream)
+        moved[0] += int(count.sum()) * row_bytes
+
     def run_round(pending, lo, W):
-        for b in pending:  # the rows of positions [lo, W) (clipped to the request's length)
-            hi = min(W, int(lens[b]))
-            if hi > lo:
-                r0 = int(trow[b])
-                t_dev[r0 + lo:r0 + hi].copy_(target_logits[r0 + lo:r0 + hi], non_blocking=True)
-                moved[0] += (hi - lo) * row_bytes
-            dhi = min(W, int(lens[b]) - 1)
-            if with_draft and not greedy[b] and dhi > lo:
-                r0 = int(drow[b])
-                d_dev[r0 + lo:r0 + dhi].copy_(draft_logits[r0 + lo:r0 + dhi], non_blocking=True)
-                moved[0] += (dhi - lo) * row_bytes
+        # the rows of positions [lo, W), clipped to each request's length (drafts: length - 1)
+        pb = np.asarray(pending)
+        n_t = np.clip(np.minimum(W, lens[pb]) - lo, 0, None)
+        copy_ranges(t_dev, target_logits, trow[pb] + lo, n_t)
+        if with_draft:
+            n_d = np.clip(np.minimum(W, lens[pb] - 1) - lo, 0, None) * (~greedy[pb])
+            copy_ranges(d_dev, draft_logits, drow[pb] + lo, n_d)
         idx_h = torch.tensor(pending, dtype=torch.int64)
         idx = idx_h.to(dev, non_blocking=True)
         moved[0] += idx_h.numel() * 8

@@ -58,10 +58,11 @@ uint64_t dsv_launch_count(void);
  * and (last 8.5 MB) the slots through which the two halves of a split row meet.  Zero it once
  * after allocation (dsv_workspace_init); every launch that ends without an internal failure
  * (error bits 0, 5-7 below) leaves it zeroed again for the next launch with the same batch
- * size, except for a counter of the logit bytes read (dsv_workspace_bytes_read).  Its regions are laid out by the batch size, so a workspace sized for the largest
- * batch serves smaller ones, but must be zeroed again when the batch size changes.  A workspace
- * without the split-row slots (the size for the batch minus that region) is accepted and then
- * no row is split. */
+ * size, except for a counter of the logit bytes read (dsv_workspace_bytes_read).  Its regions
+ * are laid out by the batch size, so a workspace sized for the largest batch serves smaller
+ * ones, but must be zeroed again when the batch size changes.  A workspace without the
+ * split-row slots (the size for the batch minus that region) is accepted and then no row is
+ * split. */
 int dsv_verify_workspace_size(int32_t batch, size_t* bytes);
 int dsv_workspace_init(void* workspace, size_t bytes, dsv_stream_t stream);
 /* Copy the device error word of a workspace to *err and clear it (synchronizes `stream`).
@@ -75,6 +76,14 @@ int dsv_workspace_error(void* workspace, uint32_t* err, dsv_stream_t stream);
  * whose outcome is already known, when it reaches them or while it reads them: those rows
  * cannot change any output.  No counterpart in the reference (a diagnostic). */
 int dsv_workspace_bytes_read(const void* workspace, uint64_t* bytes, dsv_stream_t stream);
+/* Host -> device copy of row ranges between two buffers of the same row layout (row_bytes
+ * apart): range i is rows [first_row[i], first_row[i] + n_rows[i]); ranges that continue one
+ * another are merged; one cudaMemcpyAsync per merged range on `stream` (pinned host memory
+ * makes them asynchronous).  The staged copies of dspine_b200.verify.verify_logits_host,
+ * which sends to the device only the logit rows the outcome can depend on.  No counterpart in
+ * the reference (SGLang's logits are on the device). */
+int dsv_copy_row_ranges(void* dst, const void* src, size_t row_bytes, int32_t n,
+                        const int64_t* first_row, const int64_t* n_rows, dsv_stream_t stream);
 /* bit 2 of the error word: a compaction read a KV slot position outside `slots_len`;
  * bits 3-4: a selection or a tie cut found no boundary (inconsistent input); bit 6: a chain
  * task waited past its time limit for its request; bit 7: the second half of a split row

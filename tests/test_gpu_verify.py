@@ -244,6 +244,7 @@ def test_dropped_rows_do_not_change_outputs(case, dtype):
         batch.draft_logits = -batch.draft_logits
     batch = batch.to(DEV)
     ws = verify.workspace_for(batch.B, DEV)
+    ws.prepare(batch.B)  # a change of batch size zeroes the workspace (and its byte counter)
     before = ws.bytes_read()
     got = run_kernel(batch)
     read = ws.bytes_read() - before
