@@ -291,16 +291,16 @@ def _device_rows(host: torch.Tensor, device, slot: str) -> torch.Tensor:
 @dataclass
 class HostVerifyInfo:
     """What a verify_logits_host call moved: logit bytes copied to the device, bytes read back,
-    and the windows (verify positions per request) of its rounds."""
+    and the windows (verify positions per request) of its stages."""
     h2d_bytes: int
     d2h_bytes: int
     windows: tuple
 
 
-def window_rounds(lens, first_window, run_round):
-    """The widening windows of verify_logits_host.  ``run_round(pending, lo, W)`` verifies the
+def window_stages(lens, first_window, run_stage):
+    """The widening windows of verify_logits_host.  ``run_stage(pending, lo, W)`` verifies the
     requests ``pending`` with their lengths capped at W (the rows of positions [lo, W) are new
-    to this round) and returns their accepted lengths, in order, and a callable that keeps the
+    to this stage) and returns their accepted lengths, in order, and a callable that keeps the
     results of the requests it is given (positions in ``pending``).  A request is final once
     its capped chain stops before the cap (accepted length < W - 1) or its length is at most
     W: the capped run then takes the same steps, rows and uniforms as the full one.  Returns
@@ -309,7 +309,7 @@ def window_rounds(lens, first_window, run_round):
     lo, W, windows = 0, int(first_window), []
     while pending:
         windows.append(W)
-        acc, keep = run_round(pending, lo, W)
+        acc, keep = run_stage(pending, lo, W)
         done = [int(a) < W - 1 or int(lens[b]) <= W for b, a in zip(pending, acc)]
         if any(done):
             keep([i for i, f in enumerate(done) if f])
@@ -325,8 +325,8 @@ def verify_logits_host(*, candidates, target_logits, target_rows, temperature, t
     """verify_logits for inputs in host memory (CPU tensors; pinned ones copy asynchronously),
     copying to the device only the logit rows the outcome can depend on.
 
-    A chain stops at its first rejected step, so rounds widen a window of verify positions:
-    round 1 copies the rows of positions [0, W) of every request (W = first_window) and
+    A chain stops at its first rejected step, so stages widen a window of verify positions:
+    stage 1 copies the rows of positions [0, W) of every request (W = first_window) and
     verifies with each request's length capped at W.  A request whose chain is rejected at a
     step s < W - 1, or whose length is at most W, has its final outcome (the capped run takes
     the same steps, rows and uniforms); the others are verified again with the window doubled,
@@ -381,7 +381,7 @@ def verify_logits_host(*, candidates, target_logits, target_rows, temperature, t
                   first.ctypes.data, count.ctypes.data, stream)
         moved[0] += int(count.sum()) * row_bytes
 
-    def run_round(pending, lo, W):
+    def run_stage(pending, lo, W):
         # the rows of positions [lo, W), clipped to each request's length (drafts: length - 1)
         pb = np.asarray(pending)
         n_t = np.clip(np.minimum(W, lens[pb]) - lo, 0, None)
@@ -407,7 +407,7 @@ def verify_logits_host(*, candidates, target_logits, target_rows, temperature, t
 
         return acc.tolist(), keep
 
-    windows = window_rounds(lens, first_window, run_round)
+    windows = window_stages(lens, first_window, run_stage)
     h2d, d2h = moved
     compact = None
     if slots is not None:

@@ -67,9 +67,14 @@ def check_against_exact(x, w, k, ids, vals, lse):
     region = hi >= kth - 1e-30
     unambiguous = ~((lo != hi) & region).any(dim=1)
     assert unambiguous.float().mean().item() >= 0.5
-    diff = unambiguous & ((e_ids != got_ids).any(dim=1) | (e_val != got_val).any(dim=1))
+    differs = (e_ids != got_ids).any(dim=1) | (e_val != got_val).any(dim=1)
+    diff = unambiguous & differs
     assert not diff.any(), f"{int(diff.sum())} unambiguous rows differ from the exact top-{kk}"
     torch.testing.assert_close(lse.double(), torch.logsumexp(L, dim=1), atol=2e-4, rtol=0)
+    # rows whose cut region holds a key within the fp32 error of a bf16 rounding midpoint, and
+    # those of them where the kernel's (admissible) list differs from the exact one
+    return {"rows": M, "ambiguous_rows": int((~unambiguous).sum()),
+            "ambiguous_rows_differing_from_exact": int((~unambiguous & differs).sum())}
 
 
 def check(M, N, H, k, seed, sort_ids=False):
@@ -82,8 +87,8 @@ def check(M, N, H, k, seed, sort_ids=False):
         s_ids, perm = torch.sort(r_ids, dim=1)
         assert torch.equal(ids, s_ids) and torch.equal(vals, r_vals.gather(1, perm))
         ids, vals = r_ids, r_vals
-    check_against_exact(x, w, k, ids, vals, lse)
-    return ids, vals, lse
+    stats = check_against_exact(x, w, k, ids, vals, lse)
+    return ids, vals, lse, stats
 
 
 @pytest.mark.parametrize("M,N,H,k", [(128, 4096, 64, 8), (128, 5000, 256, 8), (200, 12345, 512, 20),
@@ -97,9 +102,14 @@ def test_lmhead_sorted_ids_mode():
     check(128, 9000, 256, 8, seed=3, sort_ids=True)
 
 
-def test_lmhead_config2_full():
-    """Config 2: hidden [1024, 4096] ~ N(0,1), W [151936, 4096] ~ N(0, 0.02^2), top-8 + lse."""
-    check(1024, 151936, 4096, 8, seed=2)
+def test_lmhead_config2_full(record_property):
+    """Config 2: hidden [1024, 4096] ~ N(0,1), W [151936, 4096] ~ N(0, 0.02^2), top-8 + lse.
+    Reports how many rows were ambiguous (a key near the cut within the fp32 error of a bf16
+    midpoint) and how many of those differ from the exact list (every row is admissible)."""
+    stats = check(1024, 151936, 4096, 8, seed=2)[3]
+    for name, v in stats.items():
+        record_property(name, v)
+    print("config2 admissibility:", stats)
 
 
 def test_lmhead_vocab_smaller_than_k_pads():

@@ -2,7 +2,7 @@
 requests still pending with their lengths capped at W = 2, 4, 8, 16 and keeping each request
 once its capped chain stops before the cap (or its length fits the window) gives the outputs
 of one verification of the whole batch, bit for bit.  The device call uses the same driver
-(`verify.window_rounds`); its GPU test is in test_gpu_verify.py."""
+(`verify.window_stages`); its GPU test is in test_gpu_verify.py."""
 
 import numpy as np
 import pytest
@@ -40,7 +40,7 @@ def test_windows_give_the_outputs_of_the_whole_batch(seed, accept_all, first):
     lens = batch.verify_lens.numpy()
     got = [np.zeros_like(w) for w in want]
 
-    def run_round(pending, lo, W):
+    def run_stage(pending, lo, W):
         sub = workloads.subset(batch, pending)
         sub.verify_lens = sub.verify_lens.clamp(max=W)
         res = oracle_verify(sub)
@@ -51,7 +51,7 @@ def test_windows_give_the_outputs_of_the_whole_batch(seed, accept_all, first):
 
         return res[0].tolist(), keep
 
-    windows = verify.window_rounds(lens, first, run_round)
+    windows = verify.window_stages(lens, first, run_stage)
     for name, g, w in zip(NAMES, got, want):
         assert np.array_equal(g, w), name
     assert windows[0] == first and windows[-1] <= 16 * 2
