@@ -357,22 +357,31 @@ def verify_logits_host(*, candidates, target_logits, target_rows, temperature, t
     def up(t):
         return None if t is None else t.to(dev, non_blocking=True)
 
-    small = dict(candidates=up(candidates), target_rows=up(target_rows),
-                 temperature=up(temperature), top_k=up(top_k), top_p=up(top_p),
-                 verify_lens=up(verify_lens), uniforms=up(uniforms),
-                 uniform_final=up(uniform_final), prefix_lens=up(prefix_lens))
-    if with_draft:
-        small["draft_rows"] = up(draft_rows)
-    mp = up(min_p)
+    cand_d, trow_d, temp_d = up(candidates), up(target_rows), up(temperature)
+    topk_d, topp_d, u_d = up(top_k), up(top_p), up(uniforms)
+    uf_d, prefix_d, lens_d = up(uniform_final), up(prefix_lens), up(verify_lens)
+    drow_d, mp = up(draft_rows), up(min_p)
+    h2d = sum(t.numel() * t.element_size() for t in (
+        candidates, target_rows, temperature, top_k, top_p, uniforms, uniform_final,
+        prefix_lens, verify_lens) + ((draft_rows,) if with_draft else ()) +
+        ((min_p,) if min_p is not None else ()))
     t_dev = _device_rows(target_logits, dev, "target")
     d_dev = _device_rows(draft_logits, dev, "draft") if with_draft else None
     row_bytes = target_logits.shape[1] * target_logits.element_size()
-    h2d = sum(t.numel() * t.element_size() for t in small.values())
-    d2h = 0
-    out = new_outputs(B, dev)
-    moved = [h2d, 0]
-
     stream = _stream(dev)
+    # every stage verifies the whole batch: the requests still open with their lengths capped
+    # at the window, the finished ones at length 1 (their position-0 rows are on the device;
+    # those results are ignored), each stage into its own output slice
+    n_stages = 1
+    while first_window << (n_stages - 1) < T:
+        n_stages += 1
+    outs = new_outputs(B * n_stages, dev)
+    stage_out = [tuple(o[k * B:(k + 1) * B] for o in outs) for k in range(n_stages)]
+    cap_h = torch.ones(B, dtype=torch.int32).pin_memory()
+    cap_d = torch.empty(B, dtype=torch.int32, device=dev)
+    workspace = workspace_for(B, dev)
+    stage_of = np.zeros(B, dtype=np.int64)
+    moved = [h2d, 0]
 
     def copy_ranges(dst, src, first, count):
         first = np.ascontiguousarray(first, dtype=np.int64)
@@ -382,47 +391,52 @@ def verify_logits_host(*, candidates, target_logits, target_rows, temperature, t
         moved[0] += int(count.sum()) * row_bytes
 
     def run_stage(pending, lo, W):
+        k = len(stage_windows)
+        stage_windows.append(W)
         # the rows of positions [lo, W), clipped to each request's length (drafts: length - 1)
         pb = np.asarray(pending)
-        n_t = np.clip(np.minimum(W, lens[pb]) - lo, 0, None)
-        copy_ranges(t_dev, target_logits, trow[pb] + lo, n_t)
+        copy_ranges(t_dev, target_logits, trow[pb] + lo, np.clip(np.minimum(W, lens[pb]) - lo, 0, None))
         if with_draft:
             n_d = np.clip(np.minimum(W, lens[pb] - 1) - lo, 0, None) * (~greedy[pb])
             copy_ranges(d_dev, draft_logits, drow[pb] + lo, n_d)
-        idx_h = torch.tensor(pending, dtype=torch.int64)
-        idx = idx_h.to(dev, non_blocking=True)
-        moved[0] += idx_h.numel() * 8
-        sub = {k: v.index_select(0, idx) for k, v in small.items()}
-        sub["verify_lens"] = sub["verify_lens"].clamp(max=W)
-        res = verify_logits(**sub, target_logits=t_dev, draft_logits=d_dev,
-                            min_p=None if mp is None else mp.index_select(0, idx), mode=mode)
-        acc = res[0].cpu()
-        moved[1] += acc.numel() * 4
+        caps = cap_h.numpy()
+        caps[:] = 1
+        caps[pb] = np.minimum(lens[pb], W)
+        cap_d.copy_(cap_h, non_blocking=True)
+        moved[0] += B * 4
+        verify_logits(candidates=cand_d, target_logits=t_dev, target_rows=trow_d,
+                      temperature=temp_d, top_k=topk_d, top_p=topp_d, verify_lens=cap_d,
+                      uniforms=u_d, uniform_final=uf_d, prefix_lens=prefix_d,
+                      draft_logits=d_dev, draft_rows=drow_d, outputs=stage_out[k],
+                      workspace=workspace, min_p=mp, mode=mode)
+        acc = stage_out[k][0].cpu().numpy()
+        moved[1] += B * 4
 
         def keep(positions):
-            sel = torch.tensor(positions, dtype=torch.int64).to(dev, non_blocking=True)
-            di = idx.index_select(0, sel)
-            for full, part in zip(out, res):
-                full.index_copy_(0, di, part.index_select(0, sel))
+            stage_of[pb[positions]] = k
 
-        return acc.tolist(), keep
+        return acc[pb].tolist(), keep
 
+    stage_windows = []
     windows = window_stages(lens, first_window, run_stage)
     h2d, d2h = moved
-    compact = None
+    # every stage's outputs to the host once; each request takes those of its last stage
+    host_all = [o.to("cpu") for o in outs]
+    d2h += sum(o.numel() * o.element_size() for o in host_all)
+    pick = torch.from_numpy(stage_of * B + np.arange(B))
+    host_out = tuple(o.index_select(0, pick) for o in host_all)
+    host_compact = None
     if slots is not None:
         from .accept import accept_compact  # the compaction with the true lengths
-        compact = accept_compact(out[1], small["verify_lens"], out[3], up(slots), up(slot_rows))
-    host_out = tuple(o.to("cpu", non_blocking=True) for o in out)
-    d2h += sum(o.numel() * o.element_size() for o in host_out)
-    host_compact = None
-    if compact is not None:
-        host_compact = CompactOutputs(*(t.to("cpu", non_blocking=True) for t in (
+        commit_d, output_d = up(host_out[1]), up(host_out[3])
+        h2d += host_out[1].numel() * 4 + host_out[3].numel() * 8
+        compact = accept_compact(commit_d, lens_d, output_d, up(slots), up(slot_rows))
+        h2d += slots.numel() * slots.element_size() + slot_rows.numel() * 8
+        host_compact = CompactOutputs(*(t.to("cpu") for t in (
             compact.tokens, compact.kept_slots, compact.offsets, compact.freed_slots,
             compact.freed_offsets)))
         d2h += sum(t.numel() * t.element_size() for t in (
             compact.tokens, compact.kept_slots, compact.offsets, compact.freed_slots,
             compact.freed_offsets))
-        h2d += slots.numel() * slots.element_size() + slot_rows.numel() * 8
     torch.cuda.current_stream(dev).synchronize()
     return host_out, host_compact, HostVerifyInfo(h2d, d2h, windows)
