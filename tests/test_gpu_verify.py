@@ -306,6 +306,24 @@ def test_host_inputs_copy_only_what_the_outcome_needs(case, dtype):
     assert info.windows[0] == 2
 
 
+def test_copy_row_ranges_merges_and_copies_exactly_the_ranges():
+    """dsv_copy_row_ranges: rows [first, first + n) of each range reach the device buffer at
+    the same rows (adjacent ranges merged into one copy); every other row stays untouched."""
+    g = torch.Generator().manual_seed(3)
+    host = torch.randint(0, 1 << 15, (300, 97), generator=g, dtype=torch.int16).pin_memory()
+    dev = torch.full((300, 97), -1, dtype=torch.int16, device=DEV)
+    first = np.array([0, 3, 5, 40, 41, 42, 200, 299], dtype=np.int64)
+    count = np.array([3, 2, 0, 1, 1, 10, 50, 1], dtype=np.int64)
+    from dspine_b200 import _lib
+    _lib.call("dsv_copy_row_ranges", dev.data_ptr(), host.data_ptr(), 97 * 2, len(first),
+              first.ctypes.data, count.ctypes.data, torch.cuda.current_stream().cuda_stream)
+    torch.cuda.synchronize()
+    want = torch.full((300, 97), -1, dtype=torch.int16)
+    for f, n in zip(first, count):
+        want[f:f + n] = host[f:f + n]
+    assert torch.equal(dev.cpu(), want)
+
+
 @pytest.mark.parametrize("B,V", [(1, 1031), (1024, 521), (1025, 521)])
 def test_batch_limits_match_oracle(B, V):
     """One request; the largest batch of the one-launch bf16 path (1024: the task table and the
