@@ -25,7 +25,7 @@ struct WsHeader {
                              // bit 7: the second half of a split row gave up waiting for the
                              //        first (time limit); bits 0, 5-7 leave counters / flags
                              //        possibly set: the workspace must be zeroed again
-    unsigned int next2;      // row kernel: greedy-row counter
+    unsigned int next2;      // unused (kept zero; the header layout is fixed)
     unsigned int ready_tail; // row kernel: requests published to the ready list
     unsigned int chain_next; // row kernel: chain tasks taken
     unsigned int pad_;

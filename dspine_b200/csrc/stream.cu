@@ -2442,7 +2442,6 @@ __global__ void __launch_bounds__(kRT, DSV_ROWS_MIN_CTAS) rows_kernel(VerifyArgs
         __syncthreads();
         if (tid == 0) {
             a.ws->next = 0;
-            a.ws->next2 = 0;
             a.ws->ready_tail = 0;
             a.ws->chain_next = 0;
             a.ws->exited = 0;
