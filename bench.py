@@ -6,8 +6,11 @@
 One step = one dsv_verify_logits launch over the whole ragged batch: temperature / top-k /
 top-p / softmax of every verify row of the target and of the draft, the capped chain rejection,
 the residual bonus draw and the accept-compact of tokens and KV slots.  Inputs are seeded
-synthetic logits (dspine_b200.workloads), resident in HBM for ``value``; ``e2e`` times the same
-call with the inputs copied from pinned host memory and the outputs read back every step.
+synthetic logits (dspine_b200.workloads), resident in HBM for ``value``; ``e2e`` times the public
+call on inputs in pinned host memory (verify.verify_logits_host: only the logit rows an outcome
+can depend on cross to the device, in widening windows of verify positions) with the outputs
+read back every step.  The kernel drops rows after a known rejection, so the roofline is taken
+on the bytes it read (its own counter) with the fraction on every row's bytes beside it.
 
 Multi-GPU: verification has no exchange step (requests are independent), so each rank runs an
 independent replica on its own requests (weak scaling); no collective touches the data path.
