@@ -482,6 +482,9 @@ __device__ void key_range(int target, uint32_t kmin, uint32_t kmax, float m, flo
 #ifndef DSV_RING_VECS
 #define DSV_RING_VECS (2 * DSV_ROWS_THREADS)
 #endif
+#ifndef DSV_WATCH_PREFETCH
+#define DSV_WATCH_PREFETCH 1  // the first pass's drop test reads the step word a chunk early
+#endif
 #ifndef DSV_SPLIT_POS
 #define DSV_SPLIT_POS 3  // verification splits the rows of the first DSV_SPLIT_POS positions
 #endif
@@ -598,12 +601,14 @@ __device__ __forceinline__ int outcome_of(uint32_t w, int cap) {
 // Whether row (b, s) can still change the outcome: not once the outcome is claimed, nor when
 // a step before s is known to be rejected (the chain stops there; rows after it are never
 // read).  Both only become true over time, so a row found unneeded stays unneeded.
-__device__ __forceinline__ bool row_needed(const VerifyArgs& a, int b, int s) {
-    if (a.cand == nullptr) return true;
-    const uint32_t w = *(volatile const uint32_t*)&a.racc[2 * b + 1];
+__device__ __forceinline__ bool needed_by_word(uint32_t w, int s) {
     if (w & kClaimed) return false;
     const uint32_t rej = (w >> 16) & 0x7FFFu;
     return rej == 0u || s <= __ffs(rej) - 1;
+}
+__device__ __forceinline__ bool row_needed(const VerifyArgs& a, int b, int s) {
+    if (a.cand == nullptr) return true;
+    return needed_by_word(*(volatile const uint32_t*)&a.racc[2 * b + 1], s);
 }
 
 struct RowGeo {
@@ -673,6 +678,10 @@ __device__ __forceinline__ int stream_row(RSmem* sh, const VerifyArgs& a, const 
     const int nch = (nvr + CW - 1) / CW;
     const uint32_t base = *R.cnt;  // uniform: read before any thread updates it
     if (tid == 0) sh->stream_end = nch;
+#if DSV_WATCH_PREFETCH
+    const bool watched = tid == 0 && sh->watch_s >= 0;  // thread 0's own copy
+    uint32_t word = 0u;
+#endif
     __syncthreads();
     if (tid == 0) {
         for (int c = 0; c < nch && c < S; ++c) {
@@ -703,8 +712,14 @@ __device__ __forceinline__ int stream_row(RSmem* sh, const VerifyArgs& a, const 
         // barrier, and to a value the next iteration cannot reach
         if (c + 1 >= sh->stream_end) break;
         if (tid == 0) {
+#if DSV_WATCH_PREFETCH
+            // the request's step word is loaded one chunk before it is tested, so the test
+            // does not wait for the load (it would delay the refill and the next barrier)
+            if (watched && (c & 7) == 7 && !sh->abort_row && !needed_by_word(word, sh->watch_s)) {
+#else
             if (sh->watch_s >= 0 && !sh->abort_row && (c & 7) == 7 &&
                 !row_needed(a, sh->watch_b, sh->watch_s)) {
+#endif
                 sh->abort_row = 1;
                 sh->stream_end = min(nch, c + S);  // chunks c + 1 .. c + S - 1 are in flight
             }
@@ -715,6 +730,9 @@ __device__ __forceinline__ int stream_row(RSmem* sh, const VerifyArgs& a, const 
                 mbar_arrive_expect_tx(&R.bar[slot], (uint32_t)nv2 * 16u);
                 bulk_g2s(R.slot(slot), src + (size_t)cn * CW * 16, (uint32_t)nv2 * 16u, &R.bar[slot]);
             }
+#if DSV_WATCH_PREFETCH
+            if (watched && (c & 7) == 6) word = *(volatile const uint32_t*)&a.racc[2 * sh->watch_b + 1];
+#endif
         }
     }
     __syncthreads();
