@@ -1105,7 +1105,27 @@ __device__ uint32_t split_merge(RSmem* sh, const VerifyArgs& a, int slot, uint32
         __threadfence();
     }
     __syncthreads();
-    for (int i = tid; i < kHCap; i += kRT) sh->hist[i] += __ldcg(cnt + i);
+    if ((reinterpret_cast<uintptr_t>(cnt) & 15u) == 0u) {
+        // every load of the slot's counts issued before any is added (16-byte vectors)
+        constexpr int kV = kHCap / 4 / kRT;
+        static_assert(kHCap % (4 * kRT) == 0, "whole count vectors per thread");
+        const uint4* c4 = reinterpret_cast<const uint4*>(cnt);
+        uint4* h4 = reinterpret_cast<uint4*>(sh->hist);
+        uint4 v[kV];
+#pragma unroll
+        for (int u = 0; u < kV; ++u) v[u] = __ldcg(c4 + tid + u * kRT);
+#pragma unroll
+        for (int u = 0; u < kV; ++u) {
+            uint4 x = h4[tid + u * kRT];
+            x.x += v[u].x;
+            x.y += v[u].y;
+            x.z += v[u].z;
+            x.w += v[u].w;
+            h4[tid + u * kRT] = x;
+        }
+    } else {
+        for (int i = tid; i < kHCap; i += kRT) sh->hist[i] += __ldcg(cnt + i);
+    }
     const uint32_t mk1 = __ldcg(meta + 0), nb1 = __ldcg(meta + 1), out1 = __ldcg(meta + 2);
     const uint32_t nb0 = sh->nband;
     for (uint32_t i = tid; i < nb1 && nb0 + i < (uint32_t)kBandCap; i += kRT) sh->band[nb0 + i] = band[i];
