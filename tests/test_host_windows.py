@@ -57,3 +57,27 @@ def test_windows_give_the_outputs_of_the_whole_batch(seed, accept_all, first):
     assert windows[0] == first and windows[-1] <= 16 * 2
     if accept_all:  # every step accepted: the windows grow until the longest request fits
         assert windows[-1] >= int(lens.max())
+
+
+def _host_kwargs(batch):
+    return {k: v for k, v in batch.kwargs().items() if v is not None}
+
+
+@pytest.mark.parametrize("case", ["cpu_device", "first_window", "non_contiguous", "vocab"])
+def test_host_call_rejects_bad_arguments_before_any_copy(case):
+    """verify_logits_host raises ValueError on its argument checks before touching a device,
+    like the reference's launchers (sampling/rejection.py:113-138)."""
+    batch = _batch(7, B=4, V=257)
+    kw = _host_kwargs(batch)
+    device = "cuda"
+    extra = {}
+    if case == "cpu_device":
+        device = "cpu"
+    elif case == "first_window":
+        extra["first_window"] = 1
+    elif case == "non_contiguous":
+        kw["target_logits"] = kw["target_logits"].t().contiguous().t()
+    elif case == "vocab":
+        kw["draft_logits"] = kw["draft_logits"][:, :-1].contiguous()
+    with pytest.raises(ValueError):
+        verify.verify_logits_host(**kw, device=device, **extra)
