@@ -67,7 +67,8 @@ constexpr inline size_t verify_order_offset(int B) {
     return verify_gmax_offset(B) + (size_t)B * 16 * sizeof(unsigned long long);
 }
 // [u32 x 2 x B]: streaming path: per request its rows done and its chain steps decided (reset
-// by the last CTA of each launch)
+// by the last CTA of each launch); cluster path: [2 b] = 16 - the earliest rejected step of
+// request b (reset when the request is finalised)
 constexpr inline size_t verify_racc_offset(int B) {
     return verify_order_offset(B) + (((size_t)B * 4 + 63) & ~(size_t)63);
 }
