@@ -127,3 +127,19 @@ def test_fp8_entry_validation(lib):
     with pytest.raises(ValueError, match="multiple of 128"):
         C.coarse_scores(torch.zeros(2, 100, dtype=torch.uint8), torch.ones(2),
                         torch.zeros(8, 100, dtype=torch.uint8), torch.ones(8))
+
+
+def test_copy_row_ranges_and_bytes_read_validation(lib):
+    """Argument errors of the staged row copier and of the bytes-read query are refused before
+    any CUDA call (a negative count, a negative or null range, a null workspace)."""
+    first = (ctypes.c_int64 * 2)(0, 3)
+    count = (ctypes.c_int64 * 2)(2, 1)
+    bad = (ctypes.c_int64 * 2)(-1, 3)
+    buf = ctypes.create_string_buffer(64)
+    assert lib.dsv_copy_row_ranges(buf, buf, 8, -1, first, count, None) == 1   # n < 0
+    assert lib.dsv_copy_row_ranges(buf, buf, 8, 0, None, None, None) == 0      # nothing to copy
+    assert lib.dsv_copy_row_ranges(None, buf, 8, 2, first, count, None) == 3   # null destination
+    assert lib.dsv_copy_row_ranges(buf, buf, 8, 2, None, count, None) == 3     # null ranges
+    assert lib.dsv_copy_row_ranges(buf, buf, 8, 2, bad, count, None) == 1      # negative row
+    n = ctypes.c_uint64()
+    assert lib.dsv_workspace_bytes_read(None, ctypes.byref(n), None) == 3
